@@ -1,0 +1,424 @@
+"""Benchmark of the EXL3 decode path on B200: the Qwen3-8B-shaped 36-layer linear stack.
+
+Metric: "EXL3 GEMV HBM GB/s (% of peak) and decode tok/s at 1/2/4/8 B200 vs host CPU".  One step = every linear of
+one decode token through the library: per layer q|k|v (4096 -> 4096+1024+1024, 4 bpw, one stacked launch), o
+(4096 -> 4096, 4 bpw), gate|up (4096 -> 12288+12288, 3 bpw, one stacked launch) and down (12288 -> 4096, 3 bpw).
+Weights are random-init N(0, 0.02) (seed 1 + linear index) encoded by the library's encoder; activations N(0, 1) f16,
+each linear reading its own resident input.  `value` is algorithmic bytes (trellis + suh + svh + activations, each
+distinct weight once) per second over CUDA-graph replays of whole steps; `e2e` adds the pinned host->device copy of a
+step's inputs and the device->host copy of its outputs.  At N > 1 GPUs each linear is column-parallel (output rows
+split over ranks, 128-aligned) and every launch's output is all-gathered over NCCL (strong scaling).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HIDDEN, HEADS_Q, KV = 4096, 4096, 1024
+INTER, LAYERS = 12288, 36
+METRIC = "EXL3 GEMV HBM GB/s (% of peak) and decode tok/s at 1/2/4/8 B200 vs host CPU"
+WORKLOAD = "qwen3-8b-shaped EXL3 decode linear stack (36 layers; q/k/v/o 4 bpw, gate/up/down 3 bpw)"
+
+# (name, in, out, bits) per layer, in launch order; q|k|v and gate|up are stacked launches
+LINEARS = [("q", HIDDEN, HEADS_Q, 4), ("k", HIDDEN, KV, 4), ("v", HIDDEN, KV, 4), ("o", HIDDEN, HIDDEN, 4),
+           ("gate", HIDDEN, INTER, 3), ("up", HIDDEN, INTER, 3), ("down", INTER, HIDDEN, 3)]
+GROUPS = [("qkv", ["q", "k", "v"]), ("o", ["o"]), ("gate_up", ["gate", "up"]), ("down", ["down"])]
+
+
+def linear_bytes(i: int, o: int, bits: int, rows: int) -> int:
+    """Algorithmic bytes of one linear: trellis + suh + svh + x + y (f16)."""
+    return i * o * bits // 8 + 2 * i + 2 * o + 2 * rows * (i + o)
+
+
+def step_bytes(rows: int) -> int:
+    return LAYERS * sum(linear_bytes(i, o, b, rows) for _, i, o, b in LINEARS)
+
+
+def load_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks during the timed region
+
+class ClockSampler:
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._idx = device_index
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self._idx)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            names = {
+                "hw_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwSlowdown", 0x8),
+                "hw_thermal_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwThermalSlowdown", 0x40),
+                "sw_thermal_slowdown": getattr(nv, "nvmlClocksThrottleReasonSwThermalSlowdown", 0x20),
+                "sw_power_cap": getattr(nv, "nvmlClocksThrottleReasonSwPowerCap", 0x4),
+                "hw_power_brake_slowdown": getattr(nv, "nvmlClocksThrottleReasonHwPowerBrakeSlowdown", 0x80),
+            }
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h) if hasattr(
+                            nv, "nvmlDeviceGetCurrentClocksEventReasons") else nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                        for k, bit in names.items():
+                            if r & bit:
+                                self.reasons.add(k)
+                    except Exception:
+                        pass
+                    self._stop.wait(0.02)
+
+            self._t = threading.Thread(target=run, daemon=True)
+            self._t.start()
+        except Exception:
+            self._t = None
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=1)
+
+    def summary(self) -> dict:
+        med = statistics.median(self.samples) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ the reference arm: the CPU port of project()
+
+def cpu_sample(rows: int, budget_s: float, threads: int, seed: int = 1):
+    """Times the oracle's restatement of the reference's scalar project() (expert_exl3.zig:546-566) over the layer's
+    linears (layer 0 of the stack, random trellis of the same shapes), `rows` rows each, for about `budget_s`."""
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    lin = []
+    for name, i, o, b in LINEARS:
+        tr = rng.integers(0, 65536, (i // 16, o // 16, 16 * b), dtype=np.uint16)
+        suh = rng.standard_normal(i).astype(np.float16).view(np.uint16)
+        svh = rng.standard_normal(o).astype(np.float16).view(np.uint16)
+        x = rng.standard_normal((rows, i)).astype(np.float32)
+        lin.append((name, i, o, b, tr, suh, svh, x))
+    done_bytes, t0, reps = 0, time.perf_counter(), 0
+    while True:
+        for name, i, o, b, tr, suh, svh, x in lin:
+            for r in range(rows):
+                O.project(x[r], tr, suh, svh, i, o, 16 * b, threads=threads)
+            done_bytes += linear_bytes(i, o, b, rows)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return done_bytes / el / 1e9, el, reps
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_sample(args.batch, 0.0, threads)
+    times, gbs = [], []
+    for _ in range(args.steps):
+        g, el, reps = cpu_sample(args.batch, 0.0, threads)
+        times.append(el)
+        gbs.append(g)
+    total_bytes = args.steps * sum(linear_bytes(i, o, b, args.batch) for _, i, o, b in LINEARS)
+    value = total_bytes / sum(times) / 1e9
+    layer_s = sum(times) / args.steps
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * layer_s, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u16 trellis -> f16/f32",
+        "data": "synthetic (random trellis of the stack's shapes)",
+        "config": {"workload": WORKLOAD, "batch": args.batch, "step": "one layer's 7 linears (bounded sample)"},
+        "decode_tok_s": round(args.batch / (layer_s * LAYERS), 4),
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"layer 0's 7 linears at batch {args.batch} per step (1/36 of a decode step); "
+                                   "C restatement of expert_exl3.zig project(), OpenMP over output tiles"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ the B200 arm
+
+def build_stack(Q, E, torch, rank: int, world: int, device):
+    """Encodes every linear (seeded, identical on all ranks), keeps this rank's column shard, stacks launch groups."""
+    layers = []
+    for l in range(LAYERS):
+        parts = {}
+        for idx, (name, i, o, b) in enumerate(LINEARS):
+            seed = 1 + l * len(LINEARS) + idx
+            g = torch.Generator(device=device)
+            g.manual_seed(seed)
+            w = torch.randn((o, i), generator=g, device=device) * 0.02
+            tr, suh, svh = E.quantize(w, b, seed)
+            del w
+            if world > 1:
+                cols = o // world
+                tr = tr[:, rank * cols // 16:(rank + 1) * cols // 16, :].contiguous()
+                svh = svh[rank * cols:(rank + 1) * cols].contiguous()
+            parts[name] = Q.weight_from_tensors(tr, suh, svh)
+        groups = {}
+        for gname, members in GROUPS:
+            groups[gname] = Q.stack([parts[m] for m in members]) if len(members) > 1 else parts[members[0]]
+        layers.append(groups)
+    torch.cuda.synchronize()
+    return layers
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline sampling (rank 0, N=1)")
+    ap.add_argument("--no-batch8", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        if args.steps > 20:
+            args.steps = 20  # each reference step is a full layer on the CPU; keep the run within minutes
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from plugins_b200 import quant as Q
+    from plugins_b200 import encoder as E
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    layers = build_stack(Q, E, torch, rank, world, device)
+
+    def make_io(rows: int):
+        g = torch.Generator(device=device)
+        g.manual_seed(1234 + rows)
+        ins, outs = [], []
+        for l in range(LAYERS):
+            x = torch.randn((rows, HIDDEN), generator=g, device=device).half()
+            a = torch.randn((rows, HIDDEN), generator=g, device=device).half()
+            m = torch.randn((rows, INTER), generator=g, device=device).half()
+            ins.append({"qkv": x, "o": a, "gate_up": x, "down": m})
+            outs.append({k: torch.empty((rows, layers[l][k].out_features), dtype=torch.float16, device=device)
+                         for k, _ in GROUPS})
+        return ins, outs
+
+    def flat_views(tensors):
+        total = sum(t.numel() for t in tensors)
+        buf = torch.empty(total, dtype=torch.float16, device=device)
+        views, off = [], 0
+        for t in tensors:
+            v = buf[off:off + t.numel()].view(t.shape)
+            v.copy_(t)
+            views.append(v)
+            off += t.numel()
+        return buf, views
+
+    def run_config(rows: int, steps: int, warmup: int):
+        ins, outs = make_io(rows)
+        # inputs live in one contiguous device buffer (one H2D per step); outputs likewise (one D2H)
+        uniq_in = []
+        for l in range(LAYERS):
+            uniq_in += [ins[l]["qkv"], ins[l]["o"], ins[l]["down"]]
+        in_buf, in_views = flat_views(uniq_in)
+        for l in range(LAYERS):
+            x, a, m = in_views[3 * l: 3 * l + 3]
+            ins[l] = {"qkv": x, "o": a, "gate_up": x, "down": m}
+        gathered = []
+        if world > 1:
+            for l in range(LAYERS):
+                gathered.append({k: torch.empty((world,) + tuple(outs[l][k].shape), dtype=torch.float16,
+                                                device=device) for k, _ in GROUPS})
+        out_list = [outs[l][k] for l in range(LAYERS) for k, _ in GROUPS] if world == 1 else \
+            [gathered[l][k] for l in range(LAYERS) for k, _ in GROUPS]
+        out_buf, out_views = flat_views(out_list)
+        j = 0
+        for l in range(LAYERS):
+            for k, _ in GROUPS:
+                if world == 1:
+                    outs[l][k] = out_views[j]
+                else:
+                    gathered[l][k] = out_views[j]
+                j += 1
+
+        def step():
+            for l in range(LAYERS):
+                for k, _ in GROUPS:
+                    Q.matmul(layers[l][k], ins[l][k], out=outs[l][k])
+                    if world > 1:
+                        dist.all_gather_into_tensor(gathered[l][k], outs[l][k])
+
+        s = torch.cuda.Stream(device=device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            step()
+        torch.cuda.synchronize()
+        launches_per_step = LAYERS * len(GROUPS) * 2  # prep + GEMV per launch group
+
+        for _ in range(warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(st)
+            for _ in range(steps):
+                graph.replay()
+            e1.record(st)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+
+        # e2e: pinned host inputs -> device, the step, device -> pinned host outputs
+        h_in = torch.empty(in_buf.shape, dtype=in_buf.dtype, pin_memory=True)
+        h_in.copy_(in_buf)
+        h_out = torch.empty(out_buf.shape, dtype=out_buf.dtype, pin_memory=True)
+        for _ in range(3):
+            in_buf.copy_(h_in, non_blocking=True)
+            graph.replay()
+            h_out.copy_(out_buf, non_blocking=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record(st)
+        for _ in range(steps):
+            in_buf.copy_(h_in, non_blocking=True)
+            graph.replay()
+            h_out.copy_(out_buf, non_blocking=True)
+        e3.record(st)
+        torch.cuda.synchronize()
+        ms_e2e = e2.elapsed_time(e3) / steps
+        if world > 1:
+            t = torch.tensor([ms_e2e], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_e2e = float(t.item())
+
+        # the dominant launch (gate|up, 37.7 MB at 3 bpw) and the 4-bpw q|k|v, timed alone per layer with events
+        def time_group(k: str) -> float:
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(LAYERS)]
+            for rep in range(2):
+                for l in range(LAYERS):
+                    evs[l][0].record(st)
+                    Q.matmul(layers[l][k], ins[l][k], out=outs[l][k] if world == 1 else outs[l][k])
+                    evs[l][1].record(st)
+            torch.cuda.synchronize()
+            return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+        dom_ms = time_group("gate_up")
+        qkv_ms = time_group("qkv")
+        graph.reset()
+        return {"ms": ms, "ms_e2e": ms_e2e, "clk": clk.summary(), "launches": launches_per_step * steps,
+                "h2d": in_buf.numel() * 2, "d2h": out_buf.numel() * 2, "dom_ms": dom_ms, "qkv_ms": qkv_ms}
+
+    peaks = load_peaks()
+    r1 = run_config(args.batch, args.steps, args.warmup)
+    r8 = None if (args.no_batch8 or args.batch == 8) else run_config(8, args.steps, args.warmup)
+    total = step_bytes(args.batch)
+    value = total / (r1["ms"] * 1e-3) / 1e9
+    e2e = total / (r1["ms_e2e"] * 1e-3) / 1e9
+    # dominant kernel: the stacked gate|up launch of this rank (its shard's algorithmic bytes)
+    gu_bytes = sum(linear_bytes(HIDDEN, INTER // world, 3, args.batch) for _ in range(2))
+    achieved = gu_bytes / (r1["dom_ms"] * 1e-3) / 1e9
+    qkv_bytes = sum(linear_bytes(HIDDEN, o // world, 4, args.batch) for o in (HEADS_Q, KV, KV))
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_budget > 0:
+        threads = os.cpu_count() or 1
+        gbs, el, reps = cpu_sample(args.batch, args.cpu_budget, threads)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"layer 0's 7 linears at batch {args.batch}, {reps} pass(es) in {el:.1f} s; C restatement "
+                         "of expert_exl3.zig project() (scalar decode+GEMV), OpenMP over output tiles"}
+    if rank == 0:
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+                tj = json.load(f)
+            traffic = tj.get("gate_up_k3_batch%d" % args.batch)
+        except Exception:
+            pass
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(r1["ms"], 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u16 trellis -> f16 (f32 accumulate)",
+            "data": "synthetic: random-init N(0,0.02) weights (seeded) encoded to EXL3 mul1 by the library; "
+                    "N(0,1) f16 activations",
+            "config": {"workload": WORKLOAD, "batch": args.batch, "layers": LAYERS,
+                       "parallelism": f"tp{world} column-parallel + NCCL all-gather" if world > 1 else "single GPU",
+                       "bytes_per_step": total,
+                       "l2": "no flush: a step streams %.2f GB of distinct weights, >> 126 MB L2" % (total / 1e9)},
+            "decode_tok_s": round(args.batch / (r1["ms"] * 1e-3), 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                         "kernel": "gate|up decode GEMV (4096 -> 2x12288 @ 3 bpw, prep + stream-K launch)",
+                         "bytes_per_launch": gu_bytes, "ms_per_launch": round(r1["dom_ms"], 5),
+                         "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
+            "roofline_4bpw_qkv": {"achieved": round(qkv_bytes / (r1["qkv_ms"] * 1e-3) / 1e9, 1),
+                                  "frac": round(qkv_bytes / (r1["qkv_ms"] * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                                  "ms_per_launch": round(r1["qkv_ms"], 5), "bytes_per_launch": qkv_bytes},
+            "step_frac_of_hbm": round(value / peaks["hbm_gbs"], 4),
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": r1["h2d"],
+                    "d2h_bytes_per_step": r1["d2h"], "ms_per_step": round(r1["ms_e2e"], 4),
+                    "decode_tok_s": round(args.batch / (r1["ms_e2e"] * 1e-3), 2)},
+            "gpu_launches": r1["launches"],
+            "clocks": r1["clk"],
+            "cpu_baseline": cpu,
+        }
+        if r8 is not None:
+            v8 = step_bytes(8) / (r8["ms"] * 1e-3) / 1e9
+            line["batch8"] = {"value": round(v8, 2), "unit": "GB/s", "ms_per_step": round(r8["ms"], 4),
+                              "decode_tok_s": round(8 / (r8["ms"] * 1e-3), 2),
+                              "e2e_value": round(step_bytes(8) / (r8["ms_e2e"] * 1e-3) / 1e9, 2)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

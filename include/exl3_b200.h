@@ -1,0 +1,211 @@
+/*
+ * exl3_b200.h -- C ABI of libexl3b200.so: the EXL3 (mul1 codebook) trellis weight path on NVIDIA B200 (sm_100a).
+ *
+ * The entry points are the reference plugin's `quant` seam, one function per QuantTable slot
+ * (plugins/turboexl3_qwen38/overlay/mlx_serve/abi/quant.zig:24-108, implemented by plugins/turboexl3_ds41/plugin.zig:28-43),
+ * with device buffers in place of MLX arrays and a cudaStream_t in place of the MLX stream.  The reference's kit types
+ * (Str, Verdict, Claim, Weight, Source, LoadCtx, Swiglu) are not vendored in its tree; the structs below carry the
+ * same fields under plain C types.
+ *
+ * Conventions
+ *   - Every call that can fail returns an exl3_verdict: code EXL3_OK, or a named refusal (`why` is a static string;
+ *     the reference's Verdict.refuse / Verdict.named).  An unsupported shape, rate or codebook is refused by name
+ *     before any launch; there is no fallback path.
+ *   - claims / validate / bill never touch the GPU (quant.zig:22).
+ *   - matmul / swiglu enqueue on `stream` and return; they allocate nothing (the per-device workspace is created by
+ *     exl3_open or the first weight registered on that device) and do not synchronise.
+ *   - Calls that share a device share its workspace: order them on one stream (the reference's single inference
+ *     stream), or give concurrent streams their own device via separate processes.
+ *   - Activations are f16, bf16 or f32; the output has the input's dtype (linear.zig:17-21).
+ */
+#ifndef EXL3_B200_H
+#define EXL3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EXL3_ABI_VERSION 1u
+
+/* Str (kit_quant.Str): a byte span, not necessarily NUL-terminated. */
+typedef struct exl3_str {
+  const char *ptr;
+  size_t len;
+} exl3_str;
+
+/* Verdict.Code (kit_quant.Verdict): ok, unsupported, failed, too_large. */
+typedef enum exl3_code { EXL3_OK = 0, EXL3_UNSUPPORTED = 1, EXL3_FAILED = 2, EXL3_TOO_LARGE = 3 } exl3_code;
+
+typedef struct exl3_verdict {
+  int32_t code;    /* exl3_code */
+  const char *why; /* static text; NULL when ok */
+} exl3_verdict;
+
+/* Claim (kit_quant.Claim): how strongly a format claims a quantization block. */
+typedef enum exl3_claim { EXL3_CLAIM_NO = 0, EXL3_CLAIM_BY_MODE = 1, EXL3_CLAIM_BY_MARKER = 2 } exl3_claim;
+
+/* Element types of exl3_tensor / exl3_host_tensor. */
+typedef enum exl3_dtype {
+  EXL3_F16 = 0,
+  EXL3_BF16 = 1,
+  EXL3_F32 = 2,
+  EXL3_I32 = 3,
+  EXL3_U32 = 4,
+  EXL3_U16 = 5,
+  EXL3_I16 = 6
+} exl3_dtype;
+
+/* A device tensor (the ABI's Array): row-major, contiguous. */
+typedef struct exl3_tensor {
+  void *data;
+  int32_t dtype; /* exl3_dtype */
+  int32_t ndim;  /* 1..4 */
+  int64_t shape[4];
+} exl3_tensor;
+
+/* A host tensor handed out by a Source. */
+typedef struct exl3_host_tensor {
+  const void *data;
+  int32_t dtype;
+  int32_t ndim;
+  int64_t shape[4];
+} exl3_host_tensor;
+
+/* Source (kit_quant.Source): where a load reads a pack's tensors.  `tensor` returns 0 and fills `out` when the pack
+ * holds `name`, nonzero otherwise.  The data must stay valid until the load call that asked for it returns. */
+typedef struct exl3_source {
+  void *ctx;
+  int (*tensor)(void *ctx, exl3_str name, exl3_host_tensor *out);
+} exl3_source;
+
+/* LoadCtx (kit_quant.LoadCtx): one load sequence open -> load_tensor / load_bank* -> close. */
+typedef struct exl3_load_ctx {
+  uint32_t size; /* sizeof(exl3_load_ctx) */
+  exl3_str block_json;
+  exl3_str config_json;
+  exl3_str model_dir;
+  exl3_source source;
+  int32_t device;
+  void *stream; /* cudaStream_t the uploads run on */
+} exl3_load_ctx;
+
+/* Weight flags. */
+#define EXL3_WEIGHT_OWNED 1u   /* the library allocated trellis/suh/svh; exl3_release frees them */
+#define EXL3_WEIGHT_BANK 2u    /* routed experts stacked on axis 0 (load_bank) */
+#define EXL3_WEIGHT_GROUPED 4u /* a grouped linear: x [rows, groups, in] -> y [rows, groups, out] */
+
+#define EXL3_MAX_SEGMENTS 4
+
+/* Weight (kit_quant.Weight: w = trellis, scales = suh, biases = svh).  One projection, or `groups` projections of
+ * the same shape stacked on axis 0.  A stacked-output weight (exl3_weight_stack: linears that read the same input,
+ * the reference's linearShared) has nseg > 1: output columns seg_cols[s]..seg_cols[s+1] use suh row s. */
+typedef struct exl3_weight {
+  uint32_t size;    /* sizeof(exl3_weight) */
+  uint32_t flags;   /* EXL3_WEIGHT_* */
+  uint16_t *trellis; /* device, [groups][in/16][out/16][n] (u16 view of the pack's I16) */
+  uint16_t *suh;     /* device f16 bits, [groups][nseg][in] */
+  uint16_t *svh;     /* device f16 bits, [groups][out] */
+  int32_t groups;
+  int32_t in_features;
+  int32_t out_features;
+  int32_t n;         /* halfwords per 16x16 tile = 16 x bits per weight */
+  int32_t device;
+  int32_t nseg;
+  int32_t seg_cols[EXL3_MAX_SEGMENTS + 1];
+} exl3_weight;
+
+/* Swiglu options (kit_quant.Swiglu): `limit` > 0 clamps gate above and up symmetrically (moeClamped, 1..128);
+ * `verify_rows` keeps the decode chain at any row count. */
+typedef struct exl3_swiglu_opts {
+  uint32_t size;
+  int32_t limit;
+  int32_t verify_rows;
+} exl3_swiglu_opts;
+
+/* Extra matmul flags (QuantTable.linear_prepared / linear_split(inner)). */
+#define EXL3_MATMUL_PREPARED 1u /* x holds f16(H(x*suh)/sqrt(128)) rows: skip the prepare */
+#define EXL3_MATMUL_INNER 2u    /* stop at the inner product: y = xp W_hat in f32 (no output Hadamard, no svh) */
+#define EXL3_MATMUL_DP4A 4u     /* mul1 byte sums on dp4a instead of the tensor pipe (same bits) */
+
+/* ------------------------------------------------------------------ the quant seam (QuantTable) */
+
+/* claims (plugins/turboexl3_ds41/config.zig:43-47): an EXL3 block (`quant_method` or `format` "exl3") by marker. */
+exl3_claim exl3_claims(exl3_str block_json, exl3_str config_json);
+
+/* validate (plugins/turboexl3_ds41/config.zig:49-54; turboexl3_qwen38/config.zig:84-104): refuses by name a codebook
+ * other than mul1, a narrowed window, and a rate the kernels do not decode (fractional or above 6 bits). */
+exl3_verdict exl3_validate(exl3_str block_json, exl3_str config_json);
+
+/* bill (plugins/turboexl3_ds41/config.zig:57-61): resident bytes once loaded = the bytes the pack stores. */
+uint64_t exl3_bill(exl3_str block_json, exl3_str model_dir, uint64_t stored);
+
+/* open / close (plugins/turboexl3_ds41/plugin.zig:52-82): checks the block and creates the device workspace. */
+exl3_verdict exl3_open(exl3_load_ctx *ctx);
+void exl3_close(exl3_load_ctx *ctx);
+
+/* load_tensor (plugin.zig:86-103): `<name>.trellis` (I16/U16 [in/16, out/16, n]), `<name>.suh` (f16 [in]),
+ * `<name>.svh` (f16 [out]) uploaded once to HBM; `in_dim` (0 = any) pins the input width.  A name with no trellis but
+ * slices `<name>.slice.<g>` loads as a grouped linear (plugin.zig:107-124). */
+exl3_verdict exl3_load_tensor(const exl3_load_ctx *ctx, exl3_str name, uint32_t in_dim, exl3_weight *out);
+
+/* load_bank (plugin.zig:127-185): the routed experts `<prefix>.<e>.<proj>` for e = 0.. stacked on axis 0, refused
+ * unless the router `<layer>.gate.weight` scores exactly that many experts. `name` is `<prefix>.<proj>`. */
+exl3_verdict exl3_load_bank(const exl3_load_ctx *ctx, exl3_str name, uint32_t in_dim, exl3_weight *out);
+
+/* release (plugin.zig:231-237): frees what the weight owns and zeroes it. */
+void exl3_release(exl3_weight *w);
+
+/* matmul (plugin.zig:243-248; quant.zig:41-42): out = x @ W^T.  x [..., in] (f16/bf16/f32) -> out [..., out] in x's
+ * dtype; a grouped weight takes x [rows, groups, in].  `out` is caller-allocated. */
+exl3_verdict exl3_matmul(const exl3_weight *w, const exl3_tensor *x, void *stream, exl3_tensor *out);
+
+/* moe (plugin.zig:263-265): refused by name -- routed experts run through swiglu. */
+exl3_verdict exl3_moe(const exl3_weight *bank, const exl3_tensor *x, const exl3_tensor *lhs, const exl3_tensor *rhs,
+                      int32_t sorted, void *stream, exl3_tensor *out);
+
+/* swiglu (plugin.zig:267-283; SX/root.zig:32-167): routed SwiGLU experts.  x [B, S, D]; inds [B, S, K] (i32/u32)
+ * and scores [B, S, K] (f32) pick the banks' experts; out [B, S, D] in x's dtype is
+ * sum_k score * down_e(silu(gate_e(x)) * up_e(x)). */
+exl3_verdict exl3_swiglu(const exl3_weight *gate, const exl3_weight *up, const exl3_weight *down,
+                         const exl3_tensor *x, const exl3_tensor *inds, const exl3_tensor *scores,
+                         const exl3_swiglu_opts *opts, void *stream, exl3_tensor *out);
+
+/* ------------------------------------------------------------------ library calls beside the seam */
+
+/* matmul with EXL3_MATMUL_* flags (linear_prepared, linear_split inner: quant.zig:57-66). */
+exl3_verdict exl3_matmul_ex(const exl3_weight *w, const exl3_tensor *x, uint32_t flags, void *stream,
+                            exl3_tensor *out);
+
+/* A borrowed view of device arrays already in the pack layout (the reference's shared handles, plugin.zig:213-218):
+ * validates the shapes and creates the device workspace; exl3_release on a view frees nothing. */
+exl3_verdict exl3_weight_view(uint16_t *trellis, uint16_t *suh, uint16_t *svh, int32_t groups, int32_t in_features,
+                              int32_t out_features, int32_t n, int32_t device, exl3_weight *out);
+
+/* Linears that read the same input stacked along the output into one weight (SX/linear.zig:39-72 linearShared):
+ * `count` (2..4) one-group weights with equal in_features and n, each out_features a multiple of 128. */
+exl3_verdict exl3_weight_stack(const exl3_weight *parts, int32_t count, void *stream, exl3_weight *out);
+
+/* W_hat of group `group`: f16 bits, row-major [in][out] (the decmat / decode_table checks,
+ * plugins/turboexl3_ds41/src/exl3/selfcheck.zig:861-930). */
+exl3_verdict exl3_decode_dense(const exl3_weight *w, int32_t group, uint16_t *out, uint32_t flags, void *stream);
+
+/* Trellis encoder (no counterpart in the reference, which ships no encoder: plugins/turboexl3_ds41/NOTICE:30-32).
+ * `target` (device f32, row-major [in][out]) is the matrix the trellis should decode to -- already rotated by the
+ * 128-wide Hadamards and scaled to the codebook's unit variance; `trellis` (device) receives [in/16][out/16][n]. */
+exl3_verdict exl3_encode_trellis(const float *target, int32_t in_features, int32_t out_features, int32_t n,
+                                 uint16_t *trellis, void *stream);
+
+/* Device error bits the kernels recorded on `device` (bounded waits that gave up); `clear` resets them. */
+exl3_verdict exl3_device_error(int32_t device, uint32_t *bits, int32_t clear);
+
+/* The library's build string. */
+const char *exl3_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXL3_B200_H */

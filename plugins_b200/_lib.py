@@ -1,0 +1,155 @@
+"""ctypes binding of libexl3b200.so (include/exl3_b200.h).
+
+The library is built in-tree (``python -m plugins_b200.build``) and loaded from this package directory; there is no
+other implementation to fall back to, so a missing library is an error.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libexl3b200.so")
+
+EXL3_OK, EXL3_UNSUPPORTED, EXL3_FAILED, EXL3_TOO_LARGE = 0, 1, 2, 3
+CLAIM_NO, CLAIM_BY_MODE, CLAIM_BY_MARKER = 0, 1, 2
+F16, BF16, F32, I32, U32, U16, I16 = 0, 1, 2, 3, 4, 5, 6
+
+WEIGHT_OWNED, WEIGHT_BANK, WEIGHT_GROUPED = 1, 2, 4
+MATMUL_PREPARED, MATMUL_INNER, MATMUL_DP4A = 1, 2, 4
+MAX_SEGMENTS = 4
+
+# every symbol include/exl3_b200.h declares
+EXPORTS = (
+    "exl3_claims", "exl3_validate", "exl3_bill", "exl3_open", "exl3_close", "exl3_load_tensor", "exl3_load_bank",
+    "exl3_release", "exl3_matmul", "exl3_moe", "exl3_swiglu", "exl3_matmul_ex", "exl3_weight_view",
+    "exl3_weight_stack", "exl3_decode_dense", "exl3_encode_trellis", "exl3_device_error", "exl3_version",
+)
+
+
+class Str(ctypes.Structure):
+    _fields_ = [("ptr", ctypes.c_char_p), ("len", ctypes.c_size_t)]
+
+    @classmethod
+    def of(cls, s: str | bytes) -> "Str":
+        b = s.encode() if isinstance(s, str) else bytes(s)
+        o = cls(b, len(b))
+        o._keep = b  # keep the bytes alive with the struct
+        return o
+
+
+class Verdict(ctypes.Structure):
+    _fields_ = [("code", ctypes.c_int32), ("why", ctypes.c_char_p)]
+
+    @property
+    def ok(self) -> bool:
+        return self.code == EXL3_OK
+
+    def message(self) -> str:
+        return self.why.decode() if self.why else ""
+
+
+class Tensor(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("ndim", ctypes.c_int32),
+                ("shape", ctypes.c_int64 * 4)]
+
+
+class HostTensor(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("ndim", ctypes.c_int32),
+                ("shape", ctypes.c_int64 * 4)]
+
+
+TensorFn = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, Str, ctypes.POINTER(HostTensor))
+
+
+class Source(ctypes.Structure):
+    _fields_ = [("ctx", ctypes.c_void_p), ("tensor", TensorFn)]
+
+
+class LoadCtx(ctypes.Structure):
+    _fields_ = [("size", ctypes.c_uint32), ("block_json", Str), ("config_json", Str), ("model_dir", Str),
+                ("source", Source), ("device", ctypes.c_int32), ("stream", ctypes.c_void_p)]
+
+
+class Weight(ctypes.Structure):
+    _fields_ = [("size", ctypes.c_uint32), ("flags", ctypes.c_uint32), ("trellis", ctypes.c_void_p),
+                ("suh", ctypes.c_void_p), ("svh", ctypes.c_void_p), ("groups", ctypes.c_int32),
+                ("in_features", ctypes.c_int32), ("out_features", ctypes.c_int32), ("n", ctypes.c_int32),
+                ("device", ctypes.c_int32), ("nseg", ctypes.c_int32), ("seg_cols", ctypes.c_int32 * (MAX_SEGMENTS + 1))]
+
+
+class SwigluOpts(ctypes.Structure):
+    _fields_ = [("size", ctypes.c_uint32), ("limit", ctypes.c_int32), ("verify_rows", ctypes.c_int32)]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+class Exl3Error(RuntimeError):
+    """A refusal or failure verdict from the library: `.code` and the library's message."""
+
+    def __init__(self, code: int, why: str):
+        super().__init__(why)
+        self.code = code
+        self.why = why
+
+
+def check(v: Verdict) -> None:
+    if v.code != EXL3_OK:
+        raise Exl3Error(v.code, v.message())
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded libexl3b200.so.  Raises if it was not built -- there is no CPU or eager fallback."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m plugins_b200.build` "
+                                   "(the EXL3 path has no fallback)")
+            L = ctypes.CDLL(LIB_PATH)
+            P = ctypes.POINTER
+            L.exl3_claims.restype = ctypes.c_int32
+            L.exl3_claims.argtypes = [Str, Str]
+            L.exl3_validate.restype = Verdict
+            L.exl3_validate.argtypes = [Str, Str]
+            L.exl3_bill.restype = ctypes.c_uint64
+            L.exl3_bill.argtypes = [Str, Str, ctypes.c_uint64]
+            L.exl3_open.restype = Verdict
+            L.exl3_open.argtypes = [P(LoadCtx)]
+            L.exl3_close.restype = None
+            L.exl3_close.argtypes = [P(LoadCtx)]
+            for f in (L.exl3_load_tensor, L.exl3_load_bank):
+                f.restype = Verdict
+                f.argtypes = [P(LoadCtx), Str, ctypes.c_uint32, P(Weight)]
+            L.exl3_release.restype = None
+            L.exl3_release.argtypes = [P(Weight)]
+            L.exl3_matmul.restype = Verdict
+            L.exl3_matmul.argtypes = [P(Weight), P(Tensor), ctypes.c_void_p, P(Tensor)]
+            L.exl3_matmul_ex.restype = Verdict
+            L.exl3_matmul_ex.argtypes = [P(Weight), P(Tensor), ctypes.c_uint32, ctypes.c_void_p, P(Tensor)]
+            L.exl3_moe.restype = Verdict
+            L.exl3_moe.argtypes = [P(Weight), P(Tensor), P(Tensor), P(Tensor), ctypes.c_int32, ctypes.c_void_p,
+                                   P(Tensor)]
+            L.exl3_swiglu.restype = Verdict
+            L.exl3_swiglu.argtypes = [P(Weight), P(Weight), P(Weight), P(Tensor), P(Tensor), P(Tensor),
+                                      P(SwigluOpts), ctypes.c_void_p, P(Tensor)]
+            L.exl3_weight_view.restype = Verdict
+            L.exl3_weight_view.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                           ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, P(Weight)]
+            L.exl3_weight_stack.restype = Verdict
+            L.exl3_weight_stack.argtypes = [P(Weight), ctypes.c_int32, ctypes.c_void_p, P(Weight)]
+            L.exl3_decode_dense.restype = Verdict
+            L.exl3_decode_dense.argtypes = [P(Weight), ctypes.c_int32, ctypes.c_void_p, ctypes.c_uint32,
+                                            ctypes.c_void_p]
+            L.exl3_encode_trellis.restype = Verdict
+            L.exl3_encode_trellis.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                              ctypes.c_void_p, ctypes.c_void_p]
+            L.exl3_device_error.restype = Verdict
+            L.exl3_device_error.argtypes = [ctypes.c_int32, P(ctypes.c_uint32), ctypes.c_int32]
+            L.exl3_version.restype = ctypes.c_char_p
+            L.exl3_version.argtypes = []
+            _lib = L
+    return _lib

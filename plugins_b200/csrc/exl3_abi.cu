@@ -1,0 +1,722 @@
+// exl3_abi.cu -- the C ABI of libexl3b200.so (include/exl3_b200.h): the reference plugin's quant seam over device
+// buffers.  Host code only; the kernels live in exl3_gemv.cu, exl3_decode.cu and exl3_moe.cu.
+#include <cuda_runtime.h>
+
+#include <cctype>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/exl3_b200.h"
+#include "exl3_internal.h"
+#include "exl3_moe.h"
+
+namespace {
+
+// ------------------------------------------------------------------ verdicts
+
+constexpr exl3_verdict kOk = {EXL3_OK, nullptr};
+exl3_verdict refuse(int32_t code, const char* why) { return {code, why}; }
+
+// ------------------------------------------------------------------ a small JSON reader (config blocks only)
+
+struct JVal {
+  enum Kind { Null, Bool, Num, Str, Arr, Obj } kind = Null;
+  bool b = false;
+  double num = 0;
+  bool is_int = false;
+  std::string str;
+  std::vector<JVal> arr;
+  std::vector<std::pair<std::string, JVal>> obj;
+  const JVal* get(const char* key) const {
+    if (kind != Obj) return nullptr;
+    for (const auto& kv : obj)
+      if (kv.first == key) return &kv.second;
+    return nullptr;
+  }
+};
+
+struct JParser {
+  const char* p;
+  const char* end;
+  int depth = 0;
+  void ws() {
+    while (p < end && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
+  }
+  bool lit(const char* s) {
+    size_t n = strlen(s);
+    if (static_cast<size_t>(end - p) < n || strncmp(p, s, n) != 0) return false;
+    p += n;
+    return true;
+  }
+  bool string(std::string& out) {
+    if (p >= end || *p != '"') return false;
+    ++p;
+    while (p < end && *p != '"') {
+      if (*p == '\\') {
+        ++p;
+        if (p >= end) return false;
+        char c = *p++;
+        switch (c) {
+          case 'n': out += '\n'; break;
+          case 't': out += '\t'; break;
+          case 'r': out += '\r'; break;
+          case 'b': out += '\b'; break;
+          case 'f': out += '\f'; break;
+          case 'u': {
+            if (end - p < 4) return false;
+            unsigned v = 0;
+            for (int i = 0; i < 4; ++i) {
+              char h = *p++;
+              v <<= 4;
+              if (h >= '0' && h <= '9') v |= h - '0';
+              else if (h >= 'a' && h <= 'f') v |= h - 'a' + 10;
+              else if (h >= 'A' && h <= 'F') v |= h - 'A' + 10;
+              else return false;
+            }
+            out += static_cast<char>(v < 0x80 ? v : '?');
+            break;
+          }
+          default: out += c;
+        }
+      } else {
+        out += *p++;
+      }
+    }
+    if (p >= end) return false;
+    ++p;
+    return true;
+  }
+  bool value(JVal& v) {
+    if (++depth > 64) return false;
+    ws();
+    if (p >= end) return false;
+    bool ok = true;
+    if (*p == '{') {
+      v.kind = JVal::Obj;
+      ++p;
+      ws();
+      if (p < end && *p == '}') {
+        ++p;
+      } else {
+        while (true) {
+          ws();
+          std::string key;
+          if (!string(key)) { ok = false; break; }
+          ws();
+          if (p >= end || *p != ':') { ok = false; break; }
+          ++p;
+          JVal child;
+          if (!value(child)) { ok = false; break; }
+          v.obj.emplace_back(std::move(key), std::move(child));
+          ws();
+          if (p < end && *p == ',') { ++p; continue; }
+          if (p < end && *p == '}') { ++p; break; }
+          ok = false;
+          break;
+        }
+      }
+    } else if (*p == '[') {
+      v.kind = JVal::Arr;
+      ++p;
+      ws();
+      if (p < end && *p == ']') {
+        ++p;
+      } else {
+        while (true) {
+          JVal child;
+          if (!value(child)) { ok = false; break; }
+          v.arr.push_back(std::move(child));
+          ws();
+          if (p < end && *p == ',') { ++p; continue; }
+          if (p < end && *p == ']') { ++p; break; }
+          ok = false;
+          break;
+        }
+      }
+    } else if (*p == '"') {
+      v.kind = JVal::Str;
+      ok = string(v.str);
+    } else if (lit("true")) {
+      v.kind = JVal::Bool;
+      v.b = true;
+    } else if (lit("false")) {
+      v.kind = JVal::Bool;
+    } else if (lit("null")) {
+      v.kind = JVal::Null;
+    } else {
+      const char* s = p;
+      while (p < end && (isdigit(static_cast<unsigned char>(*p)) || *p == '-' || *p == '+' || *p == '.' || *p == 'e' || *p == 'E')) ++p;
+      if (p == s) return false;
+      std::string t(s, p);
+      char* e = nullptr;
+      v.kind = JVal::Num;
+      v.num = strtod(t.c_str(), &e);
+      v.is_int = t.find_first_of(".eE") == std::string::npos;
+      ok = e && *e == 0;
+    }
+    --depth;
+    return ok;
+  }
+};
+
+bool parse_json(exl3_str s, JVal& out) {
+  if (!s.ptr) return false;
+  JParser jp{s.ptr, s.ptr + s.len};
+  if (!jp.value(out)) return false;
+  jp.ws();
+  return jp.p == jp.end;
+}
+
+bool str_is(const JVal* v, const char* s) { return v && v->kind == JVal::Str && v->str == s; }
+
+// ------------------------------------------------------------------ per-device state
+
+struct DeviceState {
+  bool ready = false;
+  uint8_t* base = nullptr;
+  size_t bytes = 0;
+  uint8_t* xpf = nullptr;
+  float* partials = nullptr;
+  uint32_t* counters = nullptr;
+  uint32_t* err = nullptr;
+  int sms = 0;
+  int max_ctas = 0;
+};
+
+constexpr int kMaxDevices = 64;
+constexpr size_t kXpfBytes = 8u << 20;        // prepared activations: nseg * in/16 * 512 bytes
+constexpr size_t kCounterCount = 8192;        // out / 128 <= 8192
+constexpr int kCtasPerSm = 8;                 // partials capacity per SM (>= the GEMV partition's CTAs per SM)
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+namespace exl3 {
+__device__ uint32_t g_device_error;  // kErr* bits, one word per device
+}
+
+namespace {
+
+// Creates the device workspace once (load time, never inside matmul).
+exl3_verdict ensure_device(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return refuse(EXL3_UNSUPPORTED, "exl3_b200: device index out of range");
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& d = g_dev[dev];
+  if (d.ready) return kOk;
+  DeviceGuard guard(dev);
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return refuse(EXL3_FAILED, "exl3_b200: no CUDA device");
+  if (prop.major != 10) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the kernels are built for sm_100a (B200) only");
+  d.sms = prop.multiProcessorCount;
+  d.max_ctas = d.sms * kCtasPerSm;
+  const size_t partial_bytes = static_cast<size_t>(d.max_ctas) * 2 * 16 * 128 * 4;
+  const size_t counter_bytes = kCounterCount * 4;
+  d.bytes = kXpfBytes + partial_bytes + counter_bytes + 256;
+  if (cudaMalloc(&d.base, d.bytes) != cudaSuccess) return refuse(EXL3_TOO_LARGE, "exl3_b200: workspace allocation failed");
+  d.xpf = d.base;
+  d.partials = reinterpret_cast<float*>(d.base + kXpfBytes);
+  d.counters = reinterpret_cast<uint32_t*>(d.base + kXpfBytes + partial_bytes);
+  if (cudaMemset(d.counters, 0, counter_bytes) != cudaSuccess) return refuse(EXL3_FAILED, "exl3_b200: workspace init failed");
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err), exl3::g_device_error) != cudaSuccess)
+    return refuse(EXL3_FAILED, "exl3_b200: error word lookup failed");
+  if (cudaMemset(d.err, 0, 4) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
+    return refuse(EXL3_FAILED, "exl3_b200: workspace init failed");
+  d.ready = true;
+  return kOk;
+}
+
+DeviceState* device_state(int dev) {
+  if (dev < 0 || dev >= kMaxDevices || !g_dev[dev].ready) return nullptr;
+  return &g_dev[dev];
+}
+
+bool rate_served(int n) { return n % 16 == 0 && n >= 16 && n <= 96; }  // integer K 1..6
+
+exl3_verdict check_linear_shape(int groups, int in_f, int out_f, int n) {
+  if (groups < 1 || in_f <= 0 || out_f <= 0) return refuse(EXL3_UNSUPPORTED, "exl3_b200: empty weight");
+  if (in_f % 128 != 0 || out_f % 128 != 0)
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: in and out features must be multiples of 128 (the Hadamard blocks)");
+  if (!(n % 2 == 0 && n >= 16 && n <= 128)) return refuse(EXL3_UNSUPPORTED, "exl3_b200: not an admitted rate (n even, 16..128)");
+  if (!rate_served(n))
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: fractional or >6-bit rates are not served by the sm_100a kernels");
+  if (out_f / 128 > static_cast<int>(kCounterCount)) return refuse(EXL3_TOO_LARGE, "exl3_b200: out_features too large");
+  if (static_cast<size_t>(in_f / 16) * 512 * exl3::kMaxSegments > kXpfBytes)
+    return refuse(EXL3_TOO_LARGE, "exl3_b200: in_features too large");
+  return kOk;
+}
+
+int64_t numel(const exl3_tensor* t) {
+  int64_t n = 1;
+  for (int i = 0; i < t->ndim; ++i) n *= t->shape[i];
+  return n;
+}
+
+bool act_dtype(int32_t dt) { return dt == EXL3_F16 || dt == EXL3_BF16 || dt == EXL3_F32; }
+
+// ------------------------------------------------------------------ host loads
+
+std::string name_of(exl3_str s) { return s.ptr ? std::string(s.ptr, s.len) : std::string(); }
+
+bool source_get(const exl3_load_ctx* ctx, const std::string& name, exl3_host_tensor& out) {
+  if (!ctx || !ctx->source.tensor) return false;
+  exl3_str s{name.data(), name.size()};
+  memset(&out, 0, sizeof out);
+  return ctx->source.tensor(ctx->source.ctx, s, &out) == 0 && out.data != nullptr;
+}
+
+struct LinearParts {
+  exl3_host_tensor tr, su, sv;
+};
+
+// <base>.trellis / .suh / .svh as exllamav3 stores a linear (plugin.zig:96-103); 0 = missing, -1 = misshaped.
+int parts_of(const exl3_load_ctx* ctx, const std::string& base, uint32_t in_dim, LinearParts& p) {
+  if (!source_get(ctx, base + ".trellis", p.tr)) return 0;
+  if (!source_get(ctx, base + ".suh", p.su) || !source_get(ctx, base + ".svh", p.sv)) return 0;
+  if (p.tr.ndim != 3 || p.su.ndim != 1 || p.sv.ndim != 1) return -1;
+  if (p.su.shape[0] != p.tr.shape[0] * 16 || p.sv.shape[0] != p.tr.shape[1] * 16) return -1;
+  if (in_dim != 0 && p.su.shape[0] != static_cast<int64_t>(in_dim)) return -1;
+  if (p.su.dtype != EXL3_F16 || p.sv.dtype != EXL3_F16) return -1;
+  if (p.tr.dtype != EXL3_I16 && p.tr.dtype != EXL3_U16) return -1;
+  return 1;
+}
+
+const exl3_verdict kNotShaped = {EXL3_UNSUPPORTED,
+                                 "exl3_b200: not an EXL3 linear of the expected input width (trellis [in/16, out/16, n], "
+                                 "suh f16 [in], svh f16 [out])"};
+
+exl3_verdict upload_stack(const exl3_load_ctx* ctx, const std::vector<LinearParts>& parts, uint32_t flags,
+                          exl3_weight* out) {
+  const LinearParts& p0 = parts[0];
+  const int in_f = static_cast<int>(p0.su.shape[0]);
+  const int out_f = static_cast<int>(p0.sv.shape[0]);
+  const int n = static_cast<int>(p0.tr.shape[2]);
+  for (const auto& p : parts)
+    if (p.su.shape[0] != in_f || p.sv.shape[0] != out_f || p.tr.shape[2] != n) return kNotShaped;
+  const int groups = static_cast<int>(parts.size());
+  exl3_verdict v = check_linear_shape(groups, in_f, out_f, n);
+  if (v.code != EXL3_OK) return v;
+  v = ensure_device(ctx->device);
+  if (v.code != EXL3_OK) return v;
+  DeviceGuard guard(ctx->device);
+  cudaStream_t st = static_cast<cudaStream_t>(ctx->stream);
+  const size_t tw = static_cast<size_t>(in_f / 16) * (out_f / 16) * n;
+  uint16_t *tr = nullptr, *su = nullptr, *sv = nullptr;
+  if (cudaMalloc(&tr, tw * groups * 2) != cudaSuccess || cudaMalloc(&su, static_cast<size_t>(in_f) * groups * 2) != cudaSuccess ||
+      cudaMalloc(&sv, static_cast<size_t>(out_f) * groups * 2) != cudaSuccess) {
+    cudaFree(tr);
+    cudaFree(su);
+    cudaFree(sv);
+    return refuse(EXL3_TOO_LARGE, "exl3_b200: out of device memory");
+  }
+  bool ok = true;
+  for (int g = 0; g < groups && ok; ++g) {
+    ok = cudaMemcpyAsync(tr + g * tw, parts[g].tr.data, tw * 2, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+         cudaMemcpyAsync(su + static_cast<size_t>(g) * in_f, parts[g].su.data, static_cast<size_t>(in_f) * 2,
+                         cudaMemcpyHostToDevice, st) == cudaSuccess &&
+         cudaMemcpyAsync(sv + static_cast<size_t>(g) * out_f, parts[g].sv.data, static_cast<size_t>(out_f) * 2,
+                         cudaMemcpyHostToDevice, st) == cudaSuccess;
+  }
+  ok = ok && cudaStreamSynchronize(st) == cudaSuccess;  // host data is only valid during the call
+  if (!ok) {
+    cudaFree(tr);
+    cudaFree(su);
+    cudaFree(sv);
+    return refuse(EXL3_FAILED, "exl3_b200: upload failed");
+  }
+  memset(out, 0, sizeof *out);
+  out->size = sizeof(exl3_weight);
+  out->flags = EXL3_WEIGHT_OWNED | flags;
+  out->trellis = tr;
+  out->suh = su;
+  out->svh = sv;
+  out->groups = groups;
+  out->in_features = in_f;
+  out->out_features = out_f;
+  out->n = n;
+  out->device = ctx->device;
+  out->nseg = 1;
+  out->seg_cols[0] = 0;
+  out->seg_cols[1] = out_f;
+  return kOk;
+}
+
+exl3_verdict check_weight(const exl3_weight* w) {
+  if (!w || w->size != sizeof(exl3_weight) || !w->trellis || !w->suh || !w->svh)
+    return refuse(EXL3_FAILED, "exl3_b200: not a loaded weight");
+  if (w->nseg < 1 || w->nseg > EXL3_MAX_SEGMENTS) return refuse(EXL3_FAILED, "exl3_b200: bad segment count");
+  return check_linear_shape(w->groups, w->in_features, w->out_features, w->n);
+}
+
+// One decode-GEMV pass (prep + stream-K kernel) per group and per 16 rows.
+exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, int64_t rows, void* y, int32_t y_dtype,
+                        uint32_t flags, cudaStream_t st) {
+  DeviceState* d = device_state(w->device);
+  if (!d) return refuse(EXL3_FAILED, "exl3_b200: no workspace on this device (exl3_open or a weight load creates it)");
+  DeviceGuard guard(w->device);
+  const int in_f = w->in_features, out_f = w->out_features, groups = w->groups;
+  const bool grouped = (w->flags & EXL3_WEIGHT_GROUPED) != 0;
+  const int K = w->n / 16;
+  const bool imma = (flags & EXL3_MATMUL_DP4A) == 0;
+  const size_t tile_halfs = static_cast<size_t>(in_f / 16) * (out_f / 16) * w->n;
+  const size_t xsz = x_dtype == EXL3_F32 ? 4 : 2;
+  const size_t ysz = y_dtype == EXL3_F32 ? 4 : 2;
+  const int gcount = grouped ? groups : 1;
+  for (int g = 0; g < gcount; ++g) {
+    for (int64_t r0 = 0; r0 < rows; r0 += exl3::kMaxRows) {
+      const int rc = static_cast<int>(rows - r0 < exl3::kMaxRows ? rows - r0 : exl3::kMaxRows);
+      const int rg = rc <= 8 ? 1 : 2;
+      exl3::PrepParams pp{};
+      const int64_t x_stride = grouped ? static_cast<int64_t>(groups) * in_f : in_f;
+      pp.x = static_cast<const uint8_t*>(x) + (static_cast<size_t>(r0) * x_stride + static_cast<size_t>(g) * in_f) * xsz;
+      pp.x_dtype = x_dtype;
+      pp.x_row_stride = x_stride;
+      pp.suh = w->suh + static_cast<size_t>(g) * w->nseg * in_f;
+      pp.xpf = d->xpf;
+      pp.in_features = in_f;
+      pp.rows = rc;
+      pp.row_groups = rg;
+      pp.nseg = w->nseg;
+      pp.prepared = (flags & EXL3_MATMUL_PREPARED) ? 1 : 0;
+      pp.imma_order = imma ? 1 : 0;
+      if (exl3::launch_prep(pp, st, true) != cudaSuccess)
+        return refuse(EXL3_FAILED, "exl3_b200: prep launch failed");
+      exl3::GemvParams gp{};
+      gp.trellis = w->trellis + static_cast<size_t>(g) * tile_halfs;
+      gp.svh = w->svh + static_cast<size_t>(g) * out_f;
+      gp.xpf = d->xpf;
+      const int64_t y_stride = grouped ? static_cast<int64_t>(groups) * out_f : out_f;
+      gp.y = static_cast<uint8_t*>(y) + static_cast<size_t>(g) * out_f * ysz;
+      gp.y_dtype = y_dtype;
+      gp.y_row_stride = y_stride;
+      gp.row0 = static_cast<int32_t>(r0);
+      gp.rows_total = static_cast<int32_t>(rows);
+      gp.partials = d->partials;
+      gp.counters = d->counters;
+      gp.err = d->err;
+      gp.in_features = in_f;
+      gp.out_features = out_f;
+      gp.rows = rc;
+      gp.nseg = w->nseg;
+      for (int s = 0; s <= w->nseg; ++s) gp.seg_cb[s] = w->seg_cols[s] / 128;
+      gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
+      gp.max_ctas = d->max_ctas;
+      if (exl3::launch_gemv(gp, K, rg, imma, d->sms, st, true) != cudaSuccess)
+        return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
+    }
+  }
+  return kOk;
+}
+
+}  // namespace
+
+// ====================================================================== the C ABI
+
+extern "C" {
+
+const char* exl3_version(void) { return "exl3_b200 1 (sm_100a)"; }
+
+exl3_claim exl3_claims(exl3_str block_json, exl3_str config_json) {
+  (void)config_json;
+  JVal b;
+  if (!parse_json(block_json, b) || b.kind != JVal::Obj) return EXL3_CLAIM_NO;
+  if (str_is(b.get("quant_method"), "exl3") || str_is(b.get("format"), "exl3")) return EXL3_CLAIM_BY_MARKER;
+  return EXL3_CLAIM_NO;
+}
+
+exl3_verdict exl3_validate(exl3_str block_json, exl3_str config_json) {
+  (void)config_json;
+  JVal b;
+  if (!parse_json(block_json, b) || b.kind != JVal::Obj) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the block is not a JSON object");
+  if (!str_is(b.get("quant_method"), "exl3") && !str_is(b.get("format"), "exl3"))
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: not an exllamav3 block");
+  const JVal* cb = b.get("codebook");
+  if (!str_is(cb, "mul1")) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the codebook is not mul1");
+  if (const JVal* w = b.get("window")) {
+    if (w->kind != JVal::Num || !w->is_int || w->num < 8 || w->num > 16)
+      return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3WindowUnsupported");
+    if (w->num != 16) return refuse(EXL3_UNSUPPORTED, "exl3_b200: narrowed codeword windows are not served");
+  }
+  if (const JVal* k = b.get("k")) {
+    if (k->kind != JVal::Num) return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3RateUnsupported");
+    const double scaled = k->num * 16.0, n = std::round(scaled);
+    if (std::fabs(scaled - n) > 1e-6 || n < 16 || n > 128 || std::fmod(n, 2.0) != 0)
+      return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3RateUnsupported");
+    if (!rate_served(static_cast<int>(n)))
+      return refuse(EXL3_UNSUPPORTED, "exl3_b200: fractional or >6-bit rates are not served by the sm_100a kernels");
+  }
+  return kOk;
+}
+
+uint64_t exl3_bill(exl3_str block_json, exl3_str model_dir, uint64_t stored) {
+  (void)block_json;
+  (void)model_dir;
+  return stored;
+}
+
+exl3_verdict exl3_open(exl3_load_ctx* ctx) {
+  if (!ctx || ctx->size != sizeof(exl3_load_ctx)) return refuse(EXL3_FAILED, "exl3_b200: bad load context");
+  if (exl3_claims(ctx->block_json, ctx->config_json) == EXL3_CLAIM_NO)
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: not an exllamav3 mul1 block");
+  exl3_verdict v = exl3_validate(ctx->block_json, ctx->config_json);
+  if (v.code != EXL3_OK) return v;
+  return ensure_device(ctx->device);
+}
+
+void exl3_close(exl3_load_ctx* ctx) { (void)ctx; }
+
+exl3_verdict exl3_load_tensor(const exl3_load_ctx* ctx, exl3_str name, uint32_t in_dim, exl3_weight* out) {
+  if (!ctx || !out) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
+  const std::string base = name_of(name);
+  if (base.size() > 160) return refuse(EXL3_FAILED, "exl3_b200: a name too long");
+  LinearParts p;
+  const int got = parts_of(ctx, base, in_dim, p);
+  if (got < 0) return kNotShaped;
+  if (got == 1) return upload_stack(ctx, {p}, 0, out);
+  // grouped linear: <base>.slice.<g>
+  std::vector<LinearParts> parts;
+  for (int g = 0;; ++g) {
+    LinearParts q;
+    const int r = parts_of(ctx, base + ".slice." + std::to_string(g), in_dim, q);
+    if (r < 0) return kNotShaped;
+    if (r == 0) break;
+    parts.push_back(q);
+  }
+  if (parts.empty()) return refuse(EXL3_FAILED, "MissingWeight");
+  return upload_stack(ctx, parts, EXL3_WEIGHT_GROUPED, out);
+}
+
+exl3_verdict exl3_load_bank(const exl3_load_ctx* ctx, exl3_str name, uint32_t in_dim, exl3_weight* out) {
+  if (!ctx || !out) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
+  const std::string full = name_of(name);
+  const size_t dot = full.rfind('.');
+  if (dot == std::string::npos) return refuse(EXL3_FAILED, "MissingWeight");
+  const std::string prefix = full.substr(0, dot), suffix = full.substr(dot);
+  std::vector<LinearParts> parts;
+  for (int e = 0;; ++e) {
+    LinearParts q;
+    const int r = parts_of(ctx, prefix + "." + std::to_string(e) + suffix, in_dim, q);
+    if (r < 0) return kNotShaped;
+    if (r == 0) break;
+    parts.push_back(q);
+  }
+  if (parts.empty()) return refuse(EXL3_FAILED, "MissingWeight");
+  // every expert the router scores (plugin.zig:142-151)
+  const std::string tail = ".experts";
+  bool routed_ok = false;
+  if (prefix.size() > tail.size() && prefix.compare(prefix.size() - tail.size(), tail.size(), tail) == 0) {
+    exl3_host_tensor gate;
+    if (source_get(ctx, prefix.substr(0, prefix.size() - tail.size()) + ".gate.weight", gate) && gate.ndim == 2)
+      routed_ok = gate.shape[0] == static_cast<int64_t>(parts.size());
+  }
+  if (!routed_ok)
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: the bank holds another count of experts than its router scores");
+  exl3_verdict v = upload_stack(ctx, parts, EXL3_WEIGHT_BANK, out);
+  if (v.code == EXL3_OK) {
+    v = exl3::moe_reserve(out->device, out->in_features, out->out_features);
+    if (v.code != EXL3_OK) exl3_release(out);
+  }
+  return v;
+}
+
+void exl3_release(exl3_weight* w) {
+  if (!w) return;
+  if ((w->flags & EXL3_WEIGHT_OWNED) && w->size == sizeof(exl3_weight)) {
+    DeviceGuard guard(w->device);
+    cudaFree(w->trellis);
+    cudaFree(w->suh);
+    cudaFree(w->svh);
+  }
+  memset(w, 0, sizeof *w);
+}
+
+exl3_verdict exl3_matmul_ex(const exl3_weight* w, const exl3_tensor* x, uint32_t flags, void* stream, exl3_tensor* out) {
+  exl3_verdict v = check_weight(w);
+  if (v.code != EXL3_OK) return v;
+  if (!x || !out || x->ndim < 1 || x->ndim > 4 || out->ndim != x->ndim) return refuse(EXL3_FAILED, "exl3_b200: bad tensors");
+  if ((numel(x) > 0 && !x->data) || (numel(out) > 0 && !out->data)) return refuse(EXL3_FAILED, "exl3_b200: bad tensors");
+  if (!act_dtype(x->dtype)) return refuse(EXL3_UNSUPPORTED, "exl3_b200: activations must be f16, bf16 or f32");
+  if ((flags & EXL3_MATMUL_PREPARED) && x->dtype != EXL3_F16)
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: prepared rows are f16");
+  const bool grouped = (w->flags & EXL3_WEIGHT_GROUPED) != 0;
+  if (w->groups > 1 && !grouped) return refuse(EXL3_UNSUPPORTED, "exl3_b200: a bank runs through swiglu, not matmul");
+  const int64_t last = x->shape[x->ndim - 1];
+  if (last != w->in_features) return refuse(EXL3_UNSUPPORTED, "exl3_b200: x's last dim is not the weight's input width");
+  int64_t rows = numel(x) / last;
+  if (grouped) {
+    if (x->ndim < 2 || x->shape[x->ndim - 2] != w->groups)
+      return refuse(EXL3_UNSUPPORTED, "exl3_b200: a grouped linear takes x [rows, groups, in]");
+    rows /= w->groups;
+  }
+  const int32_t y_dtype = (flags & EXL3_MATMUL_INNER) ? EXL3_F32 : (flags & EXL3_MATMUL_PREPARED) ? out->dtype : x->dtype;
+  if (out->dtype != y_dtype || (flags & EXL3_MATMUL_PREPARED && !act_dtype(out->dtype)))
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: the output has the wrong dtype");
+  for (int i = 0; i < x->ndim - 1; ++i)
+    if (out->shape[i] != x->shape[i]) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the output has the wrong shape");
+  if (out->shape[out->ndim - 1] != w->out_features) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the output has the wrong shape");
+  if (rows == 0) return kOk;
+  if (rows > (1 << 24)) return refuse(EXL3_TOO_LARGE, "exl3_b200: too many rows");
+  return run_linear(w, x->data, x->dtype, rows, out->data, y_dtype, flags, static_cast<cudaStream_t>(stream));
+}
+
+exl3_verdict exl3_matmul(const exl3_weight* w, const exl3_tensor* x, void* stream, exl3_tensor* out) {
+  return exl3_matmul_ex(w, x, 0, stream, out);
+}
+
+exl3_verdict exl3_moe(const exl3_weight*, const exl3_tensor*, const exl3_tensor*, const exl3_tensor*, int32_t, void*,
+                      exl3_tensor*) {
+  return refuse(EXL3_UNSUPPORTED, "exl3_b200: routed experts run through swiglu");
+}
+
+exl3_verdict exl3_swiglu(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down, const exl3_tensor* x,
+                         const exl3_tensor* inds, const exl3_tensor* scores, const exl3_swiglu_opts* opts, void* stream,
+                         exl3_tensor* out) {
+  return exl3::moe_swiglu(gate, up, down, x, inds, scores, opts, stream, out);
+}
+
+exl3_verdict exl3_weight_view(uint16_t* trellis, uint16_t* suh, uint16_t* svh, int32_t groups, int32_t in_features,
+                              int32_t out_features, int32_t n, int32_t device, exl3_weight* out) {
+  if (!out || !trellis || !suh || !svh) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
+  exl3_verdict v = check_linear_shape(groups, in_features, out_features, n);
+  if (v.code != EXL3_OK) return v;
+  if ((reinterpret_cast<uintptr_t>(trellis) & 15u) != 0)
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: the trellis must be 16-byte aligned");
+  v = ensure_device(device);
+  if (v.code != EXL3_OK) return v;
+  memset(out, 0, sizeof *out);
+  out->size = sizeof(exl3_weight);
+  out->flags = groups > 1 ? EXL3_WEIGHT_BANK : 0;
+  out->trellis = trellis;
+  out->suh = suh;
+  out->svh = svh;
+  out->groups = groups;
+  out->in_features = in_features;
+  out->out_features = out_features;
+  out->n = n;
+  out->device = device;
+  out->nseg = 1;
+  out->seg_cols[1] = out_features;
+  return kOk;
+}
+
+exl3_verdict exl3_weight_stack(const exl3_weight* parts, int32_t count, void* stream, exl3_weight* out) {
+  if (!parts || !out || count < 2 || count > EXL3_MAX_SEGMENTS)
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: stack 2..4 linears");
+  const exl3_weight& p0 = parts[0];
+  int total = 0;
+  for (int i = 0; i < count; ++i) {
+    exl3_verdict v = check_weight(&parts[i]);
+    if (v.code != EXL3_OK) return v;
+    if (parts[i].groups != 1 || parts[i].nseg != 1 || parts[i].in_features != p0.in_features || parts[i].n != p0.n ||
+        parts[i].device != p0.device)
+      return refuse(EXL3_UNSUPPORTED, "exl3_b200: stacked linears share one input width, rate and device");
+    total += parts[i].out_features;
+  }
+  exl3_verdict v = check_linear_shape(1, p0.in_features, total, p0.n);
+  if (v.code != EXL3_OK) return v;
+  DeviceGuard guard(p0.device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int KT = p0.in_features / 16, n = p0.n;
+  uint16_t *tr = nullptr, *su = nullptr, *sv = nullptr;
+  if (cudaMalloc(&tr, static_cast<size_t>(KT) * (total / 16) * n * 2) != cudaSuccess ||
+      cudaMalloc(&su, static_cast<size_t>(count) * p0.in_features * 2) != cudaSuccess ||
+      cudaMalloc(&sv, static_cast<size_t>(total) * 2) != cudaSuccess) {
+    cudaFree(tr);
+    cudaFree(su);
+    cudaFree(sv);
+    return refuse(EXL3_TOO_LARGE, "exl3_b200: out of device memory");
+  }
+  memset(out, 0, sizeof *out);
+  int col = 0;
+  bool ok = true;
+  for (int i = 0; i < count && ok; ++i) {
+    const size_t row_bytes = static_cast<size_t>(parts[i].out_features / 16) * n * 2;
+    const size_t dst_pitch = static_cast<size_t>(total / 16) * n * 2;
+    ok = cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(tr) + static_cast<size_t>(col / 16) * n * 2, dst_pitch,
+                           parts[i].trellis, row_bytes, row_bytes, KT, cudaMemcpyDeviceToDevice, st) == cudaSuccess &&
+         cudaMemcpyAsync(su + static_cast<size_t>(i) * p0.in_features, parts[i].suh, static_cast<size_t>(p0.in_features) * 2,
+                         cudaMemcpyDeviceToDevice, st) == cudaSuccess &&
+         cudaMemcpyAsync(sv + col, parts[i].svh, static_cast<size_t>(parts[i].out_features) * 2, cudaMemcpyDeviceToDevice,
+                         st) == cudaSuccess;
+    out->seg_cols[i] = col;
+    col += parts[i].out_features;
+  }
+  if (!ok || cudaStreamSynchronize(st) != cudaSuccess) {
+    cudaFree(tr);
+    cudaFree(su);
+    cudaFree(sv);
+    memset(out, 0, sizeof *out);
+    return refuse(EXL3_FAILED, "exl3_b200: stacking copy failed");
+  }
+  out->seg_cols[count] = total;
+  out->size = sizeof(exl3_weight);
+  out->flags = EXL3_WEIGHT_OWNED;
+  out->trellis = tr;
+  out->suh = su;
+  out->svh = sv;
+  out->groups = 1;
+  out->in_features = p0.in_features;
+  out->out_features = total;
+  out->n = n;
+  out->device = p0.device;
+  out->nseg = count;
+  return kOk;
+}
+
+exl3_verdict exl3_decode_dense(const exl3_weight* w, int32_t group, uint16_t* out, uint32_t flags, void* stream) {
+  exl3_verdict v = check_weight(w);
+  if (v.code != EXL3_OK) return v;
+  if (group < 0 || group >= w->groups || !out) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
+  DeviceGuard guard(w->device);
+  const size_t tw = static_cast<size_t>(w->in_features / 16) * (w->out_features / 16) * w->n;
+  if (exl3::launch_decode_dense(w->trellis + group * tw, w->in_features, w->out_features, w->n, out,
+                                (flags & EXL3_MATMUL_DP4A) ? 0 : 1, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return refuse(EXL3_FAILED, "exl3_b200: decode launch failed");
+  return kOk;
+}
+
+exl3_verdict exl3_encode_trellis(const float* target, int32_t in_features, int32_t out_features, int32_t n,
+                                 uint16_t* trellis, void* stream) {
+  if (!target || !trellis) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
+  exl3_verdict v = check_linear_shape(1, in_features, out_features, n);
+  if (v.code != EXL3_OK) return v;
+  if (exl3::launch_encode(target, in_features, out_features, n, trellis, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return refuse(EXL3_FAILED, "exl3_b200: encoder launch failed");
+  return kOk;
+}
+
+exl3_verdict exl3_device_error(int32_t device, uint32_t* bits, int32_t clear) {
+  DeviceState* d = device_state(device);
+  if (!d || !bits) return refuse(EXL3_FAILED, "exl3_b200: no workspace on this device");
+  DeviceGuard guard(device);
+  if (cudaMemcpy(bits, d->err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return refuse(EXL3_FAILED, "exl3_b200: read failed");
+  if (clear) {
+    // a launch that gave up may have left block counters raised: reset them with the error word
+    if (cudaMemset(d->err, 0, 4) != cudaSuccess || cudaMemset(d->counters, 0, kCounterCount * 4) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess)
+      return refuse(EXL3_FAILED, "exl3_b200: reset failed");
+  }
+  return kOk;
+}
+
+}  // extern "C"

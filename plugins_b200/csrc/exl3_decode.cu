@@ -1,0 +1,91 @@
+// exl3_decode.cu -- decode a trellis to the dense W_hat (f16 bits, row-major [in][out]).
+//
+// The GPU side of the reference's bit-exact decode checks (plugins/turboexl3_ds41/src/exl3/selfcheck.zig:861-930,
+// decode_table / golden_tiles, and the decmat kernels): the same in-register decode the GEMV uses, written out.
+// One warp per 16x16 tile; lane t's eight weights land at rows {2(t%4), +1, +8, +9}, columns t/4 and t/4 + 8.
+#include <cuda_runtime.h>
+
+#include "exl3_common.cuh"
+#include "exl3_internal.h"
+
+namespace exl3 {
+
+template <int K, bool IMMA>
+__global__ void __launch_bounds__(256) decode_dense_kernel(const uint16_t* __restrict__ trellis, int in_features,
+                                                           int out_features, uint16_t* __restrict__ out) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const int ot = out_features / 16;
+  const size_t tiles = static_cast<size_t>(in_features / 16) * ot;
+  const size_t tile = static_cast<size_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (tile >= tiles) return;  // warp-uniform
+  const int tk = static_cast<int>(tile / ot), tn = static_cast<int>(tile % ot);
+  const uint32_t* tw = reinterpret_cast<const uint32_t*>(trellis + tile * (16 * K));
+  LaneWindows<K> lw;
+  lw.init(lane);
+  uint32_t w[8], a[4];
+  lane_codewords<K>(tw, lw, w);
+  const uint32_t g = lane >> 2, q = lane & 3u;
+  if constexpr (IMMA) {
+    ImmaIndicator ind;
+    ind.init(lane);
+    decode_afrag_imma(w, ind, a);
+    // a[0] = col g at k 4q, 4q+1; a[2] = col g at k 4q+2, 4q+3; a[1], a[3] = col g+8
+    const int k0 = 4 * q;
+    const int r = tk * 16, c = tn * 16;
+    const uint32_t cols[2] = {g, g + 8};
+    const uint32_t lo[2] = {a[0], a[1]}, hi[2] = {a[2], a[3]};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      out[static_cast<size_t>(r + k0 + 0) * out_features + c + cols[h]] = static_cast<uint16_t>(lo[h]);
+      out[static_cast<size_t>(r + k0 + 1) * out_features + c + cols[h]] = static_cast<uint16_t>(lo[h] >> 16);
+      out[static_cast<size_t>(r + k0 + 2) * out_features + c + cols[h]] = static_cast<uint16_t>(hi[h]);
+      out[static_cast<size_t>(r + k0 + 3) * out_features + c + cols[h]] = static_cast<uint16_t>(hi[h] >> 16);
+    }
+  } else {
+    decode_afrag_dp4a(w, a);
+    // a[0] = (j0, j1) col g k 2q..; a[1] = (j4, j5) col g+8; a[2] = (j2, j3) col g k 2q+8..; a[3] = (j6, j7)
+    const int r = tk * 16, c = tn * 16;
+    const int k0 = 2 * q;
+    out[static_cast<size_t>(r + k0) * out_features + c + g] = static_cast<uint16_t>(a[0]);
+    out[static_cast<size_t>(r + k0 + 1) * out_features + c + g] = static_cast<uint16_t>(a[0] >> 16);
+    out[static_cast<size_t>(r + k0) * out_features + c + g + 8] = static_cast<uint16_t>(a[1]);
+    out[static_cast<size_t>(r + k0 + 1) * out_features + c + g + 8] = static_cast<uint16_t>(a[1] >> 16);
+    out[static_cast<size_t>(r + k0 + 8) * out_features + c + g] = static_cast<uint16_t>(a[2]);
+    out[static_cast<size_t>(r + k0 + 9) * out_features + c + g] = static_cast<uint16_t>(a[2] >> 16);
+    out[static_cast<size_t>(r + k0 + 8) * out_features + c + g + 8] = static_cast<uint16_t>(a[3]);
+    out[static_cast<size_t>(r + k0 + 9) * out_features + c + g + 8] = static_cast<uint16_t>(a[3] >> 16);
+  }
+}
+
+template <bool IMMA>
+static cudaError_t launch_dd(const uint16_t* trellis, int in_features, int out_features, int K, uint16_t* out,
+                             cudaStream_t st) {
+  const size_t tiles = static_cast<size_t>(in_features / 16) * (out_features / 16);
+  const dim3 grid(static_cast<unsigned>((tiles + 7) / 8)), block(256);
+  switch (K) {
+    case 1: decode_dense_kernel<1, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
+    case 2: decode_dense_kernel<2, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
+    case 3: decode_dense_kernel<3, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
+    case 4: decode_dense_kernel<4, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
+    case 5: decode_dense_kernel<5, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
+    case 6: decode_dense_kernel<6, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
+                                int imma, cudaStream_t st) {
+  if (n % 16 != 0) return cudaErrorInvalidValue;
+  return imma ? launch_dd<true>(trellis, in_features, out_features, n / 16, out, st)
+              : launch_dd<false>(trellis, in_features, out_features, n / 16, out, st);
+}
+
+size_t gemv_workspace_bytes(int in_features, int out_features, int nseg, int max_ctas) {
+  const size_t xpf = static_cast<size_t>(nseg) * (in_features / 16) * 2 * 256;  // row_groups <= 2
+  const size_t partials = static_cast<size_t>(max_ctas) * 2 * 16 * 128 * 4;
+  const size_t counters = static_cast<size_t>(out_features / 128) * 4;
+  return xpf + partials + counters + 3 * 256;
+}
+
+}  // namespace exl3

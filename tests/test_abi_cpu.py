@@ -1,0 +1,91 @@
+"""The C-ABI library without a GPU: it loads, exports every entry point include/exl3_b200.h declares, and the
+seam's GPU-free calls (claims / validate / bill, plugins/turboexl3_ds41/config.zig:43-61 and its tests :66-86;
+plugins/turboexl3_qwen38/config.zig:84-104 and :151-176) behave as the reference's."""
+import ctypes
+import json
+import os
+import re
+
+import pytest
+
+from plugins_b200 import _lib as L
+from plugins_b200 import quant as Q
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared() -> set[str]:
+    text = open(os.path.join(ROOT, "include", "exl3_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(exl3_[a-z_0-9]+)\s*\(", text))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = L.lib()
+    declared = _declared()
+    assert declared == set(L.EXPORTS), declared ^ set(L.EXPORTS)
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert b"sm_100a" in lib.exl3_version()
+
+
+def test_library_is_an_sm100a_build():
+    # the shared object carries sm_100a code for every kernel (cuobjdump is not needed: the fatbin's arch tag is text)
+    data = open(L.LIB_PATH, "rb").read()
+    assert b"sm_100a" in data
+
+
+DS41_BLOCK = {"quant_method": "exl3", "bits": 2.81, "codebook": "mul1"}
+
+
+def test_claims_exl3_blocks_by_marker():
+    assert Q.claims(DS41_BLOCK, {"model_type": "deepseek_v41"}) == Q.CLAIM_BY_MARKER
+    assert Q.claims({"format": "exl3", "k": 4, "codebook": "mul1"}) == Q.CLAIM_BY_MARKER
+    assert Q.claims({"quant_method": "fp8"}) == Q.CLAIM_NO
+    assert Q.claims("{") == Q.CLAIM_NO
+    assert Q.claims("[]") == Q.CLAIM_NO
+    assert Q.claims("") == Q.CLAIM_NO
+
+
+def test_validate_refuses_by_name():
+    Q.validate(DS41_BLOCK)
+    Q.validate({"format": "exl3", "codebook": "mul1", "window": 16, "k": 3})
+    for cb in ("mcg", "3inst"):
+        with pytest.raises(Q.Exl3Error) as e:
+            Q.validate({"quant_method": "exl3", "codebook": cb})
+        assert e.value.code == L.EXL3_UNSUPPORTED and "codebook is not mul1" in e.value.why
+    with pytest.raises(Q.Exl3Error, match="Exl3WindowUnsupported"):
+        Q.validate({"format": "exl3", "codebook": "mul1", "window": 20})
+    with pytest.raises(Q.Exl3Error, match="narrowed"):
+        Q.validate({"format": "exl3", "codebook": "mul1", "window": 12})
+    with pytest.raises(Q.Exl3Error, match="Exl3RateUnsupported"):
+        Q.validate({"format": "exl3", "codebook": "mul1", "k": 9.25})
+    with pytest.raises(Q.Exl3Error, match="fractional"):
+        Q.validate({"format": "exl3", "codebook": "mul1", "k": 2.5})
+    with pytest.raises(Q.Exl3Error, match="not an exllamav3 block"):
+        Q.validate({"format": "gptq", "codebook": "mul1"})
+    with pytest.raises(Q.Exl3Error, match="not a JSON object"):
+        Q.validate("{")
+
+
+def test_validate_on_the_reference_pack_configs():
+    # turboexl3_qwen38/tests/fixtures/k{2,3,4,5}.json carry these trunk/expert blocks (integer K)
+    for k in (2, 3, 4, 5):
+        Q.validate({"format": "exl3", "codebook": "mul1", "window": 16,
+                    "source": f"turboderp/Qwen3.8-Flash-Next-exl3@{k}.05bpw"})
+        Q.validate({"format": "exl3", "k": k, "codebook": "mul1"})
+
+
+def test_bill_is_the_stored_bytes():
+    assert Q.bill(DS41_BLOCK, "/nowhere", 123456789) == 123456789
+    assert Q.bill(DS41_BLOCK, "", 0) == 0
+
+
+def test_moe_entry_refuses_by_name_without_a_gpu_call():
+    v = L.lib().exl3_moe(None, None, None, None, 0, None, None)
+    assert v.code == L.EXL3_UNSUPPORTED and b"swiglu" in v.why
+
+
+def test_matmul_rejects_a_null_weight_before_any_launch():
+    v = L.lib().exl3_matmul(ctypes.POINTER(L.Weight)(), None, None, None)
+    assert v.code == L.EXL3_FAILED
