@@ -291,7 +291,7 @@ def main() -> None:
         with torch.cuda.graph(graph, stream=s):
             step()
         torch.cuda.synchronize()
-        launches_per_step = LAYERS * len(GROUPS) * 2  # prep + GEMV per launch group
+        launches_per_step = LAYERS * len(GROUPS)  # one decode-GEMV launch per launch group
 
         for _ in range(warmup):
             graph.replay()
@@ -395,7 +395,7 @@ def main() -> None:
             "decode_tok_s": round(args.batch / (r1["ms"] * 1e-3), 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
-                         "kernel": "gate|up decode GEMV (4096 -> 2x12288 @ 3 bpw, prep + stream-K launch)",
+                         "kernel": "gate|up decode GEMV (4096 -> 2x12288 @ 3 bpw, one stream-K launch)",
                          "bytes_per_launch": gu_bytes, "ms_per_launch": round(r1["dom_ms"], 5),
                          "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
             "roofline_4bpw_qkv": {"achieved": round(qkv_bytes / (r1["qkv_ms"] * 1e-3) / 1e9, 1),

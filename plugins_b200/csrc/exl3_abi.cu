@@ -182,18 +182,16 @@ struct DeviceState {
   bool ready = false;
   uint8_t* base = nullptr;
   size_t bytes = 0;
-  uint8_t* xpf = nullptr;
   float* partials = nullptr;
+  size_t partial_floats = 0;
   uint32_t* counters = nullptr;
   uint32_t* err = nullptr;
   int sms = 0;
-  int max_ctas = 0;
 };
 
 constexpr int kMaxDevices = 64;
-constexpr size_t kXpfBytes = 8u << 20;        // prepared activations: nseg * in/16 * 512 bytes
-constexpr size_t kCounterCount = 8192;        // out / 128 <= 8192
-constexpr int kCtasPerSm = 8;                 // partials capacity per SM (>= the GEMV partition's CTAs per SM)
+constexpr size_t kCounterCount = 8192;           // out / 128 <= 8192
+constexpr size_t kPartialBytes = 128u << 20;     // decode-GEMV split partials
 
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
@@ -229,14 +227,12 @@ exl3_verdict ensure_device(int dev) {
   if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return refuse(EXL3_FAILED, "exl3_b200: no CUDA device");
   if (prop.major != 10) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the kernels are built for sm_100a (B200) only");
   d.sms = prop.multiProcessorCount;
-  d.max_ctas = d.sms * kCtasPerSm;
-  const size_t partial_bytes = static_cast<size_t>(d.max_ctas) * 2 * 16 * 128 * 4;
   const size_t counter_bytes = kCounterCount * 4;
-  d.bytes = kXpfBytes + partial_bytes + counter_bytes + 256;
+  d.bytes = kPartialBytes + counter_bytes + 256;
   if (cudaMalloc(&d.base, d.bytes) != cudaSuccess) return refuse(EXL3_TOO_LARGE, "exl3_b200: workspace allocation failed");
-  d.xpf = d.base;
-  d.partials = reinterpret_cast<float*>(d.base + kXpfBytes);
-  d.counters = reinterpret_cast<uint32_t*>(d.base + kXpfBytes + partial_bytes);
+  d.partials = reinterpret_cast<float*>(d.base);
+  d.partial_floats = kPartialBytes / 4;
+  d.counters = reinterpret_cast<uint32_t*>(d.base + kPartialBytes);
   if (cudaMemset(d.counters, 0, counter_bytes) != cudaSuccess) return refuse(EXL3_FAILED, "exl3_b200: workspace init failed");
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err), exl3::g_device_error) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_b200: error word lookup failed");
@@ -261,8 +257,6 @@ exl3_verdict check_linear_shape(int groups, int in_f, int out_f, int n) {
   if (!rate_served(n))
     return refuse(EXL3_UNSUPPORTED, "exl3_b200: fractional or >6-bit rates are not served by the sm_100a kernels");
   if (out_f / 128 > static_cast<int>(kCounterCount)) return refuse(EXL3_TOO_LARGE, "exl3_b200: out_features too large");
-  if (static_cast<size_t>(in_f / 16) * 512 * exl3::kMaxSegments > kXpfBytes)
-    return refuse(EXL3_TOO_LARGE, "exl3_b200: in_features too large");
   return kOk;
 }
 
@@ -368,7 +362,7 @@ exl3_verdict check_weight(const exl3_weight* w) {
   return check_linear_shape(w->groups, w->in_features, w->out_features, w->n);
 }
 
-// One decode-GEMV pass (prep + stream-K kernel) per group and per 16 rows.
+// One decode-GEMV launch per group and per 16 rows.
 exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, int64_t rows, void* y, int32_t y_dtype,
                         uint32_t flags, cudaStream_t st) {
   DeviceState* d = device_state(w->device);
@@ -386,25 +380,14 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
     for (int64_t r0 = 0; r0 < rows; r0 += exl3::kMaxRows) {
       const int rc = static_cast<int>(rows - r0 < exl3::kMaxRows ? rows - r0 : exl3::kMaxRows);
       const int rg = rc <= 8 ? 1 : 2;
-      exl3::PrepParams pp{};
-      const int64_t x_stride = grouped ? static_cast<int64_t>(groups) * in_f : in_f;
-      pp.x = static_cast<const uint8_t*>(x) + (static_cast<size_t>(r0) * x_stride + static_cast<size_t>(g) * in_f) * xsz;
-      pp.x_dtype = x_dtype;
-      pp.x_row_stride = x_stride;
-      pp.suh = w->suh + static_cast<size_t>(g) * w->nseg * in_f;
-      pp.xpf = d->xpf;
-      pp.in_features = in_f;
-      pp.rows = rc;
-      pp.row_groups = rg;
-      pp.nseg = w->nseg;
-      pp.prepared = (flags & EXL3_MATMUL_PREPARED) ? 1 : 0;
-      pp.imma_order = imma ? 1 : 0;
-      if (exl3::launch_prep(pp, st, true) != cudaSuccess)
-        return refuse(EXL3_FAILED, "exl3_b200: prep launch failed");
       exl3::GemvParams gp{};
+      const int64_t x_stride = grouped ? static_cast<int64_t>(groups) * in_f : in_f;
       gp.trellis = w->trellis + static_cast<size_t>(g) * tile_halfs;
+      gp.suh = w->suh + static_cast<size_t>(g) * w->nseg * in_f;
       gp.svh = w->svh + static_cast<size_t>(g) * out_f;
-      gp.xpf = d->xpf;
+      gp.x = static_cast<const uint8_t*>(x) + static_cast<size_t>(g) * in_f * xsz;
+      gp.x_dtype = x_dtype;
+      gp.x_row_stride = x_stride;
       const int64_t y_stride = grouped ? static_cast<int64_t>(groups) * out_f : out_f;
       gp.y = static_cast<uint8_t*>(y) + static_cast<size_t>(g) * out_f * ysz;
       gp.y_dtype = y_dtype;
@@ -419,9 +402,12 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
       gp.rows = rc;
       gp.nseg = w->nseg;
       for (int s = 0; s <= w->nseg; ++s) gp.seg_cb[s] = w->seg_cols[s] / 128;
+      for (int s = w->nseg + 1; s <= exl3::kMaxSegments; ++s) gp.seg_cb[s] = gp.seg_cb[w->nseg];
+      gp.prepared = (flags & EXL3_MATMUL_PREPARED) ? 1 : 0;
       gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
-      gp.max_ctas = d->max_ctas;
-      if (exl3::launch_gemv(gp, K, rg, imma, d->sms, st, true) != cudaSuccess)
+      const char* why = nullptr;
+      if (!exl3::gemv_geometry(gp, d->sms, rg, d->partial_floats, &why)) return refuse(EXL3_TOO_LARGE, why);
+      if (exl3::launch_gemv(gp, K, rg, imma, st, true) != cudaSuccess)
         return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
     }
   }

@@ -81,11 +81,4 @@ cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int ou
               : launch_dd<false>(trellis, in_features, out_features, n / 16, out, st);
 }
 
-size_t gemv_workspace_bytes(int in_features, int out_features, int nseg, int max_ctas) {
-  const size_t xpf = static_cast<size_t>(nseg) * (in_features / 16) * 2 * 256;  // row_groups <= 2
-  const size_t partials = static_cast<size_t>(max_ctas) * 2 * 16 * 128 * 4;
-  const size_t counters = static_cast<size_t>(out_features / 128) * 4;
-  return xpf + partials + counters + 3 * 256;
-}
-
 }  // namespace exl3

@@ -8,36 +8,37 @@ namespace exl3 {
 constexpr int kMaxSegments = 4;  // linears stacked into one launch (the reference's SHARED_MAX, linear.zig:39-40)
 constexpr int kMaxRows = 16;     // decode-GEMV rows per launch (two m16n8k16 row groups)
 
-struct PrepParams {
-  const void* x;            // [rows][x_row_stride] activations
-  int32_t x_dtype;          // exl3::DType
-  int64_t x_row_stride;     // elements
-  const uint16_t* suh;      // [nseg][in] f16 bits (unused when prepared)
-  uint8_t* xpf;             // [nseg][in/16][row_groups][32][4] f16 fragments
-  int32_t in_features, rows, row_groups, nseg;
-  int32_t prepared;         // x already holds f16(H(x*suh)/sqrt(128)): copy only
-  int32_t imma_order;       // fragment order of the IMMA decode (else dp4a order)
-};
+constexpr int kGemvCtasPerSm = 3;  // the decode GEMV's persistent grid: CTAs per SM (fixed: rows and byte-sum path
+                                   // do not change a row's sum order)
 
 struct GemvParams {
   const uint16_t* trellis;  // [in/16][out/16][n]
+  const uint16_t* suh;      // [nseg][in] f16 bits (unused when prepared)
   const uint16_t* svh;      // [out] f16 bits
-  const uint8_t* xpf;       // from the prep kernel
+  const void* x;            // [rows_total][x_row_stride] activations of the whole call
+  int32_t x_dtype;          // exl3::DType
+  int64_t x_row_stride;     // elements
   void* y;                  // one segment: y[row][col] at row * y_row_stride; several: [rows_total][width_s] each,
   int32_t y_dtype;          //   segments back to back
   int64_t y_row_stride;     // elements (single segment)
   int32_t row0, rows_total; // this launch's first row, and all rows of the call
-  float* partials;          // [grid][2][16][128]
+  float* partials;          // split partials, [pair][contributor][rows][128]
   uint32_t* counters;       // [out/128], zero between launches
   uint32_t* err;            // device error word
   int32_t in_features, out_features, rows, nseg;
   int32_t seg_cb[kMaxSegments + 1];  // segment bounds in 128-column blocks
+  int32_t prepared;         // x already holds f16(H(x*suh)/sqrt(128)): no rotation
   int32_t inner_only;       // skip the output Hadamard and svh: y = the f32 inner product
-  int32_t max_ctas;         // grid cap (the partials buffer's capacity)
+  // geometry (gemv_geometry)
+  int32_t kt, kr, kc;       // 16-row slabs, slabs per chunk, chunks
+  int32_t contrib_max;      // most CTAs contributing to one (segment, chunk, column block)
+  int64_t xp_bytes;         // shared memory for the rotated activations a share touches
+  int32_t grid;
 };
 
-cudaError_t launch_prep(const PrepParams& p, cudaStream_t st, bool pdl);
-cudaError_t launch_gemv(const GemvParams& p, int K, int row_groups, bool imma, int sms, cudaStream_t st, bool pdl);
+// Fills the geometry fields of `p` for `sms` SMs; false (with a reason) when the shape does not fit one launch.
+bool gemv_geometry(GemvParams& p, int sms, int row_groups, size_t partial_capacity_floats, const char** why);
+cudaError_t launch_gemv(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl);
 
 // decode a whole trellis to W_hat (f16 bits, row-major [in][out]); one warp per tile
 cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
@@ -47,7 +48,5 @@ cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int ou
 cudaError_t launch_encode(const float* target, int in_features, int out_features, int n, uint16_t* trellis,
                           cudaStream_t st);
 
-// workspace sizes of one decode-GEMV launch
-size_t gemv_workspace_bytes(int in_features, int out_features, int nseg, int max_ctas);
 
 }  // namespace exl3
