@@ -198,6 +198,16 @@ exl3_verdict exl3_decode_dense(const exl3_weight *w, int32_t group, uint16_t *ou
 exl3_verdict exl3_encode_trellis(const float *target, int32_t in_features, int32_t out_features, int32_t n,
                                  uint16_t *trellis, void *stream);
 
+/* matmul without any allocation (no counterpart in the reference): for hosts that cannot let a library call
+ * cudaMalloc -- a server that reserves its device memory up front and admits nothing beyond its memory bill, or an
+ * embedding runtime whose own allocator owns every device byte.  Same result as exl3_matmul, but the scratch (split
+ * partials, counters) lives in one static device array of 8 MiB + 32 KiB that every device loading the library holds
+ * until exit; the weight struct may be filled by hand (no exl3_weight_view needed).  One ungrouped weight (stacked
+ * segments allowed).  A layer needing more partials than the array holds is refused with EXL3_TOO_LARGE.  The first
+ * call on a device looks the array up (cudaGetSymbolAddress) and clears its counters: make it before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race -- order them on one stream. */
+exl3_verdict exl3_matmul_noalloc(const exl3_weight *w, const exl3_tensor *x, void *stream, exl3_tensor *out);
+
 /* Device error bits the kernels recorded on `device` (bounded waits that gave up); `clear` resets them. */
 exl3_verdict exl3_device_error(int32_t device, uint32_t *bits, int32_t clear);
 

@@ -24,7 +24,8 @@ MAX_SEGMENTS = 4
 EXPORTS = (
     "exl3_claims", "exl3_validate", "exl3_bill", "exl3_open", "exl3_close", "exl3_load_tensor", "exl3_load_bank",
     "exl3_release", "exl3_matmul", "exl3_moe", "exl3_swiglu", "exl3_matmul_ex", "exl3_weight_view",
-    "exl3_weight_stack", "exl3_decode_dense", "exl3_encode_trellis", "exl3_device_error", "exl3_version",
+    "exl3_weight_stack", "exl3_decode_dense", "exl3_encode_trellis", "exl3_matmul_noalloc", "exl3_device_error",
+    "exl3_version",
 )
 
 
@@ -147,6 +148,8 @@ def lib() -> ctypes.CDLL:
             L.exl3_encode_trellis.restype = Verdict
             L.exl3_encode_trellis.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_void_p, ctypes.c_void_p]
+            L.exl3_matmul_noalloc.restype = Verdict
+            L.exl3_matmul_noalloc.argtypes = [P(Weight), P(Tensor), ctypes.c_void_p, P(Tensor)]
             L.exl3_device_error.restype = Verdict
             L.exl3_device_error.argtypes = [ctypes.c_int32, P(ctypes.c_uint32), ctypes.c_int32]
             L.exl3_version.restype = ctypes.c_char_p
