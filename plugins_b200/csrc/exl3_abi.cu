@@ -602,6 +602,10 @@ exl3_verdict exl3_weight_view(uint16_t* trellis, uint16_t* suh, uint16_t* svh, i
   out->device = device;
   out->nseg = 1;
   out->seg_cols[1] = out_features;
+  if (groups > 1) {  // a bank: make sure the routed-expert path has its workspace
+    v = exl3::moe_reserve(device, in_features, out_features);
+    if (v.code != EXL3_OK) return v;
+  }
   return kOk;
 }
 

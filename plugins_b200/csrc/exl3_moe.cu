@@ -1,13 +1,555 @@
-// exl3_moe.cu -- routed SwiGLU experts (placeholder until the grouped expert kernels land).
+// exl3_moe.cu -- routed SwiGLU experts (the reference's swiglu seam, plugins/turboexl3_ds41/plugin.zig:267-283;
+// SX/root.zig:32-167; the decode chain of SX/expert_exl3_kernels.zig:2274-2650).
+//
+// Per (row r, top-k slot k), e = inds[r, k]:
+//   g = gate_e(x_r), u = up_e(x_r)                        (EXL3 linears: prepare, decode GEMV, finish)
+//   g = min(g, limit), u = clamp(u, -limit, limit)        when limit > 0   (MID_SOURCE's CLAMP_LIMIT)
+//   h = silu(g) * u
+//   y_r = sum_k score[r, k] * down_e(h)                   f32, k order (REDUCE_SOURCE)
+//
+// B200 plan, five launches chained with programmatic dependent launch, rows in passes of 512 / topk:
+//   1. route    -- one CTA: a stable counting sort of the slots by expert (deterministic), cut into chunks of at
+//                  most 8 slots of one expert (the MMA's N), the active chunk list on the device;
+//   2. prepare  -- each chunk's rows rotated for gate and for up (suh, 128-wide Hadamard, f16) into B-fragment order;
+//   3. gate|up  -- a persistent decode GEMV over (chunk, 128-column block of the intermediate) units that streams
+//                  the expert's gate and up tiles together (both contiguous per k slab), accumulates both, and in
+//                  the epilogue applies both finishes, the clamp, SwiGLU and the down projection's prepare (its
+//                  128-wide input block is exactly this column block), writing the down GEMV's B fragments;
+//   4. down     -- the same GEMV over (chunk, 128-column block of the hidden size), finishing to f32 per slot;
+//   5. combine  -- y_r = sum_k score * d in k order, in x's dtype.
+// No unit splits K, so there are no partials and the result does not depend on the grid.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "exl3_common.cuh"
+#include "exl3_internal.h"
 #include "exl3_moe.h"
 
 namespace exl3 {
 
-exl3_verdict moe_reserve(int, int, int) { return {EXL3_OK, nullptr}; }
+namespace {
 
-exl3_verdict moe_swiglu(const exl3_weight*, const exl3_weight*, const exl3_weight*, const exl3_tensor*,
-                        const exl3_tensor*, const exl3_tensor*, const exl3_swiglu_opts*, void*, exl3_tensor*) {
-  return {EXL3_UNSUPPORTED, "exl3_b200: routed SwiGLU is not built yet"};
+constexpr int kMaxTopK = 32;       // the reference's REDUCE_MAX_TOPK (SX/expert_exl3_kernels.zig:2593)
+constexpr int kMaxSlots = 512;     // (row, k) slots per pass: a pass takes kMaxSlots / topk rows
+constexpr int kChunkRows = 8;      // slots per chunk: the MMA's N
+constexpr int kWarpsM = 4;
+constexpr int kStagesM = 4;
+constexpr int kRedStrideM = 132;
+
+struct MoeParams {
+  // banks: trellis [E][in/16][out/16][n], suh [E][in], svh [E][out]
+  const uint16_t *g_tr, *g_suh, *g_svh;
+  const uint16_t *u_tr, *u_suh, *u_svh;
+  const uint16_t *d_tr, *d_suh, *d_svh;
+  int32_t experts, hidden, inter;
+  const void* x;      // [rows][hidden]
+  int32_t x_dtype;
+  const void* inds;   // [rows][topk]
+  int32_t inds_u32;
+  const float* scores;  // [rows][topk] f32
+  void* y;            // [rows][hidden]
+  int32_t rows, topk, row0;  // this pass: rows row0 .. row0 + rows - 1 of the call
+  float limit;
+  // scratch
+  int32_t* order;      // [kMaxSlots] slot ids sorted by expert (stable)
+  int32_t* chunk_e;    // [kMaxSlots] chunk -> expert
+  int32_t* chunk_s;    // [kMaxSlots] chunk -> first position in `order`
+  int32_t* chunk_n;    // [kMaxSlots] chunk -> slots
+  int32_t* nchunks;    // [1]
+  int32_t* bad;        // [1] an expert index out of range was seen
+  uint8_t* xg;         // [chunk][hidden/16][256 B] gate-prepared rows
+  uint8_t* xu;         // [chunk][hidden/16][256 B] up-prepared rows
+  uint8_t* hp;         // [chunk][inter/16][256 B] down-prepared rows
+  float* dout;         // [kMaxSlots][hidden] down outputs per slot (position in `order`)
+};
+
+__device__ __forceinline__ int slot_expert(const MoeParams& p, int slot) {
+  const int r = slot / p.topk, k = slot % p.topk;
+  const size_t at = static_cast<size_t>(p.row0 + r) * p.topk + k;
+  return p.inds_u32 ? static_cast<int>(static_cast<const uint32_t*>(p.inds)[at]) : static_cast<const int32_t*>(p.inds)[at];
+}
+
+// fragment position (IMMA order) of input element kk (0..15) of row g in a slab: halves
+__device__ __forceinline__ int frag_half(int g, int kk) { return (g * 4 + (kk >> 2)) * 4 + (kk & 3); }
+
+// ---------------------------------------------------------------- 1. route
+
+__global__ void __launch_bounds__(1024) moe_route_kernel(MoeParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ int s_cnt[1024], s_off[1025];
+  const int tid = threadIdx.x;
+  const int S = p.rows * p.topk;
+  const int E = p.experts;
+  for (int e = tid; e < E; e += blockDim.x) s_cnt[e] = 0;
+  if (tid == 0) *p.bad = 0;
+  __syncthreads();
+  for (int s = tid; s < S; s += blockDim.x) {
+    const int e = slot_expert(p, s);
+    if (e < 0 || e >= E) atomicExch(p.bad, 1);
+    else atomicAdd(&s_cnt[e], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0, nch = 0;
+    for (int e = 0; e < E; ++e) {
+      s_off[e] = acc;
+      for (int c = 0; c < s_cnt[e]; c += kChunkRows) {
+        p.chunk_e[nch] = e;
+        p.chunk_s[nch] = acc + c;
+        p.chunk_n[nch] = min(kChunkRows, s_cnt[e] - c);
+        ++nch;
+      }
+      acc += s_cnt[e];
+    }
+    s_off[E] = acc;
+    *p.nchunks = nch;
+    // stable placement: slots in index order
+    for (int s = 0; s < S; ++s) {
+      const int e = slot_expert(p, s);
+      if (e >= 0 && e < E) p.order[s_off[e]++] = s;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- 2. prepare gate / up inputs
+
+// grid: (hidden/128 blocks, kMaxSlots chunks); warp w of the block handles rows w, w+4 of the chunk
+__global__ void __launch_bounds__(128) moe_prep_kernel(MoeParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int chunk = blockIdx.y;
+  if (chunk >= *p.nchunks) return;
+  const int e = p.chunk_e[chunk], s0 = p.chunk_s[chunk], n = p.chunk_n[chunk];
+  const int blk = blockIdx.x;
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  const int KT = p.hidden / 16;
+  for (int g = warp; g < kChunkRows; g += 4) {
+    for (int which = 0; which < 2; ++which) {
+      const uint16_t* suh = (which == 0 ? p.g_suh : p.u_suh) + static_cast<size_t>(e) * p.hidden;
+      uint8_t* dst = (which == 0 ? p.xg : p.xu) + static_cast<size_t>(chunk) * KT * 256;
+      float v[4];
+      if (g < n) {
+        const int row = p.order[s0 + g] / p.topk;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const size_t k = static_cast<size_t>(blk) * 128 + lane + 32 * i;
+          v[i] = load_act(p.x, static_cast<size_t>(p.row0 + row) * p.hidden + k, p.x_dtype) * f16_bits_to_float(suh[k]);
+        }
+        fwht128_warp(v, lane);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = 0.0f;
+      }
+      __half* h = reinterpret_cast<__half*>(dst);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int kin = lane + 32 * i;
+        const int t = blk * 8 + (kin >> 4);
+        h[static_cast<size_t>(t) * 128 + frag_half(g, kin & 15)] = __float2half_rn(v[i] * kHadScale);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- 3/4. the grouped decode GEMV
+
+__device__ __forceinline__ void cp16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// PAIR: units (chunk, intermediate column block), weights gate+up, epilogue SwiGLU + down prepare.
+// !PAIR: units (chunk, hidden column block), weight down, epilogue finish to f32.
+template <int K, bool PAIR>
+__global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) {
+  constexpr uint32_t kTileBytes = 32u * K;
+  constexpr uint32_t kW = 8u * kTileBytes;                // one weight's tiles of a unit slab
+  constexpr uint32_t kSlab = (PAIR ? 2u : 1u) * (kW + 256u);  // tiles + x fragments, per weight
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+  uint8_t* ring = smem + warp * (kStagesM * kSlab);
+  float* red = reinterpret_cast<float*>(smem + kWarpsM * kStagesM * kSlab);  // [2][W][8][stride]
+  const int in_f = PAIR ? p.hidden : p.inter;
+  const int out_f = PAIR ? p.inter : p.hidden;
+  const int KT = in_f / 16, CB = out_f / 128;
+  const size_t wstride = static_cast<size_t>(in_f / 16) * (out_f / 16) * kTileBytes;  // bytes per expert
+  const uint8_t* tra = reinterpret_cast<const uint8_t*>(PAIR ? p.g_tr : p.d_tr);
+  const uint8_t* trb = reinterpret_cast<const uint8_t*>(p.u_tr);
+  const uint8_t* xa = PAIR ? p.xg : p.hp;
+  const uint8_t* xb = p.xu;
+
+  pdl_launch_dependents();
+  pdl_wait();  // the chunk table and the prepared inputs come from the previous launches
+  const int units = *p.nchunks * CB;
+  LaneWindows<K> lwin;
+  lwin.init(lane);
+  ImmaIndicator ind;
+  ind.init(lane);
+  const uint32_t g = lane >> 2, q = lane & 3u;
+
+  for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+    const int chunk = unit / CB, cb = unit % CB;
+    const int e = p.chunk_e[chunk], s0 = p.chunk_s[chunk], nrow = p.chunk_n[chunk];
+    const uint8_t* wa = tra + e * wstride + static_cast<size_t>(cb) * 8u * kTileBytes;
+    const uint8_t* wb = trb + e * wstride + static_cast<size_t>(cb) * 8u * kTileBytes;
+    const uint8_t* xca = xa + static_cast<size_t>(chunk) * KT * 256;
+    const uint8_t* xcb = xb + static_cast<size_t>(chunk) * KT * 256;
+    const size_t rowstride = static_cast<size_t>(CB) * 8u * kTileBytes;  // bytes between k slabs
+    const uint32_t mine = (static_cast<uint32_t>(KT) > warp) ? (KT - warp + kWarpsM - 1) / kWarpsM : 0u;
+    auto issue = [&](uint32_t i) {
+      if (i >= mine) return;
+      const uint32_t t = warp + kWarpsM * i;
+      uint8_t* dst = ring + (i % kStagesM) * kSlab;
+#pragma unroll
+      for (uint32_t c = lane; c < kW / 16u; c += 32u) cp16(dst + c * 16u, wa + t * rowstride + c * 16u);
+      if (lane < 16u) cp16(dst + kW + lane * 16u, xca + static_cast<size_t>(t) * 256 + lane * 16u);
+      if constexpr (PAIR) {
+        uint8_t* d2 = dst + kW + 256u;
+#pragma unroll
+        for (uint32_t c = lane; c < kW / 16u; c += 32u) cp16(d2 + c * 16u, wb + t * rowstride + c * 16u);
+        if (lane < 16u) cp16(d2 + kW + lane * 16u, xcb + static_cast<size_t>(t) * 256 + lane * 16u);
+      }
+    };
+    for (uint32_t i = 0; i + 1 < static_cast<uint32_t>(kStagesM); ++i) {
+      issue(i);
+      cp_commit();
+    }
+    float acc[PAIR ? 2 : 1][8][4];
+#pragma unroll
+    for (int w2 = 0; w2 < (PAIR ? 2 : 1); ++w2)
+#pragma unroll
+      for (int t = 0; t < 8; ++t)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[w2][t][c] = 0.0f;
+    for (uint32_t i = 0; i < mine; ++i) {
+      cp_wait<kStagesM - 2>();
+      __syncwarp();
+      const uint8_t* st = ring + (i % kStagesM) * kSlab;
+#pragma unroll
+      for (int w2 = 0; w2 < (PAIR ? 2 : 1); ++w2) {
+        const uint8_t* sw = st + w2 * (kW + 256u);
+        const uint2 xv = reinterpret_cast<const uint2*>(sw + kW)[lane];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          uint32_t w[8], a[4];
+          lane_codewords<K>(reinterpret_cast<const uint32_t*>(sw) + t * (kTileBytes / 4u), lwin, w);
+          decode_afrag_imma(w, ind, a);
+          mma_16816(acc[w2][t], a, xv.x, xv.y);
+        }
+      }
+      __syncwarp();
+      issue(i + kStagesM - 1);
+      cp_commit();
+    }
+    cp_wait<0>();
+    // warps' partials -> shared, summed in warp order
+#pragma unroll
+    for (int w2 = 0; w2 < (PAIR ? 2 : 1); ++w2) {
+      float* rw = red + (w2 * kWarpsM + warp) * 8 * kRedStrideM;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const int col = 16 * t + static_cast<int>(g), row = 2 * static_cast<int>(q);
+        rw[row * kRedStrideM + col] = acc[w2][t][0];
+        rw[(row + 1) * kRedStrideM + col] = acc[w2][t][1];
+        rw[row * kRedStrideM + col + 8] = acc[w2][t][2];
+        rw[(row + 1) * kRedStrideM + col + 8] = acc[w2][t][3];
+      }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < (PAIR ? 2 : 1) * 8 * 128; idx += kWarpsM * 32) {
+      const int w2 = idx / 1024, row = (idx / 128) % 8, col = idx % 128;
+      float v = 0.0f;
+#pragma unroll
+      for (int w3 = 0; w3 < kWarpsM; ++w3) v += red[((w2 * kWarpsM + w3) * 8 + row) * kRedStrideM + col];
+      red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
+    }
+    __syncthreads();
+    // epilogue: one warp per slot row
+    for (int row = static_cast<int>(warp); row < nrow; row += kWarpsM) {
+      float va[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) va[i] = red[row * kRedStrideM + lane + 32 * i];
+      fwht128_warp(va, lane);
+      const size_t ce = static_cast<size_t>(cb) * 128;
+      if constexpr (PAIR) {
+        float vb[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) vb[i] = red[((kWarpsM * 8) + row) * kRedStrideM + lane + 32 * i];
+        fwht128_warp(vb, lane);
+        float h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const size_t c = ce + lane + 32 * i;
+          float gv = va[i] * kHadScale * f16_bits_to_float(p.g_svh[static_cast<size_t>(e) * p.inter + c]);
+          float uv = vb[i] * kHadScale * f16_bits_to_float(p.u_svh[static_cast<size_t>(e) * p.inter + c]);
+          if (p.limit > 0.0f) {
+            gv = fminf(gv, p.limit);
+            uv = fminf(fmaxf(uv, -p.limit), p.limit);
+          }
+          const float sig = 1.0f / (1.0f + __expf(-gv));
+          h[i] = gv * sig * uv * f16_bits_to_float(p.d_suh[static_cast<size_t>(e) * p.inter + c]);
+        }
+        fwht128_warp(h, lane);
+        __half* dst = reinterpret_cast<__half*>(p.hp + static_cast<size_t>(chunk) * (p.inter / 16) * 256);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int kin = lane + 32 * i;
+          const int t = cb * 8 + (kin >> 4);
+          dst[static_cast<size_t>(t) * 128 + frag_half(row, kin & 15)] = __float2half_rn(h[i] * kHadScale);
+        }
+      } else {
+        float* dst = p.dout + static_cast<size_t>(s0 + row) * p.hidden;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const size_t c = ce + lane + 32 * i;
+          dst[c] = va[i] * kHadScale * f16_bits_to_float(p.d_svh[static_cast<size_t>(e) * p.hidden + c]);
+        }
+      }
+    }
+    if constexpr (PAIR) {
+      // rows of the chunk beyond its slots stay zero in the down GEMV's fragments
+      if (static_cast<int>(warp) == 0 && nrow < kChunkRows) {
+        __half* dst = reinterpret_cast<__half*>(p.hp + static_cast<size_t>(chunk) * (p.inter / 16) * 256);
+        for (int idx = lane; idx < 8 * 16 * kChunkRows; idx += 32) {
+          const int row = idx / 128, kin = idx % 128;
+          if (row >= nrow) dst[static_cast<size_t>(cb * 8 + (kin >> 4)) * 128 + frag_half(row, kin & 15)] = __float2half_rn(0.0f);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------- 5. combine
+
+// grid: (hidden/128, rows); y[r] = sum_k score[r,k] * dout[pos(r,k)], k in order
+__global__ void __launch_bounds__(128) moe_combine_kernel(MoeParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ int s_pos[kMaxTopK];
+  const int r = blockIdx.y;
+  const int S = p.rows * p.topk;
+  if (threadIdx.x < static_cast<unsigned>(p.topk)) {
+    // position of slot (r, k) in the sorted order
+    const int slot = r * p.topk + threadIdx.x;
+    int pos = -1;
+    for (int i = 0; i < S; ++i)
+      if (p.order[i] == slot) pos = i;
+    s_pos[threadIdx.x] = pos;
+  }
+  __syncthreads();
+  const size_t c = static_cast<size_t>(blockIdx.x) * 128 + threadIdx.x;
+  float acc = 0.0f;
+  for (int k = 0; k < p.topk; ++k) {
+    const int pos = s_pos[k];
+    if (pos >= 0) acc += p.scores[static_cast<size_t>(p.row0 + r) * p.topk + k] * p.dout[static_cast<size_t>(pos) * p.hidden + c];
+  }
+  store_act(p.y, static_cast<size_t>(p.row0 + r) * p.hidden + c, acc, p.x_dtype);
+}
+
+// ---------------------------------------------------------------- host
+
+struct MoeScratch {
+  bool ready = false;
+  uint8_t* base = nullptr;
+  size_t bytes = 0;
+  int hidden = 0, inter = 0;
+  int sms = 0;
+};
+constexpr int kMaxDev = 64;
+std::mutex g_moe_mu;
+MoeScratch g_moe[kMaxDev];
+
+size_t scratch_bytes(int hidden, int inter) {
+  const size_t ints = 4 * kMaxSlots + 64;
+  const size_t xs = 2 * static_cast<size_t>(kMaxSlots) * (hidden / 16) * 256;
+  const size_t hs = static_cast<size_t>(kMaxSlots) * (inter / 16) * 256;
+  const size_t ds = static_cast<size_t>(kMaxSlots) * hidden * 4;
+  return ints * 4 + xs + hs + ds + 4 * 256;
+}
+
+exl3_verdict refuse_m(int32_t code, const char* why) { return {code, why}; }
+
+template <int K, bool PAIR>
+cudaError_t launch_moe_gemv(const MoeParams& p, int grid, cudaStream_t st) {
+  auto kern = moe_gemv_kernel<K, PAIR>;
+  constexpr size_t slab = (PAIR ? 2u : 1u) * (8u * 32u * K + 256u);
+  const size_t smem = kWarpsM * kStagesM * slab + (PAIR ? 2 : 1) * kWarpsM * 8 * kRedStrideM * 4;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kWarpsM * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <bool PAIR>
+cudaError_t launch_moe_gemv_k(const MoeParams& p, int K, int grid, cudaStream_t st) {
+  switch (K) {
+    case 1: return launch_moe_gemv<1, PAIR>(p, grid, st);
+    case 2: return launch_moe_gemv<2, PAIR>(p, grid, st);
+    case 3: return launch_moe_gemv<3, PAIR>(p, grid, st);
+    case 4: return launch_moe_gemv<4, PAIR>(p, grid, st);
+    case 5: return launch_moe_gemv<5, PAIR>(p, grid, st);
+    case 6: return launch_moe_gemv<6, PAIR>(p, grid, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename Kern>
+cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, const MoeParams& p, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+bool bank_ok(const exl3_weight* w, int in_f, int out_f) {
+  return w && w->size == sizeof(exl3_weight) && w->trellis && w->suh && w->svh && w->nseg == 1 &&
+         w->in_features == in_f && w->out_features == out_f && w->n % 16 == 0 && w->n >= 16 && w->n <= 96 &&
+         (reinterpret_cast<uintptr_t>(w->trellis) & 15u) == 0;
+}
+
+}  // namespace
+
+exl3_verdict moe_reserve(int device, int in_features, int out_features) {
+  if (device < 0 || device >= kMaxDev) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: device index out of range");
+  // a bank is either gate/up (hidden -> inter) or down (inter -> hidden): reserve for the larger of each dim
+  std::lock_guard<std::mutex> lk(g_moe_mu);
+  MoeScratch& s = g_moe[device];
+  const int hidden = in_features > out_features ? in_features : out_features;
+  const int inter = in_features < out_features ? in_features : out_features;
+  const int nh = hidden > s.hidden ? hidden : s.hidden, ni = inter > s.inter ? inter : s.inter;
+  // inter may exceed hidden in another model: size both dims for the larger
+  const int m = nh > ni ? nh : ni;
+  const size_t need = scratch_bytes(m, m);
+  if (s.ready && need <= s.bytes) return {EXL3_OK, nullptr};
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  if (s.base) {
+    cudaDeviceSynchronize();
+    cudaFree(s.base);
+    s.base = nullptr;
+  }
+  cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, device);
+  const bool ok = cudaMalloc(&s.base, need) == cudaSuccess;
+  if (prev >= 0) cudaSetDevice(prev);
+  if (!ok) {
+    s.ready = false;
+    return refuse_m(EXL3_TOO_LARGE, "exl3_b200: MoE workspace allocation failed");
+  }
+  s.bytes = need;
+  s.hidden = m;
+  s.inter = m;
+  s.ready = true;
+  return {EXL3_OK, nullptr};
+}
+
+exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down, const exl3_tensor* x,
+                        const exl3_tensor* inds, const exl3_tensor* scores, const exl3_swiglu_opts* opts, void* stream,
+                        exl3_tensor* out) {
+  if (!gate || !up || !down || !x || !inds || !scores || !out) return refuse_m(EXL3_FAILED, "exl3_b200: bad arguments");
+  if (opts && opts->size != sizeof(exl3_swiglu_opts)) return refuse_m(EXL3_FAILED, "exl3_b200: bad swiglu options");
+  const int limit = opts ? opts->limit : 0;
+  if (limit < 0 || limit > 128) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: InvalidExl3Clamp");
+  if (x->ndim != 3 || inds->ndim != 3 || scores->ndim != 3 || out->ndim != 3)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Shape (x [B, S, D], inds / scores [B, S, K])");
+  const int hidden = static_cast<int>(x->shape[2]);
+  const int64_t rows = x->shape[0] * x->shape[1];
+  const int topk = static_cast<int>(inds->shape[2]);
+  if (inds->shape[0] != x->shape[0] || inds->shape[1] != x->shape[1] || topk <= 0 || topk > kMaxTopK)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Shape (inds)");
+  for (int i = 0; i < 3; ++i)
+    if (scores->shape[i] != inds->shape[i] || out->shape[i] != x->shape[i])
+      return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Shape (scores / out)");
+  if (x->dtype != EXL3_F16 && x->dtype != EXL3_BF16 && x->dtype != EXL3_F32) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (x)");
+  if (inds->dtype != EXL3_I32 && inds->dtype != EXL3_U32) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (inds)");
+  if (scores->dtype != EXL3_F32) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (scores are f32)");
+  if (out->dtype != x->dtype) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (out)");
+  const int inter = gate->out_features;
+  const int experts = gate->groups;
+  if (hidden <= 0 || hidden % 128 != 0 || inter <= 0 || inter % 128 != 0)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Shape (hidden and intermediate are multiples of 128)");
+  if (!bank_ok(gate, hidden, inter) || !bank_ok(up, hidden, inter) || !bank_ok(down, inter, hidden))
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Shape (banks: gate/up [E, hidden -> inter], down [E, inter -> hidden])");
+  if (up->groups != experts || down->groups != experts || experts < 1 || experts > 1024)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: the banks hold different expert counts");
+  if (gate->n != up->n) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: gate and up banks at different rates");
+  if (gate->device != up->device || gate->device != down->device) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: banks on different devices");
+  if (rows == 0) return {EXL3_OK, nullptr};
+  const int dev = gate->device;
+  MoeScratch* sc = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_moe_mu);
+    if (dev >= 0 && dev < kMaxDev && g_moe[dev].ready && g_moe[dev].hidden >= hidden && g_moe[dev].inter >= inter)
+      sc = &g_moe[dev];
+  }
+  if (!sc) return refuse_m(EXL3_FAILED, "exl3_b200: no MoE workspace for these banks (load them with exl3_load_bank)");
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != dev) cudaSetDevice(dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MoeParams p{};
+  p.g_tr = gate->trellis; p.g_suh = gate->suh; p.g_svh = gate->svh;
+  p.u_tr = up->trellis; p.u_suh = up->suh; p.u_svh = up->svh;
+  p.d_tr = down->trellis; p.d_suh = down->suh; p.d_svh = down->svh;
+  p.experts = experts; p.hidden = hidden; p.inter = inter;
+  p.x = x->data; p.x_dtype = x->dtype;
+  p.inds = inds->data; p.inds_u32 = inds->dtype == EXL3_U32;
+  p.scores = static_cast<const float*>(scores->data);
+  p.y = out->data; p.topk = topk; p.limit = static_cast<float>(limit);
+  int32_t* ints = reinterpret_cast<int32_t*>(sc->base);
+  p.order = ints;
+  p.chunk_e = ints + kMaxSlots;
+  p.chunk_s = ints + 2 * kMaxSlots;
+  p.chunk_n = ints + 3 * kMaxSlots;
+  p.nchunks = ints + 4 * kMaxSlots;
+  p.bad = ints + 4 * kMaxSlots + 1;
+  uint8_t* cur = sc->base + (4 * kMaxSlots + 64) * 4;
+  const size_t xs = static_cast<size_t>(kMaxSlots) * (hidden / 16) * 256;
+  p.xg = cur; cur += xs;
+  p.xu = cur; cur += xs;
+  p.hp = cur; cur += static_cast<size_t>(kMaxSlots) * (inter / 16) * 256;
+  p.dout = reinterpret_cast<float*>(cur);
+  const int grid_gu = sc->sms * 2, grid_d = sc->sms * 2;
+  cudaError_t err = cudaSuccess;
+  const int pass_rows = kMaxSlots / topk;  // every expert a pass touches is read once per pass
+  for (int64_t r0 = 0; r0 < rows && err == cudaSuccess; r0 += pass_rows) {
+    p.row0 = static_cast<int32_t>(r0);
+    p.rows = static_cast<int32_t>(rows - r0 < pass_rows ? rows - r0 : pass_rows);
+    const int S = p.rows * topk;
+    err = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
+    if (err == cudaSuccess) err = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S), dim3(128), p, st);
+    if (err == cudaSuccess) err = launch_moe_gemv_k<true>(p, gate->n / 16, grid_gu, st);
+    if (err == cudaSuccess) err = launch_moe_gemv_k<false>(p, down->n / 16, grid_d, st);
+    if (err == cudaSuccess) err = launch_pdl(moe_combine_kernel, dim3(hidden / 128, p.rows), dim3(128), p, st);
+  }
+  if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+  if (err != cudaSuccess) return refuse_m(EXL3_FAILED, "exl3_b200: MoE launch failed");
+  return {EXL3_OK, nullptr};
 }
 
 }  // namespace exl3
