@@ -129,6 +129,8 @@ typedef struct exl3_swiglu_opts {
 #define EXL3_MATMUL_PREPARED 1u /* x holds f16(H(x*suh)/sqrt(128)) rows: skip the prepare */
 #define EXL3_MATMUL_INNER 2u    /* stop at the inner product: y = xp W_hat in f32 (no output Hadamard, no svh) */
 #define EXL3_MATMUL_DP4A 4u     /* mul1 byte sums on dp4a instead of the tensor pipe (same bits) */
+#define EXL3_MATMUL_GEMV 8u     /* force the decode GEMV at any row count (16 rows per launch) */
+#define EXL3_MATMUL_GEMM 16u    /* force the tensor-core GEMM at any row count (the default from 64 rows) */
 
 /* ------------------------------------------------------------------ the quant seam (QuantTable) */
 
@@ -178,6 +180,13 @@ exl3_verdict exl3_swiglu(const exl3_weight *gate, const exl3_weight *up, const e
 /* matmul with EXL3_MATMUL_* flags (linear_prepared, linear_split inner: quant.zig:57-66). */
 exl3_verdict exl3_matmul_ex(const exl3_weight *w, const exl3_tensor *x, uint32_t flags, void *stream,
                             exl3_tensor *out);
+
+/* matmul_ex with CUDA events recorded on the stream between its launches, for timing a phase without a profiler.
+ * events: 4 cudaEvent_t (any may be NULL) -- [0] before the first launch; on the GEMM path (64 rows and more) [1]
+ * after the prepare, [2] after the decode and [3] after the GEMM of the first chunk of rows and columns; on the GEMV
+ * path [3] after the last launch.  A measurement aid of this library; the reference has no counterpart. */
+exl3_verdict exl3_matmul_timed(const exl3_weight *w, const exl3_tensor *x, uint32_t flags, void *stream,
+                               exl3_tensor *out, void *const *events);
 
 /* A borrowed view of device arrays already in the pack layout (the reference's shared handles, plugin.zig:213-218):
  * validates the shapes and creates the device workspace; exl3_release on a view frees nothing. */

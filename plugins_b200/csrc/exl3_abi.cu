@@ -186,12 +186,16 @@ struct DeviceState {
   size_t partial_floats = 0;
   uint32_t* counters = nullptr;
   uint32_t* err = nullptr;
+  uint8_t* image = nullptr;  // prefill GEMM operand images (A rows, then B columns)
+  size_t image_bytes = 0;
   int sms = 0;
+  int gemm_min_rows = exl3::kGemmMinRows;
 };
 
 constexpr int kMaxDevices = 64;
 constexpr size_t kCounterCount = 8192;           // out / 128 <= 8192
 constexpr size_t kPartialBytes = 128u << 20;     // decode-GEMV split partials
+constexpr size_t kImageBytes = 256u << 20;       // prefill GEMM operand images
 
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
@@ -228,11 +232,18 @@ exl3_verdict ensure_device(int dev) {
   if (prop.major != 10) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the kernels are built for sm_100a (B200) only");
   d.sms = prop.multiProcessorCount;
   const size_t counter_bytes = kCounterCount * 4;
-  d.bytes = kPartialBytes + counter_bytes + 256;
+  d.bytes = kImageBytes + kPartialBytes + counter_bytes + 256;
   if (cudaMalloc(&d.base, d.bytes) != cudaSuccess) return refuse(EXL3_TOO_LARGE, "exl3_b200: workspace allocation failed");
-  d.partials = reinterpret_cast<float*>(d.base);
+  d.image = d.base;
+  d.image_bytes = kImageBytes;
+  d.partials = reinterpret_cast<float*>(d.base + kImageBytes);
   d.partial_floats = kPartialBytes / 4;
-  d.counters = reinterpret_cast<uint32_t*>(d.base + kPartialBytes);
+  d.counters = reinterpret_cast<uint32_t*>(d.base + kImageBytes + kPartialBytes);
+  // tuning override for measurement runs
+  if (const char* e = getenv("EXL3_GEMM_MIN_ROWS")) {
+    const int v = atoi(e);
+    if (v >= 1) d.gemm_min_rows = v;
+  }
   if (cudaMemset(d.counters, 0, counter_bytes) != cudaSuccess) return refuse(EXL3_FAILED, "exl3_b200: workspace init failed");
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&d.err), exl3::g_device_error) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_b200: error word lookup failed");
@@ -362,12 +373,126 @@ exl3_verdict check_weight(const exl3_weight* w) {
   return check_linear_shape(w->groups, w->in_features, w->out_features, w->n);
 }
 
-// One decode-GEMV launch per group and per 16 rows.
+// The prefill path: per group, segment and chunk of rows, the A image of the rotated rows; per chunk of columns, the
+// B image of the decoded weights and one tensor-core GEMM into y.  The chunks keep both images inside the workspace's
+// image region, so the call allocates nothing.
+// The GEMM's tile shape for an m x n launch: the fewest tile-waves over the SMs, weighted by the tile's area (its MMA
+// time); on a tie the larger tile, which reads fewer operand bytes per flop.  EXL3_GEMM_SHAPE (0..3) overrides it,
+// for measurement runs.
+int gemm_shape_for(int64_t m, int64_t n, int sms) {
+  if (const char* e = getenv("EXL3_GEMM_SHAPE")) {
+    const int v = atoi(e);
+    if (v >= 0 && v <= 3) return v;
+  }
+  int best = 0;
+  int64_t best_cost = -1;
+  for (int shape : {3, 1, 2, 0}) {
+    const int64_t bm = exl3::gemm_block_m(shape), bn = exl3::gemm_block_n(shape);
+    const int64_t tiles = ((m + bm - 1) / bm) * ((n + bn - 1) / bn);
+    const int64_t cost = (tiles + sms - 1) / sms * bm * bn;
+    if (best_cost < 0 || cost < best_cost) {
+      best = shape;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+// ev (optional, 4 cudaEvent_t): recorded before the first launch and after the first chunk's prepare, decode and GEMM
+exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32_t x_dtype, int64_t rows, void* y,
+                      int32_t y_dtype, uint32_t flags, cudaStream_t st, void* const* ev) {
+  bool first = true;
+  auto mark = [&](int i) {
+    if (ev && first && ev[i]) cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), st);
+  };
+  mark(0);
+  const int in_f = w->in_features, out_f = w->out_features, groups = w->groups;
+  const bool grouped = (w->flags & EXL3_WEIGHT_GROUPED) != 0;
+  constexpr int bm = 256, bn = 256;  // chunk granularity: a multiple of every tile shape
+  const size_t tile_halfs = static_cast<size_t>(in_f / 16) * (out_f / 16) * w->n;
+  const size_t xsz = x_dtype == EXL3_F32 ? 4 : 2;
+  const size_t ysz = y_dtype == EXL3_F32 ? 4 : 2;
+  const size_t row_bytes = static_cast<size_t>(in_f) * 2;  // one image row (A) or column (B)
+  // rows per chunk: at most half the region; columns: what the rows leave
+  int64_t mc = static_cast<int64_t>(d->image_bytes / 2 / row_bytes) / bm * bm;
+  const int64_t rows_padded = (rows + bm - 1) / bm * bm;
+  if (mc > rows_padded) mc = rows_padded;
+  if (mc < bm) return refuse(EXL3_TOO_LARGE, "exl3_b200: in_features too large for the prefill image region");
+  uint8_t* a_img = d->image;
+  uint8_t* b_img = d->image + static_cast<size_t>(mc) * row_bytes;
+  // a multiple of the tile width, so a ragged last tile's reads stay inside the B region
+  const int64_t nc_cap = static_cast<int64_t>((d->image_bytes - static_cast<size_t>(mc) * row_bytes) / row_bytes) / bn * bn;
+  if (nc_cap < bn) return refuse(EXL3_TOO_LARGE, "exl3_b200: in_features too large for the prefill image region");
+  const int gcount = grouped ? groups : 1;
+  for (int g = 0; g < gcount; ++g) {
+    const int64_t x_stride = grouped ? static_cast<int64_t>(groups) * in_f : in_f;
+    const uint8_t* xg = static_cast<const uint8_t*>(x) + static_cast<size_t>(g) * in_f * xsz;
+    const uint16_t* trg = w->trellis + static_cast<size_t>(g) * tile_halfs;
+    for (int s = 0; s < w->nseg; ++s) {
+      const int c0 = w->seg_cols[s], c1 = w->seg_cols[s + 1], seg_w = c1 - c0;
+      const uint16_t* suh = w->suh + (static_cast<size_t>(g) * w->nseg + s) * in_f;
+      const uint16_t* svh = w->svh + static_cast<size_t>(g) * out_f + c0;
+      // y element (row, column j of this segment)
+      uint8_t* yseg;
+      int64_t ystride;
+      if (w->nseg == 1) {
+        ystride = grouped ? static_cast<int64_t>(groups) * out_f : out_f;
+        yseg = static_cast<uint8_t*>(y) + static_cast<size_t>(g) * out_f * ysz;
+      } else {
+        ystride = seg_w;
+        yseg = static_cast<uint8_t*>(y) + static_cast<size_t>(rows) * c0 * ysz;
+      }
+      for (int64_t r0 = 0; r0 < rows; r0 += mc) {
+        const int m = static_cast<int>(rows - r0 < mc ? rows - r0 : mc);
+        const int mp = (m + bm - 1) / bm * bm;  // padded rows: whole tiles of every shape
+        if (exl3::launch_prep_image(xg + static_cast<size_t>(r0) * x_stride * xsz, x_dtype, x_stride, m, mp,
+                                    in_f, suh, (flags & EXL3_MATMUL_PREPARED) ? 1 : 0, a_img, st) != cudaSuccess)
+          return refuse(EXL3_FAILED, "exl3_b200: prefill prepare launch failed");
+        mark(1);
+        for (int j0 = 0; j0 < seg_w; j0 += static_cast<int>(nc_cap)) {
+          const int nc = static_cast<int>(seg_w - j0 < nc_cap ? seg_w - j0 : nc_cap);
+          if (exl3::launch_decode_image(trg, in_f, out_f, c0 + j0, nc, w->n, b_img, st) != cudaSuccess)
+            return refuse(EXL3_FAILED, "exl3_b200: prefill decode launch failed");
+          mark(2);
+          const int shape = gemm_shape_for(m, nc, d->sms);
+          const int tbm = exl3::gemm_block_m(shape), tbn = exl3::gemm_block_n(shape);
+          exl3::GemmParams gp{};
+          gp.a_img = a_img;
+          gp.b_img = b_img;
+          gp.svh = svh + j0;
+          uint8_t* yp = yseg + (static_cast<size_t>(r0) * ystride + j0) * ysz;
+          gp.y = yp;
+          gp.y_dtype = y_dtype;
+          gp.y_row_stride = ystride;
+          gp.m = m;
+          gp.ncols = nc;
+          gp.tiles_m = (m + tbm - 1) / tbm;
+          gp.tiles_n = (nc + tbn - 1) / tbn;
+          gp.kb = in_f / 64;
+          gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
+          gp.vec_store = (reinterpret_cast<uintptr_t>(yp) % 16 == 0 && (ystride * ysz) % 16 == 0) ? 1 : 0;
+          gp.err = d->err;
+          if (exl3::launch_gemm_image(gp, shape, d->sms, st) != cudaSuccess)
+            return refuse(EXL3_FAILED, "exl3_b200: prefill GEMM launch failed");
+          mark(3);
+          first = false;
+        }
+      }
+    }
+  }
+  return kOk;
+}
+
+// Rows from the GEMM threshold on take the tensor-core GEMM; fewer rows take one decode-GEMV launch per group and
+// per 16 rows.
 exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, int64_t rows, void* y, int32_t y_dtype,
-                        uint32_t flags, cudaStream_t st) {
+                        uint32_t flags, cudaStream_t st, void* const* ev = nullptr) {
   DeviceState* d = device_state(w->device);
   if (!d) return refuse(EXL3_FAILED, "exl3_b200: no workspace on this device (exl3_open or a weight load creates it)");
   DeviceGuard guard(w->device);
+  const bool gemm = (flags & EXL3_MATMUL_GEMM) != 0 || ((flags & EXL3_MATMUL_GEMV) == 0 && rows >= d->gemm_min_rows);
+  if (gemm) return run_gemm(d, w, x, x_dtype, rows, y, y_dtype, flags, st, ev);
+  if (ev && ev[0]) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
   const int in_f = w->in_features, out_f = w->out_features, groups = w->groups;
   const bool grouped = (w->flags & EXL3_WEIGHT_GROUPED) != 0;
   const int K = w->n / 16;
@@ -411,6 +536,7 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
         return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
     }
   }
+  if (ev && ev[3]) cudaEventRecord(static_cast<cudaEvent_t>(ev[3]), st);
   return kOk;
 }
 
@@ -537,11 +663,18 @@ void exl3_release(exl3_weight* w) {
 }
 
 exl3_verdict exl3_matmul_ex(const exl3_weight* w, const exl3_tensor* x, uint32_t flags, void* stream, exl3_tensor* out) {
+  return exl3_matmul_timed(w, x, flags, stream, out, nullptr);
+}
+
+exl3_verdict exl3_matmul_timed(const exl3_weight* w, const exl3_tensor* x, uint32_t flags, void* stream,
+                               exl3_tensor* out, void* const* events) {
   exl3_verdict v = check_weight(w);
   if (v.code != EXL3_OK) return v;
   if (!x || !out || x->ndim < 1 || x->ndim > 4 || out->ndim != x->ndim) return refuse(EXL3_FAILED, "exl3_b200: bad tensors");
   if ((numel(x) > 0 && !x->data) || (numel(out) > 0 && !out->data)) return refuse(EXL3_FAILED, "exl3_b200: bad tensors");
   if (!act_dtype(x->dtype)) return refuse(EXL3_UNSUPPORTED, "exl3_b200: activations must be f16, bf16 or f32");
+  if ((flags & EXL3_MATMUL_GEMV) && (flags & EXL3_MATMUL_GEMM))
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: GEMV and GEMM forced together");
   if ((flags & EXL3_MATMUL_PREPARED) && x->dtype != EXL3_F16)
     return refuse(EXL3_UNSUPPORTED, "exl3_b200: prepared rows are f16");
   const bool grouped = (w->flags & EXL3_WEIGHT_GROUPED) != 0;
@@ -562,7 +695,7 @@ exl3_verdict exl3_matmul_ex(const exl3_weight* w, const exl3_tensor* x, uint32_t
   if (out->shape[out->ndim - 1] != w->out_features) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the output has the wrong shape");
   if (rows == 0) return kOk;
   if (rows > (1 << 24)) return refuse(EXL3_TOO_LARGE, "exl3_b200: too many rows");
-  return run_linear(w, x->data, x->dtype, rows, out->data, y_dtype, flags, static_cast<cudaStream_t>(stream));
+  return run_linear(w, x->data, x->dtype, rows, out->data, y_dtype, flags, static_cast<cudaStream_t>(stream), events);
 }
 
 exl3_verdict exl3_matmul(const exl3_weight* w, const exl3_tensor* x, void* stream, exl3_tensor* out) {

@@ -1,0 +1,485 @@
+// exl3_gemm.cu -- the prefill path of an EXL3 linear (many rows): decode once per call, contract on the
+// 5th-generation tensor cores.
+//
+// The reference routes rows > 8 through "prep + sorted GEMM + finish" (plugins/sushi_ds41/src/sushi/linear.zig:77-100)
+// and its prefill kernels decode trellis tiles into threadgroup memory ahead of the MMA
+// (kernels/dsv41_prefill_dig_gemm_*.metal, header_dig_mul1h_k3.metal:1090-1166).  The math is the same three steps as
+// the decode GEMV:  xp = f16(H128(x * suh) / sqrt(128)),  inner = xp . W_hat (f32),  y = H128(inner) / sqrt(128) * svh.
+//
+// B200 layout.  Both operands are written as "stage images": blocks of 128 rows x 64 k of f16 (16 KiB), each already
+// in the UMMA K-major canonical layout with the 128-byte swizzle (row r at byte 128 r, its 16-byte chunk c at chunk
+// c ^ (r % 8)).  One pipeline stage is then a handful of whole blocks that cp.async.bulk copies into shared memory
+// with no tensor map and no re-layout.
+//   A image: [rows/128][in/64] blocks of xp (rows padded to 128 with zeros) -- prep_image_kernel
+//   B image: [cols/128][in/64] blocks of W_hat^T (row = output column)      -- decode_image_kernel, bit-exact decode
+// The GEMM (gemm_image_kernel) is persistent, one CTA per SM, warp-specialised:
+//   warp 0      producer: bulk copies of A and B blocks into a ring of stages (mbarrier tx counts)
+//   warp 1      MMA issuer: tcgen05.mma kind::f16, M = 128 per A block, N = BN, K = 16, accumulators in TMEM (f32)
+//   warp 2      allocates and frees the TMEM columns
+//   warps 4..7  epilogue: tcgen05.ld a row's 128 accumulator columns, the output Hadamard (in registers), * svh, store
+// Two TMEM accumulators alternate when they fit, so the epilogue of one tile runs under the MMAs of the next.  Every
+// mbarrier wait is bounded (about two seconds); a wait that gives up sets an abort flag that every role polls, records
+// kErrWaitTimeout and lets the CTA reach its TMEM release.
+#include <cuda_runtime.h>
+
+#include "exl3_common.cuh"
+#include "exl3_internal.h"
+
+namespace exl3 {
+
+namespace {
+
+constexpr int kImgRows = 128;                               // rows (A) or output columns (B) of one image block
+constexpr int kImgK = 64;                                   // k of one image block: one 128-byte swizzle row of f16
+constexpr uint32_t kImgBytes = kImgRows * kImgK * 2;        // 16 KiB
+
+// Byte offset of element (r, k) inside an image block.
+__device__ __forceinline__ uint32_t image_offset(uint32_t r, uint32_t k) {
+  return r * 128u + ((((k >> 3) ^ r) & 7u) << 4) + (k & 7u) * 2u;
+}
+
+// ------------------------------------------------------------------ tcgen05 / TMEM
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, f16 inputs, f32 accumulate; issued by one thread.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on `bar` when every tcgen05 operation this thread issued before it has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor of kind::f16: f16 A and B (both K-major), f32 D, M x N.
+constexpr uint32_t umma_idesc(int m, int n) {
+  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// 32 consecutive accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Waits for the outstanding tcgen05.ld of this thread; the registers pass through the same asm so no use of them
+// can be scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]),
+        "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]),
+        "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),
+        "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+
+// Bounded wait that also gives up when another role has aborted.
+__device__ __forceinline__ bool role_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                          uint32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > 2000000000ull) {
+      *abort_flag = 1u;
+      atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// In-register 128-point Hadamard (Sylvester order, unnormalised).
+__device__ __forceinline__ void fwht128_regs(float (&v)[128]) {
+#pragma unroll
+  for (int h = 1; h < 128; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 128; ++i) {
+      if ((i & h) == 0) {
+        const float a = v[i], b = v[i + h];
+        v[i] = a + b;
+        v[i + h] = a - b;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ A image: xp rows, swizzled
+
+// One warp per (row, 128-wide input block).  Rows m..mp-1 are written as zeros (padding of the last 128-row block).
+__global__ void __launch_bounds__(256) prep_image_kernel(const void* __restrict__ x, int32_t x_dtype,
+                                                         int64_t x_row_stride, int m, int mp, int in_features,
+                                                         const uint16_t* __restrict__ suh, int prepared,
+                                                         uint8_t* __restrict__ a_img) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const int kblk = in_features / 128;
+  const int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (job >= static_cast<int64_t>(mp) * kblk) return;  // warp-uniform
+  const int row = static_cast<int>(job / kblk), b = static_cast<int>(job % kblk);
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  if (row < m) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int k = b * 128 + static_cast<int>(lane) + 32 * i;
+      const float xv = load_act(x, static_cast<size_t>(row) * x_row_stride + k, x_dtype);
+      v[i] = prepared ? xv : xv * f16_bits_to_float(suh[k]);
+    }
+    if (!prepared) {
+      fwht128_warp(v, lane);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] *= kHadScale;
+    }
+  }
+  const int kbs = in_features / kImgK;
+  const uint32_t r = static_cast<uint32_t>(row) & 127u;
+  const size_t mb = static_cast<size_t>(row) >> 7;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int k = b * 128 + static_cast<int>(lane) + 32 * i;
+    uint8_t* blk = a_img + (mb * kbs + (k >> 6)) * kImgBytes;
+    *reinterpret_cast<__half*>(blk + image_offset(r, static_cast<uint32_t>(k & 63))) = __float2half_rn(v[i]);
+  }
+}
+
+// ------------------------------------------------------------------ B image: W_hat^T, decoded once
+
+// One warp per 16x16 trellis tile of the column range [16 tn0, 16 (tn0 + ncol_tiles)); consecutive warps walk a
+// k-row of tiles, which the trellis stores contiguously.  Each lane holds one column's four consecutive k (the IMMA
+// byte-sum order) and writes them as one 8-byte store; a warp's stores fill whole 32-byte sectors.
+template <int K>
+__global__ void __launch_bounds__(256) decode_image_kernel(const uint16_t* __restrict__ trellis, int in_features,
+                                                           int out_tiles, int tn0, int ncol_tiles,
+                                                           uint8_t* __restrict__ b_img) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const size_t tiles = static_cast<size_t>(in_features / 16) * ncol_tiles;
+  const size_t tile = static_cast<size_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (tile >= tiles) return;  // warp-uniform
+  const int tk = static_cast<int>(tile / ncol_tiles), tj = static_cast<int>(tile % ncol_tiles);
+  const uint32_t* tw =
+      reinterpret_cast<const uint32_t*>(trellis + (static_cast<size_t>(tk) * out_tiles + tn0 + tj) * (16 * K));
+  LaneWindows<K> lw;
+  lw.init(lane);
+  uint32_t w[8], a[4];
+  lane_codewords<K>(tw, lw, w);
+  ImmaIndicator ind;
+  ind.init(lane);
+  decode_afrag_imma(w, ind, a);  // a[0], a[2]: column g at k 4q..4q+3; a[1], a[3]: column g + 8
+  const uint32_t g = lane >> 2, q = lane & 3u;
+  const int kbs = in_features / kImgK;
+  const uint32_t n = static_cast<uint32_t>(tj & 7) * 16u + g;
+  const uint32_t kin = static_cast<uint32_t>(tk & 3) * 16u + 4u * q;
+  uint8_t* blk = b_img + (static_cast<size_t>(tj >> 3) * kbs + (tk >> 2)) * kImgBytes;
+  *reinterpret_cast<uint2*>(blk + image_offset(n, kin)) = make_uint2(a[0], a[2]);
+  *reinterpret_cast<uint2*>(blk + image_offset(n + 8u, kin)) = make_uint2(a[1], a[3]);
+}
+
+// ------------------------------------------------------------------ the GEMM
+
+template <int MS, int NS>
+struct GemmShape {
+  static constexpr int BM = 128 * MS, BN = 128 * NS;
+  static constexpr uint32_t kStageBytes = (MS + NS) * kImgBytes;
+  static constexpr int kStages = (MS + NS) == 2 ? 6 : ((MS + NS) == 3 ? 4 : 3);
+  static constexpr int kAccCols = MS * BN;
+  static constexpr int kAccBufs = kAccCols * 2 <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = kAccCols * kAccBufs <= 256 ? 256 : 512;
+  static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
+  static_assert(BN <= 256, "one MMA covers at most 256 columns");
+  static_assert(kAccCols * kAccBufs <= 512, "TMEM holds 512 columns");
+};
+
+template <int MS, int NS>
+__global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) {
+  using S = GemmShape<MS, NS>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* stages = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // the swizzle is anchored on 1024-byte rows
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + S::kStages * S::kStageBytes);
+  uint64_t* empty = full + S::kStages;
+  uint64_t* accf = empty + S::kStages;
+  uint64_t* acce = accf + 2;
+  uint64_t* fin = acce + 2;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(fin + 1);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 128);
+    }
+    mbar_init(fin, 1);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_slot)), S::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int tiles = p.tiles_m * p.tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer
+      const uint64_t pol_a = policy_evict_last(), pol_b = policy_evict_first();
+      uint32_t stage = 0, phase = 0, fills = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        const int mb = t % p.tiles_m, nb = t / p.tiles_m;
+        for (int kb = 0; kb < p.kb; ++kb) {
+          if (!role_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = stages + stage * S::kStageBytes;
+          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+#pragma unroll
+          for (int s = 0; s < MS; ++s)
+            bulk_g2s(dst + s * kImgBytes, p.a_img + (static_cast<size_t>(mb * MS + s) * p.kb + kb) * kImgBytes,
+                     kImgBytes, &full[stage], pol_a);
+#pragma unroll
+          for (int j = 0; j < NS; ++j)
+            bulk_g2s(dst + (MS + j) * kImgBytes, p.b_img + (static_cast<size_t>(nb * NS + j) * p.kb + kb) * kImgBytes,
+                     kImgBytes, &full[stage], pol_b);
+          ++fills;
+          if (++stage == S::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // No copy may outlive the CTA: wait (bounded) for the last fill of every stage.
+      const uint32_t last = fills < static_cast<uint32_t>(S::kStages) ? fills : static_cast<uint32_t>(S::kStages);
+      for (uint32_t i = 1; i <= last; ++i) {
+        const uint32_t f = fills - i;
+        if (!mbar_wait_bounded(&full[f % S::kStages], (f / S::kStages) & 1u)) atomicOr(p.err, kErrWaitTimeout);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = umma_idesc(128, S::BN);
+      uint32_t stage = 0, phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++local) {
+        const int ab = S::kAccBufs == 2 ? (local & 1) : 0;
+        const uint32_t aph = S::kAccBufs == 2 ? ((local >> 1) & 1) : (local & 1);
+        if (!role_wait(&acce[ab], aph ^ 1u, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem + static_cast<uint32_t>(ab * S::kAccCols);
+        for (int kb = 0; kb < p.kb; ++kb) {
+          if (!role_wait(&full[stage], phase, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_u32(stages + stage * S::kStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kImgK / 16; ++kk) {
+            const uint64_t bdesc = sw128_desc(base + MS * kImgBytes + kk * 32);
+#pragma unroll
+            for (int s = 0; s < MS; ++s)
+              umma_f16(d0 + s * S::BN, sw128_desc(base + s * kImgBytes + kk * 32), bdesc, idesc,
+                       (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == S::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&accf[ab]);
+      }
+      // every MMA this thread issued has finished before TMEM is released
+      umma_commit(fin);
+      if (!mbar_wait_bounded(fin, 0)) atomicOr(p.err, kErrWaitTimeout);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ---------------- epilogue: warp 4 + j reads TMEM lanes 32 j .. 32 j + 31
+    const uint32_t wq = warp - 4;
+    int local = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+      const int ab = S::kAccBufs == 2 ? (local & 1) : 0;
+      const uint32_t aph = S::kAccBufs == 2 ? ((local >> 1) & 1) : (local & 1);
+      if (!role_wait(&accf[ab], aph, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int mb = t % p.tiles_m, nb = t / p.tiles_m;
+#pragma unroll 1
+      for (int s = 0; s < MS; ++s) {
+        const int row = (mb * MS + s) * 128 + static_cast<int>(wq * 32 + lane);
+#pragma unroll 1
+        for (int c = 0; c < NS; ++c) {
+          const int col0 = (nb * NS + c) * 128;
+          if (col0 >= p.ncols) continue;  // warp-uniform: a ragged tile's padding columns are neither read nor stored
+          float v[128];
+          const uint32_t taddr =
+              tmem + ((wq * 32u) << 16) + static_cast<uint32_t>(ab * S::kAccCols + s * S::BN + c * 128);
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            uint32_t r[32];
+            tmem_ld32(taddr + h * 32, r);
+            tmem_wait_ld(r);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[h * 32 + i] = __uint_as_float(r[i]);
+          }
+          if (!p.inner_only) {
+            fwht128_regs(v);
+            const uint4* sv4 = reinterpret_cast<const uint4*>(p.svh + col0);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const uint4 u = __ldg(sv4 + j);
+              const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+                v[j * 8 + 2 * e] *= kHadScale * f.x;
+                v[j * 8 + 2 * e + 1] *= kHadScale * f.y;
+              }
+            }
+          }
+          if (row < p.m) {
+            const size_t at = static_cast<size_t>(row) * p.y_row_stride + col0;
+            if (p.vec_store && p.y_dtype != kF32) {
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + at);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float lo = v[j * 8 + 2 * e], hi = v[j * 8 + 2 * e + 1];
+                  if (p.y_dtype == kF16) {
+                    const __half2 h2 = __floats2half2_rn(lo, hi);
+                    pk[e] = *reinterpret_cast<const uint32_t*>(&h2);
+                  } else {
+                    const __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+                    pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
+                  }
+                }
+                dst[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              }
+            } else if (p.vec_store) {
+              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.y) + at);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 128; ++i) store_act(p.y, at + i, v[i], p.y_dtype);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acce[ab]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host launchers
+
+cudaError_t launch_prep_image(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, int in_features,
+                              const uint16_t* suh, int prepared, uint8_t* a_img, cudaStream_t st) {
+  if (in_features % 128 != 0 || mp % 128 != 0 || m > mp) return cudaErrorInvalidValue;
+  const int64_t jobs = static_cast<int64_t>(mp) * (in_features / 128);
+  prep_image_kernel<<<static_cast<unsigned>((jobs + 7) / 8), 256, 0, st>>>(x, x_dtype, x_row_stride, m, mp,
+                                                                            in_features, suh, prepared, a_img);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode_image(const uint16_t* trellis, int in_features, int out_features, int col0, int ncols, int n,
+                                uint8_t* b_img, cudaStream_t st) {
+  if (n % 16 != 0 || in_features % 64 != 0 || col0 % 128 != 0 || ncols % 128 != 0) return cudaErrorInvalidValue;
+  const size_t tiles = static_cast<size_t>(in_features / 16) * (ncols / 16);
+  const dim3 grid(static_cast<unsigned>((tiles + 7) / 8)), block(256);
+  const int ot = out_features / 16, tn0 = col0 / 16, nt = ncols / 16;
+  switch (n / 16) {
+    case 1: decode_image_kernel<1><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
+    case 2: decode_image_kernel<2><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
+    case 3: decode_image_kernel<3><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
+    case 4: decode_image_kernel<4><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
+    case 5: decode_image_kernel<5><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
+    case 6: decode_image_kernel<6><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+template <int MS, int NS>
+static cudaError_t launch_gemm_t(const GemmParams& p, int sms, cudaStream_t st) {
+  using S = GemmShape<MS, NS>;
+  if (p.tiles_m * 128 * MS < p.m) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(gemm_image_kernel<MS, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(S::kSmemBytes));
+  if (e != cudaSuccess) return e;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < sms ? tiles : sms;
+  gemm_image_kernel<MS, NS><<<grid, 256, S::kSmemBytes, st>>>(p);
+  return cudaGetLastError();
+}
+
+int gemm_block_m(int shape) { return shape == 2 || shape == 3 ? 256 : 128; }
+int gemm_block_n(int shape) { return shape == 1 || shape == 3 ? 256 : 128; }
+
+cudaError_t launch_gemm_image(const GemmParams& p, int shape, int sms, cudaStream_t st) {
+  switch (shape) {
+    case 0: return launch_gemm_t<1, 1>(p, sms, st);
+    case 1: return launch_gemm_t<1, 2>(p, sms, st);
+    case 2: return launch_gemm_t<2, 1>(p, sms, st);
+    case 3: return launch_gemm_t<2, 2>(p, sms, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace exl3

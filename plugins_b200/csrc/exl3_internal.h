@@ -48,5 +48,35 @@ cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int ou
 cudaError_t launch_encode(const float* target, int in_features, int out_features, int n, uint16_t* trellis,
                           cudaStream_t st);
 
+// ---------------------------------------------------------------- prefill GEMM (exl3_gemm.cu)
+
+constexpr int kGemmMinRows = 64;  // rows from which matmul takes the tensor-core GEMM instead of the decode GEMV
+
+struct GemmParams {
+  const uint8_t* a_img;  // [tiles_m * BM / 128][kb] image blocks of xp
+  const uint8_t* b_img;  // [tiles_n * BN / 128][kb] image blocks of W_hat^T
+  const uint16_t* svh;   // [tiles_n * BN] f16 bits, this launch's columns
+  void* y;               // y[row * y_row_stride + col], col relative to this launch's first column
+  int32_t y_dtype;
+  int64_t y_row_stride;
+  int32_t m;             // valid rows
+  int32_t ncols;         // valid columns (tiles past them are computed but not stored)
+  int32_t tiles_m, tiles_n, kb;  // kb = in_features / 64
+  int32_t inner_only;    // y = the f32 inner product (no output Hadamard, no svh)
+  int32_t vec_store;     // y and y_row_stride allow 16-byte stores
+  uint32_t* err;
+};
+
+// xp rows [0, mp) as an A image (rows >= m are zeros); prepared = x already holds xp
+cudaError_t launch_prep_image(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, int in_features,
+                              const uint16_t* suh, int prepared, uint8_t* a_img, cudaStream_t st);
+// the trellis columns [col0, col0 + ncols) as a B image
+cudaError_t launch_decode_image(const uint16_t* trellis, int in_features, int out_features, int col0, int ncols, int n,
+                                uint8_t* b_img, cudaStream_t st);
+// shape: 0 = 128x128 tiles, 1 = 128x256, 2 = 256x128, 3 = 256x256 (rows x columns)
+int gemm_block_m(int shape);
+int gemm_block_n(int shape);
+cudaError_t launch_gemm_image(const GemmParams& p, int shape, int sms, cudaStream_t st);
+
 
 }  // namespace exl3

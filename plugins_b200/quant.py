@@ -219,6 +219,21 @@ def matmul_ex(w: Weight, x: torch.Tensor, flags: int = 0, stream=None, out: torc
     return out
 
 
+def matmul_timed(w: Weight, x: torch.Tensor, events, flags: int = 0, stream=None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """matmul_ex recording four torch.cuda.Event (or None) between its launches: [0] before the first, then (GEMM
+    path) after the prepare, the decode and the GEMM of the first chunk; (GEMV path) [3] after the last launch."""
+    shape = list(x.shape[:-1]) + [w.out_features]
+    if out is None:
+        dt = torch.float32 if flags & L.MATMUL_INNER else (torch.float16 if flags & L.MATMUL_PREPARED else x.dtype)
+        out = torch.empty(shape, dtype=dt, device=x.device)
+    ev = (ctypes.c_void_p * 4)(*[(e.cuda_event if e is not None else 0) for e in events])
+    xt, ot = _tensor(x), _tensor(out)
+    check(L.lib().exl3_matmul_timed(ctypes.byref(w.raw), ctypes.byref(xt), flags, _stream(stream), ctypes.byref(ot),
+                                    ev))
+    return out
+
+
 def matmul(w: Weight, x: torch.Tensor, stream=None, out: torch.Tensor | None = None) -> torch.Tensor:
     """plugins/turboexl3_ds41/plugin.zig:243-248: ``x @ W^T`` in x's dtype."""
     return matmul_ex(w, x, 0, stream, out)
