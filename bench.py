@@ -49,9 +49,139 @@ def load_peaks() -> dict:
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return {"hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]), "source": "measured"}
     except Exception:
-        return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------ the other configs (N = 1, rank 0)
+
+def _graph_ms(torch, fn, reps: int, inner: int = 4) -> float:
+    """Milliseconds per call of fn, replayed as a CUDA graph of `inner` calls after warm-up (device time, events)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(inner):
+            fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    g.reset()
+    return e0.elapsed_time(e1) / (reps * inner)
+
+
+def measure_prefill(Q, E, torch, peaks: dict, reps: int = 10) -> dict:
+    """Config 3: X [M, 4096] bf16 through the 4096 x 12288 4-bpw layer (seed 2), M = 2048 headline plus 64, 256 and
+    8192 for the GEMV/GEMM crossover.  Whole-path time per call (operand images + tensor-core GEMM) and the GEMM
+    kernel alone, from events recorded between the launches (exl3_matmul_timed); medians of `reps` calls.  At 64
+    and 256 rows the same rows forced through the decode GEMV are timed too."""
+    in_f, out_f, n = 4096, 12288, 64
+    tr, suh, svh = E.random_linear(in_f, out_f, n, seed=2)
+    w = Q.weight_from_tensors(tr, suh, svh)
+    rows_list, out = (2048, 64, 256, 8192), {}
+    for m in rows_list:
+        g = torch.Generator(device="cuda").manual_seed(m)
+        x = torch.randn((m, in_f), device="cuda", generator=g).to(torch.bfloat16)
+        y = torch.empty((m, out_f), device="cuda", dtype=torch.bfloat16)
+        rec = {}
+        for label, flags in (("gemm", 16), ("gemv", 8)):
+            if label == "gemv" and m > 256:
+                continue
+            for _ in range(3):
+                Q.matmul_ex(w, x, flags, out=y)
+            tot, img, mm = [], [], []
+            for _ in range(reps):
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+                for e in ev:
+                    e.record()
+                Q.matmul_timed(w, x, ev, flags=flags, out=y)
+                torch.cuda.synchronize()
+                tot.append(ev[0].elapsed_time(ev[3]))
+                if label == "gemm":
+                    img.append(ev[0].elapsed_time(ev[1]))
+                    mm.append(ev[1].elapsed_time(ev[2]))
+            rec[label + "_ms"] = round(statistics.median(tot), 4)
+            if label == "gemm":
+                rec["images_ms"] = round(statistics.median(img), 4)
+                rec["gemm_kernel_ms"] = round(statistics.median(mm), 4)
+        out[m] = rec
+    del w
+    flops = 2.0 * 2048 * in_f * out_f
+    h = out[2048]
+    tf_total = flops / (h["gemm_ms"] * 1e-3) / 1e12
+    tf_kernel = flops / (h["gemm_kernel_ms"] * 1e-3) / 1e12
+    return {
+        "workload": "config 3: X [2048, 4096] bf16 x EXL3 4 bpw 4096 x 12288 (random trellis, seed 2), bf16 out",
+        "value": round(tf_total, 1), "unit": "TFLOP/s", "ms": h["gemm_ms"],
+        "frac_of_bf16_peak": round(tf_total / peaks["bf16_tflops"], 4),
+        "phases_ms": {"operand_images": h["images_ms"], "gemm_kernel": h["gemm_kernel_ms"]},
+        "roofline": {"bound": "tensor", "achieved": round(tf_kernel, 1), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(tf_kernel / peaks["bf16_tflops"], 4), "traffic": None,
+                     "kernel": "gemm_image_kernel (tcgen05.mma kind::f16, TMEM accumulators)",
+                     "flops_per_launch": flops,
+                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json bf16_tflops, burst)"},
+        "crossover": [{"rows": m, **out[m]} for m in sorted(out)],
+        "l2": "no flush: each call writes and reads a 100.7 MB B image and reads 25 MB of trellis (> 126 MB L2)",
+    }
+
+
+def measure_moe(Q, E, torch, peaks: dict, reps: int = 10) -> dict:
+    """Config 4: 256 routed experts + 1 shared, hidden 4096, intermediate 2048, 3 bpw (random trellis, seed 3), 32
+    tokens, top-8 of a softmax over N(0, 1) router logits (seed 4).  The shared expert is bank entry 256, routed to
+    every token with score 1 (the reference's moeSwigluFusedWithShared sums it in the same way); one swiglu call."""
+    experts, hidden, inter, topk, tokens = 256, 4096, 2048, 8, 32
+    banks = []
+    for i, (a, b) in enumerate(((hidden, inter), (hidden, inter), (inter, hidden))):
+        tr, suh, svh = E.random_linear(a, b, 48, seed=3 + i, groups=experts + 1)
+        banks.append(Q.weight_from_tensors(tr, suh, svh))
+    g = torch.Generator(device="cuda").manual_seed(4)
+    logits = torch.randn((tokens, experts), device="cuda", generator=g)
+    sc, ind = torch.topk(torch.softmax(logits, -1), topk, -1)
+    ind = torch.cat([ind.to(torch.int32), torch.full((tokens, 1), experts, dtype=torch.int32, device="cuda")], 1)
+    sc = torch.cat([sc.float(), torch.ones((tokens, 1), device="cuda")], 1)
+    ind, sc = ind.view(1, tokens, topk + 1).contiguous(), sc.view(1, tokens, topk + 1).contiguous()
+    x = torch.randn((1, tokens, hidden), device="cuda", dtype=torch.float16, generator=g)
+    y = torch.empty_like(x)
+    ms = _graph_ms(torch, lambda: Q.swiglu(*banks, x, ind, sc, out=y), reps)
+    distinct = int(torch.unique(ind).numel())
+    per_expert = 3 * (hidden * inter * 3 // 8 + 2 * hidden + 2 * inter)
+    nbytes = distinct * per_expert + 2 * 2 * tokens * hidden
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    del banks
+    return {"workload": "config 4: routed SwiGLU, 256 + 1 shared experts, 4096 <-> 2048 @ 3 bpw, 32 tokens, top-8",
+            "value": round(gbs, 1), "unit": "GB/s", "ms": round(ms, 4), "distinct_experts": distinct,
+            "bytes_per_call": nbytes, "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4),
+            "l2": "no flush: a call streams %.2f GB of distinct experts (> 126 MB L2)" % (nbytes / 1e9)}
+
+
+def measure_c5(Q, E, torch, peaks: dict, reps: int = 5) -> dict:
+    """Config 5: K = 16384, N = 53248 at 2, 3, 4 and 5 bpw (random trellis, seed 5), batch-1 f16, one GPU."""
+    in_f, out_f = 16384, 53248
+    res = {}
+    for bits in (2, 3, 4, 5):
+        tr, suh, svh = E.random_linear(in_f, out_f, 16 * bits, seed=5)
+        w = Q.weight_from_tensors(tr, suh, svh)
+        x = torch.randn((1, in_f), device="cuda", dtype=torch.float16)
+        y = torch.empty((1, out_f), device="cuda", dtype=torch.float16)
+        ms = _graph_ms(torch, lambda: Q.matmul(w, x, out=y), reps)
+        nbytes = linear_bytes(in_f, out_f, bits, 1)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[f"{bits}bpw"] = {"ms": round(ms, 4), "value": round(gbs, 1), "unit": "GB/s",
+                             "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "bytes": nbytes}
+        del w, tr
+    return {"workload": "config 5: 16384 x 53248 decode GEMV, batch 1", **res}
 
 
 # ------------------------------------------------------------------ clocks during the timed region
@@ -200,6 +330,7 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline sampling (rank 0, N=1)")
     ap.add_argument("--no-batch8", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip configs 3-5 (prefill, MoE, large layer)")
     args = ap.parse_args()
     if args.impl == "reference":
         if args.steps > 20:
@@ -409,6 +540,10 @@ def main() -> None:
             "clocks": r1["clk"],
             "cpu_baseline": cpu,
         }
+        if world == 1 and not args.no_extras:
+            line["prefill"] = measure_prefill(Q, E, torch, peaks)
+            line["moe"] = measure_moe(Q, E, torch, peaks)
+            line["large_layer"] = measure_c5(Q, E, torch, peaks)
         if r8 is not None:
             v8 = step_bytes(8) / (r8["ms"] * 1e-3) / 1e9
             line["batch8"] = {"value": round(v8, 2), "unit": "GB/s", "ms_per_step": round(r8["ms"], 4),

@@ -182,9 +182,9 @@ exl3_verdict exl3_matmul_ex(const exl3_weight *w, const exl3_tensor *x, uint32_t
                             exl3_tensor *out);
 
 /* matmul_ex with CUDA events recorded on the stream between its launches, for timing a phase without a profiler.
- * events: 4 cudaEvent_t (any may be NULL) -- [0] before the first launch; on the GEMM path (64 rows and more) [1]
- * after the prepare, [2] after the decode and [3] after the GEMM of the first chunk of rows and columns; on the GEMV
- * path [3] after the last launch.  A measurement aid of this library; the reference has no counterpart. */
+ * events: 4 cudaEvent_t (any may be NULL) -- [0] before the first launch and [3] after the last; on the GEMM path
+ * (64 rows and more) [1] after the operand images (prepare + decode) and [2] after the GEMM of the first chunk of
+ * rows and columns.  A measurement aid of this library; the reference has no counterpart. */
 exl3_verdict exl3_matmul_timed(const exl3_weight *w, const exl3_tensor *x, uint32_t flags, void *stream,
                                exl3_tensor *out, void *const *events);
 

@@ -377,19 +377,21 @@ exl3_verdict check_weight(const exl3_weight* w) {
 // B image of the decoded weights and one tensor-core GEMM into y.  The chunks keep both images inside the workspace's
 // image region, so the call allocates nothing.
 // The GEMM's tile shape for an m x n launch: the fewest tile-waves over the SMs, weighted by the tile's area (its MMA
-// time); on a tie the larger tile, which reads fewer operand bytes per flop.  EXL3_GEMM_SHAPE (0..3) overrides it,
-// for measurement runs.
+// time) and divided by the shape's measured throughput on B200 relative to 256 x 256 (4096 x 12288 at 4 bpw:
+// 128 x 128 0.72, 128 x 256 0.93, 256 x 128 0.83 -- narrower tiles re-read more operand bytes per flop).
+// EXL3_GEMM_SHAPE (0..3) overrides it, for measurement runs.
 int gemm_shape_for(int64_t m, int64_t n, int sms) {
   if (const char* e = getenv("EXL3_GEMM_SHAPE")) {
     const int v = atoi(e);
     if (v >= 0 && v <= 3) return v;
   }
+  static const int64_t kEff[4] = {72, 93, 83, 100};
   int best = 0;
   int64_t best_cost = -1;
-  for (int shape : {3, 1, 2, 0}) {
+  for (int shape : {1, 3, 2, 0}) {
     const int64_t bm = exl3::gemm_block_m(shape), bn = exl3::gemm_block_n(shape);
     const int64_t tiles = ((m + bm - 1) / bm) * ((n + bn - 1) / bn);
-    const int64_t cost = (tiles + sms - 1) / sms * bm * bn;
+    const int64_t cost = (tiles + sms - 1) / sms * bm * bn * 100 / kEff[shape];
     if (best_cost < 0 || cost < best_cost) {
       best = shape;
       best_cost = cost;
@@ -398,7 +400,6 @@ int gemm_shape_for(int64_t m, int64_t n, int sms) {
   return best;
 }
 
-// ev (optional, 4 cudaEvent_t): recorded before the first launch and after the first chunk's prepare, decode and GEMM
 exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32_t x_dtype, int64_t rows, void* y,
                       int32_t y_dtype, uint32_t flags, cudaStream_t st, void* const* ev) {
   bool first = true;
@@ -445,15 +446,14 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
       for (int64_t r0 = 0; r0 < rows; r0 += mc) {
         const int m = static_cast<int>(rows - r0 < mc ? rows - r0 : mc);
         const int mp = (m + bm - 1) / bm * bm;  // padded rows: whole tiles of every shape
-        if (exl3::launch_prep_image(xg + static_cast<size_t>(r0) * x_stride * xsz, x_dtype, x_stride, m, mp,
-                                    in_f, suh, (flags & EXL3_MATMUL_PREPARED) ? 1 : 0, a_img, st) != cudaSuccess)
-          return refuse(EXL3_FAILED, "exl3_b200: prefill prepare launch failed");
-        mark(1);
         for (int j0 = 0; j0 < seg_w; j0 += static_cast<int>(nc_cap)) {
           const int nc = static_cast<int>(seg_w - j0 < nc_cap ? seg_w - j0 : nc_cap);
-          if (exl3::launch_decode_image(trg, in_f, out_f, c0 + j0, nc, w->n, b_img, st) != cudaSuccess)
-            return refuse(EXL3_FAILED, "exl3_b200: prefill decode launch failed");
-          mark(2);
+          // the A image with the first column chunk's B image, in one launch
+          if (exl3::launch_images(xg + static_cast<size_t>(r0) * x_stride * xsz, x_dtype, x_stride, m, mp, suh,
+                                  (flags & EXL3_MATMUL_PREPARED) ? 1 : 0, j0 == 0 ? a_img : nullptr, trg, in_f, out_f,
+                                  c0 + j0, nc, w->n, b_img, st) != cudaSuccess)
+            return refuse(EXL3_FAILED, "exl3_b200: prefill operand images launch failed");
+          mark(1);
           const int shape = gemm_shape_for(m, nc, d->sms);
           const int tbm = exl3::gemm_block_m(shape), tbn = exl3::gemm_block_n(shape);
           exl3::GemmParams gp{};
@@ -474,12 +474,13 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
           gp.err = d->err;
           if (exl3::launch_gemm_image(gp, shape, d->sms, st) != cudaSuccess)
             return refuse(EXL3_FAILED, "exl3_b200: prefill GEMM launch failed");
-          mark(3);
+          mark(2);
           first = false;
         }
       }
     }
   }
+  if (ev && ev[3]) cudaEventRecord(static_cast<cudaEvent_t>(ev[3]), st);
   return kOk;
 }
 
@@ -490,7 +491,11 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
   DeviceState* d = device_state(w->device);
   if (!d) return refuse(EXL3_FAILED, "exl3_b200: no workspace on this device (exl3_open or a weight load creates it)");
   DeviceGuard guard(w->device);
-  const bool gemm = (flags & EXL3_MATMUL_GEMM) != 0 || ((flags & EXL3_MATMUL_GEMV) == 0 && rows >= d->gemm_min_rows);
+  // the GEMM's prepare reads four elements per vector load
+  const size_t vec = x_dtype == EXL3_F32 ? 16 : 8;
+  const bool x_vec = reinterpret_cast<uintptr_t>(x) % vec == 0;
+  const bool gemm = x_vec && ((flags & EXL3_MATMUL_GEMM) != 0 ||
+                              ((flags & EXL3_MATMUL_GEMV) == 0 && rows >= d->gemm_min_rows));
   if (gemm) return run_gemm(d, w, x, x_dtype, rows, y, y_dtype, flags, st, ev);
   if (ev && ev[0]) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
   const int in_f = w->in_features, out_f = w->out_features, groups = w->groups;

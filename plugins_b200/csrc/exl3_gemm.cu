@@ -10,8 +10,9 @@
 // in the UMMA K-major canonical layout with the 128-byte swizzle (row r at byte 128 r, its 16-byte chunk c at chunk
 // c ^ (r % 8)).  One pipeline stage is then a handful of whole blocks that cp.async.bulk copies into shared memory
 // with no tensor map and no re-layout.
-//   A image: [rows/128][in/64] blocks of xp (rows padded to 128 with zeros) -- prep_image_kernel
-//   B image: [cols/128][in/64] blocks of W_hat^T (row = output column)      -- decode_image_kernel, bit-exact decode
+//   A image: [rows/128][in/64] blocks of xp (rows padded with zeros)  -- prepare warps of images_kernel
+//   B image: [cols/128][in/64] blocks of W_hat^T (row = output column) -- decode warps of images_kernel, bit-exact
+// Both images come from one launch: its decode warps and prepare warps run side by side.
 // The GEMM (gemm_image_kernel) is persistent, one CTA per SM, warp-specialised:
 //   warp 0      producer: bulk copies of A and B blocks into a ring of stages (mbarrier tx counts)
 //   warp 1      MMA issuer: tcgen05.mma kind::f16, M = 128 per A block, N = BN, K = 16, accumulators in TMEM (f32)
@@ -140,73 +141,115 @@ __device__ __forceinline__ void fwht128_regs(float (&v)[128]) {
 
 }  // namespace
 
-// ------------------------------------------------------------------ A image: xp rows, swizzled
+// ------------------------------------------------------------------ the operand images, one launch
 
-// One warp per (row, 128-wide input block).  Rows m..mp-1 are written as zeros (padding of the last 128-row block).
-__global__ void __launch_bounds__(256) prep_image_kernel(const void* __restrict__ x, int32_t x_dtype,
-                                                         int64_t x_row_stride, int m, int mp, int in_features,
-                                                         const uint16_t* __restrict__ suh, int prepared,
-                                                         uint8_t* __restrict__ a_img) {
-  const uint32_t lane = threadIdx.x & 31u;
-  const int kblk = in_features / 128;
-  const int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (job >= static_cast<int64_t>(mp) * kblk) return;  // warp-uniform
+constexpr int kDecodeTilesPerWarp = 4;  // consecutive column tiles of one k-row per decode warp (loads issued together)
+
+struct ImageJobs {
+  // A image: xp rows [0, mp) (rows >= m written as zeros); prepared = x already holds xp
+  const void* x;
+  int32_t x_dtype;
+  int64_t x_row_stride;
+  int32_t m, mp, prepared;
+  const uint16_t* suh;
+  uint8_t* a_img;
+  int64_t prep_jobs;     // mp * in/128 warps, 0 = no A image
+  // B image: trellis columns [16 tn0, 16 (tn0 + ncol_tiles))
+  const uint16_t* trellis;
+  int32_t out_tiles, tn0, ncol_tiles;
+  uint8_t* b_img;
+  int64_t decode_jobs;   // (in/16) * ncol_tiles / kDecodeTilesPerWarp warps
+  int32_t in_features;
+};
+
+// Prepare job: one warp per (row, 128-wide input block), lane t holding elements 4t..4t+3 (vector loads and one
+// 8-byte store); the Hadamard's two low stages run in registers, the other five across lanes.
+__device__ __forceinline__ void prep_job(const ImageJobs& j, int64_t job, uint32_t lane) {
+  const int kblk = j.in_features / 128;
   const int row = static_cast<int>(job / kblk), b = static_cast<int>(job % kblk);
+  const int k0 = b * 128 + 4 * static_cast<int>(lane);
   float v[4] = {0.f, 0.f, 0.f, 0.f};
-  if (row < m) {
+  if (row < j.m) {
+    const size_t at = static_cast<size_t>(row) * j.x_row_stride + k0;
+    if (j.x_dtype == kF32) {
+      const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(j.x) + at);
+      v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+    } else {
+      const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(j.x) + at);
+      const uint32_t w2[2] = {u.x, u.y};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int k = b * 128 + static_cast<int>(lane) + 32 * i;
-      const float xv = load_act(x, static_cast<size_t>(row) * x_row_stride + k, x_dtype);
-      v[i] = prepared ? xv : xv * f16_bits_to_float(suh[k]);
+      for (int e = 0; e < 2; ++e) {
+        float2 f;
+        if (j.x_dtype == kF16) f = __half22float2(*reinterpret_cast<const __half2*>(&w2[e]));
+        else f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w2[e]));
+        v[2 * e] = f.x, v[2 * e + 1] = f.y;
+      }
     }
-    if (!prepared) {
-      fwht128_warp(v, lane);
+    if (!j.prepared) {
+      const uint2 su = *reinterpret_cast<const uint2*>(j.suh + k0);
+      const float2 s01 = __half22float2(*reinterpret_cast<const __half2*>(&su.x));
+      const float2 s23 = __half22float2(*reinterpret_cast<const __half2*>(&su.y));
+      v[0] *= s01.x, v[1] *= s01.y, v[2] *= s23.x, v[3] *= s23.y;
+      const float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
+      v[0] = a0 + a2, v[1] = a1 + a3, v[2] = a0 - a2, v[3] = a1 - a3;
+#pragma unroll
+      for (uint32_t bit = 1; bit <= 16; bit <<= 1) {
+        const bool lower = (lane & bit) == 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], bit);
+          v[i] = lower ? v[i] + p : p - v[i];
+        }
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) v[i] *= kHadScale;
     }
   }
-  const int kbs = in_features / kImgK;
+  const __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
   const uint32_t r = static_cast<uint32_t>(row) & 127u;
-  const size_t mb = static_cast<size_t>(row) >> 7;
+  uint8_t* blk = j.a_img + ((static_cast<size_t>(row) >> 7) * (j.in_features / kImgK) + (k0 >> 6)) * kImgBytes;
+  *reinterpret_cast<uint2*>(blk + image_offset(r, static_cast<uint32_t>(k0 & 63))) =
+      make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+}
+
+// Decode job: kDecodeTilesPerWarp consecutive 16x16 tiles of one k-row (contiguous in the trellis).  Each lane holds
+// one column's four consecutive k per tile (the IMMA byte-sum order) and writes them as one 8-byte store; a warp's
+// stores fill whole 32-byte sectors.
+template <int K>
+__device__ __forceinline__ void decode_job(const ImageJobs& j, int64_t job, uint32_t lane) {
+  const int groups = j.ncol_tiles / kDecodeTilesPerWarp;
+  const int tk = static_cast<int>(job / groups), tj0 = static_cast<int>(job % groups) * kDecodeTilesPerWarp;
+  const uint32_t* tw =
+      reinterpret_cast<const uint32_t*>(j.trellis + (static_cast<size_t>(tk) * j.out_tiles + j.tn0 + tj0) * (16 * K));
+  LaneWindows<K> lw;
+  lw.init(lane);
+  ImmaIndicator ind;
+  ind.init(lane);
+  uint32_t w[kDecodeTilesPerWarp][8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int k = b * 128 + static_cast<int>(lane) + 32 * i;
-    uint8_t* blk = a_img + (mb * kbs + (k >> 6)) * kImgBytes;
-    *reinterpret_cast<__half*>(blk + image_offset(r, static_cast<uint32_t>(k & 63))) = __float2half_rn(v[i]);
+  for (int t = 0; t < kDecodeTilesPerWarp; ++t) lane_codewords<K>(tw + t * 8 * K, lw, w[t]);
+  const uint32_t g = lane >> 2, q = lane & 3u;
+  const int kbs = j.in_features / kImgK;
+  const uint32_t kin = static_cast<uint32_t>(tk & 3) * 16u + 4u * q;
+#pragma unroll
+  for (int t = 0; t < kDecodeTilesPerWarp; ++t) {
+    uint32_t a[4];
+    decode_afrag_imma(w[t], ind, a);  // a[0], a[2]: column g at k 4q..4q+3; a[1], a[3]: column g + 8
+    const int tj = tj0 + t;
+    const uint32_t n = static_cast<uint32_t>(tj & 7) * 16u + g;
+    uint8_t* blk = j.b_img + (static_cast<size_t>(tj >> 3) * kbs + (tk >> 2)) * kImgBytes;
+    *reinterpret_cast<uint2*>(blk + image_offset(n, kin)) = make_uint2(a[0], a[2]);
+    *reinterpret_cast<uint2*>(blk + image_offset(n + 8u, kin)) = make_uint2(a[1], a[3]);
   }
 }
 
-// ------------------------------------------------------------------ B image: W_hat^T, decoded once
-
-// One warp per 16x16 trellis tile of the column range [16 tn0, 16 (tn0 + ncol_tiles)); consecutive warps walk a
-// k-row of tiles, which the trellis stores contiguously.  Each lane holds one column's four consecutive k (the IMMA
-// byte-sum order) and writes them as one 8-byte store; a warp's stores fill whole 32-byte sectors.
+// Decode warps first (the longer jobs), then prepare warps; every job is one warp.
 template <int K>
-__global__ void __launch_bounds__(256) decode_image_kernel(const uint16_t* __restrict__ trellis, int in_features,
-                                                           int out_tiles, int tn0, int ncol_tiles,
-                                                           uint8_t* __restrict__ b_img) {
+__global__ void __launch_bounds__(256) images_kernel(const ImageJobs j) {
   const uint32_t lane = threadIdx.x & 31u;
-  const size_t tiles = static_cast<size_t>(in_features / 16) * ncol_tiles;
-  const size_t tile = static_cast<size_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (tile >= tiles) return;  // warp-uniform
-  const int tk = static_cast<int>(tile / ncol_tiles), tj = static_cast<int>(tile % ncol_tiles);
-  const uint32_t* tw =
-      reinterpret_cast<const uint32_t*>(trellis + (static_cast<size_t>(tk) * out_tiles + tn0 + tj) * (16 * K));
-  LaneWindows<K> lw;
-  lw.init(lane);
-  uint32_t w[8], a[4];
-  lane_codewords<K>(tw, lw, w);
-  ImmaIndicator ind;
-  ind.init(lane);
-  decode_afrag_imma(w, ind, a);  // a[0], a[2]: column g at k 4q..4q+3; a[1], a[3]: column g + 8
-  const uint32_t g = lane >> 2, q = lane & 3u;
-  const int kbs = in_features / kImgK;
-  const uint32_t n = static_cast<uint32_t>(tj & 7) * 16u + g;
-  const uint32_t kin = static_cast<uint32_t>(tk & 3) * 16u + 4u * q;
-  uint8_t* blk = b_img + (static_cast<size_t>(tj >> 3) * kbs + (tk >> 2)) * kImgBytes;
-  *reinterpret_cast<uint2*>(blk + image_offset(n, kin)) = make_uint2(a[0], a[2]);
-  *reinterpret_cast<uint2*>(blk + image_offset(n + 8u, kin)) = make_uint2(a[1], a[3]);
+  const int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);  // warp-uniform
+  if (job < j.decode_jobs) decode_job<K>(j, job, lane);
+  else if (job < j.decode_jobs + j.prep_jobs) prep_job(j, job - j.decode_jobs, lane);
 }
 
 // ------------------------------------------------------------------ the GEMM
@@ -429,28 +472,37 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
 
 // ------------------------------------------------------------------ host launchers
 
-cudaError_t launch_prep_image(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, int in_features,
-                              const uint16_t* suh, int prepared, uint8_t* a_img, cudaStream_t st) {
-  if (in_features % 128 != 0 || mp % 128 != 0 || m > mp) return cudaErrorInvalidValue;
-  const int64_t jobs = static_cast<int64_t>(mp) * (in_features / 128);
-  prep_image_kernel<<<static_cast<unsigned>((jobs + 7) / 8), 256, 0, st>>>(x, x_dtype, x_row_stride, m, mp,
-                                                                            in_features, suh, prepared, a_img);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_decode_image(const uint16_t* trellis, int in_features, int out_features, int col0, int ncols, int n,
-                                uint8_t* b_img, cudaStream_t st) {
-  if (n % 16 != 0 || in_features % 64 != 0 || col0 % 128 != 0 || ncols % 128 != 0) return cudaErrorInvalidValue;
-  const size_t tiles = static_cast<size_t>(in_features / 16) * (ncols / 16);
-  const dim3 grid(static_cast<unsigned>((tiles + 7) / 8)), block(256);
-  const int ot = out_features / 16, tn0 = col0 / 16, nt = ncols / 16;
+cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, const uint16_t* suh,
+                          int prepared, uint8_t* a_img, const uint16_t* trellis, int in_features, int out_features,
+                          int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st) {
+  if (in_features % 128 != 0 || n % 16 != 0) return cudaErrorInvalidValue;
+  ImageJobs j{};
+  j.in_features = in_features;
+  if (a_img) {
+    if (mp % 128 != 0 || m > mp) return cudaErrorInvalidValue;
+    const size_t vec = x_dtype == kF32 ? 16 : 8;  // four elements per vector load
+    if (reinterpret_cast<uintptr_t>(x) % vec != 0 || (x_row_stride * (x_dtype == kF32 ? 4 : 2)) % vec != 0)
+      return cudaErrorInvalidValue;
+    j.x = x, j.x_dtype = x_dtype, j.x_row_stride = x_row_stride;
+    j.m = m, j.mp = mp, j.prepared = prepared, j.suh = suh, j.a_img = a_img;
+    j.prep_jobs = static_cast<int64_t>(mp) * (in_features / 128);
+  }
+  if (b_img) {
+    if (col0 % 128 != 0 || ncols % 128 != 0) return cudaErrorInvalidValue;
+    j.trellis = trellis, j.out_tiles = out_features / 16, j.tn0 = col0 / 16, j.ncol_tiles = ncols / 16;
+    j.b_img = b_img;
+    j.decode_jobs = static_cast<int64_t>(in_features / 16) * (ncols / 16) / kDecodeTilesPerWarp;
+  }
+  const int64_t warps = j.prep_jobs + j.decode_jobs;
+  if (warps == 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>((warps + 7) / 8)), block(256);
   switch (n / 16) {
-    case 1: decode_image_kernel<1><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
-    case 2: decode_image_kernel<2><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
-    case 3: decode_image_kernel<3><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
-    case 4: decode_image_kernel<4><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
-    case 5: decode_image_kernel<5><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
-    case 6: decode_image_kernel<6><<<grid, block, 0, st>>>(trellis, in_features, ot, tn0, nt, b_img); break;
+    case 1: images_kernel<1><<<grid, block, 0, st>>>(j); break;
+    case 2: images_kernel<2><<<grid, block, 0, st>>>(j); break;
+    case 3: images_kernel<3><<<grid, block, 0, st>>>(j); break;
+    case 4: images_kernel<4><<<grid, block, 0, st>>>(j); break;
+    case 5: images_kernel<5><<<grid, block, 0, st>>>(j); break;
+    case 6: images_kernel<6><<<grid, block, 0, st>>>(j); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -67,12 +67,11 @@ struct GemmParams {
   uint32_t* err;
 };
 
-// xp rows [0, mp) as an A image (rows >= m are zeros); prepared = x already holds xp
-cudaError_t launch_prep_image(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, int in_features,
-                              const uint16_t* suh, int prepared, uint8_t* a_img, cudaStream_t st);
-// the trellis columns [col0, col0 + ncols) as a B image
-cudaError_t launch_decode_image(const uint16_t* trellis, int in_features, int out_features, int col0, int ncols, int n,
-                                uint8_t* b_img, cudaStream_t st);
+// One launch writes the A image of xp rows [0, mp) (rows >= m are zeros; prepared = x already holds xp; skipped when
+// a_img is null) and the B image of the trellis columns [col0, col0 + ncols) (skipped when b_img is null).
+cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, const uint16_t* suh,
+                          int prepared, uint8_t* a_img, const uint16_t* trellis, int in_features, int out_features,
+                          int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st);
 // shape: 0 = 128x128 tiles, 1 = 128x256, 2 = 256x128, 3 = 256x256 (rows x columns)
 int gemm_block_m(int shape);
 int gemm_block_n(int shape);

@@ -3,9 +3,10 @@
     python -m plugins_b200.profile_gemm [--in 4096] [--out 12288] [--n 64] [--rows 64,256,2048,8192] [--reps 10]
                                         [--gemv-up-to 256] [--shape S]
 
-For each row count: the whole matmul and each of its phases, timed with CUDA events recorded between the launches
-(exl3_matmul_timed) over `reps` calls after warm-up, medians reported; the GEMM kernel's TFLOP/s (2 M in out flops)
-and the decode's bytes (trellis read + B image written); and, up to --gemv-up-to rows, the same rows forced through
+For each row count: the whole matmul and its two launches (the operand images: prepare + decode; the GEMM), timed
+with CUDA events recorded between the launches (exl3_matmul_timed) over `reps` calls after warm-up, medians
+reported; the GEMM kernel's TFLOP/s (2 M in out flops) and the images' bytes (x read, trellis read, A and B images
+written); and, up to --gemv-up-to rows, the same rows forced through
 the decode GEMV, for the crossover.  One JSON line per row count.  With --shape the GEMM's tile shape is fixed
 (EXL3_GEMM_SHAPE).  Under `ncu -k regex:gemm_image_kernel` it is also the capture target for kernel profiles.
 """
@@ -34,18 +35,15 @@ def _events():
 def time_call(w, x, out, flags, reps, warmup=3):
     for _ in range(warmup):
         Q.matmul_timed(w, x, [None] * 4, flags=flags, out=out)
-    phases = {"total": [], "prepare": [], "decode": [], "gemm": []}
+    phases = {"total": [], "images": [], "gemm": []}
     for _ in range(reps):
         ev = _events()
-        end = torch.cuda.Event(enable_timing=True)
         Q.matmul_timed(w, x, ev, flags=flags, out=out)
-        end.record()
         torch.cuda.synchronize()
-        phases["total"].append(ev[0].elapsed_time(end))
-        if flags & GEMM or not flags & GEMV:
-            phases["prepare"].append(ev[0].elapsed_time(ev[1]))
-            phases["decode"].append(ev[1].elapsed_time(ev[2]))
-            phases["gemm"].append(ev[2].elapsed_time(ev[3]))
+        phases["total"].append(ev[0].elapsed_time(ev[3]))
+        if flags & GEMM:
+            phases["images"].append(ev[0].elapsed_time(ev[1]))
+            phases["gemm"].append(ev[1].elapsed_time(ev[2]))
     return {k: statistics.median(v) for k, v in phases.items() if v}
 
 
@@ -69,11 +67,11 @@ def main() -> None:
         out = torch.empty((m, a.out_f), device="cuda", dtype=torch.bfloat16)
         t = time_call(w, x, out, GEMM, a.reps)
         flops = 2.0 * m * a.in_f * a.out_f
-        dec_bytes = a.in_f * a.out_f * (a.n / 128 + 2)
+        img_bytes = a.in_f * a.out_f * (a.n / 128 + 2) + m * a.in_f * 4
         rec = {"rows": m, "in": a.in_f, "out": a.out_f, "n": a.n, "ms": {k: round(v, 4) for k, v in t.items()},
                "gemm_tflops": round(flops / (t["gemm"] * 1e-3) / 1e12, 1),
                "total_tflops": round(flops / (t["total"] * 1e-3) / 1e12, 1),
-               "decode_gbs": round(dec_bytes / (t["decode"] * 1e-3) / 1e9, 1)}
+               "images_gbs": round(img_bytes / (t["images"] * 1e-3) / 1e9, 1)}
         if m <= a.gemv_up_to:
             g = time_call(w, x, out, GEMV, a.reps)
             rec["gemv_ms"] = round(g["total"], 4)

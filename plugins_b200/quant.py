@@ -221,8 +221,8 @@ def matmul_ex(w: Weight, x: torch.Tensor, flags: int = 0, stream=None, out: torc
 
 def matmul_timed(w: Weight, x: torch.Tensor, events, flags: int = 0, stream=None,
                  out: torch.Tensor | None = None) -> torch.Tensor:
-    """matmul_ex recording four torch.cuda.Event (or None) between its launches: [0] before the first, then (GEMM
-    path) after the prepare, the decode and the GEMM of the first chunk; (GEMV path) [3] after the last launch."""
+    """matmul_ex recording four torch.cuda.Event (or None) between its launches: [0] before the first and [3] after
+    the last; on the GEMM path [1] after the operand images (prepare + decode) and [2] after the first GEMM."""
     shape = list(x.shape[:-1]) + [w.out_features]
     if out is None:
         dt = torch.float32 if flags & L.MATMUL_INNER else (torch.float16 if flags & L.MATMUL_PREPARED else x.dtype)

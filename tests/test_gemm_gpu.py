@@ -178,3 +178,16 @@ def test_prefill_layer_at_full_size(Q, E, oracle):
     ref = Q.matmul_ex(w, x, flags=GEMV)
     assert float(((y.float() - ref.float()).norm() / ref.float().norm()).item()) < REL_L2_BAR
     assert Q.device_error(0) == 0
+
+
+def test_unaligned_rows_take_the_gemv(Q, E, oracle):
+    # rows that start off an 8-byte boundary cannot feed the prepare's vector loads: the decode GEMV serves them
+    in_f, out_f, n, rows = 512, 384, 64, 80
+    tr, suh, svh = E.random_linear(in_f, out_f, n, seed=31)
+    w = Q.weight_from_tensors(tr, suh, svh)
+    buf = torch.randn(rows * in_f + 1, device="cuda").to(torch.float16)
+    x = buf[1:].view(rows, in_f)
+    assert x.data_ptr() % 8 != 0
+    y = Q.matmul(w, x)
+    want = _truth(oracle, x, tr, suh, svh, in_f, out_f, n)
+    assert _rel(y.float().cpu().numpy(), want) < REL_L2_BAR
