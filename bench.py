@@ -166,6 +166,75 @@ def measure_moe(Q, E, torch, peaks: dict, reps: int = 10) -> dict:
             "l2": "no flush: a call streams %.2f GB of distinct experts (> 126 MB L2)" % (nbytes / 1e9)}
 
 
+def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict, steps: int = 20) -> dict:
+    """Config 4 expert-parallel over the ranks (plugins_b200/sharding.py): rank r holds experts [32 r', ...) of the 256
+    (256/world each) plus the shared expert, brings 32/world of the 32 tokens, and a step is dispatch, all-to-all,
+    its experts' SwiGLU, all-to-all back, the shared expert and the combine -- captured in one CUDA graph (NCCL inside)
+    and timed as the max over ranks.  Bytes are the distinct routed experts each rank streams plus its shared
+    expert, summed over the ranks."""
+    from plugins_b200 import sharding as S
+    experts, hidden, inter, topk, total = 256, 4096, 2048, 8, 32
+    tokens = total // world
+    e0, e1 = S.expert_range(experts, rank, world)
+    local, shared = [], []
+    for i, (a, b) in enumerate(((hidden, inter), (hidden, inter), (inter, hidden))):
+        tr, suh, svh = E.random_linear(a, b, 48, seed=3 + i, groups=experts, device=device)
+        local.append(Q.weight_from_tensors(tr[e0:e1].contiguous(), suh[e0:e1].contiguous(), svh[e0:e1].contiguous()))
+        del tr, suh, svh
+        tr, suh, svh = E.random_linear(a, b, 48, seed=13 + i, groups=1, device=device)
+        shared.append(Q.weight_from_tensors(tr, suh, svh))
+    g = torch.Generator(device=device).manual_seed(4)
+    logits = torch.randn((total, experts), device=device, generator=g)
+    sc, ind = torch.topk(torch.softmax(logits, -1), topk, -1)
+    x_all = torch.randn((total, hidden), device=device, generator=g).half()
+    sl = slice(rank * tokens, (rank + 1) * tokens)
+    x, ind, sc = x_all[sl].contiguous(), ind[sl].to(torch.int32).contiguous(), sc[sl].float().contiguous()
+    ep = S.ExpertParallelSwiglu(*local, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=rank,
+                                world=world, device=device, shared=shared)
+    y = torch.empty_like(x)
+    st = torch.cuda.Stream(device=device)
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        for _ in range(3):
+            ep.forward(x, ind, sc, out=y)
+    torch.cuda.current_stream().wait_stream(st)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        ep.forward(x, ind, sc, out=y)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        graph.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    per_expert = 3 * (hidden * inter * 3 // 8 + 2 * hidden + 2 * inter)
+    all_ind = torch.topk(torch.softmax(logits, -1), topk, -1)[1]
+    mine = int(((torch.unique(all_ind) >= e0) & (torch.unique(all_ind) < e1)).sum().item())
+    stats = torch.tensor([ms, float((mine + 1) * per_expert)], device=device, dtype=torch.float64)
+    if world > 1:
+        t = stats[:1].clone()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        b = stats[1:].clone()
+        dist.all_reduce(b, op=dist.ReduceOp.SUM)
+        stats = torch.cat([t, b])
+    graph.reset()
+    ms, nbytes = float(stats[0]), float(stats[1])
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": "config 4 expert-parallel: 256 routed (256/N per GPU) + 1 shared expert, 4096 <-> 2048 "
+                        "@ 3 bpw, 32 tokens (32/N per GPU), top-8; NCCL all-to-all dispatch and combine",
+            "n_gpus": world, "ms_per_step": round(ms, 4), "tokens_per_s": round(total / (ms * 1e-3), 1),
+            "value": round(gbs, 1), "unit": "GB/s (whole box)", "bytes_per_step": int(nbytes),
+            "frac_of_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4)}
+
+
 def measure_c5(Q, E, torch, peaks: dict, reps: int = 5) -> dict:
     """Config 5: K = 16384, N = 53248 at 2, 3, 4 and 5 bpw (random trellis, seed 5), batch-1 f16, one GPU."""
     in_f, out_f = 16384, 53248
@@ -489,6 +558,7 @@ def main() -> None:
 
     peaks = load_peaks()
     r1 = run_config(args.batch, args.steps, args.warmup)
+    moe_ep = None if args.no_extras else measure_moe_ep(Q, E, torch, dist, rank, world, device, peaks)
     r8 = None if (args.no_batch8 or args.batch == 8) else run_config(8, args.steps, args.warmup)
     total = step_bytes(args.batch)
     value = total / (r1["ms"] * 1e-3) / 1e9
@@ -540,6 +610,8 @@ def main() -> None:
             "clocks": r1["clk"],
             "cpu_baseline": cpu,
         }
+        if moe_ep is not None:
+            line["moe_ep"] = moe_ep
         if world == 1 and not args.no_extras:
             line["prefill"] = measure_prefill(Q, E, torch, peaks)
             line["moe"] = measure_moe(Q, E, torch, peaks)

@@ -169,8 +169,8 @@ exl3_verdict exl3_moe(const exl3_weight *bank, const exl3_tensor *x, const exl3_
                       int32_t sorted, void *stream, exl3_tensor *out);
 
 /* swiglu (plugin.zig:267-283; SX/root.zig:32-167): routed SwiGLU experts.  x [B, S, D]; inds [B, S, K] (i32/u32)
- * and scores [B, S, K] (f32) pick the banks' experts; out [B, S, D] in x's dtype is
- * sum_k score * down_e(silu(gate_e(x)) * up_e(x)). */
+ * and scores [B, S, K] (f32) pick the banks' experts; out [B, S, D] in x's dtype (or f32) is
+ * sum_k score * down_e(silu(gate_e(x)) * up_e(x)).  Expert indices outside the bank contribute nothing. */
 exl3_verdict exl3_swiglu(const exl3_weight *gate, const exl3_weight *up, const exl3_weight *down,
                          const exl3_tensor *x, const exl3_tensor *inds, const exl3_tensor *scores,
                          const exl3_swiglu_opts *opts, void *stream, exl3_tensor *out);
@@ -187,6 +187,25 @@ exl3_verdict exl3_matmul_ex(const exl3_weight *w, const exl3_tensor *x, uint32_t
  * rows and columns.  A measurement aid of this library; the reference has no counterpart. */
 exl3_verdict exl3_matmul_timed(const exl3_weight *w, const exl3_tensor *x, uint32_t flags, void *stream,
                                exl3_tensor *out, void *const *events);
+
+/* ------------------------------------------------------------------ expert parallelism (beside the seam)
+ *
+ * The reference runs on one device; these three calls are this library's expert-parallel split of swiglu over ranks
+ * (rank r owns experts [r E/world, (r+1) E/world) of every bank), around two equal-split all-to-alls that the caller
+ * issues (NCCL).  A dispatch buffer is [world, C + 1, D] in x's dtype: per peer, C token rows in slot order and one
+ * metadata row whose 32-bit word j is row j's peer-local expert (-1 = empty).  EXL3_ERR_EP_OVERFLOW in the device
+ * error word marks a dispatch that had more than C rows for one peer (the extra slots are dropped). */
+
+/* x [T, D], inds [T, K] (global expert ids; outside 0..experts-1 = absent) -> send [world, C + 1, D] and
+ * back_slot [T, K] i32: the row of the returned buffer that holds slot (t, k), -1 if absent or dropped. */
+exl3_verdict exl3_ep_dispatch(const exl3_tensor *x, const exl3_tensor *inds, int32_t experts, int32_t world,
+                              void *stream, exl3_tensor *send, exl3_tensor *back_slot);
+/* received blocks [world, C + 1, D] -> swiglu's inds [world, C + 1, 1] i32 (metadata rows -1) and scores (all 1). */
+exl3_verdict exl3_ep_unpack(const exl3_tensor *recv, void *stream, exl3_tensor *inds, exl3_tensor *scores);
+/* out [T, D] = sum_k scores[t, k] * back[back_slot[t, k]] in k order (f32), + shared [T, D] f32 when its data is not
+ * NULL; back is f32 [world, C + 1, D] (the owners' swiglu outputs returned by the second all-to-all). */
+exl3_verdict exl3_ep_combine(const exl3_tensor *back, const exl3_tensor *back_slot, const exl3_tensor *scores,
+                             const exl3_tensor *shared, void *stream, exl3_tensor *out);
 
 /* A borrowed view of device arrays already in the pack layout (the reference's shared handles, plugin.zig:213-218):
  * validates the shapes and creates the device workspace; exl3_release on a view frees nothing. */
@@ -217,7 +236,10 @@ exl3_verdict exl3_encode_trellis(const float *target, int32_t in_features, int32
  * capture.  All calls share the array: calls that overlap on the GPU race -- order them on one stream. */
 exl3_verdict exl3_matmul_noalloc(const exl3_weight *w, const exl3_tensor *x, void *stream, exl3_tensor *out);
 
-/* Device error bits the kernels recorded on `device` (bounded waits that gave up); `clear` resets them. */
+/* Device error bits the kernels recorded on `device`; `clear` resets them. */
+#define EXL3_ERR_WAIT_TIMEOUT 1u  /* a bounded mbarrier wait gave up (the kernel left its loop and returned) */
+#define EXL3_ERR_BAD_SHAPE 2u     /* a launch saw a shape its host validation should have refused */
+#define EXL3_ERR_EP_OVERFLOW 4u   /* an expert-parallel dispatch had more rows for one peer than its capacity */
 exl3_verdict exl3_device_error(int32_t device, uint32_t *bits, int32_t clear);
 
 /* The library's build string. */

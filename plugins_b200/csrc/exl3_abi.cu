@@ -216,6 +216,12 @@ struct DeviceGuard {
 
 namespace exl3 {
 __device__ uint32_t g_device_error;  // kErr* bits, one word per device
+
+uint32_t* device_error_ptr() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+  return static_cast<uint32_t*>(p);
+}
 }
 
 namespace {

@@ -23,6 +23,7 @@ constexpr float kHadScale = 0.08838834764831845f;
 enum : uint32_t {
   kErrWaitTimeout = 1u << 0,   // a bounded mbarrier wait gave up
   kErrBadShape = 1u << 1,      // a launch saw a shape its host validation should have refused
+  kErrEpOverflow = 1u << 2,    // an expert-parallel dispatch had more rows for one peer than its capacity
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

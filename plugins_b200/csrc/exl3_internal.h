@@ -77,5 +77,8 @@ int gemm_block_m(int shape);
 int gemm_block_n(int shape);
 cudaError_t launch_gemm_image(const GemmParams& p, int shape, int sms, cudaStream_t st);
 
+// the device error word of the current device (exl3_device_error reads it), or null
+uint32_t* device_error_ptr();
+
 
 }  // namespace exl3

@@ -49,7 +49,8 @@ struct MoeParams {
   const void* inds;   // [rows][topk]
   int32_t inds_u32;
   const float* scores;  // [rows][topk] f32
-  void* y;            // [rows][hidden]
+  void* y;            // [rows][hidden], in y_dtype (x's dtype or f32)
+  int32_t y_dtype;
   int32_t rows, topk, row0;  // this pass: rows row0 .. row0 + rows - 1 of the call
   float limit;
   // scratch
@@ -349,7 +350,7 @@ __global__ void __launch_bounds__(128) moe_combine_kernel(MoeParams p) {
     const int pos = s_pos[k];
     if (pos >= 0) acc += p.scores[static_cast<size_t>(p.row0 + r) * p.topk + k] * p.dout[static_cast<size_t>(pos) * p.hidden + c];
   }
-  store_act(p.y, static_cast<size_t>(p.row0 + r) * p.hidden + c, acc, p.x_dtype);
+  store_act(p.y, static_cast<size_t>(p.row0 + r) * p.hidden + c, acc, p.y_dtype);
 }
 
 // ---------------------------------------------------------------- host
@@ -488,7 +489,8 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   if (x->dtype != EXL3_F16 && x->dtype != EXL3_BF16 && x->dtype != EXL3_F32) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (x)");
   if (inds->dtype != EXL3_I32 && inds->dtype != EXL3_U32) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (inds)");
   if (scores->dtype != EXL3_F32) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (scores are f32)");
-  if (out->dtype != x->dtype) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (out)");
+  if (out->dtype != x->dtype && out->dtype != EXL3_F32)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (out is x's dtype or f32)");
   const int inter = gate->out_features;
   const int experts = gate->groups;
   if (hidden <= 0 || hidden % 128 != 0 || inter <= 0 || inter % 128 != 0)
@@ -520,7 +522,7 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   p.x = x->data; p.x_dtype = x->dtype;
   p.inds = inds->data; p.inds_u32 = inds->dtype == EXL3_U32;
   p.scores = static_cast<const float*>(scores->data);
-  p.y = out->data; p.topk = topk; p.limit = static_cast<float>(limit);
+  p.y = out->data; p.y_dtype = out->dtype; p.topk = topk; p.limit = static_cast<float>(limit);
   int32_t* ints = reinterpret_cast<int32_t*>(sc->base);
   p.order = ints;
   p.chunk_e = ints + kMaxSlots;

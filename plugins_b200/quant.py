@@ -19,6 +19,7 @@ from . import _lib as L
 from ._lib import Exl3Error, check
 
 __all__ = ["Exl3Error", "Weight", "LoadContext", "claims", "validate", "bill", "matmul", "matmul_ex", "moe", "swiglu",
+           "ep_dispatch", "ep_unpack", "ep_combine",
            "release", "weight_from_tensors", "stack", "decode_dense", "device_error", "CLAIM_NO", "CLAIM_BY_MARKER"]
 
 CLAIM_NO, CLAIM_BY_MODE, CLAIM_BY_MARKER = L.CLAIM_NO, L.CLAIM_BY_MODE, L.CLAIM_BY_MARKER
@@ -308,6 +309,28 @@ def decode_dense(w: Weight, group: int = 0, dp4a: bool = False, stream=None) -> 
     check(L.lib().exl3_decode_dense(ctypes.byref(w.raw), group, out.data_ptr(), L.MATMUL_DP4A if dp4a else 0,
                                     _stream(stream)))
     return out
+
+
+def ep_dispatch(x: torch.Tensor, inds: torch.Tensor, experts: int, world: int, send: torch.Tensor,
+                back_slot: torch.Tensor, stream=None) -> None:
+    """Expert-parallel dispatch: x [T, D], inds [T, K] -> send [world, C + 1, D] (x's dtype), back_slot [T, K] i32."""
+    check(L.lib().exl3_ep_dispatch(ctypes.byref(_tensor(x)), ctypes.byref(_tensor(inds)), int(experts), int(world),
+                                   _stream(stream), ctypes.byref(_tensor(send)), ctypes.byref(_tensor(back_slot))))
+
+
+def ep_unpack(recv: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor, stream=None) -> None:
+    """Received blocks [world, C + 1, D] -> swiglu's inds [world, C + 1, 1] i32 and scores (all 1) f32."""
+    check(L.lib().exl3_ep_unpack(ctypes.byref(_tensor(recv)), _stream(stream), ctypes.byref(_tensor(inds)),
+                                 ctypes.byref(_tensor(scores))))
+
+
+def ep_combine(back: torch.Tensor, back_slot: torch.Tensor, scores: torch.Tensor, shared: torch.Tensor | None,
+               out: torch.Tensor, stream=None) -> None:
+    """out [T, D] = sum_k scores[t, k] * back[back_slot[t, k]] (k order, f32) + shared [T, D] f32 (optional)."""
+    sh = _tensor(shared) if shared is not None else L.Tensor()
+    check(L.lib().exl3_ep_combine(ctypes.byref(_tensor(back)), ctypes.byref(_tensor(back_slot)),
+                                  ctypes.byref(_tensor(scores)), ctypes.byref(sh), _stream(stream),
+                                  ctypes.byref(_tensor(out))))
 
 
 def device_error(device: int = 0, clear: bool = False) -> int:

@@ -1,0 +1,183 @@
+"""The decode path across the GPUs of one box: one process per GPU, torch.distributed over NCCL for the exchanges.
+
+Two splits, the only two the path has (the reference runs on one device; these are this library's):
+
+* Column parallelism for a linear (``ColumnParallelLinear``): rank r keeps the trellis tiles of its 128-aligned range
+  of output columns, the whole suh and its slice of svh; x is replicated; every rank computes its columns and one
+  all-gather assembles y.  No other exchange: the input Hadamard is per 128-row block of the input and the output
+  Hadamard per 128-column block of the output, so both stay inside a shard.
+
+* Expert parallelism for the routed experts (``ExpertParallelSwiglu``): rank r keeps experts
+  [r E/world, (r+1) E/world) of every bank; each rank's tokens are dispatched to the experts' owners and the results
+  combined back with two equal-split all-to-alls (exl3_ep_dispatch / exl3_ep_unpack / exl3_ep_combine around them).
+  A shared expert, when given, runs where the tokens live.
+
+The drivers take their compute as an ``ops`` object (default: the CUDA library) and their exchanges from
+torch.distributed, so the same sequence of collectives runs over NCCL on GPUs and over gloo with CPU stand-ins in
+the tests.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import quant as Q
+
+COL_BLOCK = 128  # output columns per Hadamard block: the unit a column shard is made of
+
+
+def column_range(out_features: int, rank: int, world: int) -> tuple[int, int]:
+    """Rank r's output columns [c0, c1): whole 128-column blocks, the first (blocks % world) ranks one block more."""
+    if out_features % COL_BLOCK:
+        raise ValueError("out_features must be a multiple of 128")
+    blocks = out_features // COL_BLOCK
+    if blocks < world:
+        raise ValueError(f"{blocks} column blocks cannot be split over {world} ranks")
+    base, extra = divmod(blocks, world)
+    b0 = rank * base + min(rank, extra)
+    b1 = b0 + base + (1 if rank < extra else 0)
+    return b0 * COL_BLOCK, b1 * COL_BLOCK
+
+
+def shard_columns(tr: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, rank: int, world: int):
+    """This rank's column shard of a linear in the pack layout: trellis [in/16, out/16, n] -> [in/16, cols/16, n],
+    suh whole, svh [c0:c1]."""
+    c0, c1 = column_range(svh.shape[-1], rank, world)
+    return tr[:, c0 // 16:c1 // 16, :].contiguous(), suh, svh[c0:c1].contiguous()
+
+
+class CudaLinearOps:
+    """The compute of the column-parallel linear: the library's matmul."""
+
+    @staticmethod
+    def load(tr, suh, svh):
+        return Q.weight_from_tensors(tr, suh, svh)
+
+    @staticmethod
+    def matmul(w, x, out=None):
+        return Q.matmul(w, x, out=out)
+
+
+class ColumnParallelLinear:
+    """y = x @ W^T with W's output columns split over the ranks and y all-gathered.
+
+    Every rank passes the full linear (the pack is readable everywhere) and keeps its shard.  Shards may differ by
+    one 128-column block; the gather runs over equal blocks padded to the largest shard and the padding is dropped
+    when y is assembled.
+    """
+
+    def __init__(self, tr, suh, svh, rank: int, world: int, group=None, ops=None):
+        self.rank, self.world, self.group = rank, world, group
+        self.ops = ops or CudaLinearOps()
+        self.out_features = svh.shape[-1]
+        self.ranges = [column_range(self.out_features, r, world) for r in range(world)]
+        self.width = max(c1 - c0 for c0, c1 in self.ranges)
+        self.weight = self.ops.load(*shard_columns(tr, suh, svh, rank, world))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        rows = x.shape[0]
+        c0, c1 = self.ranges[self.rank]
+        mine = c1 - c0
+        local = torch.empty((rows, self.width), dtype=x.dtype, device=x.device)
+        if mine == self.width:
+            self.ops.matmul(self.weight, x, local)
+        else:
+            local[:, mine:].zero_()
+            local[:, :mine].copy_(self.ops.matmul(self.weight, x, None))
+        if self.world == 1:
+            return local
+        gathered = torch.empty((self.world * rows, self.width), dtype=x.dtype, device=x.device)  # concatenated form
+        dist.all_gather_into_tensor(gathered, local, group=self.group)
+        gathered = gathered.view(self.world, rows, self.width)
+        return torch.cat([gathered[r, :, :b - a] for r, (a, b) in enumerate(self.ranges)], dim=1)
+
+
+# ------------------------------------------------------------------ expert parallelism
+
+def expert_range(experts: int, rank: int, world: int) -> tuple[int, int]:
+    if experts % world:
+        raise ValueError(f"{experts} experts do not split evenly over {world} ranks")
+    per = experts // world
+    return rank * per, (rank + 1) * per
+
+
+def ep_capacity(tokens: int, topk: int, experts: int, world: int) -> int:
+    """Rows one rank can route to one peer: each token sends at most min(K, E/world) distinct experts there."""
+    return max(1, tokens * min(topk, experts // world))
+
+
+class CudaExpertOps:
+    """The compute of the expert-parallel step: the library's dispatch, unpack, swiglu and combine."""
+
+    @staticmethod
+    def dispatch(x, inds, experts, world, send, back_slot):
+        Q.ep_dispatch(x, inds, experts, world, send, back_slot)
+
+    @staticmethod
+    def unpack(recv, inds, scores):
+        Q.ep_unpack(recv, inds, scores)
+
+    @staticmethod
+    def swiglu(gate, up, down, x, inds, scores, out, limit):
+        Q.swiglu(gate, up, down, x, inds, scores, limit=limit, out=out)
+
+    @staticmethod
+    def combine(back, back_slot, scores, shared, out):
+        Q.ep_combine(back, back_slot, scores, shared, out)
+
+
+class ExpertParallelSwiglu:
+    """Routed SwiGLU experts split over the ranks.
+
+    gate/up/down: this rank's banks (experts [r E/world, (r+1) E/world)); shared: an optional (gate, up, down) triple
+    of one-expert banks that every rank holds; tokens: the tokens each rank brings per step (the same on every rank,
+    so every block of the exchange has the same size).  ``forward(x [T, D], inds [T, K], scores [T, K])`` returns
+    out [T, D] in x's dtype: sum_k scores * expert(x) over the routed experts, plus the shared expert.
+    """
+
+    def __init__(self, gate, up, down, experts: int, tokens: int, topk: int, hidden: int, rank: int, world: int,
+                 dtype=torch.float16, device=None, group=None, shared=None, limit: int = 0, ops=None):
+        self.gate, self.up, self.down, self.shared = gate, up, down, shared
+        self.experts, self.tokens, self.topk, self.hidden = experts, tokens, topk, hidden
+        self.rank, self.world, self.group, self.limit = rank, world, group, limit
+        self.ops = ops or CudaExpertOps()
+        self.cap = ep_capacity(tokens, topk, experts, world)
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        blk = (world, self.cap + 1, hidden)
+        self.send = torch.empty(blk, dtype=dtype, device=dev)
+        self.recv = torch.empty(blk, dtype=dtype, device=dev)
+        self.ys = torch.empty(blk, dtype=torch.float32, device=dev)
+        self.back = torch.empty(blk, dtype=torch.float32, device=dev)
+        self.r_inds = torch.empty((world, self.cap + 1, 1), dtype=torch.int32, device=dev)
+        self.r_scores = torch.empty((world, self.cap + 1, 1), dtype=torch.float32, device=dev)
+        self.back_slot = torch.empty((tokens, topk), dtype=torch.int32, device=dev)
+        if shared is not None:
+            self.sh_out = torch.empty((1, tokens, hidden), dtype=torch.float32, device=dev)
+            self.sh_inds = torch.zeros((1, tokens, 1), dtype=torch.int32, device=dev)
+            self.sh_scores = torch.ones((1, tokens, 1), dtype=torch.float32, device=dev)
+
+    def _all_to_all(self, out, inp):
+        if self.world == 1:
+            out.copy_(inp)
+        else:
+            dist.all_to_all_single(out, inp, group=self.group)
+
+    def forward(self, x: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor, out: torch.Tensor | None = None):
+        if x.shape != (self.tokens, self.hidden) or inds.shape != (self.tokens, self.topk):
+            raise ValueError("x [tokens, hidden] and inds [tokens, topk] of the shapes the driver was built for")
+        ops = self.ops
+        ops.dispatch(x, inds, self.experts, self.world, self.send, self.back_slot)
+        self._all_to_all(self.recv, self.send)
+        ops.unpack(self.recv, self.r_inds, self.r_scores)
+        ops.swiglu(self.gate, self.up, self.down, self.recv, self.r_inds, self.r_scores, self.ys, self.limit)
+        self._all_to_all(self.back, self.ys)
+        shared = None
+        if self.shared is not None:
+            sg, su, sd = self.shared
+            ops.swiglu(sg, su, sd, x.view(1, self.tokens, self.hidden), self.sh_inds, self.sh_scores, self.sh_out,
+                       self.limit)
+            shared = self.sh_out.view(self.tokens, self.hidden)
+        if out is None:
+            out = torch.empty_like(x)
+        ops.combine(self.back, self.back_slot, scores, shared, out)
+        return out
