@@ -840,14 +840,16 @@ exl3_verdict exl3_encode_trellis(const float* target, int32_t in_features, int32
 }
 
 exl3_verdict exl3_device_error(int32_t device, uint32_t* bits, int32_t clear) {
-  DeviceState* d = device_state(device);
-  if (!d || !bits) return refuse(EXL3_FAILED, "exl3_b200: no workspace on this device");
+  if (!bits || device < 0 || device >= kMaxDevices) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
   DeviceGuard guard(device);
-  if (cudaMemcpy(bits, d->err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return refuse(EXL3_FAILED, "exl3_b200: read failed");
+  uint32_t* err = exl3::device_error_ptr();  // the word exists on every device, workspace or not
+  if (!err) return refuse(EXL3_FAILED, "exl3_b200: no device error word on this device");
+  if (cudaMemcpy(bits, err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return refuse(EXL3_FAILED, "exl3_b200: read failed");
   if (clear) {
     // a launch that gave up may have left block counters raised: reset them with the error word
-    if (cudaMemset(d->err, 0, 4) != cudaSuccess || cudaMemset(d->counters, 0, kCounterCount * 4) != cudaSuccess ||
-        cudaDeviceSynchronize() != cudaSuccess)
+    DeviceState* d = device_state(device);
+    if (cudaMemset(err, 0, 4) != cudaSuccess ||
+        (d && cudaMemset(d->counters, 0, kCounterCount * 4) != cudaSuccess) || cudaDeviceSynchronize() != cudaSuccess)
       return refuse(EXL3_FAILED, "exl3_b200: reset failed");
   }
   return kOk;
