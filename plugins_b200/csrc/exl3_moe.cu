@@ -107,11 +107,13 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(MoeParams p) {
     }
     s_off[E] = acc;
     *p.nchunks = nch;
-    // stable placement: slots in index order
+    // stable placement: slots in index order; the tail left by absent slots (expert outside the bank) is marked, so
+    // the combine's search over all S positions never meets an entry from an earlier call
     for (int s = 0; s < S; ++s) {
       const int e = slot_expert(p, s);
       if (e >= 0 && e < E) p.order[s_off[e]++] = s;
     }
+    for (int i = acc; i < S; ++i) p.order[i] = -1;
   }
 }
 

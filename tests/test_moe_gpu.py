@@ -76,3 +76,30 @@ def test_swiglu_is_deterministic_and_refuses_bad_shapes():
         Q.swiglu(wg, wu, wd, x, ind.view(2, 3, topk).cuda(), sc.view(2, 3, topk).cuda().half())
     with pytest.raises(Q.Exl3Error, match="swiglu"):
         Q.moe(wg, x)
+
+
+def test_absent_experts_contribute_nothing_after_a_full_call(oracle):
+    # slots whose expert is outside the bank (-1, E) are dropped; a previous call with every slot present leaves its
+    # sorted slot list in the workspace, which must not leak into this one
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    experts, hidden, inter, topk, rows, n = 8, 256, 256, 3, 7, 48
+    raw = [_bank(E, experts, i, o, n, s) for i, o, s in ((hidden, inter, 11), (hidden, inter, 12), (inter, hidden, 13))]
+    wg, wu, wd = (Q.weight_from_tensors(*b) for b in raw)
+    ind, sc = _route(rows, experts, topk, 8)
+    x = torch.randn((1, rows, hidden), device="cuda", dtype=torch.float16)
+    Q.swiglu(wg, wu, wd, x, ind.view(1, rows, topk).cuda(), sc.view(1, rows, topk).cuda())  # every slot present
+    ind2 = ind.clone()
+    ind2[0, 0], ind2[3, 2], ind2[6, 1] = -1, experts, -1
+    y = Q.swiglu(wg, wu, wd, x, ind2.view(1, rows, topk).cuda(), sc.view(1, rows, topk).cuda(), out=torch.empty(
+        (1, rows, hidden), device="cuda", dtype=torch.float32))
+    keep_i, keep_s = ind2.clone(), sc.clone()
+    absent = (keep_i < 0) | (keep_i >= experts)
+    keep_s[absent], keep_i[absent] = 0.0, 0
+    bank = lambda b: (_np16(b[0]), _np16(b[1]), _np16(b[2]), n)
+    want = oracle.moe_truth(x.float().cpu().numpy(), keep_i.numpy(), keep_s.numpy(), *[bank(b) for b in raw],
+                            hidden, inter, 0.0, threads=8)
+    got = y.view(rows, hidden).cpu().numpy()
+    for r in range(rows):  # row by row: a leaked slot shows in its own row
+        rel = np.linalg.norm(got[r] - want[r]) / np.linalg.norm(want[r])
+        assert rel < REL_L2_BAR, (r, rel)
