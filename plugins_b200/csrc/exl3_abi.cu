@@ -504,6 +504,11 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
                               ((flags & EXL3_MATMUL_GEMV) == 0 && rows >= d->gemm_min_rows));
   if (gemm) return run_gemm(d, w, x, x_dtype, rows, y, y_dtype, flags, st, ev);
   if (ev && ev[0]) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
+  // measurement overrides: EXL3_GEMV=4 takes the grid-stride GEMV, EXL3_GEMV_SPLIT the cluster size
+  const char* gv = getenv("EXL3_GEMV");
+  const bool gemv_v5 = !(gv && atoi(gv) == 4);
+  const char* sp = getenv("EXL3_GEMV_SPLIT");
+  const int split = sp ? atoi(sp) : 0;
   const int in_f = w->in_features, out_f = w->out_features, groups = w->groups;
   const bool grouped = (w->flags & EXL3_WEIGHT_GROUPED) != 0;
   const int K = w->n / 16;
@@ -542,6 +547,12 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
       gp.prepared = (flags & EXL3_MATMUL_PREPARED) ? 1 : 0;
       gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
       const char* why = nullptr;
+      // the cluster-split GEMV where a split fits (every served width), else the grid-stride one with global partials
+      if (gemv_v5 && exl3::gemv5_geometry(gp, d->sms, rg, split, &why)) {
+        if (exl3::launch_gemv5(gp, K, rg, imma, st, true) != cudaSuccess)
+          return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
+        continue;
+      }
       if (!exl3::gemv_geometry(gp, d->sms, rg, d->partial_floats, &why)) return refuse(EXL3_TOO_LARGE, why);
       if (exl3::launch_gemv(gp, K, rg, imma, st, true) != cudaSuccess)
         return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");

@@ -40,6 +40,12 @@ struct GemvParams {
 bool gemv_geometry(GemvParams& p, int sms, int row_groups, size_t partial_capacity_floats, const char** why);
 cudaError_t launch_gemv(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl);
 
+// The cluster-split decode GEMV (exl3_gemv5.cu): one thread-block cluster per 128-column block, its CTAs splitting
+// the input (kc = CTAs per cluster, kr = slabs per CTA), partials summed over distributed shared memory.
+// split_override > 0 forces the CTAs per cluster (measurement); false when no split fits.
+bool gemv5_geometry(GemvParams& p, int sms, int row_groups, int split_override, const char** why);
+cudaError_t launch_gemv5(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl);
+
 // decode a whole trellis to W_hat (f16 bits, row-major [in][out]); one warp per tile
 cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
                                 int imma, cudaStream_t st);
