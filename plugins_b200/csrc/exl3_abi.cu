@@ -548,7 +548,7 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
       gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
       const char* why = nullptr;
       // the cluster-split GEMV where a split fits (every served width), else the grid-stride one with global partials
-      if (gemv_v5 && exl3::gemv5_geometry(gp, d->sms, rg, split, &why)) {
+      if (gemv_v5 && exl3::gemv5_geometry(gp, K, d->sms, rg, split, &why)) {
         if (exl3::launch_gemv5(gp, K, rg, imma, st, true) != cudaSuccess)
           return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
         continue;

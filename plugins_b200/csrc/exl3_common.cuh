@@ -177,8 +177,15 @@ __device__ __forceinline__ uint32_t mul1_pair_dp4a(uint32_t cw_a, uint32_t cw_b)
   return out;
 }
 
+// Two decoded byte sums (f16 bits of 1024 + bytesum in the low halves) -> f16x2 (lo, hi) through the mul1 affine.
+// Both halves are below 2^16, so the packing is exact either way: a byte permute (ALU pipe) or hi * 65536 + lo (an
+// integer multiply-add, FMA pipe).  Which is faster depends on which pipe the rest of the kernel loads: measured on
+// B200, the multiply-add for the deep-ring decode GEMV, the permute elsewhere.
+template <bool kPackFma = false>
 __device__ __forceinline__ uint32_t mul1_pack_affine(uint32_t h_lo16, uint32_t h_hi16) {
-  const uint32_t h = __byte_perm(h_lo16, h_hi16, 0x5410);
+  uint32_t h;
+  if constexpr (kPackFma) asm("mad.lo.u32 %0, %1, 65536, %2;" : "=r"(h) : "r"(h_hi16), "r"(h_lo16));
+  else h = __byte_perm(h_lo16, h_hi16, 0x5410);
   const uint32_t inv2 = kHalfInv | (kHalfInv << 16), bias2 = kHalfBias | (kHalfBias << 16);
   uint32_t out;
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(out) : "r"(h), "r"(inv2), "r"(bias2));
@@ -215,6 +222,7 @@ struct ImmaIndicator {
   }
 };
 
+template <bool kPackFma = false>
 __device__ __forceinline__ void decode_afrag_imma(const uint32_t (&w)[8], const ImmaIndicator& ind,
                                                   uint32_t (&a)[4]) {
   uint32_t x0[4], x1[4], d0[4], d1[4];
@@ -225,10 +233,10 @@ __device__ __forceinline__ void decode_afrag_imma(const uint32_t (&w)[8], const 
   }
   imma_bytesum(x0, ind.b0, ind.b1, d0);
   imma_bytesum(x1, ind.b0, ind.b1, d1);
-  a[0] = mul1_pack_affine(d0[0], d0[2]);  // col g,   k' 2q..2q+1   <- phys 4q, 4q+1
-  a[1] = mul1_pack_affine(d1[0], d1[2]);  // col g+8
-  a[2] = mul1_pack_affine(d0[1], d0[3]);  // col g,   k' 2q+8..     <- phys 4q+2, 4q+3
-  a[3] = mul1_pack_affine(d1[1], d1[3]);  // col g+8
+  a[0] = mul1_pack_affine<kPackFma>(d0[0], d0[2]);  // col g,   k' 2q..2q+1   <- phys 4q, 4q+1
+  a[1] = mul1_pack_affine<kPackFma>(d1[0], d1[2]);  // col g+8
+  a[2] = mul1_pack_affine<kPackFma>(d0[1], d0[3]);  // col g,   k' 2q+8..     <- phys 4q+2, 4q+3
+  a[3] = mul1_pack_affine<kPackFma>(d1[1], d1[3]);  // col g+8
 }
 
 // D[16 x 8] += A[16 x 16] (f16) * B[16 x 8] (f16), f32 accumulate.

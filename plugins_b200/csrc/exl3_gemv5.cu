@@ -9,7 +9,7 @@
 // Work split.  One thread-block cluster per 128-column block of the output (all segments of a stacked weight in
 // order); the cluster's S CTAs split the input: CTA rank r takes the 16-row slabs [r KT/S, (r+1) KT/S).  A CTA's
 // four warps take its slabs round-robin; a slab of one column block is one unit (8 tiles, contiguous in the pack
-// layout), prefetched with 16-byte cp.async into the warp's ring before griddepcontrol.wait, so the weight stream
+// layout), prefetched with 16-byte cp.async into the warp's deep ring (8-16 units) before griddepcontrol.wait, so the weight stream
 // overlaps the previous kernel.  After the input rotation of its k-range (shared memory, MMA B-fragment order) each
 // warp decodes its tiles in registers (lane t's windows ARE the A fragment of W^T) into mma.sync m16n8k16.
 // Reduction: the warps' partials are summed in warp order into the CTA's partial; then the cluster's rank 0 reads the
@@ -27,7 +27,12 @@ namespace {
 
 constexpr int kW5 = 4;              // warps per CTA
 constexpr int kT5 = kW5 * 32;
-constexpr int kStages5 = 8;         // units in flight per warp
+// Units in flight per warp: a deep ring (prefetch measured faster at every shape) or a shallow one, whichever is the
+// deepest that keeps three CTAs per SM beside the CTA's rotated input (a unit is 256 K bytes).
+template <int K>
+constexpr int deep_stages() { return K <= 2 ? 16 : (K <= 4 ? 12 : (K == 5 ? 10 : 8)); }
+template <int K>
+constexpr int shallow_stages() { return K <= 2 ? 8 : (K <= 4 ? 8 : 6); }
 constexpr int kRed5 = 132;          // row stride of the reduction buffer (floats)
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
@@ -56,11 +61,12 @@ __device__ __forceinline__ float ld_dsmem(const float* local, uint32_t rank) {
 
 }  // namespace
 
-template <int K, int RG, bool IMMA>
+template <int K, int RG, bool IMMA, int ST>
 __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   constexpr uint32_t kTileBytes = 32u * K;
   constexpr uint32_t kUnitBytes = 8u * kTileBytes;
   constexpr uint32_t kSlabX = RG * 256u;
+  constexpr int kStages5 = ST;
 
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
@@ -186,7 +192,7 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
     for (int t = 0; t < 8; ++t) {
       uint32_t w[8], a[4];
       lane_codewords<K>(tw + t * (kTileBytes / 4u), lwin, w);
-      if constexpr (IMMA) decode_afrag_imma(w, ind, a);
+      if constexpr (IMMA) decode_afrag_imma<ST == deep_stages<K>()>(w, ind, a);
       else decode_afrag_dp4a(w, a);
 #pragma unroll
       for (int r = 0; r < RG; ++r) mma_16816(acc[t][r], a, b0[r], b1[r]);
@@ -259,16 +265,11 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
 
 // ------------------------------------------------------------------ host
 
-template <int K, int RG, bool IMMA>
-static size_t gemv5_smem(const GemvParams& p) {
-  return static_cast<size_t>(p.xp_bytes) + static_cast<size_t>(kW5) * kStages5 * 8u * 32u * K +
-         static_cast<size_t>(kW5) * p.rows * kRed5 * 4;
-}
-
-template <int K, int RG, bool IMMA>
+template <int K, int RG, bool IMMA, int ST>
 static cudaError_t launch5_t(const GemvParams& p, cudaStream_t st, bool pdl) {
-  auto kern = gemv5_kernel<K, RG, IMMA>;
-  const size_t smem = gemv5_smem<K, RG, IMMA>(p);
+  auto kern = gemv5_kernel<K, RG, IMMA, ST>;
+  const size_t smem = static_cast<size_t>(p.xp_bytes) + static_cast<size_t>(kW5) * ST * 8u * 32u * K +
+                      static_cast<size_t>(kW5) * p.rows * kRed5 * 4;
   static size_t configured = 0;
   if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -294,34 +295,55 @@ static cudaError_t launch5_t(const GemvParams& p, cudaStream_t st, bool pdl) {
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
+template <int K, int RG, bool IMMA>
+static cudaError_t launch5_s(const GemvParams& p, cudaStream_t st, bool pdl) {
+  return p.stages == deep_stages<K>() ? launch5_t<K, RG, IMMA, deep_stages<K>()>(p, st, pdl)
+                                      : launch5_t<K, RG, IMMA, shallow_stages<K>()>(p, st, pdl);
+}
+
 template <int RG, bool IMMA>
 static cudaError_t launch5_k(const GemvParams& p, int K, cudaStream_t st, bool pdl) {
   switch (K) {
-    case 1: return launch5_t<1, RG, IMMA>(p, st, pdl);
-    case 2: return launch5_t<2, RG, IMMA>(p, st, pdl);
-    case 3: return launch5_t<3, RG, IMMA>(p, st, pdl);
-    case 4: return launch5_t<4, RG, IMMA>(p, st, pdl);
-    case 5: return launch5_t<5, RG, IMMA>(p, st, pdl);
-    case 6: return launch5_t<6, RG, IMMA>(p, st, pdl);
+    case 1: return launch5_s<1, RG, IMMA>(p, st, pdl);
+    case 2: return launch5_s<2, RG, IMMA>(p, st, pdl);
+    case 3: return launch5_s<3, RG, IMMA>(p, st, pdl);
+    case 4: return launch5_s<4, RG, IMMA>(p, st, pdl);
+    case 5: return launch5_s<5, RG, IMMA>(p, st, pdl);
+    case 6: return launch5_s<6, RG, IMMA>(p, st, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
-bool gemv5_geometry(GemvParams& p, int sms, int row_groups, int split_override, const char** why) {
+static size_t gemv5_smem_for(int K, int stages, int KR, int row_groups, int rows) {
+  return static_cast<size_t>(KR) * row_groups * 256 + static_cast<size_t>(kW5) * stages * 8u * 32u * K +
+         static_cast<size_t>(kW5) * rows * kRed5 * 4;
+}
+
+bool gemv5_geometry(GemvParams& p, int K, int sms, int row_groups, int split_override, const char** why) {
   const int KT = p.in_features / 16;
   const int CB = p.out_features / 128;
+  constexpr size_t kThreePerSm = 74 * 1024;  // shared memory that still fits three CTAs on an SM
+  const int deep = K <= 2 ? 16 : (K <= 4 ? 12 : (K == 5 ? 10 : 8));  // deep_stages<K>()
+  const int shallow = K <= 4 ? 8 : 6;                                 // shallow_stages<K>()
   // CTAs per column block: a divisor of KT leaving whole 128-input blocks (8 slabs) per CTA, at most 16 (the
-  // cluster limit), at most 128 slabs per CTA (the rotated input fits shared memory); the largest whose grid still
-  // fits one wave of 3 CTAs per SM, else the smallest allowed.
-  int best = 0;
-  for (int d = 1; d <= 16; ++d) {
-    if (KT % d != 0 || (KT / d) % 8 != 0 || KT / d > 128) continue;
-    if (split_override > 0) {
-      if (d == split_override) best = d;
-      continue;
+  // cluster limit) and at most 128 slabs per CTA.  Preferred: splits whose shared memory (with the shallow ring)
+  // keeps three CTAs per SM; among those the largest whose grid still fits one wave of three CTAs per SM, else the
+  // smallest.  Then the deep ring if it still keeps three CTAs per SM.
+  int best = 0, fallback = 0;
+  for (int pass = 0; pass < 2 && best == 0; ++pass) {
+    for (int d = 1; d <= 16; ++d) {
+      if (KT % d != 0 || (KT / d) % 8 != 0 || KT / d > 128) continue;
+      const size_t smem = gemv5_smem_for(K, shallow, KT / d, row_groups, p.rows);
+      if (smem > 227 * 1024) continue;
+      if (split_override > 0) {
+        if (d == split_override) best = d;
+        continue;
+      }
+      if (pass == 0 && smem > kThreePerSm) continue;
+      if (fallback == 0) fallback = d;  // the smallest allowed in this pass
+      if (static_cast<int64_t>(CB) * d <= static_cast<int64_t>(sms) * 3) best = d;
     }
-    if (best == 0) best = d;  // smallest allowed
-    if (static_cast<int64_t>(CB) * d <= static_cast<int64_t>(sms) * 3) best = d;
+    if (best == 0) best = fallback;
   }
   if (best == 0) {
     *why = "exl3_b200: no cluster split of this input width";
@@ -330,6 +352,7 @@ bool gemv5_geometry(GemvParams& p, int sms, int row_groups, int split_override, 
   p.kt = KT;
   p.kc = best;
   p.kr = KT / best;
+  p.stages = gemv5_smem_for(K, deep, p.kr, row_groups, p.rows) <= kThreePerSm ? deep : shallow;
   p.xp_bytes = static_cast<int64_t>(p.kr) * row_groups * 256;
   p.grid = CB * best;
   p.contrib_max = 1;

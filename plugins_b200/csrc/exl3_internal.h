@@ -34,6 +34,7 @@ struct GemvParams {
   int32_t contrib_max;      // most CTAs contributing to one (segment, chunk, column block)
   int64_t xp_bytes;         // shared memory for the rotated activations a share touches
   int32_t grid;
+  int32_t stages;           // cluster-split GEMV: units in flight per warp
 };
 
 // Fills the geometry fields of `p` for `sms` SMs; false (with a reason) when the shape does not fit one launch.
@@ -43,7 +44,7 @@ cudaError_t launch_gemv(const GemvParams& p, int K, int row_groups, bool imma, c
 // The cluster-split decode GEMV (exl3_gemv5.cu): one thread-block cluster per 128-column block, its CTAs splitting
 // the input (kc = CTAs per cluster, kr = slabs per CTA), partials summed over distributed shared memory.
 // split_override > 0 forces the CTAs per cluster (measurement); false when no split fits.
-bool gemv5_geometry(GemvParams& p, int sms, int row_groups, int split_override, const char** why);
+bool gemv5_geometry(GemvParams& p, int K, int sms, int row_groups, int split_override, const char** why);
 cudaError_t launch_gemv5(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl);
 
 // decode a whole trellis to W_hat (f16 bits, row-major [in][out]); one warp per tile

@@ -40,6 +40,7 @@ def test_dispatch_unpack_combine_match_the_host_restatement(Q, dtype):
     import sharding_cpu_ops as C
     from plugins_b200 import _lib as L
     from plugins_b200 import sharding as S
+    torch.manual_seed(0)
     tokens, topk, experts, world, hidden = 5, 3, 6, 3, 256
     inds, scores = _routing(tokens, topk, experts, 1)
     inds[1, 2] = -1
@@ -75,7 +76,9 @@ def test_dispatch_unpack_combine_match_the_host_restatement(Q, dtype):
     Q.ep_combine(rows_back.cuda(), back, scores.cuda(), shared.cuda(), out)
     out_ref = torch.empty((tokens, hidden), dtype=dtype)
     C.ep_combine_ref(rows_back, back_ref, scores, shared, out_ref)
-    assert _rel(out.float().cpu(), out_ref.float()) < 1e-6
+    # same sums in the same order; the kernel fuses score * row + acc, the restatement rounds the product first, so
+    # an f16 output can differ by one unit in the last place
+    assert _rel(out.float().cpu(), out_ref.float()) < (1e-6 if dtype == torch.float32 else 2e-4)
     assert Q.device_error(0) & L.ERR_EP_OVERFLOW == 0
 
 
