@@ -400,6 +400,8 @@ def main() -> None:
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline sampling (rank 0, N=1)")
     ap.add_argument("--no-batch8", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip configs 3-5 (prefill, MoE, large layer)")
+    ap.add_argument("--tp-nccl", action="store_true",
+                    help="N > 1: gather the column shards with NCCL all-gathers instead of inside the GEMV")
     args = ap.parse_args()
     if args.impl == "reference":
         if args.steps > 20:
@@ -446,8 +448,21 @@ def main() -> None:
             off += t.numel()
         return buf, views
 
+    fused = world > 1 and not args.tp_nccl
+    seg = {"qkv": ([rank * HEADS_Q // world, rank * KV // world, rank * KV // world], [HEADS_Q, KV, KV]),
+           "o": ([rank * HIDDEN // world], [HIDDEN]),
+           "gate_up": ([rank * INTER // world] * 2, [INTER, INTER]),
+           "down": ([rank * HIDDEN // world], [HIDDEN])}
+
     def run_config(rows: int, steps: int, warmup: int):
         ins, outs = make_io(rows)
+        ex = None
+        if fused:
+            # every launch writes its columns into a slot of every rank's exchange; one gather per step
+            from plugins_b200 import sharding as S
+            ex = S.TpExchange(rank, world, slots=LAYERS * len(GROUPS), slot_bytes=rows * 2 * INTER * 2,
+                              max_cb=2 * INTER // 128)
+            tp_out = torch.empty(LAYERS * len(GROUPS) * ex.slot_bytes, dtype=torch.uint8, device=device)
         # inputs live in one contiguous device buffer (one H2D per step); outputs likewise (one D2H)
         uniq_in = []
         for l in range(LAYERS):
@@ -457,23 +472,33 @@ def main() -> None:
             x, a, m = in_views[3 * l: 3 * l + 3]
             ins[l] = {"qkv": x, "o": a, "gate_up": x, "down": m}
         gathered = []
-        if world > 1:
+        if world > 1 and not fused:
             for l in range(LAYERS):
                 gathered.append({k: torch.empty((world,) + tuple(outs[l][k].shape), dtype=torch.float16,
                                                 device=device) for k, _ in GROUPS})
-        out_list = [outs[l][k] for l in range(LAYERS) for k, _ in GROUPS] if world == 1 else \
-            [gathered[l][k] for l in range(LAYERS) for k, _ in GROUPS]
-        out_buf, out_views = flat_views(out_list)
-        j = 0
-        for l in range(LAYERS):
-            for k, _ in GROUPS:
-                if world == 1:
-                    outs[l][k] = out_views[j]
-                else:
-                    gathered[l][k] = out_views[j]
-                j += 1
+        if fused:
+            out_buf = tp_out
+        else:
+            out_list = [outs[l][k] for l in range(LAYERS) for k, _ in GROUPS] if world == 1 else \
+                [gathered[l][k] for l in range(LAYERS) for k, _ in GROUPS]
+            out_buf, out_views = flat_views(out_list)
+            j = 0
+            for l in range(LAYERS):
+                for k, _ in GROUPS:
+                    if world == 1:
+                        outs[l][k] = out_views[j]
+                    else:
+                        gathered[l][k] = out_views[j]
+                    j += 1
 
         def step():
+            if fused:
+                ex.begin()
+                for l in range(LAYERS):
+                    for j, (k, _) in enumerate(GROUPS):
+                        ex.matmul(layers[l][k], ins[l][k], l * len(GROUPS) + j, *seg[k])
+                ex.gather(0, LAYERS * len(GROUPS), tp_out)
+                return
             for l in range(LAYERS):
                 for k, _ in GROUPS:
                     Q.matmul(layers[l][k], ins[l][k], out=outs[l][k])
@@ -491,7 +516,8 @@ def main() -> None:
         with torch.cuda.graph(graph, stream=s):
             step()
         torch.cuda.synchronize()
-        launches_per_step = LAYERS * len(GROUPS)  # one decode-GEMV launch per launch group
+        # one decode-GEMV launch per launch group (+ the step begin and the gather when the exchange is fused)
+        launches_per_step = LAYERS * len(GROUPS) + (2 if fused else 0)
 
         for _ in range(warmup):
             graph.replay()
@@ -553,8 +579,14 @@ def main() -> None:
         dom_ms = time_group("gate_up")
         qkv_ms = time_group("qkv")
         graph.reset()
+        if ex is not None:
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()  # no rank unmaps its exchange while another still writes into it
+            ex.close()
         return {"ms": ms, "ms_e2e": ms_e2e, "clk": clk.summary(), "launches": launches_per_step * steps,
-                "h2d": in_buf.numel() * 2, "d2h": out_buf.numel() * 2, "dom_ms": dom_ms, "qkv_ms": qkv_ms}
+                "h2d": in_buf.numel() * in_buf.element_size(), "d2h": out_buf.numel() * out_buf.element_size(),
+                "dom_ms": dom_ms, "qkv_ms": qkv_ms}
 
     peaks = load_peaks()
     r1 = run_config(args.batch, args.steps, args.warmup)
@@ -590,7 +622,9 @@ def main() -> None:
             "data": "synthetic: random-init N(0,0.02) weights (seeded) encoded to EXL3 mul1 by the library; "
                     "N(0,1) f16 activations",
             "config": {"workload": WORKLOAD, "batch": args.batch, "layers": LAYERS,
-                       "parallelism": f"tp{world} column-parallel + NCCL all-gather" if world > 1 else "single GPU",
+                       "parallelism": ("single GPU" if world == 1 else
+                                       f"tp{world} column-parallel, NCCL all-gather per launch" if args.tp_nccl else
+                                       f"tp{world} column-parallel, all-gather inside the GEMV (NVLink peer stores)"),
                        "bytes_per_step": total,
                        "l2": "no flush: a step streams %.2f GB of distinct weights, >> 126 MB L2" % (total / 1e9)},
             "decode_tok_s": round(args.batch / (r1["ms"] * 1e-3), 2),

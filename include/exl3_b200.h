@@ -207,6 +207,36 @@ exl3_verdict exl3_ep_unpack(const exl3_tensor *recv, void *stream, exl3_tensor *
 exl3_verdict exl3_ep_combine(const exl3_tensor *back, const exl3_tensor *back_slot, const exl3_tensor *scores,
                              const exl3_tensor *shared, void *stream, exl3_tensor *out);
 
+/* ------------------------------------------------------------------ column parallelism with a fused all-gather
+ *
+ * Beside the seam (the reference is single-device): a linear split by output columns over `world` ranks (one process
+ * per GPU) whose decode GEMV writes its columns straight into every rank's exchange buffer over NVLink, so no
+ * separate all-gather runs.  Setup: exl3_tp_create on every rank (returns a 64-byte CUDA IPC handle), exchange the
+ * handles (e.g. torch.distributed), exl3_tp_connect with all of them in rank order.  A step: exl3_tp_begin, the
+ * column-parallel matmuls (exl3_matmul_tp, each into its own slot), exl3_tp_gather of the slots (waits for every
+ * rank's columns, then copies the gathered rows out).  All three are stream-ordered kernels with no host
+ * synchronisation, so a whole step can be captured in a CUDA graph.  Every rank must run the same steps. */
+typedef struct exl3_tp exl3_tp;
+
+/* An exchange of `slots` slots of slot_bytes (a multiple of 16) each, for gathered widths up to 128 * max_cb columns;
+ * ipc_handle receives 64 bytes to hand to the other ranks. */
+exl3_verdict exl3_tp_create(int32_t device, int32_t world, int32_t rank, int32_t slots, int64_t slot_bytes,
+                            int32_t max_cb, exl3_tp **out, uint8_t *ipc_handle);
+/* ipc_handles: world * 64 bytes, rank order (this rank's own entry is ignored). */
+exl3_verdict exl3_tp_connect(exl3_tp *tp, const uint8_t *ipc_handles);
+void exl3_tp_destroy(exl3_tp *tp);
+/* The next step (the slots' double buffers flip). */
+exl3_verdict exl3_tp_begin(exl3_tp *tp, void *stream);
+/* This rank's column shard of a (possibly stacked) linear: x [rows <= 16, in] -> its columns of y, written into slot
+ * `slot` of every rank.  seg_col0[s] / seg_total[s] (w->nseg entries, multiples of 128): segment s's first gathered
+ * column held by this rank, and the segment's gathered width.  The slot holds the segments back to back, each
+ * [rows][seg_total] in x's dtype. */
+exl3_verdict exl3_matmul_tp(const exl3_weight *w, const exl3_tensor *x, exl3_tp *tp, int32_t slot,
+                            const int64_t *seg_col0, const int64_t *seg_total, void *stream);
+/* Waits for every column of slots [slot0, slot0 + nslots) of this step, then copies them to out (device memory,
+ * 16-byte aligned): slot i at out + i * slot_bytes. */
+exl3_verdict exl3_tp_gather(exl3_tp *tp, int32_t slot0, int32_t nslots, void *stream, void *out);
+
 /* A borrowed view of device arrays already in the pack layout (the reference's shared handles, plugin.zig:213-218):
  * validates the shapes and creates the device workspace; exl3_release on a view frees nothing. */
 exl3_verdict exl3_weight_view(uint16_t *trellis, uint16_t *suh, uint16_t *svh, int32_t groups, int32_t in_features,
@@ -240,6 +270,7 @@ exl3_verdict exl3_matmul_noalloc(const exl3_weight *w, const exl3_tensor *x, voi
 #define EXL3_ERR_WAIT_TIMEOUT 1u  /* a bounded mbarrier wait gave up (the kernel left its loop and returned) */
 #define EXL3_ERR_BAD_SHAPE 2u     /* a launch saw a shape its host validation should have refused */
 #define EXL3_ERR_EP_OVERFLOW 4u   /* an expert-parallel dispatch had more rows for one peer than its capacity */
+#define EXL3_ERR_TP_TIMEOUT 8u    /* a column-parallel gather gave up waiting (one second) for a peer's columns */
 exl3_verdict exl3_device_error(int32_t device, uint32_t *bits, int32_t clear);
 
 /* The library's build string. */

@@ -720,6 +720,74 @@ exl3_verdict exl3_matmul_timed(const exl3_weight* w, const exl3_tensor* x, uint3
   return run_linear(w, x->data, x->dtype, rows, out->data, y_dtype, flags, static_cast<cudaStream_t>(stream), events);
 }
 
+exl3_verdict exl3_matmul_tp(const exl3_weight* w, const exl3_tensor* x, exl3_tp* tp, int32_t slot,
+                            const int64_t* seg_col0, const int64_t* seg_total, void* stream) {
+  exl3_verdict v = check_weight(w);
+  if (v.code != EXL3_OK) return v;
+  const exl3::TpDev* td = exl3::tp_device(tp);
+  if (!td) return refuse(EXL3_FAILED, "exl3_matmul_tp: not a connected exchange");
+  if (exl3::tp_device_index(tp) != w->device) return refuse(EXL3_UNSUPPORTED, "exl3_matmul_tp: weight and exchange on different devices");
+  if (slot < 0 || slot >= exl3::tp_slots(tp)) return refuse(EXL3_UNSUPPORTED, "exl3_matmul_tp: slot out of range");
+  if (w->groups != 1 || (w->flags & EXL3_WEIGHT_GROUPED)) return refuse(EXL3_UNSUPPORTED, "exl3_matmul_tp: one ungrouped weight");
+  if (!x || x->ndim < 1 || x->ndim > 4 || !act_dtype(x->dtype)) return refuse(EXL3_FAILED, "exl3_matmul_tp: bad x");
+  if (x->shape[x->ndim - 1] != w->in_features) return refuse(EXL3_UNSUPPORTED, "exl3_matmul_tp: x's last dim is not the input width");
+  const int64_t rows = numel(x) / w->in_features;
+  if (rows < 1 || rows > exl3::kMaxRows) return refuse(EXL3_UNSUPPORTED, "exl3_matmul_tp: 1..16 rows (one launch)");
+  if (!x->data || !seg_col0 || !seg_total) return refuse(EXL3_FAILED, "exl3_matmul_tp: bad arguments");
+  const size_t esize = x->dtype == EXL3_F32 ? 4 : 2;
+  int64_t total = 0;
+  for (int s = 0; s < w->nseg; ++s) {
+    const int64_t width = w->seg_cols[s + 1] - w->seg_cols[s];
+    if (seg_total[s] % 128 != 0 || seg_col0[s] % 128 != 0 || seg_col0[s] < 0 || seg_col0[s] + width > seg_total[s])
+      return refuse(EXL3_UNSUPPORTED, "exl3_matmul_tp: a segment's columns do not fit its gathered width");
+    total += seg_total[s];
+  }
+  if (total / 128 > exl3::tp_max_cb(tp)) return refuse(EXL3_TOO_LARGE, "exl3_matmul_tp: gathered width beyond the exchange's flags");
+  if (static_cast<int64_t>(rows * total * esize) > exl3::tp_slot_bytes(tp))
+    return refuse(EXL3_TOO_LARGE, "exl3_matmul_tp: gathered rows beyond the exchange's slot");
+  DeviceState* d = device_state(w->device);
+  if (!d) return refuse(EXL3_FAILED, "exl3_b200: no workspace on this device (exl3_open or a weight load creates it)");
+  DeviceGuard guard(w->device);
+  exl3::GemvParams gp{};
+  gp.trellis = w->trellis;
+  gp.suh = w->suh;
+  gp.svh = w->svh;
+  gp.x = x->data;
+  gp.x_dtype = x->dtype;
+  gp.x_row_stride = w->in_features;
+  gp.y = nullptr;
+  gp.y_dtype = x->dtype;
+  gp.row0 = 0;
+  gp.rows_total = static_cast<int32_t>(rows);
+  gp.err = d->err;
+  gp.in_features = w->in_features;
+  gp.out_features = w->out_features;
+  gp.rows = static_cast<int32_t>(rows);
+  gp.nseg = w->nseg;
+  for (int s = 0; s <= w->nseg; ++s) gp.seg_cb[s] = w->seg_cols[s] / 128;
+  for (int s = w->nseg + 1; s <= exl3::kMaxSegments; ++s) gp.seg_cb[s] = gp.seg_cb[w->nseg];
+  int64_t base = 0;
+  int32_t cbb = 0;
+  for (int s = 0; s < w->nseg; ++s) {
+    gp.tp_total[s] = seg_total[s];
+    gp.tp_col0[s] = seg_col0[s];
+    gp.tp_seg_base[s] = base;
+    gp.tp_cb_base[s] = cbb;
+    base += rows * seg_total[s];
+    cbb += static_cast<int32_t>(seg_total[s] / 128);
+  }
+  gp.tp = td;
+  gp.tp_slot = slot;
+  gp.tp_meta_cb = static_cast<uint32_t>(cbb);
+  gp.tp_meta_bytes = static_cast<uint32_t>(rows * total * esize);
+  const int rg = rows <= 8 ? 1 : 2;
+  const char* why = nullptr;
+  if (!exl3::gemv5_geometry(gp, w->n / 16, d->sms, rg, 0, &why)) return refuse(EXL3_UNSUPPORTED, why);
+  if (exl3::launch_gemv5(gp, w->n / 16, rg, true, static_cast<cudaStream_t>(stream), true) != cudaSuccess)
+    return refuse(EXL3_FAILED, "exl3_matmul_tp: GEMV launch failed");
+  return kOk;
+}
+
 exl3_verdict exl3_matmul(const exl3_weight* w, const exl3_tensor* x, void* stream, exl3_tensor* out) {
   return exl3_matmul_ex(w, x, 0, stream, out);
 }

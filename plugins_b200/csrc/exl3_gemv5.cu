@@ -246,6 +246,52 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   }
   __syncthreads();
   const int seg_c0 = seg_lo * 128, seg_w = (seg_hi - seg_lo) * 128;
+  if (p.tp) {
+    // column-parallel exchange: this block's columns into every rank's slot, then its flag (step) on every rank
+    const TpDev& tp = *p.tp;
+    const uint32_t step = *reinterpret_cast<volatile uint32_t*>(tp.step);
+    const size_t esize = p.y_dtype == kF32 ? 4 : 2;
+    const size_t slot_off = (static_cast<size_t>(step & 1u) * tp.slots + p.tp_slot) * tp.slot_bytes;
+    int64_t tot = p.tp_total[0], c0 = p.tp_col0[0], sb = p.tp_seg_base[0];
+    int cbb = p.tp_cb_base[0];
+#pragma unroll
+    for (int i = 1; i < kMaxSegments; ++i)
+      if (i == s) {
+        tot = p.tp_total[i];
+        c0 = p.tp_col0[i];
+        sb = p.tp_seg_base[i];
+        cbb = p.tp_cb_base[i];
+      }
+    const int64_t col = c0 + (cbg * 128 - seg_c0);  // first gathered column of this block
+    for (int row = static_cast<int>(warp); row < rows; row += kW5) {
+      float v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[k] = red[row * kRed5 + lane + 32 * k];
+      if (!p.inner_only) {
+        fwht128_warp(v, lane);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = v[k] * kHadScale * f16_bits_to_float(p.svh[cbg * 128 + lane + 32 * k]);
+      }
+      const size_t at = static_cast<size_t>(sb + static_cast<int64_t>(p.row0 + row) * tot + col);
+      for (int q = 0; q < tp.world; ++q) {
+        void* yq = tp.y[q] + slot_off;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) store_act(yq, at + lane + 32 * k, v[k], p.y_dtype);
+      }
+    }
+    (void)esize;
+    if (blockIdx.x == 0 && tid == 0) {  // the slot's size, for this rank's gather (same on every rank)
+      tp.meta[p.tp_slot * 4 + 0] = p.tp_meta_cb;
+      tp.meta[p.tp_slot * 4 + 1] = p.tp_meta_bytes;
+    }
+    __threadfence_system();  // this thread's stores, before the flag
+    __syncthreads();
+    if (tid < static_cast<uint32_t>(tp.world)) {
+      uint32_t* f = tp.flag[tid] + static_cast<size_t>(p.tp_slot) * tp.max_cb + cbb + static_cast<int>(col / 128);
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(step) : "memory");
+    }
+    return;
+  }
   for (int row = static_cast<int>(warp); row < rows; row += kW5) {
     const size_t grow = static_cast<size_t>(p.row0 + row);
     const size_t ybase = p.nseg == 1 ? grow * p.y_row_stride

@@ -11,6 +11,17 @@ constexpr int kMaxRows = 16;     // decode-GEMV rows per launch (two m16n8k16 ro
 constexpr int kGemvCtasPerSm = 3;  // the decode GEMV's persistent grid: CTAs per SM (fixed: rows and byte-sum path
                                    // do not change a row's sum order)
 
+// Column-parallel exchange (exl3_tp.cu): this rank's view of every rank's exchange buffer.
+constexpr int kMaxTpRanks = 8;
+struct TpDev {
+  uint8_t* y[kMaxTpRanks];      // rank q's gathered outputs: [2 parities][slots][slot_bytes]
+  uint32_t* flag[kMaxTpRanks];  // rank q's flags: [slots][max_cb], the step whose data a column block holds
+  uint32_t* step;               // this rank's step counter
+  uint32_t* meta;               // this rank's slot metadata: [slots][4] (gathered column blocks, bytes)
+  int32_t world, rank, slots, max_cb;
+  int64_t slot_bytes;
+};
+
 struct GemvParams {
   const uint16_t* trellis;  // [in/16][out/16][n]
   const uint16_t* suh;      // [nseg][in] f16 bits (unused when prepared)
@@ -35,7 +46,25 @@ struct GemvParams {
   int64_t xp_bytes;         // shared memory for the rotated activations a share touches
   int32_t grid;
   int32_t stages;           // cluster-split GEMV: units in flight per warp
+  // column-parallel exchange (cluster-split GEMV only): y goes to every rank's slot instead of p.y
+  const TpDev* tp;          // device pointer, null without exchange
+  int32_t tp_slot;
+  int64_t tp_total[kMaxSegments];    // per segment: the gathered width
+  int64_t tp_col0[kMaxSegments];     // per segment: this rank's first column in it
+  int64_t tp_seg_base[kMaxSegments]; // per segment: first element of its [rows][width] block in the slot
+  int32_t tp_cb_base[kMaxSegments];  // per segment: first gathered column block (flag index)
+  uint32_t tp_meta_cb, tp_meta_bytes; // the slot's gathered column blocks and bytes (for the gather)
 };
+
+// The exchange handle's fields the launch needs (exl3_tp.cu).
+}  // namespace exl3
+struct exl3_tp;
+namespace exl3 {
+const TpDev* tp_device(const exl3_tp* tp);
+int tp_device_index(const exl3_tp* tp);
+int tp_max_cb(const exl3_tp* tp);
+int tp_slots(const exl3_tp* tp);
+int64_t tp_slot_bytes(const exl3_tp* tp);
 
 // Fills the geometry fields of `p` for `sms` SMs; false (with a reason) when the shape does not fit one launch.
 bool gemv_geometry(GemvParams& p, int sms, int row_groups, size_t partial_capacity_floats, const char** why);

@@ -92,6 +92,67 @@ class ColumnParallelLinear:
         return torch.cat([gathered[r, :, :b - a] for r, (a, b) in enumerate(self.ranges)], dim=1)
 
 
+class TpExchange:
+    """Column-parallel outputs gathered inside the decode GEMV (exl3_tp_*): every rank's GEMV writes its columns
+    straight into every rank's exchange buffer over NVLink, and a gather kernel waits for all of them.
+
+    One per process (one GPU per rank).  A step is ``begin()``, ``matmul(w, x, slot, ...)`` per column-parallel
+    linear (each into its own slot), then ``gather(slot0, n, out)``; no host synchronisation, so whole steps can be
+    captured in a CUDA graph.  Every rank must run the same steps.
+    """
+
+    def __init__(self, rank: int, world: int, slots: int, slot_bytes: int, max_cb: int, device=None, group=None):
+        import ctypes
+        from . import _lib as L
+        self._L, self._ct = L, ctypes
+        self.rank, self.world, self.slots = rank, world, slots
+        self.slot_bytes = (int(slot_bytes) + 15) // 16 * 16
+        dev = torch.cuda.current_device() if device is None else torch.device(device).index
+        handle = (ctypes.c_uint8 * 64)()
+        ptr = ctypes.c_void_p()
+        L.check(L.lib().exl3_tp_create(dev, world, rank, slots, self.slot_bytes, max_cb, ctypes.byref(ptr), handle))
+        self._ptr = ptr
+        mine = bytes(handle)
+        if world > 1:
+            every = [None] * world
+            dist.all_gather_object(every, mine, group=group)
+        else:
+            every = [mine]
+        buf = (ctypes.c_uint8 * (64 * world)).from_buffer_copy(b"".join(every))
+        L.check(L.lib().exl3_tp_connect(self._ptr, buf))
+
+    def begin(self, stream=None):
+        self._L.check(self._L.lib().exl3_tp_begin(self._ptr, Q._stream(stream)))
+
+    def matmul(self, w, x: torch.Tensor, slot: int, seg_col0, seg_total, stream=None):
+        """This rank's shard of a (stacked) linear into slot `slot` of every rank: segment s covers gathered
+        columns [seg_col0[s], seg_col0[s] + its width) of a segment seg_total[s] wide."""
+        ct = self._ct
+        c0 = (ct.c_int64 * len(seg_col0))(*[int(v) for v in seg_col0])
+        tot = (ct.c_int64 * len(seg_total))(*[int(v) for v in seg_total])
+        self._L.check(self._L.lib().exl3_matmul_tp(ct.byref(w.raw), ct.byref(Q._tensor(x)), self._ptr, int(slot), c0,
+                                                   tot, Q._stream(stream)))
+
+    def gather(self, slot0: int, nslots: int, out: torch.Tensor, stream=None):
+        """Waits for every rank's columns of slots [slot0, slot0 + nslots) and copies them into out (a device buffer
+        of nslots * slot_bytes bytes; slot i starts at byte i * slot_bytes)."""
+        if out.numel() * out.element_size() < nslots * self.slot_bytes or not out.is_cuda:
+            raise ValueError("out holds nslots * slot_bytes bytes on the GPU")
+        self._L.check(self._L.lib().exl3_tp_gather(self._ptr, int(slot0), int(nslots), Q._stream(stream),
+                                                   out.data_ptr()))
+
+    def close(self):
+        if self._ptr:
+            self._L.lib().exl3_tp_destroy(self._ptr)
+            self._ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 # ------------------------------------------------------------------ expert parallelism
 
 def expert_range(experts: int, rank: int, world: int) -> tuple[int, int]:

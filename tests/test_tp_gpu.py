@@ -1,0 +1,161 @@
+"""Column-parallel linears with the all-gather fused into the decode GEMV (exl3_tp_*, plugins_b200/sharding.py
+TpExchange): the gathered rows against the single-GPU matmul of the whole layer and the f32 truth, stacked shards,
+graph replay across the double-buffered steps, the bounded wait's timeout status -- and, when the box has two GPUs,
+two ranks over NVLink.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+REL_L2_BAR = 2e-3
+
+
+def _rel(a, b):
+    a, b = a.double(), b.double()
+    return float(((a - b).norm() / b.norm().clamp_min(1e-30)).item())
+
+
+def _shard(tr, suh, svh, c0, c1):
+    return tr[:, c0 // 16:c1 // 16].contiguous(), suh, svh[c0:c1].contiguous()
+
+
+def test_one_rank_exchange_matches_matmul_and_replays():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    from plugins_b200 import sharding as S
+    in_f, widths, n = 512, (640, 256, 384), 48
+    raws = [E.random_linear(in_f, o, n, seed=300 + i) for i, o in enumerate(widths)]
+    stacked = Q.stack([Q.weight_from_tensors(*r) for r in raws])
+    plain = Q.weight_from_tensors(*E.random_linear(in_f, 1024, 64, seed=310))
+    ex = S.TpExchange(0, 1, slots=2, slot_bytes=16 * 1280 * 4, max_cb=16)
+    for rows, dt in ((1, torch.float16), (5, torch.bfloat16), (16, torch.float32)):
+        x = torch.randn((rows, in_f), device="cuda").to(dt)
+        out = torch.empty(2 * ex.slot_bytes, dtype=torch.uint8, device="cuda")
+        for _ in range(3):  # parities flip every step
+            ex.begin()
+            ex.matmul(stacked, x, 0, [0, 0, 0], list(widths))
+            ex.matmul(plain, x, 1, [0], [1024])
+            ex.gather(0, 2, out)
+            torch.cuda.synchronize()
+            esize = torch.finfo(dt).bits // 8
+            got0 = out[:rows * sum(widths) * esize].view(dt)
+            want0 = Q.segment_outputs(stacked, Q.matmul(stacked, x), rows)
+            off = 0
+            for wd, wo in zip(widths, want0):
+                assert _rel(got0[off:off + rows * wd].view(rows, wd).float(), wo.float()) < 1e-6
+                off += rows * wd
+            got1 = out[ex.slot_bytes:ex.slot_bytes + rows * 1024 * esize].view(dt).view(rows, 1024)
+            assert _rel(got1.float(), Q.matmul(plain, x).float()) < 1e-6
+    # a captured step replays (the step counter and parity advance on the device)
+    x = torch.randn((2, in_f), device="cuda", dtype=torch.float16)
+    out = torch.zeros(2 * ex.slot_bytes, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        ex.begin(stream=s)
+        ex.matmul(plain, x, 1, [0], [1024], stream=s)
+        ex.gather(1, 1, out, stream=s)
+    want = Q.matmul(plain, x)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out[:2 * 1024 * 2].view(torch.float16).view(2, 1024), want)
+    g.reset()
+    assert Q.device_error(0) == 0
+    ex.close()
+
+
+def test_gather_of_an_unwritten_slot_times_out_with_a_status():
+    # the wait is bounded: nothing writes slot 1 in this step, so the gather gives up after about a second, records
+    # EXL3_ERR_TP_TIMEOUT and returns -- the context stays usable
+    from plugins_b200 import _lib as L
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    from plugins_b200 import sharding as S
+    plain = Q.weight_from_tensors(*E.random_linear(256, 256, 64, seed=320))
+    ex = S.TpExchange(0, 1, slots=2, slot_bytes=4096, max_cb=4)
+    x = torch.randn((1, 256), device="cuda", dtype=torch.float16)
+    out = torch.empty(2 * 4096, dtype=torch.uint8, device="cuda")
+    Q.device_error(0, clear=True)
+    ex.begin()
+    ex.matmul(plain, x, 0, [0], [256])
+    ex.gather(0, 1, out)
+    torch.cuda.synchronize()
+    assert Q.device_error(0) == 0
+    # slot 1's metadata came from no GEMV: give it one (same step) by writing slot 1 once, then advance the step
+    ex.matmul(plain, x, 1, [0], [256])
+    ex.gather(1, 1, out)
+    torch.cuda.synchronize()
+    ex.begin()  # a new step: slot 1 has no writer now
+    ex.gather(1, 1, out)
+    torch.cuda.synchronize()
+    assert Q.device_error(0, clear=True) & L.ERR_TP_TIMEOUT
+    assert torch.equal(Q.matmul(plain, x), Q.matmul(plain, x))  # the context still runs kernels
+    ex.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tp_rank(rank, world, port):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=datetime.timedelta(seconds=60))
+    try:
+        from plugins_b200 import encoder as E
+        from plugins_b200 import quant as Q
+        from plugins_b200 import sharding as S
+        in_f, n = 1024, 64
+        widths = (1280, 512, 512)  # q|k|v-like: the 1280 = 10 blocks split 5 / 5, 512 = 4 blocks split 2 / 2
+        raws = [E.random_linear(in_f, o, n, seed=400 + i, device=dev) for i, o in enumerate(widths)]
+        shards, col0 = [], []
+        for (tr, suh, svh), wd in zip(raws, widths):
+            c0, c1 = S.column_range(wd, rank, world)
+            shards.append(Q.weight_from_tensors(*_shard(tr, suh, svh, c0, c1)))
+            col0.append(c0)
+        stacked = Q.stack(shards)
+        full = [Q.weight_from_tensors(*r) for r in raws]
+        ex = S.TpExchange(rank, world, slots=1, slot_bytes=16 * sum(widths) * 2, max_cb=64)
+        g = torch.Generator(device=dev).manual_seed(7)
+        out = torch.empty(ex.slot_bytes, dtype=torch.uint8, device=dev)
+        for rows in (1, 8, 16):
+            x = torch.randn((rows, in_f), device=dev, generator=g).half()  # the same x on both ranks
+            for _ in range(3):
+                ex.begin()
+                ex.matmul(stacked, x, 0, col0, list(widths))
+                ex.gather(0, 1, out)
+                torch.cuda.synchronize()
+                got = out[:rows * sum(widths) * 2].view(torch.float16)
+                off = 0
+                for w, wd in zip(full, widths):
+                    want = Q.matmul(w, x)
+                    rel = _rel(got[off:off + rows * wd].view(rows, wd).float(), want.float())
+                    assert rel < 1e-3, (rank, rows, wd, rel)
+                    off += rows * wd
+        assert Q.device_error(rank) == 0
+        dist.barrier()
+        ex.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_gather_inside_the_gemv():
+    import torch.multiprocessing as mp
+    mp.spawn(_tp_rank, args=(2, _free_port()), nprocs=2)
