@@ -213,8 +213,8 @@ exl3_verdict exl3_ep_combine(const exl3_tensor *back, const exl3_tensor *back_sl
  * per GPU) whose decode GEMV writes its columns straight into every rank's exchange buffer over NVLink, so no
  * separate all-gather runs.  Setup: exl3_tp_create on every rank (returns a 64-byte CUDA IPC handle), exchange the
  * handles (e.g. torch.distributed), exl3_tp_connect with all of them in rank order.  A step: exl3_tp_begin, the
- * column-parallel matmuls (exl3_matmul_tp, each into its own slot), exl3_tp_gather of the slots (waits for every
- * rank's columns, then copies the gathered rows out).  All three are stream-ordered kernels with no host
+ * column-parallel matmuls (exl3_matmul_tp, each into its own slot), exl3_tp_gather (publishes this rank's columns,
+ * waits for every rank's, then copies the gathered rows out).  All three are stream-ordered kernels with no host
  * synchronisation, so a whole step can be captured in a CUDA graph.  Every rank must run the same steps. */
 typedef struct exl3_tp exl3_tp;
 
@@ -233,8 +233,9 @@ exl3_verdict exl3_tp_begin(exl3_tp *tp, void *stream);
  * [rows][seg_total] in x's dtype. */
 exl3_verdict exl3_matmul_tp(const exl3_weight *w, const exl3_tensor *x, exl3_tp *tp, int32_t slot,
                             const int64_t *seg_col0, const int64_t *seg_total, void *stream);
-/* Waits for every column of slots [slot0, slot0 + nslots) of this step, then copies them to out (device memory,
- * 16-byte aligned): slot i at out + i * slot_bytes. */
+/* Ends this rank's step: publishes its columns of every slot of the step to every rank (one system-scope release),
+ * waits for every rank's, then copies slots [slot0, slot0 + nslots) to out (device memory, 16-byte aligned): slot i
+ * at out + i * slot_bytes.  A step's gathered outputs are readable from its gather on. */
 exl3_verdict exl3_tp_gather(exl3_tp *tp, int32_t slot0, int32_t nslots, void *stream, void *out);
 
 /* A borrowed view of device arrays already in the pack layout (the reference's shared handles, plugin.zig:213-218):

@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   __syncthreads();
   const int seg_c0 = seg_lo * 128, seg_w = (seg_hi - seg_lo) * 128;
   if (p.tp) {
-    // column-parallel exchange: this block's columns into every rank's slot, then its flag (step) on every rank
+    // column-parallel exchange: this block's columns into every rank's slot (published by the step's gather)
     const TpDev& tp = *p.tp;
     const uint32_t step = *reinterpret_cast<volatile uint32_t*>(tp.step);
     const size_t esize = p.y_dtype == kF32 ? 4 : 2;
@@ -263,6 +263,9 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
         cbb = p.tp_cb_base[i];
       }
     const int64_t col = c0 + (cbg * 128 - seg_c0);  // first gathered column of this block
+    // each warp: its row's 128 outputs through a shared-memory staging row, then 16-byte stores into every rank
+    uint8_t* stage = ring;  // this warp's weight ring: drained (cp.async waited above), at least 2 KiB
+    const uint32_t row_bytes = 128u * static_cast<uint32_t>(esize);
     for (int row = static_cast<int>(warp); row < rows; row += kW5) {
       float v[4];
 #pragma unroll
@@ -272,24 +275,22 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) v[k] = v[k] * kHadScale * f16_bits_to_float(p.svh[cbg * 128 + lane + 32 * k]);
       }
-      const size_t at = static_cast<size_t>(sb + static_cast<int64_t>(p.row0 + row) * tot + col);
-      for (int q = 0; q < tp.world; ++q) {
-        void* yq = tp.y[q] + slot_off;
+      __syncwarp();
 #pragma unroll
-        for (int k = 0; k < 4; ++k) store_act(yq, at + lane + 32 * k, v[k], p.y_dtype);
+      for (int k = 0; k < 4; ++k) store_act(stage, lane + 32 * k, v[k], p.y_dtype);
+      __syncwarp();
+      const size_t at = (static_cast<size_t>(sb + static_cast<int64_t>(p.row0 + row) * tot + col)) * esize;
+      if (lane * 16u < row_bytes) {
+        const uint4 chunk = reinterpret_cast<const uint4*>(stage)[lane];
+        for (int q = 0; q < tp.world; ++q)
+          reinterpret_cast<uint4*>(tp.y[q] + slot_off + at)[lane] = chunk;
       }
     }
-    (void)esize;
     if (blockIdx.x == 0 && tid == 0) {  // the slot's size, for this rank's gather (same on every rank)
       tp.meta[p.tp_slot * 4 + 0] = p.tp_meta_cb;
       tp.meta[p.tp_slot * 4 + 1] = p.tp_meta_bytes;
     }
-    __threadfence_system();  // this thread's stores, before the flag
-    __syncthreads();
-    if (tid < static_cast<uint32_t>(tp.world)) {
-      uint32_t* f = tp.flag[tid] + static_cast<size_t>(p.tp_slot) * tp.max_cb + cbb + static_cast<int>(col / 128);
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(step) : "memory");
-    }
+    (void)cbb;  // the step's gather releases every rank's columns at once (one system-scope fence per step)
     return;
   }
   for (int row = static_cast<int>(warp); row < rows; row += kW5) {

@@ -15,7 +15,7 @@ constexpr int kGemvCtasPerSm = 3;  // the decode GEMV's persistent grid: CTAs pe
 constexpr int kMaxTpRanks = 8;
 struct TpDev {
   uint8_t* y[kMaxTpRanks];      // rank q's gathered outputs: [2 parities][slots][slot_bytes]
-  uint32_t* flag[kMaxTpRanks];  // rank q's flags: [slots][max_cb], the step whose data a column block holds
+  uint32_t* flag[kMaxTpRanks];  // rank q's done words: [world], the last step each rank published there
   uint32_t* step;               // this rank's step counter
   uint32_t* meta;               // this rank's slot metadata: [slots][4] (gathered column blocks, bytes)
   int32_t world, rank, slots, max_cb;
@@ -52,7 +52,7 @@ struct GemvParams {
   int64_t tp_total[kMaxSegments];    // per segment: the gathered width
   int64_t tp_col0[kMaxSegments];     // per segment: this rank's first column in it
   int64_t tp_seg_base[kMaxSegments]; // per segment: first element of its [rows][width] block in the slot
-  int32_t tp_cb_base[kMaxSegments];  // per segment: first gathered column block (flag index)
+  int32_t tp_cb_base[kMaxSegments];  // per segment: first gathered column block
   uint32_t tp_meta_cb, tp_meta_bytes; // the slot's gathered column blocks and bytes (for the gather)
 };
 

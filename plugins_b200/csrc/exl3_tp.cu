@@ -2,16 +2,18 @@
 //
 // Every rank holds an exchange buffer in its own HBM, mapped into the other ranks with CUDA IPC:
 //   y region    [2 parities][slots][slot_bytes]  gathered outputs, one slot per column-parallel linear of a step;
-//   flag region [slots][max_cb] u32              per gathered 128-column block: the step whose data it holds;
-//   meta        [slots][4] u32                   per slot: its gathered column blocks and bytes (written by the GEMV);
+//   done        [world] u32                      per rank: the last step whose columns it has published here;
+//   meta        [slots][4] u32                   per slot: its gathered bytes (written by the GEMV);
 //   step        u32                              this rank's step counter.
 // A step is exl3_tp_begin (step += 1 on the device), the column-parallel GEMVs (exl3_matmul_tp: each cluster leader
-// stores its 128 output columns into the slot of EVERY rank over NVLink, then releases its flag = step on every
-// rank), and exl3_tp_gather (waits, acquire, until every flag of the slots holds the step, then copies the slots out).
-// Parity = step & 1: a rank is at most one step ahead of any other (its step s+1 GEMVs start only after it gathered
-// step s, which needed everyone's step s writes), so two copies of the slots never race.  Flags only grow, so nothing
-// is reset between steps and a CUDA graph of whole steps replays as is.  Every wait is bounded (one second): a
-// missing peer sets EXL3_ERR_TP_TIMEOUT in the device error word and the kernel returns.
+// stores its 128 output columns into the slot of EVERY rank over NVLink, plain stores), and exl3_tp_gather: one
+// thread fences at system scope and releases done[rank] = step on every rank (the step's stores of this rank, all
+// launches at once), then the slots' CTAs wait (acquire) until every rank's done holds the step and copy the slots
+// out.  One system-scope release per step, not per launch: measured, a release per GEMV launch cost more than the
+// launch.  Parity = step & 1: a rank starts step s+1 only after its gather saw every rank publish step s, and a rank
+// publishes step s+1 only after its own step-s gather finished, so the two copies of the slots never race.  The done
+// words only grow, so nothing is reset between steps and a CUDA graph of whole steps replays as is.  Every wait is
+// bounded (one second): a missing peer sets EXL3_ERR_TP_TIMEOUT in the device error word and the kernel returns.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -45,34 +47,47 @@ __global__ void tp_begin_kernel(uint32_t* step) {
   if (threadIdx.x == 0) *step += 1u;
 }
 
-// One CTA per slot: wait (bounded) until every flag of the slot holds the step, then copy the slot to out.
-__global__ void __launch_bounds__(256) tp_gather_kernel(const uint8_t* __restrict__ y, const uint32_t* flags,
-                                                        const uint32_t* meta, const uint32_t* step_p, int slots,
-                                                        int max_cb, int64_t slot_bytes, int slot0,
+// This rank's columns of the step, published to every rank: a system-scope fence (the GEMVs before this kernel in
+// stream order wrote them), then done[rank] = step on every rank.
+__global__ void tp_publish_kernel(const exl3::TpDev* tp) {
+  if (threadIdx.x != 0) return;
+  const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(tp->step);
+  asm volatile("fence.sc.sys;" ::: "memory");
+  for (int q = 0; q < tp->world; ++q) {
+    uint32_t* f = tp->flag[q] + tp->rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(step) : "memory");
+  }
+}
+
+// One CTA per slot: wait (bounded) until every rank published the step, then copy the slot to out.
+__global__ void __launch_bounds__(256) tp_gather_kernel(const uint8_t* __restrict__ y, const uint32_t* done,
+                                                        const uint32_t* meta, const uint32_t* step_p, int world,
+                                                        int slots, int64_t slot_bytes, int slot0,
                                                         uint8_t* __restrict__ out, uint32_t* err) {
   __shared__ int s_fail;
   const int slot = slot0 + static_cast<int>(blockIdx.x);
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(step_p);
-  const uint32_t ncb = meta[slot * 4 + 0], nbytes = meta[slot * 4 + 1];
   if (threadIdx.x == 0) s_fail = 0;
   __syncthreads();
-  for (uint32_t c = threadIdx.x; c < ncb && c < static_cast<uint32_t>(max_cb); c += blockDim.x) {
-    const uint32_t* f = flags + static_cast<size_t>(slot) * max_cb + c;
+  if (threadIdx.x < static_cast<uint32_t>(world)) {
+    const uint32_t* f = done + threadIdx.x;
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-    if (static_cast<int32_t>(v - step) >= 0) continue;
-    const uint64_t t0 = exl3::global_timer_ns();
-    while (true) {
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-      if (static_cast<int32_t>(v - step) >= 0) break;
-      if (exl3::global_timer_ns() - t0 > 1000000000ull) {
-        s_fail = 1;
-        break;
+    if (static_cast<int32_t>(v - step) < 0) {
+      const uint64_t t0 = exl3::global_timer_ns();
+      while (true) {
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (static_cast<int32_t>(v - step) >= 0) break;
+        if (exl3::global_timer_ns() - t0 > 1000000000ull) {
+          s_fail = 1;
+          break;
+        }
       }
     }
   }
   __syncthreads();
   if (s_fail && threadIdx.x == 0) atomicOr(err, exl3::kErrTpTimeout);
+  const uint32_t nbytes = meta[slot * 4 + 1];
   const uint8_t* src = y + (static_cast<size_t>(step & 1u) * slots + slot) * slot_bytes;
   uint8_t* dst = out + static_cast<size_t>(blockIdx.x) * slot_bytes;
   const uint32_t n16 = nbytes / 16u;
@@ -113,7 +128,7 @@ exl3_verdict exl3_tp_create(int32_t device, int32_t world, int32_t rank, int32_t
   tp->max_cb = max_cb;
   tp->slot_bytes = slot_bytes;
   tp->y_bytes = 2u * static_cast<size_t>(slots) * slot_bytes;
-  tp->flag_bytes = (static_cast<size_t>(slots) * max_cb * 4 + 255) / 256 * 256;
+  tp->flag_bytes = 256;  // done[world]
   const size_t total = tp->y_bytes + tp->flag_bytes + static_cast<size_t>(slots) * kMetaBytes + 256;
   bool ok = cudaMalloc(&tp->base, total) == cudaSuccess;
   ok = ok && cudaMemset(tp->base + tp->y_bytes, 0, total - tp->y_bytes) == cudaSuccess;
@@ -198,19 +213,20 @@ exl3_verdict exl3_tp_gather(exl3_tp* tp, int32_t slot0, int32_t nslots, void* st
   if (!tp || !tp->connected || !out) return refuse(EXL3_FAILED, "exl3_tp_gather: bad arguments");
   if (slot0 < 0 || nslots < 1 || slot0 + nslots > tp->slots) return refuse(EXL3_UNSUPPORTED, "exl3_tp_gather: slot range");
   if (reinterpret_cast<uintptr_t>(out) % 16 != 0) return refuse(EXL3_UNSUPPORTED, "exl3_tp_gather: out on a 16-byte boundary");
-  uint32_t* err = nullptr;
   int prev = -1;
   cudaGetDevice(&prev);
   if (prev != tp->device) cudaSetDevice(tp->device);
-  err = exl3::device_error_ptr();
-  const uint8_t* flags = tp->base + tp->y_bytes;
+  uint32_t* err = exl3::device_error_ptr();
+  const uint32_t* done = reinterpret_cast<const uint32_t*>(tp->base + tp->y_bytes);
   const uint32_t* meta = meta_of(tp->base, tp->y_bytes, tp->flag_bytes);
   const uint32_t* step = reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(meta) +
                                                            static_cast<size_t>(tp->slots) * kMetaBytes);
-  tp_gather_kernel<<<nslots, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      tp->base, reinterpret_cast<const uint32_t*>(flags), meta, step, tp->slots, tp->max_cb, tp->slot_bytes, slot0,
-      static_cast<uint8_t*>(out), err);
-  const bool ok = err && cudaGetLastError() == cudaSuccess;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  tp_publish_kernel<<<1, 32, 0, st>>>(tp->dev);
+  bool ok = cudaGetLastError() == cudaSuccess;
+  tp_gather_kernel<<<nslots, 256, 0, st>>>(tp->base, done, meta, step, tp->world, tp->slots, tp->slot_bytes, slot0,
+                                           static_cast<uint8_t*>(out), err);
+  ok = ok && err && cudaGetLastError() == cudaSuccess;
   if (prev >= 0 && prev != tp->device) cudaSetDevice(prev);
   return ok ? exl3_verdict{EXL3_OK, nullptr} : refuse(EXL3_FAILED, "exl3_tp_gather: launch failed");
 }
