@@ -176,21 +176,25 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
     experts, hidden, inter, topk, total = 256, 4096, 2048, 8, 32
     tokens = total // world
     e0, e1 = S.expert_range(experts, rank, world)
-    local, shared = [], []
+    local = []
     for i, (a, b) in enumerate(((hidden, inter), (hidden, inter), (inter, hidden))):
         tr, suh, svh = E.random_linear(a, b, 48, seed=3 + i, groups=experts, device=device)
-        local.append(Q.weight_from_tensors(tr[e0:e1].contiguous(), suh[e0:e1].contiguous(), svh[e0:e1].contiguous()))
+        st, ssu, ssv = E.random_linear(a, b, 48, seed=13 + i, groups=1, device=device)
+        # this rank's experts, then the shared expert (its slots stay on the token's rank)
+        local.append(Q.weight_from_tensors(torch.cat([tr[e0:e1], st]), torch.cat([suh[e0:e1], ssu]),
+                                           torch.cat([svh[e0:e1], ssv])))
         del tr, suh, svh
-        tr, suh, svh = E.random_linear(a, b, 48, seed=13 + i, groups=1, device=device)
-        shared.append(Q.weight_from_tensors(tr, suh, svh))
     g = torch.Generator(device=device).manual_seed(4)
     logits = torch.randn((total, experts), device=device, generator=g)
     sc, ind = torch.topk(torch.softmax(logits, -1), topk, -1)
     x_all = torch.randn((total, hidden), device=device, generator=g).half()
     sl = slice(rank * tokens, (rank + 1) * tokens)
-    x, ind, sc = x_all[sl].contiguous(), ind[sl].to(torch.int32).contiguous(), sc[sl].float().contiguous()
+    # the slot lists with the shared expert as the last column (id 256, score 1)
+    ind = torch.cat([ind[sl].to(torch.int32), torch.full((tokens, 1), experts, dtype=torch.int32, device=device)], 1)
+    sc = torch.cat([sc[sl].float(), torch.ones((tokens, 1), device=device)], 1)
+    x, ind, sc = x_all[sl].contiguous(), ind.contiguous(), sc.contiguous()
     ep = S.ExpertParallelSwiglu(*local, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=rank,
-                                world=world, device=device, shared=shared)
+                                world=world, device=device, shared=True)
     y = torch.empty_like(x)
     st = torch.cuda.Stream(device=device)
     st.wait_stream(torch.cuda.current_stream())
@@ -216,8 +220,8 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1) / steps
     per_expert = 3 * (hidden * inter * 3 // 8 + 2 * hidden + 2 * inter)
-    all_ind = torch.topk(torch.softmax(logits, -1), topk, -1)[1]
-    mine = int(((torch.unique(all_ind) >= e0) & (torch.unique(all_ind) < e1)).sum().item())
+    all_ind = torch.unique(torch.topk(torch.softmax(logits, -1), topk, -1)[1])
+    mine = int(((all_ind >= e0) & (all_ind < e1)).sum().item())
     stats = torch.tensor([ms, float((mine + 1) * per_expert)], device=device, dtype=torch.float64)
     if world > 1:
         t = stats[:1].clone()

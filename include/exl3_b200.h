@@ -197,9 +197,11 @@ exl3_verdict exl3_matmul_timed(const exl3_weight *w, const exl3_tensor *x, uint3
  * error word marks a dispatch that had more than C rows for one peer (the extra slots are dropped). */
 
 /* x [T, D], inds [T, K] (global expert ids; outside 0..experts-1 = absent) -> send [world, C + 1, D] and
- * back_slot [T, K] i32: the row of the returned buffer that holds slot (t, k), -1 if absent or dropped. */
+ * back_slot [T, K] i32: the row of the returned buffer that holds slot (t, k), -1 if absent or dropped.  With
+ * `shared` set, id `experts` is a shared expert that every rank holds at local index experts / world: its slots go to
+ * the calling rank's own block. */
 exl3_verdict exl3_ep_dispatch(const exl3_tensor *x, const exl3_tensor *inds, int32_t experts, int32_t world,
-                              void *stream, exl3_tensor *send, exl3_tensor *back_slot);
+                              int32_t rank, int32_t shared, void *stream, exl3_tensor *send, exl3_tensor *back_slot);
 /* received blocks [world, C + 1, D] -> swiglu's inds [world, C + 1, 1] i32 (metadata rows -1) and scores (all 1). */
 exl3_verdict exl3_ep_unpack(const exl3_tensor *recv, void *stream, exl3_tensor *inds, exl3_tensor *scores);
 /* out [T, D] = sum_k scores[t, k] * back[back_slot[t, k]] in k order (f32), + shared [T, D] f32 when its data is not

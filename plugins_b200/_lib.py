@@ -148,8 +148,8 @@ def lib() -> ctypes.CDLL:
             L.exl3_tp_gather.restype = Verdict
             L.exl3_tp_gather.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
             L.exl3_ep_dispatch.restype = Verdict
-            L.exl3_ep_dispatch.argtypes = [P(Tensor), P(Tensor), ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
-                                           P(Tensor), P(Tensor)]
+            L.exl3_ep_dispatch.argtypes = [P(Tensor), P(Tensor), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                           ctypes.c_int32, ctypes.c_void_p, P(Tensor), P(Tensor)]
             L.exl3_ep_unpack.restype = Verdict
             L.exl3_ep_unpack.argtypes = [P(Tensor), ctypes.c_void_p, P(Tensor), P(Tensor)]
             L.exl3_ep_combine.restype = Verdict

@@ -1,7 +1,8 @@
 // exl3_ep.cu -- expert parallelism for the routed experts: the dispatch and combine either side of the two NCCL
 // all-to-alls (the all-to-alls themselves are the caller's: torch.distributed or ncclSend/ncclRecv).
 //
-// Rank r of `world` owns experts [r E/world, (r+1) E/world) of every bank.  A dispatch buffer holds one block per peer,
+// Rank r of `world` owns experts [r E/world, (r+1) E/world) of every bank (plus, when a shared expert is used, the
+// shared expert as local expert E/world: its slots stay on the token's own rank).  A dispatch buffer holds one block per peer,
 // each [C + 1][D] in x's dtype:
 //   rows 0 .. C-1   token rows routed to that peer's experts, in slot order (token-major, k minor);
 //   row C           metadata: 32-bit word j (j < C) = the peer-local expert of row j, -1 for an empty row.
@@ -30,17 +31,20 @@ __device__ __forceinline__ int read_index(const void* inds, int u32, size_t i) {
   return u32 ? static_cast<int>(static_cast<const uint32_t*>(inds)[i]) : static_cast<const int32_t*>(inds)[i];
 }
 
-// One CTA per destination peer d: its thread 0 lists the slots routed to d (slot order), writes the metadata row and
-// the slots' return positions; then the CTA copies the token rows.  CTA 0 also marks slots with an expert outside the
-// bank (no peer takes them) as absent.  Slots beyond the capacity are dropped and flagged.
+// Grid (world, copy CTAs): CTA (d, c) lists the slots routed to peer d (its thread 0, in slot order) and copies every
+// c-th of their token rows; CTA (d, 0) also writes the metadata row and the slots' return positions.  A slot whose
+// expert is `experts` with `shared` set goes to this rank's own block (the shared expert, held by every rank at local
+// index experts / world); other experts outside the bank are absent (CTA (0, 0) marks them).  Slots beyond the
+// capacity are dropped and flagged.
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(const void* __restrict__ x, int32_t esize, int tokens,
                                                           int topk, int hidden, const void* __restrict__ inds,
-                                                          int inds_u32, int experts, int world, int cap,
-                                                          uint8_t* __restrict__ send, int32_t* __restrict__ back_slot,
-                                                          uint32_t* err) {
+                                                          int inds_u32, int experts, int world, int rank, int shared,
+                                                          int cap, uint8_t* __restrict__ send,
+                                                          int32_t* __restrict__ back_slot, uint32_t* err) {
   __shared__ int s_tok[kMaxEpCapacity];
   __shared__ int s_count;
   const int d = blockIdx.x;
+  const bool head = blockIdx.y == 0;
   const int per = experts / world;
   const size_t row_bytes = static_cast<size_t>(hidden) * esize;
   uint8_t* block = send + static_cast<size_t>(d) * (cap + 1) * row_bytes;
@@ -50,33 +54,43 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const void* __restrict
     bool over = false;
     for (int s = 0; s < tokens * topk; ++s) {
       const int e = read_index(inds, inds_u32, s);
-      if (e < 0 || e >= experts) {
-        if (d == 0) back_slot[s] = -1;
+      int dest, local;
+      if (e >= 0 && e < experts) {
+        dest = e / per;
+        local = e - dest * per;
+      } else if (shared && e == experts) {
+        dest = rank;
+        local = per;
+      } else {
+        if (head && d == 0) back_slot[s] = -1;
         continue;
       }
-      if (e / per != d) continue;
+      if (dest != d) continue;
       if (j < cap) {
         s_tok[j] = s / topk;
-        meta[j] = e - d * per;
-        back_slot[s] = d * (cap + 1) + j;
+        if (head) {
+          meta[j] = local;
+          back_slot[s] = d * (cap + 1) + j;
+        }
         ++j;
       } else {
-        back_slot[s] = -1;
+        if (head) back_slot[s] = -1;
         over = true;
       }
     }
-    for (int i = j; i < cap; ++i) meta[i] = -1;
+    if (head) {
+      for (int i = j; i < cap; ++i) meta[i] = -1;
+      if (over) atomicOr(err, exl3::kErrEpOverflow);
+    }
     s_count = j;
-    if (over) atomicOr(err, exl3::kErrEpOverflow);
   }
   __syncthreads();
   const int n = s_count;
   const size_t words = row_bytes / 16;  // rows are whole 16-byte vectors (hidden % 128 == 0)
-  for (size_t i = threadIdx.x; i < static_cast<size_t>(n) * words; i += blockDim.x) {
-    const int j = static_cast<int>(i / words);
-    const size_t w = i % words;
+  for (int j = static_cast<int>(blockIdx.y); j < n; j += static_cast<int>(gridDim.y)) {
     const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(x) + s_tok[j] * row_bytes);
-    reinterpret_cast<uint4*>(block + static_cast<size_t>(j) * row_bytes)[w] = src[w];
+    uint4* dst = reinterpret_cast<uint4*>(block + static_cast<size_t>(j) * row_bytes);
+    for (size_t w = threadIdx.x; w < words; w += blockDim.x) dst[w] = src[w];
   }
 }
 
@@ -137,7 +151,7 @@ struct Dev {
 extern "C" {
 
 exl3_verdict exl3_ep_dispatch(const exl3_tensor* x, const exl3_tensor* inds, int32_t experts, int32_t world,
-                              void* stream, exl3_tensor* send, exl3_tensor* back_slot) {
+                              int32_t rank, int32_t shared, void* stream, exl3_tensor* send, exl3_tensor* back_slot) {
   if (!x || !inds || !send || !back_slot) return refuse(EXL3_FAILED, "exl3_ep_dispatch: bad arguments");
   if (x->ndim != 2 || inds->ndim != 2 || send->ndim != 3 || back_slot->ndim != 2)
     return refuse(EXL3_UNSUPPORTED, "exl3_ep_dispatch: x [T, D], inds [T, K], send [world, C + 1, D], back_slot [T, K]");
@@ -151,6 +165,7 @@ exl3_verdict exl3_ep_dispatch(const exl3_tensor* x, const exl3_tensor* inds, int
     return refuse(EXL3_UNSUPPORTED, "exl3_ep_dispatch: inds and back_slot are [T, K], K <= 32");
   if (world < 1 || experts < world || experts % world != 0)
     return refuse(EXL3_UNSUPPORTED, "exl3_ep_dispatch: the experts split evenly over the ranks");
+  if (rank < 0 || rank >= world) return refuse(EXL3_UNSUPPORTED, "exl3_ep_dispatch: rank out of range");
   if (send->shape[0] != world || send->shape[2] != hidden || hidden % 128 != 0)
     return refuse(EXL3_UNSUPPORTED, "exl3_ep_dispatch: send is [world, C + 1, D], D a multiple of 128");
   if (cap < 1 || cap > kMaxEpCapacity || 4 * cap > hidden * esize_of(x->dtype))
@@ -163,10 +178,12 @@ exl3_verdict exl3_ep_dispatch(const exl3_tensor* x, const exl3_tensor* inds, int
   Dev dev(send->data);
   uint32_t* err = exl3::device_error_ptr();
   if (!err) return refuse(EXL3_FAILED, "exl3_ep_dispatch: no device error word");
-  ep_dispatch_kernel<<<world, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  // copy CTAs per peer: about 148 CTAs in all, at least one per peer
+  const int copy = world >= 148 ? 1 : (148 + world - 1) / world;
+  ep_dispatch_kernel<<<dim3(world, copy), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       x->data, esize_of(x->dtype), static_cast<int>(tokens), static_cast<int>(topk), static_cast<int>(hidden),
-      inds->data, inds->dtype == EXL3_U32, experts, world, static_cast<int>(cap), static_cast<uint8_t*>(send->data),
-      static_cast<int32_t*>(back_slot->data), err);
+      inds->data, inds->dtype == EXL3_U32, experts, world, rank, shared ? 1 : 0, static_cast<int>(cap),
+      static_cast<uint8_t*>(send->data), static_cast<int32_t*>(back_slot->data), err);
   if (cudaGetLastError() != cudaSuccess) return refuse(EXL3_FAILED, "exl3_ep_dispatch: launch failed");
   return {EXL3_OK, nullptr};
 }

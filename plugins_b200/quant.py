@@ -312,10 +312,12 @@ def decode_dense(w: Weight, group: int = 0, dp4a: bool = False, stream=None) -> 
 
 
 def ep_dispatch(x: torch.Tensor, inds: torch.Tensor, experts: int, world: int, send: torch.Tensor,
-                back_slot: torch.Tensor, stream=None) -> None:
-    """Expert-parallel dispatch: x [T, D], inds [T, K] -> send [world, C + 1, D] (x's dtype), back_slot [T, K] i32."""
+                back_slot: torch.Tensor, rank: int = 0, shared: bool = False, stream=None) -> None:
+    """Expert-parallel dispatch: x [T, D], inds [T, K] -> send [world, C + 1, D] (x's dtype), back_slot [T, K] i32.
+    With `shared`, expert id `experts` is the shared expert every rank holds (local index experts / world)."""
     check(L.lib().exl3_ep_dispatch(ctypes.byref(_tensor(x)), ctypes.byref(_tensor(inds)), int(experts), int(world),
-                                   _stream(stream), ctypes.byref(_tensor(send)), ctypes.byref(_tensor(back_slot))))
+                                   int(rank), int(bool(shared)), _stream(stream), ctypes.byref(_tensor(send)),
+                                   ctypes.byref(_tensor(back_slot))))
 
 
 def ep_unpack(recv: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor, stream=None) -> None:

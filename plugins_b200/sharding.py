@@ -162,17 +162,18 @@ def expert_range(experts: int, rank: int, world: int) -> tuple[int, int]:
     return rank * per, (rank + 1) * per
 
 
-def ep_capacity(tokens: int, topk: int, experts: int, world: int) -> int:
-    """Rows one rank can route to one peer: each token sends at most min(K, E/world) distinct experts there."""
-    return max(1, tokens * min(topk, experts // world))
+def ep_capacity(tokens: int, topk: int, experts: int, world: int, shared: bool = False) -> int:
+    """Rows one rank can route to one peer: each token sends at most min(K, E/world) distinct experts there (one more,
+    its shared-expert slot, to its own rank)."""
+    return max(1, tokens * (min(topk, experts // world) + (1 if shared else 0)))
 
 
 class CudaExpertOps:
     """The compute of the expert-parallel step: the library's dispatch, unpack, swiglu and combine."""
 
     @staticmethod
-    def dispatch(x, inds, experts, world, send, back_slot):
-        Q.ep_dispatch(x, inds, experts, world, send, back_slot)
+    def dispatch(x, inds, experts, world, rank, shared, send, back_slot):
+        Q.ep_dispatch(x, inds, experts, world, send, back_slot, rank=rank, shared=shared)
 
     @staticmethod
     def unpack(recv, inds, scores):
@@ -183,26 +184,28 @@ class CudaExpertOps:
         Q.swiglu(gate, up, down, x, inds, scores, limit=limit, out=out)
 
     @staticmethod
-    def combine(back, back_slot, scores, shared, out):
-        Q.ep_combine(back, back_slot, scores, shared, out)
+    def combine(back, back_slot, scores, out):
+        Q.ep_combine(back, back_slot, scores, None, out)
 
 
 class ExpertParallelSwiglu:
     """Routed SwiGLU experts split over the ranks.
 
-    gate/up/down: this rank's banks (experts [r E/world, (r+1) E/world)); shared: an optional (gate, up, down) triple
-    of one-expert banks that every rank holds; tokens: the tokens each rank brings per step (the same on every rank,
-    so every block of the exchange has the same size).  ``forward(x [T, D], inds [T, K], scores [T, K])`` returns
-    out [T, D] in x's dtype: sum_k scores * expert(x) over the routed experts, plus the shared expert.
+    gate/up/down: this rank's banks -- experts [r E/world, (r+1) E/world), followed, when ``shared`` is set, by the
+    shared expert (every rank holds it); tokens: the tokens each rank brings per step (the same on every rank, so every
+    block of the exchange has the same size).  ``forward(x [T, D], inds, scores)`` returns out [T, D] in x's dtype:
+    sum_k scores * expert(x) over the routed experts, plus the shared expert.  inds / scores are [T, K]; with a shared
+    expert they may also be [T, K + 1] with the last column already the shared expert (id E, score 1).  A shared slot
+    stays on the token's own rank and runs in the same swiglu call as the routed slots.
     """
 
     def __init__(self, gate, up, down, experts: int, tokens: int, topk: int, hidden: int, rank: int, world: int,
-                 dtype=torch.float16, device=None, group=None, shared=None, limit: int = 0, ops=None):
-        self.gate, self.up, self.down, self.shared = gate, up, down, shared
+                 dtype=torch.float16, device=None, group=None, shared: bool = False, limit: int = 0, ops=None):
+        self.gate, self.up, self.down, self.shared = gate, up, down, bool(shared)
         self.experts, self.tokens, self.topk, self.hidden = experts, tokens, topk, hidden
         self.rank, self.world, self.group, self.limit = rank, world, group, limit
         self.ops = ops or CudaExpertOps()
-        self.cap = ep_capacity(tokens, topk, experts, world)
+        self.cap = ep_capacity(tokens, topk, experts, world, self.shared)
         dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         blk = (world, self.cap + 1, hidden)
         self.send = torch.empty(blk, dtype=dtype, device=dev)
@@ -211,11 +214,11 @@ class ExpertParallelSwiglu:
         self.back = torch.empty(blk, dtype=torch.float32, device=dev)
         self.r_inds = torch.empty((world, self.cap + 1, 1), dtype=torch.int32, device=dev)
         self.r_scores = torch.empty((world, self.cap + 1, 1), dtype=torch.float32, device=dev)
-        self.back_slot = torch.empty((tokens, topk), dtype=torch.int32, device=dev)
-        if shared is not None:
-            self.sh_out = torch.empty((1, tokens, hidden), dtype=torch.float32, device=dev)
-            self.sh_inds = torch.zeros((1, tokens, 1), dtype=torch.int32, device=dev)
-            self.sh_scores = torch.ones((1, tokens, 1), dtype=torch.float32, device=dev)
+        k = topk + (1 if self.shared else 0)
+        self.back_slot = torch.empty((tokens, k), dtype=torch.int32, device=dev)
+        if self.shared:  # the [T, K + 1] slot lists when the caller passes [T, K]
+            self.ext_inds = torch.full((tokens, k), experts, dtype=torch.int32, device=dev)
+            self.ext_scores = torch.ones((tokens, k), dtype=torch.float32, device=dev)
 
     def _all_to_all(self, out, inp):
         if self.world == 1:
@@ -224,21 +227,20 @@ class ExpertParallelSwiglu:
             dist.all_to_all_single(out, inp, group=self.group)
 
     def forward(self, x: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor, out: torch.Tensor | None = None):
-        if x.shape != (self.tokens, self.hidden) or inds.shape != (self.tokens, self.topk):
-            raise ValueError("x [tokens, hidden] and inds [tokens, topk] of the shapes the driver was built for")
+        k = self.topk + (1 if self.shared else 0)
+        if x.shape != (self.tokens, self.hidden) or inds.shape[0] != self.tokens or inds.shape[1] not in (self.topk, k):
+            raise ValueError("x [tokens, hidden] and inds [tokens, topk (+1 with the shared expert)]")
+        if self.shared and inds.shape[1] == self.topk:
+            self.ext_inds[:, :self.topk].copy_(inds)
+            self.ext_scores[:, :self.topk].copy_(scores)
+            inds, scores = self.ext_inds, self.ext_scores
         ops = self.ops
-        ops.dispatch(x, inds, self.experts, self.world, self.send, self.back_slot)
+        ops.dispatch(x, inds, self.experts, self.world, self.rank, self.shared, self.send, self.back_slot)
         self._all_to_all(self.recv, self.send)
         ops.unpack(self.recv, self.r_inds, self.r_scores)
         ops.swiglu(self.gate, self.up, self.down, self.recv, self.r_inds, self.r_scores, self.ys, self.limit)
         self._all_to_all(self.back, self.ys)
-        shared = None
-        if self.shared is not None:
-            sg, su, sd = self.shared
-            ops.swiglu(sg, su, sd, x.view(1, self.tokens, self.hidden), self.sh_inds, self.sh_scores, self.sh_out,
-                       self.limit)
-            shared = self.sh_out.view(self.tokens, self.hidden)
         if out is None:
             out = torch.empty_like(x)
-        ops.combine(self.back, self.back_slot, scores, shared, out)
+        ops.combine(self.back, self.back_slot, scores, out)
         return out

@@ -34,7 +34,7 @@ class OracleLinearOps:
         return y
 
 
-def ep_dispatch_ref(x, inds, experts, world, send, back_slot):
+def ep_dispatch_ref(x, inds, experts, world, send, back_slot, rank=0, shared=False):
     """exl3_ep_dispatch on the host: fills send [world, C + 1, D] (x's dtype) and back_slot [T, K]."""
     tokens, topk = inds.shape
     cap = send.shape[1] - 1
@@ -46,15 +46,19 @@ def ep_dispatch_ref(x, inds, experts, world, send, back_slot):
         meta = send[d, cap].view(torch.int32)
         j = 0
         for s, e in enumerate(flat):
-            if e < 0 or e >= experts:
+            if 0 <= e < experts:
+                dest, local = e // per, e % per
+            elif shared and e == experts:
+                dest, local = rank, per
+            else:
                 if d == 0:
                     bs[s] = -1
                 continue
-            if e // per != d:
+            if dest != d:
                 continue
             if j < cap:
                 send[d, j] = x[s // topk]
-                meta[j] = e - d * per
+                meta[j] = local
                 bs[s] = d * (cap + 1) + j
                 j += 1
             else:
@@ -94,8 +98,8 @@ class OracleExpertOps:
     def __init__(self, oracle):
         self.O = oracle
 
-    def dispatch(self, x, inds, experts, world, send, back_slot):
-        ep_dispatch_ref(x, inds, experts, world, send, back_slot)
+    def dispatch(self, x, inds, experts, world, rank, shared, send, back_slot):
+        ep_dispatch_ref(x, inds, experts, world, send, back_slot, rank, shared)
 
     def unpack(self, recv, inds, scores):
         ep_unpack_ref(recv, inds, scores)
@@ -114,5 +118,5 @@ class OracleExpertOps:
                                        threads=2)
         out.copy_(torch.from_numpy(y).view(out.shape).to(out.dtype))
 
-    def combine(self, back, back_slot, scores, shared, out):
-        ep_combine_ref(back, back_slot, scores, shared, out)
+    def combine(self, back, back_slot, scores, out):
+        ep_combine_ref(back, back_slot, scores, None, out)

@@ -79,6 +79,19 @@ def test_dispatch_unpack_combine_match_the_host_restatement(Q, dtype):
     # same sums in the same order; the kernel fuses score * row + acc, the restatement rounds the product first, so
     # an f16 output can differ by one unit in the last place
     assert _rel(out.float().cpu(), out_ref.float()) < (1e-6 if dtype == torch.float32 else 2e-4)
+    # the shared expert (id `experts`) stays on the calling rank, at local index experts / world
+    sh_inds = torch.cat([inds, torch.full((tokens, 1), experts, dtype=torch.int32)], 1)
+    cap2 = S.ep_capacity(tokens, topk, experts, world, shared=True)
+    send2 = torch.empty((world, cap2 + 1, hidden), dtype=dtype, device="cuda")
+    back2 = torch.empty((tokens, topk + 1), dtype=torch.int32, device="cuda")
+    Q.ep_dispatch(x.cuda(), sh_inds.cuda(), experts, world, send2, back2, rank=2, shared=True)
+    send2_ref = torch.zeros((world, cap2 + 1, hidden), dtype=dtype)
+    back2_ref = torch.empty((tokens, topk + 1), dtype=torch.int32)
+    C.ep_dispatch_ref(x, sh_inds, experts, world, send2_ref, back2_ref, rank=2, shared=True)
+    torch.cuda.synchronize()
+    assert torch.equal(back2.cpu(), back2_ref)
+    for d in range(world):
+        assert torch.equal(send2.cpu()[d, cap2].view(torch.int32)[:cap2], send2_ref[d, cap2].view(torch.int32)[:cap2])
     assert Q.device_error(0) & L.ERR_EP_OVERFLOW == 0
 
 
@@ -113,22 +126,21 @@ def test_expert_parallel_on_one_rank_matches_swiglu_and_truth(Q, oracle):
     experts, hidden, inter, n, tokens, topk = 16, 512, 256, 48, 12, 4
     raw = _banks(E, experts, hidden, inter, n, 40)
     sraw = _banks(E, 1, hidden, inter, n, 50)
-    banks = [Q.weight_from_tensors(*b) for b in raw]
-    shared = [Q.weight_from_tensors(*b) for b in sraw]
     inds, scores = _routing(tokens, topk, experts, 2)
     inds, scores = inds.cuda(), scores.cuda()
     x = torch.randn((tokens, hidden), device="cuda", dtype=torch.float16)
-    ep = S.ExpertParallelSwiglu(*banks, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=0, world=1,
-                                shared=shared)
-    got = ep.forward(x, inds, scores)
-    # the single-GPU path: routed swiglu + the shared expert as one more slot of score 1 in an extended bank
+    # the bank with the shared expert appended (local index experts / world = experts at one rank)
     ext = [Q.weight_from_tensors(torch.cat([r[0], s[0]]), torch.cat([r[1], s[1]]), torch.cat([r[2], s[2]]))
            for r, s in zip(raw, sraw)]
+    ep = S.ExpertParallelSwiglu(*ext, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=0, world=1,
+                                shared=True)
+    got = ep.forward(x, inds, scores)
+    # the single-GPU path: the shared expert as one more slot of score 1
     inds2 = torch.cat([inds, torch.full((tokens, 1), experts, dtype=torch.int32, device="cuda")], 1)
     sc2 = torch.cat([scores, torch.ones((tokens, 1), device="cuda")], 1)
     single = Q.swiglu(*ext, x.view(1, tokens, hidden), inds2.view(1, tokens, topk + 1).contiguous(),
                       sc2.view(1, tokens, topk + 1).contiguous()).view(tokens, hidden)
-    assert _rel(_np(got.float()), _np(single.float())) < 1e-3
+    assert _rel(_np(got.float()), _np(single.float())) < 1e-5  # the same sums in the same order
     bank = lambda b: (_np(b[0]).view(np.uint16), _np(b[1]).view(np.uint16), _np(b[2]).view(np.uint16), n)
     want = oracle.moe_truth(_np(x.float()), _np(inds2), _np(sc2), *[bank(
         (torch.cat([r[0], s[0]]), torch.cat([r[1], s[1]]), torch.cat([r[2], s[2]]))) for r, s in zip(raw, sraw)],

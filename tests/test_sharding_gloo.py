@@ -97,10 +97,15 @@ def _ep_rank(rank, world, port, tokens, topk, experts, shared, limit):
             return (tr[e0:e1], su[e0:e1].view(np.uint16), sv[e0:e1].view(np.uint16), n)
 
         e0, e1 = S.expert_range(experts, rank, world)
-        local = [as_oracle(b, e0, e1) for b in banks]
         sh = [as_oracle(b) for b in sbanks] if shared else None
+        if shared:  # this rank's experts, then the shared expert (every rank holds it)
+            local = [(np.concatenate([tr[e0:e1], str_]), np.concatenate([su[e0:e1], ssu]).view(np.uint16),
+                      np.concatenate([sv[e0:e1], ssv]).view(np.uint16), n)
+                     for (tr, su, sv), (str_, ssu, ssv) in zip(banks, sbanks)]
+        else:
+            local = [as_oracle(b, e0, e1) for b in banks]
         ep = S.ExpertParallelSwiglu(*local, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=rank,
-                                    world=world, dtype=torch.float32, device=torch.device("cpu"), shared=sh,
+                                    world=world, dtype=torch.float32, device=torch.device("cpu"), shared=shared,
                                     limit=limit, ops=C.OracleExpertOps(O))
         sl = slice(rank * tokens, (rank + 1) * tokens)
         out = ep.forward(torch.from_numpy(x[sl]), torch.from_numpy(inds[sl]), torch.from_numpy(scores[sl]))
@@ -129,6 +134,15 @@ def test_dispatch_layout_and_overflow():
     import sharding_cpu_ops as C
     tokens, topk, experts, world, hidden = 3, 2, 4, 2, 128
     x = torch.arange(tokens * hidden, dtype=torch.float32).view(tokens, hidden)
+    # the shared expert (id `experts`) stays on the calling rank, at local index experts / world
+    sh_inds = torch.tensor([[0, 4], [3, 4], [2, 4]], dtype=torch.int32)
+    sh_send = torch.zeros((world, 6, hidden))  # capacity 5
+    sh_back = torch.empty((tokens, topk), dtype=torch.int32)
+    assert not C.ep_dispatch_ref(x, sh_inds, experts, world, sh_send, sh_back, rank=1, shared=True)
+    # rank 0 block: slot (0,0); rank 1 block (row 6 on): (0,1) shared, (1,0), (1,1) shared, (2,0), (2,1) shared
+    assert sh_back.tolist() == [[0, 6], [7, 8], [9, 10]]
+    assert sh_send[1, 5].view(torch.int32)[:5].tolist() == [2, 1, 2, 0, 2]
+    assert torch.equal(sh_send[1, 0], x[0]) and torch.equal(sh_send[1, 4], x[2])
     inds = torch.tensor([[0, 3], [2, -1], [1, 4]], dtype=torch.int32)  # -1 and 4 are outside the bank
     send = torch.full((world, 3, hidden), 7.0)
     back = torch.empty((tokens, topk), dtype=torch.int32)
