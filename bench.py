@@ -634,7 +634,7 @@ def main() -> None:
             "decode_tok_s": round(args.batch / (r1["ms"] * 1e-3), 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
-                         "kernel": "gate|up decode GEMV (4096 -> 2x12288 @ 3 bpw, one stream-K launch)",
+                         "kernel": "gate|up decode GEMV (4096 -> 2x12288 @ 3 bpw, one cluster-split launch, gemv5_kernel)",
                          "bytes_per_launch": gu_bytes, "ms_per_launch": round(r1["dom_ms"], 5),
                          "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
             "roofline_4bpw_qkv": {"achieved": round(qkv_bytes / (r1["qkv_ms"] * 1e-3) / 1e9, 1),
