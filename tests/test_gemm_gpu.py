@@ -78,6 +78,7 @@ def test_one_hot_rows_reproduce_w_hat(Q, E, oracle, shape, n):
 CASES = [
     # (in, out, n, rows)
     (512, 768, 64, 64), (1024, 640, 48, 200), (256, 1280, 32, 333), (768, 384, 96, 130), (384, 512, 80, 257),
+    (5120, 2304, 48, 128),  # the DeepSeek-V4.1 prefill shape (dsv41_prefill_dig_gemm_5120x2304)
 ]
 
 

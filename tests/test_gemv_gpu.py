@@ -97,6 +97,8 @@ CASES = [
     # (in, out, n, rows)
     (384, 256, 64, 1), (384, 256, 48, 3), (256, 384, 32, 8), (256, 384, 80, 5),
     (512, 640, 64, 9), (512, 256, 48, 16), (384, 512, 64, 17), (1024, 1024, 96, 2), (640, 384, 16, 4),
+    # DeepSeek-V4.1 widths (the ds41 kernels' 5120 / 2304, TK/dsv41_exl3_mul1h_k{2,3}_*.metal)
+    (5120, 2304, 32, 1), (2304, 5120, 48, 4),
 ]
 
 
