@@ -168,10 +168,10 @@ def measure_moe(Q, E, torch, peaks: dict, reps: int = 10) -> dict:
 
 def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict, steps: int = 20) -> dict:
     """Config 4 expert-parallel over the ranks (plugins_b200/sharding.py): rank r holds experts [32 r', ...) of the 256
-    (256/world each) plus the shared expert, brings 32/world of the 32 tokens, and a step is dispatch, all-to-all,
-    its experts' SwiGLU, all-to-all back, the shared expert and the combine -- captured in one CUDA graph (NCCL inside)
-    and timed as the max over ranks.  Bytes are the distinct routed experts each rank streams plus its shared
-    expert, summed over the ranks."""
+    (256/world each) plus the shared expert, brings 32/world of the 32 tokens, and a step is dispatch, exchange, its
+    experts' SwiGLU, exchange back and the combine -- captured in one CUDA graph and timed as the max over ranks, once
+    with the peer-memory exchange (exl3_epx_*, the headline) and once with NCCL all-to-alls.  Bytes are the distinct
+    routed experts each rank streams plus its shared expert, summed over the ranks."""
     from plugins_b200 import sharding as S
     experts, hidden, inter, topk, total = 256, 4096, 2048, 8, 32
     tokens = total // world
@@ -193,50 +193,61 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
     ind = torch.cat([ind[sl].to(torch.int32), torch.full((tokens, 1), experts, dtype=torch.int32, device=device)], 1)
     sc = torch.cat([sc[sl].float(), torch.ones((tokens, 1), device=device)], 1)
     x, ind, sc = x_all[sl].contiguous(), ind.contiguous(), sc.contiguous()
-    ep = S.ExpertParallelSwiglu(*local, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=rank,
-                                world=world, device=device, shared=True)
-    y = torch.empty_like(x)
-    st = torch.cuda.Stream(device=device)
-    st.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(st):
-        for _ in range(3):
-            ep.forward(x, ind, sc, out=y)
-    torch.cuda.current_stream().wait_stream(st)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=st):
-        ep.forward(x, ind, sc, out=y)
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(steps):
-        graph.replay()
-    ev1.record()
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1) / steps
     per_expert = 3 * (hidden * inter * 3 // 8 + 2 * hidden + 2 * inter)
     all_ind = torch.unique(torch.topk(torch.softmax(logits, -1), topk, -1)[1])
     mine = int(((all_ind >= e0) & (all_ind < e1)).sum().item())
-    stats = torch.tensor([ms, float((mine + 1) * per_expert)], device=device, dtype=torch.float64)
+
+    def timed(exchange):
+        ep = S.ExpertParallelSwiglu(*local, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=rank,
+                                    world=world, device=device, shared=True, exchange=exchange)
+        y = torch.empty_like(x)
+        st = torch.cuda.Stream(device=device)
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                ep.forward(x, ind, sc, out=y)
+        torch.cuda.current_stream().wait_stream(st)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            ep.forward(x, ind, sc, out=y)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(steps):
+            graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([ev0.elapsed_time(ev1) / steps], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        graph.reset()
+        if ep.peer is not None:
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()  # every rank's kernels are done before any exchange region is unmapped
+            ep.peer.close()
+        return float(t[0])
+
+    b = torch.tensor([float((mine + 1) * per_expert)], device=device, dtype=torch.float64)
     if world > 1:
-        t = stats[:1].clone()
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        b = stats[1:].clone()
         dist.all_reduce(b, op=dist.ReduceOp.SUM)
-        stats = torch.cat([t, b])
-    graph.reset()
-    ms, nbytes = float(stats[0]), float(stats[1])
+    nbytes = float(b[0])
+    ms = timed("peer")
+    ms_nccl = timed("nccl")
     gbs = nbytes / (ms * 1e-3) / 1e9
     return {"workload": "config 4 expert-parallel: 256 routed (256/N per GPU) + 1 shared expert, 4096 <-> 2048 "
-                        "@ 3 bpw, 32 tokens (32/N per GPU), top-8; NCCL all-to-all dispatch and combine",
+                        "@ 3 bpw, 32 tokens (32/N per GPU), top-8; dispatch and combine over NVLink peer memory",
             "n_gpus": world, "ms_per_step": round(ms, 4), "tokens_per_s": round(total / (ms * 1e-3), 1),
             "value": round(gbs, 1), "unit": "GB/s (whole box)", "bytes_per_step": int(nbytes),
-            "frac_of_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4)}
+            "frac_of_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4),
+            "nccl_all_to_all": {"ms_per_step": round(ms_nccl, 4),
+                                "value": round(nbytes / (ms_nccl * 1e-3) / 1e9, 1)}}
 
 
 def measure_c5(Q, E, torch, peaks: dict, reps: int = 5) -> dict:

@@ -209,6 +209,39 @@ exl3_verdict exl3_ep_unpack(const exl3_tensor *recv, void *stream, exl3_tensor *
 exl3_verdict exl3_ep_combine(const exl3_tensor *back, const exl3_tensor *back_slot, const exl3_tensor *scores,
                              const exl3_tensor *shared, void *stream, exl3_tensor *out);
 
+/* ------------------------------------------------------------------ expert parallelism over peer memory
+ *
+ * The same split as above with both all-to-alls done by this library's kernels over NVLink instead of a collective
+ * library: every rank holds a receive region [2][world][C + 1][D] (x's dtype) and a return region
+ * [2][world][C + 1][D] f32, mapped into the other ranks with CUDA IPC.  Setup as the column-parallel exchange:
+ * exl3_epx_create on every rank, exchange the 64-byte handles, exl3_epx_connect.  A step: exl3_epx_dispatch (x's
+ * rows straight into the owners' receive regions, then one system-scope release), exl3_epx_receive (bounded wait for
+ * every rank's dispatch; the received blocks into the caller's fixed buffer, with swiglu's inds and scores), swiglu
+ * on that buffer (f32 out), exl3_epx_return (each block straight back into its source rank's return region, then a
+ * release), exl3_epx_combine (bounded wait for every rank's return; the weighted sum).  Stream-ordered kernels with no
+ * host synchronisation: a whole step can be captured in a CUDA graph.  A wait that gives up (one second) sets
+ * EXL3_ERR_EP_TIMEOUT.  Every rank must run the same steps. */
+typedef struct exl3_epx exl3_epx;
+
+/* capacity C rows per (source, owner) pair, hidden D (a multiple of 128), dtype the activations' (f16, bf16, f32). */
+exl3_verdict exl3_epx_create(int32_t device, int32_t world, int32_t rank, int32_t cap, int32_t hidden, int32_t dtype,
+                             exl3_epx **out, uint8_t *ipc_handle);
+/* ipc_handles: world * 64 bytes, rank order (this rank's own entry is ignored). */
+exl3_verdict exl3_epx_connect(exl3_epx *ep, const uint8_t *ipc_handles);
+void exl3_epx_destroy(exl3_epx *ep);
+/* Begins a step: x [T, D], inds [T, K] as exl3_ep_dispatch (shared: id `experts` stays on this rank at local index
+ * experts / world) -> back_slot [T, K] i32, the return-region row of slot (t, k), -1 if absent or dropped. */
+exl3_verdict exl3_epx_dispatch(exl3_epx *ep, const exl3_tensor *x, const exl3_tensor *inds, int32_t experts,
+                               int32_t shared, void *stream, exl3_tensor *back_slot);
+/* -> xbuf [world, C + 1, D] (the rows every rank sent here, block q from rank q), inds [world, C + 1, 1] i32 (local
+ * expert, -1 = empty) and scores (1), ready for swiglu with this rank's banks. */
+exl3_verdict exl3_epx_receive(exl3_epx *ep, void *stream, exl3_tensor *xbuf, exl3_tensor *inds, exl3_tensor *scores);
+/* ys: swiglu's f32 output [world, C + 1, D]; block q goes back to rank q. */
+exl3_verdict exl3_epx_return(exl3_epx *ep, const exl3_tensor *ys, void *stream);
+/* Ends the step: out [T, D] = sum_k scores[t, k] * returned[back_slot[t, k]] in k order (f32). */
+exl3_verdict exl3_epx_combine(exl3_epx *ep, const exl3_tensor *back_slot, const exl3_tensor *scores, void *stream,
+                              exl3_tensor *out);
+
 /* ------------------------------------------------------------------ column parallelism with a fused all-gather
  *
  * Beside the seam (the reference is single-device): a linear split by output columns over `world` ranks (one process
@@ -274,6 +307,7 @@ exl3_verdict exl3_matmul_noalloc(const exl3_weight *w, const exl3_tensor *x, voi
 #define EXL3_ERR_BAD_SHAPE 2u     /* a launch saw a shape its host validation should have refused */
 #define EXL3_ERR_EP_OVERFLOW 4u   /* an expert-parallel dispatch had more rows for one peer than its capacity */
 #define EXL3_ERR_TP_TIMEOUT 8u    /* a column-parallel gather gave up waiting (one second) for a peer's columns */
+#define EXL3_ERR_EP_TIMEOUT 16u   /* a peer expert-parallel exchange gave up waiting (one second) for a peer's rows */
 exl3_verdict exl3_device_error(int32_t device, uint32_t *bits, int32_t clear);
 
 /* The library's build string. */

@@ -19,14 +19,16 @@ F16, BF16, F32, I32, U32, U16, I16 = 0, 1, 2, 3, 4, 5, 6
 WEIGHT_OWNED, WEIGHT_BANK, WEIGHT_GROUPED = 1, 2, 4
 MATMUL_PREPARED, MATMUL_INNER, MATMUL_DP4A, MATMUL_GEMV, MATMUL_GEMM = 1, 2, 4, 8, 16
 MAX_SEGMENTS = 4
-ERR_WAIT_TIMEOUT, ERR_BAD_SHAPE, ERR_EP_OVERFLOW, ERR_TP_TIMEOUT = 1, 2, 4, 8
+ERR_WAIT_TIMEOUT, ERR_BAD_SHAPE, ERR_EP_OVERFLOW, ERR_TP_TIMEOUT, ERR_EP_TIMEOUT = 1, 2, 4, 8, 16
 
 # every symbol include/exl3_b200.h declares
 EXPORTS = (
     "exl3_claims", "exl3_validate", "exl3_bill", "exl3_open", "exl3_close", "exl3_load_tensor", "exl3_load_bank",
     "exl3_release", "exl3_matmul", "exl3_moe", "exl3_swiglu", "exl3_matmul_ex", "exl3_matmul_timed",
-    "exl3_ep_dispatch", "exl3_ep_unpack", "exl3_ep_combine", "exl3_tp_create", "exl3_tp_connect", "exl3_tp_destroy",
-    "exl3_tp_begin", "exl3_matmul_tp", "exl3_tp_gather", "exl3_weight_view", "exl3_weight_stack",
+    "exl3_ep_dispatch", "exl3_ep_unpack", "exl3_ep_combine", "exl3_epx_create", "exl3_epx_connect",
+    "exl3_epx_destroy", "exl3_epx_dispatch", "exl3_epx_receive", "exl3_epx_return", "exl3_epx_combine",
+    "exl3_tp_create", "exl3_tp_connect", "exl3_tp_destroy", "exl3_tp_begin", "exl3_matmul_tp", "exl3_tp_gather",
+    "exl3_weight_view", "exl3_weight_stack",
     "exl3_decode_dense", "exl3_encode_trellis", "exl3_matmul_noalloc", "exl3_device_error", "exl3_version",
 )
 
@@ -154,6 +156,23 @@ def lib() -> ctypes.CDLL:
             L.exl3_ep_unpack.argtypes = [P(Tensor), ctypes.c_void_p, P(Tensor), P(Tensor)]
             L.exl3_ep_combine.restype = Verdict
             L.exl3_ep_combine.argtypes = [P(Tensor), P(Tensor), P(Tensor), P(Tensor), ctypes.c_void_p, P(Tensor)]
+            L.exl3_epx_create.restype = Verdict
+            L.exl3_epx_create.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p),
+                                          ctypes.c_void_p]
+            L.exl3_epx_connect.restype = Verdict
+            L.exl3_epx_connect.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+            L.exl3_epx_destroy.restype = None
+            L.exl3_epx_destroy.argtypes = [ctypes.c_void_p]
+            L.exl3_epx_dispatch.restype = Verdict
+            L.exl3_epx_dispatch.argtypes = [ctypes.c_void_p, P(Tensor), P(Tensor), ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_void_p, P(Tensor)]
+            L.exl3_epx_receive.restype = Verdict
+            L.exl3_epx_receive.argtypes = [ctypes.c_void_p, ctypes.c_void_p, P(Tensor), P(Tensor), P(Tensor)]
+            L.exl3_epx_return.restype = Verdict
+            L.exl3_epx_return.argtypes = [ctypes.c_void_p, P(Tensor), ctypes.c_void_p]
+            L.exl3_epx_combine.restype = Verdict
+            L.exl3_epx_combine.argtypes = [ctypes.c_void_p, P(Tensor), P(Tensor), ctypes.c_void_p, P(Tensor)]
             L.exl3_matmul_timed.restype = Verdict
             L.exl3_matmul_timed.argtypes = [P(Weight), P(Tensor), ctypes.c_uint32, ctypes.c_void_p, P(Tensor),
                                             ctypes.POINTER(ctypes.c_void_p)]

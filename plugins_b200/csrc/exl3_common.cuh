@@ -25,6 +25,7 @@ enum : uint32_t {
   kErrBadShape = 1u << 1,      // a launch saw a shape its host validation should have refused
   kErrEpOverflow = 1u << 2,    // an expert-parallel dispatch had more rows for one peer than its capacity
   kErrTpTimeout = 1u << 3,     // a column-parallel gather gave up waiting for a peer's columns
+  kErrEpTimeout = 1u << 4,     // a peer expert-parallel exchange gave up waiting for a peer's rows
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -188,6 +188,62 @@ class CudaExpertOps:
         Q.ep_combine(back, back_slot, scores, None, out)
 
 
+class PeerExpertExchange:
+    """The two all-to-alls of the expert-parallel step over NVLink peer memory (exl3_epx_*): the dispatch writes each
+    token row straight into its owner's receive region and the owners write their outputs straight back, each phase
+    published with one system-scope release and awaited with a bounded wait.  One per process (one GPU per rank).
+    """
+
+    def __init__(self, rank: int, world: int, cap: int, hidden: int, dtype=torch.float16, device=None, group=None):
+        import ctypes
+        from . import _lib as L
+        self._L, self._ct = L, ctypes
+        self.rank, self.world, self.cap, self.hidden = rank, world, cap, hidden
+        dev = torch.cuda.current_device() if device is None else torch.device(device).index
+        handle = (ctypes.c_uint8 * 64)()
+        ptr = ctypes.c_void_p()
+        L.check(L.lib().exl3_epx_create(dev, world, rank, cap, hidden, Q._TORCH_DT[dtype], ctypes.byref(ptr), handle))
+        self._ptr = ptr
+        mine = bytes(handle)
+        if world > 1:
+            every = [None] * world
+            dist.all_gather_object(every, mine, group=group)
+        else:
+            every = [mine]
+        buf = (ctypes.c_uint8 * (64 * world)).from_buffer_copy(b"".join(every))
+        L.check(L.lib().exl3_epx_connect(self._ptr, buf))
+
+    def dispatch(self, x, inds, experts: int, shared: bool, back_slot, stream=None):
+        self._L.check(self._L.lib().exl3_epx_dispatch(self._ptr, self._ct.byref(Q._tensor(x)),
+                                                      self._ct.byref(Q._tensor(inds)), int(experts), int(bool(shared)),
+                                                      Q._stream(stream), self._ct.byref(Q._tensor(back_slot))))
+
+    def receive(self, xbuf, inds, scores, stream=None):
+        ct = self._ct
+        self._L.check(self._L.lib().exl3_epx_receive(self._ptr, Q._stream(stream), ct.byref(Q._tensor(xbuf)),
+                                                     ct.byref(Q._tensor(inds)), ct.byref(Q._tensor(scores))))
+
+    def give_back(self, ys, stream=None):
+        self._L.check(self._L.lib().exl3_epx_return(self._ptr, self._ct.byref(Q._tensor(ys)), Q._stream(stream)))
+
+    def combine(self, back_slot, scores, out, stream=None):
+        ct = self._ct
+        self._L.check(self._L.lib().exl3_epx_combine(self._ptr, ct.byref(Q._tensor(back_slot)),
+                                                     ct.byref(Q._tensor(scores)), Q._stream(stream),
+                                                     ct.byref(Q._tensor(out))))
+
+    def close(self):
+        if self._ptr:
+            self._L.lib().exl3_epx_destroy(self._ptr)
+            self._ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class ExpertParallelSwiglu:
     """Routed SwiGLU experts split over the ranks.
 
@@ -197,10 +253,16 @@ class ExpertParallelSwiglu:
     sum_k scores * expert(x) over the routed experts, plus the shared expert.  inds / scores are [T, K]; with a shared
     expert they may also be [T, K + 1] with the last column already the shared expert (id E, score 1).  A shared slot
     stays on the token's own rank and runs in the same swiglu call as the routed slots.
+
+    ``exchange="nccl"`` moves the rows with two equal-split all_to_all_single calls (any backend, any ``ops``);
+    ``exchange="peer"`` with this library's peer-memory kernels (:class:`PeerExpertExchange`, GPUs only).
     """
 
     def __init__(self, gate, up, down, experts: int, tokens: int, topk: int, hidden: int, rank: int, world: int,
-                 dtype=torch.float16, device=None, group=None, shared: bool = False, limit: int = 0, ops=None):
+                 dtype=torch.float16, device=None, group=None, shared: bool = False, limit: int = 0, ops=None,
+                 exchange: str = "nccl"):
+        if exchange not in ("nccl", "peer"):
+            raise ValueError("exchange is 'nccl' or 'peer'")
         self.gate, self.up, self.down, self.shared = gate, up, down, bool(shared)
         self.experts, self.tokens, self.topk, self.hidden = experts, tokens, topk, hidden
         self.rank, self.world, self.group, self.limit = rank, world, group, limit
@@ -216,6 +278,9 @@ class ExpertParallelSwiglu:
         self.r_scores = torch.empty((world, self.cap + 1, 1), dtype=torch.float32, device=dev)
         k = topk + (1 if self.shared else 0)
         self.back_slot = torch.empty((tokens, k), dtype=torch.int32, device=dev)
+        self.peer = None
+        if exchange == "peer":
+            self.peer = PeerExpertExchange(rank, world, self.cap, hidden, dtype=dtype, device=dev, group=group)
         if self.shared:  # the [T, K + 1] slot lists when the caller passes [T, K]
             self.ext_inds = torch.full((tokens, k), experts, dtype=torch.int32, device=dev)
             self.ext_scores = torch.ones((tokens, k), dtype=torch.float32, device=dev)
@@ -234,13 +299,21 @@ class ExpertParallelSwiglu:
             self.ext_inds[:, :self.topk].copy_(inds)
             self.ext_scores[:, :self.topk].copy_(scores)
             inds, scores = self.ext_inds, self.ext_scores
+        if out is None:
+            out = torch.empty_like(x)
         ops = self.ops
+        if self.peer is not None:
+            pe = self.peer
+            pe.dispatch(x, inds, self.experts, self.shared, self.back_slot)
+            pe.receive(self.recv, self.r_inds, self.r_scores)
+            ops.swiglu(self.gate, self.up, self.down, self.recv, self.r_inds, self.r_scores, self.ys, self.limit)
+            pe.give_back(self.ys)
+            pe.combine(self.back_slot, scores, out)
+            return out
         ops.dispatch(x, inds, self.experts, self.world, self.rank, self.shared, self.send, self.back_slot)
         self._all_to_all(self.recv, self.send)
         ops.unpack(self.recv, self.r_inds, self.r_scores)
         ops.swiglu(self.gate, self.up, self.down, self.recv, self.r_inds, self.r_scores, self.ys, self.limit)
         self._all_to_all(self.back, self.ys)
-        if out is None:
-            out = torch.empty_like(x)
         ops.combine(self.back, self.back_slot, scores, out)
         return out

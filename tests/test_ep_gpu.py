@@ -1,6 +1,7 @@
 """Expert parallelism on the GPU: exl3_ep_dispatch / exl3_ep_unpack / exl3_ep_combine against their host restatement
-(tests/sharding_cpu_ops.py), the expert-parallel driver against the single-GPU swiglu and the f32 truth, and -- when
-the box has two GPUs -- the driver over NCCL on two ranks.
+(tests/sharding_cpu_ops.py), the expert-parallel driver against the single-GPU swiglu and the f32 truth, its
+peer-memory exchange (exl3_epx_*) against the all-to-all one, and -- when the box has two GPUs -- the driver on two
+ranks over NCCL and over peer memory, with a rank that stops taking steps.
 """
 import datetime
 import os
@@ -148,13 +149,57 @@ def test_expert_parallel_on_one_rank_matches_swiglu_and_truth(Q, oracle):
     assert _rel(_np(got.float()), want) < REL_L2_BAR
 
 
+def test_peer_exchange_on_one_rank_matches_the_all_to_all_and_replays(Q):
+    """world 1: the peer exchange's kernels (dispatch into the receive region, receive copy, return, combine) give the
+    same bits as the all-to-all path; a captured step replayed on new inputs alternates the two copies of the
+    regions and stays equal."""
+    from plugins_b200 import encoder as E
+    from plugins_b200 import sharding as S
+    experts, hidden, inter, n, tokens, topk = 8, 256, 256, 48, 10, 3
+    raw = _banks(E, experts + 1, hidden, inter, n, 70)  # 8 routed experts and the shared one last
+    banks = [Q.weight_from_tensors(*b) for b in raw]
+    kw = dict(experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=0, world=1, shared=True)
+    a2a = S.ExpertParallelSwiglu(*banks, **kw)
+    peer = S.ExpertParallelSwiglu(*banks, exchange="peer", **kw)
+    x = torch.empty((tokens, hidden), device="cuda", dtype=torch.float16)
+    inds = torch.empty((tokens, topk), device="cuda", dtype=torch.int32)
+    sc = torch.empty((tokens, topk), device="cuda")
+    out = torch.empty((tokens, hidden), device="cuda", dtype=torch.float16)
+
+    def draw(seed):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        x.copy_(torch.randn((tokens, hidden), device="cuda", generator=g).half())
+        i, s_ = _routing(tokens, topk, experts, seed)
+        i[1, 2] = -1  # an absent slot
+        inds.copy_(i)
+        sc.copy_(s_)
+
+    for seed in (1, 2, 3):
+        draw(seed)
+        assert torch.equal(peer.forward(x, inds, sc), a2a.forward(x, inds, sc))
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(st), torch.cuda.graph(graph, stream=st):
+        peer.forward(x, inds, sc, out=out)
+    torch.cuda.current_stream().wait_stream(st)
+    for seed in (4, 5, 6, 7):
+        draw(seed)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, a2a.forward(x, inds, sc)), seed
+    del graph
+    assert Q.device_error(0) == 0
+    peer.peer.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _ep_two_gpu_rank(rank, world, port):
+def _ep_two_gpu_rank(rank, world, port, exchange="nccl"):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -177,19 +222,38 @@ def _ep_two_gpu_rank(rank, world, port):
         inds_all, sc_all = inds_all.to(dev), sc_all.to(dev)
         sl = slice(rank * tokens, (rank + 1) * tokens)
         ep = S.ExpertParallelSwiglu(*local, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=rank,
-                                    world=world, device=dev)
-        got = ep.forward(x_all[sl].contiguous(), inds_all[sl].contiguous(), sc_all[sl].contiguous())
+                                    world=world, device=dev, exchange=exchange)
         full = [Q.weight_from_tensors(*b) for b in raw]
         want = Q.swiglu(*full, x_all[sl].contiguous().view(1, tokens, hidden),
                         inds_all[sl].contiguous().view(1, tokens, topk), sc_all[sl].contiguous().view(1, tokens, topk))
-        rel = float(((got.float() - want.view(tokens, hidden).float()).norm() / want.float().norm()).item())
-        assert rel < 1e-3, rel
+        for _ in range(3):  # (the peer exchange alternates its two copies of the regions)
+            got = ep.forward(x_all[sl].contiguous(), inds_all[sl].contiguous(), sc_all[sl].contiguous())
+            rel = float(((got.float() - want.view(tokens, hidden).float()).norm() / want.float().norm()).item())
+            assert rel < 1e-3, rel
+        torch.cuda.synchronize()
+        assert Q.device_error(rank) == 0
+        if exchange == "peer":
+            # a rank that stops taking steps (between steps: none of its kernels in flight): the other's receive and
+            # combine wait for flags nothing sets, give up after about a second each with EXL3_ERR_EP_TIMEOUT, and
+            # its context runs on
+            from plugins_b200 import _lib as L
+            dist.barrier()
+            if rank == 0:
+                ep.forward(x_all[sl].contiguous(), inds_all[sl].contiguous(), sc_all[sl].contiguous())
+                torch.cuda.synchronize()
+                assert Q.device_error(0, clear=True) & L.ERR_EP_TIMEOUT
+                assert torch.isfinite(Q.swiglu(*full, x_all[sl].contiguous().view(1, tokens, hidden),
+                                               inds_all[sl].contiguous().view(1, tokens, topk),
+                                               sc_all[sl].contiguous().view(1, tokens, topk)).float()).all()
+            dist.barrier()  # rank 1 keeps its regions mapped until rank 0's kernels are done
+            ep.peer.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_expert_parallel_over_nccl_on_two_gpus(Q):
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_expert_parallel_on_two_gpus(Q, exchange):
     import torch.multiprocessing as mp
-    mp.spawn(_ep_two_gpu_rank, args=(2, _free_port()), nprocs=2)
+    mp.spawn(_ep_two_gpu_rank, args=(2, _free_port(), exchange), nprocs=2)
