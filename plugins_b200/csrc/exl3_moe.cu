@@ -17,9 +17,15 @@
 //                  128-wide input block is exactly this column block), writing the down GEMV's B fragments;
 //   4. down     -- the same GEMV over (chunk, 128-column block of the hidden size), finishing to f32 per slot;
 //   5. combine  -- y_r = sum_k score * d in k order, in x's dtype.
-// No unit splits K, so there are no partials and the result does not depend on the grid.
+// Work split: whole units round-robin over the persistent grid while every CTA gets one (neighbouring CTAs stream
+// the same expert's k slabs together), then the remaining units' k slabs, laid end to end, cut into one equal run per
+// CTA (stream-K: a multiple of four slabs, at least kMinRun), so every CTA streams the same bytes however few experts
+// a call touches.  A unit that two or more runs share is finished by the run that completes it last (a per-unit
+// counter): it adds the runs' partial sums in run order and applies the epilogue.  The order of every sum is fixed by the call's routing and the
+// grid, never by timing, so results are reproducible.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -37,6 +43,7 @@ constexpr int kChunkRows = 8;      // slots per chunk: the MMA's N
 constexpr int kWarpsM = 4;
 constexpr int kStagesM = 4;
 constexpr int kRedStrideM = 132;
+constexpr int kMinRun = 32;         // slabs: the shortest run a CTA takes (eight per warp)
 
 struct MoeParams {
   // banks: trellis [E][in/16][out/16][n], suh [E][in], svh [E][out]
@@ -44,6 +51,7 @@ struct MoeParams {
   const uint16_t *u_tr, *u_suh, *u_svh;
   const uint16_t *d_tr, *d_suh, *d_svh;
   int32_t experts, hidden, inter;
+  int32_t max_cb;     // column blocks the unit_done array holds per chunk
   const void* x;      // [rows][hidden]
   int32_t x_dtype;
   const void* inds;   // [rows][topk]
@@ -64,6 +72,8 @@ struct MoeParams {
   uint8_t* xu;         // [chunk][hidden/16][256 B] up-prepared rows
   uint8_t* hp;         // [chunk][inter/16][256 B] down-prepared rows
   float* dout;         // [kMaxSlots][hidden] down outputs per slot (position in `order`)
+  float* part;         // [grid][2 runs' ends][2 weights][8][128] partial sums of units a run shares with another
+  int32_t* unit_done;  // [2 launches][kMaxSlots * max CB] runs finished per unit (each reset by its unit's last run)
 };
 
 __device__ __forceinline__ int slot_expert(const MoeParams& p, int slot) {
@@ -186,6 +196,7 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
   const uint8_t* xa = PAIR ? p.xg : p.hp;
   const uint8_t* xb = p.xu;
 
+  __shared__ int s_last;
   pdl_launch_dependents();
   pdl_wait();  // the chunk table and the prepared inputs come from the previous launches
   const int units = *p.nchunks * CB;
@@ -194,8 +205,32 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
   ImmaIndicator ind;
   ind.init(lane);
   const uint32_t g = lane >> 2, q = lane & 3u;
+  // whole units round-robin while every CTA gets one (dp of them), then this CTA's run [r0, r1) of the remaining
+  // units' slabs laid end to end
+  const int G = static_cast<int>(gridDim.x);
+  const int dp = units / G * G;
+  const int64_t work = static_cast<int64_t>(units - dp) * KT;
+  int64_t run = (work + G - 1) / G;
+  run = (run < kMinRun ? kMinRun : run + 3) & ~int64_t{3};
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * run;
+  const int64_t r1 = r0 + run < work ? r0 + run : work;
+  int32_t* done = p.unit_done + (PAIR ? 0 : kMaxSlots * static_cast<int64_t>(p.max_cb));
 
-  for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+  int next = static_cast<int>(blockIdx.x);
+  for (int64_t at = r0;;) {
+    int unit, su = 0, k0 = 0, k1 = KT;
+    if (next < dp) {
+      unit = next;
+      next += G;
+    } else if (at < r1) {
+      su = static_cast<int>(at / KT);
+      k0 = static_cast<int>(at - static_cast<int64_t>(su) * KT);
+      k1 = static_cast<int>(r1 - at < KT - k0 ? k0 + (r1 - at) : KT);
+      at += k1 - k0;
+      unit = dp + su;
+    } else {
+      break;
+    }
     const int chunk = unit / CB, cb = unit % CB;
     const int e = p.chunk_e[chunk], s0 = p.chunk_s[chunk], nrow = p.chunk_n[chunk];
     const uint8_t* wa = tra + e * wstride + static_cast<size_t>(cb) * 8u * kTileBytes;
@@ -203,10 +238,12 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
     const uint8_t* xca = xa + static_cast<size_t>(chunk) * KT * 256;
     const uint8_t* xcb = xb + static_cast<size_t>(chunk) * KT * 256;
     const size_t rowstride = static_cast<size_t>(CB) * 8u * kTileBytes;  // bytes between k slabs
-    const uint32_t mine = (static_cast<uint32_t>(KT) > warp) ? (KT - warp + kWarpsM - 1) / kWarpsM : 0u;
+    // this warp's slabs of the run: k0 + warp, k0 + warp + 4, ... (k0 and k1 are multiples of four)
+    const uint32_t nk = static_cast<uint32_t>(k1 - k0);
+    const uint32_t mine = nk > warp ? (nk - warp + kWarpsM - 1) / kWarpsM : 0u;
     auto issue = [&](uint32_t i) {
       if (i >= mine) return;
-      const uint32_t t = warp + kWarpsM * i;
+      const uint32_t t = static_cast<uint32_t>(k0) + warp + kWarpsM * i;
       uint8_t* dst = ring + (i % kStagesM) * kSlab;
 #pragma unroll
       for (uint32_t c = lane; c < kW / 16u; c += 32u) cp16(dst + c * 16u, wa + t * rowstride + c * 16u);
@@ -264,12 +301,40 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
       }
     }
     __syncthreads();
-    for (int idx = tid; idx < (PAIR ? 2 : 1) * 8 * 128; idx += kWarpsM * 32) {
+    const bool whole = k0 == 0 && k1 == KT;
+    const int64_t u0 = static_cast<int64_t>(su) * KT;  // the unit's first slab in the runs' numbering
+    constexpr int kPart = (PAIR ? 2 : 1) * 8 * 128;
+    for (int idx = tid; idx < kPart; idx += kWarpsM * 32) {
       const int w2 = idx / 1024, row = (idx / 128) % 8, col = idx % 128;
       float v = 0.0f;
 #pragma unroll
       for (int w3 = 0; w3 < kWarpsM; ++w3) v += red[((w2 * kWarpsM + w3) * 8 + row) * kRedStrideM + col];
-      red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
+      if (whole) red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
+      else __stcg(p.part + (static_cast<size_t>(blockIdx.x) * 2 + (r0 >= u0 ? 0 : 1)) * 2048 + idx, v);
+    }
+    if (!whole) {
+      // a shared unit: runs first .. last of the grid cover it; the one that completes it adds the partials in run
+      // order (run c keeps its partial of the unit its run starts in at end 0, of the unit it ends in at end 1)
+      const int first = static_cast<int>(u0 / run), last = static_cast<int>((u0 + KT - 1) / run);
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) {
+        const int prior = atomicAdd(done + unit, 1);
+        s_last = prior == last - first;
+        if (s_last) done[unit] = 0;  // ready for the next call
+      }
+      __syncthreads();
+      if (!s_last) continue;
+      __threadfence();
+      for (int idx = tid; idx < kPart; idx += kWarpsM * 32) {
+        const int w2 = idx / 1024, row = (idx / 128) % 8, col = idx % 128;
+        float v = 0.0f;
+        for (int c = first; c <= last; ++c) {
+          const int end = static_cast<int64_t>(c) * run >= u0 ? 0 : 1;
+          v += __ldcg(p.part + (static_cast<size_t>(c) * 2 + end) * 2048 + idx);
+        }
+        red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
+      }
     }
     __syncthreads();
     // epilogue: one warp per slot row
@@ -368,29 +433,55 @@ constexpr int kMaxDev = 64;
 std::mutex g_moe_mu;
 MoeScratch g_moe[kMaxDev];
 
-size_t scratch_bytes(int hidden, int inter) {
+constexpr int kMaxCtasPerSm = 4;
+
+// The fixed part of the workspace (its offsets depend only on the reserved width and the SM count, so the per-unit
+// counters, zeroed once at allocation and reset by each unit's last run, stay in place from call to call): the
+// route's ints, unit_done, the runs' partials.  The per-call arrays follow.
+size_t fixed_bytes(int width, int sms) {
   const size_t ints = 4 * kMaxSlots + 64;
-  const size_t xs = 2 * static_cast<size_t>(kMaxSlots) * (hidden / 16) * 256;
-  const size_t hs = static_cast<size_t>(kMaxSlots) * (inter / 16) * 256;
-  const size_t ds = static_cast<size_t>(kMaxSlots) * hidden * 4;
-  return ints * 4 + xs + hs + ds + 4 * 256;
+  const size_t done = 2 * static_cast<size_t>(kMaxSlots) * (width / 128);
+  const size_t part = static_cast<size_t>(sms) * kMaxCtasPerSm * 2 * 2048;
+  return (ints + done + part) * 4;
+}
+
+size_t scratch_bytes(int width, int sms) {
+  const size_t xs = 2 * static_cast<size_t>(kMaxSlots) * (width / 16) * 256;
+  const size_t hs = static_cast<size_t>(kMaxSlots) * (width / 16) * 256;
+  const size_t ds = static_cast<size_t>(kMaxSlots) * width * 4;
+  return fixed_bytes(width, sms) + xs + hs + ds + 4 * 256;
 }
 
 exl3_verdict refuse_m(int32_t code, const char* why) { return {code, why}; }
 
+// The most CTAs per SM the grouped GEMV's persistent grid may take (it takes what fits, up to this): kMaxCtasPerSm,
+// or EXL3_MOE_CTAS (1..kMaxCtasPerSm) for measurements.
+int moe_ctas_per_sm() {
+  static const int v = [] {
+    const char* e = getenv("EXL3_MOE_CTAS");
+    const int n = e ? atoi(e) : kMaxCtasPerSm;
+    return n >= 1 && n <= kMaxCtasPerSm ? n : kMaxCtasPerSm;
+  }();
+  return v;
+}
+
 template <int K, bool PAIR>
-cudaError_t launch_moe_gemv(const MoeParams& p, int grid, cudaStream_t st) {
+cudaError_t launch_moe_gemv(const MoeParams& p, int sms, cudaStream_t st) {
   auto kern = moe_gemv_kernel<K, PAIR>;
   constexpr size_t slab = (PAIR ? 2u : 1u) * (8u * 32u * K + 256u);
   const size_t smem = kWarpsM * kStagesM * slab + (PAIR ? 2 : 1) * kWarpsM * 8 * kRedStrideM * 4;
-  static bool configured = false;
-  if (!configured) {
+  static int per_sm = 0;  // resident CTAs per SM: the persistent grid is exactly one wave
+  if (per_sm == 0) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    configured = true;
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kWarpsM * 32, smem);
+    if (e != cudaSuccess) return e;
+    const int cap = moe_ctas_per_sm();
+    per_sm = occ < 1 ? 1 : (occ > cap ? cap : occ);
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(sms * per_sm);
   cfg.blockDim = dim3(kWarpsM * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -403,14 +494,14 @@ cudaError_t launch_moe_gemv(const MoeParams& p, int grid, cudaStream_t st) {
 }
 
 template <bool PAIR>
-cudaError_t launch_moe_gemv_k(const MoeParams& p, int K, int grid, cudaStream_t st) {
+cudaError_t launch_moe_gemv_k(const MoeParams& p, int K, int sms, cudaStream_t st) {
   switch (K) {
-    case 1: return launch_moe_gemv<1, PAIR>(p, grid, st);
-    case 2: return launch_moe_gemv<2, PAIR>(p, grid, st);
-    case 3: return launch_moe_gemv<3, PAIR>(p, grid, st);
-    case 4: return launch_moe_gemv<4, PAIR>(p, grid, st);
-    case 5: return launch_moe_gemv<5, PAIR>(p, grid, st);
-    case 6: return launch_moe_gemv<6, PAIR>(p, grid, st);
+    case 1: return launch_moe_gemv<1, PAIR>(p, sms, st);
+    case 2: return launch_moe_gemv<2, PAIR>(p, sms, st);
+    case 3: return launch_moe_gemv<3, PAIR>(p, sms, st);
+    case 4: return launch_moe_gemv<4, PAIR>(p, sms, st);
+    case 5: return launch_moe_gemv<5, PAIR>(p, sms, st);
+    case 6: return launch_moe_gemv<6, PAIR>(p, sms, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -447,8 +538,7 @@ exl3_verdict moe_reserve(int device, int in_features, int out_features) {
   const int nh = hidden > s.hidden ? hidden : s.hidden, ni = inter > s.inter ? inter : s.inter;
   // inter may exceed hidden in another model: size both dims for the larger
   const int m = nh > ni ? nh : ni;
-  const size_t need = scratch_bytes(m, m);
-  if (s.ready && need <= s.bytes) return {EXL3_OK, nullptr};
+  if (s.ready && m <= s.hidden) return {EXL3_OK, nullptr};
   int prev = -1;
   cudaGetDevice(&prev);
   cudaSetDevice(device);
@@ -458,7 +548,8 @@ exl3_verdict moe_reserve(int device, int in_features, int out_features) {
     s.base = nullptr;
   }
   cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, device);
-  const bool ok = cudaMalloc(&s.base, need) == cudaSuccess;
+  const size_t need = scratch_bytes(m, s.sms);
+  const bool ok = cudaMalloc(&s.base, need) == cudaSuccess && cudaMemset(s.base, 0, need) == cudaSuccess;
   if (prev >= 0) cudaSetDevice(prev);
   if (!ok) {
     s.ready = false;
@@ -532,13 +623,15 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   p.chunk_n = ints + 3 * kMaxSlots;
   p.nchunks = ints + 4 * kMaxSlots;
   p.bad = ints + 4 * kMaxSlots + 1;
-  uint8_t* cur = sc->base + (4 * kMaxSlots + 64) * 4;
+  p.max_cb = sc->hidden / 128;
+  p.unit_done = ints + 4 * kMaxSlots + 64;
+  p.part = reinterpret_cast<float*>(p.unit_done + 2 * static_cast<size_t>(kMaxSlots) * p.max_cb);
+  uint8_t* cur = sc->base + fixed_bytes(sc->hidden, sc->sms);
   const size_t xs = static_cast<size_t>(kMaxSlots) * (hidden / 16) * 256;
   p.xg = cur; cur += xs;
   p.xu = cur; cur += xs;
   p.hp = cur; cur += static_cast<size_t>(kMaxSlots) * (inter / 16) * 256;
   p.dout = reinterpret_cast<float*>(cur);
-  const int grid_gu = sc->sms * 2, grid_d = sc->sms * 2;
   cudaError_t err = cudaSuccess;
   const int pass_rows = kMaxSlots / topk;  // every expert a pass touches is read once per pass
   for (int64_t r0 = 0; r0 < rows && err == cudaSuccess; r0 += pass_rows) {
@@ -547,8 +640,8 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
     const int S = p.rows * topk;
     err = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
     if (err == cudaSuccess) err = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S), dim3(128), p, st);
-    if (err == cudaSuccess) err = launch_moe_gemv_k<true>(p, gate->n / 16, grid_gu, st);
-    if (err == cudaSuccess) err = launch_moe_gemv_k<false>(p, down->n / 16, grid_d, st);
+    if (err == cudaSuccess) err = launch_moe_gemv_k<true>(p, gate->n / 16, sc->sms, st);
+    if (err == cudaSuccess) err = launch_moe_gemv_k<false>(p, down->n / 16, sc->sms, st);
     if (err == cudaSuccess) err = launch_pdl(moe_combine_kernel, dim3(hidden / 128, p.rows), dim3(128), p, st);
   }
   if (prev >= 0 && prev != dev) cudaSetDevice(prev);
