@@ -8,8 +8,9 @@
 //   y_r = sum_k score[r, k] * down_e(h)                   f32, k order (REDUCE_SOURCE)
 //
 // B200 plan, five launches chained with programmatic dependent launch, rows in passes of 512 / topk:
-//   1. route    -- one CTA: a stable counting sort of the slots by expert (deterministic), cut into chunks of at
-//                  most 8 slots of one expert (the MMA's N), the active chunk list on the device;
+//   1. route    -- one CTA: a stable counting sort of the slots by expert (deterministic; each slot placed by its
+//                  own thread, its position kept for the combine), cut into chunks of at most 8 slots of one expert
+//                  (the MMA's N), the active chunk list on the device;
 //   2. prepare  -- each chunk's rows rotated for gate and for up (suh, 128-wide Hadamard, f16) into B-fragment order;
 //   3. gate|up  -- a persistent decode GEMV over (chunk, 128-column block of the intermediate) units that streams
 //                  the expert's gate and up tiles together (both contiguous per k slab), accumulates both, and in
@@ -44,6 +45,9 @@ constexpr int kWarpsM = 4;
 constexpr int kStagesM = 4;
 constexpr int kRedStrideM = 132;
 constexpr int kMinRun = 32;         // slabs: the shortest run a CTA takes (eight per warp)
+constexpr int kPrepChunks = 128;    // prepare: chunk columns of the grid
+constexpr int kCombineRows = 256;   // combine: row columns of the grid
+constexpr int kIntsM = 5 * kMaxSlots + 64;  // the route's ints: order, chunk_e/s/n, pos, nchunks, bad
 
 struct MoeParams {
   // banks: trellis [E][in/16][out/16][n], suh [E][in], svh [E][out]
@@ -63,6 +67,7 @@ struct MoeParams {
   float limit;
   // scratch
   int32_t* order;      // [kMaxSlots] slot ids sorted by expert (stable)
+  int32_t* pos;        // [kMaxSlots] slot id -> its position in `order` (-1: absent)
   int32_t* chunk_e;    // [kMaxSlots] chunk -> expert
   int32_t* chunk_s;    // [kMaxSlots] chunk -> first position in `order`
   int32_t* chunk_n;    // [kMaxSlots] chunk -> slots
@@ -87,81 +92,120 @@ __device__ __forceinline__ int frag_half(int g, int kk) { return (g * 4 + (kk >>
 
 // ---------------------------------------------------------------- 1. route
 
+// Block-wide exclusive scan of one int per thread (1024 threads); *total receives the sum.
+__device__ int scan_excl_1024(int v, int* s_warp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= d) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = s_warp[lane];
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, d);
+      if (lane >= d) w += y;
+    }
+    s_warp[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  *total = s_warp[31];
+  return x - v + (warp > 0 ? s_warp[warp - 1] : 0);
+}
+
+// One CTA of 1024 threads.  Slot s (< S <= kMaxSlots) of expert e goes to position off[e] + (the slots before s of
+// expert e): a stable counting sort, every slot placed by its own thread.
 __global__ void __launch_bounds__(1024) moe_route_kernel(MoeParams p) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ int s_cnt[1024], s_off[1025];
+  __shared__ int s_cnt[1024], s_off[1024], s_warp[32];
+  __shared__ int16_t s_e[kMaxSlots];
   const int tid = threadIdx.x;
   const int S = p.rows * p.topk;
   const int E = p.experts;
-  for (int e = tid; e < E; e += blockDim.x) s_cnt[e] = 0;
+  s_cnt[tid] = 0;
   if (tid == 0) *p.bad = 0;
   __syncthreads();
   for (int s = tid; s < S; s += blockDim.x) {
     const int e = slot_expert(p, s);
-    if (e < 0 || e >= E) atomicExch(p.bad, 1);
-    else atomicAdd(&s_cnt[e], 1);
+    if (e < 0 || e >= E) {
+      atomicExch(p.bad, 1);
+      s_e[s] = -1;
+    } else {
+      s_e[s] = static_cast<int16_t>(e);
+      atomicAdd(&s_cnt[e], 1);
+    }
   }
   __syncthreads();
-  if (tid == 0) {
-    int acc = 0, nch = 0;
-    for (int e = 0; e < E; ++e) {
-      s_off[e] = acc;
-      for (int c = 0; c < s_cnt[e]; c += kChunkRows) {
-        p.chunk_e[nch] = e;
-        p.chunk_s[nch] = acc + c;
-        p.chunk_n[nch] = min(kChunkRows, s_cnt[e] - c);
-        ++nch;
-      }
-      acc += s_cnt[e];
-    }
-    s_off[E] = acc;
-    *p.nchunks = nch;
-    // stable placement: slots in index order; the tail left by absent slots (expert outside the bank) is marked, so
-    // the combine's search over all S positions never meets an entry from an earlier call
-    for (int s = 0; s < S; ++s) {
-      const int e = slot_expert(p, s);
-      if (e >= 0 && e < E) p.order[s_off[e]++] = s;
-    }
-    for (int i = acc; i < S; ++i) p.order[i] = -1;
+  // slots and chunks before expert `tid` (both sums <= kMaxSlots: packed in one int)
+  const int cnt = tid < E ? s_cnt[tid] : 0;
+  const int nch = (cnt + kChunkRows - 1) / kChunkRows;
+  int total;
+  const int both = scan_excl_1024(cnt | (nch << 16), s_warp, &total);
+  const int off = both & 0xffff, cho = both >> 16;
+  s_off[tid] = off;
+  for (int j = 0; j < nch; ++j) {
+    p.chunk_e[cho + j] = tid;
+    p.chunk_s[cho + j] = off + j * kChunkRows;
+    p.chunk_n[cho + j] = min(kChunkRows, cnt - j * kChunkRows);
   }
+  if (tid == 0) *p.nchunks = total >> 16;
+  __syncthreads();
+  for (int s = tid; s < S; s += blockDim.x) {
+    const int e = s_e[s];
+    int at = -1;
+    if (e >= 0) {
+      at = s_off[e];
+      for (int s2 = 0; s2 < s; ++s2) at += s_e[s2] == e;
+      p.order[at] = s;
+    }
+    p.pos[s] = at;
+  }
+  // positions past the placed slots (absent slots leave them) are marked
+  for (int i = (total & 0xffff) + tid; i < S; i += blockDim.x) p.order[i] = -1;
 }
 
 // ---------------------------------------------------------------- 2. prepare gate / up inputs
 
-// grid: (hidden/128 blocks, kMaxSlots chunks); warp w of the block handles rows w, w+4 of the chunk
+// grid: (hidden/128 blocks, up to kPrepChunks); CTA (b, c) prepares block b of chunks c, c + gridDim.y, ...; warp w
+// handles rows w, w+4 of a chunk
 __global__ void __launch_bounds__(128) moe_prep_kernel(MoeParams p) {
   pdl_wait();
   pdl_launch_dependents();
-  const int chunk = blockIdx.y;
-  if (chunk >= *p.nchunks) return;
-  const int e = p.chunk_e[chunk], s0 = p.chunk_s[chunk], n = p.chunk_n[chunk];
-  const int blk = blockIdx.x;
-  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-  const int KT = p.hidden / 16;
-  for (int g = warp; g < kChunkRows; g += 4) {
-    for (int which = 0; which < 2; ++which) {
-      const uint16_t* suh = (which == 0 ? p.g_suh : p.u_suh) + static_cast<size_t>(e) * p.hidden;
-      uint8_t* dst = (which == 0 ? p.xg : p.xu) + static_cast<size_t>(chunk) * KT * 256;
-      float v[4];
-      if (g < n) {
-        const int row = p.order[s0 + g] / p.topk;
+  const int nchunks = *p.nchunks;
+  for (int chunk = blockIdx.y; chunk < nchunks; chunk += gridDim.y) {
+    const int e = p.chunk_e[chunk], s0 = p.chunk_s[chunk], n = p.chunk_n[chunk];
+    const int blk = blockIdx.x;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const int KT = p.hidden / 16;
+    for (int g = warp; g < kChunkRows; g += 4) {
+      for (int which = 0; which < 2; ++which) {
+        const uint16_t* suh = (which == 0 ? p.g_suh : p.u_suh) + static_cast<size_t>(e) * p.hidden;
+        uint8_t* dst = (which == 0 ? p.xg : p.xu) + static_cast<size_t>(chunk) * KT * 256;
+        float v[4];
+        if (g < n) {
+          const int row = p.order[s0 + g] / p.topk;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const size_t k = static_cast<size_t>(blk) * 128 + lane + 32 * i;
+            v[i] = load_act(p.x, static_cast<size_t>(p.row0 + row) * p.hidden + k, p.x_dtype) * f16_bits_to_float(suh[k]);
+          }
+          fwht128_warp(v, lane);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[i] = 0.0f;
+        }
+        __half* h = reinterpret_cast<__half*>(dst);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const size_t k = static_cast<size_t>(blk) * 128 + lane + 32 * i;
-          v[i] = load_act(p.x, static_cast<size_t>(p.row0 + row) * p.hidden + k, p.x_dtype) * f16_bits_to_float(suh[k]);
+          const int kin = lane + 32 * i;
+          const int t = blk * 8 + (kin >> 4);
+          h[static_cast<size_t>(t) * 128 + frag_half(g, kin & 15)] = __float2half_rn(v[i] * kHadScale);
         }
-        fwht128_warp(v, lane);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = 0.0f;
-      }
-      __half* h = reinterpret_cast<__half*>(dst);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int kin = lane + 32 * i;
-        const int t = blk * 8 + (kin >> 4);
-        h[static_cast<size_t>(t) * 128 + frag_half(g, kin & 15)] = __float2half_rn(v[i] * kHadScale);
       }
     }
   }
@@ -395,29 +439,20 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
 
 // ---------------------------------------------------------------- 5. combine
 
-// grid: (hidden/128, rows); y[r] = sum_k score[r,k] * dout[pos(r,k)], k in order
+// grid: (hidden/128, up to kCombineRows); y[r] = sum_k score[r,k] * dout[pos(r,k)], k in order
 __global__ void __launch_bounds__(128) moe_combine_kernel(MoeParams p) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ int s_pos[kMaxTopK];
-  const int r = blockIdx.y;
-  const int S = p.rows * p.topk;
-  if (threadIdx.x < static_cast<unsigned>(p.topk)) {
-    // position of slot (r, k) in the sorted order
-    const int slot = r * p.topk + threadIdx.x;
-    int pos = -1;
-    for (int i = 0; i < S; ++i)
-      if (p.order[i] == slot) pos = i;
-    s_pos[threadIdx.x] = pos;
-  }
-  __syncthreads();
   const size_t c = static_cast<size_t>(blockIdx.x) * 128 + threadIdx.x;
-  float acc = 0.0f;
-  for (int k = 0; k < p.topk; ++k) {
-    const int pos = s_pos[k];
-    if (pos >= 0) acc += p.scores[static_cast<size_t>(p.row0 + r) * p.topk + k] * p.dout[static_cast<size_t>(pos) * p.hidden + c];
+  for (int r = blockIdx.y; r < p.rows; r += gridDim.y) {
+    float acc = 0.0f;
+    for (int k = 0; k < p.topk; ++k) {
+      const int pos = p.pos[r * p.topk + k];
+      if (pos >= 0)
+        acc += p.scores[static_cast<size_t>(p.row0 + r) * p.topk + k] * p.dout[static_cast<size_t>(pos) * p.hidden + c];
+    }
+    store_act(p.y, static_cast<size_t>(p.row0 + r) * p.hidden + c, acc, p.y_dtype);
   }
-  store_act(p.y, static_cast<size_t>(p.row0 + r) * p.hidden + c, acc, p.y_dtype);
 }
 
 // ---------------------------------------------------------------- host
@@ -439,7 +474,7 @@ constexpr int kMaxCtasPerSm = 4;
 // counters, zeroed once at allocation and reset by each unit's last run, stay in place from call to call): the
 // route's ints, unit_done, the runs' partials.  The per-call arrays follow.
 size_t fixed_bytes(int width, int sms) {
-  const size_t ints = 4 * kMaxSlots + 64;
+  const size_t ints = kIntsM;
   const size_t done = 2 * static_cast<size_t>(kMaxSlots) * (width / 128);
   const size_t part = static_cast<size_t>(sms) * kMaxCtasPerSm * 2 * 2048;
   return (ints + done + part) * 4;
@@ -621,10 +656,11 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   p.chunk_e = ints + kMaxSlots;
   p.chunk_s = ints + 2 * kMaxSlots;
   p.chunk_n = ints + 3 * kMaxSlots;
-  p.nchunks = ints + 4 * kMaxSlots;
-  p.bad = ints + 4 * kMaxSlots + 1;
+  p.pos = ints + 4 * kMaxSlots;
+  p.nchunks = ints + 5 * kMaxSlots;
+  p.bad = ints + 5 * kMaxSlots + 1;
   p.max_cb = sc->hidden / 128;
-  p.unit_done = ints + 4 * kMaxSlots + 64;
+  p.unit_done = ints + kIntsM;
   p.part = reinterpret_cast<float*>(p.unit_done + 2 * static_cast<size_t>(kMaxSlots) * p.max_cb);
   uint8_t* cur = sc->base + fixed_bytes(sc->hidden, sc->sms);
   const size_t xs = static_cast<size_t>(kMaxSlots) * (hidden / 16) * 256;
@@ -639,10 +675,13 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
     p.rows = static_cast<int32_t>(rows - r0 < pass_rows ? rows - r0 : pass_rows);
     const int S = p.rows * topk;
     err = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
-    if (err == cudaSuccess) err = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S), dim3(128), p, st);
+    if (err == cudaSuccess)
+      err = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S < kPrepChunks ? S : kPrepChunks), dim3(128), p, st);
     if (err == cudaSuccess) err = launch_moe_gemv_k<true>(p, gate->n / 16, sc->sms, st);
     if (err == cudaSuccess) err = launch_moe_gemv_k<false>(p, down->n / 16, sc->sms, st);
-    if (err == cudaSuccess) err = launch_pdl(moe_combine_kernel, dim3(hidden / 128, p.rows), dim3(128), p, st);
+    if (err == cudaSuccess)
+      err = launch_pdl(moe_combine_kernel, dim3(hidden / 128, p.rows < kCombineRows ? p.rows : kCombineRows), dim3(128),
+                       p, st);
   }
   if (prev >= 0 && prev != dev) cudaSetDevice(prev);
   if (err != cudaSuccess) return refuse_m(EXL3_FAILED, "exl3_b200: MoE launch failed");
