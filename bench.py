@@ -34,6 +34,13 @@ WORKLOAD = "qwen3-8b-shaped EXL3 decode linear stack (36 layers; q/k/v/o 4 bpw, 
 LINEARS = [("q", HIDDEN, HEADS_Q, 4), ("k", HIDDEN, KV, 4), ("v", HIDDEN, KV, 4), ("o", HIDDEN, HIDDEN, 4),
            ("gate", HIDDEN, INTER, 3), ("up", HIDDEN, INTER, 3), ("down", INTER, HIDDEN, 3)]
 GROUPS = [("qkv", ["q", "k", "v"]), ("o", ["o"]), ("gate_up", ["gate", "up"]), ("down", ["down"])]
+GEMV6_MIN_SLABS = 65536  # the library's kGemv6MinSlabs (plugins_b200/csrc/exl3_internal.h)
+
+
+def gemv_kernels(in_f: int, out_f: int, exchange: bool) -> int:
+    """Kernels one decode-GEMV call launches: the persistent GEMV (prepare + GEMV) from GEMV6_MIN_SLABS slabs of 128
+    columns, else the cluster-split one (one launch; always with the column-parallel exchange)."""
+    return 2 if not exchange and (out_f // 128) * (in_f // 16) >= GEMV6_MIN_SLABS else 1
 
 
 def linear_bytes(i: int, o: int, bits: int, rows: int) -> int:
@@ -531,8 +538,10 @@ def main() -> None:
         with torch.cuda.graph(graph, stream=s):
             step()
         torch.cuda.synchronize()
-        # one decode-GEMV launch per launch group (+ the step begin and the gather when the exchange is fused)
-        launches_per_step = LAYERS * len(GROUPS) + (2 if fused else 0)
+        # the decode-GEMV kernels of each launch group (+ the step begin and the gather when the exchange is fused)
+        lin = {n: (i, o) for n, i, o, _ in LINEARS}
+        group_dims = {g: (lin[names[0]][0], sum(lin[n][1] for n in names) // world) for g, names in GROUPS}
+        launches_per_step = LAYERS * sum(gemv_kernels(i, o, fused) for i, o in group_dims.values()) + (2 if fused else 0)
 
         for _ in range(warmup):
             graph.replay()
@@ -645,7 +654,10 @@ def main() -> None:
             "decode_tok_s": round(args.batch / (r1["ms"] * 1e-3), 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
-                         "kernel": "gate|up decode GEMV (4096 -> 2x12288 @ 3 bpw, one cluster-split launch, gemv5_kernel)",
+                         "kernel": ("gate|up decode GEMV (4096 -> 2x12288 @ 3 bpw): "
+                                    + ("gemv6_prep_kernel + gemv6_kernel (persistent, balanced)"
+                                       if gemv_kernels(HIDDEN, 2 * INTER // world, world > 1 and not args.tp_nccl) == 2
+                                       else "gemv5_kernel (cluster split)")),
                          "bytes_per_launch": gu_bytes, "ms_per_launch": round(r1["dom_ms"], 5),
                          "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
             "roofline_4bpw_qkv": {"achieved": round(qkv_bytes / (r1["qkv_ms"] * 1e-3) / 1e9, 1),

@@ -504,9 +504,11 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
                               ((flags & EXL3_MATMUL_GEMV) == 0 && rows >= d->gemm_min_rows));
   if (gemm) return run_gemm(d, w, x, x_dtype, rows, y, y_dtype, flags, st, ev);
   if (ev && ev[0]) cudaEventRecord(static_cast<cudaEvent_t>(ev[0]), st);
-  // measurement overrides: EXL3_GEMV=4 takes the grid-stride GEMV, EXL3_GEMV_SPLIT the cluster size
+  // measurement overrides: EXL3_GEMV=4 takes the grid-stride GEMV, =5 the cluster-split one, =6 the persistent one;
+  // EXL3_GEMV_SPLIT the cluster size
   const char* gv = getenv("EXL3_GEMV");
-  const bool gemv_v5 = !(gv && atoi(gv) == 4);
+  const int gv_pick = gv ? atoi(gv) : 0;
+  const bool gemv_v5 = gv_pick != 4;
   const char* sp = getenv("EXL3_GEMV_SPLIT");
   const int split = sp ? atoi(sp) : 0;
   const int in_f = w->in_features, out_f = w->out_features, groups = w->groups;
@@ -547,6 +549,14 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
       gp.prepared = (flags & EXL3_MATMUL_PREPARED) ? 1 : 0;
       gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
       const char* why = nullptr;
+      // the persistent GEMV for large launches (every row count of a shape takes the same kernel, so a row's bits do
+      // not depend on the rows batched with it), the cluster-split one below
+      const bool v6 = imma && (gv_pick == 6 || (gv_pick == 0 && exl3::gemv6_prefers(gp)));
+      if (v6 && exl3::gemv6_scratch_bytes(gp, d->sms) <= d->partial_floats * 4) {
+        if (exl3::launch_gemv6(gp, K, d->sms, d->partials, d->counters, st) != cudaSuccess)
+          return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
+        continue;
+      }
       // the cluster-split GEMV where a split fits (every served width), else the grid-stride one with global partials
       if (gemv_v5 && exl3::gemv5_geometry(gp, K, d->sms, rg, split, &why)) {
         if (exl3::launch_gemv5(gp, K, rg, imma, st, true) != cudaSuccess)

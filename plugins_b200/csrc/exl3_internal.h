@@ -70,6 +70,16 @@ int64_t tp_slot_bytes(const exl3_tp* tp);
 bool gemv_geometry(GemvParams& p, int sms, int row_groups, size_t partial_capacity_floats, const char** why);
 cudaError_t launch_gemv(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl);
 
+// The persistent work-balanced decode GEMV (exl3_gemv6.cu), 1..16 rows, no column-parallel exchange: a prepare
+// launch (x rotated into fragment order in `scratch`) and the GEMV (runs' partials in `scratch` after the prepared x;
+// `counters` [out/128] zero between launches, each reset by the run that uses it).  Preferred (measured faster than
+// the cluster split) from kGemv6MinSlabs 16-row slabs of 128 columns per launch; below that its extra prepare launch
+// costs more than its balance gains.
+constexpr int64_t kGemv6MinSlabs = 65536;
+bool gemv6_prefers(const GemvParams& p);
+size_t gemv6_scratch_bytes(const GemvParams& p, int sms);
+cudaError_t launch_gemv6(const GemvParams& p, int K, int sms, void* scratch, uint32_t* counters, cudaStream_t st);
+
 // The cluster-split decode GEMV (exl3_gemv5.cu): one thread-block cluster per 128-column block, its CTAs splitting
 // the input (kc = CTAs per cluster, kr = slabs per CTA), partials summed over distributed shared memory.
 // split_override > 0 forces the CTAs per cluster (measurement); false when no split fits.
