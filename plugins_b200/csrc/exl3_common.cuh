@@ -182,7 +182,7 @@ __device__ __forceinline__ uint32_t mul1_pair_dp4a(uint32_t cw_a, uint32_t cw_b)
 // Two decoded byte sums (f16 bits of 1024 + bytesum in the low halves) -> f16x2 (lo, hi) through the mul1 affine.
 // Both halves are below 2^16, so the packing is exact either way: a byte permute (ALU pipe) or hi * 65536 + lo (an
 // integer multiply-add, FMA pipe).  Which is faster depends on which pipe the rest of the kernel loads: measured on
-// B200, the multiply-add for the deep-ring decode GEMV, the permute elsewhere.
+// B200, the multiply-add for the deep-ring decode GEMVs and the grouped expert GEMV, the permute elsewhere.
 template <bool kPackFma = false>
 __device__ __forceinline__ uint32_t mul1_pack_affine(uint32_t h_lo16, uint32_t h_hi16) {
   uint32_t h;

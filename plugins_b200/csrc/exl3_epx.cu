@@ -6,12 +6,14 @@
 //   back   [2 parities][world][C + 1][D] f32          this rank's slots' expert outputs, block q computed by rank q;
 //   done   [2 phases][world] u32                      per rank q: the last step whose dispatch (phase 0) or return
 //                                                     (phase 1) q has published here;
-//   step   u32                                        this rank's step counter.
-// A step: exl3_epx_dispatch (step += 1; the dispatch -- the layout of exl3_ep_dispatch -- writes block `rank` of
-// every peer's recv directly; one system-scope fence and a release of done[0][rank] on every rank), exl3_epx_receive
+//   step   u32                                        this rank's step counter;
+//   arrive [2 phases] u32                             CTAs of this rank's dispatch / return that have finished.
+// A step: exl3_epx_dispatch (the dispatch -- the layout of exl3_ep_dispatch -- writes block `rank` of every peer's
+// recv directly; each CTA then fences its stores at system scope and arrives; the last CTA to arrive advances the step
+// word and releases done[0][rank] = step on every rank), exl3_epx_receive
 // (waits, bounded, until every rank's done[0] holds the step; copies recv into the caller's fixed buffer and unpacks
 // swiglu's indices), the caller's swiglu on that buffer (f32 out), exl3_epx_return (block q of the output straight
-// into rank q's back, block `rank`; fence and release of done[1][rank] on every rank), exl3_epx_combine (waits for
+// into rank q's back, block `rank`; the last CTA releases done[1][rank] on every rank), exl3_epx_combine (waits for
 // every rank's done[1], then sum_k score * back[slot] in k order).  Parity = step & 1: a rank dispatches step s + 2
 // into a peer only after its step s + 1 combine saw that peer's step s + 1 return, which the peer issued after its
 // step s receive copied recv out, so the two copies of recv and back never race.  The done words only grow; nothing
@@ -36,6 +38,7 @@ struct EpxDev {
   float* back[kMaxRanks];
   uint32_t* done[kMaxRanks];  // [2][world]
   uint32_t* step;
+  uint32_t* arrive;  // [2]
   int32_t world, rank, cap, hidden, esize;
 };
 
@@ -67,18 +70,28 @@ __device__ bool wait_all(const EpxDev& d, int phase, uint32_t step, uint32_t* er
   return s_fail == 0;
 }
 
-__global__ void epx_begin_kernel(const EpxDev* d) {
-  if (threadIdx.x == 0) *d->step += 1u;
-}
-
-// This rank's writes of the phase, published on every rank: a system-scope fence, then done[phase][rank] = step.
-__global__ void epx_publish_kernel(const EpxDev* d, int phase) {
-  if (threadIdx.x != 0) return;
-  const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d->step);
-  asm volatile("fence.sc.sys;" ::: "memory");
-  for (int q = 0; q < d->world; ++q) {
-    uint32_t* f = d->done[q] + phase * d->world + d->rank;
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(step) : "memory");
+// The end of a phase's copies, run by every CTA of the launch: the CTA's stores are fenced at system scope and it
+// arrives; the last CTA to arrive resets the count, stores `step` (dispatch: the step word advances here) and releases
+// done[phase][rank] = step on every rank.
+__device__ void arrive_and_publish(const EpxDev& d, int phase, uint32_t step) {
+  __shared__ int s_last;
+  __syncthreads();  // the CTA's copies are issued
+  if (threadIdx.x == 0) {
+    asm volatile("fence.sc.sys;" ::: "memory");
+    const uint32_t total = gridDim.x * gridDim.y;
+    uint32_t prior;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prior) : "l"(d.arrive + phase) : "memory");
+    s_last = prior == total - 1;
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    d.arrive[phase] = 0u;
+    if (phase == 0) *d.step = step;
+    asm volatile("fence.sc.sys;" ::: "memory");
+    for (int q = 0; q < d.world; ++q) {
+      uint32_t* f = d.done[q] + phase * d.world + d.rank;
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(step) : "memory");
+    }
   }
 }
 
@@ -97,7 +110,7 @@ __global__ void __launch_bounds__(256) epx_dispatch_kernel(const EpxDev* dp, con
   const int dst = blockIdx.x, cap = d.cap;
   const bool head = blockIdx.y == 0;
   const int per = experts / d.world;
-  const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
+  const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step) + 1u;  // this launch's step
   const size_t row_bytes = static_cast<size_t>(d.hidden) * d.esize;
   const size_t block_bytes = static_cast<size_t>(cap + 1) * row_bytes;
   uint8_t* block = d.recv[dst] + (static_cast<size_t>(step & 1u) * d.world + d.rank) * block_bytes;
@@ -145,6 +158,7 @@ __global__ void __launch_bounds__(256) epx_dispatch_kernel(const EpxDev* dp, con
     uint4* out = reinterpret_cast<uint4*>(block + static_cast<size_t>(j) * row_bytes);
     for (size_t w = threadIdx.x; w < words; w += blockDim.x) out[w] = src[w];
   }
+  arrive_and_publish(d, 0, step);
 }
 
 // After every rank's dispatch: recv (this parity) -> the caller's fixed buffer; CTA (q, 0) also unpacks block q's
@@ -186,6 +200,7 @@ __global__ void __launch_bounds__(256) epx_return_kernel(const EpxDev* dp, const
   for (size_t w = static_cast<size_t>(blockIdx.y) * blockDim.x + threadIdx.x; w < words;
        w += static_cast<size_t>(gridDim.y) * blockDim.x)
     reinterpret_cast<float4*>(dst)[w] = reinterpret_cast<const float4*>(src)[w];
+  arrive_and_publish(d, 1, step);
 }
 
 // After every rank's return: out[t] = sum_k score * back[slot(t, k)] in k order (f32), this parity.
@@ -287,6 +302,7 @@ exl3_verdict exl3_epx_connect(exl3_epx* e, const uint8_t* ipc_handles) {
     host.done[q] = e->peer[q] ? reinterpret_cast<uint32_t*>(e->peer[q] + e->recv_bytes + e->back_bytes) : nullptr;
   }
   host.step = reinterpret_cast<uint32_t*>(e->base + e->recv_bytes + e->back_bytes + 256);
+  host.arrive = host.step + 4;
   host.world = e->world, host.rank = e->rank, host.cap = e->cap, host.hidden = e->hidden, host.esize = e->esize;
   ok = ok && cudaMalloc(&e->dev, sizeof host) == cudaSuccess &&
        cudaMemcpy(e->dev, &host, sizeof host, cudaMemcpyHostToDevice) == cudaSuccess;
@@ -321,13 +337,11 @@ exl3_verdict exl3_epx_dispatch(exl3_epx* e, const exl3_tensor* x, const exl3_ten
   DevScope scope(e->device);
   uint32_t* err = exl3::device_error_ptr();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  epx_begin_kernel<<<1, 32, 0, st>>>(e->dev);
   const int copy = e->world >= 148 ? 1 : (148 + e->world - 1) / e->world;
   epx_dispatch_kernel<<<dim3(e->world, copy), 256, 0, st>>>(e->dev, x->data, static_cast<int>(x->shape[0]),
                                                             static_cast<int>(inds->shape[1]), inds->data,
                                                             inds->dtype == EXL3_U32, experts, shared ? 1 : 0,
                                                             static_cast<int32_t*>(back_slot->data), err);
-  epx_publish_kernel<<<1, 32, 0, st>>>(e->dev, 0);
   return (err && cudaGetLastError() == cudaSuccess) ? exl3_verdict{EXL3_OK, nullptr}
                                                     : refuse(EXL3_FAILED, "exl3_epx_dispatch: launch failed");
 }
@@ -361,7 +375,6 @@ exl3_verdict exl3_epx_return(exl3_epx* e, const exl3_tensor* ys, void* stream) {
   DevScope scope(e->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   epx_return_kernel<<<dim3(e->world, 16), 256, 0, st>>>(e->dev, static_cast<const float*>(ys->data));
-  epx_publish_kernel<<<1, 32, 0, st>>>(e->dev, 1);
   return cudaGetLastError() == cudaSuccess ? exl3_verdict{EXL3_OK, nullptr}
                                            : refuse(EXL3_FAILED, "exl3_epx_return: launch failed");
 }
