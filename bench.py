@@ -34,13 +34,32 @@ WORKLOAD = "qwen3-8b-shaped EXL3 decode linear stack (36 layers; q/k/v/o 4 bpw, 
 LINEARS = [("q", HIDDEN, HEADS_Q, 4), ("k", HIDDEN, KV, 4), ("v", HIDDEN, KV, 4), ("o", HIDDEN, HIDDEN, 4),
            ("gate", HIDDEN, INTER, 3), ("up", HIDDEN, INTER, 3), ("down", INTER, HIDDEN, 3)]
 GROUPS = [("qkv", ["q", "k", "v"]), ("o", ["o"]), ("gate_up", ["gate", "up"]), ("down", ["down"])]
-GEMV6_MIN_SLABS = 65536  # the library's kGemv6MinSlabs (plugins_b200/csrc/exl3_internal.h)
+GEMV6_MIN_SLABS, GEMV6_MIN_SLABS_DEEP = 49152, 16384  # the library's kGemv6MinSlabs / kGemv6MinSlabsDeep
 
 
-def gemv_kernels(in_f: int, out_f: int, exchange: bool) -> int:
-    """Kernels one decode-GEMV call launches: the persistent GEMV (prepare + GEMV) from GEMV6_MIN_SLABS slabs of 128
-    columns, else the cluster-split one (one launch; always with the column-parallel exchange)."""
-    return 2 if not exchange and (out_f // 128) * (in_f // 16) >= GEMV6_MIN_SLABS else 1
+def gemv_kernels(in_f: int, out_f: int, exchange: bool, rows: int = 1, sms: int = 148) -> int:
+    """Kernels one decode-GEMV call launches (the selection in plugins_b200/csrc/exl3_abi.cu and exl3_gemv6.cu): the
+    persistent GEMV for large launches -- one kernel when its CTAs rotate the input themselves (1..4 rows, runs of at
+    most 128 slabs), else a prepare launch and the GEMV -- and the cluster-split GEMV otherwise (one launch; always
+    with the column-parallel exchange)."""
+    cb, kt = out_f // 128, in_f // 16
+    slabs = cb * kt
+    if exchange or not (slabs >= GEMV6_MIN_SLABS or (in_f >= 8192 and slabs >= GEMV6_MIN_SLABS_DEEP)):
+        return 1
+    v = sms * 3
+    dp = cb // v * v
+    run = -(-(cb - dp) * kt // v)
+    run = (32 if run < 32 else run + 3) & ~3
+    return 1 if rows <= 4 and dp == 0 and run <= 128 else 2
+
+
+def gemv6_mode(in_f: int, out_f: int, exchange: bool, rows: int = 1) -> int:
+    """0: the cluster-split GEMV; 1: the persistent one rotating its input in-CTA; 2: prepare launch + persistent."""
+    cb, kt = out_f // 128, in_f // 16
+    slabs = cb * kt
+    if exchange or not (slabs >= GEMV6_MIN_SLABS or (in_f >= 8192 and slabs >= GEMV6_MIN_SLABS_DEEP)):
+        return 0
+    return gemv_kernels(in_f, out_f, exchange, rows)
 
 
 def linear_bytes(i: int, o: int, bits: int, rows: int) -> int:
@@ -541,7 +560,8 @@ def main() -> None:
         # the decode-GEMV kernels of each launch group (+ the step begin and the gather when the exchange is fused)
         lin = {n: (i, o) for n, i, o, _ in LINEARS}
         group_dims = {g: (lin[names[0]][0], sum(lin[n][1] for n in names) // world) for g, names in GROUPS}
-        launches_per_step = LAYERS * sum(gemv_kernels(i, o, fused) for i, o in group_dims.values()) + (2 if fused else 0)
+        launches_per_step = (LAYERS * sum(gemv_kernels(i, o, fused, rows) for i, o in group_dims.values())
+                             + (2 if fused else 0))
 
         for _ in range(warmup):
             graph.replay()
@@ -655,9 +675,11 @@ def main() -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                          "kernel": ("gate|up decode GEMV (4096 -> 2x12288 @ 3 bpw): "
-                                    + ("gemv6_prep_kernel + gemv6_kernel (persistent, balanced)"
-                                       if gemv_kernels(HIDDEN, 2 * INTER // world, world > 1 and not args.tp_nccl) == 2
-                                       else "gemv5_kernel (cluster split)")),
+                                    + {0: "gemv5_kernel (cluster split)",
+                                       1: "gemv6_kernel (persistent, balanced; input rotated in-CTA)",
+                                       2: "gemv6_prep_kernel + gemv6_kernel (persistent, balanced)"}[
+                                        gemv6_mode(HIDDEN, 2 * INTER // world, world > 1 and not args.tp_nccl,
+                                                   args.batch)]),
                          "bytes_per_launch": gu_bytes, "ms_per_launch": round(r1["dom_ms"], 5),
                          "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
             "roofline_4bpw_qkv": {"achieved": round(qkv_bytes / (r1["qkv_ms"] * 1e-3) / 1e9, 1),

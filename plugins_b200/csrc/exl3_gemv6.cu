@@ -6,9 +6,12 @@
 //   inner[c] = sum_k xp[k] W_hat[k, c]             f32 accumulation                (main loop)
 //   y = H128(inner) / sqrt(128) * svh              per 128-block of the output     (epilogue)
 //
-// Two launches chained with programmatic dependent launch:
+// Two launches chained with programmatic dependent launch (one, for 1..4 rows split into runs of <= kXiSlabs slabs):
 //   prepare -- x of the launch's rows rotated once, per segment (each segment of a stacked weight has its own suh),
-//              into MMA B-fragment order in global memory (L2-resident: every CTA reads it);
+//              into MMA B-fragment order in global memory (L2-resident: every CTA reads it); with 1..4 rows and short
+//              runs each CTA instead rotates just the 128-input blocks its run covers into shared memory, while its
+//              first weights stream in (the same arithmetic, so the same bits: a launch saves the prepare launch's
+//              ~2 us and spends ~2 % more issue per row);
 //   GEMV    -- a persistent grid over the weight's 128-column blocks ("units", all segments in order).  The work is
 //              cut for V = 3 x SMs virtual CTAs: whole units go round-robin while every virtual CTA gets one, then
 //              the remaining units' 16-row slabs, laid end to end, are cut into one equal run per virtual CTA
@@ -37,6 +40,8 @@ constexpr int kRed6 = 132;        // row stride of the reduction buffer (floats)
 constexpr int kMinRun6 = 32;      // slabs: the shortest run a CTA takes (eight per warp)
 constexpr int kPart6 = 16 * 128;  // floats of one run's partial of a unit (up to 16 rows)
 constexpr int kVirt6 = 3;         // virtual CTAs per SM: the work split
+constexpr int kXiSlabs = 136;     // in-CTA rotation: the most slabs one piece of a run covers (17 input blocks)
+constexpr int kXiRows = 4;        // in-CTA rotation: the most rows
 
 template <int K>
 constexpr int stages6() { return K <= 2 ? 16 : (K <= 4 ? 12 : (K == 5 ? 10 : 8)); }
@@ -85,16 +90,20 @@ __global__ void __launch_bounds__(256 * RG) gemv6_prep_kernel(GemvParams p, __ha
   }
 }
 
-template <int K, int RG, int ST>
+template <int K, int RG, int ST, bool XI>
 __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams p, const __half* __restrict__ xf,
                                                                     float* __restrict__ part, uint32_t* __restrict__ done) {
+  static_assert(!XI || RG == 1, "in-CTA rotation is for one row group");
+  constexpr int kRedRows = XI ? kXiRows : 8 * RG;
   constexpr uint32_t kTileBytes = 32u * K;
   constexpr uint32_t kUnitBytes = 8u * kTileBytes;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_last;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
   uint8_t* ring = smem + warp * (ST * kUnitBytes);
-  float* red = reinterpret_cast<float*>(smem + kW6 * ST * kUnitBytes);  // [kW6][8 RG][kRed6]
+  float* red = reinterpret_cast<float*>(smem + kW6 * ST * kUnitBytes);  // [kW6][kRedRows][kRed6]
+  // XI: the run piece's rotated x, [slab][rows 0..3][16 halfs] (the first half of a slab's fragments)
+  __half* xbuf = reinterpret_cast<__half*>(smem + kW6 * ST * kUnitBytes + kW6 * kRedRows * kRed6 * 4);
   const int KT = p.in_features / 16, CB = p.out_features / 128, rows = p.rows;
   const size_t OT = static_cast<size_t>(p.out_features / 16);
   const size_t slab_stride = OT * kTileBytes;  // bytes from one slab's unit to the next
@@ -172,11 +181,46 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
       pdl_wait();
       waited = true;
     }
-    // x fragments of slab t, row group rg: 32 uint2 at xf + ((s KT + t) RG + rg) 128 halfs
-    const uint2* xs = reinterpret_cast<const uint2*>(xf + (static_cast<size_t>(s) * KT + k0 + warp) * RG * 128) + lane;
+    // x fragments of slab t, row group rg: 32 uint2 at xf + ((s KT + t) RG + rg) 128 halfs; XI: 16 uint2 per slab of
+    // xbuf, lanes of rows past the launch's reading zero
+    const uint2* xs;
+    bool live = true;
+    if constexpr (XI) {
+      const int b0 = k0 >> 3, nb = ((k1 - 1) >> 3) - b0 + 1;
+      for (int j = static_cast<int>(warp); j < nb * rows; j += kW6) {
+        const int blk = b0 + j / rows, r = j % rows, kb = blk * 128;
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          v[i] = load_act(p.x, static_cast<size_t>(p.row0 + r) * p.x_row_stride + kb + lane + 32 * i, p.x_dtype);
+        if (!p.prepared) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            v[i] *= f16_bits_to_float(p.suh[static_cast<size_t>(s) * p.in_features + kb + lane + 32 * i]);
+          fwht128_warp(v, lane);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[i] *= kHadScale;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int kin = static_cast<int>(lane) + 32 * i;
+          const int t = (blk - b0) * 8 + (kin >> 4), kk = kin & 15;
+          xbuf[t * 64 + (r * 4 + (kk >> 2)) * 4 + (kk & 3)] = __float2half_rn(v[i]);
+        }
+      }
+      __syncthreads();
+      xs = reinterpret_cast<const uint2*>(xbuf) + (k0 + static_cast<int>(warp) - 8 * b0) * 16 + lane;
+      live = static_cast<int>(g) < rows;
+    } else {
+      xs = reinterpret_cast<const uint2*>(xf + (static_cast<size_t>(s) * KT + k0 + warp) * RG * 128) + lane;
+    }
+    auto xload = [&](uint32_t i, int r) -> uint2 {
+      if constexpr (XI) return live ? xs[static_cast<size_t>(kW6) * i * 16] : make_uint2(0u, 0u);
+      else return __ldcg(xs + (static_cast<size_t>(kW6) * i * RG + r) * 32);
+    };
     uint2 xn[RG];
 #pragma unroll
-    for (int r = 0; r < RG; ++r) xn[r] = mine > 0 ? __ldcg(xs + r * 32) : make_uint2(0u, 0u);
+    for (int r = 0; r < RG; ++r) xn[r] = mine > 0 ? xload(0, r) : make_uint2(0u, 0u);
 
     float acc[8][RG][4];
 #pragma unroll
@@ -193,7 +237,7 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
 #pragma unroll
       for (int r = 0; r < RG; ++r) {
         xv[r] = xn[r];
-        if (i + 1 < mine) xn[r] = __ldcg(xs + (static_cast<size_t>(kW6) * (i + 1) * RG + r) * 32);
+        if (i + 1 < mine) xn[r] = xload(i + 1, r);
       }
       const uint32_t* tw = reinterpret_cast<const uint32_t*>(ring + (i % ST) * kUnitBytes);
 #pragma unroll
@@ -211,16 +255,18 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
     cp_async_wait6<0>();
 
     // the warps' partials, summed in warp order
-    float* rw = red + warp * 8 * RG * kRed6;
+    float* rw = red + warp * kRedRows * kRed6;
 #pragma unroll
     for (int t = 0; t < 8; ++t)
 #pragma unroll
       for (int r = 0; r < RG; ++r) {
         const int col = 16 * t + static_cast<int>(g), row = 8 * r + 2 * static_cast<int>(q);
-        rw[row * kRed6 + col] = acc[t][r][0];
-        rw[(row + 1) * kRed6 + col] = acc[t][r][1];
-        rw[row * kRed6 + col + 8] = acc[t][r][2];
-        rw[(row + 1) * kRed6 + col + 8] = acc[t][r][3];
+        if (row < kRedRows) {  // (XI: rows 4..7 are zero)
+          rw[row * kRed6 + col] = acc[t][r][0];
+          rw[(row + 1) * kRed6 + col] = acc[t][r][1];
+          rw[row * kRed6 + col + 8] = acc[t][r][2];
+          rw[(row + 1) * kRed6 + col + 8] = acc[t][r][3];
+        }
       }
     __syncthreads();
     const bool whole = k0 == 0 && k1 == KT;
@@ -229,7 +275,7 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
       const int at2 = (idx >> 7) * kRed6 + (idx & 127);
       float v = red[at2];
 #pragma unroll
-      for (int w2 = 1; w2 < kW6; ++w2) v += red[w2 * 8 * RG * kRed6 + at2];
+      for (int w2 = 1; w2 < kW6; ++w2) v += red[w2 * kRedRows * kRed6 + at2];
       if (whole) red[at2] = v;
       else __stcg(part + (static_cast<size_t>(vc) * 2 + (r0 >= u0 ? 0 : 1)) * kPart6 + idx, v);
     }
@@ -278,11 +324,12 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
   }
 }
 
-template <int K, int RG>
+template <int K, int RG, bool XI>
 cudaError_t launch6_t(const GemvParams& p, int sms, __half* xf, float* part, uint32_t* done, cudaStream_t st) {
   constexpr int ST = stages6<K>();
-  auto kern = gemv6_kernel<K, RG, ST>;
-  const size_t smem = static_cast<size_t>(kW6) * ST * 8u * 32u * K + static_cast<size_t>(kW6) * 8 * RG * kRed6 * 4;
+  auto kern = gemv6_kernel<K, RG, ST, XI>;
+  const size_t smem = static_cast<size_t>(kW6) * ST * 8u * 32u * K +
+                      static_cast<size_t>(kW6) * (XI ? kXiRows : 8 * RG) * kRed6 * 4 + (XI ? kXiSlabs * 128 : 0);
   static int per_sm = 0;  // resident CTAs per SM (at most kVirt6): the persistent grid is exactly one wave
   if (per_sm == 0) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -307,17 +354,27 @@ cudaError_t launch6_t(const GemvParams& p, int sms, __half* xf, float* part, uin
   return cudaLaunchKernelEx(&cfg, kern, q, static_cast<const __half*>(xf), part, done);
 }
 
-template <int RG>
+template <int RG, bool XI>
 cudaError_t launch6_k(const GemvParams& p, int K, int sms, __half* xf, float* part, uint32_t* done, cudaStream_t st) {
   switch (K) {
-    case 1: return launch6_t<1, RG>(p, sms, xf, part, done, st);
-    case 2: return launch6_t<2, RG>(p, sms, xf, part, done, st);
-    case 3: return launch6_t<3, RG>(p, sms, xf, part, done, st);
-    case 4: return launch6_t<4, RG>(p, sms, xf, part, done, st);
-    case 5: return launch6_t<5, RG>(p, sms, xf, part, done, st);
-    case 6: return launch6_t<6, RG>(p, sms, xf, part, done, st);
+    case 1: return launch6_t<1, RG, XI>(p, sms, xf, part, done, st);
+    case 2: return launch6_t<2, RG, XI>(p, sms, xf, part, done, st);
+    case 3: return launch6_t<3, RG, XI>(p, sms, xf, part, done, st);
+    case 4: return launch6_t<4, RG, XI>(p, sms, xf, part, done, st);
+    case 5: return launch6_t<5, RG, XI>(p, sms, xf, part, done, st);
+    case 6: return launch6_t<6, RG, XI>(p, sms, xf, part, done, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// The kernel's run length for V virtual CTAs, and whether every unit is split (no whole units round-robin).
+void split6(const GemvParams& p, int sms, int64_t* run, bool* all_runs) {
+  const int V = sms * kVirt6, CB = p.out_features / 128, KT = p.in_features / 16;
+  const int dp = CB / V * V;
+  const int64_t work = static_cast<int64_t>(CB - dp) * KT;
+  int64_t r = (work + V - 1) / V;
+  *run = (r < kMinRun6 ? kMinRun6 : r + 3) & ~int64_t{3};
+  *all_runs = dp == 0;
 }
 
 }  // namespace
@@ -329,7 +386,8 @@ size_t gemv6_scratch_bytes(const GemvParams& p, int sms) {
 }
 
 bool gemv6_prefers(const GemvParams& p) {
-  return static_cast<int64_t>(p.out_features / 128) * (p.in_features / 16) >= kGemv6MinSlabs;
+  const int64_t slabs = static_cast<int64_t>(p.out_features / 128) * (p.in_features / 16);
+  return slabs >= kGemv6MinSlabs || (p.in_features >= 8192 && slabs >= kGemv6MinSlabsDeep);
 }
 
 cudaError_t launch_gemv6(const GemvParams& p, int K, int sms, void* scratch, uint32_t* counters, cudaStream_t st) {
@@ -338,6 +396,11 @@ cudaError_t launch_gemv6(const GemvParams& p, int K, int sms, void* scratch, uin
   __half* xf = static_cast<__half*>(scratch);
   const size_t xf_bytes = static_cast<size_t>(p.nseg) * p.in_features * 32;
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + ((xf_bytes + 255) & ~size_t{255}));
+  int64_t run = 0;
+  bool all_runs = false;
+  split6(p, sms, &run, &all_runs);
+  if (p.rows <= kXiRows && all_runs && run <= kXiSlabs - 8)  // each CTA rotates its runs' inputs itself
+    return launch6_k<1, true>(p, K, sms, xf, part, counters, st);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.in_features / 128), static_cast<unsigned>(p.nseg));
   cfg.blockDim = dim3(256 * rg);
@@ -350,7 +413,8 @@ cudaError_t launch_gemv6(const GemvParams& p, int K, int sms, void* scratch, uin
   cudaError_t e = rg == 1 ? cudaLaunchKernelEx(&cfg, gemv6_prep_kernel<1>, p, xf)
                           : cudaLaunchKernelEx(&cfg, gemv6_prep_kernel<2>, p, xf);
   if (e != cudaSuccess) return e;
-  return rg == 1 ? launch6_k<1>(p, K, sms, xf, part, counters, st) : launch6_k<2>(p, K, sms, xf, part, counters, st);
+  return rg == 1 ? launch6_k<1, false>(p, K, sms, xf, part, counters, st)
+                 : launch6_k<2, false>(p, K, sms, xf, part, counters, st);
 }
 
 }  // namespace exl3

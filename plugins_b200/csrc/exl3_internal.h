@@ -73,9 +73,11 @@ cudaError_t launch_gemv(const GemvParams& p, int K, int row_groups, bool imma, c
 // The persistent work-balanced decode GEMV (exl3_gemv6.cu), 1..16 rows, no column-parallel exchange: a prepare
 // launch (x rotated into fragment order in `scratch`) and the GEMV (runs' partials in `scratch` after the prepared x;
 // `counters` [out/128] zero between launches, each reset by the run that uses it).  Preferred (measured faster than
-// the cluster split) from kGemv6MinSlabs 16-row slabs of 128 columns per launch; below that its extra prepare launch
-// costs more than its balance gains.
-constexpr int64_t kGemv6MinSlabs = 65536;
+// the cluster split) from kGemv6MinSlabs 16-row slabs of 128 columns per launch, and for inputs of 8192 and more from
+// kGemv6MinSlabsDeep (where the cluster split needs 12-16 CTAs per cluster); below that the cluster split's shorter
+// critical path wins.
+constexpr int64_t kGemv6MinSlabs = 49152;
+constexpr int64_t kGemv6MinSlabsDeep = 16384;
 bool gemv6_prefers(const GemvParams& p);
 size_t gemv6_scratch_bytes(const GemvParams& p, int sms);
 cudaError_t launch_gemv6(const GemvParams& p, int K, int sms, void* scratch, uint32_t* counters, cudaStream_t st);
