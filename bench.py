@@ -609,16 +609,28 @@ def main() -> None:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms_e2e = float(t.item())
 
-        # the dominant launch (gate|up, 37.7 MB at 3 bpw) and the 4-bpw q|k|v, timed alone per layer with events
+        # the dominant launch (gate|up, 37.7 MB at 3 bpw) and the 4-bpw q|k|v: the group's 36 launches (one per layer,
+        # distinct weights) captured back to back in one CUDA graph and timed with events on its stream, so the
+        # average is the kernels' own duration in a dense sequence, without host launch gaps
         def time_group(k: str) -> float:
-            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(LAYERS)]
-            for rep in range(2):
+            gs = torch.cuda.Stream(device=device)
+            gs.wait_stream(torch.cuda.current_stream())
+            gg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gg, stream=gs):
                 for l in range(LAYERS):
-                    evs[l][0].record(st)
-                    Q.matmul(layers[l][k], ins[l][k], out=outs[l][k] if world == 1 else outs[l][k])
-                    evs[l][1].record(st)
+                    Q.matmul(layers[l][k], ins[l][k], out=outs[l][k])
+            for _ in range(3):
+                gg.replay()
             torch.cuda.synchronize()
-            return statistics.mean(a.elapsed_time(b) for a, b in evs)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 10
+            a.record(st)
+            for _ in range(reps):
+                gg.replay()
+            b.record(st)
+            torch.cuda.synchronize()
+            gg.reset()
+            return a.elapsed_time(b) / (reps * LAYERS)
 
         dom_ms = time_group("gate_up")
         qkv_ms = time_group("qkv")

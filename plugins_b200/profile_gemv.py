@@ -9,6 +9,7 @@ launch and trellis GB/s.  Under `ncu -k regex:gemv_kernel` it is also the captur
 from __future__ import annotations
 
 import argparse
+import time
 
 import torch
 
@@ -46,9 +47,10 @@ def main() -> None:
         for _ in range(a.loops):
             for w in ws:
                 Q.matmul_ex(w, x, flags, out=y)
-    for _ in range(3):
+    t0 = time.time()
+    while time.time() - t0 < 0.3:  # clocks up from idle before the timed replays
         g.replay()
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     ev[0].record()
     for _ in range(5):
