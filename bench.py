@@ -202,13 +202,17 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
     experts, hidden, inter, topk, total = 256, 4096, 2048, 8, 32
     tokens = total // world
     e0, e1 = S.expert_range(experts, rank, world)
-    local = []
+    local, cols = [], []
     for i, (a, b) in enumerate(((hidden, inter), (hidden, inter), (inter, hidden))):
         tr, suh, svh = E.random_linear(a, b, 48, seed=3 + i, groups=experts, device=device)
         st, ssu, ssv = E.random_linear(a, b, 48, seed=13 + i, groups=1, device=device)
-        # this rank's experts, then the shared expert (its slots stay on the token's rank)
+        # expert parallel: this rank's experts, then the shared expert (its slots stay on the token's rank)
         local.append(Q.weight_from_tensors(torch.cat([tr[e0:e1], st]), torch.cat([suh[e0:e1], ssu]),
                                            torch.cat([svh[e0:e1], ssv])))
+        # column parallel: this rank's output columns of every expert, the shared one last
+        c0, c1 = rank * b // world, (rank + 1) * b // world
+        cols.append(Q.weight_from_tensors(*S.expert_columns(torch.cat([tr, st]), torch.cat([suh, ssu]),
+                                                            torch.cat([svh, ssv]), c0, c1)))
         del tr, suh, svh
     g = torch.Generator(device=device).manual_seed(4)
     logits = torch.randn((total, experts), device=device, generator=g)
@@ -224,8 +228,12 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
     mine = int(((all_ind >= e0) & (all_ind < e1)).sum().item())
 
     def timed(exchange):
-        ep = S.ExpertParallelSwiglu(*local, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=rank,
-                                    world=world, device=device, shared=True, exchange=exchange)
+        if exchange == "columns":
+            ep = S.ColumnParallelExperts(*cols, experts=experts, tokens=tokens, topk=topk, hidden=hidden, inter=inter,
+                                         rank=rank, world=world, device=device, shared=True)
+        else:
+            ep = S.ExpertParallelSwiglu(*local, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=rank,
+                                        world=world, device=device, shared=True, exchange=exchange)
         y = torch.empty_like(x)
         st = torch.cuda.Stream(device=device)
         st.wait_stream(torch.cuda.current_stream())
@@ -253,11 +261,12 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         graph.reset()
-        if ep.peer is not None:
+        closer = ep if exchange == "columns" else ep.peer
+        if closer is not None:
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()  # every rank's kernels are done before any exchange region is unmapped
-            ep.peer.close()
+            closer.close()
         return float(t[0])
 
     b = torch.tensor([float((mine + 1) * per_expert)], device=device, dtype=torch.float64)
@@ -266,6 +275,8 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
     nbytes = float(b[0])
     ms = timed("peer")
     ms_nccl = timed("nccl")
+    ms_cols = timed("columns")
+    cp_bytes = (int(all_ind.numel()) + 1) * per_expert  # every distinct expert once, the shared one once
     gbs = nbytes / (ms * 1e-3) / 1e9
     return {"workload": "config 4 expert-parallel: 256 routed (256/N per GPU) + 1 shared expert, 4096 <-> 2048 "
                         "@ 3 bpw, 32 tokens (32/N per GPU), top-8; dispatch and combine over NVLink peer memory",
@@ -273,7 +284,13 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
             "value": round(gbs, 1), "unit": "GB/s (whole box)", "bytes_per_step": int(nbytes),
             "frac_of_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4),
             "nccl_all_to_all": {"ms_per_step": round(ms_nccl, 4),
-                                "value": round(nbytes / (ms_nccl * 1e-3) / 1e9, 1)}}
+                                "value": round(nbytes / (ms_nccl * 1e-3) / 1e9, 1)},
+            "column_parallel": {"ms_per_step": round(ms_cols, 4), "tokens_per_s": round(total / (ms_cols * 1e-3), 1),
+                                "value": round(cp_bytes / (ms_cols * 1e-3) / 1e9, 1), "unit": "GB/s (whole box)",
+                                "bytes_per_step": int(cp_bytes),
+                                "note": "every rank holds 1/N of every expert's columns and streams 1/N of the "
+                                        "distinct experts' bytes; tokens, the down input and the outputs move over "
+                                        "NVLink peer memory inside one call (exl3_swiglu_cp)"}}
 
 
 def measure_c5(Q, E, torch, peaks: dict, reps: int = 5) -> dict:

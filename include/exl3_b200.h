@@ -242,6 +242,32 @@ exl3_verdict exl3_epx_return(exl3_epx *ep, const exl3_tensor *ys, void *stream);
 exl3_verdict exl3_epx_combine(exl3_epx *ep, const exl3_tensor *back_slot, const exl3_tensor *scores, void *stream,
                               exl3_tensor *out);
 
+/* ------------------------------------------------------------------ column-parallel experts over peer memory
+ *
+ * Beside the seam: routed experts split by columns instead of by experts, so every rank streams exactly 1/W of the
+ * distinct experts' bytes whatever the routing.  Rank r holds, for every expert, gate/up output columns
+ * [r inter/W, (r+1) inter/W) and down output columns [r hidden/W, (r+1) hidden/W) (down's input is the whole
+ * intermediate).  Setup: exl3_cpx_create on every rank (64-byte IPC handle out), exchange the handles,
+ * exl3_cpx_connect.  A call: every rank brings T tokens with K slots (a shared expert is one more bank entry and slot);
+ * the library gathers the tokens, runs route / prepare / gate|up on all W T rows (the gate|up epilogue stores its
+ * blocks of the down input into every rank's buffer over NVLink), waits for every rank's gate|up, runs down over
+ * its output columns and the combine, and returns each token's columns to its owner -- all stream-ordered kernels with
+ * no host synchronisation (a whole call fits in a CUDA graph).  A wait that gives up (one second) sets
+ * EXL3_ERR_EP_TIMEOUT.  Every rank must make the same calls. */
+typedef struct exl3_cpx exl3_cpx;
+
+/* tokens T and slots K per rank per call (W T K <= 512), hidden and inter multiples of 128 W, dtype the activations'. */
+exl3_verdict exl3_cpx_create(int32_t device, int32_t world, int32_t rank, int32_t tokens, int32_t topk, int32_t hidden,
+                             int32_t inter, int32_t dtype, exl3_cpx **out, uint8_t *ipc_handle);
+/* ipc_handles: world * 64 bytes, rank order (this rank's own entry is ignored). */
+exl3_verdict exl3_cpx_connect(exl3_cpx *cp, const uint8_t *ipc_handles);
+void exl3_cpx_destroy(exl3_cpx *cp);
+/* x, out [T, hidden] (the exchange's dtype, 16-byte aligned), inds i32 / scores f32 [T, K] (global expert ids, -1 or
+ * past the bank = absent); gate / up: this rank's slices [E, hidden -> inter/W], down [E, inter -> hidden/W]. */
+exl3_verdict exl3_swiglu_cp(exl3_cpx *cp, const exl3_weight *gate, const exl3_weight *up, const exl3_weight *down,
+                            const exl3_tensor *x, const exl3_tensor *inds, const exl3_tensor *scores,
+                            const exl3_swiglu_opts *opts, void *stream, exl3_tensor *out);
+
 /* ------------------------------------------------------------------ column parallelism with a fused all-gather
  *
  * Beside the seam (the reference is single-device): a linear split by output columns over `world` ranks (one process

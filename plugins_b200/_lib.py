@@ -27,6 +27,7 @@ EXPORTS = (
     "exl3_release", "exl3_matmul", "exl3_moe", "exl3_swiglu", "exl3_matmul_ex", "exl3_matmul_timed",
     "exl3_ep_dispatch", "exl3_ep_unpack", "exl3_ep_combine", "exl3_epx_create", "exl3_epx_connect",
     "exl3_epx_destroy", "exl3_epx_dispatch", "exl3_epx_receive", "exl3_epx_return", "exl3_epx_combine",
+    "exl3_cpx_create", "exl3_cpx_connect", "exl3_cpx_destroy", "exl3_swiglu_cp",
     "exl3_tp_create", "exl3_tp_connect", "exl3_tp_destroy", "exl3_tp_begin", "exl3_matmul_tp", "exl3_tp_gather",
     "exl3_weight_view", "exl3_weight_stack",
     "exl3_decode_dense", "exl3_encode_trellis", "exl3_matmul_noalloc", "exl3_device_error", "exl3_version",
@@ -173,6 +174,15 @@ def lib() -> ctypes.CDLL:
             L.exl3_epx_return.argtypes = [ctypes.c_void_p, P(Tensor), ctypes.c_void_p]
             L.exl3_epx_combine.restype = Verdict
             L.exl3_epx_combine.argtypes = [ctypes.c_void_p, P(Tensor), P(Tensor), ctypes.c_void_p, P(Tensor)]
+            L.exl3_cpx_create.restype = Verdict
+            L.exl3_cpx_create.argtypes = [ctypes.c_int32] * 8 + [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
+            L.exl3_cpx_connect.restype = Verdict
+            L.exl3_cpx_connect.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+            L.exl3_cpx_destroy.restype = None
+            L.exl3_cpx_destroy.argtypes = [ctypes.c_void_p]
+            L.exl3_swiglu_cp.restype = Verdict
+            L.exl3_swiglu_cp.argtypes = [ctypes.c_void_p, P(Weight), P(Weight), P(Weight), P(Tensor), P(Tensor),
+                                         P(Tensor), ctypes.c_void_p, ctypes.c_void_p, P(Tensor)]
             L.exl3_matmul_timed.restype = Verdict
             L.exl3_matmul_timed.argtypes = [P(Weight), P(Tensor), ctypes.c_uint32, ctypes.c_void_p, P(Tensor),
                                             ctypes.POINTER(ctypes.c_void_p)]

@@ -29,6 +29,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <new>
 
 #include "exl3_common.cuh"
 #include "exl3_internal.h"
@@ -55,6 +56,12 @@ struct MoeParams {
   const uint16_t *u_tr, *u_suh, *u_svh;
   const uint16_t *d_tr, *d_suh, *d_svh;
   int32_t experts, hidden, inter;
+  // column-parallel experts (every rank holds a column slice of every expert): inter_full is the down input's width
+  // and inter_off the first column of this rank's gate/up slice in it; hidden_out the down bank's (sliced) output
+  // width.  A single-device call has inter_full = inter, inter_off = 0, hidden_out = hidden.
+  int32_t inter_full, inter_off, hidden_out;
+  uint8_t* hp_dst[8];  // every rank's down-input buffer (same layout as hp) when hp_world > 0
+  int32_t hp_world;
   int32_t max_cb;     // column blocks the unit_done array holds per chunk
   const void* x;      // [rows][hidden]
   int32_t x_dtype;
@@ -231,8 +238,8 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
   uint8_t* ring = smem + warp * (kStagesM * kSlab);
   float* red = reinterpret_cast<float*>(smem + kWarpsM * kStagesM * kSlab);  // [2][W][8][stride]
-  const int in_f = PAIR ? p.hidden : p.inter;
-  const int out_f = PAIR ? p.inter : p.hidden;
+  const int in_f = PAIR ? p.hidden : p.inter_full;
+  const int out_f = PAIR ? p.inter : p.hidden_out;
   const int KT = in_f / 16, CB = out_f / 128;
   const size_t wstride = static_cast<size_t>(in_f / 16) * (out_f / 16) * kTileBytes;  // bytes per expert
   const uint8_t* tra = reinterpret_cast<const uint8_t*>(PAIR ? p.g_tr : p.d_tr);
@@ -331,6 +338,7 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
       cp_commit();
     }
     cp_wait<0>();
+    __half* stage = reinterpret_cast<__half*>(smem);  // warp 0's ring, drained: the down-input block's staging (2 KiB)
     // warps' partials -> shared, summed in warp order
 #pragma unroll
     for (int w2 = 0; w2 < (PAIR ? 2 : 1); ++w2) {
@@ -380,6 +388,8 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
         red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
       }
     }
+    if constexpr (PAIR)  // rows of the chunk beyond its slots stay zero in the down input
+      for (int v = static_cast<int>(tid); v < 128; v += kWarpsM * 32) reinterpret_cast<uint4*>(stage)[v] = make_uint4(0, 0, 0, 0);
     __syncthreads();
     // epilogue: one warp per slot row
     for (int row = static_cast<int>(warp); row < nrow; row += kWarpsM) {
@@ -404,33 +414,37 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
             uv = fminf(fmaxf(uv, -p.limit), p.limit);
           }
           const float sig = 1.0f / (1.0f + __expf(-gv));
-          h[i] = gv * sig * uv * f16_bits_to_float(p.d_suh[static_cast<size_t>(e) * p.inter + c]);
+          h[i] = gv * sig * uv *
+                 f16_bits_to_float(p.d_suh[static_cast<size_t>(e) * p.inter_full + p.inter_off + c]);
         }
         fwht128_warp(h, lane);
-        __half* dst = reinterpret_cast<__half*>(p.hp + static_cast<size_t>(chunk) * (p.inter / 16) * 256);
+        __half* dst = stage;  // this block's 8 slabs of the down input, [8][128 halfs]
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int kin = lane + 32 * i;
-          const int t = cb * 8 + (kin >> 4);
-          dst[static_cast<size_t>(t) * 128 + frag_half(row, kin & 15)] = __float2half_rn(h[i] * kHadScale);
+          dst[(kin >> 4) * 128 + frag_half(row, kin & 15)] = __float2half_rn(h[i] * kHadScale);
         }
       } else {
-        float* dst = p.dout + static_cast<size_t>(s0 + row) * p.hidden;
+        float* dst = p.dout + static_cast<size_t>(s0 + row) * p.hidden_out;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const size_t c = ce + lane + 32 * i;
-          dst[c] = va[i] * kHadScale * f16_bits_to_float(p.d_svh[static_cast<size_t>(e) * p.hidden + c]);
+          dst[c] = va[i] * kHadScale * f16_bits_to_float(p.d_svh[static_cast<size_t>(e) * p.hidden_out + c]);
         }
       }
     }
     if constexpr (PAIR) {
-      // rows of the chunk beyond its slots stay zero in the down GEMV's fragments
-      if (static_cast<int>(warp) == 0 && nrow < kChunkRows) {
-        __half* dst = reinterpret_cast<__half*>(p.hp + static_cast<size_t>(chunk) * (p.inter / 16) * 256);
-        for (int idx = lane; idx < 8 * 16 * kChunkRows; idx += 32) {
-          const int row = idx / 128, kin = idx % 128;
-          if (row >= nrow) dst[static_cast<size_t>(cb * 8 + (kin >> 4)) * 128 + frag_half(row, kin & 15)] = __float2half_rn(0.0f);
-        }
+      // the staged block (rows past the chunk's slots zero) -> the down input of this rank, or of every rank, with
+      // 16-byte stores: slabs (inter_off / 128 + cb) * 8 .. + 7 of the chunk, contiguous
+      __syncthreads();
+      const size_t at = (static_cast<size_t>(chunk) * (p.inter_full / 16) + (p.inter_off / 128 + cb) * 8) * 256;
+      const uint4* src = reinterpret_cast<const uint4*>(stage);
+      if (p.hp_world > 0) {
+        for (int q2 = 0; q2 < p.hp_world; ++q2)
+          for (int v = static_cast<int>(tid); v < 128; v += kWarpsM * 32)
+            reinterpret_cast<uint4*>(p.hp_dst[q2] + at)[v] = src[v];
+      } else {
+        for (int v = static_cast<int>(tid); v < 128; v += kWarpsM * 32) reinterpret_cast<uint4*>(p.hp + at)[v] = src[v];
       }
     }
     __syncthreads();
@@ -445,21 +459,21 @@ __global__ void __launch_bounds__(128) moe_combine_kernel(MoeParams p) {
   pdl_wait();
   pdl_launch_dependents();
   const size_t c = (static_cast<size_t>(blockIdx.x) * 128 + threadIdx.x) * 4;
-  if (c >= static_cast<size_t>(p.hidden)) return;  // (hidden is a multiple of 128: c + 3 < hidden otherwise)
+  if (c >= static_cast<size_t>(p.hidden_out)) return;  // (a multiple of 128: c + 3 < hidden_out otherwise)
   for (int r = blockIdx.y; r < p.rows; r += gridDim.y) {
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int k = 0; k < p.topk; ++k) {
       const int pos = p.pos[r * p.topk + k];
       if (pos >= 0) {
         const float sc = p.scores[static_cast<size_t>(p.row0 + r) * p.topk + k];
-        const float4 d = *reinterpret_cast<const float4*>(p.dout + static_cast<size_t>(pos) * p.hidden + c);
+        const float4 d = *reinterpret_cast<const float4*>(p.dout + static_cast<size_t>(pos) * p.hidden_out + c);
         acc.x += sc * d.x;
         acc.y += sc * d.y;
         acc.z += sc * d.z;
         acc.w += sc * d.w;
       }
     }
-    const size_t at = static_cast<size_t>(p.row0 + r) * p.hidden + c;
+    const size_t at = static_cast<size_t>(p.row0 + r) * p.hidden_out + c;
     store_act(p.y, at, acc.x, p.y_dtype);
     store_act(p.y, at + 1, acc.y, p.y_dtype);
     store_act(p.y, at + 2, acc.z, p.y_dtype);
@@ -659,6 +673,7 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   p.u_tr = up->trellis; p.u_suh = up->suh; p.u_svh = up->svh;
   p.d_tr = down->trellis; p.d_suh = down->suh; p.d_svh = down->svh;
   p.experts = experts; p.hidden = hidden; p.inter = inter;
+  p.inter_full = inter; p.inter_off = 0; p.hidden_out = hidden;
   p.x = x->data; p.x_dtype = x->dtype;
   p.inds = inds->data; p.inds_u32 = inds->dtype == EXL3_U32;
   p.scores = static_cast<const float*>(scores->data);
@@ -700,4 +715,365 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   return {EXL3_OK, nullptr};
 }
 
+// ================================================================ column-parallel experts over NVLink peer memory
+//
+// Every rank holds a column slice of every expert: gate/up output columns [r inter/W, (r+1) inter/W) and down output
+// columns [r hidden/W, (r+1) hidden/W) (down's input is the whole intermediate), so each rank streams exactly 1/W of the
+// distinct experts' bytes whatever the routing.  A call (every rank brings T tokens with K slots each):
+//   in     -- each rank's x, inds, scores rows into every rank's gathered block (rows [rank T, rank T + T)); the last
+//             CTA advances the step word and releases done[0][rank] on every rank;
+//   wait 0 -- every rank's rows are in (bounded);
+//   route, prepare, gate|up GEMV on all W T rows -- the same slot order and chunk table on every rank (deterministic);
+//             the gate|up epilogue stores its blocks of the down input into every rank's down-input buffer;
+//   sync 1 -- this rank's gate|up is complete: release done[1][rank] on every rank, wait for every rank's (bounded);
+//   down GEMV over this rank's output columns (the whole down input is local now), combine -> ycol [W T][hidden/W];
+//   out    -- each owner's T rows of ycol into its output block (columns [rank hidden/W, ...)); release done[2][rank];
+//   final  -- every rank's columns are in (bounded); the T rows to the caller's out.
+// One copy of each buffer suffices: a rank writes a peer's buffers of call s + 1 only after passing a wait of call
+// s + 1 that the peer releases after it finished reading them in call s.  Every wait gives up after one second with
+// EXL3_ERR_EP_TIMEOUT; the done words only grow, so graph replays need nothing reset.
+
+struct CpxDev {
+  uint8_t* buf[8];      // every rank's exchange buffer
+  uint32_t* step;       // this rank's step word
+  uint32_t* arrive;     // [3] CTAs of this rank's in / - / out launches that have finished
+  int32_t world, rank, tokens, topk, hidden, hidden_out, esize;
+  int64_t off_x, off_inds, off_scores, off_hp, off_y, off_done;
+};
+
+namespace {
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_m(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t* cpx_done(const CpxDev& d, int q, int phase) {
+  return reinterpret_cast<uint32_t*>(d.buf[q] + d.off_done) + phase * d.world;
+}
+
+// Threads 0..world-1 of the CTA wait (one second at most) until every rank's done[phase] word holds `step`.
+__device__ void cpx_wait_all(const CpxDev& d, int phase, uint32_t step, uint32_t* err) {
+  __shared__ int s_fail;
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  if (threadIdx.x < static_cast<uint32_t>(d.world)) {
+    const uint32_t* f = cpx_done(d, d.rank, phase) + threadIdx.x;
+    if (static_cast<int32_t>(ld_acquire_sys_m(f) - step) < 0) {
+      const uint64_t t0 = global_timer_ns();
+      while (static_cast<int32_t>(ld_acquire_sys_m(f) - step) < 0) {
+        if (global_timer_ns() - t0 > 1000000000ull) {
+          s_fail = 1;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (s_fail && threadIdx.x == 0) atomicOr(err, kErrEpTimeout);
+}
+
+__device__ void cpx_release(const CpxDev& d, int phase, uint32_t step) {
+  asm volatile("fence.sc.sys;" ::: "memory");
+  for (int q = 0; q < d.world; ++q) {
+    uint32_t* f = cpx_done(d, q, phase) + d.rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(step) : "memory");
+  }
+}
+
+// Every CTA of the launch: its stores fenced at system scope, then it arrives; the last resets the count, (phase 0)
+// advances the step word, and releases done[phase][rank] on every rank.
+__device__ void cpx_arrive_publish(const CpxDev& d, int phase, uint32_t step) {
+  __shared__ int s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    asm volatile("fence.sc.sys;" ::: "memory");
+    uint32_t prior;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prior) : "l"(d.arrive + phase) : "memory");
+    s_last = prior == gridDim.x * gridDim.y - 1;
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    d.arrive[phase] = 0u;
+    if (phase == 0) *d.step = step;
+    cpx_release(d, phase, step);
+  }
+}
+
+__device__ void copy16(uint8_t* dst, const uint8_t* src, size_t bytes, size_t t0, size_t stride) {
+  for (size_t w = t0; w < bytes / 16; w += stride)
+    reinterpret_cast<uint4*>(dst)[w] = reinterpret_cast<const uint4*>(src)[w];
+}
+
+// grid (world, c): this rank's rows into block `rank` of every rank's gathered x / inds / scores
+__global__ void __launch_bounds__(256) cpx_in_kernel(const CpxDev* dp, const uint8_t* __restrict__ x,
+                                                     const int32_t* __restrict__ inds, const float* __restrict__ scores) {
+  const CpxDev& d = *dp;
+  const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step) + 1u;
+  const int q = blockIdx.x;
+  const size_t xrow = static_cast<size_t>(d.hidden) * d.esize;
+  const size_t t0 = static_cast<size_t>(blockIdx.y) * blockDim.x + threadIdx.x, stride = static_cast<size_t>(gridDim.y) * blockDim.x;
+  copy16(d.buf[q] + d.off_x + static_cast<size_t>(d.rank) * d.tokens * xrow, x, d.tokens * xrow, t0, stride);
+  const int n = d.tokens * d.topk;
+  int32_t* qi = reinterpret_cast<int32_t*>(d.buf[q] + d.off_inds) + static_cast<size_t>(d.rank) * n;
+  float* qs = reinterpret_cast<float*>(d.buf[q] + d.off_scores) + static_cast<size_t>(d.rank) * n;
+  for (size_t i = t0; i < static_cast<size_t>(n); i += stride) {
+    qi[i] = inds[i];
+    qs[i] = scores[i];
+  }
+  cpx_arrive_publish(d, 0, step);
+}
+
+__global__ void cpx_wait_kernel(const CpxDev* dp, int phase, uint32_t* err) {
+  const CpxDev& d = *dp;
+  cpx_wait_all(d, phase, *reinterpret_cast<const volatile uint32_t*>(d.step), err);
+}
+
+// After this rank's gate|up (the previous launch, complete): publish it, wait for every rank's.
+__global__ void cpx_sync_kernel(const CpxDev* dp, uint32_t* err) {
+  const CpxDev& d = *dp;
+  const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
+  if (threadIdx.x == 0) cpx_release(d, 1, step);
+  cpx_wait_all(d, 1, step, err);
+}
+
+// grid (world, c): owner q's T rows of ycol [W T][hidden_out] -> its output block, columns [rank hidden_out, ...)
+__global__ void __launch_bounds__(256) cpx_out_kernel(const CpxDev* dp, const uint8_t* __restrict__ ycol) {
+  const CpxDev& d = *dp;
+  const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
+  const int q = blockIdx.x;
+  const size_t seg = static_cast<size_t>(d.hidden_out) * d.esize;  // bytes of one row's column slice
+  const size_t words = seg / 16;
+  for (size_t w = static_cast<size_t>(blockIdx.y) * blockDim.x + threadIdx.x; w < d.tokens * words;
+       w += static_cast<size_t>(gridDim.y) * blockDim.x) {
+    const size_t r = w / words, c = w % words;
+    const uint4* src = reinterpret_cast<const uint4*>(ycol + (static_cast<size_t>(q) * d.tokens + r) * seg);
+    uint4* dst = reinterpret_cast<uint4*>(d.buf[q] + d.off_y + r * d.hidden * d.esize + d.rank * seg);
+    dst[c] = src[c];
+  }
+  cpx_arrive_publish(d, 2, step);
+}
+
+// every rank's columns of this rank's rows are in (bounded), then they go to the caller's out
+__global__ void __launch_bounds__(256) cpx_final_kernel(const CpxDev* dp, uint8_t* __restrict__ out, uint32_t* err) {
+  const CpxDev& d = *dp;
+  cpx_wait_all(d, 2, *reinterpret_cast<const volatile uint32_t*>(d.step), err);
+  const size_t bytes = static_cast<size_t>(d.tokens) * d.hidden * d.esize;
+  copy16(out, d.buf[d.rank] + d.off_y, bytes, static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x,
+         static_cast<size_t>(gridDim.x) * blockDim.x);
+}
+
+}  // namespace
+
 }  // namespace exl3
+
+struct exl3_cpx {
+  int device = -1, world = 0, rank = 0, tokens = 0, topk = 0, hidden = 0, inter = 0, dtype = 0, esize = 2;
+  int chunks = 0;
+  uint8_t* base = nullptr;
+  size_t bytes = 0;
+  int64_t off_ycol = 0;
+  uint8_t* peer[8] = {};
+  exl3::CpxDev host{};
+  exl3::CpxDev* dev = nullptr;
+  bool connected = false;
+};
+
+namespace exl3 {
+
+namespace {
+struct CpxScope {
+  int prev = -1;
+  explicit CpxScope(int d) {
+    cudaGetDevice(&prev);
+    if (prev != d) cudaSetDevice(d);
+    else prev = -1;
+  }
+  ~CpxScope() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+}  // namespace
+
+}  // namespace exl3
+
+extern "C" {
+
+exl3_verdict exl3_cpx_create(int32_t device, int32_t world, int32_t rank, int32_t tokens, int32_t topk, int32_t hidden,
+                             int32_t inter, int32_t dtype, exl3_cpx** out, uint8_t* ipc_handle) {
+  using namespace exl3;
+  if (!out || !ipc_handle) return refuse_m(EXL3_FAILED, "exl3_cpx_create: bad arguments");
+  *out = nullptr;
+  if (world < 1 || world > 8 || rank < 0 || rank >= world) return refuse_m(EXL3_UNSUPPORTED, "exl3_cpx_create: 1..8 ranks");
+  if (tokens < 1 || topk < 1 || topk > kMaxTopK || static_cast<int64_t>(world) * tokens * topk > kMaxSlots)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_cpx_create: every rank's tokens x slots at most 512 in all");
+  if (hidden % (128 * world) != 0 || inter % (128 * world) != 0)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_cpx_create: hidden and intermediate split into 128-column blocks per rank");
+  if (dtype != EXL3_F16 && dtype != EXL3_BF16 && dtype != EXL3_F32) return refuse_m(EXL3_UNSUPPORTED, "exl3_cpx_create: an activation dtype");
+  CpxScope scope(device);
+  exl3_cpx* e = new (std::nothrow) exl3_cpx;
+  if (!e) return refuse_m(EXL3_FAILED, "exl3_cpx_create: out of host memory");
+  e->device = device, e->world = world, e->rank = rank, e->tokens = tokens, e->topk = topk, e->hidden = hidden;
+  e->inter = inter, e->dtype = dtype, e->esize = dtype == EXL3_F32 ? 4 : 2;
+  const int64_t rows = static_cast<int64_t>(world) * tokens;
+  e->chunks = static_cast<int>(rows * topk);  // at most one chunk per slot
+  auto up = [](int64_t v) { return (v + 255) & ~int64_t{255}; };
+  int64_t at = 0;
+  CpxDev& h = e->host;
+  h.off_x = at; at = up(at + rows * hidden * e->esize);
+  h.off_inds = at; at = up(at + rows * topk * 4);
+  h.off_scores = at; at = up(at + rows * topk * 4);
+  h.off_hp = at; at = up(at + static_cast<int64_t>(e->chunks) * (inter / 16) * 256);
+  h.off_y = at; at = up(at + static_cast<int64_t>(tokens) * hidden * e->esize);
+  h.off_done = at; at = up(at + 3 * 8 * 4);
+  const int64_t off_local = at; at = up(at + 64);  // step, arrive[3]
+  e->off_ycol = at; at = up(at + rows * (hidden / world) * e->esize);
+  e->bytes = static_cast<size_t>(at);
+  bool ok = cudaMalloc(&e->base, e->bytes) == cudaSuccess && cudaMemset(e->base, 0, e->bytes) == cudaSuccess;
+  cudaIpcMemHandle_t hd;
+  ok = ok && cudaIpcGetMemHandle(&hd, e->base) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+  if (!ok) {
+    if (e->base) cudaFree(e->base);
+    delete e;
+    return refuse_m(EXL3_TOO_LARGE, "exl3_cpx_create: exchange buffer allocation failed");
+  }
+  memcpy(ipc_handle, &hd, 64);
+  e->peer[rank] = e->base;
+  h.step = reinterpret_cast<uint32_t*>(e->base + off_local);
+  h.arrive = h.step + 4;
+  h.world = world, h.rank = rank, h.tokens = tokens, h.topk = topk, h.hidden = hidden;
+  h.hidden_out = hidden / world, h.esize = e->esize;
+  *out = e;
+  return {EXL3_OK, nullptr};
+}
+
+exl3_verdict exl3_cpx_connect(exl3_cpx* e, const uint8_t* ipc_handles) {
+  using namespace exl3;
+  if (!e || !ipc_handles || e->connected) return refuse_m(EXL3_FAILED, "exl3_cpx_connect: bad arguments");
+  CpxScope scope(e->device);
+  bool ok = true;
+  for (int q = 0; q < e->world && ok; ++q) {
+    if (q == e->rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handles + 64 * q, 64);
+    void* p = nullptr;
+    ok = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    e->peer[q] = static_cast<uint8_t*>(p);
+  }
+  for (int q = 0; q < e->world; ++q) e->host.buf[q] = e->peer[q];
+  ok = ok && cudaMalloc(&e->dev, sizeof(CpxDev)) == cudaSuccess &&
+       cudaMemcpy(e->dev, &e->host, sizeof(CpxDev), cudaMemcpyHostToDevice) == cudaSuccess;
+  if (!ok) return refuse_m(EXL3_FAILED, "exl3_cpx_connect: opening a peer's exchange buffer failed");
+  e->connected = true;
+  return {EXL3_OK, nullptr};
+}
+
+void exl3_cpx_destroy(exl3_cpx* e) {
+  if (!e) return;
+  exl3::CpxScope scope(e->device);
+  cudaDeviceSynchronize();
+  for (int q = 0; q < e->world; ++q)
+    if (q != e->rank && e->peer[q]) cudaIpcCloseMemHandle(e->peer[q]);
+  if (e->dev) cudaFree(e->dev);
+  if (e->base) cudaFree(e->base);
+  delete e;
+}
+
+exl3_verdict exl3_swiglu_cp(exl3_cpx* e, const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down,
+                            const exl3_tensor* x, const exl3_tensor* inds, const exl3_tensor* scores,
+                            const exl3_swiglu_opts* opts, void* stream, exl3_tensor* out) {
+  using namespace exl3;
+  if (!e || !e->connected || !gate || !up || !down || !x || !inds || !scores || !out)
+    return refuse_m(EXL3_FAILED, "exl3_swiglu_cp: bad arguments");
+  if (opts && opts->size != sizeof(exl3_swiglu_opts)) return refuse_m(EXL3_FAILED, "exl3_b200: bad swiglu options");
+  const int limit = opts ? opts->limit : 0;
+  if (limit < 0 || limit > 128) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: InvalidExl3Clamp");
+  const int W = e->world, T = e->tokens, K = e->topk, hidden = e->hidden, inter = e->inter;
+  if (x->ndim != 2 || x->shape[0] != T || x->shape[1] != hidden || x->dtype != e->dtype || out->ndim != 2 ||
+      out->shape[0] != T || out->shape[1] != hidden || out->dtype != e->dtype)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_swiglu_cp: x and out [T, hidden] in the exchange's dtype");
+  if (inds->ndim != 2 || inds->shape[0] != T || inds->shape[1] != K || inds->dtype != EXL3_I32 || scores->ndim != 2 ||
+      scores->shape[0] != T || scores->shape[1] != K || scores->dtype != EXL3_F32)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_swiglu_cp: inds i32 and scores f32 [T, K]");
+  if (reinterpret_cast<uintptr_t>(x->data) % 16 || reinterpret_cast<uintptr_t>(out->data) % 16)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_swiglu_cp: x and out on 16-byte boundaries");
+  const int islice = inter / W, hslice = hidden / W;
+  const int experts = gate->groups;
+  if (!bank_ok(gate, hidden, islice) || !bank_ok(up, hidden, islice) || !bank_ok(down, inter, hslice) ||
+      up->groups != experts || down->groups != experts || experts < 1 || experts > 1024 || gate->n != up->n)
+    return refuse_m(EXL3_UNSUPPORTED,
+                    "exl3_swiglu_cp: banks gate/up [E, hidden -> inter/W], down [E, inter -> hidden/W], one rate for gate and up");
+  if (gate->device != e->device || up->device != e->device || down->device != e->device)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_swiglu_cp: banks on the exchange's device");
+  MoeScratch* sc = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_moe_mu);
+    const int dev = e->device;
+    if (dev >= 0 && dev < kMaxDev && g_moe[dev].ready && g_moe[dev].hidden >= hidden && g_moe[dev].inter >= hidden)
+      sc = &g_moe[dev];
+  }
+  if (!sc) return refuse_m(EXL3_FAILED, "exl3_swiglu_cp: no MoE workspace for these banks (load them with exl3_load_bank)");
+  CpxScope scope(e->device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t* err = device_error_ptr();
+  if (!err) return refuse_m(EXL3_FAILED, "exl3_swiglu_cp: no device error word");
+  const CpxDev& h = e->host;
+  MoeParams p{};
+  p.g_tr = gate->trellis; p.g_suh = gate->suh; p.g_svh = gate->svh;
+  p.u_tr = up->trellis; p.u_suh = up->suh; p.u_svh = up->svh;
+  p.d_tr = down->trellis; p.d_suh = down->suh; p.d_svh = down->svh;
+  p.experts = experts; p.hidden = hidden; p.inter = islice;
+  p.inter_full = inter; p.inter_off = e->rank * islice; p.hidden_out = hslice;
+  p.x = e->base + h.off_x; p.x_dtype = e->dtype;
+  p.inds = e->base + h.off_inds; p.inds_u32 = 0;
+  p.scores = reinterpret_cast<const float*>(e->base + h.off_scores);
+  p.y = e->base + e->off_ycol; p.y_dtype = e->dtype; p.topk = K; p.limit = static_cast<float>(limit);
+  p.row0 = 0; p.rows = W * T;
+  int32_t* ints = reinterpret_cast<int32_t*>(sc->base);
+  p.order = ints;
+  p.chunk_e = ints + kMaxSlots;
+  p.chunk_s = ints + 2 * kMaxSlots;
+  p.chunk_n = ints + 3 * kMaxSlots;
+  p.pos = ints + 4 * kMaxSlots;
+  p.nchunks = ints + 5 * kMaxSlots;
+  p.bad = ints + 5 * kMaxSlots + 1;
+  p.max_cb = sc->hidden / 128;
+  p.unit_done = ints + kIntsM;
+  p.part = reinterpret_cast<float*>(p.unit_done + 2 * static_cast<size_t>(kMaxSlots) * p.max_cb);
+  uint8_t* cur = sc->base + fixed_bytes(sc->hidden, sc->sms);
+  const size_t xs = static_cast<size_t>(kMaxSlots) * (hidden / 16) * 256;
+  p.xg = cur; cur += xs;
+  p.xu = cur; cur += xs;
+  cur += static_cast<size_t>(kMaxSlots) * (sc->hidden / 16) * 256;  // (the local down input lives in the exchange)
+  p.dout = reinterpret_cast<float*>(cur);
+  p.hp = e->base + h.off_hp;
+  for (int q = 0; q < W; ++q) p.hp_dst[q] = e->peer[q] + h.off_hp;
+  p.hp_world = W;
+  const int S = W * T * K;
+  const int copy = W >= 148 ? 1 : (148 + W - 1) / W;
+  cpx_in_kernel<<<dim3(W, copy), 256, 0, st>>>(e->dev, static_cast<const uint8_t*>(x->data),
+                                               static_cast<const int32_t*>(inds->data),
+                                               static_cast<const float*>(scores->data));
+  cpx_wait_kernel<<<1, 32, 0, st>>>(e->dev, 0, err);
+  cudaError_t er = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
+  if (er == cudaSuccess)
+    er = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S < kPrepChunks ? S : kPrepChunks), dim3(128), p, st);
+  if (er == cudaSuccess) er = launch_moe_gemv_k<true>(p, gate->n / 16, sc->sms, st);
+  if (er == cudaSuccess) {
+    cpx_sync_kernel<<<1, 32, 0, st>>>(e->dev, err);
+    er = cudaGetLastError();
+  }
+  if (er == cudaSuccess) er = launch_moe_gemv_k<false>(p, down->n / 16, sc->sms, st);
+  if (er == cudaSuccess)
+    er = launch_pdl(moe_combine_kernel, dim3((hslice + 511) / 512, p.rows < kCombineRows ? p.rows : kCombineRows),
+                    dim3(128), p, st);
+  if (er == cudaSuccess) {
+    cpx_out_kernel<<<dim3(W, copy), 256, 0, st>>>(e->dev, e->base + e->off_ycol);
+    cpx_final_kernel<<<16, 256, 0, st>>>(e->dev, static_cast<uint8_t*>(out->data), err);
+    er = cudaGetLastError();
+  }
+  return er == cudaSuccess ? exl3_verdict{EXL3_OK, nullptr} : refuse_m(EXL3_FAILED, "exl3_swiglu_cp: launch failed");
+}
+
+}  // extern "C"

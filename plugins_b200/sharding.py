@@ -244,6 +244,84 @@ class PeerExpertExchange:
             pass
 
 
+def expert_columns(tr: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, c0: int, c1: int):
+    """A bank's output columns [c0, c1) (multiples of 128): trellis [E, in/16, out/16, n] -> [E, in/16, (c1-c0)/16, n],
+    svh [E, out] -> [E, c1-c0]; suh (the input side) whole."""
+    if c0 % 128 or c1 % 128:
+        raise ValueError("column slices are whole 128-column blocks")
+    return tr[:, :, c0 // 16:c1 // 16].contiguous(), suh.contiguous(), svh[:, c0:c1].contiguous()
+
+
+class ColumnParallelExperts:
+    """Routed SwiGLU experts split by columns over the ranks (exl3_cpx_* / exl3_swiglu_cp): rank r holds, for every
+    expert, gate/up output columns [r inter/W, (r+1) inter/W) and down output columns [r hidden/W, (r+1) hidden/W)
+    (``expert_columns``), so every rank streams 1/W of the distinct experts' bytes whatever the routing.  The tokens
+    are gathered, the down input exchanged and the outputs returned over NVLink peer memory inside one call; no host
+    synchronisation, so a whole step can be captured in a CUDA graph.  One per process (one GPU per rank).
+
+    gate/up/down: this rank's slices of the banks (the shared expert, when ``shared`` is set, last); ``forward(x [T, D],
+    inds, scores)`` -> out [T, D] in x's dtype; inds / scores [T, K], or [T, K + 1] with the shared expert's column.
+    """
+
+    def __init__(self, gate, up, down, experts: int, tokens: int, topk: int, hidden: int, inter: int, rank: int,
+                 world: int, dtype=torch.float16, device=None, group=None, shared: bool = False, limit: int = 0):
+        import ctypes
+        from . import _lib as L
+        self._L, self._ct = L, ctypes
+        self.gate, self.up, self.down, self.shared = gate, up, down, bool(shared)
+        self.experts, self.tokens, self.topk, self.hidden, self.inter = experts, tokens, topk, hidden, inter
+        self.rank, self.world, self.limit = rank, world, limit
+        self.k = topk + (1 if self.shared else 0)
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        index = torch.device(dev).index if torch.device(dev).index is not None else torch.cuda.current_device()
+        handle = (ctypes.c_uint8 * 64)()
+        ptr = ctypes.c_void_p()
+        L.check(L.lib().exl3_cpx_create(index, world, rank, tokens, self.k, hidden, inter, Q._TORCH_DT[dtype],
+                                        ctypes.byref(ptr), handle))
+        self._ptr = ptr
+        mine = bytes(handle)
+        if world > 1:
+            every = [None] * world
+            dist.all_gather_object(every, mine, group=group)
+        else:
+            every = [mine]
+        buf = (ctypes.c_uint8 * (64 * world)).from_buffer_copy(b"".join(every))
+        L.check(L.lib().exl3_cpx_connect(self._ptr, buf))
+        self._opts = L.SwigluOpts(ctypes.sizeof(L.SwigluOpts), int(limit), 0)
+        if self.shared:  # the [T, K + 1] slot lists when the caller passes [T, K]
+            self.ext_inds = torch.full((tokens, self.k), experts, dtype=torch.int32, device=dev)
+            self.ext_scores = torch.ones((tokens, self.k), dtype=torch.float32, device=dev)
+
+    def forward(self, x: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor, out: torch.Tensor | None = None,
+                stream=None):
+        if x.shape != (self.tokens, self.hidden) or inds.shape[0] != self.tokens or \
+                inds.shape[1] not in (self.topk, self.k):
+            raise ValueError("x [tokens, hidden] and inds [tokens, topk (+1 with the shared expert)]")
+        if self.shared and inds.shape[1] == self.topk:
+            self.ext_inds[:, :self.topk].copy_(inds)
+            self.ext_scores[:, :self.topk].copy_(scores)
+            inds, scores = self.ext_inds, self.ext_scores
+        if out is None:
+            out = torch.empty_like(x)
+        ct = self._ct
+        self._L.check(self._L.lib().exl3_swiglu_cp(
+            self._ptr, ct.byref(self.gate.raw), ct.byref(self.up.raw), ct.byref(self.down.raw),
+            ct.byref(Q._tensor(x)), ct.byref(Q._tensor(inds)), ct.byref(Q._tensor(scores)), ct.byref(self._opts),
+            Q._stream(stream), ct.byref(Q._tensor(out))))
+        return out
+
+    def close(self):
+        if self._ptr:
+            self._L.lib().exl3_cpx_destroy(self._ptr)
+            self._ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class ExpertParallelSwiglu:
     """Routed SwiGLU experts split over the ranks.
 

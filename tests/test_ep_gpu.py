@@ -1,7 +1,7 @@
 """Expert parallelism on the GPU: exl3_ep_dispatch / exl3_ep_unpack / exl3_ep_combine against their host restatement
 (tests/sharding_cpu_ops.py), the expert-parallel driver against the single-GPU swiglu and the f32 truth, its
-peer-memory exchange (exl3_epx_*) against the all-to-all one, and -- when the box has two GPUs -- the driver on two
-ranks over NCCL and over peer memory, with a rank that stops taking steps.
+peer-memory exchange (exl3_epx_*) against the all-to-all one, the column-parallel experts (exl3_swiglu_cp) against the
+single-GPU swiglu, and -- when the box has two GPUs -- both drivers on two ranks, with a rank that stops taking steps.
 """
 import datetime
 import os
@@ -193,6 +193,54 @@ def test_peer_exchange_on_one_rank_matches_the_all_to_all_and_replays(Q):
     peer.peer.close()
 
 
+def test_column_parallel_experts_on_one_rank_match_swiglu_and_replay(Q):
+    """world 1: the column-parallel call (gather, route, gate|up storing the down input through the exchange, down,
+    combine, return) gives swiglu's bits; a captured call replayed on new inputs stays equal."""
+    from plugins_b200 import encoder as E
+    from plugins_b200 import sharding as S
+    experts, hidden, inter, n, tokens, topk = 8, 256, 384, 48, 10, 3
+    raw = _banks(E, experts + 1, hidden, inter, n, 80)  # 8 routed experts and the shared one last
+    banks = [Q.weight_from_tensors(*b) for b in raw]
+    cp = S.ColumnParallelExperts(*banks, experts=experts, tokens=tokens, topk=topk, hidden=hidden, inter=inter, rank=0,
+                                 world=1, shared=True)
+    x = torch.empty((tokens, hidden), device="cuda", dtype=torch.float16)
+    inds = torch.empty((tokens, topk), device="cuda", dtype=torch.int32)
+    sc = torch.empty((tokens, topk), device="cuda")
+    out = torch.empty((tokens, hidden), device="cuda", dtype=torch.float16)
+
+    def draw(seed):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        x.copy_(torch.randn((tokens, hidden), device="cuda", generator=g).half())
+        i, s_ = _routing(tokens, topk, experts, seed)
+        i[2, 1] = -1  # an absent slot
+        inds.copy_(i)
+        sc.copy_(s_)
+
+    def single():
+        i2 = torch.cat([inds, torch.full((tokens, 1), experts, dtype=torch.int32, device="cuda")], 1)
+        s2 = torch.cat([sc, torch.ones((tokens, 1), device="cuda")], 1)
+        return Q.swiglu(*banks, x.view(1, tokens, hidden), i2.view(1, tokens, topk + 1).contiguous(),
+                        s2.view(1, tokens, topk + 1).contiguous()).view(tokens, hidden)
+
+    for seed in (1, 2):
+        draw(seed)
+        assert torch.equal(cp.forward(x, inds, sc), single())
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(st), torch.cuda.graph(graph, stream=st):
+        cp.forward(x, inds, sc, out=out)
+    torch.cuda.current_stream().wait_stream(st)
+    for seed in (3, 4, 5):
+        draw(seed)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, single()), seed
+    del graph
+    assert Q.device_error(0) == 0
+    cp.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -250,6 +298,66 @@ def _ep_two_gpu_rank(rank, world, port, exchange="nccl"):
         dist.barrier()
     finally:
         dist.destroy_process_group()
+
+
+def _cp_two_gpu_rank(rank, world, port):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from plugins_b200 import encoder as E
+        from plugins_b200 import quant as Q
+        from plugins_b200 import sharding as S
+        experts, hidden, inter, n, tokens, topk = 8, 512, 512, 48, 6, 3
+        raw = _banks(E, experts + 1, hidden, inter, n, 90, device=dev)  # seeded: identical on both GPUs; shared last
+        c0, c1 = rank * inter // world, (rank + 1) * inter // world
+        h0, h1 = rank * hidden // world, (rank + 1) * hidden // world
+        local = [Q.weight_from_tensors(*S.expert_columns(*raw[0], c0, c1)),
+                 Q.weight_from_tensors(*S.expert_columns(*raw[1], c0, c1)),
+                 Q.weight_from_tensors(*S.expert_columns(*raw[2], h0, h1))]
+        g = torch.Generator(device=dev).manual_seed(3)
+        x_all = torch.randn((world * tokens, hidden), device=dev, generator=g).half()
+        inds_all, sc_all = _routing(world * tokens, topk, experts, 4)
+        inds_all, sc_all = inds_all.to(dev), sc_all.to(dev)
+        sl = slice(rank * tokens, (rank + 1) * tokens)
+        cp = S.ColumnParallelExperts(*local, experts=experts, tokens=tokens, topk=topk, hidden=hidden, inter=inter,
+                                     rank=rank, world=world, device=dev, shared=True)
+        full = [Q.weight_from_tensors(*b) for b in raw]
+        i2 = torch.cat([inds_all[sl], torch.full((tokens, 1), experts, dtype=torch.int32, device=dev)], 1).contiguous()
+        s2 = torch.cat([sc_all[sl], torch.ones((tokens, 1), device=dev)], 1).contiguous()
+        want = Q.swiglu(*full, x_all[sl].contiguous().view(1, tokens, hidden), i2.view(1, tokens, topk + 1),
+                        s2.view(1, tokens, topk + 1)).view(tokens, hidden)
+        for _ in range(3):
+            got = cp.forward(x_all[sl].contiguous(), inds_all[sl].contiguous(), sc_all[sl].contiguous())
+            rel = float(((got.float() - want.float()).norm() / want.float().norm()).item())
+            assert rel < 1e-3, rel
+        torch.cuda.synchronize()
+        assert Q.device_error(rank) == 0
+        # a rank that stops taking calls (between calls: none of its kernels in flight): the other's waits give up
+        # after about a second each with EXL3_ERR_EP_TIMEOUT, and its context runs on
+        from plugins_b200 import _lib as L
+        dist.barrier()
+        if rank == 0:
+            cp.forward(x_all[sl].contiguous(), inds_all[sl].contiguous(), sc_all[sl].contiguous())
+            torch.cuda.synchronize()
+            assert Q.device_error(0, clear=True) & L.ERR_EP_TIMEOUT
+            assert torch.isfinite(Q.swiglu(*full, x_all[sl].contiguous().view(1, tokens, hidden),
+                                           i2.view(1, tokens, topk + 1), s2.view(1, tokens, topk + 1)).float()).all()
+        dist.barrier()  # rank 1 keeps its exchange mapped until rank 0's kernels are done
+        cp.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_column_parallel_experts_on_two_gpus(Q):
+    import torch.multiprocessing as mp
+    mp.spawn(_cp_two_gpu_rank, args=(2, _free_port()), nprocs=2)
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
