@@ -111,6 +111,35 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Exclusive scan of one int per thread over the CTA (blockDim.x a multiple of 32, at most 1024); *total receives the
+// sum.  s_warp: 32 ints of shared memory, reusable when the call returns.
+__device__ __forceinline__ int cta_scan_excl(int v, int* s_warp, int* total) {
+  const int lane = static_cast<int>(threadIdx.x & 31u), warp = static_cast<int>(threadIdx.x >> 5);
+  const int nw = static_cast<int>(blockDim.x >> 5);
+  int x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= d) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, d);
+      if (lane >= d) w += y;
+    }
+    if (lane < nw) s_warp[lane] = w;
+  }
+  __syncthreads();
+  *total = s_warp[nw - 1];
+  const int r = x - v + (warp > 0 ? s_warp[warp - 1] : 0);
+  __syncthreads();
+  return r;
+}
+
 // ------------------------------------------------------------------ tile decode
 
 // The 64 stream bits of a tile ending at lane t's last window end E = 8 (t+1) K, as (hi, lo).  `words` is the tile's

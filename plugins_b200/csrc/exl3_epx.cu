@@ -115,41 +115,53 @@ __global__ void __launch_bounds__(256) epx_dispatch_kernel(const EpxDev* dp, con
   const size_t block_bytes = static_cast<size_t>(cap + 1) * row_bytes;
   uint8_t* block = d.recv[dst] + (static_cast<size_t>(step & 1u) * d.world + d.rank) * block_bytes;
   int32_t* meta = reinterpret_cast<int32_t*>(block + static_cast<size_t>(cap) * row_bytes);
-  if (threadIdx.x == 0) {
-    int j = 0;
-    bool over = false;
-    for (int s = 0; s < tokens * topk; ++s) {
+  // the slots routed to peer dst in slot order: a CTA-wide stable compaction, 256 slots at a time
+  __shared__ int s_warp[32];
+  __shared__ int s_over;
+  if (threadIdx.x == 0) s_over = 0;
+  int base = 0;
+  const int nslots = tokens * topk;
+  for (int s0 = 0; s0 < nslots; s0 += static_cast<int>(blockDim.x)) {
+    const int s = s0 + static_cast<int>(threadIdx.x);
+    int flag = 0, local = 0;
+    if (s < nslots) {
       const int e = read_index(inds, inds_u32, s);
-      int dest, local;
+      int dest = -1;
       if (e >= 0 && e < experts) {
         dest = e / per;
         local = e - dest * per;
       } else if (shared && e == experts) {
         dest = d.rank;
         local = per;
-      } else {
-        if (head && dst == 0) back_slot[s] = -1;
-        continue;
+      } else if (head && dst == 0) {
+        back_slot[s] = -1;
       }
-      if (dest != dst) continue;
+      flag = dest == dst;
+    }
+    int total;
+    const int pos = exl3::cta_scan_excl(flag, s_warp, &total);
+    if (flag) {
+      const int j = base + pos;
       if (j < cap) {
         s_tok[j] = s / topk;
         if (head) {
           meta[j] = local;
           back_slot[s] = dst * (cap + 1) + j;
         }
-        ++j;
       } else {
         if (head) back_slot[s] = -1;
-        over = true;
+        s_over = 1;
       }
     }
-    if (head) {
-      for (int i = j; i < cap; ++i) meta[i] = -1;
-      if (over) atomicOr(err, exl3::kErrEpOverflow);
-    }
-    s_count = j;
+    base += total;
   }
+  if (head) {
+    for (int i = (base < cap ? base : cap) + static_cast<int>(threadIdx.x); i < cap; i += static_cast<int>(blockDim.x))
+      meta[i] = -1;
+  }
+  __syncthreads();
+  if (head && threadIdx.x == 0 && s_over) atomicOr(err, exl3::kErrEpOverflow);
+  if (threadIdx.x == 0) s_count = base < cap ? base : cap;
   __syncthreads();
   const int n = s_count;
   const size_t words = row_bytes / 16;
