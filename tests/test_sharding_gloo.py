@@ -1,4 +1,4 @@
-"""The multi-GPU drivers' host logic on gloo ranks (CPU, world size 2).
+"""The multi-GPU drivers' host logic on gloo ranks (CPU, world size 2), and the column-parallel experts' split.
 
 plugins_b200/sharding.py splits the path the two ways it shards: linears column-parallel with an all-gather of y, and
 routed experts expert-parallel with a dispatch all-to-all and a combine all-to-all.  Here the drivers run unchanged
@@ -156,3 +156,52 @@ def test_dispatch_layout_and_overflow():
     small = torch.zeros((world, 2, hidden))  # capacity 1: the second slot for each peer is dropped
     assert C.ep_dispatch_ref(x, inds, experts, world, small, back)
     assert back.tolist() == [[0, 2], [-1, -1], [-1, -1]]
+
+
+def test_column_parallel_experts_decompose_exactly(oracle):
+    """The column-parallel experts' split (exl3_swiglu_cp): with every rank's expert_columns slices -- gate/up output
+    columns [r I/W, (r+1) I/W), down output columns [r D/W, (r+1) D/W) -- the slices' gate/up columns are the whole
+    expert's columns bit for bit (output blocks are independent), the down input gathered from all ranks is the whole
+    intermediate, and the ranks' output columns reassemble the f32 truth."""
+    from plugins_b200 import sharding as S
+    O = oracle
+    rng = np.random.default_rng(21)
+    experts, hidden, inter, n, world, rows, topk = 3, 256, 256, 48, 2, 4, 2
+    banks = [_rand_linear(rng, a, b, n, (experts,)) for a, b in ((hidden, inter), (hidden, inter), (inter, hidden))]
+    x = rng.standard_normal((rows, hidden)).astype(np.float16).astype(np.float32)
+    inds = np.stack([rng.permutation(experts)[:topk] for _ in range(rows)]).astype(np.int32)
+    scores = rng.random((rows, topk)).astype(np.float32)
+
+    def sliced(b, c0, c1):
+        tr, su, sv = (torch.from_numpy(a.view(np.int16) if a.dtype == np.uint16 else a) for a in b)
+        t2, s2, v2 = S.expert_columns(tr, su, sv, c0, c1)
+        return t2.numpy().view(np.uint16), s2.numpy(), v2.numpy()
+
+    def proj(b, e, xin, in_f, out_f):
+        tr, su, sv = b
+        return O.host_project(xin, tr[e], su[e].view(np.uint16), sv[e].view(np.uint16), in_f, out_f, n, threads=2)
+
+    want = O.moe_truth(x, inds, scores, *[(tr, su.view(np.uint16), sv.view(np.uint16), n) for tr, su, sv in banks],
+                       hidden, inter, 0.0, threads=2)
+    y = np.zeros((rows, hidden), np.float32)
+    for t in range(rows):
+        for k in range(topk):
+            e = int(inds[t, k])
+            hs = []
+            for r in range(world):  # every rank's slice of the intermediate
+                c0, c1 = r * inter // world, (r + 1) * inter // world
+                g = proj(sliced(banks[0], c0, c1), e, x[t:t + 1], hidden, c1 - c0)
+                u = proj(sliced(banks[1], c0, c1), e, x[t:t + 1], hidden, c1 - c0)
+                assert np.array_equal(g, proj(banks[0], e, x[t:t + 1], hidden, inter)[:, c0:c1])
+                hs.append(g / (1.0 + np.exp(-g)) * u)
+            h = np.concatenate(hs, 1)  # the gathered down input
+            outs = []
+            for r in range(world):  # every rank's output columns
+                d0, d1 = r * hidden // world, (r + 1) * hidden // world
+                outs.append(proj(sliced(banks[2], d0, d1), e, h, inter, d1 - d0))
+            y[t] += scores[t, k] * np.concatenate(outs, 1)[0]
+    rel = np.sqrt(((y - want) ** 2).sum() / (want ** 2).sum())
+    assert rel < 1e-5, rel
+    with pytest.raises(ValueError):
+        S.expert_columns(torch.zeros((1, 1, 16, 48), dtype=torch.int16), torch.zeros((1, 16)), torch.zeros((1, 256)),
+                         64, 192)
