@@ -89,3 +89,26 @@ def test_moe_entry_refuses_by_name_without_a_gpu_call():
 def test_matmul_rejects_a_null_weight_before_any_launch():
     v = L.lib().exl3_matmul(ctypes.POINTER(L.Weight)(), None, None, None)
     assert v.code == L.EXL3_FAILED
+
+
+def test_bench_counts_launches_with_the_librarys_gemv_selection():
+    """bench.py's gpu_launches claim mirrors the library's decode-GEMV selection (exl3_abi.cu run_linear,
+    exl3_gemv6.cu launch_gemv6): the thresholds and the in-CTA rotation limits it restates are the library's."""
+    import importlib.util
+    import re
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    hdr = open(os.path.join(root, "plugins_b200", "csrc", "exl3_internal.h")).read()
+    g6 = open(os.path.join(root, "plugins_b200", "csrc", "exl3_gemv6.cu")).read()
+    val = lambda src, name: int(re.search(r"constexpr int(?:64_t)? %s = (\d+);" % name, src).group(1))
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(root, "bench.py"))
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    assert b.GEMV6_MIN_SLABS == val(hdr, "kGemv6MinSlabs")
+    assert b.GEMV6_MIN_SLABS_DEEP == val(hdr, "kGemv6MinSlabsDeep")
+    assert val(g6, "kVirt6") == 3 and val(g6, "kMinRun6") == 32 and val(g6, "kXiRows") == 4
+    assert val(g6, "kXiSlabs") - 8 == 128  # the longest run rotated in-CTA
+    # config 2's launches at batch 1 and 8, one GPU: gate|up and down on the persistent GEMV
+    assert [b.gemv6_mode(i, o, False, 1) for i, o in ((4096, 6144), (4096, 4096), (4096, 24576), (12288, 4096))] == \
+        [0, 0, 1, 1]
+    assert [b.gemv_kernels(i, o, False, 8) for i, o in ((4096, 24576), (12288, 4096))] == [2, 2]
+    assert b.gemv_kernels(4096, 24576, True, 1) == 1  # the column-parallel exchange stays on the cluster split
