@@ -7,7 +7,7 @@ the GPU box has no reference tree).  The fixtures are the reference's own test d
   mul1 table digest and the four splitmix64 planes (seed, K, projection, code/W_hat/one-hot digests), checked by
   plugins/turboexl3_ds41/src/exl3/selfcheck.zig:861-930.
 
-Usage: python tests/golden/make_golden.py [reference_root]
+Usage: python tests/golden/make_golden.py REFERENCE_ROOT   (or set EXL3_REFERENCE_ROOT)
 """
 import json
 import os
@@ -34,4 +34,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("EXL3_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT (the reference checkout), or set EXL3_REFERENCE_ROOT")
+    main(root)
