@@ -112,3 +112,27 @@ def test_bench_counts_launches_with_the_librarys_gemv_selection():
         [0, 0, 1, 1]
     assert [b.gemv_kernels(i, o, False, 8) for i, o in ((4096, 24576), (12288, 4096))] == [2, 2]
     assert b.gemv_kernels(4096, 24576, True, 1) == 1  # the column-parallel exchange stays on the cluster split
+
+
+def test_exchanges_refuse_bad_shapes_before_touching_the_gpu():
+    """The multi-GPU exchanges validate their arguments before any CUDA call: refusals come back by name on a box
+    without a GPU (exl3_tp.cu, exl3_epx.cu, exl3_moe.cu exl3_cpx_create)."""
+    lib = L.lib()
+    handle = (ctypes.c_uint8 * 64)()
+    out = ctypes.c_void_p()
+    cases = [
+        (lib.exl3_tp_create, (0, 9, 0, 1, 16, 1), "1..8 ranks"),
+        (lib.exl3_tp_create, (0, 2, 2, 1, 16, 1), "1..8 ranks"),
+        (lib.exl3_tp_create, (0, 2, 0, 1, 24, 1), "slot_bytes a multiple of 16"),
+        (lib.exl3_epx_create, (0, 0, 0, 8, 256, L.F16), "1..8 ranks"),
+        (lib.exl3_epx_create, (0, 2, 0, 4, 200, L.F16), "hidden a multiple of 128"),
+        (lib.exl3_epx_create, (0, 2, 0, 4, 256, L.I32), "an activation dtype"),
+        (lib.exl3_cpx_create, (0, 9, 0, 4, 9, 4096, 2048, L.F16), "1..8 ranks"),
+        (lib.exl3_cpx_create, (0, 8, 0, 8, 9, 4096, 2048, L.F16), "at most 512"),
+        (lib.exl3_cpx_create, (0, 8, 0, 4, 9, 4096, 1536, L.F16), "128-column blocks per rank"),
+        (lib.exl3_cpx_create, (0, 2, 0, 4, 9, 4096, 2048, L.I32), "an activation dtype"),
+    ]
+    for fn, args, why in cases:
+        v = fn(*args, ctypes.byref(out), handle)
+        assert v.code == L.EXL3_UNSUPPORTED and why in v.message(), (fn.__name__, args, v.message())
+        assert not out.value
