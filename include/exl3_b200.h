@@ -299,6 +299,24 @@ exl3_verdict exl3_matmul_tp(const exl3_weight *w, const exl3_tensor *x, exl3_tp 
  * at out + i * slot_bytes.  A step's gathered outputs are readable from its gather on. */
 exl3_verdict exl3_tp_gather(exl3_tp *tp, int32_t slot0, int32_t nslots, void *stream, void *out);
 
+/* ------------------------------------------------------------------ the model seam's parse (linears only)
+ *
+ * plugins/turboexl3_qwen38/plugin.zig:38-53 ModelTable.claims / parse (config.zig:19-119, src/direct/config.zig:301-420),
+ * narrowed to the keys the linears need.  MLX-free and GPU-free; refusals carry the reference's names
+ * ("turboexl3_qwen38: NotExl3", "...: Exl3CodebookUnsupported", "...: Exl3WindowUnsupported", "...:
+ * Exl3RateUnsupported", "...: Exl3TopKExceedsReduceBank", "...: TrunkQuantNotAnObject", "...: InvalidConfigField",
+ * "...: Unsupported", "...: InvalidConfig"). */
+typedef struct exl3_model_config {
+  uint32_t size; /* sizeof(exl3_model_config), set by the caller */
+  uint32_t hidden_size, intermediate_size, num_hidden_layers, num_attention_heads, num_key_value_heads, head_dim;
+  uint32_t num_experts, num_experts_per_tok, moe_intermediate_size, shared_expert_intermediate_size;
+  uint32_t expert_rate_n; /* the routed banks' halfwords per tile (16 x bits per weight); 0 without expert_quant */
+  char weight_prefix[96];  /* NUL-terminated */
+} exl3_model_config;
+/* A qwen4_exp pack whose config names a trunk_quant block: by marker; everything else: no. */
+exl3_claim exl3_model_claims(exl3_str model_type, exl3_str config_json);
+exl3_verdict exl3_model_parse(exl3_str config_json, exl3_model_config *out);
+
 /* A borrowed view of device arrays already in the pack layout (the reference's shared handles, plugin.zig:213-218):
  * validates the shapes and creates the device workspace; exl3_release on a view frees nothing. */
 exl3_verdict exl3_weight_view(uint16_t *trellis, uint16_t *suh, uint16_t *svh, int32_t groups, int32_t in_features,

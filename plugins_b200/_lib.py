@@ -31,7 +31,18 @@ EXPORTS = (
     "exl3_tp_create", "exl3_tp_connect", "exl3_tp_destroy", "exl3_tp_begin", "exl3_matmul_tp", "exl3_tp_gather",
     "exl3_weight_view", "exl3_weight_stack",
     "exl3_decode_dense", "exl3_encode_trellis", "exl3_matmul_noalloc", "exl3_device_error", "exl3_version",
+    "exl3_model_claims", "exl3_model_parse",
 )
+
+
+class ModelConfig(ctypes.Structure):
+    """exl3_model_config: the model seam's parsed keys (include/exl3_b200.h)."""
+    _fields_ = [("size", ctypes.c_uint32), ("hidden_size", ctypes.c_uint32), ("intermediate_size", ctypes.c_uint32),
+                ("num_hidden_layers", ctypes.c_uint32), ("num_attention_heads", ctypes.c_uint32),
+                ("num_key_value_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
+                ("num_experts", ctypes.c_uint32), ("num_experts_per_tok", ctypes.c_uint32),
+                ("moe_intermediate_size", ctypes.c_uint32), ("shared_expert_intermediate_size", ctypes.c_uint32),
+                ("expert_rate_n", ctypes.c_uint32), ("weight_prefix", ctypes.c_char * 96)]
 
 
 class Str(ctypes.Structure):
@@ -157,6 +168,10 @@ def lib() -> ctypes.CDLL:
             L.exl3_ep_unpack.argtypes = [P(Tensor), ctypes.c_void_p, P(Tensor), P(Tensor)]
             L.exl3_ep_combine.restype = Verdict
             L.exl3_ep_combine.argtypes = [P(Tensor), P(Tensor), P(Tensor), P(Tensor), ctypes.c_void_p, P(Tensor)]
+            L.exl3_model_claims.restype = ctypes.c_int
+            L.exl3_model_claims.argtypes = [Str, Str]
+            L.exl3_model_parse.restype = Verdict
+            L.exl3_model_parse.argtypes = [Str, P(ModelConfig)]
             L.exl3_epx_create.restype = Verdict
             L.exl3_epx_create.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                           ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p),

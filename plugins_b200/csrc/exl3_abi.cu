@@ -618,6 +618,108 @@ uint64_t exl3_bill(exl3_str block_json, exl3_str model_dir, uint64_t stored) {
   return stored;
 }
 
+// ---------------------------------------------------------------- the model seam's parse (linears only)
+//
+// plugins/turboexl3_qwen38/config.zig:19-119 (claims, parse, checkPack / checkBlock) and src/direct/config.zig:301-420
+// (parseJson): MLX-free and bounds-checked, the EXL3 blocks refused with the reference's names, narrowed to what this
+// library decodes (the mul1 codebook named, 16-bit windows, whole bits per weight 1..6).
+
+namespace {
+
+constexpr uint32_t kModelMaxTopK = 32;  // the widest top-k the routed reduction holds (config.zig:16)
+
+bool is_qwen38(const std::string& mt) { return mt == "qwen4_exp" || mt == "qwen4_exp_text"; }
+
+const char* check_model_block(const JVal& o, bool bank, uint32_t* rate_n) {
+  if (!str_is(o.get("format"), "exl3")) return "turboexl3_qwen38: NotExl3";
+  // the reference also decodes mcg and lets a trunk block leave its codebook unnamed; here mul1, named
+  if (!str_is(o.get("codebook"), "mul1")) return "turboexl3_qwen38: Exl3CodebookUnsupported";
+  if (const JVal* w = o.get("window"))
+    if (w->kind != JVal::Num || !w->is_int || w->num != 16) return "turboexl3_qwen38: Exl3WindowUnsupported";
+  if (bank) {
+    const JVal* k = o.get("k");
+    if (!k || k->kind != JVal::Num) return "turboexl3_qwen38: Exl3RateUnsupported";
+    const double scaled = k->num * 16.0, n = std::round(scaled);
+    if (!std::isfinite(scaled) || std::fabs(scaled - n) > 1e-6 || n < 16 || n > 96 || std::fmod(n, 16.0) != 0)
+      return "turboexl3_qwen38: Exl3RateUnsupported";
+    *rate_n = static_cast<uint32_t>(n);
+  }
+  return nullptr;
+}
+
+// A u32 field: absent keeps the default; anything but a non-negative integer below 2^32 is refused.
+bool model_u32(const JVal& o, const char* key, uint32_t* v) {
+  const JVal* f = o.get(key);
+  if (!f) return true;
+  if (f->kind != JVal::Num || !f->is_int || f->num < 0 || f->num > 4294967295.0) return false;
+  *v = static_cast<uint32_t>(f->num);
+  return true;
+}
+
+}  // namespace
+
+exl3_claim exl3_model_claims(exl3_str model_type, exl3_str config_json) {
+  if (!is_qwen38(name_of(model_type))) return EXL3_CLAIM_NO;
+  JVal doc;
+  if (!parse_json(config_json, doc) || doc.kind != JVal::Obj) return EXL3_CLAIM_NO;
+  const JVal* t = doc.get("trunk_quant");
+  return (t && t->kind != JVal::Null) ? EXL3_CLAIM_BY_MARKER : EXL3_CLAIM_NO;
+}
+
+exl3_verdict exl3_model_parse(exl3_str config_json, exl3_model_config* out) {
+  if (!out || out->size != sizeof(exl3_model_config)) return refuse(EXL3_FAILED, "exl3_b200: bad model config");
+  JVal root;
+  if (!parse_json(config_json, root) || root.kind != JVal::Obj) return refuse(EXL3_UNSUPPORTED, "turboexl3_qwen38: InvalidConfig");
+  exl3_model_config c{};
+  c.size = sizeof(exl3_model_config);
+  // the pack's EXL3 blocks first (config.zig:35-41: checkPack runs before the model's parse)
+  const JVal* t = root.get("trunk_quant");
+  if (t && t->kind == JVal::Null) t = nullptr;
+  if (t) {
+    if (t->kind != JVal::Obj) return refuse(EXL3_UNSUPPORTED, "turboexl3_qwen38: TrunkQuantNotAnObject");
+    if (const char* why = check_model_block(*t, false, nullptr)) return refuse(EXL3_UNSUPPORTED, why);
+  }
+  const JVal* tc = root.get("text_config");
+  if (tc && tc->kind != JVal::Obj) return refuse(EXL3_UNSUPPORTED, "turboexl3_qwen38: InvalidConfigField");
+  const JVal& text = tc ? *tc : root;
+  const JVal* e = root.get("expert_quant");
+  if (e && e->kind == JVal::Null) e = nullptr;
+  if (e) {
+    if (e->kind != JVal::Obj) return refuse(EXL3_UNSUPPORTED, "turboexl3_qwen38: NotExl3");
+    if (const char* why = check_model_block(*e, true, &c.expert_rate_n)) return refuse(EXL3_UNSUPPORTED, why);
+    if (const JVal* k = text.get("num_experts_per_tok"))
+      if (k->kind == JVal::Num && k->is_int && k->num > kModelMaxTopK)
+        return refuse(EXL3_UNSUPPORTED, "turboexl3_qwen38: Exl3TopKExceedsReduceBank");
+  }
+  if (!t) return refuse(EXL3_UNSUPPORTED, "turboexl3_qwen38: Unsupported");  // a K pack is fully EXL3
+  // src/direct/config.zig:24-78 defaults
+  c.hidden_size = 3840, c.intermediate_size = 15360, c.num_hidden_layers = 48, c.num_attention_heads = 16;
+  c.num_key_value_heads = 8, c.head_dim = 256;
+  const struct { const char* key; uint32_t* v; } fields[] = {
+      {"hidden_size", &c.hidden_size}, {"intermediate_size", &c.intermediate_size},
+      {"num_hidden_layers", &c.num_hidden_layers}, {"num_attention_heads", &c.num_attention_heads},
+      {"num_key_value_heads", &c.num_key_value_heads}, {"head_dim", &c.head_dim}, {"num_experts", &c.num_experts},
+      {"num_experts_per_tok", &c.num_experts_per_tok}, {"moe_intermediate_size", &c.moe_intermediate_size},
+      {"shared_expert_intermediate_size", &c.shared_expert_intermediate_size}};
+  for (const auto& f : fields)
+    if (!model_u32(text, f.key, f.v)) return refuse(EXL3_UNSUPPORTED, "turboexl3_qwen38: InvalidConfigField");
+  // the bounds the linears need: whole 128-column blocks, heads that divide, a routed bank when experts are named
+  if (c.hidden_size == 0 || c.hidden_size % 128 || c.num_hidden_layers == 0 || c.num_key_value_heads == 0 ||
+      c.num_attention_heads % c.num_key_value_heads || c.intermediate_size % 128 || c.moe_intermediate_size % 128 ||
+      c.shared_expert_intermediate_size % 128)
+    return refuse(EXL3_UNSUPPORTED, "turboexl3_qwen38: InvalidConfigField");
+  if (c.num_experts && (!e || c.num_experts_per_tok == 0 || c.num_experts_per_tok > c.num_experts ||
+                        c.num_experts > 1024 || c.moe_intermediate_size == 0))
+    return refuse(EXL3_UNSUPPORTED, "turboexl3_qwen38: InvalidConfigField");
+  const char* prefix = "language_model.model";
+  if (const JVal* wp = root.get("weight_prefix"))
+    if (wp->kind == JVal::Str) prefix = wp->str.c_str();
+  if (strlen(prefix) >= sizeof(c.weight_prefix)) return refuse(EXL3_UNSUPPORTED, "turboexl3_qwen38: InvalidConfigField");
+  strcpy(c.weight_prefix, prefix);
+  *out = c;
+  return kOk;
+}
+
 exl3_verdict exl3_open(exl3_load_ctx* ctx) {
   if (!ctx || ctx->size != sizeof(exl3_load_ctx)) return refuse(EXL3_FAILED, "exl3_b200: bad load context");
   if (exl3_claims(ctx->block_json, ctx->config_json) == EXL3_CLAIM_NO)

@@ -5,12 +5,12 @@ Qwen3.8-Flash-Next EXL3 pack: attention, caches, a drafter.  On this path only f
 module is them, over this library's quant seam (:mod:`plugins_b200.quant`):
 
 * ``claims(model_type, config_json)`` -- config.zig:19-33: a ``qwen4_exp`` pack whose config names a ``trunk_quant``
-  block is claimed by marker;
+  block is claimed by marker (the library's ``exl3_model_claims``);
 * ``parse(config_json)`` -- config.zig:35-119 ``parse`` / ``checkPack`` and src/direct/config.zig:301-420
-  ``parseJson``: MLX-free and bounds-checked; the pack's EXL3 blocks are checked with the reference's refusal names
-  (``NotExl3``, ``Exl3CodebookUnsupported``, ``Exl3WindowUnsupported``, ``Exl3RateUnsupported``,
-  ``Exl3TopKExceedsReduceBank``), narrowed to what this library decodes (the mul1 codebook, 16-bit windows, whole
-  bits per weight 1..6);
+  ``parseJson``, in the library (``exl3_model_parse``, C++): MLX-free and bounds-checked; the pack's EXL3 blocks are
+  checked with the reference's refusal names (``NotExl3``, ``Exl3CodebookUnsupported``, ``Exl3WindowUnsupported``,
+  ``Exl3RateUnsupported``, ``Exl3TopKExceedsReduceBank``), narrowed to what this library decodes (the mul1 codebook,
+  16-bit windows, whole bits per weight 1..6);
 * ``bill(cfg, source)`` -- the resident bytes: EXL3 weights stay resident as the pack stores them
   (plugins/turboexl3_ds41/config.zig:57-61);
 * :class:`ModelLinears` -- the load (every EXL3 linear and routed bank of the pack uploaded once, the linears that
@@ -24,13 +24,10 @@ from __future__ import annotations
 
 import dataclasses
 import json
-import math
 import re
 
 from ._lib import CLAIM_BY_MARKER, CLAIM_NO, EXL3_UNSUPPORTED, Exl3Error
 
-MODEL_TYPES = ("qwen4_exp", "qwen4_exp_text")  # plugins/turboexl3_qwen38/src/direct/config.zig:11
-MAX_TOPK = 32  # the widest top-k the routed reduction holds (plugins/turboexl3_qwen38/config.zig:16)
 _NAME = "turboexl3_qwen38"
 
 
@@ -58,104 +55,26 @@ class ModelConfig:
 
 
 def claims(model_type: str, config_json: str) -> int:
-    """A qwen4_exp pack whose config names a ``trunk_quant`` block (config.zig:19-29); everything else is not ours."""
-    if model_type not in MODEL_TYPES:
-        return CLAIM_NO
-    try:
-        doc = json.loads(config_json)
-    except (ValueError, TypeError):
-        return CLAIM_NO
-    if not isinstance(doc, dict):
-        return CLAIM_NO
-    t = doc.get("trunk_quant")
-    return CLAIM_NO if t is None else CLAIM_BY_MARKER
-
-
-def _check_block(o: dict, bank: bool) -> None:
-    """config.zig:101-119 checkBlock, narrowed to this library's decode."""
-    if o.get("format") != "exl3":
-        _refuse("NotExl3")
-    if o.get("codebook") != "mul1":
-        # the reference also decodes mcg, and lets a trunk block leave its codebook unnamed; this library decodes
-        # mul1 only and needs the block to say so
-        _refuse("Exl3CodebookUnsupported")
-    w = o.get("window")
-    if w is not None and (not isinstance(w, int) or isinstance(w, bool) or w != 16):
-        _refuse("Exl3WindowUnsupported")  # the reference admits 8..16; narrowed windows are not decoded here
-    if bank:
-        k = o.get("k")
-        if isinstance(k, bool) or not isinstance(k, (int, float)):
-            _refuse("Exl3RateUnsupported")
-        scaled = float(k) * 16.0
-        n = round(scaled)
-        if not math.isfinite(scaled) or abs(scaled - n) > 1e-6 or n < 16 or n > 96 or n % 16:
-            _refuse("Exl3RateUnsupported")  # the reference admits even n in 16..128; here whole bits per weight
-
-
-def _u32(obj: dict, key: str, default: int, required: bool = False) -> int:
-    v = obj.get(key)
-    if v is None:
-        if required:
-            _refuse("InvalidConfigField")
-        return default
-    if isinstance(v, bool) or not isinstance(v, int) or v < 0 or v > 0xFFFFFFFF:
-        _refuse("InvalidConfigField")
-    return v
+    """A qwen4_exp pack whose config names a ``trunk_quant`` block (config.zig:19-29): by marker (exl3_model_claims)."""
+    from . import _lib as L
+    return int(L.lib().exl3_model_claims(L.Str.of(model_type), L.Str.of(config_json)))
 
 
 def parse(config_json: str) -> ModelConfig:
-    """config.json -> :class:`ModelConfig`, refusing by name what the reference refuses and what this library does
-    not decode."""
-    try:
-        root = json.loads(config_json)
-    except (ValueError, TypeError):
-        _refuse("InvalidConfig")
-    if not isinstance(root, dict):
-        _refuse("InvalidConfig")
-    # the pack's EXL3 blocks first (config.zig:35-41: checkPack runs before the model's parse)
-    t = root.get("trunk_quant")
-    if t is not None:
-        if not isinstance(t, dict):
-            _refuse("TrunkQuantNotAnObject")
-        _check_block(t, False)
-    e = root.get("expert_quant")
-    text = root.get("text_config", root)
-    if not isinstance(text, dict):
-        _refuse("InvalidConfigField")
-    if e is not None:
-        if not isinstance(e, dict):
-            _refuse("NotExl3")
-        _check_block(e, True)
-        k = text.get("num_experts_per_tok")
-        if isinstance(k, int) and not isinstance(k, bool) and k > MAX_TOPK:
-            _refuse("Exl3TopKExceedsReduceBank")
-    if t is None:
-        _refuse("Unsupported")  # a K pack is fully EXL3 (src/direct/config.zig:372-374)
-    c = ModelConfig(model_type=str(root.get("model_type", "qwen4_exp")), trunk_quant=t, expert_quant=e)
-    if isinstance(root.get("weight_prefix"), str):
-        c.weight_prefix = root["weight_prefix"]
-    c.hidden_size = _u32(text, "hidden_size", c.hidden_size)
-    c.intermediate_size = _u32(text, "intermediate_size", c.intermediate_size)
-    c.num_hidden_layers = _u32(text, "num_hidden_layers", c.num_hidden_layers)
-    c.num_attention_heads = _u32(text, "num_attention_heads", c.num_attention_heads)
-    c.num_key_value_heads = _u32(text, "num_key_value_heads", c.num_key_value_heads)
-    c.head_dim = _u32(text, "head_dim", c.head_dim)
-    c.num_experts = _u32(text, "num_experts", 0)
-    c.num_experts_per_tok = _u32(text, "num_experts_per_tok", 0)
-    c.moe_intermediate_size = _u32(text, "moe_intermediate_size", 0)
-    c.shared_expert_intermediate_size = _u32(text, "shared_expert_intermediate_size", 0)
-    # bounds the linears need: every width a whole number of 128-column blocks, heads that divide
-    if c.hidden_size == 0 or c.hidden_size % 128 or c.num_hidden_layers == 0:
-        _refuse("InvalidConfigField")
-    if c.num_key_value_heads == 0 or c.num_attention_heads % c.num_key_value_heads:
-        _refuse("InvalidConfigField")
-    for width in (c.intermediate_size, c.moe_intermediate_size, c.shared_expert_intermediate_size):
-        if width % 128:
-            _refuse("InvalidConfigField")
-    if c.num_experts:
-        if e is None or c.num_experts_per_tok == 0 or c.num_experts_per_tok > c.num_experts or \
-                c.num_experts > 1024 or c.moe_intermediate_size == 0:
-            _refuse("InvalidConfigField")
+    """config.json -> :class:`ModelConfig` through the library's parse (exl3_model_parse: MLX-free, bounds-checked,
+    refusals by the reference's names); the EXL3 blocks ride along for the load."""
+    import ctypes
+    from . import _lib as L
+    raw = L.ModelConfig()
+    raw.size = ctypes.sizeof(L.ModelConfig)
+    L.check(L.lib().exl3_model_parse(L.Str.of(config_json), ctypes.byref(raw)))
+    root = json.loads(config_json)  # (parsed by the library above: a JSON object)
+    c = ModelConfig(model_type=str(root.get("model_type", "qwen4_exp")), weight_prefix=raw.weight_prefix.decode(),
+                    trunk_quant=root["trunk_quant"], expert_quant=root.get("expert_quant"))
+    for f in ("hidden_size", "intermediate_size", "num_hidden_layers", "num_attention_heads", "num_key_value_heads",
+              "head_dim", "num_experts", "num_experts_per_tok", "moe_intermediate_size",
+              "shared_expert_intermediate_size"):
+        setattr(c, f, int(getattr(raw, f)))
     return c
 
 
