@@ -211,6 +211,26 @@ def test_north_star_layer_parity(Q, E, oracle):
     assert Q.device_error(0) == 0
 
 
+def test_persistent_gemv_layer_against_truth_and_row_invariance(Q, E, oracle):
+    # config 2's down layer, 12288 -> 4096 at 3 bpw: large enough for the persistent GEMV (exl3_gemv6.cu: 8192
+    # inputs and 16384 slab-units or more), at 1-4 rows with the input rotated in-CTA, at 8 with the prepare launch,
+    # at 12-16 with two row groups; against the f32 truth, and row r's bytes the same at every width
+    in_f, out_f, n = 12288, 4096, 48
+    tr, suh, svh = _linear(E, in_f, out_f, n, seed=12)
+    w = Q.weight_from_tensors(tr, suh, svh)
+    x = torch.randn((16, in_f), device="cuda", dtype=torch.float16)
+    want = oracle.host_project(x.float().cpu().numpy(), _np(tr).view(np.uint16), _np(suh).view(np.uint16),
+                               _np(svh).view(np.uint16), in_f, out_f, n, threads=os.cpu_count() or 8)
+    ys = {}
+    for rows in (1, 3, 4, 8, 12, 16):
+        y = Q.matmul(w, x[:rows].contiguous())
+        assert _rel(y.float().cpu().numpy(), want[:rows]) < REL_L2_BAR, rows
+        ys[rows] = y
+    for rows, y in ys.items():
+        assert torch.equal(y.view(torch.int16), ys[16][:rows].view(torch.int16)), rows
+    assert Q.device_error(0) == 0
+
+
 def test_encoder_round_trip(Q, E, oracle):
     # encode -> decode on the GPU is bit-identical to the oracle's decode of the same bitstream, and the decoded
     # layer approximates the dense weight it encoded
