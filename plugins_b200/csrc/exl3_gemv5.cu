@@ -373,15 +373,18 @@ bool gemv5_geometry(GemvParams& p, int K, int sms, int row_groups, int split_ove
   const int deep = K <= 2 ? 16 : (K <= 4 ? 12 : (K == 5 ? 10 : 8));  // deep_stages<K>()
   const int shallow = K <= 4 ? 8 : 6;                                 // shallow_stages<K>()
   // CTAs per column block: a divisor of KT leaving whole 128-input blocks (8 slabs) per CTA, at most 16 (the
-  // cluster limit) and at most 128 slabs per CTA.  Preferred: splits whose shared memory (with the shallow ring)
-  // keeps three CTAs per SM; among those the largest whose grid still fits one wave of three CTAs per SM, else the
-  // smallest.  Then the deep ring if it still keeps three CTAs per SM.
+  // cluster limit) and at most 128 slabs per CTA.  The split fixes a row's summation order (slabs per warp, CTA
+  // partials in rank order), so it is chosen for every width at once -- a row's bytes must not depend on the rows
+  // batched with it: splits whose shared memory (with the shallow ring) fits at the widest launch, preferred by their
+  // footprint at 8 rows: those that keep three CTAs per SM, among them the largest whose grid still fits one wave of
+  // three CTAs per SM, else the smallest.  Only the ring depth follows the launch's rows (it sets prefetch, not the
+  // order of the sums): the deep ring where it still keeps three CTAs per SM.
   int best = 0, fallback = 0;
   for (int pass = 0; pass < 2 && best == 0; ++pass) {
     for (int d = 1; d <= 16; ++d) {
       if (KT % d != 0 || (KT / d) % 8 != 0 || KT / d > 128) continue;
-      const size_t smem = gemv5_smem_for(K, shallow, KT / d, row_groups, p.rows);
-      if (smem > 227 * 1024) continue;
+      if (gemv5_smem_for(K, shallow, KT / d, 2, kMaxRows) > 227 * 1024) continue;
+      const size_t smem = gemv5_smem_for(K, shallow, KT / d, 1, 8);
       if (split_override > 0) {
         if (d == split_override) best = d;
         continue;

@@ -133,13 +133,19 @@ def test_imma_and_dp4a_paths_agree_bitwise(Q, E):
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
-def test_rows_share_a_launch_without_changing_bytes(Q, E):
+@pytest.mark.parametrize("in_f,out_f,n", [
+    (2048, 3072, 48),
+    # config 2's layer at 3 and 4 bpw: the cluster split's shared memory grows with the rows, and a split chosen per
+    # width would change at 9 and 13 rows (exl3_gemv5.cu chooses it for every width at once)
+    (4096, 12288, 48), (4096, 12288, 64),
+])
+def test_rows_share_a_launch_without_changing_bytes(Q, E, in_f, out_f, n):
     # linear.zig:450-491: row r has the same bytes at widths 1..16
-    tr, suh, svh = _linear(E, 2048, 3072, 48, seed=5)
+    tr, suh, svh = _linear(E, in_f, out_f, n, seed=5)
     w = Q.weight_from_tensors(tr, suh, svh)
-    x = (torch.rand((16, 2048), device="cuda") * 8 - 4).to(torch.bfloat16)
+    x = (torch.rand((16, in_f), device="cuda") * 8 - 4).to(torch.bfloat16)
     solo = [Q.matmul(w, x[r:r + 1].contiguous()) for r in range(16)]
-    for width in (2, 3, 5, 8, 9, 16):
+    for width in (2, 3, 5, 8, 9, 12, 13, 16):
         y = Q.matmul(w, x[:width].contiguous())
         for r in range(width):
             assert torch.equal(y[r].view(torch.int16), solo[r][0].view(torch.int16)), (width, r)
