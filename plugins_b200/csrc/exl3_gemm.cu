@@ -512,9 +512,8 @@ template <int MS, int NS>
 static cudaError_t launch_gemm_t(const GemmParams& p, int sms, cudaStream_t st) {
   using S = GemmShape<MS, NS>;
   if (p.tiles_m * 128 * MS < p.m) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(gemm_image_kernel<MS, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(S::kSmemBytes));
-  if (e != cudaSuccess) return e;
+  static KernelSetup setup;
+  if (cudaError_t e = kernel_setup(setup, gemm_image_kernel<MS, NS>, 256, S::kSmemBytes); e != cudaSuccess) return e;
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < sms ? tiles : sms;
   gemm_image_kernel<MS, NS><<<grid, 256, S::kSmemBytes, st>>>(p);

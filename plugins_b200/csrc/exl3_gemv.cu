@@ -390,12 +390,8 @@ template <int K, int RG, bool IMMA>
 static cudaError_t launch_gemv_t(const GemvParams& p, unsigned grid, cudaStream_t st, bool pdl) {
   auto kern = gemv_kernel<K, RG, IMMA>;
   const size_t smem = gemv_smem_bytes<K, RG, IMMA>(p.xp_bytes, p.rows);
-  static size_t configured = 0;  // per instantiation
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static KernelSetup setup;
+  if (cudaError_t e = kernel_setup(setup, kern, kThreads, smem); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);

@@ -317,14 +317,8 @@ static cudaError_t launch5_t(const GemvParams& p, cudaStream_t st, bool pdl) {
   auto kern = gemv5_kernel<K, RG, IMMA, ST>;
   const size_t smem = static_cast<size_t>(p.xp_bytes) + static_cast<size_t>(kW5) * ST * 8u * 32u * K +
                       static_cast<size_t>(kW5) * p.rows * kRed5 * 4;
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
+  static KernelSetup setup;
+  if (cudaError_t e = kernel_setup(setup, kern, kT5, smem, true); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.grid));
   cfg.blockDim = dim3(kT5);

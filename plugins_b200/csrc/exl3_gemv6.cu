@@ -330,15 +330,9 @@ cudaError_t launch6_t(const GemvParams& p, int sms, __half* xf, float* part, uin
   auto kern = gemv6_kernel<K, RG, ST, XI>;
   const size_t smem = static_cast<size_t>(kW6) * ST * 8u * 32u * K +
                       static_cast<size_t>(kW6) * (XI ? kXiRows : 8 * RG) * kRed6 * 4 + (XI ? kXiSlabs * 128 : 0);
-  static int per_sm = 0;  // resident CTAs per SM (at most kVirt6): the persistent grid is exactly one wave
-  if (per_sm == 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kT6, smem);
-    if (e != cudaSuccess) return e;
-    per_sm = occ < 1 ? 1 : (occ > kVirt6 ? kVirt6 : occ);
-  }
+  static KernelSetup setup;
+  int per_sm = 0;  // resident CTAs per SM (at most kVirt6): the persistent grid is exactly one wave
+  if (cudaError_t e = kernel_setup(setup, kern, kT6, smem, false, &per_sm, kVirt6); e != cudaSuccess) return e;
   GemvParams q = p;
   q.grid = sms * kVirt6;  // the virtual CTAs the work is cut for
   cudaLaunchConfig_t cfg = {};

@@ -3,7 +3,55 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 namespace exl3 {
+
+// One kernel's launch setup, per device: dynamic shared memory above 48 KiB is opted into in each device's context,
+// and the resident CTAs per SM it leaves are that device's.  Launchers keep one (a function-local static per kernel
+// instantiation); the first launch on a device, or one needing more shared memory than any before it, takes the
+// mutex, so concurrent first launches from several host threads set the attribute once and in order.
+struct KernelSetup {
+  static constexpr int kDevices = 64;
+  std::atomic<int> smem[kDevices] = {};    // bytes opted into on the device (0: none yet)
+  std::atomic<int> per_sm[kDevices] = {};  // resident CTAs per SM found at that opt-in (when asked for)
+  std::mutex mu;
+};
+
+// Opts `kern` into `smem` bytes (and, with `cluster`, non-portable cluster sizes) on the current device, once per
+// device and size; with `per_sm` non-null, also returns the kernel's resident CTAs per SM there at `threads` threads,
+// clamped to 1 .. cap (kernels whose shared memory does not vary from launch to launch).
+template <typename Kern>
+cudaError_t kernel_setup(KernelSetup& s, Kern kern, int threads, size_t smem, bool cluster = false,
+                         int* per_sm = nullptr, int cap = 1) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= KernelSetup::kDevices) return cudaErrorInvalidDevice;
+  const int bytes = static_cast<int>(smem);
+  if (s.smem[dev].load(std::memory_order_acquire) < bytes || (per_sm && s.per_sm[dev].load(std::memory_order_acquire) == 0)) {
+    std::lock_guard<std::mutex> lk(s.mu);
+    if (s.smem[dev].load(std::memory_order_relaxed) < bytes || (per_sm && s.per_sm[dev].load(std::memory_order_relaxed) == 0)) {
+      const int set = bytes > s.smem[dev].load(std::memory_order_relaxed) ? bytes : s.smem[dev].load(std::memory_order_relaxed);
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, set);
+      if (e != cudaSuccess) return e;
+      if (cluster) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+      }
+      if (per_sm) {
+        int occ = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+        if (e != cudaSuccess) return e;
+        s.per_sm[dev].store(occ < 1 ? 1 : (occ > cap ? cap : occ), std::memory_order_release);
+      }
+      s.smem[dev].store(set, std::memory_order_release);
+    }
+  }
+  if (per_sm) *per_sm = s.per_sm[dev].load(std::memory_order_acquire);
+  return cudaSuccess;
+}
 
 constexpr int kMaxSegments = 4;  // linears stacked into one launch (the reference's SHARED_MAX, linear.zig:39-40)
 constexpr int kMaxRows = 16;     // decode-GEMV rows per launch (two m16n8k16 row groups)

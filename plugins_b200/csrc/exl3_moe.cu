@@ -531,16 +531,10 @@ cudaError_t launch_moe_gemv(const MoeParams& p, int sms, cudaStream_t st) {
   auto kern = moe_gemv_kernel<K, PAIR>;
   constexpr size_t slab = (PAIR ? 2u : 1u) * (8u * 32u * K + 256u);
   const size_t smem = kWarpsM * kStagesM * slab + (PAIR ? 2 : 1) * kWarpsM * 8 * kRedStrideM * 4;
-  static int per_sm = 0;  // resident CTAs per SM: the persistent grid is exactly one wave
-  if (per_sm == 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kWarpsM * 32, smem);
-    if (e != cudaSuccess) return e;
-    const int cap = moe_ctas_per_sm();
-    per_sm = occ < 1 ? 1 : (occ > cap ? cap : occ);
-  }
+  static KernelSetup setup;
+  int per_sm = 0;  // resident CTAs per SM: the persistent grid is exactly one wave
+  if (cudaError_t e = kernel_setup(setup, kern, kWarpsM * 32, smem, false, &per_sm, moe_ctas_per_sm()); e != cudaSuccess)
+    return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sms * per_sm);
   cfg.blockDim = dim3(kWarpsM * 32);
