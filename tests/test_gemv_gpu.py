@@ -265,3 +265,22 @@ def test_shapes_are_refused_by_name(Q, E):
         Q.weight_from_tensors(tr40, suh, svh)
     y = Q.matmul(w, torch.zeros((0, 256), device="cuda", dtype=torch.float16))
     assert y.shape == (0, 256)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_second_device_in_one_process(Q, E):
+    # a kernel's shared-memory opt-in and occupancy belong to each device's context: the cluster-split GEMV, the
+    # persistent GEMV and the GEMM on the second GPU of a process that ran them on the first give the same bytes
+    outs = {}
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            for in_f, out_f, n, rows in ((4096, 12288, 64, 1), (12288, 4096, 48, 1), (512, 768, 64, 128)):
+                tr, suh, svh = _linear(E, in_f, out_f, n, seed=in_f + out_f)
+                w = Q.weight_from_tensors(tr, suh, svh)
+                g = torch.Generator(device="cuda").manual_seed(rows)
+                x = torch.randn((rows, in_f), generator=g, device="cuda").to(torch.float16)
+                outs[(dev, in_f, out_f)] = Q.matmul(w, x).cpu()
+            assert Q.device_error(dev) == 0
+    for key, y in outs.items():
+        if key[0] == 1:
+            assert torch.equal(y.view(torch.int16), outs[(0,) + key[1:]].view(torch.int16)), key
