@@ -237,6 +237,37 @@ def test_persistent_gemv_layer_against_truth_and_row_invariance(Q, E, oracle):
     assert Q.device_error(0) == 0
 
 
+@pytest.mark.parametrize("n", [32, 48, 64, 80])
+def test_large_layer_at_full_size(Q, E, oracle, n):
+    # config 5's layer, 16384 x 53248 at 2-5 bpw (the persistent GEMV), through two size-independent properties:
+    # one-hot prepared rows with the inner product give W_hat's rows bit for bit (the oracle decodes those slabs), and
+    # batch-1 outputs of sampled 128-column blocks hold the f32 truth's bar (the output rotation is per block, so a
+    # block's truth needs only its own columns)
+    in_f, out_f = 16384, 53248
+    tr, suh, svh = _linear(E, in_f, out_f, n, seed=5 + n)
+    w = Q.weight_from_tensors(tr, suh, svh)
+    ks = (0, 9999, in_f - 1)
+    x = torch.zeros((len(ks), in_f), device="cuda", dtype=torch.float16)
+    for i, k in enumerate(ks):
+        x[i, k] = 1.0
+    got = Q.matmul_ex(w, x, flags=1 | 2).to(torch.float16).view(torch.uint16).cpu().numpy()  # PREPARED | INNER
+    for i, k in enumerate(ks):
+        slab = _np(tr[k // 16:k // 16 + 1]).view(np.uint16)
+        want = oracle.reconstruct_inner(slab, 16, out_f, n)[k % 16]
+        assert np.array_equal(got[i], want), k
+    x = torch.randn((1, in_f), device="cuda", dtype=torch.float16)
+    y = Q.matmul(w, x).float().cpu().numpy()
+    got, want = [], []
+    for cb in (0, 137, out_f // 128 - 1):
+        cols = slice(cb * 128, cb * 128 + 128)
+        want.append(oracle.host_project(x.float().cpu().numpy(), _np(tr[:, cb * 8:cb * 8 + 8].contiguous()).view(np.uint16),
+                                        _np(suh).view(np.uint16), _np(svh[cols].contiguous()).view(np.uint16), in_f, 128, n,
+                                        threads=os.cpu_count() or 8))
+        got.append(y[:, cols])
+    assert _rel(np.concatenate(got, 1), np.concatenate(want, 1)) < REL_L2_BAR
+    assert Q.device_error(0) == 0
+
+
 def test_encoder_round_trip(Q, E, oracle):
     # encode -> decode on the GPU is bit-identical to the oracle's decode of the same bitstream, and the decoded
     # layer approximates the dense weight it encoded
