@@ -103,3 +103,36 @@ def test_absent_experts_contribute_nothing_after_a_full_call(oracle):
     for r in range(rows):  # row by row: a leaked slot shows in its own row
         rel = np.linalg.norm(got[r] - want[r]) / np.linalg.norm(want[r])
         assert rel < REL_L2_BAR, (r, rel)
+
+
+def test_config4_call_at_full_size(oracle):
+    # config 4 as the bench runs it -- 256 routed experts + the shared one (bank entry 256, score 1), 4096 <-> 2048 at
+    # 3 bpw, 32 tokens, top-8 -- in one call; a token's output needs only its own experts, so sampled tokens are held
+    # to the f32 truth on the banks' slices of just those experts
+    import os
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    experts, hidden, inter, topk, tokens, n = 256, 4096, 2048, 8, 32, 48
+    raw = [E.random_linear(a, b, n, seed=3 + i, groups=experts + 1)
+           for i, (a, b) in enumerate(((hidden, inter), (hidden, inter), (inter, hidden)))]
+    banks = [Q.weight_from_tensors(*r) for r in raw]
+    g = torch.Generator(device="cuda").manual_seed(4)
+    logits = torch.randn((tokens, experts), device="cuda", generator=g)
+    sc, ind = torch.topk(torch.softmax(logits, -1), topk, -1)
+    ind = torch.cat([ind.to(torch.int32), torch.full((tokens, 1), experts, dtype=torch.int32, device="cuda")], 1)
+    sc = torch.cat([sc.float(), torch.ones((tokens, 1), device="cuda")], 1)
+    ind, sc = ind.view(1, tokens, topk + 1).contiguous(), sc.view(1, tokens, topk + 1).contiguous()
+    x = torch.randn((1, tokens, hidden), device="cuda", dtype=torch.float16, generator=g)
+    y = Q.swiglu(*banks, x, ind, sc).float().cpu().numpy().reshape(tokens, hidden)
+    picked = [0, 13, 31]
+    sub = ind[0, picked]
+    used = torch.unique(sub)
+    local = torch.searchsorted(used, sub.contiguous()).to(torch.int32)
+    sl = [tuple(_np16(t.index_select(0, used.long()).contiguous()) for t in r) + (n,) for r in raw]
+    want = oracle.moe_truth(x[0, picked].float().cpu().numpy(), local.cpu().numpy(), sc[0, picked].cpu().numpy(),
+                            sl[0], sl[1], sl[2], hidden, inter, threads=os.cpu_count() or 8)
+    got = y[picked]
+    err = float(np.sqrt(((got - want) ** 2).sum() / (want ** 2).sum()))
+    floor = float(np.sqrt(((torch.from_numpy(want).half().float().numpy() - want) ** 2).sum() / (want ** 2).sum()))
+    assert err < np.sqrt(REL_L2_BAR ** 2 + floor ** 2), (err, floor)
+    assert Q.device_error(0) == 0
