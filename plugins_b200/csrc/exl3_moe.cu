@@ -18,12 +18,17 @@
 //                  128-wide input block is exactly this column block), writing the down GEMV's B fragments;
 //   4. down     -- the same GEMV over (chunk, 128-column block of the hidden size), finishing to f32 per slot;
 //   5. combine  -- y_r = sum_k score * d in k order, in x's dtype.
-// Work split: whole units round-robin over the persistent grid while every CTA gets one (neighbouring CTAs stream
-// the same expert's k slabs together), then the remaining units' k slabs, laid end to end, cut into one equal run per
-// CTA (stream-K: a multiple of four slabs, at least kMinRun), so every CTA streams the same bytes however few experts
-// a call touches.  A unit that two or more runs share is finished by the run that completes it last (a per-unit
-// counter): it adds the runs' partial sums in run order and applies the epilogue.  The order of every sum is fixed by the call's routing and the
-// grid, never by timing, so results are reproducible.
+// Work split: every unit's k range is cut into the same runs in every call (at most kMaxRuns runs of about 32 slabs,
+// set by the input width alone).  Whole units go round-robin over the persistent grid while every CTA gets one
+// (neighbouring CTAs stream the same expert's k slabs together); the remaining units' runs, laid end to end, are cut
+// into one equal range per CTA, so every CTA streams about the same bytes however few experts a call touches.  Each
+// warp sums a run's slabs from zero in its MMA accumulators and adds the run to its running total in run order; a
+// unit's value is the warps' totals in warp order.  A unit that two or more CTAs share is finished by the CTA that
+// completes it last (a per-unit counter): it continues each warp's total of the first CTA's runs with the later
+// runs, one by one in run order, then sums the warps -- the same sums a whole unit makes.  So the order of every
+// sum is fixed by the input width and the tile layout, never by the routing, the grid or timing: a slot's output
+// has the same bytes whatever other rows and experts share the call (the reference checks its expert kernels for
+// this row invariance, plugins/turboexl3_ds41/src/exl3/selfcheck.zig:755-851).
 #include <cuda_runtime.h>
 
 #include <cstdlib>
@@ -45,7 +50,14 @@ constexpr int kChunkRows = 8;      // slots per chunk: the MMA's N
 constexpr int kWarpsM = 4;
 constexpr int kStagesM = 4;
 constexpr int kRedStrideM = 132;
-constexpr int kMinRun = 32;         // slabs: the shortest run a CTA takes (eight per warp)
+constexpr int kMaxRuns = 8;         // runs per unit at most (the partial slots a CTA may need)
+
+// A unit's run length in slabs for kt slabs of input: about 32 (eight per warp), a multiple of four, at most kMaxRuns
+// runs (the last one shorter).
+__host__ __device__ constexpr int moe_run_slabs(int kt) {
+  const int r = (kt + 31) / 32 < kMaxRuns ? (kt + 31) / 32 : kMaxRuns;
+  return ((kt + r - 1) / r + 3) & ~3;
+}
 constexpr int kPrepChunks = 48;     // prepare: chunk columns of the grid
 constexpr int kCombineRows = 64;    // combine: row columns of the grid
 constexpr int kIntsM = 5 * kMaxSlots + 64;  // the route's ints: order, chunk_e/s/n, pos, nchunks, bad
@@ -84,7 +96,9 @@ struct MoeParams {
   uint8_t* xu;         // [chunk][hidden/16][256 B] up-prepared rows
   uint8_t* hp;         // [chunk][inter/16][256 B] down-prepared rows
   float* dout;         // [kMaxSlots][hidden] down outputs per slot (position in `order`)
-  float* part;         // [grid][2 runs' ends][2 weights][8][128] partial sums of units a run shares with another
+  float* part;         // [grid][P runs][4 warps][2 weights][8][128] sums of the units a CTA shares with others: slots
+                       // 0 .. P - 2 the runs of a unit it joins after its first run, P - 1 the warps' totals of the
+                       // unit it starts but does not finish
   int32_t* unit_done;  // [2 launches][kMaxSlots * max CB] runs finished per unit (each reset by its unit's last run)
 };
 
@@ -256,32 +270,36 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
   ImmaIndicator ind;
   ind.init(lane);
   const uint32_t g = lane >> 2, q = lane & 3u;
-  // whole units round-robin while every CTA gets one (dp of them), then this CTA's run [r0, r1) of the remaining
-  // units' slabs laid end to end
+  // Every unit's k range is cut the same way whatever the call: P runs of L slabs (the last run shorter), a warp's
+  // slabs of a run summed from zero in its MMA accumulators, the warp's runs added in run order, then the warps in
+  // warp order.  Whole units go round-robin while every CTA gets one (dp of them); the remaining units' runs, laid
+  // end to end, are cut into one equal range [R0, R1) per CTA.
   const int G = static_cast<int>(gridDim.x);
+  const int L = moe_run_slabs(KT), P = (KT + L - 1) / L, Lw = L / kWarpsM;
   const int dp = units / G * G;
-  const int64_t work = static_cast<int64_t>(units - dp) * KT;
-  int64_t run = (work + G - 1) / G;
-  run = (run < kMinRun ? kMinRun : run + 3) & ~int64_t{3};
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * run;
-  const int64_t r1 = r0 + run < work ? r0 + run : work;
+  const int64_t sk_runs = static_cast<int64_t>(units - dp) * P;
+  const int64_t per = sk_runs > 0 ? (sk_runs + G - 1) / G : 1;
+  const int64_t R0 = static_cast<int64_t>(blockIdx.x) * per;
+  const int64_t R1 = R0 + per < sk_runs ? R0 + per : sk_runs;
   int32_t* done = p.unit_done + (PAIR ? 0 : kMaxSlots * static_cast<int64_t>(p.max_cb));
+  constexpr int kPart = (PAIR ? 2 : 1) * 8 * 128;  // one warp's sums of a unit: [weight][row][column]
 
   int next = static_cast<int>(blockIdx.x);
-  for (int64_t at = r0;;) {
-    int unit, su = 0, k0 = 0, k1 = KT;
+  for (int64_t at = R0;;) {
+    int unit, su = 0, ra = 0, rb = P;  // this item: runs ra .. rb - 1 of the unit
     if (next < dp) {
       unit = next;
       next += G;
-    } else if (at < r1) {
-      su = static_cast<int>(at / KT);
-      k0 = static_cast<int>(at - static_cast<int64_t>(su) * KT);
-      k1 = static_cast<int>(r1 - at < KT - k0 ? k0 + (r1 - at) : KT);
-      at += k1 - k0;
+    } else if (at < R1) {
+      su = static_cast<int>(at / P);
+      ra = static_cast<int>(at - static_cast<int64_t>(su) * P);
+      rb = static_cast<int>(R1 - at < P - ra ? ra + (R1 - at) : P);
+      at += rb - ra;
       unit = dp + su;
     } else {
       break;
     }
+    const int k0 = ra * L, k1 = rb * L < KT ? rb * L : KT;
     const int chunk = unit / CB, cb = unit % CB;
     const int e = p.chunk_e[chunk], s0 = p.chunk_s[chunk], nrow = p.chunk_n[chunk];
     const uint8_t* wa = tra + e * wstride + static_cast<size_t>(cb) * 8u * kTileBytes;
@@ -289,7 +307,8 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
     const uint8_t* xca = xa + static_cast<size_t>(chunk) * KT * 256;
     const uint8_t* xcb = xb + static_cast<size_t>(chunk) * KT * 256;
     const size_t rowstride = static_cast<size_t>(CB) * 8u * kTileBytes;  // bytes between k slabs
-    // this warp's slabs of the run: k0 + warp, k0 + warp + 4, ... (k0 and k1 are multiples of four)
+    // this warp's slabs of the item: k0 + warp, k0 + warp + 4, ... (k0 and k1 are multiples of four); every run
+    // gives each warp L / 4 of them (the unit's last run fewer: it ends the item)
     const uint32_t nk = static_cast<uint32_t>(k1 - k0);
     const uint32_t mine = nk > warp ? (nk - warp + kWarpsM - 1) / kWarpsM : 0u;
     auto issue = [&](uint32_t i) {
@@ -317,6 +336,32 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
       for (int t = 0; t < 8; ++t)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[w2][t][c] = 0.0f;
+    // run r's sums of this warp leave the accumulators: into the warp's running total in shared memory when this CTA
+    // holds the unit from its first run, else into this CTA's slot for run r in global memory (the unit's last CTA
+    // adds them in run order); no barrier, the ring keeps streaming
+    auto flush = [&](int r) {
+      const size_t slot = static_cast<size_t>(static_cast<int64_t>(su) * P + r - R0);  // (ra > 0 only)
+      float* gw = p.part + ((static_cast<size_t>(blockIdx.x) * P + slot) * kWarpsM + warp) * kPart;
+#pragma unroll
+      for (int w2 = 0; w2 < (PAIR ? 2 : 1); ++w2) {
+        float* rw = red + (w2 * kWarpsM + warp) * 8 * kRedStrideM;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int row = 2 * static_cast<int>(q) + (c & 1), col = 16 * t + static_cast<int>(g) + 8 * (c >> 1);
+            if (ra == 0) {
+              float& tot = rw[row * kRedStrideM + col];
+              tot = r == 0 ? acc[w2][t][c] : tot + acc[w2][t][c];
+            } else {
+              __stcg(gw + w2 * 1024 + row * 128 + col, acc[w2][t][c]);
+            }
+            acc[w2][t][c] = 0.0f;
+          }
+        }
+      }
+    };
+    int run = ra, left = Lw;
     for (uint32_t i = 0; i < mine; ++i) {
       cp_wait<kStagesM - 2>();
       __syncwarp();
@@ -336,54 +381,58 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
       __syncwarp();
       issue(i + kStagesM - 1);
       cp_commit();
-    }
-    cp_wait<0>();
-    __half* stage = reinterpret_cast<__half*>(smem);  // warp 0's ring, drained: the down-input block's staging (2 KiB)
-    // warps' partials -> shared, summed in warp order
-#pragma unroll
-    for (int w2 = 0; w2 < (PAIR ? 2 : 1); ++w2) {
-      float* rw = red + (w2 * kWarpsM + warp) * 8 * kRedStrideM;
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const int col = 16 * t + static_cast<int>(g), row = 2 * static_cast<int>(q);
-        rw[row * kRedStrideM + col] = acc[w2][t][0];
-        rw[(row + 1) * kRedStrideM + col] = acc[w2][t][1];
-        rw[row * kRedStrideM + col + 8] = acc[w2][t][2];
-        rw[(row + 1) * kRedStrideM + col + 8] = acc[w2][t][3];
+      if (--left == 0 && i + 1 < mine) {
+        flush(run++);
+        left = Lw;
       }
     }
+    cp_wait<0>();
+    flush(run);  // the item's last run (rb - 1)
+    __half* stage = reinterpret_cast<__half*>(smem);  // warp 0's ring, drained: the down-input block's staging (2 KiB)
     __syncthreads();
-    const bool whole = k0 == 0 && k1 == KT;
-    const int64_t u0 = static_cast<int64_t>(su) * KT;  // the unit's first slab in the runs' numbering
-    constexpr int kPart = (PAIR ? 2 : 1) * 8 * 128;
-    for (int idx = tid; idx < kPart; idx += kWarpsM * 32) {
-      const int w2 = idx / 1024, row = (idx / 128) % 8, col = idx % 128;
-      float v = 0.0f;
+    if (ra == 0 && rb == P) {
+      // a whole unit: the warps' totals in warp order
+      for (int idx = tid; idx < kPart; idx += kWarpsM * 32) {
+        const int w2 = idx / 1024, row = (idx / 128) % 8, col = idx % 128;
+        float v = 0.0f;
 #pragma unroll
-      for (int w3 = 0; w3 < kWarpsM; ++w3) v += red[((w2 * kWarpsM + w3) * 8 + row) * kRedStrideM + col];
-      if (whole) red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
-      else __stcg(p.part + (static_cast<size_t>(blockIdx.x) * 2 + (r0 >= u0 ? 0 : 1)) * 2048 + idx, v);
-    }
-    if (!whole) {
-      // a shared unit: runs first .. last of the grid cover it; the one that completes it adds the partials in run
-      // order (run c keeps its partial of the unit its run starts in at end 0, of the unit it ends in at end 1)
-      const int first = static_cast<int>(u0 / run), last = static_cast<int>((u0 + KT - 1) / run);
+        for (int w3 = 0; w3 < kWarpsM; ++w3) v += red[((w2 * kWarpsM + w3) * 8 + row) * kRedStrideM + col];
+        red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
+      }
+    } else {
+      // a unit shared with other CTAs: CTAs cf .. cl of the grid hold its runs; cf, which holds runs 0 .. j0, keeps
+      // every warp's total of them in its slot P - 1, the others each run in its own slot; the last to finish adds
+      // each warp's runs in run order onto that total, then the warps in warp order -- the sums a whole unit makes
+      if (ra == 0)
+        for (int idx = tid; idx < kWarpsM * kPart; idx += kWarpsM * 32) {
+          const int w3 = idx / kPart, w2 = (idx % kPart) / 1024, row = (idx / 128) % 8, col = idx % 128;
+          __stcg(p.part + (static_cast<size_t>(blockIdx.x) * P + P - 1) * kWarpsM * kPart + idx,
+                 red[((w2 * kWarpsM + w3) * 8 + row) * kRedStrideM + col]);
+        }
+      const int64_t u0 = static_cast<int64_t>(su) * P;  // the unit's first run in the ranges' numbering
+      const int cf = static_cast<int>(u0 / per), cl = static_cast<int>((u0 + P - 1) / per);
       __threadfence();
       __syncthreads();
       if (tid == 0) {
         const int prior = atomicAdd(done + unit, 1);
-        s_last = prior == last - first;
+        s_last = prior == cl - cf;
         if (s_last) done[unit] = 0;  // ready for the next call
       }
       __syncthreads();
       if (!s_last) continue;
       __threadfence();
+      const int j0 = static_cast<int>((static_cast<int64_t>(cf) + 1) * per - 1 - u0);  // < P - 1: cf ends inside
       for (int idx = tid; idx < kPart; idx += kWarpsM * 32) {
         const int w2 = idx / 1024, row = (idx / 128) % 8, col = idx % 128;
         float v = 0.0f;
-        for (int c = first; c <= last; ++c) {
-          const int end = static_cast<int64_t>(c) * run >= u0 ? 0 : 1;
-          v += __ldcg(p.part + (static_cast<size_t>(c) * 2 + end) * 2048 + idx);
+        for (int w3 = 0; w3 < kWarpsM; ++w3) {
+          float tw = __ldcg(p.part + ((static_cast<size_t>(cf) * P + P - 1) * kWarpsM + w3) * kPart + idx);
+          for (int r = j0 + 1; r < P; ++r) {
+            const int64_t R = u0 + r, c = R / per;
+            tw += __ldcg(p.part + ((static_cast<size_t>(c) * P + static_cast<size_t>(R - c * per)) * kWarpsM + w3) *
+                                      kPart + idx);
+          }
+          v += tw;
         }
         red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
       }
@@ -502,7 +551,7 @@ constexpr int kMaxCtasPerSm = 4;
 size_t fixed_bytes(int width, int sms) {
   const size_t ints = kIntsM;
   const size_t done = 2 * static_cast<size_t>(kMaxSlots) * (width / 128);
-  const size_t part = static_cast<size_t>(sms) * kMaxCtasPerSm * 2 * 2048;
+  const size_t part = static_cast<size_t>(sms) * kMaxCtasPerSm * kMaxRuns * kWarpsM * 1024;
   return (ints + done + part) * 4;
 }
 
@@ -535,8 +584,13 @@ cudaError_t launch_moe_gemv(const MoeParams& p, int sms, cudaStream_t st) {
   int per_sm = 0;  // resident CTAs per SM: the persistent grid is exactly one wave
   if (cudaError_t e = kernel_setup(setup, kern, kWarpsM * 32, smem, false, &per_sm, moe_ctas_per_sm()); e != cudaSuccess)
     return e;
+  // the grid's partial slots ([grid][P][4 warps][kPart]) must fit the workspace's (sized for kMaxCtasPerSm CTAs per
+  // SM of kMaxRuns slots of 1024 floats): at most 2 CTAs per SM for gate|up at kMaxRuns runs
+  const int kt = (PAIR ? p.hidden : p.inter_full) / 16;
+  const int runs = (kt + moe_run_slabs(kt) - 1) / moe_run_slabs(kt);
+  const int fit = kMaxCtasPerSm * kMaxRuns * 1024 / (runs * (PAIR ? 2048 : 1024));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sms * per_sm);
+  cfg.gridDim = dim3(sms * (per_sm < fit ? per_sm : fit));
   cfg.blockDim = dim3(kWarpsM * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
