@@ -78,7 +78,9 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   const int t0 = static_cast<int>(rank) * KR;        // first slab
   uint8_t* xps = smem;                                                  // [KR][RG][32][8 B]
   uint8_t* ring = smem + p.xp_bytes + warp * (kStages5 * kUnitBytes);
-  float* red = reinterpret_cast<float*>(smem + p.xp_bytes + kW5 * kStages5 * kUnitBytes);  // [kW5][rows][kRed5]
+  // after the main loop, the reduction buffer [kW5][rows][kRed5] overlays the rotated input and the rings (both dead
+  // by then), and the exchange's staging rows follow it: the launch takes the larger of the two footprints
+  float* red = reinterpret_cast<float*>(smem);
 
   // segment of this column block
   int s = 0;
@@ -202,6 +204,7 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
     cp_async_commit();
   }
   cp_async_wait<0>();
+  __syncthreads();  // every warp is past the main loop: the rotated input and the rings are free
 
   // ---- the CTA's partial: the warps' sums in warp order, into red[0]
   float* rw = red + warp * rows * kRed5;
@@ -264,7 +267,7 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
       }
     const int64_t col = c0 + (cbg * 128 - seg_c0);  // first gathered column of this block
     // each warp: its row's 128 outputs through a shared-memory staging row, then 16-byte stores into every rank
-    uint8_t* stage = ring;  // this warp's weight ring: drained (cp.async waited above), at least 2 KiB
+    uint8_t* stage = smem + static_cast<size_t>(kW5) * rows * kRed5 * 4 + warp * 512u;  // this warp's row, after red
     const uint32_t row_bytes = 128u * static_cast<uint32_t>(esize);
     for (int row = static_cast<int>(warp); row < rows; row += kW5) {
       float v[4];
@@ -315,8 +318,9 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
 template <int K, int RG, bool IMMA, int ST>
 static cudaError_t launch5_t(const GemvParams& p, cudaStream_t st, bool pdl) {
   auto kern = gemv5_kernel<K, RG, IMMA, ST>;
-  const size_t smem = static_cast<size_t>(p.xp_bytes) + static_cast<size_t>(kW5) * ST * 8u * 32u * K +
-                      static_cast<size_t>(kW5) * p.rows * kRed5 * 4;
+  const size_t loop = static_cast<size_t>(p.xp_bytes) + static_cast<size_t>(kW5) * ST * 8u * 32u * K;
+  const size_t tail = static_cast<size_t>(kW5) * p.rows * kRed5 * 4 + kW5 * 512u;
+  const size_t smem = loop > tail ? loop : tail;
   static KernelSetup setup;
   if (cudaError_t e = kernel_setup(setup, kern, kT5, smem, true); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -355,9 +359,12 @@ static cudaError_t launch5_k(const GemvParams& p, int K, cudaStream_t st, bool p
   }
 }
 
+// The launch's shared memory: the main loop's (rotated input + rings) or, overlaying it, the tail's (reduction buffer
+// + exchange staging), whichever is larger.
 static size_t gemv5_smem_for(int K, int stages, int KR, int row_groups, int rows) {
-  return static_cast<size_t>(KR) * row_groups * 256 + static_cast<size_t>(kW5) * stages * 8u * 32u * K +
-         static_cast<size_t>(kW5) * rows * kRed5 * 4;
+  const size_t loop = static_cast<size_t>(KR) * row_groups * 256 + static_cast<size_t>(kW5) * stages * 8u * 32u * K;
+  const size_t tail = static_cast<size_t>(kW5) * rows * kRed5 * 4 + kW5 * 512u;
+  return loop > tail ? loop : tail;
 }
 
 bool gemv5_geometry(GemvParams& p, int K, int sms, int row_groups, int split_override, const char** why) {
