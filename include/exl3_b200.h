@@ -346,6 +346,20 @@ exl3_verdict exl3_encode_trellis(const float *target, int32_t in_features, int32
  * capture.  All calls share the array: calls that overlap on the GPU race -- order them on one stream. */
 exl3_verdict exl3_matmul_noalloc(const exl3_weight *w, const exl3_tensor *x, void *stream, exl3_tensor *out);
 
+/* Resident decoded matrices (QuantTable.resident / resident_pending, plugins/turboexl3_qwen38/overlay/mlx_serve/abi/
+ * quant.zig:96-101: memory for speed).  Keeps each of the `count` weights' decoded matrices from its first prefill
+ * (GEMM) call on, so later prefill calls skip the weight decode: device memory for the tensor-core GEMM's operand
+ * image of W_hat^T, f16, about 2 x in x out bytes per group, is reserved here (calls stay allocation-free) and filled
+ * by the first call.  Admitted only if everything kept, old and new, fits in `room` bytes (0: no bound), else refused
+ * EXL3_TOO_LARGE and nothing changes; `bytes` (may be null) receives the bytes kept.  A weight already kept is kept
+ * once.  `count` 0 drops every kept matrix.  exl3_release drops the matrices of the weight it frees; a borrowed weight
+ * (exl3_weight_view) must be dropped before its memory is freed or reused.  The first prefill call on a kept weight
+ * fills it on that call's stream: calls on other streams must not run before that call is ordered before them. */
+exl3_verdict exl3_resident(const exl3_weight *ws, int32_t count, uint64_t room, void *stream, uint64_t *bytes);
+
+/* The bytes exl3_resident admitted and no prefill call has filled yet (QuantTable.resident_pending). */
+uint64_t exl3_resident_pending(void);
+
 /* Device error bits the kernels recorded on `device`; `clear` resets them. */
 #define EXL3_ERR_WAIT_TIMEOUT 1u  /* a bounded mbarrier wait gave up (the kernel left its loop and returned) */
 #define EXL3_ERR_BAD_SHAPE 2u     /* a launch saw a shape its host validation should have refused */

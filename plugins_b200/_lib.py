@@ -31,7 +31,7 @@ EXPORTS = (
     "exl3_tp_create", "exl3_tp_connect", "exl3_tp_destroy", "exl3_tp_begin", "exl3_matmul_tp", "exl3_tp_gather",
     "exl3_weight_view", "exl3_weight_stack",
     "exl3_decode_dense", "exl3_encode_trellis", "exl3_matmul_noalloc", "exl3_device_error", "exl3_version",
-    "exl3_model_claims", "exl3_model_parse",
+    "exl3_model_claims", "exl3_model_parse", "exl3_resident", "exl3_resident_pending",
 )
 
 
@@ -222,6 +222,10 @@ def lib() -> ctypes.CDLL:
             L.exl3_matmul_noalloc.argtypes = [P(Weight), P(Tensor), ctypes.c_void_p, P(Tensor)]
             L.exl3_device_error.restype = Verdict
             L.exl3_device_error.argtypes = [ctypes.c_int32, P(ctypes.c_uint32), ctypes.c_int32]
+            L.exl3_resident.restype = Verdict
+            L.exl3_resident.argtypes = [P(Weight), ctypes.c_int32, ctypes.c_uint64, ctypes.c_void_p, P(ctypes.c_uint64)]
+            L.exl3_resident_pending.restype = ctypes.c_uint64
+            L.exl3_resident_pending.argtypes = []
             L.exl3_version.restype = ctypes.c_char_p
             L.exl3_version.argtypes = []
             _lib = L

@@ -372,6 +372,37 @@ exl3_verdict upload_stack(const exl3_load_ctx* ctx, const std::vector<LinearPart
   return kOk;
 }
 
+// ------------------------------------------------------------------ resident decoded matrices
+
+// A kept weight's GEMM B image (W_hat^T blocks of 128 columns x 64 k, f16; the layout images_kernel writes), per
+// group, with two column blocks of padding so a ragged last tile's reads stay inside it.  Keyed on the weight's
+// device pointers and shape.
+struct Resident {
+  int device;
+  const uint16_t *trellis, *suh, *svh;
+  int groups, in_f, out_f, n, nseg;
+  size_t group_bytes;
+  uint8_t* image;
+  bool filled;
+};
+std::mutex g_res_mu;
+std::vector<std::unique_ptr<Resident>> g_res;
+
+size_t resident_group_bytes(const exl3_weight* w) {
+  return static_cast<size_t>(w->out_features / 128 + 2) * w->in_features * 256;  // in/64 blocks of 16 KiB per column block
+}
+
+bool resident_is(const Resident& r, const exl3_weight* w) {
+  return r.device == w->device && r.trellis == w->trellis && r.suh == w->suh && r.svh == w->svh &&
+         r.groups == w->groups && r.in_f == w->in_features && r.out_f == w->out_features && r.n == w->n &&
+         r.nseg == w->nseg;
+}
+
+void resident_free(Resident& r) {
+  DeviceGuard guard(r.device);
+  cudaFree(r.image);
+}
+
 exl3_verdict check_weight(const exl3_weight* w) {
   if (!w || w->size != sizeof(exl3_weight) || !w->trellis || !w->suh || !w->svh)
     return refuse(EXL3_FAILED, "exl3_b200: not a loaded weight");
@@ -428,9 +459,31 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
   uint8_t* a_img = d->image;
   uint8_t* b_img = d->image + static_cast<size_t>(mc) * row_bytes;
   // a multiple of the tile width, so a ragged last tile's reads stay inside the B region
-  const int64_t nc_cap = static_cast<int64_t>((d->image_bytes - static_cast<size_t>(mc) * row_bytes) / row_bytes) / bn * bn;
+  int64_t nc_cap = static_cast<int64_t>((d->image_bytes - static_cast<size_t>(mc) * row_bytes) / row_bytes) / bn * bn;
   if (nc_cap < bn) return refuse(EXL3_TOO_LARGE, "exl3_b200: in_features too large for the prefill image region");
   const int gcount = grouped ? groups : 1;
+  // a kept weight: its B image is decoded once (the first call fills it, on this stream) and read from there
+  uint8_t* kept = nullptr;
+  size_t kept_group = 0;
+  bool fill = false;
+  {
+    std::lock_guard<std::mutex> lk(g_res_mu);
+    for (auto& r : g_res)
+      if (resident_is(*r, w)) {
+        kept = r->image;
+        kept_group = r->group_bytes;
+        fill = !r->filled;
+        r->filled = true;
+        break;
+      }
+  }
+  if (kept) {
+    nc_cap = (static_cast<int64_t>(out_f) + bn - 1) / bn * bn;  // no column chunks: the B image is the kept one
+    for (int g = 0; fill && g < gcount; ++g)
+      if (exl3::launch_images(nullptr, x_dtype, 0, 0, 0, nullptr, 0, nullptr, w->trellis + static_cast<size_t>(g) * tile_halfs,
+                              in_f, out_f, 0, out_f, w->n, kept + static_cast<size_t>(g) * kept_group, st) != cudaSuccess)
+        return refuse(EXL3_FAILED, "exl3_b200: resident image launch failed");
+  }
   for (int g = 0; g < gcount; ++g) {
     const int64_t x_stride = grouped ? static_cast<int64_t>(groups) * in_f : in_f;
     const uint8_t* xg = static_cast<const uint8_t*>(x) + static_cast<size_t>(g) * in_f * xsz;
@@ -457,14 +510,15 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
           // the A image with the first column chunk's B image, in one launch
           if (exl3::launch_images(xg + static_cast<size_t>(r0) * x_stride * xsz, x_dtype, x_stride, m, mp, suh,
                                   (flags & EXL3_MATMUL_PREPARED) ? 1 : 0, j0 == 0 ? a_img : nullptr, trg, in_f, out_f,
-                                  c0 + j0, nc, w->n, b_img, st) != cudaSuccess)
+                                  c0 + j0, nc, w->n, kept ? nullptr : b_img, st) != cudaSuccess)
             return refuse(EXL3_FAILED, "exl3_b200: prefill operand images launch failed");
           mark(1);
           const int shape = gemm_shape_for(m, nc, d->sms);
           const int tbm = exl3::gemm_block_m(shape), tbn = exl3::gemm_block_n(shape);
           exl3::GemmParams gp{};
           gp.a_img = a_img;
-          gp.b_img = b_img;
+          gp.b_img = kept ? kept + static_cast<size_t>(g) * kept_group + static_cast<size_t>((c0 + j0) / 128) * in_f * 256
+                          : b_img;
           gp.svh = svh + j0;
           uint8_t* yp = yseg + (static_cast<size_t>(r0) * ystride + j0) * ysz;
           gp.y = yp;
@@ -787,6 +841,16 @@ exl3_verdict exl3_load_bank(const exl3_load_ctx* ctx, exl3_str name, uint32_t in
 
 void exl3_release(exl3_weight* w) {
   if (!w) return;
+  if (w->size == sizeof(exl3_weight)) {  // its kept matrices go with it
+    std::lock_guard<std::mutex> lk(g_res_mu);
+    for (size_t i = 0; i < g_res.size();)
+      if (resident_is(*g_res[i], w)) {
+        resident_free(*g_res[i]);
+        g_res.erase(g_res.begin() + static_cast<std::ptrdiff_t>(i));
+      } else {
+        ++i;
+      }
+  }
   if ((w->flags & EXL3_WEIGHT_OWNED) && w->size == sizeof(exl3_weight)) {
     DeviceGuard guard(w->device);
     cudaFree(w->trellis);
@@ -1028,6 +1092,59 @@ exl3_verdict exl3_encode_trellis(const float* target, int32_t in_features, int32
   if (exl3::launch_encode(target, in_features, out_features, n, trellis, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_b200: encoder launch failed");
   return kOk;
+}
+
+exl3_verdict exl3_resident(const exl3_weight* ws, int32_t count, uint64_t room, void* stream, uint64_t* bytes) {
+  (void)stream;  // the memory is reserved here and filled by the first prefill call, on that call's stream
+  std::lock_guard<std::mutex> lk(g_res_mu);
+  uint64_t held = 0;
+  if (count == 0) {
+    for (auto& r : g_res) resident_free(*r);
+    g_res.clear();
+  } else {
+    if (!ws || count < 0) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
+    for (const auto& r : g_res) held += static_cast<uint64_t>(r->group_bytes) * r->groups;
+    std::vector<const exl3_weight*> add;
+    uint64_t more = 0;
+    for (int i = 0; i < count; ++i) {
+      const exl3_weight* w = &ws[i];
+      exl3_verdict v = check_weight(w);
+      if (v.code != EXL3_OK) return v;
+      if ((w->flags & EXL3_WEIGHT_BANK) && !(w->flags & EXL3_WEIGHT_GROUPED))
+        return refuse(EXL3_UNSUPPORTED, "exl3_b200: routed banks are not kept (their calls are decode GEMVs)");
+      bool kept = false;
+      for (const auto& r : g_res) kept = kept || resident_is(*r, w);
+      for (const exl3_weight* a : add) kept = kept || (a->device == w->device && a->trellis == w->trellis);
+      if (kept) continue;
+      add.push_back(w);
+      more += static_cast<uint64_t>(resident_group_bytes(w)) * w->groups;
+    }
+    if (room > 0 && held + more > room) return refuse(EXL3_TOO_LARGE, "exl3_b200: the kept matrices pass the room");
+    std::vector<std::unique_ptr<Resident>> made;
+    for (const exl3_weight* w : add) {
+      auto r = std::make_unique<Resident>();
+      *r = Resident{w->device, w->trellis, w->suh, w->svh, w->groups, w->in_features, w->out_features, w->n, w->nseg,
+                    resident_group_bytes(w), nullptr, false};
+      DeviceGuard guard(w->device);
+      if (cudaMalloc(&r->image, r->group_bytes * w->groups) != cudaSuccess) {
+        for (auto& m : made) resident_free(*m);
+        return refuse(EXL3_TOO_LARGE, "exl3_b200: out of device memory for the kept matrices");
+      }
+      made.push_back(std::move(r));
+    }
+    for (auto& r : made) g_res.push_back(std::move(r));
+    held += more;
+  }
+  if (bytes) *bytes = held;
+  return kOk;
+}
+
+uint64_t exl3_resident_pending(void) {
+  std::lock_guard<std::mutex> lk(g_res_mu);
+  uint64_t pending = 0;
+  for (const auto& r : g_res)
+    if (!r->filled) pending += static_cast<uint64_t>(r->group_bytes) * r->groups;
+  return pending;
 }
 
 exl3_verdict exl3_device_error(int32_t device, uint32_t* bits, int32_t clear) {

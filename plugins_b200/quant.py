@@ -101,8 +101,10 @@ class Weight:
         self._keep = ()
 
     def __del__(self):
+        # an owned weight frees its memory; a borrowed one drops its kept matrices (exl3_resident), whose key -- the
+        # device pointers -- a later weight may reuse once the tensors go
         try:
-            if self.raw.size and (self.raw.flags & L.WEIGHT_OWNED):
+            if self.raw.size:
                 self.release()
         except Exception:
             pass
@@ -333,6 +335,21 @@ def ep_combine(back: torch.Tensor, back_slot: torch.Tensor, scores: torch.Tensor
     check(L.lib().exl3_ep_combine(ctypes.byref(_tensor(back)), ctypes.byref(_tensor(back_slot)),
                                   ctypes.byref(_tensor(scores)), ctypes.byref(sh), _stream(stream),
                                   ctypes.byref(_tensor(out))))
+
+
+def resident(ws: list[Weight], room: int = 0, stream=None) -> int:
+    """quant.zig:96-99 ``resident``: keep the weights' decoded matrices from their first prefill call on (memory for
+    speed), if everything kept fits in ``room`` bytes (0: no bound); returns the bytes kept.  An empty list drops every
+    kept matrix."""
+    arr = (L.Weight * max(len(ws), 1))(*[w.raw for w in ws])
+    got = ctypes.c_uint64(0)
+    check(L.lib().exl3_resident(arr, len(ws), int(room), _stream(stream), ctypes.byref(got)))
+    return got.value
+
+
+def resident_pending() -> int:
+    """quant.zig:100-101 ``resident_pending``: the bytes ``resident`` admitted that no prefill call has filled yet."""
+    return int(L.lib().exl3_resident_pending())
 
 
 def device_error(device: int = 0, clear: bool = False) -> int:

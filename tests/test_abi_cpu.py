@@ -91,6 +91,17 @@ def test_matmul_rejects_a_null_weight_before_any_launch():
     assert v.code == L.EXL3_FAILED
 
 
+def test_resident_keeps_nothing_and_refuses_a_bad_weight_without_a_gpu_call():
+    # quant.zig:96-101: an empty list drops every kept matrix; a weight that is not loaded is refused before any
+    # allocation
+    got = ctypes.c_uint64(7)
+    v = L.lib().exl3_resident(ctypes.POINTER(L.Weight)(), 0, 0, None, ctypes.byref(got))
+    assert v.code == L.EXL3_OK and got.value == 0 and L.lib().exl3_resident_pending() == 0
+    bad = L.Weight()
+    v = L.lib().exl3_resident(ctypes.byref(bad), 1, 0, None, ctypes.byref(got))
+    assert v.code == L.EXL3_FAILED and b"not a loaded weight" in v.why
+
+
 def test_bench_counts_launches_with_the_librarys_gemv_selection():
     """bench.py's gpu_launches claim mirrors the library's decode-GEMV selection (exl3_abi.cu run_linear,
     exl3_gemv6.cu launch_gemv6): the thresholds and the in-CTA rotation limits it restates are the library's."""
