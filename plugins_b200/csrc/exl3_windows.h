@@ -47,7 +47,9 @@ template <int N>
 EXL3_HD void lane_windows(const uint32_t* tile_words, const LaneWin<N>& lw, uint32_t (&w)[8]) {
   const uint32_t a = tile_words[lw.o0], b = tile_words[lw.o1], c = tile_words[lw.o2];
   const uint32_t vlo = funnel_r(c, b, lw.sh), vhi = funnel_r(b, a, lw.sh);  // the 64 bits below E
+#if defined(__CUDACC__)
 #pragma unroll
+#endif
   for (int j = 0; j < 8; ++j) {
     const int s = N / 2 - ((j + 1) * N) / 16;  // compile-time per j
     uint32_t v;
