@@ -67,6 +67,28 @@ def test_decode_dense_bit_exact(Q, E, oracle, n, dp4a):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("n", [24, 32, 40, 48])
+@pytest.mark.parametrize("dp4a", [False, True])
+def test_frac_tiles_decode_on_gpu(Q, oracle, n, dp4a):
+    # the real exllamav3 tiles at 1.5-3 bits (plugins/turboexl3_ds41/src/frac_tiles.json, frac_test.zig:23-57) laid
+    # into a 128 x 128 layer (random words elsewhere) decode on the GPU to their pinned f16 bits, tile for tile
+    tiles = [t for t in json.load(open(os.path.join(GOLD, "frac_tiles.json")))["tiles"] if t["n"] == n]
+    assert 14 <= len(tiles) <= 64
+    rng = np.random.default_rng(n)
+    words = rng.integers(0, 65536, (8, 8, n), dtype=np.uint16)
+    for i, t in enumerate(tiles):
+        words[i // 8, i % 8] = t["words"]
+    tr = torch.from_numpy(words.view(np.int16)).cuda()
+    suh = torch.ones(128, dtype=torch.float16, device="cuda")
+    svh = torch.ones(128, dtype=torch.float16, device="cuda")
+    w = Q.weight_from_tensors(tr, suh, svh)
+    got = Q.decode_dense(w, dp4a=dp4a).view(torch.uint16).cpu().numpy()
+    for i, t in enumerate(tiles):
+        ti, tj = i // 8, i % 8
+        assert got[16 * ti:16 * ti + 16, 16 * tj:16 * tj + 16].reshape(-1).tolist() == t["expect"], t["src"]
+    assert np.array_equal(got, oracle.reconstruct_inner(words, 128, 128, n))
+
+
 @pytest.mark.parametrize("name", ["down_k2", "gate_up_k2", "down", "gate_up"])
 def test_golden_planes_on_gpu(Q, oracle, name):
     # the manifest's splitmix64 planes decode on the GPU to the pinned W_hat digest, and the one-hot rows through
