@@ -9,10 +9,10 @@
 // columns t/4 and t/4 + 8 -- exactly the A fragment of W^T (rows = output columns, cols = k).
 #pragma once
 #include <cuda_fp16.h>
-
-#include "exl3_windows.h"
 #include <cuda_bf16.h>
 #include <stdint.h>
+
+#include "exl3_windows.h"
 
 namespace exl3 {
 
