@@ -264,7 +264,7 @@ DeviceState* device_state(int dev) {
   return &g_dev[dev];
 }
 
-bool rate_served(int n) { return n % 16 == 0 && n >= 16 && n <= 96; }  // integer K 1..6
+bool rate_served(int n) { return exl3::rate_served_n(n); }
 
 exl3_verdict check_linear_shape(int groups, int in_f, int out_f, int n) {
   if (groups < 1 || in_f <= 0 || out_f <= 0) return refuse(EXL3_UNSUPPORTED, "exl3_b200: empty weight");
@@ -272,7 +272,7 @@ exl3_verdict check_linear_shape(int groups, int in_f, int out_f, int n) {
     return refuse(EXL3_UNSUPPORTED, "exl3_b200: in and out features must be multiples of 128 (the Hadamard blocks)");
   if (!(n % 2 == 0 && n >= 16 && n <= 128)) return refuse(EXL3_UNSUPPORTED, "exl3_b200: not an admitted rate (n even, 16..128)");
   if (!rate_served(n))
-    return refuse(EXL3_UNSUPPORTED, "exl3_b200: fractional or >6-bit rates are not served by the sm_100a kernels");
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: rates off the half-bit grid or above 6 bits are not served by the sm_100a kernels");
   if (out_f / 128 > static_cast<int>(kCounterCount)) return refuse(EXL3_TOO_LARGE, "exl3_b200: out_features too large");
   return kOk;
 }
@@ -567,7 +567,6 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
   const int split = sp ? atoi(sp) : 0;
   const int in_f = w->in_features, out_f = w->out_features, groups = w->groups;
   const bool grouped = (w->flags & EXL3_WEIGHT_GROUPED) != 0;
-  const int K = w->n / 16;
   const bool imma = (flags & EXL3_MATMUL_DP4A) == 0;
   const size_t tile_halfs = static_cast<size_t>(in_f / 16) * (out_f / 16) * w->n;
   const size_t xsz = x_dtype == EXL3_F32 ? 4 : 2;
@@ -607,18 +606,18 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
       // not depend on the rows batched with it), the cluster-split one below
       const bool v6 = imma && (gv_pick == 6 || (gv_pick == 0 && exl3::gemv6_prefers(gp)));
       if (v6 && exl3::gemv6_scratch_bytes(gp, d->sms) <= d->partial_floats * 4) {
-        if (exl3::launch_gemv6(gp, K, d->sms, d->partials, d->counters, st) != cudaSuccess)
+        if (exl3::launch_gemv6(gp, w->n, d->sms, d->partials, d->counters, st) != cudaSuccess)
           return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
         continue;
       }
       // the cluster-split GEMV where a split fits (every served width), else the grid-stride one with global partials
-      if (gemv_v5 && exl3::gemv5_geometry(gp, K, d->sms, rg, split, &why)) {
-        if (exl3::launch_gemv5(gp, K, rg, imma, st, true) != cudaSuccess)
+      if (gemv_v5 && exl3::gemv5_geometry(gp, w->n, d->sms, rg, split, &why)) {
+        if (exl3::launch_gemv5(gp, w->n, rg, imma, st, true) != cudaSuccess)
           return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
         continue;
       }
       if (!exl3::gemv_geometry(gp, d->sms, rg, d->partial_floats, &why)) return refuse(EXL3_TOO_LARGE, why);
-      if (exl3::launch_gemv(gp, K, rg, imma, st, true) != cudaSuccess)
+      if (exl3::launch_gemv(gp, w->n, rg, imma, st, true) != cudaSuccess)
         return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
     }
   }
@@ -661,7 +660,7 @@ exl3_verdict exl3_validate(exl3_str block_json, exl3_str config_json) {
     if (std::fabs(scaled - n) > 1e-6 || n < 16 || n > 128 || std::fmod(n, 2.0) != 0)
       return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3RateUnsupported");
     if (!rate_served(static_cast<int>(n)))
-      return refuse(EXL3_UNSUPPORTED, "exl3_b200: fractional or >6-bit rates are not served by the sm_100a kernels");
+      return refuse(EXL3_UNSUPPORTED, "exl3_b200: rates off the half-bit grid or above 6 bits are not served by the sm_100a kernels");
   }
   return kOk;
 }
@@ -694,7 +693,7 @@ const char* check_model_block(const JVal& o, bool bank, uint32_t* rate_n) {
     const JVal* k = o.get("k");
     if (!k || k->kind != JVal::Num) return "turboexl3_qwen38: Exl3RateUnsupported";
     const double scaled = k->num * 16.0, n = std::round(scaled);
-    if (!std::isfinite(scaled) || std::fabs(scaled - n) > 1e-6 || n < 16 || n > 96 || std::fmod(n, 16.0) != 0)
+    if (!std::isfinite(scaled) || std::fabs(scaled - n) > 1e-6 || !exl3::rate_served_n(static_cast<int>(n)))
       return "turboexl3_qwen38: Exl3RateUnsupported";
     *rate_n = static_cast<uint32_t>(n);
   }
@@ -958,8 +957,8 @@ exl3_verdict exl3_matmul_tp(const exl3_weight* w, const exl3_tensor* x, exl3_tp*
   gp.tp_meta_bytes = static_cast<uint32_t>(rows * total * esize);
   const int rg = rows <= 8 ? 1 : 2;
   const char* why = nullptr;
-  if (!exl3::gemv5_geometry(gp, w->n / 16, d->sms, rg, 0, &why)) return refuse(EXL3_UNSUPPORTED, why);
-  if (exl3::launch_gemv5(gp, w->n / 16, rg, true, static_cast<cudaStream_t>(stream), true) != cudaSuccess)
+  if (!exl3::gemv5_geometry(gp, w->n, d->sms, rg, 0, &why)) return refuse(EXL3_UNSUPPORTED, why);
+  if (exl3::launch_gemv5(gp, w->n, rg, true, static_cast<cudaStream_t>(stream), true) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_matmul_tp: GEMV launch failed");
   return kOk;
 }
@@ -1089,6 +1088,7 @@ exl3_verdict exl3_encode_trellis(const float* target, int32_t in_features, int32
   if (!target || !trellis) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
   exl3_verdict v = check_linear_shape(1, in_features, out_features, n);
   if (v.code != EXL3_OK) return v;
+  if (n % 16 != 0) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the encoder searches whole-bit trellises only");
   if (exl3::launch_encode(target, in_features, out_features, n, trellis, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_b200: encoder launch failed");
   return kOk;

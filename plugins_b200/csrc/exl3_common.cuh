@@ -12,6 +12,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "exl3_windows.h"
+
 namespace exl3 {
 
 constexpr uint32_t kMul1Mult = 0x83DCD12Du;
@@ -193,6 +195,22 @@ __device__ __forceinline__ void lane_codewords(const uint32_t* tile_words, const
       else v = __funnelshift_r(vlo, vhi, s);
       w[j] = v & 0xFFFFu;
     }
+  }
+}
+
+// A tile of N halfwords (N = 16 x bits per weight; half-bit rates included): whole-bit rates take the extraction
+// above, half-bit rates the general rule of exl3_windows.h (the same windows: both follow the bitstream rule).
+template <int N>
+__device__ __forceinline__ void tile_codewords(const uint32_t* tile_words, const LaneWin<N>& lw, uint32_t (&w)[8]) {
+  if constexpr (N % 16 == 0) {
+    LaneWindows<N / 16> lk;
+    lk.o0 = lw.o0;
+    lk.o1 = lw.o1;
+    lk.o2 = lw.o2;
+    lk.sh = lw.sh;
+    lane_codewords<N / 16>(tile_words, lk, w);
+  } else {
+    lane_windows<N>(tile_words, lw, w);
   }
 }
 

@@ -10,7 +10,7 @@
 
 namespace exl3 {
 
-template <int K, bool IMMA>
+template <int N, bool IMMA>
 __global__ void __launch_bounds__(256) decode_dense_kernel(const uint16_t* __restrict__ trellis, int in_features,
                                                            int out_features, uint16_t* __restrict__ out) {
   const uint32_t lane = threadIdx.x & 31u;
@@ -19,11 +19,11 @@ __global__ void __launch_bounds__(256) decode_dense_kernel(const uint16_t* __res
   const size_t tile = static_cast<size_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (tile >= tiles) return;  // warp-uniform
   const int tk = static_cast<int>(tile / ot), tn = static_cast<int>(tile % ot);
-  const uint32_t* tw = reinterpret_cast<const uint32_t*>(trellis + tile * (16 * K));
-  LaneWindows<K> lw;
+  const uint32_t* tw = reinterpret_cast<const uint32_t*>(trellis + tile * N);
+  LaneWin<N> lw;
   lw.init(lane);
   uint32_t w[8], a[4];
-  lane_codewords<K>(tw, lw, w);
+  tile_codewords<N>(tw, lw, w);
   const uint32_t g = lane >> 2, q = lane & 3u;
   if constexpr (IMMA) {
     ImmaIndicator ind;
@@ -58,27 +58,20 @@ __global__ void __launch_bounds__(256) decode_dense_kernel(const uint16_t* __res
 }
 
 template <bool IMMA>
-static cudaError_t launch_dd(const uint16_t* trellis, int in_features, int out_features, int K, uint16_t* out,
+static cudaError_t launch_dd(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
                              cudaStream_t st) {
   const size_t tiles = static_cast<size_t>(in_features / 16) * (out_features / 16);
   const dim3 grid(static_cast<unsigned>((tiles + 7) / 8)), block(256);
-  switch (K) {
-    case 1: decode_dense_kernel<1, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    case 2: decode_dense_kernel<2, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    case 3: decode_dense_kernel<3, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    case 4: decode_dense_kernel<4, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    case 5: decode_dense_kernel<5, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    case 6: decode_dense_kernel<6, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    default: return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  const bool served = with_rate(n, [&](auto N) {
+    decode_dense_kernel<decltype(N)::value, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out);
+  });
+  return served ? cudaGetLastError() : cudaErrorInvalidValue;
 }
 
 cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
                                 int imma, cudaStream_t st) {
-  if (n % 16 != 0) return cudaErrorInvalidValue;
-  return imma ? launch_dd<true>(trellis, in_features, out_features, n / 16, out, st)
-              : launch_dd<false>(trellis, in_features, out_features, n / 16, out, st);
+  return imma ? launch_dd<true>(trellis, in_features, out_features, n, out, st)
+              : launch_dd<false>(trellis, in_features, out_features, n, out, st);
 }
 
 }  // namespace exl3

@@ -215,19 +215,19 @@ __device__ __forceinline__ void prep_job(const ImageJobs& j, int64_t job, uint32
 // Decode job: kDecodeTilesPerWarp consecutive 16x16 tiles of one k-row (contiguous in the trellis).  Each lane holds
 // one column's four consecutive k per tile (the IMMA byte-sum order) and writes them as one 8-byte store; a warp's
 // stores fill whole 32-byte sectors.
-template <int K>
+template <int N>
 __device__ __forceinline__ void decode_job(const ImageJobs& j, int64_t job, uint32_t lane) {
   const int groups = j.ncol_tiles / kDecodeTilesPerWarp;
   const int tk = static_cast<int>(job / groups), tj0 = static_cast<int>(job % groups) * kDecodeTilesPerWarp;
   const uint32_t* tw =
-      reinterpret_cast<const uint32_t*>(j.trellis + (static_cast<size_t>(tk) * j.out_tiles + j.tn0 + tj0) * (16 * K));
-  LaneWindows<K> lw;
+      reinterpret_cast<const uint32_t*>(j.trellis + (static_cast<size_t>(tk) * j.out_tiles + j.tn0 + tj0) * N);
+  LaneWin<N> lw;
   lw.init(lane);
   ImmaIndicator ind;
   ind.init(lane);
   uint32_t w[kDecodeTilesPerWarp][8];
 #pragma unroll
-  for (int t = 0; t < kDecodeTilesPerWarp; ++t) lane_codewords<K>(tw + t * 8 * K, lw, w[t]);
+  for (int t = 0; t < kDecodeTilesPerWarp; ++t) tile_codewords<N>(tw + t * (N / 2), lw, w[t]);
   const uint32_t g = lane >> 2, q = lane & 3u;
   const int kbs = j.in_features / kImgK;
   const uint32_t kin = static_cast<uint32_t>(tk & 3) * 16u + 4u * q;
@@ -244,11 +244,11 @@ __device__ __forceinline__ void decode_job(const ImageJobs& j, int64_t job, uint
 }
 
 // Decode warps first (the longer jobs), then prepare warps; every job is one warp.
-template <int K>
+template <int N>
 __global__ void __launch_bounds__(256) images_kernel(const ImageJobs j) {
   const uint32_t lane = threadIdx.x & 31u;
   const int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);  // warp-uniform
-  if (job < j.decode_jobs) decode_job<K>(j, job, lane);
+  if (job < j.decode_jobs) decode_job<N>(j, job, lane);
   else if (job < j.decode_jobs + j.prep_jobs) prep_job(j, job - j.decode_jobs, lane);
 }
 
@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
 cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, const uint16_t* suh,
                           int prepared, uint8_t* a_img, const uint16_t* trellis, int in_features, int out_features,
                           int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st) {
-  if (in_features % 128 != 0 || n % 16 != 0) return cudaErrorInvalidValue;
+  if (in_features % 128 != 0 || !rate_served_n(n)) return cudaErrorInvalidValue;
   ImageJobs j{};
   j.in_features = in_features;
   if (a_img) {
@@ -496,16 +496,8 @@ cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, 
   const int64_t warps = j.prep_jobs + j.decode_jobs;
   if (warps == 0) return cudaSuccess;
   const dim3 grid(static_cast<unsigned>((warps + 7) / 8)), block(256);
-  switch (n / 16) {
-    case 1: images_kernel<1><<<grid, block, 0, st>>>(j); break;
-    case 2: images_kernel<2><<<grid, block, 0, st>>>(j); break;
-    case 3: images_kernel<3><<<grid, block, 0, st>>>(j); break;
-    case 4: images_kernel<4><<<grid, block, 0, st>>>(j); break;
-    case 5: images_kernel<5><<<grid, block, 0, st>>>(j); break;
-    case 6: images_kernel<6><<<grid, block, 0, st>>>(j); break;
-    default: return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  const bool served = with_rate(n, [&](auto N) { images_kernel<decltype(N)::value><<<grid, block, 0, st>>>(j); });
+  return served ? cudaGetLastError() : cudaErrorInvalidValue;
 }
 
 template <int MS, int NS>

@@ -5,6 +5,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 
 namespace exl3 {
 
@@ -51,6 +52,28 @@ cudaError_t kernel_setup(KernelSetup& s, Kern kern, int threads, size_t smem, bo
   }
   if (per_sm) *per_sm = s.per_sm[dev].load(std::memory_order_acquire);
   return cudaSuccess;
+}
+
+// The rates the kernels serve: n halfwords per 256-weight tile, 16 x bits per weight, whole and half bits 1..6.
+inline bool rate_served_n(int n) { return n % 8 == 0 && n >= 16 && n <= 96; }
+
+// Calls f(std::integral_constant<int, N>{}) for the served rate n; false (nothing called) for any other n.
+template <typename F>
+inline bool with_rate(int n, F&& f) {
+  switch (n) {
+    case 16: f(std::integral_constant<int, 16>{}); return true;
+    case 24: f(std::integral_constant<int, 24>{}); return true;
+    case 32: f(std::integral_constant<int, 32>{}); return true;
+    case 40: f(std::integral_constant<int, 40>{}); return true;
+    case 48: f(std::integral_constant<int, 48>{}); return true;
+    case 56: f(std::integral_constant<int, 56>{}); return true;
+    case 64: f(std::integral_constant<int, 64>{}); return true;
+    case 72: f(std::integral_constant<int, 72>{}); return true;
+    case 80: f(std::integral_constant<int, 80>{}); return true;
+    case 88: f(std::integral_constant<int, 88>{}); return true;
+    case 96: f(std::integral_constant<int, 96>{}); return true;
+    default: return false;
+  }
 }
 
 constexpr int kMaxSegments = 4;  // linears stacked into one launch (the reference's SHARED_MAX, linear.zig:39-40)
@@ -116,7 +139,7 @@ int64_t tp_slot_bytes(const exl3_tp* tp);
 
 // Fills the geometry fields of `p` for `sms` SMs; false (with a reason) when the shape does not fit one launch.
 bool gemv_geometry(GemvParams& p, int sms, int row_groups, size_t partial_capacity_floats, const char** why);
-cudaError_t launch_gemv(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl);
+cudaError_t launch_gemv(const GemvParams& p, int n, int row_groups, bool imma, cudaStream_t st, bool pdl);
 
 // The persistent work-balanced decode GEMV (exl3_gemv6.cu), 1..16 rows, no column-parallel exchange: a prepare
 // launch (x rotated into fragment order in `scratch`) and the GEMV (runs' partials in `scratch` after the prepared x;
@@ -128,13 +151,13 @@ constexpr int64_t kGemv6MinSlabs = 49152;
 constexpr int64_t kGemv6MinSlabsDeep = 16384;
 bool gemv6_prefers(const GemvParams& p);
 size_t gemv6_scratch_bytes(const GemvParams& p, int sms);
-cudaError_t launch_gemv6(const GemvParams& p, int K, int sms, void* scratch, uint32_t* counters, cudaStream_t st);
+cudaError_t launch_gemv6(const GemvParams& p, int n, int sms, void* scratch, uint32_t* counters, cudaStream_t st);
 
 // The cluster-split decode GEMV (exl3_gemv5.cu): one thread-block cluster per 128-column block, its CTAs splitting
 // the input (kc = CTAs per cluster, kr = slabs per CTA), partials summed over distributed shared memory.
 // split_override > 0 forces the CTAs per cluster (measurement); false when no split fits.
-bool gemv5_geometry(GemvParams& p, int K, int sms, int row_groups, int split_override, const char** why);
-cudaError_t launch_gemv5(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl);
+bool gemv5_geometry(GemvParams& p, int n, int sms, int row_groups, int split_override, const char** why);
+cudaError_t launch_gemv5(const GemvParams& p, int n, int row_groups, bool imma, cudaStream_t st, bool pdl);
 
 // decode a whole trellis to W_hat (f16 bits, row-major [in][out]); one warp per tile
 cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,

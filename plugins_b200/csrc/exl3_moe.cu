@@ -243,9 +243,9 @@ __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0
 
 // PAIR: units (chunk, intermediate column block), weights gate+up, epilogue SwiGLU + down prepare.
 // !PAIR: units (chunk, hidden column block), weight down, epilogue finish to f32.
-template <int K, bool PAIR>
+template <int N, bool PAIR>
 __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) {
-  constexpr uint32_t kTileBytes = 32u * K;
+  constexpr uint32_t kTileBytes = 2u * N;
   constexpr uint32_t kW = 8u * kTileBytes;                // one weight's tiles of a unit slab
   constexpr uint32_t kSlab = (PAIR ? 2u : 1u) * (kW + 256u);  // tiles + x fragments, per weight
   extern __shared__ __align__(128) uint8_t smem[];
@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
   pdl_launch_dependents();
   pdl_wait();  // the chunk table and the prepared inputs come from the previous launches
   const int units = *p.nchunks * CB;
-  LaneWindows<K> lwin;
+  LaneWin<N> lwin;
   lwin.init(lane);
   ImmaIndicator ind;
   ind.init(lane);
@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
           uint32_t w[8], a[4];
-          lane_codewords<K>(reinterpret_cast<const uint32_t*>(sw) + t * (kTileBytes / 4u), lwin, w);
+          tile_codewords<N>(reinterpret_cast<const uint32_t*>(sw) + t * (kTileBytes / 4u), lwin, w);
           decode_afrag_imma<true>(w, ind, a);  // pairs packed on the FMA pipe: measured 2.5 % faster
           mma_16816(acc[w2][t], a, xv.x, xv.y);
         }
@@ -575,10 +575,10 @@ int moe_ctas_per_sm() {
   return v;
 }
 
-template <int K, bool PAIR>
+template <int N, bool PAIR>
 cudaError_t launch_moe_gemv(const MoeParams& p, int sms, cudaStream_t st) {
-  auto kern = moe_gemv_kernel<K, PAIR>;
-  constexpr size_t slab = (PAIR ? 2u : 1u) * (8u * 32u * K + 256u);
+  auto kern = moe_gemv_kernel<N, PAIR>;
+  constexpr size_t slab = (PAIR ? 2u : 1u) * (8u * 2u * N + 256u);
   const size_t smem = kWarpsM * kStagesM * slab + (PAIR ? 2 : 1) * kWarpsM * 8 * kRedStrideM * 4;
   static KernelSetup setup;
   int per_sm = 0;  // resident CTAs per SM: the persistent grid is exactly one wave
@@ -603,16 +603,10 @@ cudaError_t launch_moe_gemv(const MoeParams& p, int sms, cudaStream_t st) {
 }
 
 template <bool PAIR>
-cudaError_t launch_moe_gemv_k(const MoeParams& p, int K, int sms, cudaStream_t st) {
-  switch (K) {
-    case 1: return launch_moe_gemv<1, PAIR>(p, sms, st);
-    case 2: return launch_moe_gemv<2, PAIR>(p, sms, st);
-    case 3: return launch_moe_gemv<3, PAIR>(p, sms, st);
-    case 4: return launch_moe_gemv<4, PAIR>(p, sms, st);
-    case 5: return launch_moe_gemv<5, PAIR>(p, sms, st);
-    case 6: return launch_moe_gemv<6, PAIR>(p, sms, st);
-    default: return cudaErrorInvalidValue;
-  }
+cudaError_t launch_moe_gemv_k(const MoeParams& p, int n, int sms, cudaStream_t st) {
+  cudaError_t e = cudaErrorInvalidValue;
+  with_rate(n, [&](auto N) { e = launch_moe_gemv<decltype(N)::value, PAIR>(p, sms, st); });
+  return e;
 }
 
 template <typename Kern>
@@ -631,7 +625,7 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, const MoeParams& p, cud
 
 bool bank_ok(const exl3_weight* w, int in_f, int out_f) {
   return w && w->size == sizeof(exl3_weight) && w->trellis && w->suh && w->svh && w->nseg == 1 &&
-         w->in_features == in_f && w->out_features == out_f && w->n % 16 == 0 && w->n >= 16 && w->n <= 96 &&
+         w->in_features == in_f && w->out_features == out_f && exl3::rate_served_n(w->n) &&
          (reinterpret_cast<uintptr_t>(w->trellis) & 15u) == 0;
 }
 
@@ -752,8 +746,8 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
     err = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
     if (err == cudaSuccess)
       err = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S < kPrepChunks ? S : kPrepChunks), dim3(128), p, st);
-    if (err == cudaSuccess) err = launch_moe_gemv_k<true>(p, gate->n / 16, sc->sms, st);
-    if (err == cudaSuccess) err = launch_moe_gemv_k<false>(p, down->n / 16, sc->sms, st);
+    if (err == cudaSuccess) err = launch_moe_gemv_k<true>(p, gate->n, sc->sms, st);
+    if (err == cudaSuccess) err = launch_moe_gemv_k<false>(p, down->n, sc->sms, st);
     if (err == cudaSuccess)
       err = launch_pdl(moe_combine_kernel, dim3((hidden + 511) / 512, p.rows < kCombineRows ? p.rows : kCombineRows),
                        dim3(128), p, st);
@@ -1107,12 +1101,12 @@ exl3_verdict exl3_swiglu_cp(exl3_cpx* e, const exl3_weight* gate, const exl3_wei
   cudaError_t er = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
   if (er == cudaSuccess)
     er = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S < kPrepChunks ? S : kPrepChunks), dim3(128), p, st);
-  if (er == cudaSuccess) er = launch_moe_gemv_k<true>(p, gate->n / 16, sc->sms, st);
+  if (er == cudaSuccess) er = launch_moe_gemv_k<true>(p, gate->n, sc->sms, st);
   if (er == cudaSuccess) {
     cpx_sync_kernel<<<1, 32, 0, st>>>(e->dev, err);
     er = cudaGetLastError();
   }
-  if (er == cudaSuccess) er = launch_moe_gemv_k<false>(p, down->n / 16, sc->sms, st);
+  if (er == cudaSuccess) er = launch_moe_gemv_k<false>(p, down->n, sc->sms, st);
   if (er == cudaSuccess)
     er = launch_pdl(moe_combine_kernel, dim3((hslice + 511) / 512, p.rows < kCombineRows ? p.rows : kCombineRows),
                     dim3(128), p, st);

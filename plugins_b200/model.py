@@ -50,6 +50,7 @@ class ModelConfig:
     num_experts_per_tok: int = 0
     moe_intermediate_size: int = 0
     shared_expert_intermediate_size: int = 0
+    expert_rate_n: int = 0  # the expert bank's halfwords per tile (16 k), 0 without experts
     trunk_quant: dict = dataclasses.field(default_factory=dict)
     expert_quant: dict | None = None
 
@@ -73,7 +74,7 @@ def parse(config_json: str) -> ModelConfig:
                     trunk_quant=root["trunk_quant"], expert_quant=root.get("expert_quant"))
     for f in ("hidden_size", "intermediate_size", "num_hidden_layers", "num_attention_heads", "num_key_value_heads",
               "head_dim", "num_experts", "num_experts_per_tok", "moe_intermediate_size",
-              "shared_expert_intermediate_size"):
+              "shared_expert_intermediate_size", "expert_rate_n"):
         setattr(c, f, int(getattr(raw, f)))
     return c
 

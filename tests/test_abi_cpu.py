@@ -60,8 +60,10 @@ def test_validate_refuses_by_name():
         Q.validate({"format": "exl3", "codebook": "mul1", "window": 12})
     with pytest.raises(Q.Exl3Error, match="Exl3RateUnsupported"):
         Q.validate({"format": "exl3", "codebook": "mul1", "k": 9.25})
-    with pytest.raises(Q.Exl3Error, match="fractional"):
-        Q.validate({"format": "exl3", "codebook": "mul1", "k": 2.5})
+    Q.validate({"format": "exl3", "codebook": "mul1", "k": 2.5})  # half-bit rates are served (n = 40)
+    for k in (2.25, 6.5):  # n = 36 (a quarter bit) and n = 104 (above 6 bits): admitted rates, not served
+        with pytest.raises(Q.Exl3Error, match="half-bit grid"):
+            Q.validate({"format": "exl3", "codebook": "mul1", "k": k})
     with pytest.raises(Q.Exl3Error, match="not an exllamav3 block"):
         Q.validate({"format": "gptq", "codebook": "mul1"})
     with pytest.raises(Q.Exl3Error, match="not a JSON object"):

@@ -61,7 +61,7 @@ def _truth(oracle, x, tr, suh, svh, in_f, out_f, n):
                                _np(svh).view(np.uint16), in_f, out_f, n, threads=os.cpu_count() or 8)
 
 
-@pytest.mark.parametrize("n", [16, 48, 64, 96])
+@pytest.mark.parametrize("n", [16, 40, 48, 64, 88, 96])
 def test_one_hot_rows_reproduce_w_hat(Q, E, oracle, shape, n):
     # prepared x = the identity, inner product: every output row is a row of W_hat, exactly (1.0 * w + 0s in f32)
     in_f, out_f = 256, 640  # 640 columns: a ragged last tile for the 256-wide shapes
@@ -79,6 +79,7 @@ CASES = [
     # (in, out, n, rows)
     (512, 768, 64, 64), (1024, 640, 48, 200), (256, 1280, 32, 333), (768, 384, 96, 130), (384, 512, 80, 257),
     (5120, 2304, 48, 128),  # the DeepSeek-V4.1 prefill shape (dsv41_prefill_dig_gemm_5120x2304)
+    (512, 768, 56, 96), (768, 512, 24, 300),  # half-bit rates: 3.5 and 1.5 bits per weight
 ]
 
 

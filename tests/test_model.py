@@ -43,7 +43,7 @@ def test_claims_by_marker_only_a_qwen38_pack_with_a_trunk_block():
     ({"trunk_quant": {"format": "exl3", "codebook": "mcg"}}, "Exl3CodebookUnsupported"),
     ({"trunk_quant": {"format": "exl3", "codebook": "mul1", "window": 12}}, "Exl3WindowUnsupported"),
     ({"expert_quant": {"format": "exl3", "codebook": "mul1"}}, "Exl3RateUnsupported"),
-    ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 2.5}}, "Exl3RateUnsupported"),
+    ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 2.25}}, "Exl3RateUnsupported"),
     ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 8}}, "Exl3RateUnsupported"),
     ({"expert_quant": {"format": "exl3", "k": 3}}, "Exl3CodebookUnsupported"),
     ({"num_experts_per_tok": 33}, "Exl3TopKExceedsReduceBank"),
@@ -70,6 +70,8 @@ def test_parse_reads_the_linears_keys():
     flat = _config()
     flat.update(flat.pop("text_config"))  # keys at the root read the same
     assert M.parse(json.dumps(flat)).moe_intermediate_size == MOE_INTER
+    half = _config(expert_quant={"format": "exl3", "codebook": "mul1", "k": 2.5})
+    assert M.parse(json.dumps(half)).expert_rate_n == 40  # the half-bit rates are served: n = 16 k halfwords
 
 
 def _linear(rng, i, o, n):

@@ -34,6 +34,7 @@ def _route(rows, experts, topk, seed):
     (16, 384, 256, 4, 20, 32, 64, 0, "float32"),
     (8, 256, 256, 8, 16, 48, 48, 7, "float16"),
     (64, 512, 256, 6, 5, 48, 32, 0, "float16"),
+    (16, 256, 384, 4, 7, 40, 56, 0, "bfloat16"),  # half-bit banks: 2.5 and 3.5 bits per weight
 ])
 def test_swiglu_against_f32_truth(oracle, experts, hidden, inter, topk, rows, ng, nd, limit, dtype):
     from plugins_b200 import encoder as E

@@ -1,0 +1,53 @@
+"""The lane-window rule the decode kernels use (plugins_b200/csrc/exl3_windows.h), compiled for the host, against the
+oracle's unpacking of the bitstream (oracle/exl3_oracle.c exl3o_unpack_tile, SX/expert_exl3.zig:317-336): every
+lane's eight windows of random tiles, at every rate the kernels serve -- whole and half bits per weight, n = 16..96.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+RATES = tuple(range(16, 97, 8))  # n halfwords per tile: 1, 1.5, 2, ..., 6 bits per weight
+
+SHIM = r"""
+#include "exl3_windows.h"
+extern "C" int lane_windows_host(const uint32_t* words, int n, uint32_t lane, uint32_t* out) {
+  uint32_t w[8];
+  switch (n) {
+#define CASE(N) case N: { exl3::LaneWin<N> lw; lw.init(lane); exl3::lane_windows<N>(words, lw, w); break; }
+    CASE(16) CASE(24) CASE(32) CASE(40) CASE(48) CASE(56) CASE(64) CASE(72) CASE(80) CASE(88) CASE(96)
+    default: return 1;
+  }
+  for (int j = 0; j < 8; ++j) out[j] = w[j];
+  return 0;
+}
+"""
+
+
+@pytest.fixture(scope="module")
+def shim(tmp_path_factory):
+    d = tmp_path_factory.mktemp("windows")
+    src, so = d / "shim.cpp", d / "shim.so"
+    src.write_text(SHIM)
+    subprocess.check_call(["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-I", os.path.join(ROOT, "plugins_b200", "csrc"),
+                           str(src), "-o", str(so)])
+    lib = ctypes.CDLL(str(so))
+    lib.lane_windows_host.restype = ctypes.c_int
+    lib.lane_windows_host.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p]
+    return lib
+
+
+@pytest.mark.parametrize("n", RATES)
+def test_lane_windows_are_the_bitstreams_windows(shim, oracle, n):
+    rng = np.random.default_rng(n)
+    for _ in range(20):
+        halves = rng.integers(0, 65536, n, dtype=np.uint16)
+        words = halves.view(np.uint32).copy()  # u32 word m = hw[2m] | hw[2m+1] << 16
+        want = oracle.unpack_tile(halves, n)
+        out = np.empty(8, np.uint32)
+        for lane in range(32):
+            assert shim.lane_windows_host(words.ctypes.data, n, lane, out.ctypes.data) == 0
+            assert np.array_equal(out, want[8 * lane:8 * lane + 8].astype(np.uint32)), (n, lane)
