@@ -340,8 +340,9 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
     // holds the unit from its first run, else into this CTA's slot for run r in global memory (the unit's last CTA
     // adds them in run order); no barrier, the ring keeps streaming
     auto flush = [&](int r) {
-      const size_t slot = static_cast<size_t>(static_cast<int64_t>(su) * P + r - R0);  // (ra > 0 only)
-      float* gw = p.part + ((static_cast<size_t>(blockIdx.x) * P + slot) * kWarpsM + warp) * kPart;
+      // (ra > 0) this CTA's slot for run r: its offset in the CTA's range, below P - 1
+      const int64_t slot = ra > 0 ? static_cast<int64_t>(su) * P + r - R0 : 0;
+      float* gw = p.part + ((static_cast<size_t>(blockIdx.x) * P + static_cast<size_t>(slot)) * kWarpsM + warp) * kPart;
 #pragma unroll
       for (int w2 = 0; w2 < (PAIR ? 2 : 1); ++w2) {
         float* rw = red + (w2 * kWarpsM + warp) * 8 * kRedStrideM;
