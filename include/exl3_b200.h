@@ -96,6 +96,14 @@ typedef struct exl3_load_ctx {
 #define EXL3_WEIGHT_OWNED 1u   /* the library allocated trellis/suh/svh; exl3_release frees them */
 #define EXL3_WEIGHT_BANK 2u    /* routed experts stacked on axis 0 (load_bank) */
 #define EXL3_WEIGHT_GROUPED 4u /* a grouped linear: x [rows, groups, in] -> y [rows, groups, out] */
+/* A narrowed codeword window (the block's "window", 8..16 bits; the codeword is the low w bits of each 16-bit
+ * window, expert_exl3.zig Window): bits 8..11 of flags hold 16 - w, 0 for the full window.  The loaders set it from
+ * the block; a borrowed weight (exl3_weight_view) sets it by hand.  Such a weight takes the cluster-split decode GEMV
+ * (any row count below the GEMM's), the GEMM and the routed experts (gate and up share one window); the
+ * grid-stride entry exl3_matmul_noalloc and the dp4a byte sums refuse it. */
+#define EXL3_WEIGHT_WINDOW_SHIFT 8
+#define EXL3_WEIGHT_WINDOW_MASK 0xF00u
+#define EXL3_WEIGHT_WINDOW(w) ((((uint32_t)(16 - (w))) << EXL3_WEIGHT_WINDOW_SHIFT) & EXL3_WEIGHT_WINDOW_MASK)
 
 #define EXL3_MAX_SEGMENTS 4
 

@@ -17,6 +17,12 @@ CLAIM_NO, CLAIM_BY_MODE, CLAIM_BY_MARKER = 0, 1, 2
 F16, BF16, F32, I32, U32, U16, I16 = 0, 1, 2, 3, 4, 5, 6
 
 WEIGHT_OWNED, WEIGHT_BANK, WEIGHT_GROUPED = 1, 2, 4
+WEIGHT_WINDOW_SHIFT, WEIGHT_WINDOW_MASK = 8, 0xF00
+
+
+def weight_window(bits: int) -> int:
+    """EXL3_WEIGHT_WINDOW(bits): a narrowed codeword window (8..16 bits) as weight flags."""
+    return ((16 - int(bits)) << WEIGHT_WINDOW_SHIFT) & WEIGHT_WINDOW_MASK
 MATMUL_PREPARED, MATMUL_INNER, MATMUL_DP4A, MATMUL_GEMV, MATMUL_GEMM = 1, 2, 4, 8, 16
 MAX_SEGMENTS = 4
 ERR_WAIT_TIMEOUT, ERR_BAD_SHAPE, ERR_EP_OVERFLOW, ERR_TP_TIMEOUT, ERR_EP_TIMEOUT = 1, 2, 4, 8, 16

@@ -316,6 +316,15 @@ const exl3_verdict kNotShaped = {EXL3_UNSUPPORTED,
                                  "exl3_b200: not an EXL3 linear of the expected input width (trellis [in/16, out/16, n], "
                                  "suh f16 [in], svh f16 [out])"};
 
+// The block's codeword window as weight flags (EXL3_WEIGHT_WINDOW); 0 (the full window) when absent.
+uint32_t block_window_flags(exl3_str block_json) {
+  JVal b;
+  if (!parse_json(block_json, b) || b.kind != JVal::Obj) return 0;
+  const JVal* w = b.get("window");
+  if (!w || w->kind != JVal::Num || !w->is_int || w->num < 8 || w->num > 16) return 0;
+  return EXL3_WEIGHT_WINDOW(static_cast<int>(w->num));
+}
+
 exl3_verdict upload_stack(const exl3_load_ctx* ctx, const std::vector<LinearParts>& parts, uint32_t flags,
                           exl3_weight* out) {
   const LinearParts& p0 = parts[0];
@@ -357,7 +366,7 @@ exl3_verdict upload_stack(const exl3_load_ctx* ctx, const std::vector<LinearPart
   }
   memset(out, 0, sizeof *out);
   out->size = sizeof(exl3_weight);
-  out->flags = EXL3_WEIGHT_OWNED | flags;
+  out->flags = EXL3_WEIGHT_OWNED | flags | block_window_flags(ctx->block_json);
   out->trellis = tr;
   out->suh = su;
   out->svh = sv;
@@ -407,6 +416,7 @@ exl3_verdict check_weight(const exl3_weight* w) {
   if (!w || w->size != sizeof(exl3_weight) || !w->trellis || !w->suh || !w->svh)
     return refuse(EXL3_FAILED, "exl3_b200: not a loaded weight");
   if (w->nseg < 1 || w->nseg > EXL3_MAX_SEGMENTS) return refuse(EXL3_FAILED, "exl3_b200: bad segment count");
+  if (exl3::flags_window_bits(w->flags) < 8) return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3WindowUnsupported");
   return check_linear_shape(w->groups, w->in_features, w->out_features, w->n);
 }
 
@@ -462,6 +472,7 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
   int64_t nc_cap = static_cast<int64_t>((d->image_bytes - static_cast<size_t>(mc) * row_bytes) / row_bytes) / bn * bn;
   if (nc_cap < bn) return refuse(EXL3_TOO_LARGE, "exl3_b200: in_features too large for the prefill image region");
   const int gcount = grouped ? groups : 1;
+  const uint32_t cw_mask = exl3::window_mask(exl3::flags_window_bits(w->flags));
   // a kept weight: its B image is decoded once (the first call fills it, on this stream) and read from there
   uint8_t* kept = nullptr;
   size_t kept_group = 0;
@@ -481,7 +492,8 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
     nc_cap = (static_cast<int64_t>(out_f) + bn - 1) / bn * bn;  // no column chunks: the B image is the kept one
     for (int g = 0; fill && g < gcount; ++g)
       if (exl3::launch_images(nullptr, x_dtype, 0, 0, 0, nullptr, 0, nullptr, w->trellis + static_cast<size_t>(g) * tile_halfs,
-                              in_f, out_f, 0, out_f, w->n, kept + static_cast<size_t>(g) * kept_group, st) != cudaSuccess)
+                              in_f, out_f, 0, out_f, w->n, kept + static_cast<size_t>(g) * kept_group, st,
+                              cw_mask) != cudaSuccess)
         return refuse(EXL3_FAILED, "exl3_b200: resident image launch failed");
   }
   for (int g = 0; g < gcount; ++g) {
@@ -510,7 +522,7 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
           // the A image with the first column chunk's B image, in one launch
           if (exl3::launch_images(xg + static_cast<size_t>(r0) * x_stride * xsz, x_dtype, x_stride, m, mp, suh,
                                   (flags & EXL3_MATMUL_PREPARED) ? 1 : 0, j0 == 0 ? a_img : nullptr, trg, in_f, out_f,
-                                  c0 + j0, nc, w->n, kept ? nullptr : b_img, st) != cudaSuccess)
+                                  c0 + j0, nc, w->n, kept ? nullptr : b_img, st, cw_mask) != cudaSuccess)
             return refuse(EXL3_FAILED, "exl3_b200: prefill operand images launch failed");
           mark(1);
           const int shape = gemm_shape_for(m, nc, d->sms);
@@ -601,10 +613,13 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
       for (int s = w->nseg + 1; s <= exl3::kMaxSegments; ++s) gp.seg_cb[s] = gp.seg_cb[w->nseg];
       gp.prepared = (flags & EXL3_MATMUL_PREPARED) ? 1 : 0;
       gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
+      gp.cw_mask = exl3::window_mask(exl3::flags_window_bits(w->flags));
+      if (gp.cw_mask && !imma)
+        return refuse(EXL3_UNSUPPORTED, "exl3_b200: a narrowed codeword window takes the tensor-pipe byte sums (no dp4a)");
       const char* why = nullptr;
       // the persistent GEMV for large launches (every row count of a shape takes the same kernel, so a row's bits do
-      // not depend on the rows batched with it), the cluster-split one below
-      const bool v6 = imma && (gv_pick == 6 || (gv_pick == 0 && exl3::gemv6_prefers(gp)));
+      // not depend on the rows batched with it), the cluster-split one below (and for a narrowed codeword window)
+      const bool v6 = imma && !gp.cw_mask && (gv_pick == 6 || (gv_pick == 0 && exl3::gemv6_prefers(gp)));
       if (v6 && exl3::gemv6_scratch_bytes(gp, d->sms) <= d->partial_floats * 4) {
         if (exl3::launch_gemv6(gp, w->n, d->sms, d->partials, d->counters, st) != cudaSuccess)
           return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
@@ -616,6 +631,7 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
           return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
         continue;
       }
+      if (gp.cw_mask) return refuse(EXL3_UNSUPPORTED, "exl3_b200: a narrowed codeword window needs a cluster split of this input width");
       if (!exl3::gemv_geometry(gp, d->sms, rg, d->partial_floats, &why)) return refuse(EXL3_TOO_LARGE, why);
       if (exl3::launch_gemv(gp, w->n, rg, imma, st, true) != cudaSuccess)
         return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
@@ -652,7 +668,6 @@ exl3_verdict exl3_validate(exl3_str block_json, exl3_str config_json) {
   if (const JVal* w = b.get("window")) {
     if (w->kind != JVal::Num || !w->is_int || w->num < 8 || w->num > 16)
       return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3WindowUnsupported");
-    if (w->num != 16) return refuse(EXL3_UNSUPPORTED, "exl3_b200: narrowed codeword windows are not served");
   }
   if (const JVal* k = b.get("k")) {
     if (k->kind != JVal::Num) return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3RateUnsupported");
@@ -675,7 +690,7 @@ uint64_t exl3_bill(exl3_str block_json, exl3_str model_dir, uint64_t stored) {
 //
 // plugins/turboexl3_qwen38/config.zig:19-119 (claims, parse, checkPack / checkBlock) and src/direct/config.zig:301-420
 // (parseJson): MLX-free and bounds-checked, the EXL3 blocks refused with the reference's names, narrowed to what this
-// library decodes (the mul1 codebook named, 16-bit windows, whole bits per weight 1..6).
+// library decodes (the mul1 codebook named; windows 8..16; whole and half bits per weight 1..6).
 
 namespace {
 
@@ -688,7 +703,7 @@ const char* check_model_block(const JVal& o, bool bank, uint32_t* rate_n) {
   // the reference also decodes mcg and lets a trunk block leave its codebook unnamed; here mul1, named
   if (!str_is(o.get("codebook"), "mul1")) return "turboexl3_qwen38: Exl3CodebookUnsupported";
   if (const JVal* w = o.get("window"))
-    if (w->kind != JVal::Num || !w->is_int || w->num != 16) return "turboexl3_qwen38: Exl3WindowUnsupported";
+    if (w->kind != JVal::Num || !w->is_int || w->num < 8 || w->num > 16) return "turboexl3_qwen38: Exl3WindowUnsupported";
   if (bank) {
     const JVal* k = o.get("k");
     if (!k || k->kind != JVal::Num) return "turboexl3_qwen38: Exl3RateUnsupported";
@@ -952,6 +967,7 @@ exl3_verdict exl3_matmul_tp(const exl3_weight* w, const exl3_tensor* x, exl3_tp*
     cbb += static_cast<int32_t>(seg_total[s] / 128);
   }
   gp.tp = td;
+  gp.cw_mask = exl3::window_mask(exl3::flags_window_bits(w->flags));
   gp.tp_slot = slot;
   gp.tp_meta_cb = static_cast<uint32_t>(cbb);
   gp.tp_meta_bytes = static_cast<uint32_t>(rows * total * esize);
@@ -1016,8 +1032,8 @@ exl3_verdict exl3_weight_stack(const exl3_weight* parts, int32_t count, void* st
     exl3_verdict v = check_weight(&parts[i]);
     if (v.code != EXL3_OK) return v;
     if (parts[i].groups != 1 || parts[i].nseg != 1 || parts[i].in_features != p0.in_features || parts[i].n != p0.n ||
-        parts[i].device != p0.device)
-      return refuse(EXL3_UNSUPPORTED, "exl3_b200: stacked linears share one input width, rate and device");
+        parts[i].device != p0.device || ((parts[i].flags ^ p0.flags) & EXL3_WEIGHT_WINDOW_MASK))
+      return refuse(EXL3_UNSUPPORTED, "exl3_b200: stacked linears share one input width, rate, codeword window and device");
     total += parts[i].out_features;
   }
   exl3_verdict v = check_linear_shape(1, p0.in_features, total, p0.n);
@@ -1058,7 +1074,7 @@ exl3_verdict exl3_weight_stack(const exl3_weight* parts, int32_t count, void* st
   }
   out->seg_cols[count] = total;
   out->size = sizeof(exl3_weight);
-  out->flags = EXL3_WEIGHT_OWNED;
+  out->flags = EXL3_WEIGHT_OWNED | (p0.flags & EXL3_WEIGHT_WINDOW_MASK);
   out->trellis = tr;
   out->suh = su;
   out->svh = sv;
@@ -1078,7 +1094,8 @@ exl3_verdict exl3_decode_dense(const exl3_weight* w, int32_t group, uint16_t* ou
   DeviceGuard guard(w->device);
   const size_t tw = static_cast<size_t>(w->in_features / 16) * (w->out_features / 16) * w->n;
   if (exl3::launch_decode_dense(w->trellis + group * tw, w->in_features, w->out_features, w->n, out,
-                                (flags & EXL3_MATMUL_DP4A) ? 0 : 1, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+                                (flags & EXL3_MATMUL_DP4A) ? 0 : 1, static_cast<cudaStream_t>(stream),
+                                exl3::window_mask(exl3::flags_window_bits(w->flags))) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_b200: decode launch failed");
   return kOk;
 }

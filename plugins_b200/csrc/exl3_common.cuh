@@ -199,10 +199,11 @@ __device__ __forceinline__ void lane_codewords(const uint32_t* tile_words, const
 }
 
 // A tile of N halfwords (N = 16 x bits per weight; half-bit rates included): whole-bit rates take the extraction
-// above, half-bit rates the general rule of exl3_windows.h (the same windows: both follow the bitstream rule).
-template <int N>
+// above, half-bit rates the general rule of exl3_windows.h (the same windows: both follow the bitstream rule).  NW
+// (a narrowed codeword window, lw.mask): the general rule at every rate, each window masked.
+template <int N, bool NW = false>
 __device__ __forceinline__ void tile_codewords(const uint32_t* tile_words, const LaneWin<N>& lw, uint32_t (&w)[8]) {
-  if constexpr (N % 16 == 0) {
+  if constexpr (N % 16 == 0 && !NW) {
     LaneWindows<N / 16> lk;
     lk.o0 = lw.o0;
     lk.o1 = lw.o1;
@@ -210,7 +211,7 @@ __device__ __forceinline__ void tile_codewords(const uint32_t* tile_words, const
     lk.sh = lw.sh;
     lane_codewords<N / 16>(tile_words, lk, w);
   } else {
-    lane_windows<N>(tile_words, lw, w);
+    lane_windows<N, NW>(tile_words, lw, w);
   }
 }
 

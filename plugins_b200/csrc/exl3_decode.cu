@@ -10,9 +10,10 @@
 
 namespace exl3 {
 
-template <int N, bool IMMA>
+template <int N, bool IMMA, bool NW>
 __global__ void __launch_bounds__(256) decode_dense_kernel(const uint16_t* __restrict__ trellis, int in_features,
-                                                           int out_features, uint16_t* __restrict__ out) {
+                                                           int out_features, uint16_t* __restrict__ out,
+                                                           uint32_t cw_mask) {
   const uint32_t lane = threadIdx.x & 31u;
   const int ot = out_features / 16;
   const size_t tiles = static_cast<size_t>(in_features / 16) * ot;
@@ -22,8 +23,9 @@ __global__ void __launch_bounds__(256) decode_dense_kernel(const uint16_t* __res
   const uint32_t* tw = reinterpret_cast<const uint32_t*>(trellis + tile * N);
   LaneWin<N> lw;
   lw.init(lane);
+  lw.mask = cw_mask;
   uint32_t w[8], a[4];
-  tile_codewords<N>(tw, lw, w);
+  tile_codewords<N, NW>(tw, lw, w);
   const uint32_t g = lane >> 2, q = lane & 3u;
   if constexpr (IMMA) {
     ImmaIndicator ind;
@@ -59,19 +61,20 @@ __global__ void __launch_bounds__(256) decode_dense_kernel(const uint16_t* __res
 
 template <bool IMMA>
 static cudaError_t launch_dd(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
-                             cudaStream_t st) {
+                             cudaStream_t st, uint32_t cw_mask) {
   const size_t tiles = static_cast<size_t>(in_features / 16) * (out_features / 16);
   const dim3 grid(static_cast<unsigned>((tiles + 7) / 8)), block(256);
-  const bool served = with_rate(n, [&](auto N) {
-    decode_dense_kernel<decltype(N)::value, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out);
+  const bool served = with_rate_window(n, cw_mask, [&](auto N, auto NW) {
+    decode_dense_kernel<decltype(N)::value, IMMA, decltype(NW)::value>
+        <<<grid, block, 0, st>>>(trellis, in_features, out_features, out, cw_mask);
   });
   return served ? cudaGetLastError() : cudaErrorInvalidValue;
 }
 
 cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
-                                int imma, cudaStream_t st) {
-  return imma ? launch_dd<true>(trellis, in_features, out_features, n, out, st)
-              : launch_dd<false>(trellis, in_features, out_features, n, out, st);
+                                int imma, cudaStream_t st, uint32_t cw_mask) {
+  return imma ? launch_dd<true>(trellis, in_features, out_features, n, out, st, cw_mask)
+              : launch_dd<false>(trellis, in_features, out_features, n, out, st, cw_mask);
 }
 
 }  // namespace exl3

@@ -63,7 +63,7 @@ __device__ __forceinline__ float ld_dsmem(const float* local, uint32_t rank) {
 
 }  // namespace
 
-template <int N, int RG, bool IMMA, int ST>
+template <int N, int RG, bool IMMA, int ST, bool NW>
 __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   constexpr uint32_t kTileBytes = 2u * N;
   constexpr uint32_t kUnitBytes = 8u * kTileBytes;
@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   // ---- main loop
   LaneWin<N> lwin;
   lwin.init(lane);
+  lwin.mask = p.cw_mask;
   ImmaIndicator ind;
   ind.init(lane);
   const uint32_t g = lane >> 2, q = lane & 3u;
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
       uint32_t w[8], a[4];
-      tile_codewords<N>(tw + t * (kTileBytes / 4u), lwin, w);
+      tile_codewords<N, NW>(tw + t * (kTileBytes / 4u), lwin, w);
       if constexpr (IMMA) decode_afrag_imma<ST == deep_stages<N>()>(w, ind, a);
       else decode_afrag_dp4a(w, a);
 #pragma unroll
@@ -317,9 +318,9 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
 
 // ------------------------------------------------------------------ host
 
-template <int N, int RG, bool IMMA, int ST>
+template <int N, int RG, bool IMMA, int ST, bool NW>
 static cudaError_t launch5_t(const GemvParams& p, cudaStream_t st, bool pdl) {
-  auto kern = gemv5_kernel<N, RG, IMMA, ST>;
+  auto kern = gemv5_kernel<N, RG, IMMA, ST, NW>;
   const size_t loop = static_cast<size_t>(p.xp_bytes) + static_cast<size_t>(kW5) * ST * 8u * 2u * N;
   const size_t tail = static_cast<size_t>(kW5) * p.rows * kRed5 * 4 + kW5 * 512u;
   const size_t smem = loop > tail ? loop : tail;
@@ -342,16 +343,22 @@ static cudaError_t launch5_t(const GemvParams& p, cudaStream_t st, bool pdl) {
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <int N, int RG, bool IMMA>
+template <int N, int RG, bool IMMA, bool NW>
 static cudaError_t launch5_s(const GemvParams& p, cudaStream_t st, bool pdl) {
-  return p.stages == deep_stages<N>() ? launch5_t<N, RG, IMMA, deep_stages<N>()>(p, st, pdl)
-                                      : launch5_t<N, RG, IMMA, shallow_stages<N>()>(p, st, pdl);
+  return p.stages == deep_stages<N>() ? launch5_t<N, RG, IMMA, deep_stages<N>(), NW>(p, st, pdl)
+                                      : launch5_t<N, RG, IMMA, shallow_stages<N>(), NW>(p, st, pdl);
 }
 
+// A narrowed codeword window (p.cw_mask) takes the tensor-pipe byte sums only.
 template <int RG, bool IMMA>
 static cudaError_t launch5_k(const GemvParams& p, int n, cudaStream_t st, bool pdl) {
   cudaError_t e = cudaErrorInvalidValue;
-  with_rate(n, [&](auto N) { e = launch5_s<decltype(N)::value, RG, IMMA>(p, st, pdl); });
+  if constexpr (IMMA)
+    with_rate_window(n, p.cw_mask, [&](auto N, auto NW) {
+      e = launch5_s<decltype(N)::value, RG, IMMA, decltype(NW)::value>(p, st, pdl);
+    });
+  else if (!p.cw_mask)
+    with_rate(n, [&](auto N) { e = launch5_s<decltype(N)::value, RG, IMMA, false>(p, st, pdl); });
   return e;
 }
 

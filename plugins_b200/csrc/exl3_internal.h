@@ -76,6 +76,20 @@ inline bool with_rate(int n, F&& f) {
   }
 }
 
+// The codeword mask of a window of `bits` (8..16): 0 for the full 16-bit window (no masking instantiation).
+inline uint32_t window_mask(int bits) { return bits >= 16 ? 0u : (1u << bits) - 1u; }
+// A weight's window bits from its flags (bits 8..11 hold 16 - w: EXL3_WEIGHT_WINDOW in exl3_b200.h).
+inline int flags_window_bits(uint32_t flags) { return 16 - static_cast<int>((flags >> 8) & 0xFu); }
+
+// with_rate with a narrowed codeword window: f(N, NW) for the served rate n, NW = (cw_mask != 0).
+template <typename F>
+inline bool with_rate_window(int n, uint32_t cw_mask, F&& f) {
+  return with_rate(n, [&](auto N) {
+    if (cw_mask) f(N, std::true_type{});
+    else f(N, std::false_type{});
+  });
+}
+
 constexpr int kMaxSegments = 4;  // linears stacked into one launch (the reference's SHARED_MAX, linear.zig:39-40)
 constexpr int kMaxRows = 16;     // decode-GEMV rows per launch (two m16n8k16 row groups)
 
@@ -111,6 +125,7 @@ struct GemvParams {
   int32_t seg_cb[kMaxSegments + 1];  // segment bounds in 128-column blocks
   int32_t prepared;         // x already holds f16(H(x*suh)/sqrt(128)): no rotation
   int32_t inner_only;       // skip the output Hadamard and svh: y = the f32 inner product
+  uint32_t cw_mask;         // a narrowed codeword window's mask (window_mask), 0 for the full 16-bit window
   // geometry (gemv_geometry)
   int32_t kt, kr, kc;       // 16-row slabs, slabs per chunk, chunks
   int32_t contrib_max;      // most CTAs contributing to one (segment, chunk, column block)
@@ -161,7 +176,7 @@ cudaError_t launch_gemv5(const GemvParams& p, int n, int row_groups, bool imma, 
 
 // decode a whole trellis to W_hat (f16 bits, row-major [in][out]); one warp per tile
 cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
-                                int imma, cudaStream_t st);
+                                int imma, cudaStream_t st, uint32_t cw_mask = 0);
 
 // trellis encoder (exl3_encode.cu): target [in][out] f32 (rotated, unit variance) -> trellis [in/16][out/16][n]
 cudaError_t launch_encode(const float* target, int in_features, int out_features, int n, uint16_t* trellis,
@@ -190,7 +205,7 @@ struct GemmParams {
 // a_img is null) and the B image of the trellis columns [col0, col0 + ncols) (skipped when b_img is null).
 cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, const uint16_t* suh,
                           int prepared, uint8_t* a_img, const uint16_t* trellis, int in_features, int out_features,
-                          int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st);
+                          int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st, uint32_t cw_mask = 0);
 // shape: 0 = 128x128 tiles, 1 = 128x256, 2 = 256x128, 3 = 256x256 (rows x columns)
 int gemm_block_m(int shape);
 int gemm_block_n(int shape);

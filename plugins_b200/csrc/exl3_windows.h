@@ -23,6 +23,7 @@ struct LaneWin {
   static_assert(N % 2 == 0 && N >= 16 && N <= 96, "n even, 16..96");
   uint32_t o0, o1, o2;  // word offsets (c - 2, c - 1, c) mod n/2 of the u32 words around E
   uint32_t sh;          // right funnel shift that brings E to a word boundary (0 when E is word-aligned)
+  uint32_t mask = 0xFFFFu;  // the codeword: the low w bits of the 16-bit window (w = 8..16, a narrowed window)
   EXL3_HD void init(uint32_t lane) {
     constexpr uint32_t nw = N / 2;  // u32 words per tile
     const uint32_t e = (lane + 1u) * (N / 2);
@@ -42,8 +43,8 @@ EXL3_HD uint32_t funnel_r(uint32_t lo, uint32_t hi, uint32_t s) {  // (hi:lo) >>
 #endif
 }
 
-// Lane t's eight codewords (low 16 bits of each) from the tile's u32 words.
-template <int N>
+// Lane t's eight codewords (low 16 bits of each; with MASKED, the low w bits: lw.mask) from the tile's u32 words.
+template <int N, bool MASKED = false>
 EXL3_HD void lane_windows(const uint32_t* tile_words, const LaneWin<N>& lw, uint32_t (&w)[8]) {
   const uint32_t a = tile_words[lw.o0], b = tile_words[lw.o1], c = tile_words[lw.o2];
   const uint32_t vlo = funnel_r(c, b, lw.sh), vhi = funnel_r(b, a, lw.sh);  // the 64 bits below E
@@ -56,7 +57,7 @@ EXL3_HD void lane_windows(const uint32_t* tile_words, const LaneWin<N>& lw, uint
     if (s >= 32) v = vhi >> (s - 32);
     else if (s + 16 <= 32) v = vlo >> s;
     else v = funnel_r(vlo, vhi, static_cast<uint32_t>(s));
-    w[j] = v & 0xFFFFu;
+    w[j] = v & (MASKED ? lw.mask : 0xFFFFu);
   }
 }
 

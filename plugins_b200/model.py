@@ -10,7 +10,7 @@ module is them, over this library's quant seam (:mod:`plugins_b200.quant`):
   ``parseJson``, in the library (``exl3_model_parse``, C++): MLX-free and bounds-checked; the pack's EXL3 blocks are
   checked with the reference's refusal names (``NotExl3``, ``Exl3CodebookUnsupported``, ``Exl3WindowUnsupported``,
   ``Exl3RateUnsupported``, ``Exl3TopKExceedsReduceBank``), narrowed to what this library decodes (the mul1 codebook,
-  16-bit windows, whole bits per weight 1..6);
+  windows 8..16, whole and half bits per weight 1..6);
 * ``bill(cfg, source)`` -- the resident bytes: EXL3 weights stay resident as the pack stores them
   (plugins/turboexl3_ds41/config.zig:57-61);
 * :class:`ModelLinears` -- the load (every EXL3 linear and routed bank of the pack uploaded once, the linears that

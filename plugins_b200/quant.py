@@ -85,6 +85,11 @@ class Weight:
         return self.raw.n
 
     @property
+    def window(self) -> int:
+        """The codeword window in bits (16 unless the pack narrowed it)."""
+        return 16 - ((self.raw.flags & L.WEIGHT_WINDOW_MASK) >> L.WEIGHT_WINDOW_SHIFT)
+
+    @property
     def bits(self) -> float:
         return self.raw.n / 16.0
 
@@ -266,9 +271,9 @@ def swiglu(gate: Weight, up: Weight, down: Weight, x: torch.Tensor, inds: torch.
 
 # ------------------------------------------------------------------ weights already on the device
 
-def weight_from_tensors(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor) -> Weight:
+def weight_from_tensors(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, window: int = 16) -> Weight:
     """A borrowed view of device tensors in the pack layout: trellis [(G,) in/16, out/16, n] (int16/uint16),
-    suh [(G,) in] f16, svh [(G,) out] f16."""
+    suh [(G,) in] f16, svh [(G,) out] f16; ``window`` the block's codeword window (8..16 bits)."""
     if trellis.dim() == 3:
         g = 1
         kt, ot, n = trellis.shape
@@ -284,6 +289,9 @@ def weight_from_tensors(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Ten
     w = L.Weight()
     check(L.lib().exl3_weight_view(trellis.data_ptr(), suh.data_ptr(), svh.data_ptr(), g, kt * 16, ot * 16, n,
                                    trellis.device.index, ctypes.byref(w)))
+    if not 8 <= int(window) <= 16:
+        raise Exl3Error(L.EXL3_UNSUPPORTED, "exl3_b200: Exl3WindowUnsupported")
+    w.flags |= L.weight_window(window)
     return Weight(w, keep=(trellis, suh, svh))
 
 

@@ -41,7 +41,8 @@ def test_claims_by_marker_only_a_qwen38_pack_with_a_trunk_block():
     ({"trunk_quant": {"format": "awq"}}, "NotExl3"),
     ({"trunk_quant": "exl3"}, "TrunkQuantNotAnObject"),
     ({"trunk_quant": {"format": "exl3", "codebook": "mcg"}}, "Exl3CodebookUnsupported"),
-    ({"trunk_quant": {"format": "exl3", "codebook": "mul1", "window": 12}}, "Exl3WindowUnsupported"),
+    ({"trunk_quant": {"format": "exl3", "codebook": "mul1", "window": 7}}, "Exl3WindowUnsupported"),
+    ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 3, "window": 17}}, "Exl3WindowUnsupported"),
     ({"expert_quant": {"format": "exl3", "codebook": "mul1"}}, "Exl3RateUnsupported"),
     ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 2.25}}, "Exl3RateUnsupported"),
     ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 8}}, "Exl3RateUnsupported"),
@@ -72,6 +73,9 @@ def test_parse_reads_the_linears_keys():
     assert M.parse(json.dumps(flat)).moe_intermediate_size == MOE_INTER
     half = _config(expert_quant={"format": "exl3", "codebook": "mul1", "k": 2.5})
     assert M.parse(json.dumps(half)).expert_rate_n == 40  # the half-bit rates are served: n = 16 k halfwords
+    narrow = _config(trunk_quant={"format": "exl3", "codebook": "mul1", "window": 12},
+                     expert_quant={"format": "exl3", "codebook": "mul1", "k": 3, "window": 8})
+    assert M.parse(json.dumps(narrow)).expert_rate_n == 48  # narrowed codeword windows 8..15 are served
 
 
 def _linear(rng, i, o, n):

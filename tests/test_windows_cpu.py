@@ -51,3 +51,29 @@ def test_lane_windows_are_the_bitstreams_windows(shim, oracle, n):
         for lane in range(32):
             assert shim.lane_windows_host(words.ctypes.data, n, lane, out.ctypes.data) == 0
             assert np.array_equal(out, want[8 * lane:8 * lane + 8].astype(np.uint32)), (n, lane)
+
+
+def test_narrowed_window_truth_is_the_masked_decode(oracle):
+    # expert_exl3.zig Window: a narrowed window decodes the low w bits of each 16-bit window.  The oracle's W_hat at
+    # window w is the tile decode of the masked codewords, differs from the 16-bit one, and its f32 truth is the
+    # rotated product with that W_hat
+    rng = np.random.default_rng(12)
+    in_f, out_f, n = 256, 384, 40
+    tr = rng.integers(0, 65536, (in_f // 16, out_f // 16, n), dtype=np.uint16)
+    suh = (rng.choice([-1.0, 1.0], in_f) * (0.002 + 0.02 * rng.random(in_f))).astype(np.float16).view(np.uint16)
+    svh = (rng.choice([-1.0, 1.0], out_f) * (0.5 + rng.random(out_f))).astype(np.float16).view(np.uint16)
+    for w in (8, 12, 15):
+        full = oracle.reconstruct_inner(tr, in_f, out_f, n)
+        narrow = oracle.reconstruct_inner(tr, in_f, out_f, n, window=w)
+        assert not np.array_equal(full, narrow)
+        tile = oracle.decode_tile(tr[1, 2], n, window=w)
+        assert np.array_equal(narrow[16:32, 32:48].reshape(-1), tile)
+        x = rng.standard_normal((2, in_f)).astype(np.float32)
+        got = oracle.host_project(x, tr, suh, svh, in_f, out_f, n, threads=2, window=w)
+        s = x * suh.view(np.float16).astype(np.float32)
+        s = np.concatenate([np.stack([oracle.hadamard128(r[b:b + 128]) for b in range(0, in_f, 128)]).reshape(-1)
+                            for r in s]).reshape(2, in_f)
+        inner = s @ narrow.view(np.float16).astype(np.float32)
+        y = np.stack([np.concatenate([oracle.hadamard128(r[b:b + 128]) for b in range(0, out_f, 128)]) for r in inner])
+        y *= svh.view(np.float16).astype(np.float32)
+        assert np.allclose(got, y, rtol=1e-4, atol=1e-4 * np.abs(y).max())
