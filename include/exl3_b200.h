@@ -101,6 +101,9 @@ typedef struct exl3_load_ctx {
  * the block; a borrowed weight (exl3_weight_view) sets it by hand.  Such a weight takes the cluster-split decode GEMV
  * (any row count below the GEMM's), the GEMM and the routed experts (gate and up share one window); the
  * grid-stride entry exl3_matmul_noalloc and the dp4a byte sums refuse it. */
+/* The mcg codebook (the block's "codebook": "mcg", expert_exl3.zig decodeMcg) instead of mul1; a weight takes the
+ * same paths as a narrowed window's. */
+#define EXL3_WEIGHT_MCG 16u
 #define EXL3_WEIGHT_WINDOW_SHIFT 8
 #define EXL3_WEIGHT_WINDOW_MASK 0xF00u
 #define EXL3_WEIGHT_WINDOW(w) ((((uint32_t)(16 - (w))) << EXL3_WEIGHT_WINDOW_SHIFT) & EXL3_WEIGHT_WINDOW_MASK)

@@ -18,6 +18,7 @@ F16, BF16, F32, I32, U32, U16, I16 = 0, 1, 2, 3, 4, 5, 6
 
 WEIGHT_OWNED, WEIGHT_BANK, WEIGHT_GROUPED = 1, 2, 4
 WEIGHT_WINDOW_SHIFT, WEIGHT_WINDOW_MASK = 8, 0xF00
+WEIGHT_MCG = 16
 
 
 def weight_window(bits: int) -> int:

@@ -316,13 +316,15 @@ const exl3_verdict kNotShaped = {EXL3_UNSUPPORTED,
                                  "exl3_b200: not an EXL3 linear of the expected input width (trellis [in/16, out/16, n], "
                                  "suh f16 [in], svh f16 [out])"};
 
-// The block's codeword window as weight flags (EXL3_WEIGHT_WINDOW); 0 (the full window) when absent.
+// The block's codebook and codeword window as weight flags (EXL3_WEIGHT_MCG, EXL3_WEIGHT_WINDOW); 0 for mul1 at the
+// full window.
 uint32_t block_window_flags(exl3_str block_json) {
   JVal b;
   if (!parse_json(block_json, b) || b.kind != JVal::Obj) return 0;
   const JVal* w = b.get("window");
-  if (!w || w->kind != JVal::Num || !w->is_int || w->num < 8 || w->num > 16) return 0;
-  return EXL3_WEIGHT_WINDOW(static_cast<int>(w->num));
+  uint32_t f = str_is(b.get("codebook"), "mcg") ? EXL3_WEIGHT_MCG : 0u;
+  if (!w || w->kind != JVal::Num || !w->is_int || w->num < 8 || w->num > 16) return f;
+  return f | EXL3_WEIGHT_WINDOW(static_cast<int>(w->num));
 }
 
 exl3_verdict upload_stack(const exl3_load_ctx* ctx, const std::vector<LinearParts>& parts, uint32_t flags,
@@ -473,6 +475,7 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
   if (nc_cap < bn) return refuse(EXL3_TOO_LARGE, "exl3_b200: in_features too large for the prefill image region");
   const int gcount = grouped ? groups : 1;
   const uint32_t cw_mask = exl3::window_mask(exl3::flags_window_bits(w->flags));
+  const int mcg = (w->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
   // a kept weight: its B image is decoded once (the first call fills it, on this stream) and read from there
   uint8_t* kept = nullptr;
   size_t kept_group = 0;
@@ -493,7 +496,7 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
     for (int g = 0; fill && g < gcount; ++g)
       if (exl3::launch_images(nullptr, x_dtype, 0, 0, 0, nullptr, 0, nullptr, w->trellis + static_cast<size_t>(g) * tile_halfs,
                               in_f, out_f, 0, out_f, w->n, kept + static_cast<size_t>(g) * kept_group, st,
-                              cw_mask) != cudaSuccess)
+                              cw_mask, mcg) != cudaSuccess)
         return refuse(EXL3_FAILED, "exl3_b200: resident image launch failed");
   }
   for (int g = 0; g < gcount; ++g) {
@@ -522,7 +525,7 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
           // the A image with the first column chunk's B image, in one launch
           if (exl3::launch_images(xg + static_cast<size_t>(r0) * x_stride * xsz, x_dtype, x_stride, m, mp, suh,
                                   (flags & EXL3_MATMUL_PREPARED) ? 1 : 0, j0 == 0 ? a_img : nullptr, trg, in_f, out_f,
-                                  c0 + j0, nc, w->n, kept ? nullptr : b_img, st, cw_mask) != cudaSuccess)
+                                  c0 + j0, nc, w->n, kept ? nullptr : b_img, st, cw_mask, mcg) != cudaSuccess)
             return refuse(EXL3_FAILED, "exl3_b200: prefill operand images launch failed");
           mark(1);
           const int shape = gemm_shape_for(m, nc, d->sms);
@@ -614,12 +617,13 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
       gp.prepared = (flags & EXL3_MATMUL_PREPARED) ? 1 : 0;
       gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
       gp.cw_mask = exl3::window_mask(exl3::flags_window_bits(w->flags));
-      if (gp.cw_mask && !imma)
-        return refuse(EXL3_UNSUPPORTED, "exl3_b200: a narrowed codeword window takes the tensor-pipe byte sums (no dp4a)");
+      gp.mcg = (w->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
+      if ((gp.cw_mask || gp.mcg) && !imma)
+        return refuse(EXL3_UNSUPPORTED, "exl3_b200: a narrowed codeword window or mcg takes the tensor-pipe order (no dp4a)");
       const char* why = nullptr;
       // the persistent GEMV for large launches (every row count of a shape takes the same kernel, so a row's bits do
       // not depend on the rows batched with it), the cluster-split one below (and for a narrowed codeword window)
-      const bool v6 = imma && !gp.cw_mask && (gv_pick == 6 || (gv_pick == 0 && exl3::gemv6_prefers(gp)));
+      const bool v6 = imma && !gp.cw_mask && !gp.mcg && (gv_pick == 6 || (gv_pick == 0 && exl3::gemv6_prefers(gp)));
       if (v6 && exl3::gemv6_scratch_bytes(gp, d->sms) <= d->partial_floats * 4) {
         if (exl3::launch_gemv6(gp, w->n, d->sms, d->partials, d->counters, st) != cudaSuccess)
           return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
@@ -631,7 +635,8 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
           return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
         continue;
       }
-      if (gp.cw_mask) return refuse(EXL3_UNSUPPORTED, "exl3_b200: a narrowed codeword window needs a cluster split of this input width");
+      if (gp.cw_mask || gp.mcg)
+        return refuse(EXL3_UNSUPPORTED, "exl3_b200: a narrowed codeword window or mcg needs a cluster split of this input width");
       if (!exl3::gemv_geometry(gp, d->sms, rg, d->partial_floats, &why)) return refuse(EXL3_TOO_LARGE, why);
       if (exl3::launch_gemv(gp, w->n, rg, imma, st, true) != cudaSuccess)
         return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
@@ -690,7 +695,7 @@ uint64_t exl3_bill(exl3_str block_json, exl3_str model_dir, uint64_t stored) {
 //
 // plugins/turboexl3_qwen38/config.zig:19-119 (claims, parse, checkPack / checkBlock) and src/direct/config.zig:301-420
 // (parseJson): MLX-free and bounds-checked, the EXL3 blocks refused with the reference's names, narrowed to what this
-// library decodes (the mul1 codebook named; windows 8..16; whole and half bits per weight 1..6).
+// library decodes (the mul1 or mcg codebook named; windows 8..16; whole and half bits per weight 1..6).
 
 namespace {
 
@@ -700,8 +705,9 @@ bool is_qwen38(const std::string& mt) { return mt == "qwen4_exp" || mt == "qwen4
 
 const char* check_model_block(const JVal& o, bool bank, uint32_t* rate_n) {
   if (!str_is(o.get("format"), "exl3")) return "turboexl3_qwen38: NotExl3";
-  // the reference also decodes mcg and lets a trunk block leave its codebook unnamed; here mul1, named
-  if (!str_is(o.get("codebook"), "mul1")) return "turboexl3_qwen38: Exl3CodebookUnsupported";
+  // mul1 or mcg (the reference also lets a trunk block leave its codebook unnamed; here it is named)
+  if (!str_is(o.get("codebook"), "mul1") && !str_is(o.get("codebook"), "mcg"))
+    return "turboexl3_qwen38: Exl3CodebookUnsupported";
   if (const JVal* w = o.get("window"))
     if (w->kind != JVal::Num || !w->is_int || w->num < 8 || w->num > 16) return "turboexl3_qwen38: Exl3WindowUnsupported";
   if (bank) {
@@ -792,6 +798,16 @@ exl3_verdict exl3_open(exl3_load_ctx* ctx) {
   if (!ctx || ctx->size != sizeof(exl3_load_ctx)) return refuse(EXL3_FAILED, "exl3_b200: bad load context");
   if (exl3_claims(ctx->block_json, ctx->config_json) == EXL3_CLAIM_NO)
     return refuse(EXL3_UNSUPPORTED, "exl3_b200: not an exllamav3 mul1 block");
+  // a pack the model seam claims (qwen38) loads by that seam's block rules (mul1 or mcg, windows 8..16,
+  // config.zig:86-104); the quant seam's own validate is the ds41 plugin's (mul1 only, config.zig:49-53)
+  JVal cfg, blk;
+  if (parse_json(ctx->config_json, cfg) && cfg.kind == JVal::Obj && cfg.get("model_type") &&
+      cfg.get("model_type")->kind == JVal::Str && is_qwen38(cfg.get("model_type")->str) &&
+      parse_json(ctx->block_json, blk) && blk.kind == JVal::Obj) {
+    uint32_t rate_n = 0;
+    if (const char* why = check_model_block(blk, blk.get("k") != nullptr, &rate_n)) return refuse(EXL3_UNSUPPORTED, why);
+    return ensure_device(ctx->device);
+  }
   exl3_verdict v = exl3_validate(ctx->block_json, ctx->config_json);
   if (v.code != EXL3_OK) return v;
   return ensure_device(ctx->device);
@@ -968,6 +984,7 @@ exl3_verdict exl3_matmul_tp(const exl3_weight* w, const exl3_tensor* x, exl3_tp*
   }
   gp.tp = td;
   gp.cw_mask = exl3::window_mask(exl3::flags_window_bits(w->flags));
+  gp.mcg = (w->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
   gp.tp_slot = slot;
   gp.tp_meta_cb = static_cast<uint32_t>(cbb);
   gp.tp_meta_bytes = static_cast<uint32_t>(rows * total * esize);
@@ -1032,8 +1049,8 @@ exl3_verdict exl3_weight_stack(const exl3_weight* parts, int32_t count, void* st
     exl3_verdict v = check_weight(&parts[i]);
     if (v.code != EXL3_OK) return v;
     if (parts[i].groups != 1 || parts[i].nseg != 1 || parts[i].in_features != p0.in_features || parts[i].n != p0.n ||
-        parts[i].device != p0.device || ((parts[i].flags ^ p0.flags) & EXL3_WEIGHT_WINDOW_MASK))
-      return refuse(EXL3_UNSUPPORTED, "exl3_b200: stacked linears share one input width, rate, codeword window and device");
+        parts[i].device != p0.device || ((parts[i].flags ^ p0.flags) & (EXL3_WEIGHT_WINDOW_MASK | EXL3_WEIGHT_MCG)))
+      return refuse(EXL3_UNSUPPORTED, "exl3_b200: stacked linears share one input width, rate, codebook, codeword window and device");
     total += parts[i].out_features;
   }
   exl3_verdict v = check_linear_shape(1, p0.in_features, total, p0.n);
@@ -1074,7 +1091,7 @@ exl3_verdict exl3_weight_stack(const exl3_weight* parts, int32_t count, void* st
   }
   out->seg_cols[count] = total;
   out->size = sizeof(exl3_weight);
-  out->flags = EXL3_WEIGHT_OWNED | (p0.flags & EXL3_WEIGHT_WINDOW_MASK);
+  out->flags = EXL3_WEIGHT_OWNED | (p0.flags & (EXL3_WEIGHT_WINDOW_MASK | EXL3_WEIGHT_MCG));
   out->trellis = tr;
   out->suh = su;
   out->svh = sv;
@@ -1095,7 +1112,8 @@ exl3_verdict exl3_decode_dense(const exl3_weight* w, int32_t group, uint16_t* ou
   const size_t tw = static_cast<size_t>(w->in_features / 16) * (w->out_features / 16) * w->n;
   if (exl3::launch_decode_dense(w->trellis + group * tw, w->in_features, w->out_features, w->n, out,
                                 (flags & EXL3_MATMUL_DP4A) ? 0 : 1, static_cast<cudaStream_t>(stream),
-                                exl3::window_mask(exl3::flags_window_bits(w->flags))) != cudaSuccess)
+                                exl3::window_mask(exl3::flags_window_bits(w->flags)),
+                                (w->flags & EXL3_WEIGHT_MCG) ? 1 : 0) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_b200: decode launch failed");
   return kOk;
 }

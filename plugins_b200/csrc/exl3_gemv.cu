@@ -488,7 +488,7 @@ bool gemv_geometry(GemvParams& p, int sms, int row_groups, size_t partial_capaci
 }
 
 cudaError_t launch_gemv(const GemvParams& p, int n, int row_groups, bool imma, cudaStream_t st, bool pdl) {
-  if (p.cw_mask) return cudaErrorInvalidValue;  // narrowed codeword windows take the cluster-split GEMV
+  if (p.cw_mask || p.mcg) return cudaErrorInvalidValue;  // narrowed windows and mcg take the cluster-split GEMV
   const unsigned grid = static_cast<unsigned>(p.grid);
   if (row_groups == 1) return imma ? launch_gemv_k<1, true>(p, n, grid, st, pdl) : launch_gemv_k<1, false>(p, n, grid, st, pdl);
   if (row_groups == 2) return imma ? launch_gemv_k<2, true>(p, n, grid, st, pdl) : launch_gemv_k<2, false>(p, n, grid, st, pdl);

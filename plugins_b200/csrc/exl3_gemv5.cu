@@ -63,7 +63,7 @@ __device__ __forceinline__ float ld_dsmem(const float* local, uint32_t rank) {
 
 }  // namespace
 
-template <int N, int RG, bool IMMA, int ST, bool NW>
+template <int N, int RG, bool IMMA, int ST, int DS>
 __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   constexpr uint32_t kTileBytes = 2u * N;
   constexpr uint32_t kUnitBytes = 8u * kTileBytes;
@@ -169,9 +169,11 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   // ---- main loop
   LaneWin<N> lwin;
   lwin.init(lane);
-  lwin.mask = p.cw_mask;
+  lwin.mask = spec_mask(p.cw_mask);
   ImmaIndicator ind;
   ind.init(lane);
+  ImmaWin<N> iwin;
+  if constexpr (IMMA && DS == 2) iwin.init(lane, lwin.mask);
   const uint32_t g = lane >> 2, q = lane & 3u;
   float acc[8][RG][4];
 #pragma unroll
@@ -195,10 +197,9 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
     }
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-      uint32_t w[8], a[4];
-      tile_codewords<N, NW>(tw + t * (kTileBytes / 4u), lwin, w);
-      if constexpr (IMMA) decode_afrag_imma<ST == deep_stages<N>()>(w, ind, a);
-      else decode_afrag_dp4a(w, a);
+      uint32_t a[4];
+      if constexpr (IMMA) decode_tile_imma<N, DS, ST == deep_stages<N>()>(tw + t * (kTileBytes / 4u), lwin, iwin, ind, a);
+      else decode_tile_natural<N, DS>(tw + t * (kTileBytes / 4u), lwin, a);
 #pragma unroll
       for (int r = 0; r < RG; ++r) mma_16816(acc[t][r], a, b0[r], b1[r]);
     }
@@ -318,9 +319,9 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
 
 // ------------------------------------------------------------------ host
 
-template <int N, int RG, bool IMMA, int ST, bool NW>
+template <int N, int RG, bool IMMA, int ST, int DS>
 static cudaError_t launch5_t(const GemvParams& p, cudaStream_t st, bool pdl) {
-  auto kern = gemv5_kernel<N, RG, IMMA, ST, NW>;
+  auto kern = gemv5_kernel<N, RG, IMMA, ST, DS>;
   const size_t loop = static_cast<size_t>(p.xp_bytes) + static_cast<size_t>(kW5) * ST * 8u * 2u * N;
   const size_t tail = static_cast<size_t>(kW5) * p.rows * kRed5 * 4 + kW5 * 512u;
   const size_t smem = loop > tail ? loop : tail;
@@ -343,22 +344,22 @@ static cudaError_t launch5_t(const GemvParams& p, cudaStream_t st, bool pdl) {
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <int N, int RG, bool IMMA, bool NW>
+template <int N, int RG, bool IMMA, int DS>
 static cudaError_t launch5_s(const GemvParams& p, cudaStream_t st, bool pdl) {
-  return p.stages == deep_stages<N>() ? launch5_t<N, RG, IMMA, deep_stages<N>(), NW>(p, st, pdl)
-                                      : launch5_t<N, RG, IMMA, shallow_stages<N>(), NW>(p, st, pdl);
+  return p.stages == deep_stages<N>() ? launch5_t<N, RG, IMMA, deep_stages<N>(), DS>(p, st, pdl)
+                                      : launch5_t<N, RG, IMMA, shallow_stages<N>(), DS>(p, st, pdl);
 }
 
-// A narrowed codeword window (p.cw_mask) takes the tensor-pipe byte sums only.
+// A narrowed codeword window or the mcg codebook takes the tensor-pipe operand order only.
 template <int RG, bool IMMA>
 static cudaError_t launch5_k(const GemvParams& p, int n, cudaStream_t st, bool pdl) {
   cudaError_t e = cudaErrorInvalidValue;
   if constexpr (IMMA)
-    with_rate_window(n, p.cw_mask, [&](auto N, auto NW) {
-      e = launch5_s<decltype(N)::value, RG, IMMA, decltype(NW)::value>(p, st, pdl);
+    with_rate_decode(n, p.cw_mask, p.mcg != 0, [&](auto N, auto DS) {
+      e = launch5_s<decltype(N)::value, RG, IMMA, decltype(DS)::value>(p, st, pdl);
     });
-  else if (!p.cw_mask)
-    with_rate(n, [&](auto N) { e = launch5_s<decltype(N)::value, RG, IMMA, false>(p, st, pdl); });
+  else if (!p.cw_mask && !p.mcg)
+    with_rate(n, [&](auto N) { e = launch5_s<decltype(N)::value, RG, IMMA, 0>(p, st, pdl); });
   return e;
 }
 

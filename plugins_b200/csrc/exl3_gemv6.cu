@@ -379,7 +379,7 @@ bool gemv6_prefers(const GemvParams& p) {
 }
 
 cudaError_t launch_gemv6(const GemvParams& p, int n, int sms, void* scratch, uint32_t* counters, cudaStream_t st) {
-  if (p.cw_mask) return cudaErrorInvalidValue;  // narrowed codeword windows take the cluster-split GEMV
+  if (p.cw_mask || p.mcg) return cudaErrorInvalidValue;  // narrowed windows and mcg take the cluster-split GEMV
   if (p.rows < 1 || p.rows > 16 || p.tp) return cudaErrorInvalidValue;
   const int rg = p.rows <= 8 ? 1 : 2;
   __half* xf = static_cast<__half*>(scratch);

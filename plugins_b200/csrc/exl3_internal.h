@@ -81,14 +81,22 @@ inline uint32_t window_mask(int bits) { return bits >= 16 ? 0u : (1u << bits) - 
 // A weight's window bits from its flags (bits 8..11 hold 16 - w: EXL3_WEIGHT_WINDOW in exl3_b200.h).
 inline int flags_window_bits(uint32_t flags) { return 16 - static_cast<int>((flags >> 8) & 0xFu); }
 
-// with_rate with a narrowed codeword window: f(N, NW) for the served rate n, NW = (cw_mask != 0).
+// The decode spec of a weight: 0 mul1 at the full window, 1 mul1 at a narrowed window, 2 mcg.
+inline int decode_spec(uint32_t cw_mask, bool mcg) { return mcg ? 2 : (cw_mask ? 1 : 0); }
+
+// with_rate and the decode spec: f(N, DS) for the served rate n, DS = decode_spec(cw_mask, mcg).
 template <typename F>
-inline bool with_rate_window(int n, uint32_t cw_mask, F&& f) {
+inline bool with_rate_decode(int n, uint32_t cw_mask, bool mcg, F&& f) {
   return with_rate(n, [&](auto N) {
-    if (cw_mask) f(N, std::true_type{});
-    else f(N, std::false_type{});
+    switch (decode_spec(cw_mask, mcg)) {
+      case 0: f(N, std::integral_constant<int, 0>{}); break;
+      case 1: f(N, std::integral_constant<int, 1>{}); break;
+      default: f(N, std::integral_constant<int, 2>{}); break;
+    }
   });
 }
+// The codeword mask a decode spec reads: the window's, or all 16 bits for mcg at the full window.
+constexpr uint32_t spec_mask(uint32_t cw_mask) { return cw_mask ? cw_mask : 0xFFFFu; }
 
 constexpr int kMaxSegments = 4;  // linears stacked into one launch (the reference's SHARED_MAX, linear.zig:39-40)
 constexpr int kMaxRows = 16;     // decode-GEMV rows per launch (two m16n8k16 row groups)
@@ -126,6 +134,7 @@ struct GemvParams {
   int32_t prepared;         // x already holds f16(H(x*suh)/sqrt(128)): no rotation
   int32_t inner_only;       // skip the output Hadamard and svh: y = the f32 inner product
   uint32_t cw_mask;         // a narrowed codeword window's mask (window_mask), 0 for the full 16-bit window
+  int32_t mcg;              // the mcg codebook (else mul1)
   // geometry (gemv_geometry)
   int32_t kt, kr, kc;       // 16-row slabs, slabs per chunk, chunks
   int32_t contrib_max;      // most CTAs contributing to one (segment, chunk, column block)
@@ -176,7 +185,7 @@ cudaError_t launch_gemv5(const GemvParams& p, int n, int row_groups, bool imma, 
 
 // decode a whole trellis to W_hat (f16 bits, row-major [in][out]); one warp per tile
 cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
-                                int imma, cudaStream_t st, uint32_t cw_mask = 0);
+                                int imma, cudaStream_t st, uint32_t cw_mask = 0, int mcg = 0);
 
 // trellis encoder (exl3_encode.cu): target [in][out] f32 (rotated, unit variance) -> trellis [in/16][out/16][n]
 cudaError_t launch_encode(const float* target, int in_features, int out_features, int n, uint16_t* trellis,
@@ -205,7 +214,8 @@ struct GemmParams {
 // a_img is null) and the B image of the trellis columns [col0, col0 + ncols) (skipped when b_img is null).
 cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, const uint16_t* suh,
                           int prepared, uint8_t* a_img, const uint16_t* trellis, int in_features, int out_features,
-                          int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st, uint32_t cw_mask = 0);
+                          int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st, uint32_t cw_mask = 0,
+                          int mcg = 0);
 // shape: 0 = 128x128 tiles, 1 = 128x256, 2 = 256x128, 3 = 256x256 (rows x columns)
 int gemm_block_m(int shape);
 int gemm_block_n(int shape);

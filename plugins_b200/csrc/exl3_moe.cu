@@ -76,6 +76,7 @@ struct MoeParams {
   int32_t hp_world;
   int32_t max_cb;     // column blocks the unit_done array holds per chunk
   uint32_t cw_mask_gu, cw_mask_d;  // gate|up's and down's narrowed codeword window masks (0: the full 16 bits)
+  int32_t mcg_gu, mcg_d;           // gate|up's and down's codebook is mcg (else mul1)
   const void* x;      // [rows][hidden]
   int32_t x_dtype;
   const void* inds;   // [rows][topk]
@@ -244,7 +245,7 @@ __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0
 
 // PAIR: units (chunk, intermediate column block), weights gate+up, epilogue SwiGLU + down prepare.
 // !PAIR: units (chunk, hidden column block), weight down, epilogue finish to f32.
-template <int N, bool PAIR, bool NW>
+template <int N, bool PAIR, int DS>
 __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) {
   constexpr uint32_t kTileBytes = 2u * N;
   constexpr uint32_t kW = 8u * kTileBytes;                // one weight's tiles of a unit slab
@@ -268,9 +269,11 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
   const int units = *p.nchunks * CB;
   LaneWin<N> lwin;
   lwin.init(lane);
-  lwin.mask = PAIR ? p.cw_mask_gu : p.cw_mask_d;
+  lwin.mask = spec_mask(PAIR ? p.cw_mask_gu : p.cw_mask_d);
   ImmaIndicator ind;
   ind.init(lane);
+  ImmaWin<N> iwin;
+  if constexpr (DS == 2) iwin.init(lane, lwin.mask);
   const uint32_t g = lane >> 2, q = lane & 3u;
   // Every unit's k range is cut the same way whatever the call: P runs of L slabs (the last run shorter), a warp's
   // slabs of a run summed from zero in its MMA accumulators, the warp's runs added in run order, then the warps in
@@ -375,9 +378,8 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
         const uint2 xv = reinterpret_cast<const uint2*>(sw + kW)[lane];
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-          uint32_t w[8], a[4];
-          tile_codewords<N, NW>(reinterpret_cast<const uint32_t*>(sw) + t * (kTileBytes / 4u), lwin, w);
-          decode_afrag_imma<true>(w, ind, a);  // pairs packed on the FMA pipe: measured 2.5 % faster
+          uint32_t a[4];  // (mul1 pairs packed on the FMA pipe: measured 2.5 % faster)
+          decode_tile_imma<N, DS, true>(reinterpret_cast<const uint32_t*>(sw) + t * (kTileBytes / 4u), lwin, iwin, ind, a);
           mma_16816(acc[w2][t], a, xv.x, xv.y);
         }
       }
@@ -578,9 +580,9 @@ int moe_ctas_per_sm() {
   return v;
 }
 
-template <int N, bool PAIR, bool NW>
+template <int N, bool PAIR, int DS>
 cudaError_t launch_moe_gemv(const MoeParams& p, int sms, cudaStream_t st) {
-  auto kern = moe_gemv_kernel<N, PAIR, NW>;
+  auto kern = moe_gemv_kernel<N, PAIR, DS>;
   constexpr size_t slab = (PAIR ? 2u : 1u) * (8u * 2u * N + 256u);
   const size_t smem = kWarpsM * kStagesM * slab + (PAIR ? 2 : 1) * kWarpsM * 8 * kRedStrideM * 4;
   static KernelSetup setup;
@@ -608,8 +610,8 @@ cudaError_t launch_moe_gemv(const MoeParams& p, int sms, cudaStream_t st) {
 template <bool PAIR>
 cudaError_t launch_moe_gemv_k(const MoeParams& p, int n, int sms, cudaStream_t st) {
   cudaError_t e = cudaErrorInvalidValue;
-  with_rate_window(n, PAIR ? p.cw_mask_gu : p.cw_mask_d, [&](auto N, auto NW) {
-    e = launch_moe_gemv<decltype(N)::value, PAIR, decltype(NW)::value>(p, sms, st);
+  with_rate_decode(n, PAIR ? p.cw_mask_gu : p.cw_mask_d, (PAIR ? p.mcg_gu : p.mcg_d) != 0, [&](auto N, auto DS) {
+    e = launch_moe_gemv<decltype(N)::value, PAIR, decltype(DS)::value>(p, sms, st);
   });
   return e;
 }
@@ -701,8 +703,8 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   if (up->groups != experts || down->groups != experts || experts < 1 || experts > 1024)
     return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: the banks hold different expert counts");
   if (gate->n != up->n) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: gate and up banks at different rates");
-  if ((gate->flags ^ up->flags) & EXL3_WEIGHT_WINDOW_MASK)
-    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: gate and up banks with different codeword windows");
+  if ((gate->flags ^ up->flags) & (EXL3_WEIGHT_WINDOW_MASK | EXL3_WEIGHT_MCG))
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: gate and up banks with different codeword windows or codebooks");
   if (gate->device != up->device || gate->device != down->device) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: banks on different devices");
   if (rows == 0) return {EXL3_OK, nullptr};
   const int dev = gate->device;
@@ -738,6 +740,8 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   p.max_cb = sc->hidden / 128;
   p.cw_mask_gu = window_mask(flags_window_bits(gate->flags));
   p.cw_mask_d = window_mask(flags_window_bits(down->flags));
+  p.mcg_gu = (gate->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
+  p.mcg_d = (down->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
   p.unit_done = ints + kIntsM;
   p.part = reinterpret_cast<float*>(p.unit_done + 2 * static_cast<size_t>(kMaxSlots) * p.max_cb);
   uint8_t* cur = sc->base + fixed_bytes(sc->hidden, sc->sms);
@@ -1053,7 +1057,7 @@ exl3_verdict exl3_swiglu_cp(exl3_cpx* e, const exl3_weight* gate, const exl3_wei
   const int experts = gate->groups;
   if (!bank_ok(gate, hidden, islice) || !bank_ok(up, hidden, islice) || !bank_ok(down, inter, hslice) ||
       up->groups != experts || down->groups != experts || experts < 1 || experts > 1024 || gate->n != up->n ||
-      ((gate->flags ^ up->flags) & EXL3_WEIGHT_WINDOW_MASK))
+      ((gate->flags ^ up->flags) & (EXL3_WEIGHT_WINDOW_MASK | EXL3_WEIGHT_MCG)))
     return refuse_m(EXL3_UNSUPPORTED,
                     "exl3_swiglu_cp: banks gate/up [E, hidden -> inter/W], down [E, inter -> hidden/W], one rate and window for gate and up");
   if (gate->device != e->device || up->device != e->device || down->device != e->device)
@@ -1093,6 +1097,8 @@ exl3_verdict exl3_swiglu_cp(exl3_cpx* e, const exl3_weight* gate, const exl3_wei
   p.max_cb = sc->hidden / 128;
   p.cw_mask_gu = window_mask(flags_window_bits(gate->flags));
   p.cw_mask_d = window_mask(flags_window_bits(down->flags));
+  p.mcg_gu = (gate->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
+  p.mcg_d = (down->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
   p.unit_done = ints + kIntsM;
   p.part = reinterpret_cast<float*>(p.unit_done + 2 * static_cast<size_t>(kMaxSlots) * p.max_cb);
   uint8_t* cur = sc->base + fixed_bytes(sc->hidden, sc->sms);

@@ -92,8 +92,8 @@ extern "C" exl3_verdict exl3_matmul_noalloc(const exl3_weight* w, const exl3_ten
   const int in_f = w->in_features, out_f = w->out_features, n = w->n;
   if (in_f <= 0 || out_f <= 0 || in_f % 128 != 0 || out_f % 128 != 0)
     return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: in and out features must be multiples of 128");
-  if (w->flags & EXL3_WEIGHT_WINDOW_MASK)
-    return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: narrowed codeword windows take exl3_matmul");
+  if (w->flags & (EXL3_WEIGHT_WINDOW_MASK | EXL3_WEIGHT_MCG))
+    return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: narrowed codeword windows and mcg take exl3_matmul");
   if (!exl3::rate_served_n(n))
     return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: rates off the half-bit grid or above 6 bits are not served");
   if (out_f / 128 > static_cast<int>(kCounters))

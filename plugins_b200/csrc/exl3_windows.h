@@ -61,4 +61,40 @@ EXL3_HD void lane_windows(const uint32_t* tile_words, const LaneWin<N>& lw, uint
   }
 }
 
+// The codewords a lane needs when its MMA operand is in the tensor-pipe byte-sum order (lane (g, q) holding column g's
+// and g + 8's weights at k = 4q .. 4q + 3) and the codebook decodes per codeword (no byte sums to carry them across
+// lanes): the windows of lanes (g, 2q mod 4) and (g, 2q + 1 mod 4) at positions jb, jb + 1, jb + 4, jb + 5 (jb = 0 for
+// q < 2, else 2) -- the natural fragment's (k 2q', 2q' + 1) and (k 2q' + 8, 2q' + 9) pairs that cover k = 4q .. 4q + 3.
+template <int N>
+struct ImmaWin {
+  LaneWin<N> src[2];
+  uint32_t sh[2][4];  // per source lane, per window: its shift below that lane's window end E (in the 64 bits below E)
+  EXL3_HD void init(uint32_t lane, uint32_t mask) {
+    const uint32_t g = lane >> 2, q = lane & 3u, jb = q < 2u ? 0u : 2u;
+    const uint32_t js[4] = {jb, jb + 1u, jb + 4u, jb + 5u};
+    for (int i = 0; i < 2; ++i) {
+      src[i].init(4u * g + ((2u * q + static_cast<uint32_t>(i)) & 3u));
+      src[i].mask = mask;
+      for (int k = 0; k < 4; ++k) sh[i][k] = N / 2 - ((js[k] + 1u) * N) / 16;
+    }
+  }
+};
+
+// w[0..3]: the first source lane's windows jb, jb + 1, jb + 4, jb + 5; w[4..7] the second's; each masked (src mask).
+template <int N>
+EXL3_HD void imma_windows(const uint32_t* tile_words, const ImmaWin<N>& iw, uint32_t (&w)[8]) {
+#if defined(__CUDACC__)
+#pragma unroll
+#endif
+  for (int i = 0; i < 2; ++i) {
+    const LaneWin<N>& lw = iw.src[i];
+    const uint32_t a = tile_words[lw.o0], b = tile_words[lw.o1], c = tile_words[lw.o2];
+    const uint64_t v = (static_cast<uint64_t>(funnel_r(b, a, lw.sh)) << 32) | funnel_r(c, b, lw.sh);
+#if defined(__CUDACC__)
+#pragma unroll
+#endif
+    for (int k = 0; k < 4; ++k) w[4 * i + k] = static_cast<uint32_t>(v >> iw.sh[i][k]) & lw.mask;
+  }
+}
+
 }  // namespace exl3

@@ -85,6 +85,10 @@ class Weight:
         return self.raw.n
 
     @property
+    def codebook(self) -> str:
+        return "mcg" if self.raw.flags & L.WEIGHT_MCG else "mul1"
+
+    @property
     def window(self) -> int:
         """The codeword window in bits (16 unless the pack narrowed it)."""
         return 16 - ((self.raw.flags & L.WEIGHT_WINDOW_MASK) >> L.WEIGHT_WINDOW_SHIFT)
@@ -271,9 +275,11 @@ def swiglu(gate: Weight, up: Weight, down: Weight, x: torch.Tensor, inds: torch.
 
 # ------------------------------------------------------------------ weights already on the device
 
-def weight_from_tensors(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, window: int = 16) -> Weight:
+def weight_from_tensors(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, window: int = 16,
+                        codebook: str = "mul1") -> Weight:
     """A borrowed view of device tensors in the pack layout: trellis [(G,) in/16, out/16, n] (int16/uint16),
-    suh [(G,) in] f16, svh [(G,) out] f16; ``window`` the block's codeword window (8..16 bits)."""
+    suh [(G,) in] f16, svh [(G,) out] f16; ``window`` the block's codeword window (8..16 bits), ``codebook`` its
+    codebook (mul1 or mcg)."""
     if trellis.dim() == 3:
         g = 1
         kt, ot, n = trellis.shape
@@ -291,7 +297,9 @@ def weight_from_tensors(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Ten
                                    trellis.device.index, ctypes.byref(w)))
     if not 8 <= int(window) <= 16:
         raise Exl3Error(L.EXL3_UNSUPPORTED, "exl3_b200: Exl3WindowUnsupported")
-    w.flags |= L.weight_window(window)
+    if codebook not in ("mul1", "mcg"):
+        raise Exl3Error(L.EXL3_UNSUPPORTED, "exl3_b200: Exl3CodebookUnsupported")
+    w.flags |= L.weight_window(window) | (L.WEIGHT_MCG if codebook == "mcg" else 0)
     return Weight(w, keep=(trellis, suh, svh))
 
 

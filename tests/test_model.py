@@ -40,7 +40,7 @@ def test_claims_by_marker_only_a_qwen38_pack_with_a_trunk_block():
 @pytest.mark.parametrize("edit,name", [
     ({"trunk_quant": {"format": "awq"}}, "NotExl3"),
     ({"trunk_quant": "exl3"}, "TrunkQuantNotAnObject"),
-    ({"trunk_quant": {"format": "exl3", "codebook": "mcg"}}, "Exl3CodebookUnsupported"),
+    ({"trunk_quant": {"format": "exl3", "codebook": "3inst"}}, "Exl3CodebookUnsupported"),
     ({"trunk_quant": {"format": "exl3", "codebook": "mul1", "window": 7}}, "Exl3WindowUnsupported"),
     ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 3, "window": 17}}, "Exl3WindowUnsupported"),
     ({"expert_quant": {"format": "exl3", "codebook": "mul1"}}, "Exl3RateUnsupported"),
@@ -76,6 +76,9 @@ def test_parse_reads_the_linears_keys():
     narrow = _config(trunk_quant={"format": "exl3", "codebook": "mul1", "window": 12},
                      expert_quant={"format": "exl3", "codebook": "mul1", "k": 3, "window": 8})
     assert M.parse(json.dumps(narrow)).expert_rate_n == 48  # narrowed codeword windows 8..15 are served
+    mcg = _config(trunk_quant={"format": "exl3", "codebook": "mcg"},
+                  expert_quant={"format": "exl3", "codebook": "mcg", "k": 2.5, "window": 12})
+    assert M.parse(json.dumps(mcg)).expert_rate_n == 40  # the mcg codebook too (config.zig:86-104)
 
 
 def _linear(rng, i, o, n):

@@ -77,3 +77,51 @@ def test_narrowed_window_truth_is_the_masked_decode(oracle):
         y = np.stack([np.concatenate([oracle.hadamard128(r[b:b + 128]) for b in range(0, out_f, 128)]) for r in inner])
         y *= svh.view(np.float16).astype(np.float32)
         assert np.allclose(got, y, rtol=1e-4, atol=1e-4 * np.abs(y).max())
+
+
+IMMA_SHIM = r"""
+#include "exl3_windows.h"
+extern "C" int imma_windows_host(const uint32_t* words, int n, uint32_t lane, uint32_t mask, uint32_t* out) {
+  uint32_t w[8];
+  switch (n) {
+#define CASE(N) case N: { exl3::ImmaWin<N> iw; iw.init(lane, mask); exl3::imma_windows<N>(words, iw, w); break; }
+    CASE(16) CASE(24) CASE(32) CASE(40) CASE(48) CASE(56) CASE(64) CASE(72) CASE(80) CASE(88) CASE(96)
+    default: return 1;
+  }
+  for (int j = 0; j < 8; ++j) out[j] = w[j];
+  return 0;
+}
+"""
+
+
+@pytest.fixture(scope="module")
+def imma_shim(tmp_path_factory):
+    d = tmp_path_factory.mktemp("imma_windows")
+    src, so = d / "shim.cpp", d / "shim.so"
+    src.write_text(IMMA_SHIM)
+    subprocess.check_call(["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-I", os.path.join(ROOT, "plugins_b200", "csrc"),
+                           str(src), "-o", str(so)])
+    lib = ctypes.CDLL(str(so))
+    lib.imma_windows_host.restype = ctypes.c_int
+    lib.imma_windows_host.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p]
+    return lib
+
+
+@pytest.mark.parametrize("n", RATES)
+@pytest.mark.parametrize("window", [16, 12])
+def test_imma_order_windows_are_the_neighbours_windows(imma_shim, oracle, n, window):
+    # lane (g, q) of the tensor-pipe order reads lanes (g, 2q mod 4) and (g, 2q + 1 mod 4)'s windows jb, jb+1, jb+4,
+    # jb+5 (jb = 0 for q < 2, else 2): checked against the oracle's unpacking of the bitstream, masked to the window
+    rng = np.random.default_rng(n + window)
+    mask = (1 << window) - 1
+    for _ in range(10):
+        halves = rng.integers(0, 65536, n, dtype=np.uint16)
+        words = halves.view(np.uint32).copy()
+        cw = oracle.unpack_tile(halves, n).astype(np.uint32) & mask
+        out = np.empty(8, np.uint32)
+        for lane in range(32):
+            g, q = lane >> 2, lane & 3
+            jb = 0 if q < 2 else 2
+            want = [cw[8 * (4 * g + ((2 * q + i) & 3)) + j] for i in (0, 1) for j in (jb, jb + 1, jb + 4, jb + 5)]
+            assert imma_shim.imma_windows_host(words.ctypes.data, n, lane, mask, out.ctypes.data) == 0
+            assert out.tolist() == want, (n, lane)
