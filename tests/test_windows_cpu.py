@@ -125,3 +125,23 @@ def test_imma_order_windows_are_the_neighbours_windows(imma_shim, oracle, n, win
             want = [cw[8 * (4 * g + ((2 * q + i) & 3)) + j] for i in (0, 1) for j in (jb, jb + 1, jb + 4, jb + 5)]
             assert imma_shim.imma_windows_host(words.ctypes.data, n, lane, mask, out.ctypes.data) == 0
             assert out.tolist() == want, (n, lane)
+
+
+@pytest.mark.parametrize("n", [24, 48, 64, 88])
+def test_imma_order_mcg_fragment_is_the_tiles_weights(imma_shim, oracle, n):
+    # the tensor-pipe operand order (lane (g, q): column g's and g + 8's weights at k = 4q .. 4q + 3, pairs
+    # (4q, 4q + 1) then (4q + 2, 4q + 3)): the neighbours' windows decoded by mcg in the order the kernels pack them
+    # (a[0] = w0, w1; a[1] = w2, w3 (column g + 8); a[2] = w4, w5; a[3] = w6, w7) are the tile's weights there
+    rng = np.random.default_rng(n)
+    halves = rng.integers(0, 65536, n, dtype=np.uint16)
+    words = halves.view(np.uint32).copy()
+    tile = oracle.decode_tile(halves, n, codebook="mcg").reshape(16, 16)  # [k][column]
+    out = np.empty(8, np.uint32)
+    for lane in range(32):
+        g, q = lane >> 2, lane & 3
+        assert imma_shim.imma_windows_host(words.ctypes.data, n, lane, 0xFFFF, out.ctypes.data) == 0
+        dec = [oracle.decode_mcg(int(c)) for c in out]
+        k = 4 * q
+        want = [tile[k, g], tile[k + 1, g], tile[k, g + 8], tile[k + 1, g + 8],
+                tile[k + 2, g], tile[k + 3, g], tile[k + 2, g + 8], tile[k + 3, g + 8]]
+        assert dec == [int(v) for v in want], (n, lane)
