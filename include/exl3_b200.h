@@ -96,6 +96,17 @@ typedef struct exl3_load_ctx {
 #define EXL3_WEIGHT_OWNED 1u   /* the library allocated trellis/suh/svh; exl3_release frees them */
 #define EXL3_WEIGHT_BANK 2u    /* routed experts stacked on axis 0 (load_bank) */
 #define EXL3_WEIGHT_GROUPED 4u /* a grouped linear: x [rows, groups, in] -> y [rows, groups, out] */
+/* A narrowed codeword window (the block's "window", 8..16 bits; the codeword is the low w bits of each 16-bit
+ * window, expert_exl3.zig Window): bits 8..11 of flags hold 16 - w, 0 for the full window.  The loaders set it from
+ * the block; a borrowed weight (exl3_weight_view) sets it by hand.  Such a weight takes the cluster-split decode GEMV
+ * (any row count below the GEMM's), the GEMM and the routed experts (gate and up share one window); the
+ * grid-stride entry exl3_matmul_noalloc and the dp4a byte sums refuse it. */
+/* The mcg codebook (the block's "codebook": "mcg", expert_exl3.zig decodeMcg) instead of mul1; a weight takes the
+ * same paths as a narrowed window's. */
+#define EXL3_WEIGHT_MCG 16u
+#define EXL3_WEIGHT_WINDOW_SHIFT 8
+#define EXL3_WEIGHT_WINDOW_MASK 0xF00u
+#define EXL3_WEIGHT_WINDOW(w) ((((uint32_t)(16 - (w))) << EXL3_WEIGHT_WINDOW_SHIFT) & EXL3_WEIGHT_WINDOW_MASK)
 
 #define EXL3_MAX_SEGMENTS 4
 
@@ -345,6 +356,20 @@ exl3_verdict exl3_encode_trellis(const float *target, int32_t in_features, int32
  * call on a device looks the array up (cudaGetSymbolAddress) and clears its counters: make it before any stream
  * capture.  All calls share the array: calls that overlap on the GPU race -- order them on one stream. */
 exl3_verdict exl3_matmul_noalloc(const exl3_weight *w, const exl3_tensor *x, void *stream, exl3_tensor *out);
+
+/* Resident decoded matrices (QuantTable.resident / resident_pending, plugins/turboexl3_qwen38/overlay/mlx_serve/abi/
+ * quant.zig:96-101: memory for speed).  Keeps each of the `count` weights' decoded matrices from its first prefill
+ * (GEMM) call on, so later prefill calls skip the weight decode: device memory for the tensor-core GEMM's operand
+ * image of W_hat^T, f16, about 2 x in x out bytes per group, is reserved here (calls stay allocation-free) and filled
+ * by the first call.  Admitted only if everything kept, old and new, fits in `room` bytes (0: no bound), else refused
+ * EXL3_TOO_LARGE and nothing changes; `bytes` (may be null) receives the bytes kept.  A weight already kept is kept
+ * once.  `count` 0 drops every kept matrix.  exl3_release drops the matrices of the weight it frees; a borrowed weight
+ * (exl3_weight_view) must be dropped before its memory is freed or reused.  The first prefill call on a kept weight
+ * fills it on that call's stream: calls on other streams must not run before that call is ordered before them. */
+exl3_verdict exl3_resident(const exl3_weight *ws, int32_t count, uint64_t room, void *stream, uint64_t *bytes);
+
+/* The bytes exl3_resident admitted and no prefill call has filled yet (QuantTable.resident_pending). */
+uint64_t exl3_resident_pending(void);
 
 /* Device error bits the kernels recorded on `device`; `clear` resets them. */
 #define EXL3_ERR_WAIT_TIMEOUT 1u  /* a bounded mbarrier wait gave up (the kernel left its loop and returned) */

@@ -233,6 +233,12 @@ void exl3o_decode_tile_mcg(const uint16_t *words, uint32_t n, uint32_t window_bi
     for (uint32_t i = 0; i < TILE_VALUES; i++) out[g_perm[i]] = exl3o_decode_mcg((uint16_t)(cw[i] & mask));
 }
 
+/* One tile at codebook `cb` (0 mul1, 1 mcg) and window `window_bits` (SX/expert_exl3.zig decodeTile with a Decode). */
+static void decode_tile_cb(const uint16_t *words, uint32_t n, uint32_t window_bits, int cb, uint16_t *out) {
+    if (cb == 1) exl3o_decode_tile_mcg(words, n, window_bits, out);
+    else exl3o_decode_tile(words, n, window_bits, out);
+}
+
 /* ---------------------------------------------------------------- Hadamard (SX/expert_exl3.zig:400-414) */
 
 void exl3o_hadamard128(float *values /* [128] */) {
@@ -250,15 +256,22 @@ void exl3o_hadamard128(float *values /* [128] */) {
 
 /* ---------------------------------------------------------------- reconstruct (SX/expert_exl3.zig:416-488) */
 
-/* reconstructInner: W_hat f16 bits [in][out] row-major. */
+/* reconstructInner: W_hat f16 bits [in][out] row-major, codeword window `window_bits` (8..16). */
+void exl3o_reconstruct_inner_w(const uint16_t *trellis, uint32_t in_features, uint32_t out_features, uint32_t n,
+                               uint32_t window_bits, int codebook, uint16_t *out);
 void exl3o_reconstruct_inner(const uint16_t *trellis, uint32_t in_features, uint32_t out_features, uint32_t n,
                              uint16_t *out) {
+    exl3o_reconstruct_inner_w(trellis, in_features, out_features, n, 16, 0, out);
+}
+/* codebook 0 mul1, 1 mcg; window_bits 8..16 */
+void exl3o_reconstruct_inner_w(const uint16_t *trellis, uint32_t in_features, uint32_t out_features, uint32_t n,
+                               uint32_t window_bits, int codebook, uint16_t *out) {
     uint32_t in_tiles = in_features / TILE, out_tiles = out_features / TILE;
     uint16_t tile[TILE_VALUES];
     for (uint32_t tk = 0; tk < in_tiles; tk++) {
         for (uint32_t tn = 0; tn < out_tiles; tn++) {
             size_t off = ((size_t)tk * out_tiles + tn) * n;
-            exl3o_decode_tile(trellis + off, n, 16, tile);
+            decode_tile_cb(trellis + off, n, window_bits, codebook, tile);
             for (uint32_t r = 0; r < TILE; r++)
                 memcpy(out + (size_t)(tk * TILE + r) * out_features + tn * TILE, tile + r * TILE, TILE * 2);
         }
@@ -402,9 +415,18 @@ int exl3o_project(const float *x, const uint16_t *trellis, const uint16_t *suh, 
 /* ---------------------------------------------------------------- f32 truth (SX/linear.zig:121-197) */
 
 /* Host.project (SX/linear.zig:178-197): no intermediate f16 rounding anywhere; rows are independent. */
+int exl3o_host_project_w(const float *x, const uint16_t *trellis, const uint16_t *suh, const uint16_t *svh,
+                         uint32_t rows, uint32_t in_features, uint32_t out_features, uint32_t n, uint32_t window_bits,
+                         int codebook, int threads, float *out);
 int exl3o_host_project(const float *x, const uint16_t *trellis, const uint16_t *suh, const uint16_t *svh,
                        uint32_t rows, uint32_t in_features, uint32_t out_features, uint32_t n, int threads,
                        float *out) {
+    return exl3o_host_project_w(x, trellis, suh, svh, rows, in_features, out_features, n, 16, 0, threads, out);
+}
+/* The same at a codeword window (8..16 bits) and codebook (0 mul1, 1 mcg). */
+int exl3o_host_project_w(const float *x, const uint16_t *trellis, const uint16_t *suh, const uint16_t *svh,
+                         uint32_t rows, uint32_t in_features, uint32_t out_features, uint32_t n, uint32_t window_bits,
+                         int codebook, int threads, float *out) {
     ensure_tables();
     uint32_t in_tiles = in_features / TILE, out_tiles = out_features / TILE;
     float *sc = (float *)malloc((size_t)rows * in_features * 4);
@@ -425,7 +447,7 @@ int exl3o_host_project(const float *x, const uint16_t *trellis, const uint16_t *
             for (uint32_t c = a * TILE; c < b * TILE; c++) out[(size_t)r * out_features + c] = 0.0f;
         for (uint32_t tk = 0; tk < in_tiles; tk++) {
             for (uint32_t tn = a; tn < b; tn++) {
-                exl3o_decode_tile(trellis + ((size_t)tk * out_tiles + tn) * n, n, 16, tile);
+                decode_tile_cb(trellis + ((size_t)tk * out_tiles + tn) * n, n, window_bits, codebook, tile);
                 for (uint32_t i = 0; i < TILE_VALUES; i++) wf[i] = exl3o_f16_to_f32(tile[i]);
                 for (uint32_t r = 0; r < rows; r++) {
                     const float *s = sc + (size_t)r * in_features + tk * TILE;
@@ -452,11 +474,27 @@ int exl3o_host_project(const float *x, const uint16_t *trellis, const uint16_t *
  *   h = silu(g) * u
  *   y_row = sum_k score[row, k] * down_e(h)        (REDUCE_SOURCE: f32 score-weighted sum)
  * Banks are stacked on the expert axis: trellis [E][in/16][out/16][n], suh [E][in], svh [E][out]. */
+int exl3o_moe_truth_w(const float *x, const int32_t *inds, const float *scores, uint32_t rows, uint32_t topk,
+                      const uint16_t *g_tr, const uint16_t *g_suh, const uint16_t *g_svh, uint32_t g_n,
+                      const uint16_t *u_tr, const uint16_t *u_suh, const uint16_t *u_svh, uint32_t u_n,
+                      const uint16_t *d_tr, const uint16_t *d_suh, const uint16_t *d_svh, uint32_t d_n,
+                      uint32_t gu_window, uint32_t d_window, int gu_cb, int d_cb, uint32_t hidden, uint32_t inter,
+                      float limit, int threads, float *y);
 int exl3o_moe_truth(const float *x, const int32_t *inds, const float *scores, uint32_t rows, uint32_t topk,
                     const uint16_t *g_tr, const uint16_t *g_suh, const uint16_t *g_svh, uint32_t g_n,
                     const uint16_t *u_tr, const uint16_t *u_suh, const uint16_t *u_svh, uint32_t u_n,
                     const uint16_t *d_tr, const uint16_t *d_suh, const uint16_t *d_svh, uint32_t d_n,
                     uint32_t hidden, uint32_t inter, float limit, int threads, float *y) {
+    return exl3o_moe_truth_w(x, inds, scores, rows, topk, g_tr, g_suh, g_svh, g_n, u_tr, u_suh, u_svh, u_n, d_tr,
+                             d_suh, d_svh, d_n, 16, 16, 0, 0, hidden, inter, limit, threads, y);
+}
+/* The same with gate/up and down at codeword windows (8..16 bits) and codebooks (0 mul1, 1 mcg). */
+int exl3o_moe_truth_w(const float *x, const int32_t *inds, const float *scores, uint32_t rows, uint32_t topk,
+                      const uint16_t *g_tr, const uint16_t *g_suh, const uint16_t *g_svh, uint32_t g_n,
+                      const uint16_t *u_tr, const uint16_t *u_suh, const uint16_t *u_svh, uint32_t u_n,
+                      const uint16_t *d_tr, const uint16_t *d_suh, const uint16_t *d_svh, uint32_t d_n,
+                      uint32_t gu_window, uint32_t d_window, int gu_cb, int d_cb, uint32_t hidden, uint32_t inter,
+                      float limit, int threads, float *y) {
     size_t gate_words = (size_t)(hidden / 16) * (inter / 16) * g_n;
     size_t up_words = (size_t)(hidden / 16) * (inter / 16) * u_n;
     size_t down_words = (size_t)(inter / 16) * (hidden / 16) * d_n;
@@ -475,10 +513,10 @@ int exl3o_moe_truth(const float *x, const int32_t *inds, const float *scores, ui
         for (uint32_t k = 0; k < topk; k++) {
             uint32_t e = (uint32_t)inds[r * topk + k];
             const float *xr = x + (size_t)r * hidden;
-            exl3o_host_project(xr, g_tr + e * gate_words, g_suh + (size_t)e * hidden, g_svh + (size_t)e * inter, 1,
-                               hidden, inter, g_n, threads, g);
-            exl3o_host_project(xr, u_tr + e * up_words, u_suh + (size_t)e * hidden, u_svh + (size_t)e * inter, 1,
-                               hidden, inter, u_n, threads, u);
+            exl3o_host_project_w(xr, g_tr + e * gate_words, g_suh + (size_t)e * hidden, g_svh + (size_t)e * inter, 1,
+                                 hidden, inter, g_n, gu_window, gu_cb, threads, g);
+            exl3o_host_project_w(xr, u_tr + e * up_words, u_suh + (size_t)e * hidden, u_svh + (size_t)e * inter, 1,
+                               hidden, inter, u_n, gu_window, gu_cb, threads, u);
             for (uint32_t i = 0; i < inter; i++) {
                 float gv = g[i], uv = u[i];
                 if (limit > 0.0f) {
@@ -488,8 +526,8 @@ int exl3o_moe_truth(const float *x, const int32_t *inds, const float *scores, ui
                 float sig = 1.0f / (1.0f + expf(-gv));
                 g[i] = gv * sig * uv;
             }
-            exl3o_host_project(g, d_tr + e * down_words, d_suh + (size_t)e * inter, d_svh + (size_t)e * hidden, 1,
-                               inter, hidden, d_n, threads, d);
+            exl3o_host_project_w(g, d_tr + e * down_words, d_suh + (size_t)e * inter, d_svh + (size_t)e * hidden, 1,
+                                 inter, hidden, d_n, d_window, d_cb, threads, d);
             float w = scores[r * topk + k];
             for (uint32_t c = 0; c < hidden; c++) yr[c] += w * d[c];
         }

@@ -63,6 +63,7 @@ def lib():
             L.exl3o_decode_tile_mcg.argtypes = [_u16p, _u, _u, _u16p]
             L.exl3o_hadamard128.argtypes = [_f32p]
             L.exl3o_reconstruct_inner.argtypes = [_u16p, _u, _u, _u, _u16p]
+            L.exl3o_reconstruct_inner_w.argtypes = [_u16p, _u, _u, _u, _u, ctypes.c_int, _u16p]
             L.exl3o_reconstruct_states.argtypes = [_u16p, _u, _u, _u, _u16p, _u16p]
             L.exl3o_reconstruct_public.restype = ctypes.c_int
             L.exl3o_reconstruct_public.argtypes = [_u16p, _u16p, _u16p, _u, _u, _u, _u16p]
@@ -73,16 +74,29 @@ def lib():
             L.exl3o_project.argtypes = [_f32p, _u16p, _u16p, _u16p, _u, _u, _u, ctypes.c_int, _f32p]
             L.exl3o_host_project.restype = ctypes.c_int
             L.exl3o_host_project.argtypes = [_f32p, _u16p, _u16p, _u16p, _u, _u, _u, _u, ctypes.c_int, _f32p]
+            L.exl3o_host_project_w.restype = ctypes.c_int
+            L.exl3o_host_project_w.argtypes = [_f32p, _u16p, _u16p, _u16p, _u, _u, _u, _u, _u, ctypes.c_int, ctypes.c_int,
+                                               _f32p]
             L.exl3o_moe_truth.restype = ctypes.c_int
             L.exl3o_moe_truth.argtypes = [_f32p, _i32p, _f32p, _u, _u,
                                           _u16p, _u16p, _u16p, _u, _u16p, _u16p, _u16p, _u, _u16p, _u16p, _u16p, _u,
                                           _u, _u, ctypes.c_float, ctypes.c_int, _f32p]
+            L.exl3o_moe_truth_w.restype = ctypes.c_int
+            L.exl3o_moe_truth_w.argtypes = [_f32p, _i32p, _f32p, _u, _u,
+                                            _u16p, _u16p, _u16p, _u, _u16p, _u16p, _u16p, _u, _u16p, _u16p, _u16p, _u,
+                                            _u, _u, ctypes.c_int, ctypes.c_int, _u, _u, ctypes.c_float, ctypes.c_int, _f32p]
             L.exl3o_splitmix64.restype = ctypes.c_uint64
             L.exl3o_splitmix64.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
             L.exl3o_synth_plane.argtypes = [ctypes.c_uint64, ctypes.c_size_t, _u16p]
             L.exl3o_init()
             _lib = L
     return _lib
+
+
+def _cb(codebook: str) -> int:
+    if codebook not in ("mul1", "mcg"):
+        raise ValueError(codebook)
+    return 1 if codebook == "mcg" else 0
 
 
 def _c(a, dtype):
@@ -152,10 +166,13 @@ def hadamard128(v) -> np.ndarray:
     return a
 
 
-def reconstruct_inner(trellis, in_features: int, out_features: int, n: int) -> np.ndarray:
-    """W_hat as f16 bits, row-major [in, out]."""
+def reconstruct_inner(trellis, in_features: int, out_features: int, n: int, window: int = 16,
+                      codebook: str = "mul1") -> np.ndarray:
+    """W_hat as f16 bits, row-major [in, out]; ``window`` the codeword window in bits (8..16), ``codebook`` mul1 or
+    mcg."""
     out = np.empty(in_features * out_features, np.uint16)
-    lib().exl3o_reconstruct_inner(_c(trellis, np.uint16).reshape(-1), in_features, out_features, n, out)
+    lib().exl3o_reconstruct_inner_w(_c(trellis, np.uint16).reshape(-1), in_features, out_features, n, window,
+                                    _cb(codebook), out)
     return out.reshape(in_features, out_features)
 
 
@@ -185,20 +202,25 @@ def project(x, trellis, suh, svh, in_features: int, out_features: int, n: int, t
     return out
 
 
-def host_project(x, trellis, suh, svh, in_features: int, out_features: int, n: int, threads: int = 1) -> np.ndarray:
-    """The f32 truth (Host.project): x [rows, in] -> y [rows, out] f32, no intermediate f16 rounding."""
+def host_project(x, trellis, suh, svh, in_features: int, out_features: int, n: int, threads: int = 1,
+                 window: int = 16, codebook: str = "mul1") -> np.ndarray:
+    """The f32 truth (Host.project): x [rows, in] -> y [rows, out] f32, no intermediate f16 rounding; ``window``
+    the codeword window in bits (8..16)."""
     x2 = _c(x, np.float32).reshape(-1, in_features)
     rows = x2.shape[0]
     out = np.empty(rows * out_features, np.float32)
-    rc = lib().exl3o_host_project(x2.reshape(-1), _c(trellis, np.uint16).reshape(-1), _c(suh, np.uint16).reshape(-1),
-                                  _c(svh, np.uint16).reshape(-1), rows, in_features, out_features, n, threads, out)
+    rc = lib().exl3o_host_project_w(x2.reshape(-1), _c(trellis, np.uint16).reshape(-1), _c(suh, np.uint16).reshape(-1),
+                                    _c(svh, np.uint16).reshape(-1), rows, in_features, out_features, n, window,
+                                    _cb(codebook), threads, out)
     if rc != 0:
         raise MemoryError("exl3o_host_project")
     return out.reshape(rows, out_features)
 
 
-def moe_truth(x, inds, scores, gate, up, down, hidden: int, inter: int, limit: float = 0.0, threads: int = 1):
-    """Routed SwiGLU f32 truth.  gate/up/down = (trellis [E, ...], suh [E, in], svh [E, out], n)."""
+def moe_truth(x, inds, scores, gate, up, down, hidden: int, inter: int, limit: float = 0.0, threads: int = 1,
+              windows=(16, 16), codebooks=("mul1", "mul1")):
+    """Routed SwiGLU f32 truth.  gate/up/down = (trellis [E, ...], suh [E, in], svh [E, out], n); ``windows`` the
+    codeword windows of gate|up and of down (8..16 bits)."""
     x2 = _c(x, np.float32).reshape(-1, hidden)
     rows = x2.shape[0]
     inds2 = _c(inds, np.int32).reshape(rows, -1)
@@ -208,8 +230,9 @@ def moe_truth(x, inds, scores, gate, up, down, hidden: int, inter: int, limit: f
     args = []
     for tr, su, sv, n in (gate, up, down):
         args += [_c(tr, np.uint16).reshape(-1), _c(su, np.uint16).reshape(-1), _c(sv, np.uint16).reshape(-1), n]
-    rc = lib().exl3o_moe_truth(x2.reshape(-1), inds2.reshape(-1), sc.reshape(-1), rows, topk, *args, hidden, inter,
-                               float(limit), threads, y)
+    rc = lib().exl3o_moe_truth_w(x2.reshape(-1), inds2.reshape(-1), sc.reshape(-1), rows, topk, *args,
+                                 int(windows[0]), int(windows[1]), _cb(codebooks[0]), _cb(codebooks[1]), hidden, inter,
+                                 float(limit), threads, y)
     if rc != 0:
         raise MemoryError("exl3o_moe_truth")
     return y.reshape(rows, hidden)

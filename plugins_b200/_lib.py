@@ -17,6 +17,13 @@ CLAIM_NO, CLAIM_BY_MODE, CLAIM_BY_MARKER = 0, 1, 2
 F16, BF16, F32, I32, U32, U16, I16 = 0, 1, 2, 3, 4, 5, 6
 
 WEIGHT_OWNED, WEIGHT_BANK, WEIGHT_GROUPED = 1, 2, 4
+WEIGHT_WINDOW_SHIFT, WEIGHT_WINDOW_MASK = 8, 0xF00
+WEIGHT_MCG = 16
+
+
+def weight_window(bits: int) -> int:
+    """EXL3_WEIGHT_WINDOW(bits): a narrowed codeword window (8..16 bits) as weight flags."""
+    return ((16 - int(bits)) << WEIGHT_WINDOW_SHIFT) & WEIGHT_WINDOW_MASK
 MATMUL_PREPARED, MATMUL_INNER, MATMUL_DP4A, MATMUL_GEMV, MATMUL_GEMM = 1, 2, 4, 8, 16
 MAX_SEGMENTS = 4
 ERR_WAIT_TIMEOUT, ERR_BAD_SHAPE, ERR_EP_OVERFLOW, ERR_TP_TIMEOUT, ERR_EP_TIMEOUT = 1, 2, 4, 8, 16
@@ -31,7 +38,7 @@ EXPORTS = (
     "exl3_tp_create", "exl3_tp_connect", "exl3_tp_destroy", "exl3_tp_begin", "exl3_matmul_tp", "exl3_tp_gather",
     "exl3_weight_view", "exl3_weight_stack",
     "exl3_decode_dense", "exl3_encode_trellis", "exl3_matmul_noalloc", "exl3_device_error", "exl3_version",
-    "exl3_model_claims", "exl3_model_parse",
+    "exl3_model_claims", "exl3_model_parse", "exl3_resident", "exl3_resident_pending",
 )
 
 
@@ -222,6 +229,10 @@ def lib() -> ctypes.CDLL:
             L.exl3_matmul_noalloc.argtypes = [P(Weight), P(Tensor), ctypes.c_void_p, P(Tensor)]
             L.exl3_device_error.restype = Verdict
             L.exl3_device_error.argtypes = [ctypes.c_int32, P(ctypes.c_uint32), ctypes.c_int32]
+            L.exl3_resident.restype = Verdict
+            L.exl3_resident.argtypes = [P(Weight), ctypes.c_int32, ctypes.c_uint64, ctypes.c_void_p, P(ctypes.c_uint64)]
+            L.exl3_resident_pending.restype = ctypes.c_uint64
+            L.exl3_resident_pending.argtypes = []
             L.exl3_version.restype = ctypes.c_char_p
             L.exl3_version.argtypes = []
             _lib = L

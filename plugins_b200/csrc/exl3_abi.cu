@@ -264,7 +264,7 @@ DeviceState* device_state(int dev) {
   return &g_dev[dev];
 }
 
-bool rate_served(int n) { return n % 16 == 0 && n >= 16 && n <= 96; }  // integer K 1..6
+bool rate_served(int n) { return exl3::rate_served_n(n); }
 
 exl3_verdict check_linear_shape(int groups, int in_f, int out_f, int n) {
   if (groups < 1 || in_f <= 0 || out_f <= 0) return refuse(EXL3_UNSUPPORTED, "exl3_b200: empty weight");
@@ -272,7 +272,7 @@ exl3_verdict check_linear_shape(int groups, int in_f, int out_f, int n) {
     return refuse(EXL3_UNSUPPORTED, "exl3_b200: in and out features must be multiples of 128 (the Hadamard blocks)");
   if (!(n % 2 == 0 && n >= 16 && n <= 128)) return refuse(EXL3_UNSUPPORTED, "exl3_b200: not an admitted rate (n even, 16..128)");
   if (!rate_served(n))
-    return refuse(EXL3_UNSUPPORTED, "exl3_b200: fractional or >6-bit rates are not served by the sm_100a kernels");
+    return refuse(EXL3_UNSUPPORTED, "exl3_b200: rates off the half-bit grid or above 6 bits are not served by the sm_100a kernels");
   if (out_f / 128 > static_cast<int>(kCounterCount)) return refuse(EXL3_TOO_LARGE, "exl3_b200: out_features too large");
   return kOk;
 }
@@ -316,6 +316,17 @@ const exl3_verdict kNotShaped = {EXL3_UNSUPPORTED,
                                  "exl3_b200: not an EXL3 linear of the expected input width (trellis [in/16, out/16, n], "
                                  "suh f16 [in], svh f16 [out])"};
 
+// The block's codebook and codeword window as weight flags (EXL3_WEIGHT_MCG, EXL3_WEIGHT_WINDOW); 0 for mul1 at the
+// full window.
+uint32_t block_window_flags(exl3_str block_json) {
+  JVal b;
+  if (!parse_json(block_json, b) || b.kind != JVal::Obj) return 0;
+  const JVal* w = b.get("window");
+  uint32_t f = str_is(b.get("codebook"), "mcg") ? EXL3_WEIGHT_MCG : 0u;
+  if (!w || w->kind != JVal::Num || !w->is_int || w->num < 8 || w->num > 16) return f;
+  return f | EXL3_WEIGHT_WINDOW(static_cast<int>(w->num));
+}
+
 exl3_verdict upload_stack(const exl3_load_ctx* ctx, const std::vector<LinearParts>& parts, uint32_t flags,
                           exl3_weight* out) {
   const LinearParts& p0 = parts[0];
@@ -357,7 +368,7 @@ exl3_verdict upload_stack(const exl3_load_ctx* ctx, const std::vector<LinearPart
   }
   memset(out, 0, sizeof *out);
   out->size = sizeof(exl3_weight);
-  out->flags = EXL3_WEIGHT_OWNED | flags;
+  out->flags = EXL3_WEIGHT_OWNED | flags | block_window_flags(ctx->block_json);
   out->trellis = tr;
   out->suh = su;
   out->svh = sv;
@@ -372,10 +383,42 @@ exl3_verdict upload_stack(const exl3_load_ctx* ctx, const std::vector<LinearPart
   return kOk;
 }
 
+// ------------------------------------------------------------------ resident decoded matrices
+
+// A kept weight's GEMM B image (W_hat^T blocks of 128 columns x 64 k, f16; the layout images_kernel writes), per
+// group, with two column blocks of padding so a ragged last tile's reads stay inside it.  Keyed on the weight's
+// device pointers and shape.
+struct Resident {
+  int device;
+  const uint16_t *trellis, *suh, *svh;
+  int groups, in_f, out_f, n, nseg;
+  size_t group_bytes;
+  uint8_t* image;
+  bool filled;
+};
+std::mutex g_res_mu;
+std::vector<std::unique_ptr<Resident>> g_res;
+
+size_t resident_group_bytes(const exl3_weight* w) {
+  return static_cast<size_t>(w->out_features / 128 + 2) * w->in_features * 256;  // in/64 blocks of 16 KiB per column block
+}
+
+bool resident_is(const Resident& r, const exl3_weight* w) {
+  return r.device == w->device && r.trellis == w->trellis && r.suh == w->suh && r.svh == w->svh &&
+         r.groups == w->groups && r.in_f == w->in_features && r.out_f == w->out_features && r.n == w->n &&
+         r.nseg == w->nseg;
+}
+
+void resident_free(Resident& r) {
+  DeviceGuard guard(r.device);
+  cudaFree(r.image);
+}
+
 exl3_verdict check_weight(const exl3_weight* w) {
   if (!w || w->size != sizeof(exl3_weight) || !w->trellis || !w->suh || !w->svh)
     return refuse(EXL3_FAILED, "exl3_b200: not a loaded weight");
   if (w->nseg < 1 || w->nseg > EXL3_MAX_SEGMENTS) return refuse(EXL3_FAILED, "exl3_b200: bad segment count");
+  if (exl3::flags_window_bits(w->flags) < 8) return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3WindowUnsupported");
   return check_linear_shape(w->groups, w->in_features, w->out_features, w->n);
 }
 
@@ -428,9 +471,34 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
   uint8_t* a_img = d->image;
   uint8_t* b_img = d->image + static_cast<size_t>(mc) * row_bytes;
   // a multiple of the tile width, so a ragged last tile's reads stay inside the B region
-  const int64_t nc_cap = static_cast<int64_t>((d->image_bytes - static_cast<size_t>(mc) * row_bytes) / row_bytes) / bn * bn;
+  int64_t nc_cap = static_cast<int64_t>((d->image_bytes - static_cast<size_t>(mc) * row_bytes) / row_bytes) / bn * bn;
   if (nc_cap < bn) return refuse(EXL3_TOO_LARGE, "exl3_b200: in_features too large for the prefill image region");
   const int gcount = grouped ? groups : 1;
+  const uint32_t cw_mask = exl3::window_mask(exl3::flags_window_bits(w->flags));
+  const int mcg = (w->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
+  // a kept weight: its B image is decoded once (the first call fills it, on this stream) and read from there
+  uint8_t* kept = nullptr;
+  size_t kept_group = 0;
+  bool fill = false;
+  {
+    std::lock_guard<std::mutex> lk(g_res_mu);
+    for (auto& r : g_res)
+      if (resident_is(*r, w)) {
+        kept = r->image;
+        kept_group = r->group_bytes;
+        fill = !r->filled;
+        r->filled = true;
+        break;
+      }
+  }
+  if (kept) {
+    nc_cap = (static_cast<int64_t>(out_f) + bn - 1) / bn * bn;  // no column chunks: the B image is the kept one
+    for (int g = 0; fill && g < gcount; ++g)
+      if (exl3::launch_images(nullptr, x_dtype, 0, 0, 0, nullptr, 0, nullptr, w->trellis + static_cast<size_t>(g) * tile_halfs,
+                              in_f, out_f, 0, out_f, w->n, kept + static_cast<size_t>(g) * kept_group, st,
+                              cw_mask, mcg) != cudaSuccess)
+        return refuse(EXL3_FAILED, "exl3_b200: resident image launch failed");
+  }
   for (int g = 0; g < gcount; ++g) {
     const int64_t x_stride = grouped ? static_cast<int64_t>(groups) * in_f : in_f;
     const uint8_t* xg = static_cast<const uint8_t*>(x) + static_cast<size_t>(g) * in_f * xsz;
@@ -457,14 +525,15 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
           // the A image with the first column chunk's B image, in one launch
           if (exl3::launch_images(xg + static_cast<size_t>(r0) * x_stride * xsz, x_dtype, x_stride, m, mp, suh,
                                   (flags & EXL3_MATMUL_PREPARED) ? 1 : 0, j0 == 0 ? a_img : nullptr, trg, in_f, out_f,
-                                  c0 + j0, nc, w->n, b_img, st) != cudaSuccess)
+                                  c0 + j0, nc, w->n, kept ? nullptr : b_img, st, cw_mask, mcg) != cudaSuccess)
             return refuse(EXL3_FAILED, "exl3_b200: prefill operand images launch failed");
           mark(1);
           const int shape = gemm_shape_for(m, nc, d->sms);
           const int tbm = exl3::gemm_block_m(shape), tbn = exl3::gemm_block_n(shape);
           exl3::GemmParams gp{};
           gp.a_img = a_img;
-          gp.b_img = b_img;
+          gp.b_img = kept ? kept + static_cast<size_t>(g) * kept_group + static_cast<size_t>((c0 + j0) / 128) * in_f * 256
+                          : b_img;
           gp.svh = svh + j0;
           uint8_t* yp = yseg + (static_cast<size_t>(r0) * ystride + j0) * ysz;
           gp.y = yp;
@@ -513,7 +582,6 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
   const int split = sp ? atoi(sp) : 0;
   const int in_f = w->in_features, out_f = w->out_features, groups = w->groups;
   const bool grouped = (w->flags & EXL3_WEIGHT_GROUPED) != 0;
-  const int K = w->n / 16;
   const bool imma = (flags & EXL3_MATMUL_DP4A) == 0;
   const size_t tile_halfs = static_cast<size_t>(in_f / 16) * (out_f / 16) * w->n;
   const size_t xsz = x_dtype == EXL3_F32 ? 4 : 2;
@@ -548,23 +616,29 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
       for (int s = w->nseg + 1; s <= exl3::kMaxSegments; ++s) gp.seg_cb[s] = gp.seg_cb[w->nseg];
       gp.prepared = (flags & EXL3_MATMUL_PREPARED) ? 1 : 0;
       gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
+      gp.cw_mask = exl3::window_mask(exl3::flags_window_bits(w->flags));
+      gp.mcg = (w->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
+      if ((gp.cw_mask || gp.mcg) && !imma)
+        return refuse(EXL3_UNSUPPORTED, "exl3_b200: a narrowed codeword window or mcg takes the tensor-pipe order (no dp4a)");
       const char* why = nullptr;
       // the persistent GEMV for large launches (every row count of a shape takes the same kernel, so a row's bits do
-      // not depend on the rows batched with it), the cluster-split one below
-      const bool v6 = imma && (gv_pick == 6 || (gv_pick == 0 && exl3::gemv6_prefers(gp)));
+      // not depend on the rows batched with it), the cluster-split one below (and for a narrowed codeword window)
+      const bool v6 = imma && !gp.cw_mask && !gp.mcg && (gv_pick == 6 || (gv_pick == 0 && exl3::gemv6_prefers(gp)));
       if (v6 && exl3::gemv6_scratch_bytes(gp, d->sms) <= d->partial_floats * 4) {
-        if (exl3::launch_gemv6(gp, K, d->sms, d->partials, d->counters, st) != cudaSuccess)
+        if (exl3::launch_gemv6(gp, w->n, d->sms, d->partials, d->counters, st) != cudaSuccess)
           return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
         continue;
       }
       // the cluster-split GEMV where a split fits (every served width), else the grid-stride one with global partials
-      if (gemv_v5 && exl3::gemv5_geometry(gp, K, d->sms, rg, split, &why)) {
-        if (exl3::launch_gemv5(gp, K, rg, imma, st, true) != cudaSuccess)
+      if (gemv_v5 && exl3::gemv5_geometry(gp, w->n, d->sms, rg, split, &why)) {
+        if (exl3::launch_gemv5(gp, w->n, rg, imma, st, true) != cudaSuccess)
           return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
         continue;
       }
+      if (gp.cw_mask || gp.mcg)
+        return refuse(EXL3_UNSUPPORTED, "exl3_b200: a narrowed codeword window or mcg needs a cluster split of this input width");
       if (!exl3::gemv_geometry(gp, d->sms, rg, d->partial_floats, &why)) return refuse(EXL3_TOO_LARGE, why);
-      if (exl3::launch_gemv(gp, K, rg, imma, st, true) != cudaSuccess)
+      if (exl3::launch_gemv(gp, w->n, rg, imma, st, true) != cudaSuccess)
         return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
     }
   }
@@ -599,7 +673,6 @@ exl3_verdict exl3_validate(exl3_str block_json, exl3_str config_json) {
   if (const JVal* w = b.get("window")) {
     if (w->kind != JVal::Num || !w->is_int || w->num < 8 || w->num > 16)
       return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3WindowUnsupported");
-    if (w->num != 16) return refuse(EXL3_UNSUPPORTED, "exl3_b200: narrowed codeword windows are not served");
   }
   if (const JVal* k = b.get("k")) {
     if (k->kind != JVal::Num) return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3RateUnsupported");
@@ -607,7 +680,7 @@ exl3_verdict exl3_validate(exl3_str block_json, exl3_str config_json) {
     if (std::fabs(scaled - n) > 1e-6 || n < 16 || n > 128 || std::fmod(n, 2.0) != 0)
       return refuse(EXL3_UNSUPPORTED, "exl3_b200: Exl3RateUnsupported");
     if (!rate_served(static_cast<int>(n)))
-      return refuse(EXL3_UNSUPPORTED, "exl3_b200: fractional or >6-bit rates are not served by the sm_100a kernels");
+      return refuse(EXL3_UNSUPPORTED, "exl3_b200: rates off the half-bit grid or above 6 bits are not served by the sm_100a kernels");
   }
   return kOk;
 }
@@ -622,7 +695,7 @@ uint64_t exl3_bill(exl3_str block_json, exl3_str model_dir, uint64_t stored) {
 //
 // plugins/turboexl3_qwen38/config.zig:19-119 (claims, parse, checkPack / checkBlock) and src/direct/config.zig:301-420
 // (parseJson): MLX-free and bounds-checked, the EXL3 blocks refused with the reference's names, narrowed to what this
-// library decodes (the mul1 codebook named, 16-bit windows, whole bits per weight 1..6).
+// library decodes (the mul1 or mcg codebook named; windows 8..16; whole and half bits per weight 1..6).
 
 namespace {
 
@@ -632,15 +705,16 @@ bool is_qwen38(const std::string& mt) { return mt == "qwen4_exp" || mt == "qwen4
 
 const char* check_model_block(const JVal& o, bool bank, uint32_t* rate_n) {
   if (!str_is(o.get("format"), "exl3")) return "turboexl3_qwen38: NotExl3";
-  // the reference also decodes mcg and lets a trunk block leave its codebook unnamed; here mul1, named
-  if (!str_is(o.get("codebook"), "mul1")) return "turboexl3_qwen38: Exl3CodebookUnsupported";
+  // mul1 or mcg (the reference also lets a trunk block leave its codebook unnamed; here it is named)
+  if (!str_is(o.get("codebook"), "mul1") && !str_is(o.get("codebook"), "mcg"))
+    return "turboexl3_qwen38: Exl3CodebookUnsupported";
   if (const JVal* w = o.get("window"))
-    if (w->kind != JVal::Num || !w->is_int || w->num != 16) return "turboexl3_qwen38: Exl3WindowUnsupported";
+    if (w->kind != JVal::Num || !w->is_int || w->num < 8 || w->num > 16) return "turboexl3_qwen38: Exl3WindowUnsupported";
   if (bank) {
     const JVal* k = o.get("k");
     if (!k || k->kind != JVal::Num) return "turboexl3_qwen38: Exl3RateUnsupported";
     const double scaled = k->num * 16.0, n = std::round(scaled);
-    if (!std::isfinite(scaled) || std::fabs(scaled - n) > 1e-6 || n < 16 || n > 96 || std::fmod(n, 16.0) != 0)
+    if (!std::isfinite(scaled) || std::fabs(scaled - n) > 1e-6 || !exl3::rate_served_n(static_cast<int>(n)))
       return "turboexl3_qwen38: Exl3RateUnsupported";
     *rate_n = static_cast<uint32_t>(n);
   }
@@ -724,6 +798,16 @@ exl3_verdict exl3_open(exl3_load_ctx* ctx) {
   if (!ctx || ctx->size != sizeof(exl3_load_ctx)) return refuse(EXL3_FAILED, "exl3_b200: bad load context");
   if (exl3_claims(ctx->block_json, ctx->config_json) == EXL3_CLAIM_NO)
     return refuse(EXL3_UNSUPPORTED, "exl3_b200: not an exllamav3 mul1 block");
+  // a pack the model seam claims (qwen38) loads by that seam's block rules (mul1 or mcg, windows 8..16,
+  // config.zig:86-104); the quant seam's own validate is the ds41 plugin's (mul1 only, config.zig:49-53)
+  JVal cfg, blk;
+  if (parse_json(ctx->config_json, cfg) && cfg.kind == JVal::Obj && cfg.get("model_type") &&
+      cfg.get("model_type")->kind == JVal::Str && is_qwen38(cfg.get("model_type")->str) &&
+      parse_json(ctx->block_json, blk) && blk.kind == JVal::Obj) {
+    uint32_t rate_n = 0;
+    if (const char* why = check_model_block(blk, blk.get("k") != nullptr, &rate_n)) return refuse(EXL3_UNSUPPORTED, why);
+    return ensure_device(ctx->device);
+  }
   exl3_verdict v = exl3_validate(ctx->block_json, ctx->config_json);
   if (v.code != EXL3_OK) return v;
   return ensure_device(ctx->device);
@@ -787,6 +871,16 @@ exl3_verdict exl3_load_bank(const exl3_load_ctx* ctx, exl3_str name, uint32_t in
 
 void exl3_release(exl3_weight* w) {
   if (!w) return;
+  if (w->size == sizeof(exl3_weight)) {  // its kept matrices go with it
+    std::lock_guard<std::mutex> lk(g_res_mu);
+    for (size_t i = 0; i < g_res.size();)
+      if (resident_is(*g_res[i], w)) {
+        resident_free(*g_res[i]);
+        g_res.erase(g_res.begin() + static_cast<std::ptrdiff_t>(i));
+      } else {
+        ++i;
+      }
+  }
   if ((w->flags & EXL3_WEIGHT_OWNED) && w->size == sizeof(exl3_weight)) {
     DeviceGuard guard(w->device);
     cudaFree(w->trellis);
@@ -889,13 +983,15 @@ exl3_verdict exl3_matmul_tp(const exl3_weight* w, const exl3_tensor* x, exl3_tp*
     cbb += static_cast<int32_t>(seg_total[s] / 128);
   }
   gp.tp = td;
+  gp.cw_mask = exl3::window_mask(exl3::flags_window_bits(w->flags));
+  gp.mcg = (w->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
   gp.tp_slot = slot;
   gp.tp_meta_cb = static_cast<uint32_t>(cbb);
   gp.tp_meta_bytes = static_cast<uint32_t>(rows * total * esize);
   const int rg = rows <= 8 ? 1 : 2;
   const char* why = nullptr;
-  if (!exl3::gemv5_geometry(gp, w->n / 16, d->sms, rg, 0, &why)) return refuse(EXL3_UNSUPPORTED, why);
-  if (exl3::launch_gemv5(gp, w->n / 16, rg, true, static_cast<cudaStream_t>(stream), true) != cudaSuccess)
+  if (!exl3::gemv5_geometry(gp, w->n, d->sms, rg, 0, &why)) return refuse(EXL3_UNSUPPORTED, why);
+  if (exl3::launch_gemv5(gp, w->n, rg, true, static_cast<cudaStream_t>(stream), true) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_matmul_tp: GEMV launch failed");
   return kOk;
 }
@@ -953,8 +1049,8 @@ exl3_verdict exl3_weight_stack(const exl3_weight* parts, int32_t count, void* st
     exl3_verdict v = check_weight(&parts[i]);
     if (v.code != EXL3_OK) return v;
     if (parts[i].groups != 1 || parts[i].nseg != 1 || parts[i].in_features != p0.in_features || parts[i].n != p0.n ||
-        parts[i].device != p0.device)
-      return refuse(EXL3_UNSUPPORTED, "exl3_b200: stacked linears share one input width, rate and device");
+        parts[i].device != p0.device || ((parts[i].flags ^ p0.flags) & (EXL3_WEIGHT_WINDOW_MASK | EXL3_WEIGHT_MCG)))
+      return refuse(EXL3_UNSUPPORTED, "exl3_b200: stacked linears share one input width, rate, codebook, codeword window and device");
     total += parts[i].out_features;
   }
   exl3_verdict v = check_linear_shape(1, p0.in_features, total, p0.n);
@@ -995,7 +1091,7 @@ exl3_verdict exl3_weight_stack(const exl3_weight* parts, int32_t count, void* st
   }
   out->seg_cols[count] = total;
   out->size = sizeof(exl3_weight);
-  out->flags = EXL3_WEIGHT_OWNED;
+  out->flags = EXL3_WEIGHT_OWNED | (p0.flags & (EXL3_WEIGHT_WINDOW_MASK | EXL3_WEIGHT_MCG));
   out->trellis = tr;
   out->suh = su;
   out->svh = sv;
@@ -1015,7 +1111,9 @@ exl3_verdict exl3_decode_dense(const exl3_weight* w, int32_t group, uint16_t* ou
   DeviceGuard guard(w->device);
   const size_t tw = static_cast<size_t>(w->in_features / 16) * (w->out_features / 16) * w->n;
   if (exl3::launch_decode_dense(w->trellis + group * tw, w->in_features, w->out_features, w->n, out,
-                                (flags & EXL3_MATMUL_DP4A) ? 0 : 1, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+                                (flags & EXL3_MATMUL_DP4A) ? 0 : 1, static_cast<cudaStream_t>(stream),
+                                exl3::window_mask(exl3::flags_window_bits(w->flags)),
+                                (w->flags & EXL3_WEIGHT_MCG) ? 1 : 0) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_b200: decode launch failed");
   return kOk;
 }
@@ -1025,9 +1123,63 @@ exl3_verdict exl3_encode_trellis(const float* target, int32_t in_features, int32
   if (!target || !trellis) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
   exl3_verdict v = check_linear_shape(1, in_features, out_features, n);
   if (v.code != EXL3_OK) return v;
+  if (n % 16 != 0) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the encoder searches whole-bit trellises only");
   if (exl3::launch_encode(target, in_features, out_features, n, trellis, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_b200: encoder launch failed");
   return kOk;
+}
+
+exl3_verdict exl3_resident(const exl3_weight* ws, int32_t count, uint64_t room, void* stream, uint64_t* bytes) {
+  (void)stream;  // the memory is reserved here and filled by the first prefill call, on that call's stream
+  std::lock_guard<std::mutex> lk(g_res_mu);
+  uint64_t held = 0;
+  if (count == 0) {
+    for (auto& r : g_res) resident_free(*r);
+    g_res.clear();
+  } else {
+    if (!ws || count < 0) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
+    for (const auto& r : g_res) held += static_cast<uint64_t>(r->group_bytes) * r->groups;
+    std::vector<const exl3_weight*> add;
+    uint64_t more = 0;
+    for (int i = 0; i < count; ++i) {
+      const exl3_weight* w = &ws[i];
+      exl3_verdict v = check_weight(w);
+      if (v.code != EXL3_OK) return v;
+      if ((w->flags & EXL3_WEIGHT_BANK) && !(w->flags & EXL3_WEIGHT_GROUPED))
+        return refuse(EXL3_UNSUPPORTED, "exl3_b200: routed banks are not kept (their calls are decode GEMVs)");
+      bool kept = false;
+      for (const auto& r : g_res) kept = kept || resident_is(*r, w);
+      for (const exl3_weight* a : add) kept = kept || (a->device == w->device && a->trellis == w->trellis);
+      if (kept) continue;
+      add.push_back(w);
+      more += static_cast<uint64_t>(resident_group_bytes(w)) * w->groups;
+    }
+    if (room > 0 && held + more > room) return refuse(EXL3_TOO_LARGE, "exl3_b200: the kept matrices pass the room");
+    std::vector<std::unique_ptr<Resident>> made;
+    for (const exl3_weight* w : add) {
+      auto r = std::make_unique<Resident>();
+      *r = Resident{w->device, w->trellis, w->suh, w->svh, w->groups, w->in_features, w->out_features, w->n, w->nseg,
+                    resident_group_bytes(w), nullptr, false};
+      DeviceGuard guard(w->device);
+      if (cudaMalloc(&r->image, r->group_bytes * w->groups) != cudaSuccess) {
+        for (auto& m : made) resident_free(*m);
+        return refuse(EXL3_TOO_LARGE, "exl3_b200: out of device memory for the kept matrices");
+      }
+      made.push_back(std::move(r));
+    }
+    for (auto& r : made) g_res.push_back(std::move(r));
+    held += more;
+  }
+  if (bytes) *bytes = held;
+  return kOk;
+}
+
+uint64_t exl3_resident_pending(void) {
+  std::lock_guard<std::mutex> lk(g_res_mu);
+  uint64_t pending = 0;
+  for (const auto& r : g_res)
+    if (!r->filled) pending += static_cast<uint64_t>(r->group_bytes) * r->groups;
+  return pending;
 }
 
 exl3_verdict exl3_device_error(int32_t device, uint32_t* bits, int32_t clear) {

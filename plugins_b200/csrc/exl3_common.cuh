@@ -12,6 +12,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "exl3_windows.h"
+
 namespace exl3 {
 
 constexpr uint32_t kMul1Mult = 0x83DCD12Du;
@@ -196,6 +198,23 @@ __device__ __forceinline__ void lane_codewords(const uint32_t* tile_words, const
   }
 }
 
+// A tile of N halfwords (N = 16 x bits per weight; half-bit rates included): whole-bit rates take the extraction
+// above, half-bit rates the general rule of exl3_windows.h (the same windows: both follow the bitstream rule).  NW
+// (a narrowed codeword window, lw.mask): the general rule at every rate, each window masked.
+template <int N, bool NW = false>
+__device__ __forceinline__ void tile_codewords(const uint32_t* tile_words, const LaneWin<N>& lw, uint32_t (&w)[8]) {
+  if constexpr (N % 16 == 0 && !NW) {
+    LaneWindows<N / 16> lk;
+    lk.o0 = lw.o0;
+    lk.o1 = lw.o1;
+    lk.o2 = lw.o2;
+    lk.sh = lw.sh;
+    lane_codewords<N / 16>(tile_words, lk, w);
+  } else {
+    lane_windows<N, NW>(tile_words, lw, w);
+  }
+}
+
 // mul1 of a pair of codewords: f16x2 (lo = cw_a, hi = cw_b) with exactly one rounding, as the reference.
 __device__ __forceinline__ uint32_t mul1_pair_dp4a(uint32_t cw_a, uint32_t cw_b) {
   // unsigned byte sums (the int overload of __dp4a sums signed bytes)
@@ -268,6 +287,58 @@ __device__ __forceinline__ void decode_afrag_imma(const uint32_t (&w)[8], const 
   a[1] = mul1_pack_affine<kPackFma>(d1[0], d1[2]);  // col g+8
   a[2] = mul1_pack_affine<kPackFma>(d0[1], d0[3]);  // col g,   k' 2q+8..     <- phys 4q+2, 4q+3
   a[3] = mul1_pack_affine<kPackFma>(d1[1], d1[3]);  // col g+8
+}
+
+// ------------------------------------------------------------------ the mcg codebook
+
+constexpr uint32_t kMcgMult = 0xCBAC1FEDu;
+
+// mcg of a pair of codewords (plugins/sushi_ds41/src/sushi/exl3/expert_exl3.zig:267-273 decodeMcg): each codeword's
+// product, masked and flipped, is a pair of f16 halves whose sum is the weight.  The halves are normal with biased
+// exponents 12..15, so their f32 sum is exact and its single f16 rounding is the f16x2 add's (the same bits for all
+// 65,536 codewords).  Out: f16x2, lo = cw_a's weight, hi = cw_b's.
+__device__ __forceinline__ uint32_t mcg_pair(uint32_t cw_a, uint32_t cw_b) {
+  const uint32_t pa = ((cw_a * kMcgMult) & 0x8FFF8FFFu) ^ 0x3B603B60u;
+  const uint32_t pb = ((cw_b * kMcgMult) & 0x8FFF8FFFu) ^ 0x3B603B60u;
+  const uint32_t lo = __byte_perm(pa, pb, 0x5410), hi = __byte_perm(pa, pb, 0x7632);
+  uint32_t out;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(out) : "r"(lo), "r"(hi));
+  return out;
+}
+
+// ------------------------------------------------------------------ one tile's A fragment, by decode spec
+//
+// DS: 0 = mul1 at the full 16-bit window, 1 = mul1 at a narrowed window (lw.mask), 2 = mcg (any window: lw.mask).
+
+template <int N, int DS, bool kPackFma = false>
+__device__ __forceinline__ void decode_tile_imma(const uint32_t* tile_words, const LaneWin<N>& lw,
+                                                 const ImmaWin<N>& iw, const ImmaIndicator& ind, uint32_t (&a)[4]) {
+  uint32_t w[8];
+  if constexpr (DS == 2) {
+    // the tensor-pipe order: this lane's k = 4q .. 4q + 3 come from two neighbours' windows (exl3_windows.h)
+    imma_windows<N>(tile_words, iw, w);
+    a[0] = mcg_pair(w[0], w[1]);  // column g,     k 4q, 4q + 1
+    a[1] = mcg_pair(w[2], w[3]);  // column g + 8
+    a[2] = mcg_pair(w[4], w[5]);  // column g,     k 4q + 2, 4q + 3
+    a[3] = mcg_pair(w[6], w[7]);  // column g + 8
+  } else {
+    tile_codewords<N, DS == 1>(tile_words, lw, w);
+    decode_afrag_imma<kPackFma>(w, ind, a);
+  }
+}
+
+template <int N, int DS>
+__device__ __forceinline__ void decode_tile_natural(const uint32_t* tile_words, const LaneWin<N>& lw, uint32_t (&a)[4]) {
+  uint32_t w[8];
+  tile_codewords<N, DS != 0>(tile_words, lw, w);
+  if constexpr (DS == 2) {
+    a[0] = mcg_pair(w[0], w[1]);
+    a[1] = mcg_pair(w[4], w[5]);
+    a[2] = mcg_pair(w[2], w[3]);
+    a[3] = mcg_pair(w[6], w[7]);
+  } else {
+    decode_afrag_dp4a(w, a);
+  }
 }
 
 // D[16 x 8] += A[16 x 16] (f16) * B[16 x 8] (f16), f32 accumulate.

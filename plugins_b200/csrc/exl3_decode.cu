@@ -10,25 +10,28 @@
 
 namespace exl3 {
 
-template <int K, bool IMMA>
+template <int N, bool IMMA, int DS>
 __global__ void __launch_bounds__(256) decode_dense_kernel(const uint16_t* __restrict__ trellis, int in_features,
-                                                           int out_features, uint16_t* __restrict__ out) {
+                                                           int out_features, uint16_t* __restrict__ out,
+                                                           uint32_t cw_mask) {
   const uint32_t lane = threadIdx.x & 31u;
   const int ot = out_features / 16;
   const size_t tiles = static_cast<size_t>(in_features / 16) * ot;
   const size_t tile = static_cast<size_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (tile >= tiles) return;  // warp-uniform
   const int tk = static_cast<int>(tile / ot), tn = static_cast<int>(tile % ot);
-  const uint32_t* tw = reinterpret_cast<const uint32_t*>(trellis + tile * (16 * K));
-  LaneWindows<K> lw;
+  const uint32_t* tw = reinterpret_cast<const uint32_t*>(trellis + tile * N);
+  LaneWin<N> lw;
   lw.init(lane);
-  uint32_t w[8], a[4];
-  lane_codewords<K>(tw, lw, w);
+  lw.mask = cw_mask;
+  uint32_t a[4];
   const uint32_t g = lane >> 2, q = lane & 3u;
   if constexpr (IMMA) {
     ImmaIndicator ind;
     ind.init(lane);
-    decode_afrag_imma(w, ind, a);
+    ImmaWin<N> iw;
+    if constexpr (DS == 2) iw.init(lane, cw_mask);
+    decode_tile_imma<N, DS>(tw, lw, iw, ind, a);
     // a[0] = col g at k 4q, 4q+1; a[2] = col g at k 4q+2, 4q+3; a[1], a[3] = col g+8
     const int k0 = 4 * q;
     const int r = tk * 16, c = tn * 16;
@@ -42,7 +45,7 @@ __global__ void __launch_bounds__(256) decode_dense_kernel(const uint16_t* __res
       out[static_cast<size_t>(r + k0 + 3) * out_features + c + cols[h]] = static_cast<uint16_t>(hi[h] >> 16);
     }
   } else {
-    decode_afrag_dp4a(w, a);
+    decode_tile_natural<N, DS>(tw, lw, a);
     // a[0] = (j0, j1) col g k 2q..; a[1] = (j4, j5) col g+8; a[2] = (j2, j3) col g k 2q+8..; a[3] = (j6, j7)
     const int r = tk * 16, c = tn * 16;
     const int k0 = 2 * q;
@@ -58,27 +61,21 @@ __global__ void __launch_bounds__(256) decode_dense_kernel(const uint16_t* __res
 }
 
 template <bool IMMA>
-static cudaError_t launch_dd(const uint16_t* trellis, int in_features, int out_features, int K, uint16_t* out,
-                             cudaStream_t st) {
+static cudaError_t launch_dd(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
+                             cudaStream_t st, uint32_t cw_mask, int mcg) {
   const size_t tiles = static_cast<size_t>(in_features / 16) * (out_features / 16);
   const dim3 grid(static_cast<unsigned>((tiles + 7) / 8)), block(256);
-  switch (K) {
-    case 1: decode_dense_kernel<1, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    case 2: decode_dense_kernel<2, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    case 3: decode_dense_kernel<3, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    case 4: decode_dense_kernel<4, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    case 5: decode_dense_kernel<5, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    case 6: decode_dense_kernel<6, IMMA><<<grid, block, 0, st>>>(trellis, in_features, out_features, out); break;
-    default: return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  const bool served = with_rate_decode(n, cw_mask, mcg != 0, [&](auto N, auto DS) {
+    decode_dense_kernel<decltype(N)::value, IMMA, decltype(DS)::value>
+        <<<grid, block, 0, st>>>(trellis, in_features, out_features, out, spec_mask(cw_mask));
+  });
+  return served ? cudaGetLastError() : cudaErrorInvalidValue;
 }
 
 cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
-                                int imma, cudaStream_t st) {
-  if (n % 16 != 0) return cudaErrorInvalidValue;
-  return imma ? launch_dd<true>(trellis, in_features, out_features, n / 16, out, st)
-              : launch_dd<false>(trellis, in_features, out_features, n / 16, out, st);
+                                int imma, cudaStream_t st, uint32_t cw_mask, int mcg) {
+  return imma ? launch_dd<true>(trellis, in_features, out_features, n, out, st, cw_mask, mcg)
+              : launch_dd<false>(trellis, in_features, out_features, n, out, st, cw_mask, mcg);
 }
 
 }  // namespace exl3

@@ -93,6 +93,7 @@ cudaError_t launch_encode(const float* target, int in_features, int out_features
                           cudaStream_t st) {
   const size_t tiles = static_cast<size_t>(in_features / 16) * (out_features / 16);
   const dim3 grid(static_cast<unsigned>((tiles + 63) / 64)), block(64);
+  if (n % 16 != 0) return cudaErrorInvalidValue;  // the encoder searches whole-bit trellises only
   switch (n / 16) {
     case 1: encode_kernel<1><<<grid, block, 0, st>>>(target, in_features, out_features, trellis); break;
     case 2: encode_kernel<2><<<grid, block, 0, st>>>(target, in_features, out_features, trellis); break;

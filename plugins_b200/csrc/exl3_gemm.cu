@@ -160,6 +160,7 @@ struct ImageJobs {
   uint8_t* b_img;
   int64_t decode_jobs;   // (in/16) * ncol_tiles / kDecodeTilesPerWarp warps
   int32_t in_features;
+  uint32_t cw_mask;      // a narrowed codeword window's mask (0: the full 16-bit window)
 };
 
 // Prepare job: one warp per (row, 128-wide input block), lane t holding elements 4t..4t+3 (vector loads and one
@@ -215,26 +216,32 @@ __device__ __forceinline__ void prep_job(const ImageJobs& j, int64_t job, uint32
 // Decode job: kDecodeTilesPerWarp consecutive 16x16 tiles of one k-row (contiguous in the trellis).  Each lane holds
 // one column's four consecutive k per tile (the IMMA byte-sum order) and writes them as one 8-byte store; a warp's
 // stores fill whole 32-byte sectors.
-template <int K>
+template <int N, int DS>
 __device__ __forceinline__ void decode_job(const ImageJobs& j, int64_t job, uint32_t lane) {
   const int groups = j.ncol_tiles / kDecodeTilesPerWarp;
   const int tk = static_cast<int>(job / groups), tj0 = static_cast<int>(job % groups) * kDecodeTilesPerWarp;
   const uint32_t* tw =
-      reinterpret_cast<const uint32_t*>(j.trellis + (static_cast<size_t>(tk) * j.out_tiles + j.tn0 + tj0) * (16 * K));
-  LaneWindows<K> lw;
+      reinterpret_cast<const uint32_t*>(j.trellis + (static_cast<size_t>(tk) * j.out_tiles + j.tn0 + tj0) * N);
+  LaneWin<N> lw;
   lw.init(lane);
+  lw.mask = j.cw_mask;
   ImmaIndicator ind;
   ind.init(lane);
+  ImmaWin<N> iw;
+  if constexpr (DS == 2) iw.init(lane, j.cw_mask);
   uint32_t w[kDecodeTilesPerWarp][8];
+  if constexpr (DS != 2) {
 #pragma unroll
-  for (int t = 0; t < kDecodeTilesPerWarp; ++t) lane_codewords<K>(tw + t * 8 * K, lw, w[t]);
+    for (int t = 0; t < kDecodeTilesPerWarp; ++t) tile_codewords<N, DS == 1>(tw + t * (N / 2), lw, w[t]);
+  }
   const uint32_t g = lane >> 2, q = lane & 3u;
   const int kbs = j.in_features / kImgK;
   const uint32_t kin = static_cast<uint32_t>(tk & 3) * 16u + 4u * q;
 #pragma unroll
   for (int t = 0; t < kDecodeTilesPerWarp; ++t) {
-    uint32_t a[4];
-    decode_afrag_imma(w[t], ind, a);  // a[0], a[2]: column g at k 4q..4q+3; a[1], a[3]: column g + 8
+    uint32_t a[4];  // a[0], a[2]: column g at k 4q..4q+3; a[1], a[3]: column g + 8
+    if constexpr (DS == 2) decode_tile_imma<N, 2>(tw + t * (N / 2), lw, iw, ind, a);
+    else decode_afrag_imma(w[t], ind, a);
     const int tj = tj0 + t;
     const uint32_t n = static_cast<uint32_t>(tj & 7) * 16u + g;
     uint8_t* blk = j.b_img + (static_cast<size_t>(tj >> 3) * kbs + (tk >> 2)) * kImgBytes;
@@ -244,11 +251,11 @@ __device__ __forceinline__ void decode_job(const ImageJobs& j, int64_t job, uint
 }
 
 // Decode warps first (the longer jobs), then prepare warps; every job is one warp.
-template <int K>
+template <int N, int DS>
 __global__ void __launch_bounds__(256) images_kernel(const ImageJobs j) {
   const uint32_t lane = threadIdx.x & 31u;
   const int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);  // warp-uniform
-  if (job < j.decode_jobs) decode_job<K>(j, job, lane);
+  if (job < j.decode_jobs) decode_job<N, DS>(j, job, lane);
   else if (job < j.decode_jobs + j.prep_jobs) prep_job(j, job - j.decode_jobs, lane);
 }
 
@@ -474,10 +481,11 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
 
 cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, const uint16_t* suh,
                           int prepared, uint8_t* a_img, const uint16_t* trellis, int in_features, int out_features,
-                          int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st) {
-  if (in_features % 128 != 0 || n % 16 != 0) return cudaErrorInvalidValue;
+                          int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st, uint32_t cw_mask, int mcg) {
+  if (in_features % 128 != 0 || !rate_served_n(n)) return cudaErrorInvalidValue;
   ImageJobs j{};
   j.in_features = in_features;
+  j.cw_mask = spec_mask(cw_mask);
   if (a_img) {
     if (mp % 128 != 0 || m > mp) return cudaErrorInvalidValue;
     const size_t vec = x_dtype == kF32 ? 16 : 8;  // four elements per vector load
@@ -496,16 +504,10 @@ cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, 
   const int64_t warps = j.prep_jobs + j.decode_jobs;
   if (warps == 0) return cudaSuccess;
   const dim3 grid(static_cast<unsigned>((warps + 7) / 8)), block(256);
-  switch (n / 16) {
-    case 1: images_kernel<1><<<grid, block, 0, st>>>(j); break;
-    case 2: images_kernel<2><<<grid, block, 0, st>>>(j); break;
-    case 3: images_kernel<3><<<grid, block, 0, st>>>(j); break;
-    case 4: images_kernel<4><<<grid, block, 0, st>>>(j); break;
-    case 5: images_kernel<5><<<grid, block, 0, st>>>(j); break;
-    case 6: images_kernel<6><<<grid, block, 0, st>>>(j); break;
-    default: return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  const bool served = with_rate_decode(n, b_img ? cw_mask : 0u, b_img && mcg, [&](auto N, auto DS) {
+    images_kernel<decltype(N)::value, decltype(DS)::value><<<grid, block, 0, st>>>(j);
+  });
+  return served ? cudaGetLastError() : cudaErrorInvalidValue;
 }
 
 template <int MS, int NS>

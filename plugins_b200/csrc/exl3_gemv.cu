@@ -116,9 +116,9 @@ __device__ __forceinline__ uint32_t release_add(uint32_t* ctr) {
   return atomicAdd(ctr, 1u);
 }
 
-template <int K, int RG, bool IMMA>
+template <int N, int RG, bool IMMA>
 __global__ void __launch_bounds__(kThreads, RG == 1 ? kGemvCtasPerSm : 2) gemv_kernel(GemvParams p) {
-  constexpr uint32_t kTileBytes = 32u * K;           // 2n bytes
+  constexpr uint32_t kTileBytes = 2u * N;            // 2n bytes
   constexpr uint32_t kUnitBytes = 8u * kTileBytes;   // one unit: 8 tiles, contiguous in the pack layout
   constexpr uint32_t kSlabX = RG * 256u;             // activation fragments of one slab
   constexpr uint32_t W = kWarps;
@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, RG == 1 ? kGemvCtasPerSm : 2) gemv_k
   }
 
   // ---- main loop: runs of one (segment, chunk, column block), each ending in the block epilogue
-  LaneWindows<K> lwin;
+  LaneWin<N> lwin;
   lwin.init(lane);
   ImmaIndicator ind;
   ind.init(lane);
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, RG == 1 ? kGemvCtasPerSm : 2) gemv_k
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         uint32_t w[8], a[4];
-        lane_codewords<K>(tw + t * (kTileBytes / 4u), lwin, w);
+        tile_codewords<N>(tw + t * (kTileBytes / 4u), lwin, w);
         if constexpr (IMMA) decode_afrag_imma(w, ind, a);
         else decode_afrag_dp4a(w, a);
 #pragma unroll
@@ -380,16 +380,16 @@ __global__ void __launch_bounds__(kThreads, RG == 1 ? kGemvCtasPerSm : 2) gemv_k
 
 // ------------------------------------------------------------------ host launch
 
-template <int K, int RG, bool IMMA>
+template <int N, int RG, bool IMMA>
 static size_t gemv_smem_bytes(size_t xp_bytes, int rows) {
-  return xp_bytes + static_cast<size_t>(kWarps) * kStages * 8u * 32u * K +
+  return xp_bytes + static_cast<size_t>(kWarps) * kStages * 8u * 2u * N +
          static_cast<size_t>(kWarps) * rows * kRedStride * 4 + 16 + (2 * kMaxChunks + kMaxContrib) * 4;
 }
 
-template <int K, int RG, bool IMMA>
+template <int N, int RG, bool IMMA>
 static cudaError_t launch_gemv_t(const GemvParams& p, unsigned grid, cudaStream_t st, bool pdl) {
-  auto kern = gemv_kernel<K, RG, IMMA>;
-  const size_t smem = gemv_smem_bytes<K, RG, IMMA>(p.xp_bytes, p.rows);
+  auto kern = gemv_kernel<N, RG, IMMA>;
+  const size_t smem = gemv_smem_bytes<N, RG, IMMA>(p.xp_bytes, p.rows);
   static KernelSetup setup;
   if (cudaError_t e = kernel_setup(setup, kern, kThreads, smem); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -406,16 +406,10 @@ static cudaError_t launch_gemv_t(const GemvParams& p, unsigned grid, cudaStream_
 }
 
 template <int RG, bool IMMA>
-static cudaError_t launch_gemv_k(const GemvParams& p, int K, unsigned grid, cudaStream_t st, bool pdl) {
-  switch (K) {
-    case 1: return launch_gemv_t<1, RG, IMMA>(p, grid, st, pdl);
-    case 2: return launch_gemv_t<2, RG, IMMA>(p, grid, st, pdl);
-    case 3: return launch_gemv_t<3, RG, IMMA>(p, grid, st, pdl);
-    case 4: return launch_gemv_t<4, RG, IMMA>(p, grid, st, pdl);
-    case 5: return launch_gemv_t<5, RG, IMMA>(p, grid, st, pdl);
-    case 6: return launch_gemv_t<6, RG, IMMA>(p, grid, st, pdl);
-    default: return cudaErrorInvalidValue;
-  }
+static cudaError_t launch_gemv_k(const GemvParams& p, int n, unsigned grid, cudaStream_t st, bool pdl) {
+  cudaError_t e = cudaErrorInvalidValue;
+  with_rate(n, [&](auto N) { e = launch_gemv_t<decltype(N)::value, RG, IMMA>(p, grid, st, pdl); });
+  return e;
 }
 
 // Host copy of the kernel's partition arithmetic.
@@ -493,10 +487,11 @@ bool gemv_geometry(GemvParams& p, int sms, int row_groups, size_t partial_capaci
   return true;
 }
 
-cudaError_t launch_gemv(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl) {
+cudaError_t launch_gemv(const GemvParams& p, int n, int row_groups, bool imma, cudaStream_t st, bool pdl) {
+  if (p.cw_mask || p.mcg) return cudaErrorInvalidValue;  // narrowed windows and mcg take the cluster-split GEMV
   const unsigned grid = static_cast<unsigned>(p.grid);
-  if (row_groups == 1) return imma ? launch_gemv_k<1, true>(p, K, grid, st, pdl) : launch_gemv_k<1, false>(p, K, grid, st, pdl);
-  if (row_groups == 2) return imma ? launch_gemv_k<2, true>(p, K, grid, st, pdl) : launch_gemv_k<2, false>(p, K, grid, st, pdl);
+  if (row_groups == 1) return imma ? launch_gemv_k<1, true>(p, n, grid, st, pdl) : launch_gemv_k<1, false>(p, n, grid, st, pdl);
+  if (row_groups == 2) return imma ? launch_gemv_k<2, true>(p, n, grid, st, pdl) : launch_gemv_k<2, false>(p, n, grid, st, pdl);
   return cudaErrorInvalidValue;
 }
 

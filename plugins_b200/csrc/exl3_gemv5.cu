@@ -28,11 +28,13 @@ namespace {
 constexpr int kW5 = 4;              // warps per CTA
 constexpr int kT5 = kW5 * 32;
 // Units in flight per warp: a deep ring (prefetch measured faster at every shape) or a shallow one, whichever is the
-// deepest that keeps three CTAs per SM beside the CTA's rotated input (a unit is 256 K bytes).
-template <int K>
-constexpr int deep_stages() { return K <= 2 ? 16 : (K <= 4 ? 12 : (K == 5 ? 10 : 8)); }
-template <int K>
-constexpr int shallow_stages() { return K <= 2 ? 8 : (K <= 4 ? 8 : 6); }
+// deepest that keeps three CTAs per SM beside the CTA's rotated input (a unit is 16 n bytes; n = 16 x bits).
+constexpr int deep_stages_n(int n) { return n <= 32 ? 16 : (n <= 64 ? 12 : (n <= 80 ? 10 : 8)); }
+constexpr int shallow_stages_n(int n) { return n <= 64 ? 8 : 6; }
+template <int N>
+constexpr int deep_stages() { return deep_stages_n(N); }
+template <int N>
+constexpr int shallow_stages() { return shallow_stages_n(N); }
 constexpr int kRed5 = 132;          // row stride of the reduction buffer (floats)
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
@@ -61,9 +63,9 @@ __device__ __forceinline__ float ld_dsmem(const float* local, uint32_t rank) {
 
 }  // namespace
 
-template <int K, int RG, bool IMMA, int ST>
+template <int N, int RG, bool IMMA, int ST, int DS>
 __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
-  constexpr uint32_t kTileBytes = 32u * K;
+  constexpr uint32_t kTileBytes = 2u * N;
   constexpr uint32_t kUnitBytes = 8u * kTileBytes;
   constexpr uint32_t kSlabX = RG * 256u;
   constexpr int kStages5 = ST;
@@ -78,7 +80,9 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   const int t0 = static_cast<int>(rank) * KR;        // first slab
   uint8_t* xps = smem;                                                  // [KR][RG][32][8 B]
   uint8_t* ring = smem + p.xp_bytes + warp * (kStages5 * kUnitBytes);
-  float* red = reinterpret_cast<float*>(smem + p.xp_bytes + kW5 * kStages5 * kUnitBytes);  // [kW5][rows][kRed5]
+  // after the main loop, the reduction buffer [kW5][rows][kRed5] overlays the rotated input and the rings (both dead
+  // by then), and the exchange's staging rows follow it: the launch takes the larger of the two footprints
+  float* red = reinterpret_cast<float*>(smem);
 
   // segment of this column block
   int s = 0;
@@ -163,10 +167,13 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   }
 
   // ---- main loop
-  LaneWindows<K> lwin;
+  LaneWin<N> lwin;
   lwin.init(lane);
+  lwin.mask = spec_mask(p.cw_mask);
   ImmaIndicator ind;
   ind.init(lane);
+  ImmaWin<N> iwin;
+  if constexpr (IMMA && DS == 2) iwin.init(lane, lwin.mask);
   const uint32_t g = lane >> 2, q = lane & 3u;
   float acc[8][RG][4];
 #pragma unroll
@@ -190,10 +197,9 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
     }
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
-      uint32_t w[8], a[4];
-      lane_codewords<K>(tw + t * (kTileBytes / 4u), lwin, w);
-      if constexpr (IMMA) decode_afrag_imma<ST == deep_stages<K>()>(w, ind, a);
-      else decode_afrag_dp4a(w, a);
+      uint32_t a[4];
+      if constexpr (IMMA) decode_tile_imma<N, DS, ST == deep_stages<N>()>(tw + t * (kTileBytes / 4u), lwin, iwin, ind, a);
+      else decode_tile_natural<N, DS>(tw + t * (kTileBytes / 4u), lwin, a);
 #pragma unroll
       for (int r = 0; r < RG; ++r) mma_16816(acc[t][r], a, b0[r], b1[r]);
     }
@@ -202,6 +208,7 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
     cp_async_commit();
   }
   cp_async_wait<0>();
+  __syncthreads();  // every warp is past the main loop: the rotated input and the rings are free
 
   // ---- the CTA's partial: the warps' sums in warp order, into red[0]
   float* rw = red + warp * rows * kRed5;
@@ -264,7 +271,7 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
       }
     const int64_t col = c0 + (cbg * 128 - seg_c0);  // first gathered column of this block
     // each warp: its row's 128 outputs through a shared-memory staging row, then 16-byte stores into every rank
-    uint8_t* stage = ring;  // this warp's weight ring: drained (cp.async waited above), at least 2 KiB
+    uint8_t* stage = smem + static_cast<size_t>(kW5) * rows * kRed5 * 4 + warp * 512u;  // this warp's row, after red
     const uint32_t row_bytes = 128u * static_cast<uint32_t>(esize);
     for (int row = static_cast<int>(warp); row < rows; row += kW5) {
       float v[4];
@@ -312,11 +319,12 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
 
 // ------------------------------------------------------------------ host
 
-template <int K, int RG, bool IMMA, int ST>
+template <int N, int RG, bool IMMA, int ST, int DS>
 static cudaError_t launch5_t(const GemvParams& p, cudaStream_t st, bool pdl) {
-  auto kern = gemv5_kernel<K, RG, IMMA, ST>;
-  const size_t smem = static_cast<size_t>(p.xp_bytes) + static_cast<size_t>(kW5) * ST * 8u * 32u * K +
-                      static_cast<size_t>(kW5) * p.rows * kRed5 * 4;
+  auto kern = gemv5_kernel<N, RG, IMMA, ST, DS>;
+  const size_t loop = static_cast<size_t>(p.xp_bytes) + static_cast<size_t>(kW5) * ST * 8u * 2u * N;
+  const size_t tail = static_cast<size_t>(kW5) * p.rows * kRed5 * 4 + kW5 * 512u;
+  const size_t smem = loop > tail ? loop : tail;
   static KernelSetup setup;
   if (cudaError_t e = kernel_setup(setup, kern, kT5, smem, true); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -336,36 +344,38 @@ static cudaError_t launch5_t(const GemvParams& p, cudaStream_t st, bool pdl) {
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <int K, int RG, bool IMMA>
+template <int N, int RG, bool IMMA, int DS>
 static cudaError_t launch5_s(const GemvParams& p, cudaStream_t st, bool pdl) {
-  return p.stages == deep_stages<K>() ? launch5_t<K, RG, IMMA, deep_stages<K>()>(p, st, pdl)
-                                      : launch5_t<K, RG, IMMA, shallow_stages<K>()>(p, st, pdl);
+  return p.stages == deep_stages<N>() ? launch5_t<N, RG, IMMA, deep_stages<N>(), DS>(p, st, pdl)
+                                      : launch5_t<N, RG, IMMA, shallow_stages<N>(), DS>(p, st, pdl);
 }
 
+// A narrowed codeword window or the mcg codebook takes the tensor-pipe operand order only.
 template <int RG, bool IMMA>
-static cudaError_t launch5_k(const GemvParams& p, int K, cudaStream_t st, bool pdl) {
-  switch (K) {
-    case 1: return launch5_s<1, RG, IMMA>(p, st, pdl);
-    case 2: return launch5_s<2, RG, IMMA>(p, st, pdl);
-    case 3: return launch5_s<3, RG, IMMA>(p, st, pdl);
-    case 4: return launch5_s<4, RG, IMMA>(p, st, pdl);
-    case 5: return launch5_s<5, RG, IMMA>(p, st, pdl);
-    case 6: return launch5_s<6, RG, IMMA>(p, st, pdl);
-    default: return cudaErrorInvalidValue;
-  }
+static cudaError_t launch5_k(const GemvParams& p, int n, cudaStream_t st, bool pdl) {
+  cudaError_t e = cudaErrorInvalidValue;
+  if constexpr (IMMA)
+    with_rate_decode(n, p.cw_mask, p.mcg != 0, [&](auto N, auto DS) {
+      e = launch5_s<decltype(N)::value, RG, IMMA, decltype(DS)::value>(p, st, pdl);
+    });
+  else if (!p.cw_mask && !p.mcg)
+    with_rate(n, [&](auto N) { e = launch5_s<decltype(N)::value, RG, IMMA, 0>(p, st, pdl); });
+  return e;
 }
 
-static size_t gemv5_smem_for(int K, int stages, int KR, int row_groups, int rows) {
-  return static_cast<size_t>(KR) * row_groups * 256 + static_cast<size_t>(kW5) * stages * 8u * 32u * K +
-         static_cast<size_t>(kW5) * rows * kRed5 * 4;
+// The launch's shared memory: the main loop's (rotated input + rings) or, overlaying it, the tail's (reduction buffer
+// + exchange staging), whichever is larger.
+static size_t gemv5_smem_for(int n, int stages, int KR, int row_groups, int rows) {
+  const size_t loop = static_cast<size_t>(KR) * row_groups * 256 + static_cast<size_t>(kW5) * stages * 8u * 2u * n;
+  const size_t tail = static_cast<size_t>(kW5) * rows * kRed5 * 4 + kW5 * 512u;
+  return loop > tail ? loop : tail;
 }
 
-bool gemv5_geometry(GemvParams& p, int K, int sms, int row_groups, int split_override, const char** why) {
+bool gemv5_geometry(GemvParams& p, int n, int sms, int row_groups, int split_override, const char** why) {
   const int KT = p.in_features / 16;
   const int CB = p.out_features / 128;
   constexpr size_t kThreePerSm = 74 * 1024;  // shared memory that still fits three CTAs on an SM
-  const int deep = K <= 2 ? 16 : (K <= 4 ? 12 : (K == 5 ? 10 : 8));  // deep_stages<K>()
-  const int shallow = K <= 4 ? 8 : 6;                                 // shallow_stages<K>()
+  const int deep = deep_stages_n(n), shallow = shallow_stages_n(n);
   // CTAs per column block: a divisor of KT leaving whole 128-input blocks (8 slabs) per CTA, at most 16 (the
   // cluster limit) and at most 128 slabs per CTA.  The split fixes a row's summation order (slabs per warp, CTA
   // partials in rank order), so it is chosen for every width at once -- a row's bytes must not depend on the rows
@@ -377,8 +387,8 @@ bool gemv5_geometry(GemvParams& p, int K, int sms, int row_groups, int split_ove
   for (int pass = 0; pass < 2 && best == 0; ++pass) {
     for (int d = 1; d <= 16; ++d) {
       if (KT % d != 0 || (KT / d) % 8 != 0 || KT / d > 128) continue;
-      if (gemv5_smem_for(K, shallow, KT / d, 2, kMaxRows) > 227 * 1024) continue;
-      const size_t smem = gemv5_smem_for(K, shallow, KT / d, 1, 8);
+      if (gemv5_smem_for(n, shallow, KT / d, 2, kMaxRows) > 227 * 1024) continue;
+      const size_t smem = gemv5_smem_for(n, shallow, KT / d, 1, 8);
       if (split_override > 0) {
         if (d == split_override) best = d;
         continue;
@@ -396,16 +406,16 @@ bool gemv5_geometry(GemvParams& p, int K, int sms, int row_groups, int split_ove
   p.kt = KT;
   p.kc = best;
   p.kr = KT / best;
-  p.stages = gemv5_smem_for(K, deep, p.kr, row_groups, p.rows) <= kThreePerSm ? deep : shallow;
+  p.stages = gemv5_smem_for(n, deep, p.kr, row_groups, p.rows) <= kThreePerSm ? deep : shallow;
   p.xp_bytes = static_cast<int64_t>(p.kr) * row_groups * 256;
   p.grid = CB * best;
   p.contrib_max = 1;
   return true;
 }
 
-cudaError_t launch_gemv5(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl) {
-  if (row_groups == 1) return imma ? launch5_k<1, true>(p, K, st, pdl) : launch5_k<1, false>(p, K, st, pdl);
-  if (row_groups == 2) return imma ? launch5_k<2, true>(p, K, st, pdl) : launch5_k<2, false>(p, K, st, pdl);
+cudaError_t launch_gemv5(const GemvParams& p, int n, int row_groups, bool imma, cudaStream_t st, bool pdl) {
+  if (row_groups == 1) return imma ? launch5_k<1, true>(p, n, st, pdl) : launch5_k<1, false>(p, n, st, pdl);
+  if (row_groups == 2) return imma ? launch5_k<2, true>(p, n, st, pdl) : launch5_k<2, false>(p, n, st, pdl);
   return cudaErrorInvalidValue;
 }
 

@@ -43,8 +43,8 @@ constexpr int kVirt6 = 3;         // virtual CTAs per SM: the work split
 constexpr int kXiSlabs = 136;     // in-CTA rotation: the most slabs one piece of a run covers (17 input blocks)
 constexpr int kXiRows = 4;        // in-CTA rotation: the most rows
 
-template <int K>
-constexpr int stages6() { return K <= 2 ? 16 : (K <= 4 ? 12 : (K == 5 ? 10 : 8)); }
+template <int N>  // n halfwords per tile (16 x bits per weight)
+constexpr int stages6() { return N <= 32 ? 16 : (N <= 64 ? 12 : (N <= 80 ? 10 : 8)); }
 
 __device__ __forceinline__ void cp_async16_6(void* smem_dst, const void* gmem_src) {
   asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
@@ -90,12 +90,12 @@ __global__ void __launch_bounds__(256 * RG) gemv6_prep_kernel(GemvParams p, __ha
   }
 }
 
-template <int K, int RG, int ST, bool XI>
+template <int N, int RG, int ST, bool XI>
 __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams p, const __half* __restrict__ xf,
                                                                     float* __restrict__ part, uint32_t* __restrict__ done) {
   static_assert(!XI || RG == 1, "in-CTA rotation is for one row group");
   constexpr int kRedRows = XI ? kXiRows : 8 * RG;
-  constexpr uint32_t kTileBytes = 32u * K;
+  constexpr uint32_t kTileBytes = 2u * N;
   constexpr uint32_t kUnitBytes = 8u * kTileBytes;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_last;
@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
   int64_t run = (work + V - 1) / V;
   run = (run < kMinRun6 ? kMinRun6 : run + 3) & ~int64_t{3};
 
-  LaneWindows<K> lwin;
+  LaneWin<N> lwin;
   lwin.init(lane);
   ImmaIndicator ind;
   ind.init(lane);
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         uint32_t w[8], a[4];
-        lane_codewords<K>(tw + t * (kTileBytes / 4u), lwin, w);
+        tile_codewords<N>(tw + t * (kTileBytes / 4u), lwin, w);
         decode_afrag_imma<true>(w, ind, a);
 #pragma unroll
         for (int r = 0; r < RG; ++r) mma_16816(acc[t][r], a, xv[r].x, xv[r].y);
@@ -324,11 +324,11 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
   }
 }
 
-template <int K, int RG, bool XI>
+template <int N, int RG, bool XI>
 cudaError_t launch6_t(const GemvParams& p, int sms, __half* xf, float* part, uint32_t* done, cudaStream_t st) {
-  constexpr int ST = stages6<K>();
-  auto kern = gemv6_kernel<K, RG, ST, XI>;
-  const size_t smem = static_cast<size_t>(kW6) * ST * 8u * 32u * K +
+  constexpr int ST = stages6<N>();
+  auto kern = gemv6_kernel<N, RG, ST, XI>;
+  const size_t smem = static_cast<size_t>(kW6) * ST * 8u * 2u * N +
                       static_cast<size_t>(kW6) * (XI ? kXiRows : 8 * RG) * kRed6 * 4 + (XI ? kXiSlabs * 128 : 0);
   static KernelSetup setup;
   int per_sm = 0;  // resident CTAs per SM (at most kVirt6): the persistent grid is exactly one wave
@@ -349,16 +349,10 @@ cudaError_t launch6_t(const GemvParams& p, int sms, __half* xf, float* part, uin
 }
 
 template <int RG, bool XI>
-cudaError_t launch6_k(const GemvParams& p, int K, int sms, __half* xf, float* part, uint32_t* done, cudaStream_t st) {
-  switch (K) {
-    case 1: return launch6_t<1, RG, XI>(p, sms, xf, part, done, st);
-    case 2: return launch6_t<2, RG, XI>(p, sms, xf, part, done, st);
-    case 3: return launch6_t<3, RG, XI>(p, sms, xf, part, done, st);
-    case 4: return launch6_t<4, RG, XI>(p, sms, xf, part, done, st);
-    case 5: return launch6_t<5, RG, XI>(p, sms, xf, part, done, st);
-    case 6: return launch6_t<6, RG, XI>(p, sms, xf, part, done, st);
-    default: return cudaErrorInvalidValue;
-  }
+cudaError_t launch6_k(const GemvParams& p, int n, int sms, __half* xf, float* part, uint32_t* done, cudaStream_t st) {
+  cudaError_t e = cudaErrorInvalidValue;
+  with_rate(n, [&](auto N) { e = launch6_t<decltype(N)::value, RG, XI>(p, sms, xf, part, done, st); });
+  return e;
 }
 
 // The kernel's run length for V virtual CTAs, and whether every unit is split (no whole units round-robin).
@@ -384,7 +378,8 @@ bool gemv6_prefers(const GemvParams& p) {
   return slabs >= kGemv6MinSlabs || (p.in_features >= 8192 && slabs >= kGemv6MinSlabsDeep);
 }
 
-cudaError_t launch_gemv6(const GemvParams& p, int K, int sms, void* scratch, uint32_t* counters, cudaStream_t st) {
+cudaError_t launch_gemv6(const GemvParams& p, int n, int sms, void* scratch, uint32_t* counters, cudaStream_t st) {
+  if (p.cw_mask || p.mcg) return cudaErrorInvalidValue;  // narrowed windows and mcg take the cluster-split GEMV
   if (p.rows < 1 || p.rows > 16 || p.tp) return cudaErrorInvalidValue;
   const int rg = p.rows <= 8 ? 1 : 2;
   __half* xf = static_cast<__half*>(scratch);
@@ -394,7 +389,7 @@ cudaError_t launch_gemv6(const GemvParams& p, int K, int sms, void* scratch, uin
   bool all_runs = false;
   split6(p, sms, &run, &all_runs);
   if (p.rows <= kXiRows && all_runs && run <= kXiSlabs - 8)  // each CTA rotates its runs' inputs itself
-    return launch6_k<1, true>(p, K, sms, xf, part, counters, st);
+    return launch6_k<1, true>(p, n, sms, xf, part, counters, st);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.in_features / 128), static_cast<unsigned>(p.nseg));
   cfg.blockDim = dim3(256 * rg);
@@ -407,8 +402,8 @@ cudaError_t launch_gemv6(const GemvParams& p, int K, int sms, void* scratch, uin
   cudaError_t e = rg == 1 ? cudaLaunchKernelEx(&cfg, gemv6_prep_kernel<1>, p, xf)
                           : cudaLaunchKernelEx(&cfg, gemv6_prep_kernel<2>, p, xf);
   if (e != cudaSuccess) return e;
-  return rg == 1 ? launch6_k<1, false>(p, K, sms, xf, part, counters, st)
-                 : launch6_k<2, false>(p, K, sms, xf, part, counters, st);
+  return rg == 1 ? launch6_k<1, false>(p, n, sms, xf, part, counters, st)
+                 : launch6_k<2, false>(p, n, sms, xf, part, counters, st);
 }
 
 }  // namespace exl3

@@ -5,6 +5,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 
 namespace exl3 {
 
@@ -53,6 +54,50 @@ cudaError_t kernel_setup(KernelSetup& s, Kern kern, int threads, size_t smem, bo
   return cudaSuccess;
 }
 
+// The rates the kernels serve: n halfwords per 256-weight tile, 16 x bits per weight, whole and half bits 1..6.
+inline bool rate_served_n(int n) { return n % 8 == 0 && n >= 16 && n <= 96; }
+
+// Calls f(std::integral_constant<int, N>{}) for the served rate n; false (nothing called) for any other n.
+template <typename F>
+inline bool with_rate(int n, F&& f) {
+  switch (n) {
+    case 16: f(std::integral_constant<int, 16>{}); return true;
+    case 24: f(std::integral_constant<int, 24>{}); return true;
+    case 32: f(std::integral_constant<int, 32>{}); return true;
+    case 40: f(std::integral_constant<int, 40>{}); return true;
+    case 48: f(std::integral_constant<int, 48>{}); return true;
+    case 56: f(std::integral_constant<int, 56>{}); return true;
+    case 64: f(std::integral_constant<int, 64>{}); return true;
+    case 72: f(std::integral_constant<int, 72>{}); return true;
+    case 80: f(std::integral_constant<int, 80>{}); return true;
+    case 88: f(std::integral_constant<int, 88>{}); return true;
+    case 96: f(std::integral_constant<int, 96>{}); return true;
+    default: return false;
+  }
+}
+
+// The codeword mask of a window of `bits` (8..16): 0 for the full 16-bit window (no masking instantiation).
+inline uint32_t window_mask(int bits) { return bits >= 16 ? 0u : (1u << bits) - 1u; }
+// A weight's window bits from its flags (bits 8..11 hold 16 - w: EXL3_WEIGHT_WINDOW in exl3_b200.h).
+inline int flags_window_bits(uint32_t flags) { return 16 - static_cast<int>((flags >> 8) & 0xFu); }
+
+// The decode spec of a weight: 0 mul1 at the full window, 1 mul1 at a narrowed window, 2 mcg.
+inline int decode_spec(uint32_t cw_mask, bool mcg) { return mcg ? 2 : (cw_mask ? 1 : 0); }
+
+// with_rate and the decode spec: f(N, DS) for the served rate n, DS = decode_spec(cw_mask, mcg).
+template <typename F>
+inline bool with_rate_decode(int n, uint32_t cw_mask, bool mcg, F&& f) {
+  return with_rate(n, [&](auto N) {
+    switch (decode_spec(cw_mask, mcg)) {
+      case 0: f(N, std::integral_constant<int, 0>{}); break;
+      case 1: f(N, std::integral_constant<int, 1>{}); break;
+      default: f(N, std::integral_constant<int, 2>{}); break;
+    }
+  });
+}
+// The codeword mask a decode spec reads: the window's, or all 16 bits for mcg at the full window.
+constexpr uint32_t spec_mask(uint32_t cw_mask) { return cw_mask ? cw_mask : 0xFFFFu; }
+
 constexpr int kMaxSegments = 4;  // linears stacked into one launch (the reference's SHARED_MAX, linear.zig:39-40)
 constexpr int kMaxRows = 16;     // decode-GEMV rows per launch (two m16n8k16 row groups)
 
@@ -88,6 +133,8 @@ struct GemvParams {
   int32_t seg_cb[kMaxSegments + 1];  // segment bounds in 128-column blocks
   int32_t prepared;         // x already holds f16(H(x*suh)/sqrt(128)): no rotation
   int32_t inner_only;       // skip the output Hadamard and svh: y = the f32 inner product
+  uint32_t cw_mask;         // a narrowed codeword window's mask (window_mask), 0 for the full 16-bit window
+  int32_t mcg;              // the mcg codebook (else mul1)
   // geometry (gemv_geometry)
   int32_t kt, kr, kc;       // 16-row slabs, slabs per chunk, chunks
   int32_t contrib_max;      // most CTAs contributing to one (segment, chunk, column block)
@@ -116,7 +163,7 @@ int64_t tp_slot_bytes(const exl3_tp* tp);
 
 // Fills the geometry fields of `p` for `sms` SMs; false (with a reason) when the shape does not fit one launch.
 bool gemv_geometry(GemvParams& p, int sms, int row_groups, size_t partial_capacity_floats, const char** why);
-cudaError_t launch_gemv(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl);
+cudaError_t launch_gemv(const GemvParams& p, int n, int row_groups, bool imma, cudaStream_t st, bool pdl);
 
 // The persistent work-balanced decode GEMV (exl3_gemv6.cu), 1..16 rows, no column-parallel exchange: a prepare
 // launch (x rotated into fragment order in `scratch`) and the GEMV (runs' partials in `scratch` after the prepared x;
@@ -128,17 +175,17 @@ constexpr int64_t kGemv6MinSlabs = 49152;
 constexpr int64_t kGemv6MinSlabsDeep = 16384;
 bool gemv6_prefers(const GemvParams& p);
 size_t gemv6_scratch_bytes(const GemvParams& p, int sms);
-cudaError_t launch_gemv6(const GemvParams& p, int K, int sms, void* scratch, uint32_t* counters, cudaStream_t st);
+cudaError_t launch_gemv6(const GemvParams& p, int n, int sms, void* scratch, uint32_t* counters, cudaStream_t st);
 
 // The cluster-split decode GEMV (exl3_gemv5.cu): one thread-block cluster per 128-column block, its CTAs splitting
 // the input (kc = CTAs per cluster, kr = slabs per CTA), partials summed over distributed shared memory.
 // split_override > 0 forces the CTAs per cluster (measurement); false when no split fits.
-bool gemv5_geometry(GemvParams& p, int K, int sms, int row_groups, int split_override, const char** why);
-cudaError_t launch_gemv5(const GemvParams& p, int K, int row_groups, bool imma, cudaStream_t st, bool pdl);
+bool gemv5_geometry(GemvParams& p, int n, int sms, int row_groups, int split_override, const char** why);
+cudaError_t launch_gemv5(const GemvParams& p, int n, int row_groups, bool imma, cudaStream_t st, bool pdl);
 
 // decode a whole trellis to W_hat (f16 bits, row-major [in][out]); one warp per tile
 cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
-                                int imma, cudaStream_t st);
+                                int imma, cudaStream_t st, uint32_t cw_mask = 0, int mcg = 0);
 
 // trellis encoder (exl3_encode.cu): target [in][out] f32 (rotated, unit variance) -> trellis [in/16][out/16][n]
 cudaError_t launch_encode(const float* target, int in_features, int out_features, int n, uint16_t* trellis,
@@ -167,7 +214,8 @@ struct GemmParams {
 // a_img is null) and the B image of the trellis columns [col0, col0 + ncols) (skipped when b_img is null).
 cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, int m, int mp, const uint16_t* suh,
                           int prepared, uint8_t* a_img, const uint16_t* trellis, int in_features, int out_features,
-                          int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st);
+                          int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st, uint32_t cw_mask = 0,
+                          int mcg = 0);
 // shape: 0 = 128x128 tiles, 1 = 128x256, 2 = 256x128, 3 = 256x256 (rows x columns)
 int gemm_block_m(int shape);
 int gemm_block_n(int shape);

@@ -18,12 +18,17 @@
 //                  128-wide input block is exactly this column block), writing the down GEMV's B fragments;
 //   4. down     -- the same GEMV over (chunk, 128-column block of the hidden size), finishing to f32 per slot;
 //   5. combine  -- y_r = sum_k score * d in k order, in x's dtype.
-// Work split: whole units round-robin over the persistent grid while every CTA gets one (neighbouring CTAs stream
-// the same expert's k slabs together), then the remaining units' k slabs, laid end to end, cut into one equal run per
-// CTA (stream-K: a multiple of four slabs, at least kMinRun), so every CTA streams the same bytes however few experts
-// a call touches.  A unit that two or more runs share is finished by the run that completes it last (a per-unit
-// counter): it adds the runs' partial sums in run order and applies the epilogue.  The order of every sum is fixed by the call's routing and the
-// grid, never by timing, so results are reproducible.
+// Work split: every unit's k range is cut into the same runs in every call (at most kMaxRuns runs of about 32 slabs,
+// set by the input width alone).  Whole units go round-robin over the persistent grid while every CTA gets one
+// (neighbouring CTAs stream the same expert's k slabs together); the remaining units' runs, laid end to end, are cut
+// into one equal range per CTA, so every CTA streams about the same bytes however few experts a call touches.  Each
+// warp sums a run's slabs from zero in its MMA accumulators and adds the run to its running total in run order; a
+// unit's value is the warps' totals in warp order.  A unit that two or more CTAs share is finished by the CTA that
+// completes it last (a per-unit counter): it continues each warp's total of the first CTA's runs with the later
+// runs, one by one in run order, then sums the warps -- the same sums a whole unit makes.  So the order of every
+// sum is fixed by the input width and the tile layout, never by the routing, the grid or timing: a slot's output
+// has the same bytes whatever other rows and experts share the call (the reference checks its expert kernels for
+// this row invariance, plugins/turboexl3_ds41/src/exl3/selfcheck.zig:755-851).
 #include <cuda_runtime.h>
 
 #include <cstdlib>
@@ -45,7 +50,14 @@ constexpr int kChunkRows = 8;      // slots per chunk: the MMA's N
 constexpr int kWarpsM = 4;
 constexpr int kStagesM = 4;
 constexpr int kRedStrideM = 132;
-constexpr int kMinRun = 32;         // slabs: the shortest run a CTA takes (eight per warp)
+constexpr int kMaxRuns = 8;         // runs per unit at most (the partial slots a CTA may need)
+
+// A unit's run length in slabs for kt slabs of input: about 32 (eight per warp), a multiple of four, at most kMaxRuns
+// runs (the last one shorter).
+__host__ __device__ constexpr int moe_run_slabs(int kt) {
+  const int r = (kt + 31) / 32 < kMaxRuns ? (kt + 31) / 32 : kMaxRuns;
+  return ((kt + r - 1) / r + 3) & ~3;
+}
 constexpr int kPrepChunks = 48;     // prepare: chunk columns of the grid
 constexpr int kCombineRows = 64;    // combine: row columns of the grid
 constexpr int kIntsM = 5 * kMaxSlots + 64;  // the route's ints: order, chunk_e/s/n, pos, nchunks, bad
@@ -63,6 +75,8 @@ struct MoeParams {
   uint8_t* hp_dst[8];  // every rank's down-input buffer (same layout as hp) when hp_world > 0
   int32_t hp_world;
   int32_t max_cb;     // column blocks the unit_done array holds per chunk
+  uint32_t cw_mask_gu, cw_mask_d;  // gate|up's and down's narrowed codeword window masks (0: the full 16 bits)
+  int32_t mcg_gu, mcg_d;           // gate|up's and down's codebook is mcg (else mul1)
   const void* x;      // [rows][hidden]
   int32_t x_dtype;
   const void* inds;   // [rows][topk]
@@ -84,7 +98,9 @@ struct MoeParams {
   uint8_t* xu;         // [chunk][hidden/16][256 B] up-prepared rows
   uint8_t* hp;         // [chunk][inter/16][256 B] down-prepared rows
   float* dout;         // [kMaxSlots][hidden] down outputs per slot (position in `order`)
-  float* part;         // [grid][2 runs' ends][2 weights][8][128] partial sums of units a run shares with another
+  float* part;         // [grid][P runs][4 warps][2 weights][8][128] sums of the units a CTA shares with others: slots
+                       // 0 .. P - 2 the runs of a unit it joins after its first run, P - 1 the warps' totals of the
+                       // unit it starts but does not finish
   int32_t* unit_done;  // [2 launches][kMaxSlots * max CB] runs finished per unit (each reset by its unit's last run)
 };
 
@@ -229,9 +245,9 @@ __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0
 
 // PAIR: units (chunk, intermediate column block), weights gate+up, epilogue SwiGLU + down prepare.
 // !PAIR: units (chunk, hidden column block), weight down, epilogue finish to f32.
-template <int K, bool PAIR>
+template <int N, bool PAIR, int DS>
 __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) {
-  constexpr uint32_t kTileBytes = 32u * K;
+  constexpr uint32_t kTileBytes = 2u * N;
   constexpr uint32_t kW = 8u * kTileBytes;                // one weight's tiles of a unit slab
   constexpr uint32_t kSlab = (PAIR ? 2u : 1u) * (kW + 256u);  // tiles + x fragments, per weight
   extern __shared__ __align__(128) uint8_t smem[];
@@ -251,37 +267,44 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
   pdl_launch_dependents();
   pdl_wait();  // the chunk table and the prepared inputs come from the previous launches
   const int units = *p.nchunks * CB;
-  LaneWindows<K> lwin;
+  LaneWin<N> lwin;
   lwin.init(lane);
+  lwin.mask = spec_mask(PAIR ? p.cw_mask_gu : p.cw_mask_d);
   ImmaIndicator ind;
   ind.init(lane);
+  ImmaWin<N> iwin;
+  if constexpr (DS == 2) iwin.init(lane, lwin.mask);
   const uint32_t g = lane >> 2, q = lane & 3u;
-  // whole units round-robin while every CTA gets one (dp of them), then this CTA's run [r0, r1) of the remaining
-  // units' slabs laid end to end
+  // Every unit's k range is cut the same way whatever the call: P runs of L slabs (the last run shorter), a warp's
+  // slabs of a run summed from zero in its MMA accumulators, the warp's runs added in run order, then the warps in
+  // warp order.  Whole units go round-robin while every CTA gets one (dp of them); the remaining units' runs, laid
+  // end to end, are cut into one equal range [R0, R1) per CTA.
   const int G = static_cast<int>(gridDim.x);
+  const int L = moe_run_slabs(KT), P = (KT + L - 1) / L, Lw = L / kWarpsM;
   const int dp = units / G * G;
-  const int64_t work = static_cast<int64_t>(units - dp) * KT;
-  int64_t run = (work + G - 1) / G;
-  run = (run < kMinRun ? kMinRun : run + 3) & ~int64_t{3};
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * run;
-  const int64_t r1 = r0 + run < work ? r0 + run : work;
+  const int64_t sk_runs = static_cast<int64_t>(units - dp) * P;
+  const int64_t per = sk_runs > 0 ? (sk_runs + G - 1) / G : 1;
+  const int64_t R0 = static_cast<int64_t>(blockIdx.x) * per;
+  const int64_t R1 = R0 + per < sk_runs ? R0 + per : sk_runs;
   int32_t* done = p.unit_done + (PAIR ? 0 : kMaxSlots * static_cast<int64_t>(p.max_cb));
+  constexpr int kPart = (PAIR ? 2 : 1) * 8 * 128;  // one warp's sums of a unit: [weight][row][column]
 
   int next = static_cast<int>(blockIdx.x);
-  for (int64_t at = r0;;) {
-    int unit, su = 0, k0 = 0, k1 = KT;
+  for (int64_t at = R0;;) {
+    int unit, su = 0, ra = 0, rb = P;  // this item: runs ra .. rb - 1 of the unit
     if (next < dp) {
       unit = next;
       next += G;
-    } else if (at < r1) {
-      su = static_cast<int>(at / KT);
-      k0 = static_cast<int>(at - static_cast<int64_t>(su) * KT);
-      k1 = static_cast<int>(r1 - at < KT - k0 ? k0 + (r1 - at) : KT);
-      at += k1 - k0;
+    } else if (at < R1) {
+      su = static_cast<int>(at / P);
+      ra = static_cast<int>(at - static_cast<int64_t>(su) * P);
+      rb = static_cast<int>(R1 - at < P - ra ? ra + (R1 - at) : P);
+      at += rb - ra;
       unit = dp + su;
     } else {
       break;
     }
+    const int k0 = ra * L, k1 = rb * L < KT ? rb * L : KT;
     const int chunk = unit / CB, cb = unit % CB;
     const int e = p.chunk_e[chunk], s0 = p.chunk_s[chunk], nrow = p.chunk_n[chunk];
     const uint8_t* wa = tra + e * wstride + static_cast<size_t>(cb) * 8u * kTileBytes;
@@ -289,7 +312,8 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
     const uint8_t* xca = xa + static_cast<size_t>(chunk) * KT * 256;
     const uint8_t* xcb = xb + static_cast<size_t>(chunk) * KT * 256;
     const size_t rowstride = static_cast<size_t>(CB) * 8u * kTileBytes;  // bytes between k slabs
-    // this warp's slabs of the run: k0 + warp, k0 + warp + 4, ... (k0 and k1 are multiples of four)
+    // this warp's slabs of the item: k0 + warp, k0 + warp + 4, ... (k0 and k1 are multiples of four); every run
+    // gives each warp L / 4 of them (the unit's last run fewer: it ends the item)
     const uint32_t nk = static_cast<uint32_t>(k1 - k0);
     const uint32_t mine = nk > warp ? (nk - warp + kWarpsM - 1) / kWarpsM : 0u;
     auto issue = [&](uint32_t i) {
@@ -317,6 +341,33 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
       for (int t = 0; t < 8; ++t)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[w2][t][c] = 0.0f;
+    // run r's sums of this warp leave the accumulators: into the warp's running total in shared memory when this CTA
+    // holds the unit from its first run, else into this CTA's slot for run r in global memory (the unit's last CTA
+    // adds them in run order); no barrier, the ring keeps streaming
+    auto flush = [&](int r) {
+      // (ra > 0) this CTA's slot for run r: its offset in the CTA's range, below P - 1
+      const int64_t slot = ra > 0 ? static_cast<int64_t>(su) * P + r - R0 : 0;
+      float* gw = p.part + ((static_cast<size_t>(blockIdx.x) * P + static_cast<size_t>(slot)) * kWarpsM + warp) * kPart;
+#pragma unroll
+      for (int w2 = 0; w2 < (PAIR ? 2 : 1); ++w2) {
+        float* rw = red + (w2 * kWarpsM + warp) * 8 * kRedStrideM;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int row = 2 * static_cast<int>(q) + (c & 1), col = 16 * t + static_cast<int>(g) + 8 * (c >> 1);
+            if (ra == 0) {
+              float& tot = rw[row * kRedStrideM + col];
+              tot = r == 0 ? acc[w2][t][c] : tot + acc[w2][t][c];
+            } else {
+              __stcg(gw + w2 * 1024 + row * 128 + col, acc[w2][t][c]);
+            }
+            acc[w2][t][c] = 0.0f;
+          }
+        }
+      }
+    };
+    int run = ra, left = Lw;
     for (uint32_t i = 0; i < mine; ++i) {
       cp_wait<kStagesM - 2>();
       __syncwarp();
@@ -327,63 +378,66 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
         const uint2 xv = reinterpret_cast<const uint2*>(sw + kW)[lane];
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-          uint32_t w[8], a[4];
-          lane_codewords<K>(reinterpret_cast<const uint32_t*>(sw) + t * (kTileBytes / 4u), lwin, w);
-          decode_afrag_imma<true>(w, ind, a);  // pairs packed on the FMA pipe: measured 2.5 % faster
+          uint32_t a[4];  // (mul1 pairs packed on the FMA pipe: measured 2.5 % faster)
+          decode_tile_imma<N, DS, true>(reinterpret_cast<const uint32_t*>(sw) + t * (kTileBytes / 4u), lwin, iwin, ind, a);
           mma_16816(acc[w2][t], a, xv.x, xv.y);
         }
       }
       __syncwarp();
       issue(i + kStagesM - 1);
       cp_commit();
-    }
-    cp_wait<0>();
-    __half* stage = reinterpret_cast<__half*>(smem);  // warp 0's ring, drained: the down-input block's staging (2 KiB)
-    // warps' partials -> shared, summed in warp order
-#pragma unroll
-    for (int w2 = 0; w2 < (PAIR ? 2 : 1); ++w2) {
-      float* rw = red + (w2 * kWarpsM + warp) * 8 * kRedStrideM;
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const int col = 16 * t + static_cast<int>(g), row = 2 * static_cast<int>(q);
-        rw[row * kRedStrideM + col] = acc[w2][t][0];
-        rw[(row + 1) * kRedStrideM + col] = acc[w2][t][1];
-        rw[row * kRedStrideM + col + 8] = acc[w2][t][2];
-        rw[(row + 1) * kRedStrideM + col + 8] = acc[w2][t][3];
+      if (--left == 0 && i + 1 < mine) {
+        flush(run++);
+        left = Lw;
       }
     }
+    cp_wait<0>();
+    flush(run);  // the item's last run (rb - 1)
+    __half* stage = reinterpret_cast<__half*>(smem);  // warp 0's ring, drained: the down-input block's staging (2 KiB)
     __syncthreads();
-    const bool whole = k0 == 0 && k1 == KT;
-    const int64_t u0 = static_cast<int64_t>(su) * KT;  // the unit's first slab in the runs' numbering
-    constexpr int kPart = (PAIR ? 2 : 1) * 8 * 128;
-    for (int idx = tid; idx < kPart; idx += kWarpsM * 32) {
-      const int w2 = idx / 1024, row = (idx / 128) % 8, col = idx % 128;
-      float v = 0.0f;
+    if (ra == 0 && rb == P) {
+      // a whole unit: the warps' totals in warp order
+      for (int idx = tid; idx < kPart; idx += kWarpsM * 32) {
+        const int w2 = idx / 1024, row = (idx / 128) % 8, col = idx % 128;
+        float v = 0.0f;
 #pragma unroll
-      for (int w3 = 0; w3 < kWarpsM; ++w3) v += red[((w2 * kWarpsM + w3) * 8 + row) * kRedStrideM + col];
-      if (whole) red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
-      else __stcg(p.part + (static_cast<size_t>(blockIdx.x) * 2 + (r0 >= u0 ? 0 : 1)) * 2048 + idx, v);
-    }
-    if (!whole) {
-      // a shared unit: runs first .. last of the grid cover it; the one that completes it adds the partials in run
-      // order (run c keeps its partial of the unit its run starts in at end 0, of the unit it ends in at end 1)
-      const int first = static_cast<int>(u0 / run), last = static_cast<int>((u0 + KT - 1) / run);
+        for (int w3 = 0; w3 < kWarpsM; ++w3) v += red[((w2 * kWarpsM + w3) * 8 + row) * kRedStrideM + col];
+        red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
+      }
+    } else {
+      // a unit shared with other CTAs: CTAs cf .. cl of the grid hold its runs; cf, which holds runs 0 .. j0, keeps
+      // every warp's total of them in its slot P - 1, the others each run in its own slot; the last to finish adds
+      // each warp's runs in run order onto that total, then the warps in warp order -- the sums a whole unit makes
+      if (ra == 0)
+        for (int idx = tid; idx < kWarpsM * kPart; idx += kWarpsM * 32) {
+          const int w3 = idx / kPart, w2 = (idx % kPart) / 1024, row = (idx / 128) % 8, col = idx % 128;
+          __stcg(p.part + (static_cast<size_t>(blockIdx.x) * P + P - 1) * kWarpsM * kPart + idx,
+                 red[((w2 * kWarpsM + w3) * 8 + row) * kRedStrideM + col]);
+        }
+      const int64_t u0 = static_cast<int64_t>(su) * P;  // the unit's first run in the ranges' numbering
+      const int cf = static_cast<int>(u0 / per), cl = static_cast<int>((u0 + P - 1) / per);
       __threadfence();
       __syncthreads();
       if (tid == 0) {
         const int prior = atomicAdd(done + unit, 1);
-        s_last = prior == last - first;
+        s_last = prior == cl - cf;
         if (s_last) done[unit] = 0;  // ready for the next call
       }
       __syncthreads();
       if (!s_last) continue;
       __threadfence();
+      const int j0 = static_cast<int>((static_cast<int64_t>(cf) + 1) * per - 1 - u0);  // < P - 1: cf ends inside
       for (int idx = tid; idx < kPart; idx += kWarpsM * 32) {
         const int w2 = idx / 1024, row = (idx / 128) % 8, col = idx % 128;
         float v = 0.0f;
-        for (int c = first; c <= last; ++c) {
-          const int end = static_cast<int64_t>(c) * run >= u0 ? 0 : 1;
-          v += __ldcg(p.part + (static_cast<size_t>(c) * 2 + end) * 2048 + idx);
+        for (int w3 = 0; w3 < kWarpsM; ++w3) {
+          float tw = __ldcg(p.part + ((static_cast<size_t>(cf) * P + P - 1) * kWarpsM + w3) * kPart + idx);
+          for (int r = j0 + 1; r < P; ++r) {
+            const int64_t R = u0 + r, c = R / per;
+            tw += __ldcg(p.part + ((static_cast<size_t>(c) * P + static_cast<size_t>(R - c * per)) * kWarpsM + w3) *
+                                      kPart + idx);
+          }
+          v += tw;
         }
         red[((w2 * kWarpsM) * 8 + row) * kRedStrideM + col] = v;
       }
@@ -502,7 +556,7 @@ constexpr int kMaxCtasPerSm = 4;
 size_t fixed_bytes(int width, int sms) {
   const size_t ints = kIntsM;
   const size_t done = 2 * static_cast<size_t>(kMaxSlots) * (width / 128);
-  const size_t part = static_cast<size_t>(sms) * kMaxCtasPerSm * 2 * 2048;
+  const size_t part = static_cast<size_t>(sms) * kMaxCtasPerSm * kMaxRuns * kWarpsM * 1024;
   return (ints + done + part) * 4;
 }
 
@@ -526,17 +580,22 @@ int moe_ctas_per_sm() {
   return v;
 }
 
-template <int K, bool PAIR>
+template <int N, bool PAIR, int DS>
 cudaError_t launch_moe_gemv(const MoeParams& p, int sms, cudaStream_t st) {
-  auto kern = moe_gemv_kernel<K, PAIR>;
-  constexpr size_t slab = (PAIR ? 2u : 1u) * (8u * 32u * K + 256u);
+  auto kern = moe_gemv_kernel<N, PAIR, DS>;
+  constexpr size_t slab = (PAIR ? 2u : 1u) * (8u * 2u * N + 256u);
   const size_t smem = kWarpsM * kStagesM * slab + (PAIR ? 2 : 1) * kWarpsM * 8 * kRedStrideM * 4;
   static KernelSetup setup;
   int per_sm = 0;  // resident CTAs per SM: the persistent grid is exactly one wave
   if (cudaError_t e = kernel_setup(setup, kern, kWarpsM * 32, smem, false, &per_sm, moe_ctas_per_sm()); e != cudaSuccess)
     return e;
+  // the grid's partial slots ([grid][P][4 warps][kPart]) must fit the workspace's (sized for kMaxCtasPerSm CTAs per
+  // SM of kMaxRuns slots of 1024 floats): at most 2 CTAs per SM for gate|up at kMaxRuns runs
+  const int kt = (PAIR ? p.hidden : p.inter_full) / 16;
+  const int runs = (kt + moe_run_slabs(kt) - 1) / moe_run_slabs(kt);
+  const int fit = kMaxCtasPerSm * kMaxRuns * 1024 / (runs * (PAIR ? 2048 : 1024));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(sms * per_sm);
+  cfg.gridDim = dim3(sms * (per_sm < fit ? per_sm : fit));
   cfg.blockDim = dim3(kWarpsM * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -549,16 +608,12 @@ cudaError_t launch_moe_gemv(const MoeParams& p, int sms, cudaStream_t st) {
 }
 
 template <bool PAIR>
-cudaError_t launch_moe_gemv_k(const MoeParams& p, int K, int sms, cudaStream_t st) {
-  switch (K) {
-    case 1: return launch_moe_gemv<1, PAIR>(p, sms, st);
-    case 2: return launch_moe_gemv<2, PAIR>(p, sms, st);
-    case 3: return launch_moe_gemv<3, PAIR>(p, sms, st);
-    case 4: return launch_moe_gemv<4, PAIR>(p, sms, st);
-    case 5: return launch_moe_gemv<5, PAIR>(p, sms, st);
-    case 6: return launch_moe_gemv<6, PAIR>(p, sms, st);
-    default: return cudaErrorInvalidValue;
-  }
+cudaError_t launch_moe_gemv_k(const MoeParams& p, int n, int sms, cudaStream_t st) {
+  cudaError_t e = cudaErrorInvalidValue;
+  with_rate_decode(n, PAIR ? p.cw_mask_gu : p.cw_mask_d, (PAIR ? p.mcg_gu : p.mcg_d) != 0, [&](auto N, auto DS) {
+    e = launch_moe_gemv<decltype(N)::value, PAIR, decltype(DS)::value>(p, sms, st);
+  });
+  return e;
 }
 
 template <typename Kern>
@@ -577,7 +632,7 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, const MoeParams& p, cud
 
 bool bank_ok(const exl3_weight* w, int in_f, int out_f) {
   return w && w->size == sizeof(exl3_weight) && w->trellis && w->suh && w->svh && w->nseg == 1 &&
-         w->in_features == in_f && w->out_features == out_f && w->n % 16 == 0 && w->n >= 16 && w->n <= 96 &&
+         w->in_features == in_f && w->out_features == out_f && exl3::rate_served_n(w->n) &&
          (reinterpret_cast<uintptr_t>(w->trellis) & 15u) == 0;
 }
 
@@ -648,6 +703,8 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   if (up->groups != experts || down->groups != experts || experts < 1 || experts > 1024)
     return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: the banks hold different expert counts");
   if (gate->n != up->n) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: gate and up banks at different rates");
+  if ((gate->flags ^ up->flags) & (EXL3_WEIGHT_WINDOW_MASK | EXL3_WEIGHT_MCG))
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: gate and up banks with different codeword windows or codebooks");
   if (gate->device != up->device || gate->device != down->device) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: banks on different devices");
   if (rows == 0) return {EXL3_OK, nullptr};
   const int dev = gate->device;
@@ -681,6 +738,10 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   p.nchunks = ints + 5 * kMaxSlots;
   p.bad = ints + 5 * kMaxSlots + 1;
   p.max_cb = sc->hidden / 128;
+  p.cw_mask_gu = window_mask(flags_window_bits(gate->flags));
+  p.cw_mask_d = window_mask(flags_window_bits(down->flags));
+  p.mcg_gu = (gate->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
+  p.mcg_d = (down->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
   p.unit_done = ints + kIntsM;
   p.part = reinterpret_cast<float*>(p.unit_done + 2 * static_cast<size_t>(kMaxSlots) * p.max_cb);
   uint8_t* cur = sc->base + fixed_bytes(sc->hidden, sc->sms);
@@ -698,8 +759,8 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
     err = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
     if (err == cudaSuccess)
       err = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S < kPrepChunks ? S : kPrepChunks), dim3(128), p, st);
-    if (err == cudaSuccess) err = launch_moe_gemv_k<true>(p, gate->n / 16, sc->sms, st);
-    if (err == cudaSuccess) err = launch_moe_gemv_k<false>(p, down->n / 16, sc->sms, st);
+    if (err == cudaSuccess) err = launch_moe_gemv_k<true>(p, gate->n, sc->sms, st);
+    if (err == cudaSuccess) err = launch_moe_gemv_k<false>(p, down->n, sc->sms, st);
     if (err == cudaSuccess)
       err = launch_pdl(moe_combine_kernel, dim3((hidden + 511) / 512, p.rows < kCombineRows ? p.rows : kCombineRows),
                        dim3(128), p, st);
@@ -995,9 +1056,10 @@ exl3_verdict exl3_swiglu_cp(exl3_cpx* e, const exl3_weight* gate, const exl3_wei
   const int islice = inter / W, hslice = hidden / W;
   const int experts = gate->groups;
   if (!bank_ok(gate, hidden, islice) || !bank_ok(up, hidden, islice) || !bank_ok(down, inter, hslice) ||
-      up->groups != experts || down->groups != experts || experts < 1 || experts > 1024 || gate->n != up->n)
+      up->groups != experts || down->groups != experts || experts < 1 || experts > 1024 || gate->n != up->n ||
+      ((gate->flags ^ up->flags) & (EXL3_WEIGHT_WINDOW_MASK | EXL3_WEIGHT_MCG)))
     return refuse_m(EXL3_UNSUPPORTED,
-                    "exl3_swiglu_cp: banks gate/up [E, hidden -> inter/W], down [E, inter -> hidden/W], one rate for gate and up");
+                    "exl3_swiglu_cp: banks gate/up [E, hidden -> inter/W], down [E, inter -> hidden/W], one rate and window for gate and up");
   if (gate->device != e->device || up->device != e->device || down->device != e->device)
     return refuse_m(EXL3_UNSUPPORTED, "exl3_swiglu_cp: banks on the exchange's device");
   MoeScratch* sc = nullptr;
@@ -1033,6 +1095,10 @@ exl3_verdict exl3_swiglu_cp(exl3_cpx* e, const exl3_weight* gate, const exl3_wei
   p.nchunks = ints + 5 * kMaxSlots;
   p.bad = ints + 5 * kMaxSlots + 1;
   p.max_cb = sc->hidden / 128;
+  p.cw_mask_gu = window_mask(flags_window_bits(gate->flags));
+  p.cw_mask_d = window_mask(flags_window_bits(down->flags));
+  p.mcg_gu = (gate->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
+  p.mcg_d = (down->flags & EXL3_WEIGHT_MCG) ? 1 : 0;
   p.unit_done = ints + kIntsM;
   p.part = reinterpret_cast<float*>(p.unit_done + 2 * static_cast<size_t>(kMaxSlots) * p.max_cb);
   uint8_t* cur = sc->base + fixed_bytes(sc->hidden, sc->sms);
@@ -1053,12 +1119,12 @@ exl3_verdict exl3_swiglu_cp(exl3_cpx* e, const exl3_weight* gate, const exl3_wei
   cudaError_t er = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
   if (er == cudaSuccess)
     er = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S < kPrepChunks ? S : kPrepChunks), dim3(128), p, st);
-  if (er == cudaSuccess) er = launch_moe_gemv_k<true>(p, gate->n / 16, sc->sms, st);
+  if (er == cudaSuccess) er = launch_moe_gemv_k<true>(p, gate->n, sc->sms, st);
   if (er == cudaSuccess) {
     cpx_sync_kernel<<<1, 32, 0, st>>>(e->dev, err);
     er = cudaGetLastError();
   }
-  if (er == cudaSuccess) er = launch_moe_gemv_k<false>(p, down->n / 16, sc->sms, st);
+  if (er == cudaSuccess) er = launch_moe_gemv_k<false>(p, down->n, sc->sms, st);
   if (er == cudaSuccess)
     er = launch_pdl(moe_combine_kernel, dim3((hslice + 511) / 512, p.rows < kCombineRows ? p.rows : kCombineRows),
                     dim3(128), p, st);

@@ -92,8 +92,10 @@ extern "C" exl3_verdict exl3_matmul_noalloc(const exl3_weight* w, const exl3_ten
   const int in_f = w->in_features, out_f = w->out_features, n = w->n;
   if (in_f <= 0 || out_f <= 0 || in_f % 128 != 0 || out_f % 128 != 0)
     return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: in and out features must be multiples of 128");
-  if (n % 16 != 0 || n < 16 || n > 96)
-    return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: fractional or >6-bit rates are not served");
+  if (w->flags & (EXL3_WEIGHT_WINDOW_MASK | EXL3_WEIGHT_MCG))
+    return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: narrowed codeword windows and mcg take exl3_matmul");
+  if (!exl3::rate_served_n(n))
+    return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: rates off the half-bit grid or above 6 bits are not served");
   if (out_f / 128 > static_cast<int>(kCounters))
     return refuse(EXL3_TOO_LARGE, "exl3_matmul_noalloc: out_features beyond the static scratch's 8192 column blocks");
   if ((reinterpret_cast<uintptr_t>(w->trellis) & 15u) != 0)
@@ -152,7 +154,7 @@ extern "C" exl3_verdict exl3_matmul_noalloc(const exl3_weight* w, const exl3_ten
       v = refuse(EXL3_TOO_LARGE, "exl3_matmul_noalloc: the layer needs more split partials than the 8 MiB static scratch");
       break;
     }
-    if (exl3::launch_gemv(gp, n / 16, rg, true, static_cast<cudaStream_t>(stream), true) != cudaSuccess)
+    if (exl3::launch_gemv(gp, n, rg, true, static_cast<cudaStream_t>(stream), true) != cudaSuccess)
       v = refuse(EXL3_FAILED, "exl3_matmul_noalloc: GEMV launch failed");
   }
   if (prev >= 0 && prev != w->device) cudaSetDevice(prev);

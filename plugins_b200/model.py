@@ -10,7 +10,7 @@ module is them, over this library's quant seam (:mod:`plugins_b200.quant`):
   ``parseJson``, in the library (``exl3_model_parse``, C++): MLX-free and bounds-checked; the pack's EXL3 blocks are
   checked with the reference's refusal names (``NotExl3``, ``Exl3CodebookUnsupported``, ``Exl3WindowUnsupported``,
   ``Exl3RateUnsupported``, ``Exl3TopKExceedsReduceBank``), narrowed to what this library decodes (the mul1 codebook,
-  16-bit windows, whole bits per weight 1..6);
+  windows 8..16, whole and half bits per weight 1..6);
 * ``bill(cfg, source)`` -- the resident bytes: EXL3 weights stay resident as the pack stores them
   (plugins/turboexl3_ds41/config.zig:57-61);
 * :class:`ModelLinears` -- the load (every EXL3 linear and routed bank of the pack uploaded once, the linears that
@@ -50,6 +50,7 @@ class ModelConfig:
     num_experts_per_tok: int = 0
     moe_intermediate_size: int = 0
     shared_expert_intermediate_size: int = 0
+    expert_rate_n: int = 0  # the expert bank's halfwords per tile (16 k), 0 without experts
     trunk_quant: dict = dataclasses.field(default_factory=dict)
     expert_quant: dict | None = None
 
@@ -73,7 +74,7 @@ def parse(config_json: str) -> ModelConfig:
                     trunk_quant=root["trunk_quant"], expert_quant=root.get("expert_quant"))
     for f in ("hidden_size", "intermediate_size", "num_hidden_layers", "num_attention_heads", "num_key_value_heads",
               "head_dim", "num_experts", "num_experts_per_tok", "moe_intermediate_size",
-              "shared_expert_intermediate_size"):
+              "shared_expert_intermediate_size", "expert_rate_n"):
         setattr(c, f, int(getattr(raw, f)))
     return c
 

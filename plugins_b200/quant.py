@@ -85,6 +85,15 @@ class Weight:
         return self.raw.n
 
     @property
+    def codebook(self) -> str:
+        return "mcg" if self.raw.flags & L.WEIGHT_MCG else "mul1"
+
+    @property
+    def window(self) -> int:
+        """The codeword window in bits (16 unless the pack narrowed it)."""
+        return 16 - ((self.raw.flags & L.WEIGHT_WINDOW_MASK) >> L.WEIGHT_WINDOW_SHIFT)
+
+    @property
     def bits(self) -> float:
         return self.raw.n / 16.0
 
@@ -101,8 +110,10 @@ class Weight:
         self._keep = ()
 
     def __del__(self):
+        # an owned weight frees its memory; a borrowed one drops its kept matrices (exl3_resident), whose key -- the
+        # device pointers -- a later weight may reuse once the tensors go
         try:
-            if self.raw.size and (self.raw.flags & L.WEIGHT_OWNED):
+            if self.raw.size:
                 self.release()
         except Exception:
             pass
@@ -264,9 +275,11 @@ def swiglu(gate: Weight, up: Weight, down: Weight, x: torch.Tensor, inds: torch.
 
 # ------------------------------------------------------------------ weights already on the device
 
-def weight_from_tensors(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor) -> Weight:
+def weight_from_tensors(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, window: int = 16,
+                        codebook: str = "mul1") -> Weight:
     """A borrowed view of device tensors in the pack layout: trellis [(G,) in/16, out/16, n] (int16/uint16),
-    suh [(G,) in] f16, svh [(G,) out] f16."""
+    suh [(G,) in] f16, svh [(G,) out] f16; ``window`` the block's codeword window (8..16 bits), ``codebook`` its
+    codebook (mul1 or mcg)."""
     if trellis.dim() == 3:
         g = 1
         kt, ot, n = trellis.shape
@@ -282,6 +295,11 @@ def weight_from_tensors(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Ten
     w = L.Weight()
     check(L.lib().exl3_weight_view(trellis.data_ptr(), suh.data_ptr(), svh.data_ptr(), g, kt * 16, ot * 16, n,
                                    trellis.device.index, ctypes.byref(w)))
+    if not 8 <= int(window) <= 16:
+        raise Exl3Error(L.EXL3_UNSUPPORTED, "exl3_b200: Exl3WindowUnsupported")
+    if codebook not in ("mul1", "mcg"):
+        raise Exl3Error(L.EXL3_UNSUPPORTED, "exl3_b200: Exl3CodebookUnsupported")
+    w.flags |= L.weight_window(window) | (L.WEIGHT_MCG if codebook == "mcg" else 0)
     return Weight(w, keep=(trellis, suh, svh))
 
 
@@ -333,6 +351,21 @@ def ep_combine(back: torch.Tensor, back_slot: torch.Tensor, scores: torch.Tensor
     check(L.lib().exl3_ep_combine(ctypes.byref(_tensor(back)), ctypes.byref(_tensor(back_slot)),
                                   ctypes.byref(_tensor(scores)), ctypes.byref(sh), _stream(stream),
                                   ctypes.byref(_tensor(out))))
+
+
+def resident(ws: list[Weight], room: int = 0, stream=None) -> int:
+    """quant.zig:96-99 ``resident``: keep the weights' decoded matrices from their first prefill call on (memory for
+    speed), if everything kept fits in ``room`` bytes (0: no bound); returns the bytes kept.  An empty list drops every
+    kept matrix."""
+    arr = (L.Weight * max(len(ws), 1))(*[w.raw for w in ws])
+    got = ctypes.c_uint64(0)
+    check(L.lib().exl3_resident(arr, len(ws), int(room), _stream(stream), ctypes.byref(got)))
+    return got.value
+
+
+def resident_pending() -> int:
+    """quant.zig:100-101 ``resident_pending``: the bytes ``resident`` admitted that no prefill call has filled yet."""
+    return int(L.lib().exl3_resident_pending())
 
 
 def device_error(device: int = 0, clear: bool = False) -> int:

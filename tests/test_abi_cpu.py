@@ -56,12 +56,15 @@ def test_validate_refuses_by_name():
         assert e.value.code == L.EXL3_UNSUPPORTED and "codebook is not mul1" in e.value.why
     with pytest.raises(Q.Exl3Error, match="Exl3WindowUnsupported"):
         Q.validate({"format": "exl3", "codebook": "mul1", "window": 20})
-    with pytest.raises(Q.Exl3Error, match="narrowed"):
-        Q.validate({"format": "exl3", "codebook": "mul1", "window": 12})
+    Q.validate({"format": "exl3", "codebook": "mul1", "window": 12})  # narrowed windows 8..15 are served
+    with pytest.raises(Q.Exl3Error, match="Exl3WindowUnsupported"):
+        Q.validate({"format": "exl3", "codebook": "mul1", "window": 7})
     with pytest.raises(Q.Exl3Error, match="Exl3RateUnsupported"):
         Q.validate({"format": "exl3", "codebook": "mul1", "k": 9.25})
-    with pytest.raises(Q.Exl3Error, match="fractional"):
-        Q.validate({"format": "exl3", "codebook": "mul1", "k": 2.5})
+    Q.validate({"format": "exl3", "codebook": "mul1", "k": 2.5})  # half-bit rates are served (n = 40)
+    for k in (2.25, 6.5):  # n = 36 (a quarter bit) and n = 104 (above 6 bits): admitted rates, not served
+        with pytest.raises(Q.Exl3Error, match="half-bit grid"):
+            Q.validate({"format": "exl3", "codebook": "mul1", "k": k})
     with pytest.raises(Q.Exl3Error, match="not an exllamav3 block"):
         Q.validate({"format": "gptq", "codebook": "mul1"})
     with pytest.raises(Q.Exl3Error, match="not a JSON object"):
@@ -89,6 +92,17 @@ def test_moe_entry_refuses_by_name_without_a_gpu_call():
 def test_matmul_rejects_a_null_weight_before_any_launch():
     v = L.lib().exl3_matmul(ctypes.POINTER(L.Weight)(), None, None, None)
     assert v.code == L.EXL3_FAILED
+
+
+def test_resident_keeps_nothing_and_refuses_a_bad_weight_without_a_gpu_call():
+    # quant.zig:96-101: an empty list drops every kept matrix; a weight that is not loaded is refused before any
+    # allocation
+    got = ctypes.c_uint64(7)
+    v = L.lib().exl3_resident(ctypes.POINTER(L.Weight)(), 0, 0, None, ctypes.byref(got))
+    assert v.code == L.EXL3_OK and got.value == 0 and L.lib().exl3_resident_pending() == 0
+    bad = L.Weight()
+    v = L.lib().exl3_resident(ctypes.byref(bad), 1, 0, None, ctypes.byref(got))
+    assert v.code == L.EXL3_FAILED and b"not a loaded weight" in v.why
 
 
 def test_bench_counts_launches_with_the_librarys_gemv_selection():

@@ -61,7 +61,7 @@ def _truth(oracle, x, tr, suh, svh, in_f, out_f, n):
                                _np(svh).view(np.uint16), in_f, out_f, n, threads=os.cpu_count() or 8)
 
 
-@pytest.mark.parametrize("n", [16, 48, 64, 96])
+@pytest.mark.parametrize("n", [16, 40, 48, 64, 88, 96])
 def test_one_hot_rows_reproduce_w_hat(Q, E, oracle, shape, n):
     # prepared x = the identity, inner product: every output row is a row of W_hat, exactly (1.0 * w + 0s in f32)
     in_f, out_f = 256, 640  # 640 columns: a ragged last tile for the 256-wide shapes
@@ -79,6 +79,7 @@ CASES = [
     # (in, out, n, rows)
     (512, 768, 64, 64), (1024, 640, 48, 200), (256, 1280, 32, 333), (768, 384, 96, 130), (384, 512, 80, 257),
     (5120, 2304, 48, 128),  # the DeepSeek-V4.1 prefill shape (dsv41_prefill_dig_gemm_5120x2304)
+    (512, 768, 56, 96), (768, 512, 24, 300),  # half-bit rates: 3.5 and 1.5 bits per weight
 ]
 
 
@@ -192,3 +193,38 @@ def test_unaligned_rows_take_the_gemv(Q, E, oracle):
     y = Q.matmul(w, x)
     want = _truth(oracle, x, tr, suh, svh, in_f, out_f, n)
     assert _rel(y.float().cpu().numpy(), want) < REL_L2_BAR
+
+
+def test_kept_matrices_give_the_decoding_calls_bytes(Q, E):
+    # quant.zig:96-101 resident / resident_pending: the first prefill call after exl3_resident fills the kept matrix,
+    # later calls read it instead of decoding; every call gives the bytes of the decoding path, for a plain linear
+    # (640 columns: a ragged last tile), a stacked one and a grouped one
+    from plugins_b200 import _lib as L
+    plain = Q.weight_from_tensors(*E.random_linear(512, 640, 48, seed=31))
+    stacked = Q.stack([Q.weight_from_tensors(*E.random_linear(512, o, 64, seed=40 + i))
+                       for i, o in enumerate((384, 128, 128))])
+    grouped = Q.weight_from_tensors(*E.random_linear(256, 384, 64, seed=50, groups=3))
+    grouped.raw.flags |= L.WEIGHT_GROUPED
+    xs = {id(plain): torch.randn((100, 512), device="cuda", dtype=torch.float16),
+          id(stacked): torch.randn((300, 512), device="cuda", dtype=torch.bfloat16),
+          id(grouped): torch.randn((70, 3, 256), device="cuda", dtype=torch.float16)}
+    ws = (plain, stacked, grouped)
+    want = {id(w): Q.matmul(w, xs[id(w)]) for w in ws}
+    try:
+        kept = Q.resident(list(ws))
+        assert kept == (640 // 128 + 2) * 512 * 256 + (640 // 128 + 2) * 512 * 256 + 3 * (384 // 128 + 2) * 256 * 256
+        assert Q.resident_pending() == kept
+        assert Q.resident([plain]) == kept  # kept once
+        for rep in range(2):
+            for w in ws:
+                y = Q.matmul(w, xs[id(w)])
+                assert torch.equal(y.view(torch.int16), want[id(w)].view(torch.int16)), (rep, w.out_features)
+            assert Q.resident_pending() == 0
+        with pytest.raises(Q.Exl3Error, match="room"):
+            Q.resident([Q.weight_from_tensors(*E.random_linear(256, 256, 32, seed=60))], room=kept + 1)
+        assert Q.resident([]) == 0 and Q.resident_pending() == 0
+        y = Q.matmul(plain, xs[id(plain)])
+        assert torch.equal(y.view(torch.int16), want[id(plain)].view(torch.int16))
+    finally:
+        Q.resident([])
+    assert Q.device_error(0) == 0

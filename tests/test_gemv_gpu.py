@@ -56,7 +56,7 @@ def _np(t):
     return t.detach().cpu().numpy()
 
 
-@pytest.mark.parametrize("n", [16, 32, 48, 64, 80, 96])
+@pytest.mark.parametrize("n", list(range(16, 97, 8)))  # whole and half bits per weight, 1..6
 @pytest.mark.parametrize("dp4a", [False, True])
 def test_decode_dense_bit_exact(Q, E, oracle, n, dp4a):
     in_f, out_f = 256, 384
@@ -65,6 +65,28 @@ def test_decode_dense_bit_exact(Q, E, oracle, n, dp4a):
     got = Q.decode_dense(w, dp4a=dp4a).view(torch.uint16).cpu().numpy()
     want = oracle.reconstruct_inner(_np(tr).view(np.uint16), in_f, out_f, n)
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("n", [24, 32, 40, 48])
+@pytest.mark.parametrize("dp4a", [False, True])
+def test_frac_tiles_decode_on_gpu(Q, oracle, n, dp4a):
+    # the real exllamav3 tiles at 1.5-3 bits (plugins/turboexl3_ds41/src/frac_tiles.json, frac_test.zig:23-57) laid
+    # into a 128 x 128 layer (random words elsewhere) decode on the GPU to their pinned f16 bits, tile for tile
+    tiles = [t for t in json.load(open(os.path.join(GOLD, "frac_tiles.json")))["tiles"] if t["n"] == n]
+    assert 14 <= len(tiles) <= 64
+    rng = np.random.default_rng(n)
+    words = rng.integers(0, 65536, (8, 8, n), dtype=np.uint16)
+    for i, t in enumerate(tiles):
+        words[i // 8, i % 8] = t["words"]
+    tr = torch.from_numpy(words.view(np.int16)).cuda()
+    suh = torch.ones(128, dtype=torch.float16, device="cuda")
+    svh = torch.ones(128, dtype=torch.float16, device="cuda")
+    w = Q.weight_from_tensors(tr, suh, svh)
+    got = Q.decode_dense(w, dp4a=dp4a).view(torch.uint16).cpu().numpy()
+    for i, t in enumerate(tiles):
+        ti, tj = i // 8, i % 8
+        assert got[16 * ti:16 * ti + 16, 16 * tj:16 * tj + 16].reshape(-1).tolist() == t["expect"], t["src"]
+    assert np.array_equal(got, oracle.reconstruct_inner(words, 128, 128, n))
 
 
 @pytest.mark.parametrize("name", ["down_k2", "gate_up_k2", "down", "gate_up"])
@@ -99,6 +121,8 @@ CASES = [
     (512, 640, 64, 9), (512, 256, 48, 16), (384, 512, 64, 17), (1024, 1024, 96, 2), (640, 384, 16, 4),
     # DeepSeek-V4.1 widths (the ds41 kernels' 5120 / 2304, TK/dsv41_exl3_mul1h_k{2,3}_*.metal)
     (5120, 2304, 32, 1), (2304, 5120, 48, 4),
+    # half-bit rates (n = 16 k halfwords, k = 1.5 .. 5.5): the lane windows straddle word boundaries
+    (384, 256, 24, 1), (256, 384, 40, 8), (512, 640, 56, 9), (512, 256, 72, 16), (1024, 1024, 88, 3),
 ]
 
 
@@ -217,11 +241,12 @@ def test_north_star_layer_parity(Q, E, oracle):
     assert Q.device_error(0) == 0
 
 
-def test_persistent_gemv_layer_against_truth_and_row_invariance(Q, E, oracle):
-    # config 2's down layer, 12288 -> 4096 at 3 bpw: large enough for the persistent GEMV (exl3_gemv6.cu: 8192
-    # inputs and 16384 slab-units or more), at 1-4 rows with the input rotated in-CTA, at 8 with the prepare launch,
-    # at 12-16 with two row groups; against the f32 truth, and row r's bytes the same at every width
-    in_f, out_f, n = 12288, 4096, 48
+@pytest.mark.parametrize("n", [48, 40])
+def test_persistent_gemv_layer_against_truth_and_row_invariance(Q, E, oracle, n):
+    # config 2's down layer, 12288 -> 4096 at 3 (and 2.5) bpw: large enough for the persistent GEMV (exl3_gemv6.cu:
+    # 8192 inputs and 16384 slab-units or more), at 1-4 rows with the input rotated in-CTA, at 8 with the prepare
+    # launch, at 12-16 with two row groups; against the f32 truth, and row r's bytes the same at every width
+    in_f, out_f = 12288, 4096
     tr, suh, svh = _linear(E, in_f, out_f, n, seed=12)
     w = Q.weight_from_tensors(tr, suh, svh)
     x = torch.randn((16, in_f), device="cuda", dtype=torch.float16)
@@ -291,9 +316,9 @@ def test_shapes_are_refused_by_name(Q, E):
         Q.matmul(w, torch.zeros((1, 384), device="cuda", dtype=torch.float16))
     with pytest.raises(Q.Exl3Error, match="f16, bf16 or f32"):
         Q.matmul(w, torch.zeros((1, 256), device="cuda", dtype=torch.int32))
-    tr40 = torch.zeros((16, 16, 40), dtype=torch.int16, device="cuda")
-    with pytest.raises(Q.Exl3Error, match="fractional"):
-        Q.weight_from_tensors(tr40, suh, svh)
+    tr36 = torch.zeros((16, 16, 36), dtype=torch.int16, device="cuda")  # 2.25 bits: off the half-bit grid
+    with pytest.raises(Q.Exl3Error, match="half-bit grid"):
+        Q.weight_from_tensors(tr36, suh, svh)
     y = Q.matmul(w, torch.zeros((0, 256), device="cuda", dtype=torch.float16))
     assert y.shape == (0, 256)
 

@@ -40,10 +40,11 @@ def test_claims_by_marker_only_a_qwen38_pack_with_a_trunk_block():
 @pytest.mark.parametrize("edit,name", [
     ({"trunk_quant": {"format": "awq"}}, "NotExl3"),
     ({"trunk_quant": "exl3"}, "TrunkQuantNotAnObject"),
-    ({"trunk_quant": {"format": "exl3", "codebook": "mcg"}}, "Exl3CodebookUnsupported"),
-    ({"trunk_quant": {"format": "exl3", "codebook": "mul1", "window": 12}}, "Exl3WindowUnsupported"),
+    ({"trunk_quant": {"format": "exl3", "codebook": "3inst"}}, "Exl3CodebookUnsupported"),
+    ({"trunk_quant": {"format": "exl3", "codebook": "mul1", "window": 7}}, "Exl3WindowUnsupported"),
+    ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 3, "window": 17}}, "Exl3WindowUnsupported"),
     ({"expert_quant": {"format": "exl3", "codebook": "mul1"}}, "Exl3RateUnsupported"),
-    ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 2.5}}, "Exl3RateUnsupported"),
+    ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 2.25}}, "Exl3RateUnsupported"),
     ({"expert_quant": {"format": "exl3", "codebook": "mul1", "k": 8}}, "Exl3RateUnsupported"),
     ({"expert_quant": {"format": "exl3", "k": 3}}, "Exl3CodebookUnsupported"),
     ({"num_experts_per_tok": 33}, "Exl3TopKExceedsReduceBank"),
@@ -70,6 +71,14 @@ def test_parse_reads_the_linears_keys():
     flat = _config()
     flat.update(flat.pop("text_config"))  # keys at the root read the same
     assert M.parse(json.dumps(flat)).moe_intermediate_size == MOE_INTER
+    half = _config(expert_quant={"format": "exl3", "codebook": "mul1", "k": 2.5})
+    assert M.parse(json.dumps(half)).expert_rate_n == 40  # the half-bit rates are served: n = 16 k halfwords
+    narrow = _config(trunk_quant={"format": "exl3", "codebook": "mul1", "window": 12},
+                     expert_quant={"format": "exl3", "codebook": "mul1", "k": 3, "window": 8})
+    assert M.parse(json.dumps(narrow)).expert_rate_n == 48  # narrowed codeword windows 8..15 are served
+    mcg = _config(trunk_quant={"format": "exl3", "codebook": "mcg"},
+                  expert_quant={"format": "exl3", "codebook": "mcg", "k": 2.5, "window": 12})
+    assert M.parse(json.dumps(mcg)).expert_rate_n == 40  # the mcg codebook too (config.zig:86-104)
 
 
 def _linear(rng, i, o, n):

@@ -34,6 +34,7 @@ def _route(rows, experts, topk, seed):
     (16, 384, 256, 4, 20, 32, 64, 0, "float32"),
     (8, 256, 256, 8, 16, 48, 48, 7, "float16"),
     (64, 512, 256, 6, 5, 48, 32, 0, "float16"),
+    (16, 256, 384, 4, 7, 40, 56, 0, "bfloat16"),  # half-bit banks: 2.5 and 3.5 bits per weight
 ])
 def test_swiglu_against_f32_truth(oracle, experts, hidden, inter, topk, rows, ng, nd, limit, dtype):
     from plugins_b200 import encoder as E
@@ -136,3 +137,27 @@ def test_config4_call_at_full_size(oracle):
     floor = float(np.sqrt(((torch.from_numpy(want).half().float().numpy() - want) ** 2).sum() / (want ** 2).sum()))
     assert err < np.sqrt(REL_L2_BAR ** 2 + floor ** 2), (err, floor)
     assert Q.device_error(0) == 0
+
+
+@pytest.mark.parametrize("experts,hidden,inter,topk,n", [
+    (64, 2048, 1024, 8, 48),  # 32 rows: whole units and shared ones; 1-16 rows: shared only
+    (16, 1024, 512, 4, 64),
+    (256, 4096, 2048, 8, 48),  # config 4's widths
+])
+def test_rows_share_a_call_without_changing_bytes(experts, hidden, inter, topk, n):
+    # the reference's row invariance on its expert kernels (plugins/turboexl3_ds41/src/exl3/selfcheck.zig:755-851):
+    # rows slot .. slot + m - 1 computed alone have the bytes they have in the full call, whichever other rows and
+    # experts share it (exl3_moe.cu cuts every unit's k range into the same runs in every call)
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    wg, wu, wd = (Q.weight_from_tensors(*_bank(E, experts, i, o, n, s))
+                  for i, o, s in ((hidden, inter, 1), (hidden, inter, 2), (inter, hidden, 3)))
+    rows = 32
+    ind, sc = _route(rows, experts, topk, 7)
+    ind, sc = ind.view(1, rows, topk).cuda(), sc.view(1, rows, topk).cuda()
+    x = (torch.randn((1, rows, hidden), generator=torch.Generator().manual_seed(8)) * 2).to(torch.float16).cuda()
+    full = Q.swiglu(wg, wu, wd, x, ind, sc)
+    for m, slot in ((1, 0), (1, 17), (2, 30), (3, 5), (8, 24), (16, 0), (31, 1)):
+        y = Q.swiglu(wg, wu, wd, x[:, slot:slot + m].contiguous(), ind[:, slot:slot + m].contiguous(),
+                     sc[:, slot:slot + m].contiguous())
+        assert torch.equal(y.view(torch.int16), full[:, slot:slot + m].view(torch.int16)), (m, slot)
