@@ -349,12 +349,16 @@ exl3_verdict exl3_encode_trellis(const float *target, int32_t in_features, int32
 
 /* matmul without any allocation (no counterpart in the reference): for hosts that cannot let a library call
  * cudaMalloc -- a server that reserves its device memory up front and admits nothing beyond its memory bill, or an
- * embedding runtime whose own allocator owns every device byte.  Same result as exl3_matmul, but the scratch (split
- * partials, counters) lives in one static device array of 8 MiB + 32 KiB that every device loading the library holds
- * until exit; the weight struct may be filled by hand (no exl3_weight_view needed).  One ungrouped weight (stacked
- * segments allowed).  A layer needing more partials than the array holds is refused with EXL3_TOO_LARGE.  The first
- * call on a device looks the array up (cudaGetSymbolAddress) and clears its counters: make it before any stream
- * capture.  All calls share the array: calls that overlap on the GPU race -- order them on one stream. */
+ * embedding runtime whose own allocator owns every device byte.  The same decode and f32 accumulation as
+ * exl3_matmul, within the same 2e-3 rel-L2 of the f32 truth but not bit-identical to it (exl3_matmul chooses other
+ * kernels by shape, whose sums run in another order); kernel errors land in the word exl3_device_error reads.  The
+ * scratch (split partials, counters) lives in one static device array of 8 MiB + 32 KiB that every device loading
+ * the library holds until exit; the weight struct may be filled by hand (no exl3_weight_view needed), and its
+ * seg_cols must run from 0 to out_features in whole 128-column blocks.  One ungrouped weight (stacked segments
+ * allowed), at most 2^24 rows.  A layer needing more partials than the array holds is refused with EXL3_TOO_LARGE.
+ * The first call on a device looks the array up (cudaGetSymbolAddress) and clears its counters with a memset on the
+ * caller's stream: make it before any stream capture.  All calls share the array: calls that overlap on the GPU
+ * race -- order them on one stream. */
 exl3_verdict exl3_matmul_noalloc(const exl3_weight *w, const exl3_tensor *x, void *stream, exl3_tensor *out);
 
 /* Resident decoded matrices (QuantTable.resident / resident_pending, plugins/turboexl3_qwen38/overlay/mlx_serve/abi/

@@ -6,13 +6,18 @@
 // first time a weight is registered.  This entry point runs the same kernel with its scratch (the split partials,
 // the per-column-block counters and an error word) in one static device array instead, so the caller passes the
 // weight, the input and the output and nothing is allocated -- no cudaMalloc, no cudaFree, no allocating library.
+// The kernel is the grid-stride decode GEMV (exl3_gemv.cu): the same decode and the same f32 accumulation as
+// exl3_matmul, within its 2e-3 rel-L2 bar of the f32 truth, but not bit-identical to it (exl3_matmul picks other
+// kernels by shape, and their sums run in another order).  Kernel errors land in the device error word that
+// exl3_device_error reads and clears.
 //
 // Limits and rules:
 //   * the static array holds 8 MiB of split partials and 8192 counters; a call whose layer needs more partials
 //     (large in_features x out_features at many rows) is refused with EXL3_TOO_LARGE before any launch;
 //   * every device that loads the library holds the array (about 8 MiB) until the process exits;
 //   * the first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device
-//     current) and clears the counters; make that first call before any stream capture;
+//     current) and clears the counters with a memset on the caller's stream; make that first call before any
+//     stream capture;
 //   * all calls share the array and it keeps the last call's contents: the kernel returns every counter it raised
 //     to zero, and calls that overlap on the GPU (concurrent streams, or two devices' calls racing through one
 //     device) race on it -- order them on one stream.
@@ -28,7 +33,7 @@ namespace {
 
 constexpr size_t kPartialFloats = size_t(2) << 20;  // 8 MiB of split partials
 constexpr size_t kCounters = 8192;                   // column blocks (out_features <= 1,048,576)
-constexpr size_t kScratchWords = kPartialFloats + kCounters + 64;
+constexpr size_t kScratchWords = kPartialFloats + kCounters;
 
 // The scratch.  In host code this name is only a stand-in for the device array: its device address comes from
 // cudaGetSymbolAddress, per device.
@@ -38,7 +43,7 @@ struct Scratch {
   bool ready = false;
   float* partials = nullptr;
   uint32_t* counters = nullptr;
-  uint32_t* err = nullptr;
+  uint32_t* err = nullptr;  // the library's device error word (exl3_device_error), not part of the array
   int sms = 0;
 };
 
@@ -48,8 +53,9 @@ Scratch g_scratch[kMaxDevices];
 
 exl3_verdict refuse(int32_t code, const char* why) { return {code, why}; }
 
-// Once per device, with that device current: the array's device address, the SM count, zeroed counters.
-exl3_verdict scratch_for(int dev, Scratch** out) {
+// Once per device, with that device current: the array's device address, the SM count, the counters zeroed on the
+// caller's stream.
+exl3_verdict scratch_for(int dev, cudaStream_t st, Scratch** out) {
   if (dev < 0 || dev >= kMaxDevices) return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: device index out of range");
   std::lock_guard<std::mutex> lk(g_mu);
   Scratch& s = g_scratch[dev];
@@ -65,9 +71,9 @@ exl3_verdict scratch_for(int dev, Scratch** out) {
     uint32_t* words = static_cast<uint32_t*>(base);
     s.partials = reinterpret_cast<float*>(words);
     s.counters = words + kPartialFloats;
-    s.err = words + kPartialFloats + kCounters;
-    if (cudaMemset(s.counters, 0, (kCounters + 64) * sizeof(uint32_t)) != cudaSuccess ||
-        cudaDeviceSynchronize() != cudaSuccess)
+    s.err = exl3::device_error_ptr();
+    if (s.err == nullptr) return refuse(EXL3_FAILED, "exl3_matmul_noalloc: no device error word");
+    if (cudaMemsetAsync(s.counters, 0, kCounters * sizeof(uint32_t), st) != cudaSuccess)
       return refuse(EXL3_FAILED, "exl3_matmul_noalloc: clearing the static scratch failed");
     s.ready = true;
   }
@@ -96,6 +102,13 @@ extern "C" exl3_verdict exl3_matmul_noalloc(const exl3_weight* w, const exl3_ten
     return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: narrowed codeword windows and mcg take exl3_matmul");
   if (!exl3::rate_served_n(n))
     return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: rates off the half-bit grid or above 6 bits are not served");
+  // stacked segments: bounds from 0 to out_features, each a multiple of 128 and above the one before (a weight
+  // struct filled by hand is checked here; the launch geometry divides by each segment's width)
+  if (w->seg_cols[0] != 0 || w->seg_cols[w->nseg] != out_f)
+    return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: seg_cols must run from 0 to out_features");
+  for (int s = 0; s < w->nseg; ++s)
+    if (w->seg_cols[s + 1] <= w->seg_cols[s] || w->seg_cols[s + 1] % 128 != 0)
+      return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: seg_cols must rise in steps of whole 128-column blocks");
   if (out_f / 128 > static_cast<int>(kCounters))
     return refuse(EXL3_TOO_LARGE, "exl3_matmul_noalloc: out_features beyond the static scratch's 8192 column blocks");
   if ((reinterpret_cast<uintptr_t>(w->trellis) & 15u) != 0)
@@ -109,6 +122,7 @@ extern "C" exl3_verdict exl3_matmul_noalloc(const exl3_weight* w, const exl3_ten
   for (int i = 0; i < x->ndim - 1; ++i)
     if (out->shape[i] != x->shape[i]) return refuse(EXL3_UNSUPPORTED, "exl3_matmul_noalloc: the output has the wrong shape");
   const int64_t rows = numel(x) / in_f;
+  if (rows > (int64_t{1} << 24)) return refuse(EXL3_TOO_LARGE, "exl3_matmul_noalloc: more than 2^24 rows");
   if (rows == 0) return {EXL3_OK, nullptr};
   if (!x->data || !out->data) return refuse(EXL3_FAILED, "exl3_matmul_noalloc: bad tensors");
 
@@ -117,9 +131,7 @@ extern "C" exl3_verdict exl3_matmul_noalloc(const exl3_weight* w, const exl3_ten
   if (prev != w->device && cudaSetDevice(w->device) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_matmul_noalloc: cannot select the weight's device");
   Scratch* sc = nullptr;
-  exl3_verdict v = scratch_for(w->device, &sc);
-  const size_t xsz = x->dtype == EXL3_F32 ? 4 : 2;
-  (void)xsz;
+  exl3_verdict v = scratch_for(w->device, static_cast<cudaStream_t>(stream), &sc);
   for (int64_t r0 = 0; v.code == EXL3_OK && r0 < rows; r0 += exl3::kMaxRows) {
     const int rc = static_cast<int>(rows - r0 < exl3::kMaxRows ? rows - r0 : exl3::kMaxRows);
     const int rg = rc <= 8 ? 1 : 2;
