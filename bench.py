@@ -108,6 +108,58 @@ def _graph_ms(torch, fn, reps: int, inner: int = 4) -> float:
     return e0.elapsed_time(e1) / (reps * inner)
 
 
+def measure_layer(Q, E, torch, peaks: dict, in_f: int, out_f: int, bits: int, seed: int, label: str,
+                  copies: int = 36, reps: int = 20) -> dict:
+    """One decode-GEMV layer at batch 1: W N(0, 0.02) (seed) encoded at `bits` by the library's encoder, held as
+    `copies` distinct device copies (so consecutive launches stream distinct bytes, >> 126 MB L2), the copies' launches
+    captured back to back in one CUDA graph; each replay is timed with events on its stream, and the median and the
+    fastest replay give microseconds per launch (the reference's chainNs statistics, SX/bench_util.zig:41-74)."""
+    n = 16 * bits
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w = torch.randn((out_f, in_f), generator=g, device="cuda") * 0.02
+    tr, suh, svh = E.quantize(w, bits, seed)
+    del w
+    trs = [tr.clone() for _ in range(copies)]
+    ws = [Q.weight_from_tensors(t, suh, svh) for t in trs]
+    x = torch.randn((1, in_f), generator=g, device="cuda").half()
+    y = torch.empty((1, out_f), device="cuda", dtype=torch.float16)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for wi in ws[:3]:
+            Q.matmul(wi, x, out=y)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=s):
+        for wi in ws:
+            Q.matmul(wi, x, out=y)
+    for _ in range(5):
+        gr.replay()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    with torch.cuda.stream(s):
+        ev[0].record(s)
+        for i in range(reps):
+            gr.replay()
+            ev[i + 1].record(s)
+    torch.cuda.synchronize()
+    per = sorted(ev[i].elapsed_time(ev[i + 1]) * 1000.0 / copies for i in range(reps))
+    gr.reset()
+    nbytes = linear_bytes(in_f, out_f, bits, 1)
+    med, fast = statistics.median(per), per[0]
+    gbs = nbytes / (med * 1e-6) / 1e9
+    del ws, trs
+    return {"workload": label, "us_per_launch": round(med, 3), "us_fastest": round(fast, 3),
+            "value": round(gbs, 1), "unit": "GB/s", "bytes_per_launch": nbytes,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4),
+                         "frac_fastest": round(nbytes / (fast * 1e-6) / 1e9 / peaks["hbm_gbs"], 4),
+                         "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
+            "timing": f"{copies} distinct copies per CUDA-graph replay, {reps} replays timed one by one with events; "
+                      "median (value) and fastest",
+            "l2": "no flush: a replay streams %.2f GB of distinct weights (> 126 MB L2)" % (copies * nbytes / 1e9)}
+
+
 def measure_prefill(Q, E, torch, peaks: dict, reps: int = 10) -> dict:
     """Config 3: X [M, 4096] bf16 through the 4096 x 12288 4-bpw layer (seed 2), M = 2048 headline plus 64, 256 and
     8192 for the GEMV/GEMM crossover.  Whole-path time per call (operand images + tensor-core GEMM) and the GEMM
@@ -391,6 +443,30 @@ def cpu_sample(rows: int, budget_s: float, threads: int, seed: int = 1):
     return done_bytes / el / 1e9, el, reps
 
 
+def zig_probe() -> str:
+    """`zig version` on this host: the reference's own build (Zig ReleaseFast) needs it."""
+    import shutil
+    import subprocess
+    z = shutil.which("zig")
+    if z is None:
+        return "absent (no zig on PATH): the C restatement of project() is timed instead"
+    try:
+        return "zig " + subprocess.run([z, "version"], capture_output=True, text=True, timeout=20).stdout.strip()
+    except Exception as e:  # noqa: BLE001
+        return f"zig present but `zig version` failed: {e}"
+
+
+def host_cpu() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip() + f", {os.cpu_count()} threads"
+    except OSError:
+        pass
+    return f"{os.cpu_count()} threads"
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -415,7 +491,8 @@ def run_reference(args) -> None:
         "decode_tok_s": round(args.batch / (layer_s * LAYERS), 4),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"layer 0's 7 linears at batch {args.batch} per step (1/36 of a decode step); "
-                                   "C restatement of expert_exl3.zig project(), OpenMP over output tiles"},
+                                   "C restatement of expert_exl3.zig project(), OpenMP over output tiles",
+                         "host_cpu": host_cpu(), "zig": zig_probe()},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -587,14 +664,20 @@ def main() -> None:
             dist.barrier()
         torch.cuda.synchronize()
         st = torch.cuda.current_stream()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
         with ClockSampler(local) as clk:
-            e0.record(st)
-            for _ in range(steps):
+            evs[0].record(st)
+            for i in range(steps):
                 graph.replay()
-            e1.record(st)
+                evs[i + 1].record(st)
             torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / steps
+        ms = evs[0].elapsed_time(evs[steps]) / steps
+        per_step = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(steps))
+        ms_med, ms_fast = statistics.median(per_step), per_step[0]
+        if world > 1:
+            t = torch.tensor([ms_med, ms_fast], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_med, ms_fast = float(t[0].item()), float(t[1].item())
         if world > 1:
             t = torch.tensor([ms], device=device)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -657,7 +740,8 @@ def main() -> None:
             if world > 1:
                 dist.barrier()  # no rank unmaps its exchange while another still writes into it
             ex.close()
-        return {"ms": ms, "ms_e2e": ms_e2e, "clk": clk.summary(), "launches": launches_per_step * steps,
+        return {"ms": ms, "ms_med": ms_med, "ms_fast": ms_fast, "ms_e2e": ms_e2e, "clk": clk.summary(),
+                "launches": launches_per_step * steps,
                 "h2d": in_buf.numel() * in_buf.element_size(), "d2h": out_buf.numel() * out_buf.element_size(),
                 "dom_ms": dom_ms, "qkv_ms": qkv_ms}
 
@@ -677,9 +761,14 @@ def main() -> None:
     if rank == 0 and world == 1 and args.cpu_budget > 0:
         threads = os.cpu_count() or 1
         gbs, el, reps = cpu_sample(args.batch, args.cpu_budget, threads)
+        gbs1, el1, reps1 = cpu_sample(args.batch, args.cpu_budget, 1)
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"layer 0's 7 linears at batch {args.batch}, {reps} pass(es) in {el:.1f} s; C restatement "
-                         "of expert_exl3.zig project() (scalar decode+GEMV), OpenMP over output tiles"}
+                         "of expert_exl3.zig project() (scalar decode+GEMV), OpenMP over output tiles",
+               "single_core": {"value": round(gbs1, 4), "unit": "GB/s", "cores": 1,
+                               "sample": f"the same linears, {reps1} pass(es) in {el1:.1f} s on one thread (the "
+                                         "reference's project() is single-threaded)"},
+               "host_cpu": host_cpu(), "zig": zig_probe()}
     if rank == 0:
         traffic = None
         try:
@@ -690,7 +779,9 @@ def main() -> None:
             pass
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(r1["ms"], 4), "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": round(r1["ms"], 4),
+            "ms_per_step_median": round(r1["ms_med"], 4), "ms_per_step_fastest": round(r1["ms_fast"], 4),
+            "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "u16 trellis -> f16 (f32 accumulate)",
             "data": "synthetic: random-init N(0,0.02) weights (seeded) encoded to EXL3 mul1 by the library; "
                     "N(0,1) f16 activations",
@@ -725,6 +816,12 @@ def main() -> None:
         if moe_ep is not None:
             line["moe_ep"] = moe_ep
         if world == 1 and not args.no_extras:
+            line["north_star"] = measure_layer(Q, E, torch, peaks, 4096, 12288, 4, 0,
+                                               "north-star layer: 4096 x 12288 @ 4 bpw decode GEMV, batch 1 "
+                                               "(W N(0,0.02) seed 0, 36 distinct copies)")
+            line["config1"] = measure_layer(Q, E, torch, peaks, 4096, 4096, 4, 0,
+                                            "config 1: 4096 x 4096 @ 4 bpw decode GEMV, batch 1 "
+                                            "(W N(0,0.02) seed 0, 36 distinct copies)")
             line["prefill"] = measure_prefill(Q, E, torch, peaks)
             line["moe"] = measure_moe(Q, E, torch, peaks)
             line["large_layer"] = measure_c5(Q, E, torch, peaks)

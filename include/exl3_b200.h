@@ -341,6 +341,12 @@ exl3_verdict exl3_weight_stack(const exl3_weight *parts, int32_t count, void *st
  * plugins/turboexl3_ds41/src/exl3/selfcheck.zig:861-930). */
 exl3_verdict exl3_decode_dense(const exl3_weight *w, int32_t group, uint16_t *out, uint32_t flags, void *stream);
 
+/* The dense effective W of group `group` (plugins/sushi_ds41/src/sushi/exl3/expert_exl3.zig:440-488
+ * reconstructPublic, the dense twin SX/linear.zig:200-224 checks against): f16 bits, row-major [in][out], with
+ * x @ W_eff = the linear's output -- W_eff[r][c] = f16(svh[c] * (H128 (suh[r] * (H128 W_hat)[r][.]))[c]), the
+ * Hadamards orthonormal, in f32.  One linear (nseg 1). */
+exl3_verdict exl3_reconstruct_public(const exl3_weight *w, int32_t group, uint16_t *out, void *stream);
+
 /* Trellis encoder (no counterpart in the reference, which ships no encoder: plugins/turboexl3_ds41/NOTICE:30-32).
  * `target` (device f32, row-major [in][out]) is the matrix the trellis should decode to -- already rotated by the
  * 128-wide Hadamards and scaled to the codebook's unit variance; `trellis` (device) receives [in/16][out/16][n]. */

@@ -37,7 +37,7 @@ EXPORTS = (
     "exl3_cpx_create", "exl3_cpx_connect", "exl3_cpx_destroy", "exl3_swiglu_cp",
     "exl3_tp_create", "exl3_tp_connect", "exl3_tp_destroy", "exl3_tp_begin", "exl3_matmul_tp", "exl3_tp_gather",
     "exl3_weight_view", "exl3_weight_stack",
-    "exl3_decode_dense", "exl3_encode_trellis", "exl3_matmul_noalloc", "exl3_device_error", "exl3_version",
+    "exl3_decode_dense", "exl3_reconstruct_public", "exl3_encode_trellis", "exl3_matmul_noalloc", "exl3_device_error", "exl3_version",
     "exl3_model_claims", "exl3_model_parse", "exl3_resident", "exl3_resident_pending",
 )
 
@@ -222,6 +222,8 @@ def lib() -> ctypes.CDLL:
             L.exl3_decode_dense.restype = Verdict
             L.exl3_decode_dense.argtypes = [P(Weight), ctypes.c_int32, ctypes.c_void_p, ctypes.c_uint32,
                                             ctypes.c_void_p]
+            L.exl3_reconstruct_public.restype = Verdict
+            L.exl3_reconstruct_public.argtypes = [P(Weight), ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
             L.exl3_encode_trellis.restype = Verdict
             L.exl3_encode_trellis.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_void_p, ctypes.c_void_p]

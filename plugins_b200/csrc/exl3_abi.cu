@@ -1118,6 +1118,22 @@ exl3_verdict exl3_decode_dense(const exl3_weight* w, int32_t group, uint16_t* ou
   return kOk;
 }
 
+exl3_verdict exl3_reconstruct_public(const exl3_weight* w, int32_t group, uint16_t* out, void* stream) {
+  exl3_verdict v = check_weight(w);
+  if (v.code != EXL3_OK) return v;
+  if (group < 0 || group >= w->groups || !out) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");
+  if (w->nseg != 1) return refuse(EXL3_UNSUPPORTED, "exl3_b200: the dense effective W of one linear (not a stack)");
+  DeviceGuard guard(w->device);
+  const size_t tw = static_cast<size_t>(w->in_features / 16) * (w->out_features / 16) * w->n;
+  if (exl3::launch_reconstruct_public(w->trellis + group * tw, w->suh + static_cast<size_t>(group) * w->in_features,
+                                      w->svh + static_cast<size_t>(group) * w->out_features, w->in_features,
+                                      w->out_features, w->n, out, static_cast<cudaStream_t>(stream),
+                                      exl3::window_mask(exl3::flags_window_bits(w->flags)),
+                                      (w->flags & EXL3_WEIGHT_MCG) ? 1 : 0) != cudaSuccess)
+    return refuse(EXL3_FAILED, "exl3_b200: reconstruct launch failed");
+  return kOk;
+}
+
 exl3_verdict exl3_encode_trellis(const float* target, int32_t in_features, int32_t out_features, int32_t n,
                                  uint16_t* trellis, void* stream) {
   if (!target || !trellis) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");

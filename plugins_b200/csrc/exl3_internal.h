@@ -187,6 +187,11 @@ cudaError_t launch_gemv5(const GemvParams& p, int n, int row_groups, bool imma, 
 cudaError_t launch_decode_dense(const uint16_t* trellis, int in_features, int out_features, int n, uint16_t* out,
                                 int imma, cudaStream_t st, uint32_t cw_mask = 0, int mcg = 0);
 
+// the dense effective W (f16 bits, row-major [in][out]) of one group: svh * H (suh * H W_hat), per 128 x 128 block
+cudaError_t launch_reconstruct_public(const uint16_t* trellis, const uint16_t* suh, const uint16_t* svh,
+                                      int in_features, int out_features, int n, uint16_t* out, cudaStream_t st,
+                                      uint32_t cw_mask = 0, int mcg = 0);
+
 // trellis encoder (exl3_encode.cu): target [in][out] f32 (rotated, unit variance) -> trellis [in/16][out/16][n]
 cudaError_t launch_encode(const float* target, int in_features, int out_features, int n, uint16_t* trellis,
                           cudaStream_t st);

@@ -329,6 +329,15 @@ def decode_dense(w: Weight, group: int = 0, dp4a: bool = False, stream=None) -> 
     return out
 
 
+def reconstruct_public(w: Weight, group: int = 0, stream=None) -> torch.Tensor:
+    """The dense effective W (f16, row-major [in, out]; x @ W_eff = the linear's output), built on the GPU
+    (SX/expert_exl3.zig:440-488 reconstructPublic)."""
+    dev = torch.device("cuda", w.device)
+    out = torch.empty((w.in_features, w.out_features), dtype=torch.float16, device=dev)
+    check(L.lib().exl3_reconstruct_public(ctypes.byref(w.raw), group, out.data_ptr(), _stream(stream)))
+    return out
+
+
 def ep_dispatch(x: torch.Tensor, inds: torch.Tensor, experts: int, world: int, send: torch.Tensor,
                 back_slot: torch.Tensor, rank: int = 0, shared: bool = False, stream=None) -> None:
     """Expert-parallel dispatch: x [T, D], inds [T, K] -> send [world, C + 1, D] (x's dtype), back_slot [T, K] i32.

@@ -67,6 +67,36 @@ def test_decode_dense_bit_exact(Q, E, oracle, n, dp4a):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("in_f,out_f,n", [(256, 384, 64), (512, 256, 48), (384, 640, 40), (128, 128, 96)])
+def test_reconstruct_public_against_oracle(Q, E, oracle, in_f, out_f, n):
+    # reconstructPublic (SX/expert_exl3.zig:440-488): the dense effective W.  The oracle sums each Hadamard directly
+    # and the GPU in butterflies, both in f32, so an f16 result may differ by one unit in the last place where the f32
+    # value sits at a rounding boundary; and x @ W_eff is the linear (SX/linear.zig:200-224, the dense twin).
+    tr, suh, svh = _linear(E, in_f, out_f, n, seed=in_f + n)
+    w = Q.weight_from_tensors(tr, suh, svh)
+    got = Q.reconstruct_public(w).view(torch.int16).cpu().numpy().astype(np.int32)
+    want = oracle.reconstruct_public(_np(tr).view(np.uint16), _np(suh).view(np.uint16), _np(svh).view(np.uint16),
+                                     in_f, out_f, n).view(np.int16).astype(np.int32)
+    ulp = np.abs(got - want)
+    assert ulp.max() <= 1 and (ulp == 0).mean() > 0.99, (ulp.max(), (ulp == 0).mean())
+    x = np.random.default_rng(n).standard_normal((3, in_f)).astype(np.float32)
+    dense = x @ torch.from_numpy(got.astype(np.int16)).view(torch.float16).float().numpy()
+    truth = oracle.host_project(x, _np(tr).view(np.uint16), _np(suh).view(np.uint16), _np(svh).view(np.uint16),
+                                in_f, out_f, n, threads=8)
+    assert _rel(dense, truth) < REL_L2_BAR
+
+
+def test_reconstruct_public_group_of_a_bank(Q, E, oracle):
+    groups, in_f, out_f, n = 3, 256, 128, 48
+    tr, suh, svh = E.random_linear(in_f, out_f, n, seed=77, groups=groups)
+    w = Q.weight_from_tensors(tr, suh, svh)
+    for gi in range(groups):
+        got = Q.reconstruct_public(w, gi).view(torch.int16).cpu().numpy().astype(np.int32)
+        want = oracle.reconstruct_public(_np(tr[gi]).view(np.uint16), _np(suh[gi]).view(np.uint16),
+                                         _np(svh[gi]).view(np.uint16), in_f, out_f, n).view(np.int16).astype(np.int32)
+        assert np.abs(got - want).max() <= 1, gi
+
+
 @pytest.mark.parametrize("n", [24, 32, 40, 48])
 @pytest.mark.parametrize("dp4a", [False, True])
 def test_frac_tiles_decode_on_gpu(Q, oracle, n, dp4a):
