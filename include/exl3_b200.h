@@ -186,6 +186,31 @@ exl3_verdict exl3_swiglu(const exl3_weight *gate, const exl3_weight *up, const e
                          const exl3_tensor *x, const exl3_tensor *inds, const exl3_tensor *scores,
                          const exl3_swiglu_opts *opts, void *stream, exl3_tensor *out);
 
+/* The shared expert beside the routed ones (SharedSwiglu, plugins/turboexl3_qwen38/overlay/mlx_serve/abi/
+ * quant.zig:185-199; SX/root.zig:38-68 moeWithShared / moeWithGatedShared, :80-83 moeClampedWithShared). */
+typedef struct exl3_shared_swiglu {
+  uint32_t size;                /* sizeof(exl3_shared_swiglu) */
+  int32_t limit;                /* the routed experts' clamp (exl3_swiglu_opts.limit; 0: none) */
+  /* The shared expert's linears (one group each: gate/up [D -> I_s], down [I_s -> D]); all null when `shared` is
+   * given instead. */
+  const exl3_weight *gate;
+  const exl3_weight *up;
+  const exl3_weight *down;
+  const void *shared;   /* device [B, S, D] in x's dtype: the shared expert's output, already computed */
+  const void *logit;    /* device [B, S] in x's dtype: the shared gate's logit per row, or null */
+  const void *gate_vec; /* device [D] in x's dtype: logit = x . gate_vec (f32 sum, rounded to x's dtype), or null */
+  const void *sigtab;   /* device [65536] in x's dtype: the host's sigmoid of every 16-bit pattern (f16 / bf16
+                         * activations), or null: sigmoid in f32 rounded to x's dtype */
+} exl3_shared_swiglu;
+
+/* swiglu_shared (quant.zig:95 swiglu_shared): the routed experts (exl3_swiglu) plus the shared expert, folded into
+ * the routed output's rounding: out = RN(RN(routed) + g), g = RN(RN(sigmoid(logit)) * shared) with a gate (`logit`
+ * or `gate_vec`), else g = shared (RN: to x's dtype; out in x's dtype).  With the shared expert's linears, shared =
+ * RN(down(silu(gate(x)) * up(x))) is computed first, into `out`, by the same expert kernels. */
+exl3_verdict exl3_swiglu_shared(const exl3_weight *gate, const exl3_weight *up, const exl3_weight *down,
+                                const exl3_tensor *x, const exl3_tensor *inds, const exl3_tensor *scores,
+                                const exl3_shared_swiglu *opts, void *stream, exl3_tensor *out);
+
 /* ------------------------------------------------------------------ library calls beside the seam */
 
 /* matmul with EXL3_MATMUL_* flags (linear_prepared, linear_split inner: quant.zig:57-66). */

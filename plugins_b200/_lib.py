@@ -31,7 +31,7 @@ ERR_WAIT_TIMEOUT, ERR_BAD_SHAPE, ERR_EP_OVERFLOW, ERR_TP_TIMEOUT, ERR_EP_TIMEOUT
 # every symbol include/exl3_b200.h declares
 EXPORTS = (
     "exl3_claims", "exl3_validate", "exl3_bill", "exl3_open", "exl3_close", "exl3_load_tensor", "exl3_load_bank",
-    "exl3_release", "exl3_matmul", "exl3_moe", "exl3_swiglu", "exl3_matmul_ex", "exl3_matmul_timed",
+    "exl3_release", "exl3_matmul", "exl3_moe", "exl3_swiglu", "exl3_swiglu_shared", "exl3_matmul_ex", "exl3_matmul_timed",
     "exl3_ep_dispatch", "exl3_ep_unpack", "exl3_ep_combine", "exl3_epx_create", "exl3_epx_connect",
     "exl3_epx_destroy", "exl3_epx_dispatch", "exl3_epx_receive", "exl3_epx_return", "exl3_epx_combine",
     "exl3_cpx_create", "exl3_cpx_connect", "exl3_cpx_destroy", "exl3_swiglu_cp",
@@ -105,6 +105,13 @@ class Weight(ctypes.Structure):
 
 class SwigluOpts(ctypes.Structure):
     _fields_ = [("size", ctypes.c_uint32), ("limit", ctypes.c_int32), ("verify_rows", ctypes.c_int32)]
+
+
+class SharedSwiglu(ctypes.Structure):
+    """exl3_shared_swiglu: the shared expert's linears (or its output), its gate and the sigmoid table."""
+    _fields_ = [("size", ctypes.c_uint32), ("limit", ctypes.c_int32), ("gate", ctypes.c_void_p),
+                ("up", ctypes.c_void_p), ("down", ctypes.c_void_p), ("shared", ctypes.c_void_p),
+                ("logit", ctypes.c_void_p), ("gate_vec", ctypes.c_void_p), ("sigtab", ctypes.c_void_p)]
 
 
 _lock = threading.Lock()
@@ -214,6 +221,9 @@ def lib() -> ctypes.CDLL:
             L.exl3_swiglu.restype = Verdict
             L.exl3_swiglu.argtypes = [P(Weight), P(Weight), P(Weight), P(Tensor), P(Tensor), P(Tensor),
                                       P(SwigluOpts), ctypes.c_void_p, P(Tensor)]
+            L.exl3_swiglu_shared.restype = Verdict
+            L.exl3_swiglu_shared.argtypes = [P(Weight), P(Weight), P(Weight), P(Tensor), P(Tensor), P(Tensor),
+                                             P(SharedSwiglu), ctypes.c_void_p, P(Tensor)]
             L.exl3_weight_view.restype = Verdict
             L.exl3_weight_view.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                            ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, P(Weight)]

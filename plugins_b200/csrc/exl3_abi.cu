@@ -1011,6 +1011,12 @@ exl3_verdict exl3_swiglu(const exl3_weight* gate, const exl3_weight* up, const e
   return exl3::moe_swiglu(gate, up, down, x, inds, scores, opts, stream, out);
 }
 
+exl3_verdict exl3_swiglu_shared(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down,
+                                const exl3_tensor* x, const exl3_tensor* inds, const exl3_tensor* scores,
+                                const exl3_shared_swiglu* opts, void* stream, exl3_tensor* out) {
+  return exl3::moe_swiglu_shared(gate, up, down, x, inds, scores, opts, stream, out);
+}
+
 exl3_verdict exl3_weight_view(uint16_t* trellis, uint16_t* suh, uint16_t* svh, int32_t groups, int32_t in_features,
                               int32_t out_features, int32_t n, int32_t device, exl3_weight* out) {
   if (!out || !trellis || !suh || !svh) return refuse(EXL3_FAILED, "exl3_b200: bad arguments");

@@ -34,6 +34,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 #include <new>
 
 #include "exl3_common.cuh"
@@ -102,6 +103,12 @@ struct MoeParams {
                        // 0 .. P - 2 the runs of a unit it joins after its first run, P - 1 the warps' totals of the
                        // unit it starts but does not finish
   int32_t* unit_done;  // [2 launches][kMaxSlots * max CB] runs finished per unit (each reset by its unit's last run)
+  // the shared expert folded into the combine (exl3_swiglu_shared): y = RN(RN(routed) + g), g = shared or, gated,
+  // RN(RN(sigmoid(logit)) * shared); RN rounds to x's dtype (y_dtype == x_dtype)
+  const void* shared;       // [rows][hidden] in x's dtype, or null (no fold)
+  const void* sh_logit;     // [rows] in x's dtype, or null
+  const void* sh_gate_vec;  // [hidden] in x's dtype: logit = RN(x . gate_vec), or null
+  const void* sigtab;       // [65536] in x's dtype (16-bit activations), or null: sigmoid in f32, rounded
 };
 
 __device__ __forceinline__ int slot_expert(const MoeParams& p, int slot) {
@@ -507,31 +514,74 @@ __global__ void __launch_bounds__(kWarpsM * 32, 2) moe_gemv_kernel(MoeParams p) 
 
 // ---------------------------------------------------------------- 5. combine
 
+__device__ __forceinline__ float round_act(float v, int32_t dt) {
+  if (dt == kF16) return __half2float(__float2half_rn(v));
+  if (dt == kBF16) return __bfloat162float(__float2bfloat16_rn(v));
+  return v;
+}
+
+__device__ __forceinline__ uint16_t act_bits16(float v, int32_t dt) {
+  return dt == kF16 ? __half_as_ushort(__float2half_rn(v)) : __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+// The shared gate of row `row` as sigmoid(logit) in x's dtype (SX/root.zig:50-68: MLX's sigmoid of the logit's
+// 16-bit pattern where the host gives its table).  With a gate vector every CTA of the row sums x . gate_vec in the
+// same fixed order (each thread a strided run, then the warps in order), so all agree; every thread must call it.
+__device__ float shared_gate(const MoeParams& p, int row, float* s_red) {
+  float logit;
+  if (p.sh_logit) {
+    logit = load_act(p.sh_logit, static_cast<size_t>(row), p.x_dtype);
+  } else {
+    float part = 0.0f;
+    for (int d = static_cast<int>(threadIdx.x); d < p.hidden; d += 128)
+      part += load_act(p.x, static_cast<size_t>(row) * p.hidden + d, p.x_dtype) * load_act(p.sh_gate_vec, d, p.x_dtype);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, o);
+    __syncthreads();  // s_red is free (the previous row's readers are past it)
+    if ((threadIdx.x & 31u) == 0) s_red[threadIdx.x >> 5] = part;
+    __syncthreads();
+    logit = round_act(((s_red[0] + s_red[1]) + s_red[2]) + s_red[3], p.x_dtype);
+  }
+  if (p.sigtab)
+    return load_act(p.sigtab, act_bits16(logit, p.x_dtype), p.x_dtype);
+  return round_act(1.0f / (1.0f + expf(-logit)), p.x_dtype);
+}
+
 // grid: (ceil(hidden/512), up to kCombineRows), 128 threads of four columns each; y[r] = sum_k score[r,k] *
-// dout[pos(r,k)], k in order
+// dout[pos(r,k)], k in order; with a shared expert, y[r] = RN(RN(that sum) + g) (exl3_swiglu_shared)
 __global__ void __launch_bounds__(128) moe_combine_kernel(MoeParams p) {
+  __shared__ float s_red[4];
   pdl_wait();
   pdl_launch_dependents();
   const size_t c = (static_cast<size_t>(blockIdx.x) * 128 + threadIdx.x) * 4;
-  if (c >= static_cast<size_t>(p.hidden_out)) return;  // (a multiple of 128: c + 3 < hidden_out otherwise)
+  const bool live = c < static_cast<size_t>(p.hidden_out);  // (a multiple of 128: c + 3 < hidden_out when live)
+  const bool gated = p.shared && (p.sh_logit || p.sh_gate_vec);
   for (int r = blockIdx.y; r < p.rows; r += gridDim.y) {
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float sig = gated ? shared_gate(p, p.row0 + r, s_red) : 1.0f;
+    if (!live) continue;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int k = 0; k < p.topk; ++k) {
       const int pos = p.pos[r * p.topk + k];
       if (pos >= 0) {
         const float sc = p.scores[static_cast<size_t>(p.row0 + r) * p.topk + k];
         const float4 d = *reinterpret_cast<const float4*>(p.dout + static_cast<size_t>(pos) * p.hidden_out + c);
-        acc.x += sc * d.x;
-        acc.y += sc * d.y;
-        acc.z += sc * d.z;
-        acc.w += sc * d.w;
+        acc[0] += sc * d.x;
+        acc[1] += sc * d.y;
+        acc[2] += sc * d.z;
+        acc[3] += sc * d.w;
       }
     }
     const size_t at = static_cast<size_t>(p.row0 + r) * p.hidden_out + c;
-    store_act(p.y, at, acc.x, p.y_dtype);
-    store_act(p.y, at + 1, acc.y, p.y_dtype);
-    store_act(p.y, at + 2, acc.z, p.y_dtype);
-    store_act(p.y, at + 3, acc.w, p.y_dtype);
+    if (p.shared) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float sh = load_act(p.shared, at + j, p.x_dtype);
+        const float g = gated ? round_act(sig * sh, p.x_dtype) : sh;
+        acc[j] = round_act(acc[j], p.y_dtype) + g;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) store_act(p.y, at + j, acc[j], p.y_dtype);
   }
 }
 
@@ -560,11 +610,15 @@ size_t fixed_bytes(int width, int sms) {
   return (ints + done + part) * 4;
 }
 
+// The routing of a call through one expert (the shared expert's linears as a one-expert bank): kMaxSlots i32 zeros
+// then kMaxSlots f32 ones, at the end of the workspace.
+constexpr size_t kOneExpertBytes = 2 * static_cast<size_t>(kMaxSlots) * 4;
+
 size_t scratch_bytes(int width, int sms) {
   const size_t xs = 2 * static_cast<size_t>(kMaxSlots) * (width / 16) * 256;
   const size_t hs = static_cast<size_t>(kMaxSlots) * (width / 16) * 256;
   const size_t ds = static_cast<size_t>(kMaxSlots) * width * 4;
-  return fixed_bytes(width, sms) + xs + hs + ds + 4 * 256;
+  return fixed_bytes(width, sms) + xs + hs + ds + 4 * 256 + kOneExpertBytes;
 }
 
 exl3_verdict refuse_m(int32_t code, const char* why) { return {code, why}; }
@@ -659,7 +713,12 @@ exl3_verdict moe_reserve(int device, int in_features, int out_features) {
   }
   cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, device);
   const size_t need = scratch_bytes(m, s.sms);
-  const bool ok = cudaMalloc(&s.base, need) == cudaSuccess && cudaMemset(s.base, 0, need) == cudaSuccess;
+  bool ok = cudaMalloc(&s.base, need) == cudaSuccess && cudaMemset(s.base, 0, need) == cudaSuccess;
+  if (ok) {
+    std::vector<float> ones(kMaxSlots, 1.0f);
+    ok = cudaMemcpy(s.base + need - kOneExpertBytes / 2, ones.data(), kOneExpertBytes / 2, cudaMemcpyHostToDevice) ==
+         cudaSuccess;
+  }
   if (prev >= 0) cudaSetDevice(prev);
   if (!ok) {
     s.ready = false;
@@ -672,12 +731,92 @@ exl3_verdict moe_reserve(int device, int in_features, int out_features) {
   return {EXL3_OK, nullptr};
 }
 
+namespace {
+
+// What the combine folds in (exl3_swiglu_shared); all null for a plain routed call.
+struct SharedFold {
+  const void* shared = nullptr;
+  const void* logit = nullptr;
+  const void* gate_vec = nullptr;
+  const void* sigtab = nullptr;
+};
+
+exl3_verdict moe_swiglu_impl(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down,
+                             const exl3_tensor* x, const exl3_tensor* inds, const exl3_tensor* scores, int limit,
+                             const SharedFold& fold, void* stream, exl3_tensor* out);
+
+}  // namespace
+
 exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down, const exl3_tensor* x,
                         const exl3_tensor* inds, const exl3_tensor* scores, const exl3_swiglu_opts* opts, void* stream,
                         exl3_tensor* out) {
-  if (!gate || !up || !down || !x || !inds || !scores || !out) return refuse_m(EXL3_FAILED, "exl3_b200: bad arguments");
   if (opts && opts->size != sizeof(exl3_swiglu_opts)) return refuse_m(EXL3_FAILED, "exl3_b200: bad swiglu options");
-  const int limit = opts ? opts->limit : 0;
+  return moe_swiglu_impl(gate, up, down, x, inds, scores, opts ? opts->limit : 0, SharedFold{}, stream, out);
+}
+
+exl3_verdict moe_swiglu_shared(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down,
+                               const exl3_tensor* x, const exl3_tensor* inds, const exl3_tensor* scores,
+                               const exl3_shared_swiglu* opts, void* stream, exl3_tensor* out) {
+  if (!opts || opts->size != sizeof(exl3_shared_swiglu)) return refuse_m(EXL3_FAILED, "exl3_b200: bad shared-expert options");
+  if (!x || !out || x->ndim != 3 || out->ndim != 3) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Shape (x [B, S, D])");
+  if (out->dtype != x->dtype) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (out is x's dtype)");
+  const bool linears = opts->gate || opts->up || opts->down;
+  if (linears == (opts->shared != nullptr))
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: the shared expert's three linears or its output, one of the two");
+  if (opts->logit && opts->gate_vec) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: the shared gate's logit or its vector, not both");
+  if (opts->sigtab && x->dtype == EXL3_F32)
+    return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Dtype (a sigmoid table is for 16-bit activations)");
+  const int hidden = static_cast<int>(x->shape[2]);
+  const int64_t rows = x->shape[0] * x->shape[1];
+  SharedFold fold;
+  fold.shared = opts->shared ? opts->shared : out->data;
+  fold.logit = opts->logit;
+  fold.gate_vec = opts->gate_vec;
+  fold.sigtab = opts->sigtab;
+  if (linears) {
+    if (!opts->gate || !opts->up || !opts->down) return refuse_m(EXL3_FAILED, "exl3_b200: the shared expert needs gate, up and down");
+    const exl3_weight* sg = opts->gate;
+    if (sg->groups != 1 || opts->up->groups != 1 || opts->down->groups != 1)
+      return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Shape (the shared expert's linears are one group each)");
+    if (sg->in_features != hidden || opts->down->out_features != hidden)
+      return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Shape (the shared expert reads and writes D)");
+    const int dev = sg->device;
+    uint8_t* k1 = nullptr;
+    {
+      std::lock_guard<std::mutex> lk(g_moe_mu);
+      if (dev >= 0 && dev < kMaxDev && g_moe[dev].ready) k1 = g_moe[dev].base + g_moe[dev].bytes - kOneExpertBytes;
+    }
+    if (!k1) return refuse_m(EXL3_FAILED, "exl3_b200: no MoE workspace on the shared expert's device");
+    // the shared expert first, into out (one expert, score 1, kMaxSlots rows a call), then the routed call reads it
+    const size_t es = x->dtype == EXL3_F32 ? 4 : 2;
+    for (int64_t r0 = 0; r0 < rows; r0 += kMaxSlots) {
+      const int64_t rc = rows - r0 < kMaxSlots ? rows - r0 : kMaxSlots;
+      exl3_tensor xc = *x, oc = *out, ic{}, sc{};
+      xc.data = static_cast<uint8_t*>(x->data) + static_cast<size_t>(r0) * hidden * es;
+      oc.data = static_cast<uint8_t*>(out->data) + static_cast<size_t>(r0) * hidden * es;
+      xc.shape[0] = oc.shape[0] = 1;
+      xc.shape[1] = oc.shape[1] = rc;
+      ic.data = k1;
+      ic.dtype = EXL3_I32;
+      sc.data = k1 + kOneExpertBytes / 2;
+      sc.dtype = EXL3_F32;
+      ic.ndim = sc.ndim = 3;
+      ic.shape[0] = sc.shape[0] = 1;
+      ic.shape[1] = sc.shape[1] = rc;
+      ic.shape[2] = sc.shape[2] = 1;
+      exl3_verdict v = moe_swiglu_impl(opts->gate, opts->up, opts->down, &xc, &ic, &sc, 0, SharedFold{}, stream, &oc);
+      if (v.code != EXL3_OK) return v;
+    }
+  }
+  return moe_swiglu_impl(gate, up, down, x, inds, scores, opts->limit, fold, stream, out);
+}
+
+namespace {
+
+exl3_verdict moe_swiglu_impl(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down,
+                             const exl3_tensor* x, const exl3_tensor* inds, const exl3_tensor* scores, int limit,
+                             const SharedFold& fold, void* stream, exl3_tensor* out) {
+  if (!gate || !up || !down || !x || !inds || !scores || !out) return refuse_m(EXL3_FAILED, "exl3_b200: bad arguments");
   if (limit < 0 || limit > 128) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: InvalidExl3Clamp");
   if (x->ndim != 3 || inds->ndim != 3 || scores->ndim != 3 || out->ndim != 3)
     return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: BadExl3Shape (x [B, S, D], inds / scores [B, S, K])");
@@ -729,6 +868,10 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   p.inds = inds->data; p.inds_u32 = inds->dtype == EXL3_U32;
   p.scores = static_cast<const float*>(scores->data);
   p.y = out->data; p.y_dtype = out->dtype; p.topk = topk; p.limit = static_cast<float>(limit);
+  p.shared = fold.shared;
+  p.sh_logit = fold.logit;
+  p.sh_gate_vec = fold.gate_vec;
+  p.sigtab = fold.sigtab;
   int32_t* ints = reinterpret_cast<int32_t*>(sc->base);
   p.order = ints;
   p.chunk_e = ints + kMaxSlots;
@@ -769,6 +912,8 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
   if (err != cudaSuccess) return refuse_m(EXL3_FAILED, "exl3_b200: MoE launch failed");
   return {EXL3_OK, nullptr};
 }
+
+}  // namespace
 
 // ================================================================ column-parallel experts over NVLink peer memory
 //

@@ -273,6 +273,30 @@ def swiglu(gate: Weight, up: Weight, down: Weight, x: torch.Tensor, inds: torch.
     return out
 
 
+def swiglu_shared(gate: Weight, up: Weight, down: Weight, x: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor,
+                  shared_linears: tuple[Weight, Weight, Weight] | None = None, shared: torch.Tensor | None = None,
+                  logit: torch.Tensor | None = None, gate_vec: torch.Tensor | None = None,
+                  sigtab: torch.Tensor | None = None, limit: int = 0, stream=None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """quant.zig:95 swiglu_shared / SX/root.zig:38-68: the routed experts plus the shared expert (its three linears,
+    or its output `shared`), gated by sigmoid(logit) when `logit` [B, S] or `gate_vec` [D] is given:
+    out = RN(RN(routed) + RN(RN(sigmoid(logit)) * shared)), everything in x's dtype."""
+    if out is None:
+        out = torch.empty_like(x)
+    for t in (shared, logit, gate_vec, sigtab):
+        if t is not None and (not t.is_cuda or not t.is_contiguous() or t.dtype != x.dtype):
+            raise Exl3Error(L.EXL3_UNSUPPORTED, "exl3_b200: shared-expert arrays are contiguous, on the GPU, in x's dtype")
+    ptr = (lambda t: t.data_ptr() if t is not None else None)
+    opts = L.SharedSwiglu(ctypes.sizeof(L.SharedSwiglu), int(limit),
+                          *(ctypes.addressof(w.raw) if w is not None else None for w in (shared_linears or (None,) * 3)),
+                          ptr(shared), ptr(logit), ptr(gate_vec), ptr(sigtab))
+    xt, it, st, ot = _tensor(x), _tensor(inds), _tensor(scores), _tensor(out)
+    check(L.lib().exl3_swiglu_shared(ctypes.byref(gate.raw), ctypes.byref(up.raw), ctypes.byref(down.raw),
+                                     ctypes.byref(xt), ctypes.byref(it), ctypes.byref(st), ctypes.byref(opts),
+                                     _stream(stream), ctypes.byref(ot)))
+    return out
+
+
 # ------------------------------------------------------------------ weights already on the device
 
 def weight_from_tensors(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, window: int = 16,

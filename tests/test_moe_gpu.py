@@ -161,3 +161,91 @@ def test_rows_share_a_call_without_changing_bytes(experts, hidden, inter, topk, 
         y = Q.swiglu(wg, wu, wd, x[:, slot:slot + m].contiguous(), ind[:, slot:slot + m].contiguous(),
                      sc[:, slot:slot + m].contiguous())
         assert torch.equal(y.view(torch.int16), full[:, slot:slot + m].view(torch.int16)), (m, slot)
+
+
+def _shared_setup(E, Q, experts, hidden, inter, inter_s, rows, topk, dt, seed):
+    gate = _bank(E, experts, hidden, inter, 48, seed)
+    up = _bank(E, experts, hidden, inter, 48, seed + 1)
+    down = _bank(E, experts, inter, hidden, 48, seed + 2)
+    sh = [E.random_linear(i, o, 64, seed=seed + 3 + j) for j, (i, o) in
+          enumerate(((hidden, inter_s), (hidden, inter_s), (inter_s, hidden)))]
+    banks = [Q.weight_from_tensors(*b) for b in (gate, up, down)]
+    shw = [Q.weight_from_tensors(*b) for b in sh]
+    ind, sc = _route(rows, experts, topk, seed)
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn((1, rows, hidden), generator=g) * 2).to(dt).cuda()
+    return (gate, up, down), sh, banks, shw, ind.view(1, rows, topk).cuda(), sc.view(1, rows, topk).cuda(), x
+
+
+def _sigtab(dt):
+    # the host's table: sigmoid of every 16-bit pattern, in the activations' dtype
+    pats = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(dt)
+    return torch.sigmoid(pats.float()).to(dt).cuda()
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_swiglu_shared_gated_is_the_composition_bit_for_bit(dt):
+    # SX/root.zig:50-68 moeWithGatedShared: bit-identical to the sigmoid, multiply and add it replaces; the shared
+    # expert through its own linears (quant.zig:95 swiglu_shared) is the routed kernels' one-expert call
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    rows, topk, hidden = 5, 4, 256
+    _, _, banks, shw, ind, sc, x = _shared_setup(E, Q, 8, hidden, 384, 256, rows, topk, dt, 40)
+    logit = (torch.randn((1, rows), generator=torch.Generator().manual_seed(3)) * 3).to(dt).cuda()
+    tab = _sigtab(dt)
+    got = Q.swiglu_shared(*banks, x, ind, sc, shared_linears=tuple(shw), logit=logit, sigtab=tab)
+    routed = Q.swiglu(*banks, x, ind, sc)
+    one_i = torch.zeros((1, rows, 1), dtype=torch.int32, device="cuda")
+    one_s = torch.ones((1, rows, 1), dtype=torch.float32, device="cuda")
+    shared = Q.swiglu(*shw, x, one_i, one_s)
+    sig = tab[logit.view(torch.int16).long() & 0xFFFF]
+    want = routed + sig[..., None] * shared
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    # the shared expert's output given instead of its linears: the same bytes
+    got2 = Q.swiglu_shared(*banks, x, ind, sc, shared=shared, logit=logit, sigtab=tab)
+    assert torch.equal(got2.view(torch.int16), want.view(torch.int16))
+    # ungated (moeWithShared, SX/root.zig:38-48): the routed output's rounding, then the add
+    got3 = Q.swiglu_shared(*banks, x, ind, sc, shared=shared)
+    assert torch.equal(got3.view(torch.int16), (routed + shared).view(torch.int16))
+    assert Q.device_error(0) == 0
+
+
+def test_swiglu_shared_against_f32_truth(oracle):
+    # the gate's logit from its vector inside the combine, sigmoid without a table, clamped routed experts, 40 rows
+    # (the routed call's passes take 512 / 6 = 85 rows each), a shared expert wider than the routed ones
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    rows, topk, hidden, inter, inter_s, limit = 40, 6, 384, 256, 512, 7
+    (gate, up, down), sh, banks, shw, ind, sc, x = _shared_setup(E, Q, 16, hidden, inter, inter_s, rows, topk,
+                                                                 torch.float16, 60)
+    gv = (torch.randn(hidden, generator=torch.Generator().manual_seed(9)) * 0.05).half().cuda()
+    got = Q.swiglu_shared(*banks, x, ind, sc, shared_linears=tuple(shw), gate_vec=gv, limit=limit)
+    xf = x.float().cpu().numpy().reshape(rows, hidden)
+    routed = oracle.moe_truth(xf, ind.cpu().numpy().reshape(rows, topk), sc.cpu().numpy().reshape(rows, topk),
+                              (_np16(gate[0]), _np16(gate[1]), _np16(gate[2]), 48),
+                              (_np16(up[0]), _np16(up[1]), _np16(up[2]), 48),
+                              (_np16(down[0]), _np16(down[1]), _np16(down[2]), 48),
+                              hidden, inter, limit=float(limit), threads=8)
+    shared = oracle.moe_truth(xf, np.zeros((rows, 1), np.int32), np.ones((rows, 1), np.float32),
+                              *[(_np16(t[0])[None], _np16(t[1])[None], _np16(t[2])[None], 64) for t in sh],
+                              hidden, inter_s, threads=8)
+    logit = xf @ gv.float().cpu().numpy()
+    want = routed + (1.0 / (1.0 + np.exp(-logit)))[:, None] * shared
+    out = got.float().cpu().numpy().reshape(rows, hidden)
+    err = float(np.sqrt(((out - want) ** 2).sum() / (want ** 2).sum()))
+    assert err < 2 * REL_L2_BAR, err
+    assert Q.device_error(0) == 0
+
+
+def test_swiglu_shared_refuses_by_name():
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    _, _, banks, shw, ind, sc, x = _shared_setup(E, Q, 8, 256, 256, 256, 3, 2, torch.float16, 80)
+    with pytest.raises(Q.Exl3Error, match="one of the two"):
+        Q.swiglu_shared(*banks, x, ind, sc)
+    with pytest.raises(Q.Exl3Error, match="one of the two"):
+        Q.swiglu_shared(*banks, x, ind, sc, shared_linears=tuple(shw), shared=torch.zeros_like(x))
+    logit = torch.zeros((1, 3), dtype=torch.float16, device="cuda")
+    with pytest.raises(Q.Exl3Error, match="not both"):
+        Q.swiglu_shared(*banks, x, ind, sc, shared=torch.zeros_like(x), logit=logit,
+                        gate_vec=torch.zeros(256, dtype=torch.float16, device="cuda"))
