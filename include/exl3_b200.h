@@ -353,6 +353,45 @@ typedef struct exl3_model_config {
 exl3_claim exl3_model_claims(exl3_str model_type, exl3_str config_json);
 exl3_verdict exl3_model_parse(exl3_str config_json, exl3_model_config *out);
 
+/* The model seam's load, bill and forward over the EXL3 linears (ModelTable.bill / load / unload / forward,
+ * plugins/turboexl3_qwen38/plugin.zig:38-53, narrowed to the linears: attention, caches, norms and the drafter are the
+ * host's).  A pack's tensors are named <prefix>.layers.<i>.<module>.{trellis,suh,svh}; a routed bank's members
+ * <bank>.experts.<e>.<proj>.  `names` lists the pack's tensor names (count of them), `source` hands out their data. */
+typedef struct exl3_model exl3_model;
+
+/* bill: the resident bytes of every EXL3 tensor of the pack's layers, as the pack stores them (EXL3 weights stay
+ * resident as stored, plugins/turboexl3_ds41/config.zig:57-61); 0 for a config exl3_model_parse refuses.  Never
+ * touches the GPU. */
+uint64_t exl3_model_bill(exl3_str config_json, const exl3_source *source, const exl3_str *names, int32_t count);
+
+/* load: parses the config (exl3_model_parse) and uploads once every EXL3 linear of every layer under the trunk block
+ * (trunk_quant) and every routed bank under the expert block (expert_quant, else the trunk's); the linears of a layer
+ * that read one input -- <m>.q_proj|k_proj|v_proj and <m>.gate_proj|up_proj -- are also stacked into one launch
+ * (SX/linear.zig:39-72).  The dense MLP's intermediate buffers are reserved here for up to `max_rows` rows, so the
+ * forward calls allocate nothing.  *out receives the model (free it with exl3_model_unload). */
+exl3_verdict exl3_model_load(exl3_str config_json, const exl3_source *source, const exl3_str *names, int32_t count,
+                             int32_t device, int32_t max_rows, void *stream, exl3_model **out);
+void exl3_model_unload(exl3_model *m);
+
+/* The weight of one module (a linear, or a stack named "a|b|c"), borrowed from the model: 1 when found. */
+int32_t exl3_model_weight(const exl3_model *m, int32_t layer, exl3_str module, exl3_weight *out);
+
+/* forward over the linears.  linear: one module, x [..., in] -> out [..., out] in x's dtype.  linears: modules that
+ * read one x, out holding each one's [rows, out] back to back -- one stacked launch where the load stacked them.
+ * mlp: the dense SwiGLU MLP <module>.{gate,up,down}_proj, down(RN(silu(gate x) * up x)), at most max_rows rows.
+ * experts: the routed bank <bank> (exl3_swiglu; x [B, S, D], inds / scores [B, S, K]) plus, when `shared` names a
+ * module with gate/up/down_proj, that shared expert folded in by exl3_swiglu_shared -- gated by `shared_logit`
+ * (device [B, S] in x's dtype) when given. */
+exl3_verdict exl3_model_linear(const exl3_model *m, int32_t layer, exl3_str module, const exl3_tensor *x, void *stream,
+                               exl3_tensor *out);
+exl3_verdict exl3_model_linears(const exl3_model *m, int32_t layer, const exl3_str *modules, int32_t count,
+                                const exl3_tensor *x, void *stream, exl3_tensor *out);
+exl3_verdict exl3_model_mlp(const exl3_model *m, int32_t layer, exl3_str module, const exl3_tensor *x, void *stream,
+                            exl3_tensor *out);
+exl3_verdict exl3_model_experts(const exl3_model *m, int32_t layer, exl3_str bank, exl3_str shared,
+                                const exl3_tensor *x, const exl3_tensor *inds, const exl3_tensor *scores,
+                                const void *shared_logit, void *stream, exl3_tensor *out);
+
 /* A borrowed view of device arrays already in the pack layout (the reference's shared handles, plugin.zig:213-218):
  * validates the shapes and creates the device workspace; exl3_release on a view frees nothing. */
 exl3_verdict exl3_weight_view(uint16_t *trellis, uint16_t *suh, uint16_t *svh, int32_t groups, int32_t in_features,

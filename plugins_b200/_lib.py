@@ -38,7 +38,8 @@ EXPORTS = (
     "exl3_tp_create", "exl3_tp_connect", "exl3_tp_destroy", "exl3_tp_begin", "exl3_matmul_tp", "exl3_tp_gather",
     "exl3_weight_view", "exl3_weight_stack",
     "exl3_decode_dense", "exl3_reconstruct_public", "exl3_encode_trellis", "exl3_matmul_noalloc", "exl3_device_error", "exl3_version",
-    "exl3_model_claims", "exl3_model_parse", "exl3_resident", "exl3_resident_pending",
+    "exl3_model_claims", "exl3_model_parse", "exl3_model_bill", "exl3_model_load", "exl3_model_unload",
+    "exl3_model_weight", "exl3_model_linear", "exl3_model_linears", "exl3_model_mlp", "exl3_model_experts", "exl3_resident", "exl3_resident_pending",
 )
 
 
@@ -221,6 +222,26 @@ def lib() -> ctypes.CDLL:
             L.exl3_swiglu.restype = Verdict
             L.exl3_swiglu.argtypes = [P(Weight), P(Weight), P(Weight), P(Tensor), P(Tensor), P(Tensor),
                                       P(SwigluOpts), ctypes.c_void_p, P(Tensor)]
+            L.exl3_model_bill.restype = ctypes.c_uint64
+            L.exl3_model_bill.argtypes = [Str, P(Source), ctypes.c_void_p, ctypes.c_int32]
+            L.exl3_model_load.restype = Verdict
+            L.exl3_model_load.argtypes = [Str, P(Source), ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, ctypes.c_void_p, P(ctypes.c_void_p)]
+            L.exl3_model_unload.restype = None
+            L.exl3_model_unload.argtypes = [ctypes.c_void_p]
+            L.exl3_model_weight.restype = ctypes.c_int32
+            L.exl3_model_weight.argtypes = [ctypes.c_void_p, ctypes.c_int32, Str, P(Weight)]
+            L.exl3_model_linear.restype = Verdict
+            L.exl3_model_linear.argtypes = [ctypes.c_void_p, ctypes.c_int32, Str, P(Tensor), ctypes.c_void_p,
+                                            P(Tensor)]
+            L.exl3_model_linears.restype = Verdict
+            L.exl3_model_linears.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32,
+                                             P(Tensor), ctypes.c_void_p, P(Tensor)]
+            L.exl3_model_mlp.restype = Verdict
+            L.exl3_model_mlp.argtypes = [ctypes.c_void_p, ctypes.c_int32, Str, P(Tensor), ctypes.c_void_p, P(Tensor)]
+            L.exl3_model_experts.restype = Verdict
+            L.exl3_model_experts.argtypes = [ctypes.c_void_p, ctypes.c_int32, Str, Str, P(Tensor), P(Tensor),
+                                             P(Tensor), ctypes.c_void_p, ctypes.c_void_p, P(Tensor)]
             L.exl3_swiglu_shared.restype = Verdict
             L.exl3_swiglu_shared.argtypes = [P(Weight), P(Weight), P(Weight), P(Tensor), P(Tensor), P(Tensor),
                                              P(SharedSwiglu), ctypes.c_void_p, P(Tensor)]

@@ -48,7 +48,7 @@ template <int N, bool MASKED = false>
 EXL3_HD void lane_windows(const uint32_t* tile_words, const LaneWin<N>& lw, uint32_t (&w)[8]) {
   const uint32_t a = tile_words[lw.o0], b = tile_words[lw.o1], c = tile_words[lw.o2];
   const uint32_t vlo = funnel_r(c, b, lw.sh), vhi = funnel_r(b, a, lw.sh);  // the 64 bits below E
-#if defined(__CUDACC__)
+#if defined(__CUDA_ARCH__)
 #pragma unroll
 #endif
   for (int j = 0; j < 8; ++j) {
@@ -83,14 +83,14 @@ struct ImmaWin {
 // w[0..3]: the first source lane's windows jb, jb + 1, jb + 4, jb + 5; w[4..7] the second's; each masked (src mask).
 template <int N>
 EXL3_HD void imma_windows(const uint32_t* tile_words, const ImmaWin<N>& iw, uint32_t (&w)[8]) {
-#if defined(__CUDACC__)
+#if defined(__CUDA_ARCH__)
 #pragma unroll
 #endif
   for (int i = 0; i < 2; ++i) {
     const LaneWin<N>& lw = iw.src[i];
     const uint32_t a = tile_words[lw.o0], b = tile_words[lw.o1], c = tile_words[lw.o2];
     const uint64_t v = (static_cast<uint64_t>(funnel_r(b, a, lw.sh)) << 32) | funnel_r(c, b, lw.sh);
-#if defined(__CUDACC__)
+#if defined(__CUDA_ARCH__)
 #pragma unroll
 #endif
     for (int k = 0; k < 4; ++k) w[4 * i + k] = static_cast<uint32_t>(v >> iw.sh[i][k]) & lw.mask;

@@ -251,3 +251,129 @@ class ModelLinears:
         self.w.clear()
         self.stacked.clear()
         self.banks.clear()
+
+
+# ------------------------------------------------------------------ the same seam inside the library (C ABI)
+
+def _native_names(source):
+    from . import _lib as L
+    names = [L.Str.of(n) for n in source.names()]
+    arr = (L.Str * max(1, len(names)))(*names)
+    return names, arr
+
+
+def bill_native(config_json: str, source) -> int:
+    """The bill through the library (exl3_model_bill): what a C or Zig host calls; no GPU."""
+    import ctypes
+    from . import _lib as L
+    held = []
+    cb = L.TensorFn(_host_tensor_cb(source, held))
+    src = L.Source(None, cb)
+    keep, arr = _native_names(source)
+    return int(L.lib().exl3_model_bill(L.Str.of(config_json), ctypes.byref(src), arr, len(keep)))
+
+
+def _host_tensor_cb(source, held: list):
+    import numpy as np
+    from .quant import _NP_DT
+
+    def cb(_ctx, name, out) -> int:
+        import ctypes
+        a = source(ctypes.string_at(name.ptr, name.len).decode())
+        if a is None:
+            return 1
+        a = np.ascontiguousarray(a)
+        dt = _NP_DT.get(a.dtype)
+        if dt is None or a.ndim > 4:
+            return 1
+        held.append(a)
+        out.contents.data = a.ctypes.data
+        out.contents.dtype = dt
+        out.contents.ndim = a.ndim
+        for i, s in enumerate(a.shape):
+            out.contents.shape[i] = s
+        return 0
+
+    return cb
+
+
+class NativeModel:
+    """The model seam's load and forward over the linears inside the library (exl3_model_load / _linear / _linears /
+    _mlp / _experts / _unload): the entries a C or Zig host binds in place of the reference's ModelTable
+    (plugins/turboexl3_qwen38/plugin.zig:38-53).  ``source``: the pack (``source(name)`` and ``source.names()``)."""
+
+    def __init__(self, config_json: str, source, device: int | None = None, max_rows: int = 64, stream=None):
+        import ctypes
+        import torch
+        from . import _lib as L
+        from .quant import _stream
+        self.L, self.torch = L, torch
+        self.device = torch.cuda.current_device() if device is None else device
+        held: list = []
+        self._cb = L.TensorFn(_host_tensor_cb(source, held))
+        src = L.Source(None, self._cb)
+        keep, arr = _native_names(source)
+        self.m = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            L.check(L.lib().exl3_model_load(L.Str.of(config_json), ctypes.byref(src), arr, len(keep), self.device,
+                                            int(max_rows), _stream(stream), ctypes.byref(self.m)))
+        held.clear()
+
+    def _out(self, x, width):
+        return self.torch.empty(tuple(x.shape[:-1]) + (width,), dtype=x.dtype, device=x.device)
+
+    def weight(self, layer: int, module: str):
+        import ctypes
+        w = self.L.Weight()
+        if not self.L.lib().exl3_model_weight(self.m, layer, self.L.Str.of(module), ctypes.byref(w)):
+            _refuse(f"MissingLinear {layer}.{module}")
+        return w
+
+    def linear(self, layer: int, module: str, x, stream=None):
+        import ctypes
+        from .quant import _stream, _tensor
+        out = self._out(x, self.weight(layer, module).out_features)
+        self.L.check(self.L.lib().exl3_model_linear(self.m, layer, self.L.Str.of(module), ctypes.byref(_tensor(x)),
+                                                    _stream(stream), ctypes.byref(_tensor(out))))
+        return out
+
+    def linears(self, layer: int, modules, x, stream=None):
+        import ctypes
+        from .quant import _stream, _tensor
+        widths = [self.weight(layer, m).out_features for m in modules]
+        rows = x.numel() // x.shape[-1]
+        flat = self.torch.empty(rows * sum(widths), dtype=x.dtype, device=x.device)
+        mods = (self.L.Str * len(modules))(*[self.L.Str.of(m) for m in modules])
+        self.L.check(self.L.lib().exl3_model_linears(self.m, layer, mods, len(modules), ctypes.byref(_tensor(x)),
+                                                     _stream(stream), ctypes.byref(_tensor(flat))))
+        outs, c0 = [], 0
+        for wd in widths:
+            outs.append(flat[rows * c0: rows * (c0 + wd)].view(tuple(x.shape[:-1]) + (wd,)))
+            c0 += wd
+        return outs
+
+    def mlp(self, layer: int, x, module: str = "mlp", stream=None):
+        import ctypes
+        from .quant import _stream, _tensor
+        out = self._out(x, self.weight(layer, module + ".down_proj").out_features)
+        self.L.check(self.L.lib().exl3_model_mlp(self.m, layer, self.L.Str.of(module), ctypes.byref(_tensor(x)),
+                                                 _stream(stream), ctypes.byref(_tensor(out))))
+        return out
+
+    def experts(self, layer: int, x, inds, scores, bank: str = "mlp", shared: str | None = "mlp.shared_expert",
+                logit=None, stream=None):
+        """x [B, S, D], inds / scores [B, S, K] -> [B, S, D]: the routed bank plus the shared expert (gated by
+        sigmoid(logit) when `logit` [B, S] is given)."""
+        import ctypes
+        from .quant import _stream, _tensor
+        out = self.torch.empty_like(x)
+        self.L.check(self.L.lib().exl3_model_experts(
+            self.m, layer, self.L.Str.of(bank), self.L.Str.of(shared or ""), ctypes.byref(_tensor(x)),
+            ctypes.byref(_tensor(inds)), ctypes.byref(_tensor(scores)),
+            None if logit is None else logit.data_ptr(), _stream(stream), ctypes.byref(_tensor(out))))
+        return out
+
+    def unload(self):
+        if self.m:
+            self.L.lib().exl3_model_unload(self.m)
+            self.m = None

@@ -248,3 +248,81 @@ def test_load_and_forward_over_the_linears_on_the_gpu(tmp_path, oracle):
     assert rel(got, cpu.experts(1, xf, inds, sc)) < 2e-3
     gpu.release()
     pk.close()
+
+
+def test_native_bill_matches_the_stored_bytes(tmp_path):
+    # exl3_model_bill: the bill a C or Zig host calls (no GPU)
+    from plugins_b200 import model as M
+    from plugins_b200 import pack as P
+    t = _write_pack(tmp_path)
+    pk = P.PackSource(str(tmp_path))
+    want = sum(v.nbytes for k, v in t.items() if k.endswith((".trellis", ".suh", ".svh")))
+    assert M.bill_native(pk.config_json, pk) == want == M.bill(M.parse(pk.config_json), pk)
+    assert M.bill_native(json.dumps(_config(trunk_quant={"format": "awq"})), pk) == 0  # a refused pack bills nothing
+    pk.close()
+
+
+def test_native_load_refuses_a_pack_before_any_upload(tmp_path):
+    import ctypes
+    from plugins_b200 import _lib as L
+    from plugins_b200 import model as M
+    from plugins_b200 import pack as P
+    _write_pack(tmp_path)
+    pk = P.PackSource(str(tmp_path))
+    keep, arr = M._native_names(pk)
+    held = []
+    src = L.Source(None, L.TensorFn(M._host_tensor_cb(pk, held)))
+    m = ctypes.c_void_p()
+    v = L.lib().exl3_model_load(L.Str.of(json.dumps(_config(trunk_quant={"format": "exl3", "codebook": "3inst"}))),
+                                ctypes.byref(src), arr, len(keep), 0, 8, None, ctypes.byref(m))
+    assert v.code == L.EXL3_UNSUPPORTED and v.message().endswith("Exl3CodebookUnsupported") and not m
+    v = L.lib().exl3_model_load(L.Str.of(json.dumps(_config())), ctypes.byref(src), arr, len(keep), 0, 0, None,
+                                ctypes.byref(m))
+    assert v.code == L.EXL3_FAILED and not m  # max_rows 0
+    pk.close()
+
+
+@pytest.mark.gpu
+def test_native_model_against_the_mirror_and_the_oracle(tmp_path, oracle):
+    # the library's own load and forward (exl3_model_*) against the Python mirror on the same kernels (bit for bit
+    # where both take the same launches) and against the oracle's f32 truth
+    torch = pytest.importorskip("torch")
+    from plugins_b200 import model as M
+    from plugins_b200 import pack as P
+    t = _write_pack(tmp_path)
+    pk = P.PackSource(str(tmp_path))
+    cfg = M.parse(pk.config_json)
+    nat = M.NativeModel(pk.config_json, pk, max_rows=8)
+    mir = M.ModelLinears(cfg, pk, pk.config_json)
+    cpu = M.ModelLinears(cfg, pk, pk.config_json, ops=OracleModelOps(oracle))
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((3, HIDDEN)).astype(np.float16)
+    xg = torch.from_numpy(x).cuda()
+    xf = x.astype(np.float32)
+
+    def rel(a, b):
+        a = a.float().cpu().numpy() if hasattr(a, "cpu") else a
+        return float(np.sqrt(((a - b) ** 2).sum() / (b ** 2).sum()))
+
+    qkv = ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj")
+    for a, b in zip(nat.linears(0, qkv, xg), mir.linears(0, qkv, xg)):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    for a, b in zip(nat.linears(1, ("self_attn.k_proj", "self_attn.o_proj"), xg),
+                    (mir.linear(1, "self_attn.k_proj", xg), mir.linear(1, "self_attn.o_proj", xg))):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))  # not stacked at load: one launch each
+    assert torch.equal(nat.linear(1, "self_attn.o_proj", xg).view(torch.int16),
+                       mir.linear(1, "self_attn.o_proj", xg).view(torch.int16))
+    assert rel(nat.mlp(0, xg), cpu.mlp(0, xf)) < 4e-3
+    inds = np.array([[0, 3], [2, 1], [1, 0]], dtype=np.int32)
+    sc = rng.random((3, TOPK)).astype(np.float32)
+    y = nat.experts(1, xg.view(1, 3, HIDDEN), torch.from_numpy(inds).cuda().view(1, 3, TOPK),
+                    torch.from_numpy(sc).cuda().view(1, 3, TOPK))
+    assert rel(y.view(3, HIDDEN), cpu.experts(1, xf, inds, sc)) < 4e-3
+    from plugins_b200._lib import Exl3Error
+    with pytest.raises(Exl3Error, match="MissingLinear"):
+        nat.linear(0, "self_attn.nope", xg)
+    with pytest.raises(Exl3Error, match="max_rows"):
+        nat.mlp(0, torch.zeros((9, HIDDEN), dtype=torch.float16, device="cuda"))
+    nat.unload()
+    mir.release()
+    pk.close()
