@@ -414,6 +414,9 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
   return kOk;
 }
 
+// The most rows a cluster-split GEMV launch rotates in each CTA; more take the prepare launch.
+constexpr int kCtaRotateRows = 1;
+
 // Rows from the GEMM threshold on take the tensor-core GEMM; fewer rows take one decode-GEMV launch per group and
 // per 16 rows.
 exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, int64_t rows, void* y, int32_t y_dtype,
@@ -486,6 +489,12 @@ exl3_verdict run_linear(const exl3_weight* w, const void* x, int32_t x_dtype, in
       }
       // the cluster-split GEMV where a split fits (every served width), else the grid-stride one with global partials
       if (gemv_v5 && exl3::gemv5_geometry(gp, w->n, d->sms, rg, split, &why)) {
+        // more than four rows: x is rotated once by a prepare launch instead of by every CTA for its slabs
+        if (imma && rc > kCtaRotateRows && exl3::gemv_prep_bytes(gp, rg) <= d->partial_floats * 4) {
+          if (exl3::launch_gemv_prep(gp, rg, d->partials, st) != cudaSuccess)
+            return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
+          gp.xf = d->partials;
+        }
         if (exl3::launch_gemv5(gp, w->n, rg, imma, st, true) != cudaSuccess)
           return refuse(EXL3_FAILED, "exl3_b200: GEMV launch failed");
         continue;
@@ -864,6 +873,11 @@ exl3_verdict exl3_swiglu(const exl3_weight* gate, const exl3_weight* up, const e
                          const exl3_tensor* inds, const exl3_tensor* scores, const exl3_swiglu_opts* opts, void* stream,
                          exl3_tensor* out) {
   return exl3::moe_swiglu(gate, up, down, x, inds, scores, opts, stream, out);
+}
+
+exl3_verdict exl3_moe_prefill_reserve(int32_t device, int32_t experts, int32_t hidden, int32_t inter, int32_t max_slots,
+                                      uint64_t* bytes) {
+  return exl3::moe_prefill_reserve(device, experts, hidden, inter, max_slots, bytes);
 }
 
 exl3_verdict exl3_swiglu_shared(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down,

@@ -122,45 +122,74 @@ __global__ void __launch_bounds__(kT5, 3) gemv5_kernel(GemvParams p) {
   pdl_wait();
   {
     const int per_row = KR / 8;  // 128-wide input blocks
-    const int jobs = per_row * rows;
+    const int jobs = p.xf ? 0 : per_row * rows;
     __half* xh = reinterpret_cast<__half*>(xps);
-    if (rows % 8 != 0 || RG * 8 != rows) {  // rows that no job writes must read as zero
+    if (p.xf) {
+      // rotated once by the prepare launch (the same arithmetic, so the same bits): this CTA's slabs, rows past the
+      // launch's already zero
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.xf) +
+                                                        (static_cast<size_t>(s) * p.kt + t0) * kSlabX);
+      uint4* dst = reinterpret_cast<uint4*>(xps);
+      const uint32_t n16 = static_cast<uint32_t>(KR) * kSlabX / 16u;
+      for (uint32_t i = tid; i < n16; i += 4 * kT5) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i + u * kT5 < n16) v[u] = __ldcg(src + i + u * kT5);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i + u * kT5 < n16) dst[i + u * kT5] = v[u];
+      }
+    }
+    if (!p.xf && (rows % 8 != 0 || RG * 8 != rows)) {  // rows that no job writes must read as zero
       uint4* z = reinterpret_cast<uint4*>(xps);
       const uint32_t nz = static_cast<uint32_t>(KR) * kSlabX / 16u;
       for (uint32_t i = tid; i < nz; i += kT5) z[i] = make_uint4(0, 0, 0, 0);
       __syncthreads();
     }
-    for (int job = static_cast<int>(warp); job < jobs; job += kW5) {
-      const int h = job / rows, row = job % rows;
-      const int k0 = (t0 + h * 8) * 16;
-      float v[4];
+    // four of the warp's jobs at a time: every job's loads (x, suh) are issued before the first rotation, so their
+    // latency is paid once per four jobs (the same arithmetic per job, so the same bits)
+    constexpr int kJobBatch = 4;
+    for (int base = static_cast<int>(warp); base < jobs; base += kJobBatch * kW5) {
+      float v[kJobBatch][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const size_t k = static_cast<size_t>(k0) + lane + 32 * i;
-        v[i] = load_act(p.x, static_cast<size_t>(p.row0 + row) * p.x_row_stride + k, p.x_dtype);
-      }
-      if (!p.prepared) {
+      for (int u = 0; u < kJobBatch; ++u) {
+        const int job = base + u * kW5;
+        if (job >= jobs) continue;  // (warp-uniform)
+        const int h = job / rows, row = job % rows;
+        const int k0 = (t0 + h * 8) * 16;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          v[i] *= f16_bits_to_float(p.suh[static_cast<size_t>(s) * p.in_features + k0 + lane + 32 * i]);
-        fwht128_warp(v, lane);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] *= kHadScale;
-      }
-      const int rg = row >> 3, g = row & 7;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int kk_all = static_cast<int>(lane) + 32 * i;
-        const int t = h * 8 + (kk_all >> 4), kk = kk_all & 15;
-        int q, e;
-        if (IMMA) {
-          q = kk >> 2;
-          e = kk & 3;
-        } else {
-          q = (kk & 7) >> 1;
-          e = (kk & 1) | ((kk >> 3) << 1);
+        for (int i = 0; i < 4; ++i) {
+          const size_t k = static_cast<size_t>(k0) + lane + 32 * i;
+          v[u][i] = load_act(p.x, static_cast<size_t>(p.row0 + row) * p.x_row_stride + k, p.x_dtype);
+          if (!p.prepared) v[u][i] *= f16_bits_to_float(p.suh[static_cast<size_t>(s) * p.in_features + k]);
         }
-        xh[(static_cast<size_t>(t) * RG + rg) * 128 + (g * 4 + q) * 4 + e] = __float2half_rn(v[i]);
+      }
+#pragma unroll
+      for (int u = 0; u < kJobBatch; ++u) {
+        const int job = base + u * kW5;
+        if (job >= jobs) continue;
+        const int h = job / rows, row = job % rows;
+        if (!p.prepared) {
+          fwht128_warp(v[u], lane);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[u][i] *= kHadScale;
+        }
+        const int rg = row >> 3, g = row & 7;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int kk_all = static_cast<int>(lane) + 32 * i;
+          const int t = h * 8 + (kk_all >> 4), kk = kk_all & 15;
+          int q, e;
+          if (IMMA) {
+            q = kk >> 2;
+            e = kk & 3;
+          } else {
+            q = (kk & 7) >> 1;
+            e = (kk & 1) | ((kk >> 3) << 1);
+          }
+          xh[(static_cast<size_t>(t) * RG + rg) * 128 + (g * 4 + q) * 4 + e] = __float2half_rn(v[u][i]);
+        }
       }
     }
     __syncthreads();

@@ -187,25 +187,37 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
     bool live = true;
     if constexpr (XI) {
       const int b0 = k0 >> 3, nb = ((k1 - 1) >> 3) - b0 + 1;
-      for (int j = static_cast<int>(warp); j < nb * rows; j += kW6) {
-        const int blk = b0 + j / rows, r = j % rows, kb = blk * 128;
-        float v[4];
+      // four of the warp's jobs at a time: their loads are issued before the first rotation (same bits)
+      for (int base = static_cast<int>(warp); base < nb * rows; base += 4 * kW6) {
+        float v[4][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          v[i] = load_act(p.x, static_cast<size_t>(p.row0 + r) * p.x_row_stride + kb + lane + 32 * i, p.x_dtype);
-        if (!p.prepared) {
+        for (int u = 0; u < 4; ++u) {
+          const int j = base + u * kW6;
+          if (j >= nb * rows) continue;  // (warp-uniform)
+          const int blk = b0 + j / rows, r = j % rows, kb = blk * 128;
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            v[i] *= f16_bits_to_float(p.suh[static_cast<size_t>(s) * p.in_features + kb + lane + 32 * i]);
-          fwht128_warp(v, lane);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) v[i] *= kHadScale;
+          for (int i = 0; i < 4; ++i) {
+            v[u][i] = load_act(p.x, static_cast<size_t>(p.row0 + r) * p.x_row_stride + kb + lane + 32 * i, p.x_dtype);
+            if (!p.prepared)
+              v[u][i] *= f16_bits_to_float(p.suh[static_cast<size_t>(s) * p.in_features + kb + lane + 32 * i]);
+          }
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int kin = static_cast<int>(lane) + 32 * i;
-          const int t = (blk - b0) * 8 + (kin >> 4), kk = kin & 15;
-          xbuf[t * 64 + (r * 4 + (kk >> 2)) * 4 + (kk & 3)] = __float2half_rn(v[i]);
+        for (int u = 0; u < 4; ++u) {
+          const int j = base + u * kW6;
+          if (j >= nb * rows) continue;
+          const int blk = b0 + j / rows, r = j % rows;
+          if (!p.prepared) {
+            fwht128_warp(v[u], lane);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[u][i] *= kHadScale;
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int kin = static_cast<int>(lane) + 32 * i;
+            const int t = (blk - b0) * 8 + (kin >> 4), kk = kin & 15;
+            xbuf[t * 64 + (r * 4 + (kk >> 2)) * 4 + (kk & 3)] = __float2half_rn(v[u][i]);
+          }
         }
       }
       __syncthreads();
@@ -371,6 +383,25 @@ size_t gemv6_scratch_bytes(const GemvParams& p, int sms) {
   const size_t xf = static_cast<size_t>(p.nseg) * p.in_features * 32;  // [nseg][in/16][2][128 halfs]
   const size_t parts = static_cast<size_t>(sms) * kVirt6 * 2 * kPart6 * 4;
   return ((xf + 255) & ~size_t{255}) + parts;
+}
+
+size_t gemv_prep_bytes(const GemvParams& p, int row_groups) {
+  return static_cast<size_t>(p.nseg) * (p.in_features / 16) * row_groups * 256;
+}
+
+cudaError_t launch_gemv_prep(const GemvParams& p, int row_groups, void* xf, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.in_features / 128), static_cast<unsigned>(p.nseg));
+  cfg.blockDim = dim3(256 * row_groups);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  __half* dst = static_cast<__half*>(xf);
+  return row_groups == 1 ? cudaLaunchKernelEx(&cfg, gemv6_prep_kernel<1>, p, dst)
+                         : cudaLaunchKernelEx(&cfg, gemv6_prep_kernel<2>, p, dst);
 }
 
 bool gemv6_prefers(const GemvParams& p) {

@@ -133,6 +133,8 @@ struct GemvParams {
   int32_t seg_cb[kMaxSegments + 1];  // segment bounds in 128-column blocks
   int32_t prepared;         // x already holds f16(H(x*suh)/sqrt(128)): no rotation
   int32_t inner_only;       // skip the output Hadamard and svh: y = the f32 inner product
+  const void* xf;           // cluster-split GEMV: x already rotated into fragment order by launch_gemv_prep
+                            //   ([nseg][in/16][row groups][128 halfs]), or null: each CTA rotates its slabs itself
   uint32_t cw_mask;         // a narrowed codeword window's mask (window_mask), 0 for the full 16-bit window
   int32_t mcg;              // the mcg codebook (else mul1)
   // geometry (gemv_geometry)
@@ -174,6 +176,10 @@ cudaError_t launch_gemv(const GemvParams& p, int n, int row_groups, bool imma, c
 constexpr int64_t kGemv6MinSlabs = 49152;
 constexpr int64_t kGemv6MinSlabsDeep = 16384;
 bool gemv6_prefers(const GemvParams& p);
+// x of the launch's rows rotated once into the GEMVs' fragment order (IMMA k order) at xf: [nseg][in/16][row_groups]
+// [128 halfs], rows past the launch's zero; chained to the next launch with programmatic dependent launch.
+size_t gemv_prep_bytes(const GemvParams& p, int row_groups);
+cudaError_t launch_gemv_prep(const GemvParams& p, int row_groups, void* xf, cudaStream_t st);
 size_t gemv6_scratch_bytes(const GemvParams& p, int sms);
 cudaError_t launch_gemv6(const GemvParams& p, int n, int sms, void* scratch, uint32_t* counters, cudaStream_t st);
 
@@ -213,6 +219,17 @@ struct GemmParams {
   int32_t inner_only;    // y = the f32 inner product (no output Hadamard, no svh)
   int32_t vec_store;     // y and y_row_stride allow 16-byte stores
   uint32_t* err;
+  // grouped (the routed experts' prefill, 128-row blocks only): the blocks [mt_range[0], mt_range[1]) of the padded
+  // rows (device words; null: blocks 0 .. tiles_m), block b's expert m_group[b]; expert e's B image at
+  // b_img + (e - group0) * b_group_bytes, its svh at svh + e * svh_group (svh2 + e * svh_group - svh_split for the
+  // columns from svh_split on: a stacked gate|up)
+  const int32_t* mt_range;
+  const int32_t* m_group;
+  int32_t group0;
+  int64_t b_group_bytes;
+  int64_t svh_group;
+  const uint16_t* svh2;
+  int32_t svh_split;
 };
 
 // One launch writes the A image of xp rows [0, mp) (rows >= m are zeros; prepared = x already holds xp; skipped when
@@ -221,6 +238,32 @@ cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, 
                           int prepared, uint8_t* a_img, const uint16_t* trellis, int in_features, int out_features,
                           int col0, int ncols, int n, uint8_t* b_img, cudaStream_t st, uint32_t cw_mask = 0,
                           int mcg = 0);
+// The routed experts' prefill (exl3_moe_prefill.cu): operand images of rows sorted by expert, each expert's rows
+// padded to whole 128-row blocks (row_slot[row] = token * topk + k, -1 for padding; m_group[row / 128] = expert).
+struct MoeImages {
+  const int32_t* row_slot;
+  const int32_t* m_group;
+  const int32_t* rows_total;  // device: the call's padded rows (A images)
+  const int32_t* row_range;   // device: {first row, end row} (the down input's A image)
+  int32_t topk;
+  const void* x;
+  int32_t x_dtype;
+  int64_t x_row_stride;
+  int32_t hidden, inter;
+  const uint16_t *suh_g, *suh_u, *suh_d;  // [E][hidden], [E][hidden], [E][inter]
+  uint8_t *a_g, *a_u, *a_d;               // A images: [rows / 128][hidden / 64] (gate, up), [rows / 128][inter / 64]
+  const float* gu;                         // the gate|up GEMMs' outputs, [rows][gu_stride] f32
+  int64_t gu_stride;
+  float limit;
+};
+cudaError_t launch_moe_a_images(const MoeImages& j, int sms, cudaStream_t st);
+cudaError_t launch_moe_mid_images(const MoeImages& j, int sms, cudaStream_t st);
+// B images (W_hat^T) of the bank's experts e0 .. e0 + count - 1 (experts with counts[e] == 0 skipped), expert e at
+// b_img + (e - e0) * b_group_bytes.
+cudaError_t launch_moe_b_images(const uint16_t* trellis, int in_features, int out_features, int n, int e0, int count,
+                                const int32_t* counts, uint8_t* b_img, int64_t b_group_bytes, cudaStream_t st,
+                                uint32_t cw_mask = 0, int mcg = 0);
+
 // shape: 0 = 128x128 tiles, 1 = 128x256, 2 = 256x128, 3 = 256x256 (rows x columns)
 int gemm_block_m(int shape);
 int gemm_block_n(int shape);
