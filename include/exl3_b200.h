@@ -186,6 +186,17 @@ exl3_verdict exl3_swiglu(const exl3_weight *gate, const exl3_weight *up, const e
                          const exl3_tensor *x, const exl3_tensor *inds, const exl3_tensor *scores,
                          const exl3_swiglu_opts *opts, void *stream, exl3_tensor *out);
 
+/* The routed experts at prompt widths (SX/expert_exl3_kernels.zig:2955-3029 moePrefill, expert-sorted windows through
+ * a GEMM): reserves, on `device`, the workspace with which exl3_swiglu runs calls of 1024 and more (token, k) slots --
+ * up to `max_slots` -- on the tensor cores for banks of up to `experts` experts of hidden -> inter -> hidden: slots
+ * sorted by expert into 128-row blocks, the experts' W_hat^T decoded once per call, grouped tcgen05 GEMMs for gate, up
+ * and down, the SwiGLU between them.  Memory for speed, like exl3_resident: `bytes` (may be null) receives what it
+ * takes (about (max_slots + 127 experts) x (6 hidden + 2 inter) bytes, plus 96 x hidden x inter bytes); max_slots 0
+ * frees it.  Without it, or with verify_rows, or for a shared-expert fold, calls take the decode chain in passes.  Not
+ * to be called while a call on the device runs. */
+exl3_verdict exl3_moe_prefill_reserve(int32_t device, int32_t experts, int32_t hidden, int32_t inter, int32_t max_slots,
+                                      uint64_t *bytes);
+
 /* The shared expert beside the routed ones (SharedSwiglu, plugins/turboexl3_qwen38/overlay/mlx_serve/abi/
  * quant.zig:185-199; SX/root.zig:38-68 moeWithShared / moeWithGatedShared, :80-83 moeClampedWithShared). */
 typedef struct exl3_shared_swiglu {

@@ -31,7 +31,7 @@ ERR_WAIT_TIMEOUT, ERR_BAD_SHAPE, ERR_EP_OVERFLOW, ERR_TP_TIMEOUT, ERR_EP_TIMEOUT
 # every symbol include/exl3_b200.h declares
 EXPORTS = (
     "exl3_claims", "exl3_validate", "exl3_bill", "exl3_open", "exl3_close", "exl3_load_tensor", "exl3_load_bank",
-    "exl3_release", "exl3_matmul", "exl3_moe", "exl3_swiglu", "exl3_swiglu_shared", "exl3_matmul_ex", "exl3_matmul_timed",
+    "exl3_release", "exl3_matmul", "exl3_moe", "exl3_swiglu", "exl3_swiglu_shared", "exl3_moe_prefill_reserve", "exl3_matmul_ex", "exl3_matmul_timed",
     "exl3_ep_dispatch", "exl3_ep_unpack", "exl3_ep_combine", "exl3_epx_create", "exl3_epx_connect",
     "exl3_epx_destroy", "exl3_epx_dispatch", "exl3_epx_receive", "exl3_epx_return", "exl3_epx_combine",
     "exl3_cpx_create", "exl3_cpx_connect", "exl3_cpx_destroy", "exl3_swiglu_cp",
@@ -242,6 +242,9 @@ def lib() -> ctypes.CDLL:
             L.exl3_model_experts.restype = Verdict
             L.exl3_model_experts.argtypes = [ctypes.c_void_p, ctypes.c_int32, Str, Str, P(Tensor), P(Tensor),
                                              P(Tensor), ctypes.c_void_p, ctypes.c_void_p, P(Tensor)]
+            L.exl3_moe_prefill_reserve.restype = Verdict
+            L.exl3_moe_prefill_reserve.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                                   ctypes.c_int32, P(ctypes.c_uint64)]
             L.exl3_swiglu_shared.restype = Verdict
             L.exl3_swiglu_shared.argtypes = [P(Weight), P(Weight), P(Weight), P(Tensor), P(Tensor), P(Tensor),
                                              P(SharedSwiglu), ctypes.c_void_p, P(Tensor)]

@@ -259,6 +259,117 @@ __global__ void __launch_bounds__(256) images_kernel(const ImageJobs j) {
   else if (job < j.decode_jobs + j.prep_jobs) prep_job(j, job - j.decode_jobs, lane);
 }
 
+// ------------------------------------------------------------------ the routed experts' prefill images
+//
+// Rows are the call's (token, k) slots sorted by expert, each expert's rows padded to whole 128-row blocks
+// (row_slot[row] = token * topk + k, or -1 for padding; m_group[row / 128] = the block's expert).  The A images hold
+// the gate- and up-prepared rows (x read once per job, rotated twice), the down input's A image the SwiGLU of the
+// gate|up GEMMs' outputs prepared for down; B images are each expert's decoded W_hat^T, as for a single linear.
+
+// xp = f16-ready H128(v * suh) / sqrt(128) of one warp's 128 inputs (lane t: elements 4t .. 4t + 3), the two low
+// stages in registers, the other five across lanes (prep_job's arithmetic).
+__device__ __forceinline__ void rotate128(float (&v)[4], const uint16_t* suh, uint32_t lane) {
+  const uint2 su = *reinterpret_cast<const uint2*>(suh);
+  const float2 s01 = __half22float2(*reinterpret_cast<const __half2*>(&su.x));
+  const float2 s23 = __half22float2(*reinterpret_cast<const __half2*>(&su.y));
+  v[0] *= s01.x, v[1] *= s01.y, v[2] *= s23.x, v[3] *= s23.y;
+  const float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
+  v[0] = a0 + a2, v[1] = a1 + a3, v[2] = a0 - a2, v[3] = a1 - a3;
+#pragma unroll
+  for (uint32_t bit = 1; bit <= 16; bit <<= 1) {
+    const bool lower = (lane & bit) == 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], bit);
+      v[i] = lower ? v[i] + p : p - v[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] *= kHadScale;
+}
+
+__device__ __forceinline__ void store_image4(uint8_t* img, int kblocks64, int row, int k0, const float (&v)[4]) {
+  const __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
+  uint8_t* blk = img + ((static_cast<size_t>(row) >> 7) * kblocks64 + (k0 >> 6)) * kImgBytes;
+  *reinterpret_cast<uint2*>(blk + image_offset(static_cast<uint32_t>(row) & 127u, static_cast<uint32_t>(k0 & 63))) =
+      make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+}
+
+// One warp per (padded row, 128-input block), grid-stride over the call's rows (a device count).
+__global__ void __launch_bounds__(256) moe_a_images_kernel(const MoeImages j) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const int kblk = j.hidden / 128;
+  const int64_t jobs = static_cast<int64_t>(*j.rows_total) * kblk;
+  for (int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); job < jobs;
+       job += static_cast<int64_t>(gridDim.x) * 8) {
+    const int row = static_cast<int>(job / kblk), b = static_cast<int>(job % kblk);
+    const int k0 = b * 128 + 4 * static_cast<int>(lane);
+    const int slot = j.row_slot[row];
+    float vg[4] = {0.f, 0.f, 0.f, 0.f}, vu[4] = {0.f, 0.f, 0.f, 0.f};
+    if (slot >= 0) {  // (warp-uniform)
+      const size_t at = static_cast<size_t>(slot / j.topk) * j.x_row_stride + k0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) vg[i] = load_act(j.x, at + i, j.x_dtype);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) vu[i] = vg[i];
+      const size_t e = static_cast<size_t>(j.m_group[row >> 7]);
+      rotate128(vg, j.suh_g + e * j.hidden + k0, lane);
+      rotate128(vu, j.suh_u + e * j.hidden + k0, lane);
+    }
+    store_image4(j.a_g, j.hidden / kImgK, row, k0, vg);
+    store_image4(j.a_u, j.hidden / kImgK, row, k0, vu);
+  }
+}
+
+// The down input: h = silu(g) * u of the gate|up GEMMs' f32 outputs (g, u: columns [0, inter) and [inter, 2 inter)
+// of gu), clamped as the routed experts' epilogue clamps, times the down bank's suh, rotated, f16 -- one warp per
+// (row, 128-block) of the rows [row_range[0], row_range[1]).
+__global__ void __launch_bounds__(256) moe_mid_images_kernel(const MoeImages j) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const int kblk = j.inter / 128;
+  const int r0 = j.row_range[0];
+  const int64_t jobs = static_cast<int64_t>(j.row_range[1] - r0) * kblk;
+  for (int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); job < jobs;
+       job += static_cast<int64_t>(gridDim.x) * 8) {
+    const int row = r0 + static_cast<int>(job / kblk), b = static_cast<int>(job % kblk);
+    const int k0 = b * 128 + 4 * static_cast<int>(lane);
+    float h[4] = {0.f, 0.f, 0.f, 0.f};
+    if (j.row_slot[row] >= 0) {
+      const float4 g = *reinterpret_cast<const float4*>(j.gu + static_cast<size_t>(row) * j.gu_stride + k0);
+      const float4 u = *reinterpret_cast<const float4*>(j.gu + static_cast<size_t>(row) * j.gu_stride + j.inter + k0);
+      const float gv[4] = {g.x, g.y, g.z, g.w}, uv0[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float gi = gv[i], ui = uv0[i];
+        if (j.limit > 0.0f) {
+          gi = fminf(gi, j.limit);
+          ui = fminf(fmaxf(ui, -j.limit), j.limit);
+        }
+        const float sig = 1.0f / (1.0f + __expf(-gi));
+        h[i] = gi * sig * ui;
+      }
+      const size_t e = static_cast<size_t>(j.m_group[row >> 7]);
+      rotate128(h, j.suh_d + e * j.inter + k0, lane);
+    }
+    store_image4(j.a_d, j.inter / kImgK, row, k0, h);
+  }
+}
+
+// B images of experts e0 .. e0 + count - 1 (experts without rows skipped): expert e's decode jobs write its W_hat^T
+// blocks at b_img + (e - e0) * b_group_bytes.
+template <int N, int DS>
+__global__ void __launch_bounds__(256) moe_b_images_kernel(ImageJobs j, int e0, int64_t jobs_per, const int32_t* counts,
+                                                           int64_t tr_group, int64_t b_group_bytes) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int e = e0 + static_cast<int>(job / jobs_per);
+  if (job >= j.decode_jobs || counts[e] == 0) return;  // (warp-uniform)
+  ImageJobs je = j;
+  je.trellis = j.trellis + static_cast<size_t>(e) * tr_group;
+  je.b_img = j.b_img + static_cast<size_t>(e - e0) * b_group_bytes;
+  decode_job<N, DS>(je, job % jobs_per, lane);
+}
+
 // ------------------------------------------------------------------ the GEMM
 
 template <int MS, int NS>
@@ -310,7 +421,13 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int tiles = p.tiles_m * p.tiles_n;
+  // grouped: this launch's M blocks come from the device (the routing wrote them); MS is 1 there
+  int mt0 = 0, tiles_m = p.tiles_m;
+  if (p.mt_range) {
+    mt0 = p.mt_range[0];
+    tiles_m = p.mt_range[1] - mt0;
+  }
+  const int tiles = tiles_m * p.tiles_n;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -319,7 +436,8 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
       uint32_t stage = 0, phase = 0, fills = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-        const int mb = t % p.tiles_m, nb = t / p.tiles_m;
+        const int mb = mt0 + t % tiles_m, nb = t / tiles_m;
+        const uint8_t* bimg = p.b_img + (p.m_group ? (p.m_group[mb] - p.group0) * p.b_group_bytes : 0);
         for (int kb = 0; kb < p.kb; ++kb) {
           if (!role_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
             ok = false;
@@ -333,7 +451,7 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
                      kImgBytes, &full[stage], pol_a);
 #pragma unroll
           for (int j = 0; j < NS; ++j)
-            bulk_g2s(dst + (MS + j) * kImgBytes, p.b_img + (static_cast<size_t>(nb * NS + j) * p.kb + kb) * kImgBytes,
+            bulk_g2s(dst + (MS + j) * kImgBytes, bimg + (static_cast<size_t>(nb * NS + j) * p.kb + kb) * kImgBytes,
                      kImgBytes, &full[stage], pol_b);
           ++fills;
           if (++stage == S::kStages) {
@@ -400,7 +518,8 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
       const uint32_t aph = S::kAccBufs == 2 ? ((local >> 1) & 1) : (local & 1);
       if (!role_wait(&accf[ab], aph, abort_flag, p.err)) break;
       tc_fence_after();
-      const int mb = t % p.tiles_m, nb = t / p.tiles_m;
+      const int mb = mt0 + t % tiles_m, nb = t / tiles_m;
+      const int64_t sv_e = p.m_group ? static_cast<int64_t>(p.m_group[mb]) * p.svh_group : 0;
 #pragma unroll 1
       for (int s = 0; s < MS; ++s) {
         const int row = (mb * MS + s) * 128 + static_cast<int>(wq * 32 + lane);
@@ -421,7 +540,9 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
           }
           if (!p.inner_only) {
             fwht128_regs(v);
-            const uint4* sv4 = reinterpret_cast<const uint4*>(p.svh + col0);
+            const uint16_t* svc = p.svh2 && col0 >= p.svh_split ? p.svh2 + sv_e + (col0 - p.svh_split)
+                                                                : p.svh + sv_e + col0;
+            const uint4* sv4 = reinterpret_cast<const uint4*>(svc);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const uint4 u = __ldg(sv4 + j);
@@ -510,13 +631,46 @@ cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, 
   return served ? cudaGetLastError() : cudaErrorInvalidValue;
 }
 
+cudaError_t launch_moe_a_images(const MoeImages& j, int sms, cudaStream_t st) {
+  if (j.hidden % 128 != 0) return cudaErrorInvalidValue;
+  moe_a_images_kernel<<<sms * 8, 256, 0, st>>>(j);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_mid_images(const MoeImages& j, int sms, cudaStream_t st) {
+  if (j.inter % 128 != 0) return cudaErrorInvalidValue;
+  moe_mid_images_kernel<<<sms * 8, 256, 0, st>>>(j);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_b_images(const uint16_t* trellis, int in_features, int out_features, int n, int e0, int count,
+                                const int32_t* counts, uint8_t* b_img, int64_t b_group_bytes, cudaStream_t st,
+                                uint32_t cw_mask, int mcg) {
+  if (in_features % 128 != 0 || out_features % 128 != 0 || !rate_served_n(n) || count < 1) return cudaErrorInvalidValue;
+  ImageJobs j{};
+  j.in_features = in_features;
+  j.cw_mask = spec_mask(cw_mask);
+  j.trellis = trellis, j.out_tiles = out_features / 16, j.tn0 = 0, j.ncol_tiles = out_features / 16;
+  j.b_img = b_img;
+  const int64_t per = static_cast<int64_t>(in_features / 16) * (out_features / 16) / kDecodeTilesPerWarp;
+  j.decode_jobs = per * count;
+  const int64_t tr_group = static_cast<int64_t>(in_features / 16) * (out_features / 16) * n;
+  const dim3 grid(static_cast<unsigned>((j.decode_jobs + 7) / 8)), block(256);
+  const bool served = with_rate_decode(n, cw_mask, mcg != 0, [&](auto N, auto DS) {
+    moe_b_images_kernel<decltype(N)::value, decltype(DS)::value>
+        <<<grid, block, 0, st>>>(j, e0, per, counts, tr_group, b_group_bytes);
+  });
+  return served ? cudaGetLastError() : cudaErrorInvalidValue;
+}
+
 template <int MS, int NS>
 static cudaError_t launch_gemm_t(const GemmParams& p, int sms, cudaStream_t st) {
   using S = GemmShape<MS, NS>;
   if (p.tiles_m * 128 * MS < p.m) return cudaErrorInvalidValue;
+  if ((p.mt_range || p.m_group) && MS != 1) return cudaErrorInvalidValue;
   static KernelSetup setup;
   if (cudaError_t e = kernel_setup(setup, gemm_image_kernel<MS, NS>, 256, S::kSmemBytes); e != cudaSuccess) return e;
-  const int tiles = p.tiles_m * p.tiles_n;
+  const int tiles = p.tiles_m * p.tiles_n;  // (grouped: an upper bound; the kernel reads the launch's blocks)
   const int grid = tiles < sms ? tiles : sms;
   gemm_image_kernel<MS, NS><<<grid, 256, S::kSmemBytes, st>>>(p);
   return cudaGetLastError();

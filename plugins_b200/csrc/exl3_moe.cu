@@ -743,7 +743,7 @@ struct SharedFold {
 
 exl3_verdict moe_swiglu_impl(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down,
                              const exl3_tensor* x, const exl3_tensor* inds, const exl3_tensor* scores, int limit,
-                             const SharedFold& fold, void* stream, exl3_tensor* out);
+                             const SharedFold& fold, void* stream, exl3_tensor* out, bool verify_rows = false);
 
 }  // namespace
 
@@ -751,7 +751,8 @@ exl3_verdict moe_swiglu(const exl3_weight* gate, const exl3_weight* up, const ex
                         const exl3_tensor* inds, const exl3_tensor* scores, const exl3_swiglu_opts* opts, void* stream,
                         exl3_tensor* out) {
   if (opts && opts->size != sizeof(exl3_swiglu_opts)) return refuse_m(EXL3_FAILED, "exl3_b200: bad swiglu options");
-  return moe_swiglu_impl(gate, up, down, x, inds, scores, opts ? opts->limit : 0, SharedFold{}, stream, out);
+  return moe_swiglu_impl(gate, up, down, x, inds, scores, opts ? opts->limit : 0, SharedFold{}, stream, out,
+                         opts && opts->verify_rows);
 }
 
 exl3_verdict moe_swiglu_shared(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down,
@@ -815,7 +816,7 @@ namespace {
 
 exl3_verdict moe_swiglu_impl(const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down,
                              const exl3_tensor* x, const exl3_tensor* inds, const exl3_tensor* scores, int limit,
-                             const SharedFold& fold, void* stream, exl3_tensor* out) {
+                             const SharedFold& fold, void* stream, exl3_tensor* out, bool verify_rows) {
   if (!gate || !up || !down || !x || !inds || !scores || !out) return refuse_m(EXL3_FAILED, "exl3_b200: bad arguments");
   if (limit < 0 || limit > 128) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: InvalidExl3Clamp");
   if (x->ndim != 3 || inds->ndim != 3 || scores->ndim != 3 || out->ndim != 3)
@@ -847,6 +848,10 @@ exl3_verdict moe_swiglu_impl(const exl3_weight* gate, const exl3_weight* up, con
   if (gate->device != up->device || gate->device != down->device) return refuse_m(EXL3_UNSUPPORTED, "exl3_b200: banks on different devices");
   if (rows == 0) return {EXL3_OK, nullptr};
   const int dev = gate->device;
+  // prompt widths: the tensor-core path where a prefill workspace serves the banks (the decode chain with verify_rows)
+  if (!verify_rows && !fold.shared && rows * topk >= kPrefillMinSlots && out->dtype == x->dtype &&
+      moe_prefill_serves(dev, experts, hidden, inter, rows * topk))
+    return moe_prefill_run(gate, up, down, x, inds, scores, static_cast<float>(limit), stream, out);
   MoeScratch* sc = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_moe_mu);

@@ -2,6 +2,7 @@
 profiles of the grouped expert GEMV.
 
     python -m plugins_b200.profile_moe EXPERTS TOKENS TOPK [--hidden 4096] [--inter 2048] [--n 48] [--ep-share WORLD]
+                                   [--prefill]
 
 Random-trellis banks (seeded) of EXPERTS experts, TOKENS rows routed top-TOPK by softmax of seeded logits.  With
 --ep-share WORLD the call is instead one rank's share of an expert-parallel step over WORLD ranks: the receive layout
@@ -30,6 +31,8 @@ def main() -> None:
     ap.add_argument("--n", type=int, default=48, help="halfwords per tile (16 x bits per weight)")
     ap.add_argument("--ep-share", type=int, default=0, metavar="WORLD")
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--prefill", action="store_true",
+                    help="reserve the prefill workspace (calls of 1024+ slots then run on the tensor cores)")
     a = ap.parse_args()
     h, m, n = a.hidden, a.inter, a.n
     g = torch.Generator(device="cuda").manual_seed(4)
@@ -66,6 +69,8 @@ def main() -> None:
         distinct = int(torch.unique(ii).numel())
     banks = [Q.weight_from_tensors(*E.random_linear(i, o, n, seed=7 + k, groups=bank_e))
              for k, (i, o) in enumerate(((h, m), (h, m), (m, h)))]
+    if a.prefill:
+        Q.moe_prefill_reserve(bank_e, h, m, x.shape[1] * ii.shape[2])
     for _ in range(3):
         Q.swiglu(*banks, x, ii, sc, out=y)
     torch.cuda.synchronize()
@@ -86,8 +91,10 @@ def main() -> None:
     torch.cuda.synchronize()
     us = ev[0].elapsed_time(ev[1]) * 1000 / (4 * a.reps)
     nbytes = distinct * 3 * h * m * n // 128
+    flops = 2.0 * 3 * h * m * int((ii >= 0).sum().item())
     print(f"{'ep-share ' + str(a.ep_share) if a.ep_share else 'call'} experts {a.experts} tokens {a.tokens} "
-          f"top-{a.topk}: {us:.1f} us, {distinct} distinct experts, {nbytes / us / 1e3:.1f} GB/s", flush=True)
+          f"top-{a.topk}: {us:.1f} us, {distinct} distinct experts, {nbytes / us / 1e3:.1f} GB/s, "
+          f"{flops / us / 1e6:.1f} TFLOP/s", flush=True)
 
 
 if __name__ == "__main__":

@@ -273,6 +273,15 @@ def swiglu(gate: Weight, up: Weight, down: Weight, x: torch.Tensor, inds: torch.
     return out
 
 
+def moe_prefill_reserve(experts: int, hidden: int, inter: int, max_slots: int, device: int | None = None) -> int:
+    """Reserves the workspace with which swiglu runs prompt-width calls (>= 1024 slots) on the tensor cores; returns its
+    bytes (max_slots 0 frees it)."""
+    b = ctypes.c_uint64(0)
+    dev = torch.cuda.current_device() if device is None else device
+    check(L.lib().exl3_moe_prefill_reserve(dev, int(experts), int(hidden), int(inter), int(max_slots), ctypes.byref(b)))
+    return int(b.value)
+
+
 def swiglu_shared(gate: Weight, up: Weight, down: Weight, x: torch.Tensor, inds: torch.Tensor, scores: torch.Tensor,
                   shared_linears: tuple[Weight, Weight, Weight] | None = None, shared: torch.Tensor | None = None,
                   logit: torch.Tensor | None = None, gate_vec: torch.Tensor | None = None,

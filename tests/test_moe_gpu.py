@@ -249,3 +249,79 @@ def test_swiglu_shared_refuses_by_name():
     with pytest.raises(Q.Exl3Error, match="not both"):
         Q.swiglu_shared(*banks, x, ind, sc, shared=torch.zeros_like(x), logit=logit,
                         gate_vec=torch.zeros(256, dtype=torch.float16, device="cuda"))
+
+
+def _sub_truth(oracle, x, ind, sc, banks, hidden, inter, ns, rows_idx, limit=0.0):
+    """moe_truth of some tokens only (a token's output depends on its own row alone)."""
+    xs = x.float().cpu().numpy().reshape(-1, hidden)[rows_idx]
+    k = ind.shape[-1]
+    return oracle.moe_truth(xs, ind.cpu().numpy().reshape(-1, k)[rows_idx], sc.cpu().numpy().reshape(-1, k)[rows_idx],
+                            *[(_np16(b[0]), _np16(b[1]), _np16(b[2]), n) for b, n in zip(banks, ns)],
+                            hidden, inter, limit=float(limit), threads=8)
+
+
+@pytest.mark.parametrize("experts,hidden,inter,topk,rows,ng,nd,limit,dtype", [
+    (16, 256, 384, 4, 300, 48, 40, 0, "float16"),    # 1200 slots; 384-wide gate/up take 128-column tiles
+    (8, 384, 256, 8, 160, 64, 48, 7, "bfloat16"),    # clamped, every expert with many rows
+])
+def test_moe_prefill_against_truth_and_the_decode_chain(oracle, experts, hidden, inter, topk, rows, ng, nd, limit,
+                                                        dtype):
+    # SX/expert_exl3_kernels.zig:2955-3029 moePrefill: prompt-width calls through expert-sorted GEMMs
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    dt = getattr(torch, dtype)
+    banks = [_bank(E, experts, hidden, inter, ng, 300 + rows), _bank(E, experts, hidden, inter, ng, 301 + rows),
+             _bank(E, experts, inter, hidden, nd, 302 + rows)]
+    wg, wu, wd = (Q.weight_from_tensors(*b) for b in banks)
+    assert Q.moe_prefill_reserve(experts, hidden, inter, rows * topk) > 0
+    try:
+        ind, sc = _route(rows, experts, topk, rows)
+        x = (torch.randn((1, rows, hidden), generator=torch.Generator().manual_seed(rows)) * 2).to(dt).cuda()
+        i3, s3 = ind.view(1, rows, topk).cuda(), sc.view(1, rows, topk).cuda()
+        Q.device_error(0, clear=True)
+        y = Q.swiglu(wg, wu, wd, x, i3, s3, limit=limit)
+        chain = Q.swiglu(wg, wu, wd, x, i3, s3, limit=limit, verify_rows=True)  # the decode chain, in passes
+        torch.cuda.synchronize()
+        assert Q.device_error(0) == 0
+        want = _sub_truth(oracle, x, ind, sc, banks, hidden, inter, (ng, ng, nd), np.arange(rows), limit)
+        got = y.float().cpu().numpy().reshape(rows, hidden)
+        assert np.isfinite(got).all()
+        err = float(np.sqrt(((got - want) ** 2).sum() / (want ** 2).sum()))
+        floor = float(np.sqrt(((torch.from_numpy(want).to(dt).float().numpy() - want) ** 2).sum() / (want ** 2).sum()))
+        assert err < np.sqrt(REL_L2_BAR ** 2 + floor ** 2), (err, floor)
+        c = chain.float().cpu().numpy().reshape(rows, hidden)
+        assert float(np.sqrt(((got - c) ** 2).sum() / (c ** 2).sum())) < 2 * REL_L2_BAR
+        # every row's bytes are its own: a call of the first half of the rows gives the same bytes for them
+        half = rows // 2
+        if half * topk >= 1024:
+            yh = Q.swiglu(wg, wu, wd, x[:, :half].contiguous(), i3[:, :half].contiguous(), s3[:, :half].contiguous(),
+                          limit=limit)
+            assert torch.equal(yh.view(torch.int16), y[:, :half].contiguous().view(torch.int16))
+    finally:
+        Q.moe_prefill_reserve(experts, hidden, inter, 0)
+
+
+def test_moe_prefill_config4_widths_2048_tokens_top8(oracle):
+    # config 4's expert widths (4096 <-> 2048 at 3 bpw) at a 2048-token prompt, top-8 of 64 experts; 24 tokens checked
+    # against the truth on their own rows
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    experts, hidden, inter, topk, rows = 64, 4096, 2048, 8, 2048
+    banks = [_bank(E, experts, hidden, inter, 48, 40), _bank(E, experts, hidden, inter, 48, 41),
+             _bank(E, experts, inter, hidden, 48, 42)]
+    wg, wu, wd = (Q.weight_from_tensors(*b) for b in banks)
+    Q.moe_prefill_reserve(experts, hidden, inter, rows * topk)
+    try:
+        ind, sc = _route(rows, experts, topk, 9)
+        x = torch.randn((1, rows, hidden), generator=torch.Generator().manual_seed(9)).half().cuda()
+        Q.device_error(0, clear=True)
+        y = Q.swiglu(wg, wu, wd, x, ind.view(1, rows, topk).cuda(), sc.view(1, rows, topk).cuda())
+        torch.cuda.synchronize()
+        assert Q.device_error(0) == 0
+        pick = np.random.default_rng(3).choice(rows, 24, replace=False)
+        want = _sub_truth(oracle, x, ind, sc, banks, hidden, inter, (48, 48, 48), pick)
+        got = y.float().cpu().numpy().reshape(rows, hidden)[pick]
+        err = float(np.sqrt(((got - want) ** 2).sum() / (want ** 2).sum()))
+        assert err < 2 * REL_L2_BAR, err
+    finally:
+        Q.moe_prefill_reserve(experts, hidden, inter, 0)
