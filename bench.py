@@ -35,17 +35,21 @@ LINEARS = [("q", HIDDEN, HEADS_Q, 4), ("k", HIDDEN, KV, 4), ("v", HIDDEN, KV, 4)
            ("gate", HIDDEN, INTER, 3), ("up", HIDDEN, INTER, 3), ("down", INTER, HIDDEN, 3)]
 GROUPS = [("qkv", ["q", "k", "v"]), ("o", ["o"]), ("gate_up", ["gate", "up"]), ("down", ["down"])]
 GEMV6_MIN_SLABS, GEMV6_MIN_SLABS_DEEP = 49152, 16384  # the library's kGemv6MinSlabs / kGemv6MinSlabsDeep
+CTA_ROTATE_ROWS = 1  # the library's kCtaRotateRows: more rows take the cluster-split GEMV's prepare launch
 
 
 def gemv_kernels(in_f: int, out_f: int, exchange: bool, rows: int = 1, sms: int = 148) -> int:
     """Kernels one decode-GEMV call launches (the selection in plugins_b200/csrc/exl3_abi.cu and exl3_gemv6.cu): the
     persistent GEMV for large launches -- one kernel when its CTAs rotate the input themselves (1..4 rows, runs of at
-    most 128 slabs), else a prepare launch and the GEMV -- and the cluster-split GEMV otherwise (one launch; always
-    with the column-parallel exchange)."""
+    most 128 slabs), else a prepare launch and the GEMV -- and the cluster-split GEMV otherwise: one launch at one row
+    (its CTAs rotate their slabs' input) and with the column-parallel exchange, a prepare launch and the GEMV from
+    CTA_ROTATE_ROWS + 1 rows."""
     cb, kt = out_f // 128, in_f // 16
     slabs = cb * kt
-    if exchange or not (slabs >= GEMV6_MIN_SLABS or (in_f >= 8192 and slabs >= GEMV6_MIN_SLABS_DEEP)):
+    if exchange:
         return 1
+    if not (slabs >= GEMV6_MIN_SLABS or (in_f >= 8192 and slabs >= GEMV6_MIN_SLABS_DEEP)):
+        return 1 if rows <= CTA_ROTATE_ROWS else 2
     v = sms * 3
     dp = cb // v * v
     run = -(-(cb - dp) * kt // v)
@@ -195,6 +199,26 @@ def measure_prefill(Q, E, torch, peaks: dict, reps: int = 10) -> dict:
                 rec["images_ms"] = round(statistics.median(img), 4)
                 rec["gemm_kernel_ms"] = round(statistics.median(mm), 4)
         out[m] = rec
+    # resident (quant.zig:96-101): the decoded matrix kept from the first prefill call on, so later calls only prepare
+    # the rows (no decode); the same 2048-row call
+    x = torch.randn((2048, in_f), device="cuda", generator=torch.Generator(device="cuda").manual_seed(2048)).to(
+        torch.bfloat16)
+    y = torch.empty((2048, out_f), device="cuda", dtype=torch.bfloat16)
+    kept = Q.resident([w])
+    try:
+        for _ in range(3):
+            Q.matmul_ex(w, x, 16, out=y)
+        tot = []
+        for _ in range(reps):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            for e in ev:
+                e.record()
+            Q.matmul_timed(w, x, ev, flags=16, out=y)
+            torch.cuda.synchronize()
+            tot.append(ev[0].elapsed_time(ev[3]))
+        res_ms = statistics.median(tot)
+    finally:
+        Q.resident([])
     del w
     flops = 2.0 * 2048 * in_f * out_f
     h = out[2048]
@@ -211,6 +235,10 @@ def measure_prefill(Q, E, torch, peaks: dict, reps: int = 10) -> dict:
                      "flops_per_launch": flops,
                      "peak_source": peaks["source"] + " (MEASURED_PEAKS.json bf16_tflops, burst)"},
         "crossover": [{"rows": m, **out[m]} for m in sorted(out)],
+        "resident": {"ms": round(res_ms, 4), "value": round(flops / (res_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                     "kept_bytes": kept,
+                     "note": "exl3_resident: W_hat^T's operand image kept from the first call; later calls prepare "
+                             "only the rows (no decode) before the GEMM"},
         "l2": "no flush: each call writes and reads a 100.7 MB B image and reads 25 MB of trellis (> 126 MB L2)",
     }
 
@@ -242,6 +270,39 @@ def measure_moe(Q, E, torch, peaks: dict, reps: int = 10) -> dict:
             "value": round(gbs, 1), "unit": "GB/s", "ms": round(ms, 4), "distinct_experts": distinct,
             "bytes_per_call": nbytes, "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4),
             "l2": "no flush: a call streams %.2f GB of distinct experts (> 126 MB L2)" % (nbytes / 1e9)}
+
+
+def measure_moe_prefill(Q, E, torch, peaks: dict, tokens: int = 2048, reps: int = 5) -> dict:
+    """Config 4's banks (256 routed + 1 shared expert, 4096 <-> 2048 @ 3 bpw) at a prompt of `tokens` rows, top-8 of a
+    softmax over N(0, 1) router logits plus the shared expert's slot: one swiglu call on the tensor-core prefill path
+    (exl3_moe_prefill_reserve), replayed in a CUDA graph; TFLOP/s of the routed and shared experts' three GEMMs."""
+    experts, hidden, inter, topk = 256, 4096, 2048, 8
+    banks = []
+    for i, (a, b) in enumerate(((hidden, inter), (hidden, inter), (inter, hidden))):
+        tr, suh, svh = E.random_linear(a, b, 48, seed=3 + i, groups=experts + 1)
+        banks.append(Q.weight_from_tensors(tr, suh, svh))
+    g = torch.Generator(device="cuda").manual_seed(4)
+    logits = torch.randn((tokens, experts), device="cuda", generator=g)
+    sc, ind = torch.topk(torch.softmax(logits, -1), topk, -1)
+    ind = torch.cat([ind.to(torch.int32), torch.full((tokens, 1), experts, dtype=torch.int32, device="cuda")], 1)
+    sc = torch.cat([sc.float(), torch.ones((tokens, 1), device="cuda")], 1)
+    ind, sc = ind.view(1, tokens, topk + 1).contiguous(), sc.view(1, tokens, topk + 1).contiguous()
+    x = torch.randn((1, tokens, hidden), device="cuda", dtype=torch.bfloat16, generator=g)
+    y = torch.empty_like(x)
+    ws = Q.moe_prefill_reserve(experts + 1, hidden, inter, tokens * (topk + 1))
+    try:
+        ms = _graph_ms(torch, lambda: Q.swiglu(*banks, x, ind, sc, out=y), reps, inner=1)
+    finally:
+        Q.moe_prefill_reserve(experts + 1, hidden, inter, 0)
+    flops = 2.0 * 3 * hidden * inter * tokens * (topk + 1)
+    tf = flops / (ms * 1e-3) / 1e12
+    del banks
+    return {"workload": f"config 4 banks at a {tokens}-token prompt: 256 routed + 1 shared experts, 4096 <-> 2048 "
+                        "@ 3 bpw, top-8 + the shared slot, bf16",
+            "value": round(tf, 1), "unit": "TFLOP/s", "ms": round(ms, 4), "flops_per_call": flops,
+            "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4), "workspace_bytes": ws,
+            "path": "slots sorted into per-expert 128-row blocks; experts' W_hat^T decoded once per call (32 at a "
+                    "time); grouped tcgen05 GEMMs for gate, up and down; SwiGLU between (exl3_moe_prefill.cu)"}
 
 
 def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict, steps: int = 20) -> dict:
@@ -824,6 +885,7 @@ def main() -> None:
                                             "(W N(0,0.02) seed 0, 36 distinct copies)")
             line["prefill"] = measure_prefill(Q, E, torch, peaks)
             line["moe"] = measure_moe(Q, E, torch, peaks)
+            line["moe_prefill"] = measure_moe_prefill(Q, E, torch, peaks)
             line["large_layer"] = measure_c5(Q, E, torch, peaks)
         if r8 is not None:
             v8 = step_bytes(8) / (r8["ms"] * 1e-3) / 1e9

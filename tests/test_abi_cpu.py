@@ -120,6 +120,10 @@ def test_bench_counts_launches_with_the_librarys_gemv_selection():
         [0, 0, 1, 1]
     assert [b.gemv_kernels(i, o, False, 8) for i, o in ((4096, 24576), (12288, 4096))] == [2, 2]
     assert b.gemv_kernels(4096, 24576, True, 1) == 1  # the column-parallel exchange stays on the cluster split
+    # the cluster split rotates in-CTA at one row, else takes the prepare launch
+    abi = open(os.path.join(root, "plugins_b200", "csrc", "exl3_abi.cu")).read()
+    assert b.CTA_ROTATE_ROWS == val(abi, "kCtaRotateRows")
+    assert [b.gemv_kernels(4096, 6144, False, r) for r in (1, 2, 8)] == [1, 2, 2]
 
 
 def test_exchanges_refuse_bad_shapes_before_touching_the_gpu():
