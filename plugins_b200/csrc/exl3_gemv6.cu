@@ -165,16 +165,23 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
     const uint32_t nk = static_cast<uint32_t>(k1 - k0);
     const uint32_t mine = nk > warp ? (nk - warp + kW6 - 1) / kW6 : 0u;
     const uint8_t* src0 = tr + (static_cast<size_t>(k0 + static_cast<int>(warp)) * OT + static_cast<size_t>(cb) * 8u) * kTileBytes;
-    auto issue = [&](uint32_t i) {
-      if (i >= mine) return;
-      const uint8_t* src = src0 + static_cast<size_t>(kW6) * i * slab_stride;
-      uint8_t* dst = ring + (i % ST) * kUnitBytes;
+    // the ring's next slot and source advance by one unit per issue (no per-unit division or 64-bit multiply)
+    const uint8_t* src_next = src0;
+    const size_t src_step = static_cast<size_t>(kW6) * slab_stride;
+    uint32_t slot_next = 0, issued = 0, slot_use = 0;
+    auto issue = [&]() {
+      if (issued < mine) {
+        uint8_t* dst = ring + slot_next * kUnitBytes;
 #pragma unroll
-      for (uint32_t ch = lane; ch < kUnitBytes / 16u; ch += 32u) cp_async16_6(dst + ch * 16u, src + ch * 16u);
+        for (uint32_t ch = lane; ch < kUnitBytes / 16u; ch += 32u) cp_async16_6(dst + ch * 16u, src_next + ch * 16u);
+        src_next += src_step;
+      }
+      ++issued;
+      slot_next = slot_next + 1u == static_cast<uint32_t>(ST) ? 0u : slot_next + 1u;
     };
 #pragma unroll 1
     for (uint32_t i = 0; i + 1 < static_cast<uint32_t>(ST); ++i) {
-      issue(i);
+      issue();
       cp_async_commit6();
     }
     if (!waited) {  // the prepared x (and, for the stream, nothing else) comes from the prepare launch
@@ -251,7 +258,8 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
         xv[r] = xn[r];
         if (i + 1 < mine) xn[r] = xload(i + 1, r);
       }
-      const uint32_t* tw = reinterpret_cast<const uint32_t*>(ring + (i % ST) * kUnitBytes);
+      const uint32_t* tw = reinterpret_cast<const uint32_t*>(ring + slot_use * kUnitBytes);
+      slot_use = slot_use + 1u == static_cast<uint32_t>(ST) ? 0u : slot_use + 1u;
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
         uint32_t w[8], a[4];
@@ -261,7 +269,7 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
         for (int r = 0; r < RG; ++r) mma_16816(acc[t][r], a, xv[r].x, xv[r].y);
       }
       __syncwarp();
-      issue(i + ST - 1);
+      issue();
       cp_async_commit6();
     }
     cp_async_wait6<0>();
