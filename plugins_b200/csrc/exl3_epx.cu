@@ -7,14 +7,14 @@
 //   done   [2 phases][world] u32                      per rank q: the last step whose dispatch (phase 0) or return
 //                                                     (phase 1) q has published here;
 //   step   u32                                        this rank's step counter;
-//   arrive [2 phases] u32                             CTAs of this rank's dispatch / return that have finished.
+//   arrive [2 phases] u32                             CTAs of this rank's dispatch that have finished (phase 0).
 // A step: exl3_epx_dispatch (the dispatch -- the layout of exl3_ep_dispatch -- writes block `rank` of every peer's
-// recv directly; each CTA then fences its stores at system scope and arrives; the last CTA to arrive advances the step
-// word and releases done[0][rank] = step on every rank), exl3_epx_receive
-// (waits, bounded, until every rank's done[0] holds the step; copies recv into the caller's fixed buffer and unpacks
-// swiglu's indices), the caller's swiglu on that buffer (f32 out), exl3_epx_return (block q of the output straight
-// into rank q's back, block `rank`; the last CTA releases done[1][rank] on every rank), exl3_epx_combine (waits for
-// every rank's done[1], then sum_k score * back[slot] in k order).  Parity = step & 1: a rank dispatches step s + 2
+// recv directly; each CTA arrives; the last CTA to arrive advances the step word), exl3_epx_receive (its first CTA
+// releases done[0][rank] = step on every rank -- one system-scope fence after the dispatch launch completed -- then
+// every CTA waits, bounded, until every rank's done[0] holds the step; copies recv into the caller's fixed buffer and
+// unpacks swiglu's indices), the caller's swiglu on that buffer (f32 out), exl3_epx_return (block q of the output
+// straight into rank q's back, block `rank`; then a one-CTA launch releases done[1][rank] on every rank),
+// exl3_epx_combine (waits for every rank's done[1], then sum_k score * back[slot] in k order).  Parity = step & 1: a rank dispatches step s + 2
 // into a peer only after its step s + 1 combine saw that peer's step s + 1 return, which the peer issued after its
 // step s receive copied recv out, so the two copies of recv and back never race.  The done words only grow; nothing
 // is reset, and graph replays need no host work.  Every wait is bounded (one second): a missing peer sets
@@ -70,28 +70,31 @@ __device__ bool wait_all(const EpxDev& d, int phase, uint32_t step, uint32_t* er
   return s_fail == 0;
 }
 
-// The end of a phase's copies, run by every CTA of the launch: the CTA's stores are fenced at system scope and it
-// arrives; the last CTA to arrive resets the count, stores `step` (dispatch: the step word advances here) and releases
-// done[phase][rank] = step on every rank.
-__device__ void arrive_and_publish(const EpxDev& d, int phase, uint32_t step) {
+// Releases done[phase][rank] = step on every rank: one system-scope fence for every store this rank made before it
+// (the copies of a launch that has completed), then a release store per rank.
+__device__ void publish(const EpxDev& d, int phase, uint32_t step) {
+  asm volatile("fence.sc.sys;" ::: "memory");
+  for (int q = 0; q < d.world; ++q) {
+    uint32_t* f = d.done[q] + phase * d.world + d.rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(step) : "memory");
+  }
+}
+
+// The end of the dispatch's copies, run by every CTA: it arrives; the last CTA to arrive (every CTA has read the
+// step word by then) resets the count and advances the step word.  The release waits for the launch boundary.
+__device__ void arrive_and_advance(const EpxDev& d, uint32_t step) {
   __shared__ int s_last;
-  __syncthreads();  // the CTA's copies are issued
+  __syncthreads();
   if (threadIdx.x == 0) {
-    asm volatile("fence.sc.sys;" ::: "memory");
     const uint32_t total = gridDim.x * gridDim.y;
     uint32_t prior;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prior) : "l"(d.arrive + phase) : "memory");
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prior) : "l"(d.arrive) : "memory");
     s_last = prior == total - 1;
   }
   __syncthreads();
   if (s_last && threadIdx.x == 0) {
-    d.arrive[phase] = 0u;
-    if (phase == 0) *d.step = step;
-    asm volatile("fence.sc.sys;" ::: "memory");
-    for (int q = 0; q < d.world; ++q) {
-      uint32_t* f = d.done[q] + phase * d.world + d.rank;
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(step) : "memory");
-    }
+    d.arrive[0] = 0u;
+    *d.step = step;
   }
 }
 
@@ -170,7 +173,7 @@ __global__ void __launch_bounds__(256) epx_dispatch_kernel(const EpxDev* dp, con
     uint4* out = reinterpret_cast<uint4*>(block + static_cast<size_t>(j) * row_bytes);
     for (size_t w = threadIdx.x; w < words; w += blockDim.x) out[w] = src[w];
   }
-  arrive_and_publish(d, 0, step);
+  arrive_and_advance(d, step);
 }
 
 // After every rank's dispatch: recv (this parity) -> the caller's fixed buffer; CTA (q, 0) also unpacks block q's
@@ -180,6 +183,7 @@ __global__ void __launch_bounds__(256) epx_receive_kernel(const EpxDev* dp, uint
                                                           uint32_t* err) {
   const EpxDev& d = *dp;
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) publish(d, 0, step);  // this rank's dispatch is done
   wait_all(d, 0, step, err);
   const int q = blockIdx.x, cap = d.cap;
   const size_t row_bytes = static_cast<size_t>(d.hidden) * d.esize;
@@ -212,7 +216,12 @@ __global__ void __launch_bounds__(256) epx_return_kernel(const EpxDev* dp, const
   for (size_t w = static_cast<size_t>(blockIdx.y) * blockDim.x + threadIdx.x; w < words;
        w += static_cast<size_t>(gridDim.y) * blockDim.x)
     reinterpret_cast<float4*>(dst)[w] = reinterpret_cast<const float4*>(src)[w];
-  arrive_and_publish(d, 1, step);
+}
+
+// After the return's copies (the previous launch, complete): release them to every rank, once.
+__global__ void epx_publish_return_kernel(const EpxDev* dp) {
+  const EpxDev& d = *dp;
+  if (threadIdx.x == 0) publish(d, 1, *reinterpret_cast<const volatile uint32_t*>(d.step));
 }
 
 // After every rank's return: out[t] = sum_k score * back[slot(t, k)] in k order (f32), this parity.
@@ -387,6 +396,7 @@ exl3_verdict exl3_epx_return(exl3_epx* e, const exl3_tensor* ys, void* stream) {
   DevScope scope(e->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   epx_return_kernel<<<dim3(e->world, 16), 256, 0, st>>>(e->dev, static_cast<const float*>(ys->data));
+  epx_publish_return_kernel<<<1, 32, 0, st>>>(e->dev);
   return cudaGetLastError() == cudaSuccess ? exl3_verdict{EXL3_OK, nullptr}
                                            : refuse(EXL3_FAILED, "exl3_epx_return: launch failed");
 }

@@ -944,7 +944,7 @@ exl3_verdict moe_swiglu_impl(const exl3_weight* gate, const exl3_weight* up, con
 struct CpxDev {
   uint8_t* buf[8];      // every rank's exchange buffer
   uint32_t* step;       // this rank's step word
-  uint32_t* arrive;     // [3] CTAs of this rank's in / - / out launches that have finished
+  uint32_t* arrive;     // [3] (unused: each phase publishes once, from the launch that waits for it)
   int32_t world, rank, tokens, topk, hidden, hidden_out, esize;
   int64_t off_x, off_inds, off_scores, off_hp, off_y, off_done;
 };
@@ -990,25 +990,6 @@ __device__ void cpx_release(const CpxDev& d, int phase, uint32_t step) {
   }
 }
 
-// Every CTA of the launch: its stores fenced at system scope, then it arrives; the last resets the count, (phase 0)
-// advances the step word, and releases done[phase][rank] on every rank.
-__device__ void cpx_arrive_publish(const CpxDev& d, int phase, uint32_t step) {
-  __shared__ int s_last;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    asm volatile("fence.sc.sys;" ::: "memory");
-    uint32_t prior;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prior) : "l"(d.arrive + phase) : "memory");
-    s_last = prior == gridDim.x * gridDim.y - 1;
-  }
-  __syncthreads();
-  if (s_last && threadIdx.x == 0) {
-    d.arrive[phase] = 0u;
-    if (phase == 0) *d.step = step;
-    cpx_release(d, phase, step);
-  }
-}
-
 __device__ void copy16(uint8_t* dst, const uint8_t* src, size_t bytes, size_t t0, size_t stride) {
   for (size_t w = t0; w < bytes / 16; w += stride)
     reinterpret_cast<uint4*>(dst)[w] = reinterpret_cast<const uint4*>(src)[w];
@@ -1018,7 +999,6 @@ __device__ void copy16(uint8_t* dst, const uint8_t* src, size_t bytes, size_t t0
 __global__ void __launch_bounds__(256) cpx_in_kernel(const CpxDev* dp, const uint8_t* __restrict__ x,
                                                      const int32_t* __restrict__ inds, const float* __restrict__ scores) {
   const CpxDev& d = *dp;
-  const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step) + 1u;
   const int q = blockIdx.x;
   const size_t xrow = static_cast<size_t>(d.hidden) * d.esize;
   const size_t t0 = static_cast<size_t>(blockIdx.y) * blockDim.x + threadIdx.x, stride = static_cast<size_t>(gridDim.y) * blockDim.x;
@@ -1030,12 +1010,21 @@ __global__ void __launch_bounds__(256) cpx_in_kernel(const CpxDev* dp, const uin
     qi[i] = inds[i];
     qs[i] = scores[i];
   }
-  cpx_arrive_publish(d, 0, step);
 }
 
-__global__ void cpx_wait_kernel(const CpxDev* dp, int phase, uint32_t* err) {
+// After this rank's copies into every rank (the previous launch, complete): advance the step word, publish phase 0
+// -- one system-scope fence for all of the launch's stores -- and wait (bounded) for every rank's.
+__global__ void cpx_in_publish_kernel(const CpxDev* dp, uint32_t* err) {
   const CpxDev& d = *dp;
-  cpx_wait_all(d, phase, *reinterpret_cast<const volatile uint32_t*>(d.step), err);
+  __shared__ uint32_t s_step;
+  if (threadIdx.x == 0) {
+    const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step) + 1u;
+    *d.step = step;
+    cpx_release(d, 0, step);
+    s_step = step;
+  }
+  __syncthreads();
+  cpx_wait_all(d, 0, s_step, err);
 }
 
 // After this rank's gate|up (the previous launch, complete): publish it, wait for every rank's.
@@ -1049,7 +1038,6 @@ __global__ void cpx_sync_kernel(const CpxDev* dp, uint32_t* err) {
 // grid (world, c): owner q's T rows of ycol [W T][hidden_out] -> its output block, columns [rank hidden_out, ...)
 __global__ void __launch_bounds__(256) cpx_out_kernel(const CpxDev* dp, const uint8_t* __restrict__ ycol) {
   const CpxDev& d = *dp;
-  const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
   const int q = blockIdx.x;
   const size_t seg = static_cast<size_t>(d.hidden_out) * d.esize;  // bytes of one row's column slice
   const size_t words = seg / 16;
@@ -1060,13 +1048,15 @@ __global__ void __launch_bounds__(256) cpx_out_kernel(const CpxDev* dp, const ui
     uint4* dst = reinterpret_cast<uint4*>(d.buf[q] + d.off_y + r * d.hidden * d.esize + d.rank * seg);
     dst[c] = src[c];
   }
-  cpx_arrive_publish(d, 2, step);
 }
 
-// every rank's columns of this rank's rows are in (bounded), then they go to the caller's out
+// After the out copies (the previous launch, complete): CTA 0 publishes phase 2 (one system-scope fence for all of
+// them); every rank's columns of this rank's rows are in (bounded), then they go to the caller's out
 __global__ void __launch_bounds__(256) cpx_final_kernel(const CpxDev* dp, uint8_t* __restrict__ out, uint32_t* err) {
   const CpxDev& d = *dp;
-  cpx_wait_all(d, 2, *reinterpret_cast<const volatile uint32_t*>(d.step), err);
+  const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
+  if (blockIdx.x == 0 && threadIdx.x == 0) cpx_release(d, 2, step);
+  cpx_wait_all(d, 2, step, err);
   const size_t bytes = static_cast<size_t>(d.tokens) * d.hidden * d.esize;
   copy16(out, d.buf[d.rank] + d.off_y, bytes, static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x,
          static_cast<size_t>(gridDim.x) * blockDim.x);
@@ -1268,7 +1258,7 @@ exl3_verdict exl3_swiglu_cp(exl3_cpx* e, const exl3_weight* gate, const exl3_wei
   cpx_in_kernel<<<dim3(W, copy), 256, 0, st>>>(e->dev, static_cast<const uint8_t*>(x->data),
                                                static_cast<const int32_t*>(inds->data),
                                                static_cast<const float*>(scores->data));
-  cpx_wait_kernel<<<1, 32, 0, st>>>(e->dev, 0, err);
+  cpx_in_publish_kernel<<<1, 32, 0, st>>>(e->dev, err);
   cudaError_t er = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
   if (er == cudaSuccess)
     er = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S < kPrepChunks ? S : kPrepChunks), dim3(128), p, st);
