@@ -35,33 +35,41 @@ LINEARS = [("q", HIDDEN, HEADS_Q, 4), ("k", HIDDEN, KV, 4), ("v", HIDDEN, KV, 4)
            ("gate", HIDDEN, INTER, 3), ("up", HIDDEN, INTER, 3), ("down", INTER, HIDDEN, 3)]
 GROUPS = [("qkv", ["q", "k", "v"]), ("o", ["o"]), ("gate_up", ["gate", "up"]), ("down", ["down"])]
 GEMV6_MIN_SLABS, GEMV6_MIN_SLABS_DEEP = 49152, 16384  # the library's kGemv6MinSlabs / kGemv6MinSlabsDeep
+GEMV6_NARROW_CB, GEMV6_NARROW_SLABS = 64, 8192  # the library's kGemv6NarrowCb / kGemv6NarrowSlabs
 CTA_ROTATE_ROWS = 1  # the library's kCtaRotateRows: more rows take the cluster-split GEMV's prepare launch
+XI_TAKE = 1  # the library's kXiTake: more rows take the persistent GEMV's prepare launch
 
 
 def gemv_kernels(in_f: int, out_f: int, exchange: bool, rows: int = 1, sms: int = 148) -> int:
     """Kernels one decode-GEMV call launches (the selection in plugins_b200/csrc/exl3_abi.cu and exl3_gemv6.cu): the
-    persistent GEMV for large launches -- one kernel when its CTAs rotate the input themselves (1..4 rows, runs of at
-    most 128 slabs), else a prepare launch and the GEMV -- and the cluster-split GEMV otherwise: one launch at one row
-    (its CTAs rotate their slabs' input) and with the column-parallel exchange, a prepare launch and the GEMV from
-    CTA_ROTATE_ROWS + 1 rows."""
+    persistent GEMV for large and for narrow launches -- one kernel when its CTAs rotate the input themselves (XI_TAKE
+    rows, runs of at most 128 slabs), else a prepare launch and the GEMV -- and the cluster-split GEMV otherwise: one
+    launch at one row (its CTAs rotate their slabs' input) and with the column-parallel exchange, a prepare launch and
+    the GEMV from CTA_ROTATE_ROWS + 1 rows."""
     cb, kt = out_f // 128, in_f // 16
     slabs = cb * kt
     if exchange:
         return 1
-    if not (slabs >= GEMV6_MIN_SLABS or (in_f >= 8192 and slabs >= GEMV6_MIN_SLABS_DEEP)):
+    if not gemv6_serves(in_f, out_f):
         return 1 if rows <= CTA_ROTATE_ROWS else 2
     v = sms * 3
     dp = cb // v * v
     run = -(-(cb - dp) * kt // v)
     run = (32 if run < 32 else run + 3) & ~3
-    return 1 if rows <= 4 and dp == 0 and run <= 128 else 2
+    return 1 if rows <= XI_TAKE and dp == 0 and run <= 128 else 2
+
+
+def gemv6_serves(in_f: int, out_f: int) -> bool:
+    """The library's gemv6_prefers: the shapes the persistent GEMV takes."""
+    cb, kt = out_f // 128, in_f // 16
+    slabs = cb * kt
+    return (slabs >= GEMV6_MIN_SLABS or (in_f >= 8192 and slabs >= GEMV6_MIN_SLABS_DEEP)
+            or (cb <= GEMV6_NARROW_CB and slabs >= GEMV6_NARROW_SLABS))
 
 
 def gemv6_mode(in_f: int, out_f: int, exchange: bool, rows: int = 1) -> int:
     """0: the cluster-split GEMV; 1: the persistent one rotating its input in-CTA; 2: prepare launch + persistent."""
-    cb, kt = out_f // 128, in_f // 16
-    slabs = cb * kt
-    if exchange or not (slabs >= GEMV6_MIN_SLABS or (in_f >= 8192 and slabs >= GEMV6_MIN_SLABS_DEEP)):
+    if exchange or not gemv6_serves(in_f, out_f):
         return 0
     return gemv_kernels(in_f, out_f, exchange, rows)
 
@@ -340,13 +348,17 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
     all_ind = torch.unique(torch.topk(torch.softmax(logits, -1), topk, -1)[1])
     mine = int(((all_ind >= e0) & (all_ind < e1)).sum().item())
 
-    def timed(exchange):
+    def timed(exchange, trace: bool = False):
+        # trace: a second exchange built with EXL3_TRACE=1 records the kernels' %globaltimer stamps per step
+        if trace:
+            os.environ["EXL3_TRACE"] = "1"
         if exchange == "columns":
             ep = S.ColumnParallelExperts(*cols, experts=experts, tokens=tokens, topk=topk, hidden=hidden, inter=inter,
                                          rank=rank, world=world, device=device, shared=True)
         else:
             ep = S.ExpertParallelSwiglu(*local, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=rank,
                                         world=world, device=device, shared=True, exchange=exchange)
+        os.environ.pop("EXL3_TRACE", None)
         y = torch.empty_like(x)
         st = torch.cuda.Stream(device=device)
         st.wait_stream(torch.cuda.current_stream())
@@ -375,12 +387,13 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         graph.reset()
         closer = ep if exchange == "columns" else ep.peer
+        stamps = closer.trace() if trace else None
         if closer is not None:
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()  # every rank's kernels are done before any exchange region is unmapped
             closer.close()
-        return float(t[0])
+        return (float(t[0]), stamps) if trace else float(t[0])
 
     b = torch.tensor([float((mine + 1) * per_expert)], device=device, dtype=torch.float64)
     if world > 1:
@@ -389,6 +402,12 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
     ms = timed("peer")
     ms_nccl = timed("nccl")
     ms_cols = timed("columns")
+    phases = phases_cols = None
+    if world > 1:
+        _, st_peer = timed("peer", trace=True)
+        _, st_cols = timed("columns", trace=True)
+        phases = phase_table(dist, world, st_peer, EPX_PHASES)
+        phases_cols = phase_table(dist, world, st_cols, CPX_PHASES)
     cp_bytes = (int(all_ind.numel()) + 1) * per_expert  # every distinct expert once, the shared one once
     gbs = nbytes / (ms * 1e-3) / 1e9
     return {"workload": "config 4 expert-parallel: 256 routed (256/N per GPU) + 1 shared expert, 4096 <-> 2048 "
@@ -403,7 +422,36 @@ def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict
                                 "bytes_per_step": int(cp_bytes),
                                 "note": "every rank holds 1/N of every expert's columns and streams 1/N of the "
                                         "distinct experts' bytes; tokens, the down input and the outputs move over "
-                                        "NVLink peer memory inside one call (exl3_swiglu_cp)"}}
+                                        "NVLink peer memory inside one call (exl3_swiglu_cp)"},
+            **({"phases_us": phases, "column_parallel_phases_us": phases_cols} if phases else {})}
+
+
+# the stamps an exchange's kernels record per step (include/exl3_b200.h, exchange timelines) and the phases between
+# them: (name, from stamp, to stamp); "next" is the stretch from a step's last stamp to the next step's first
+EPX_PHASES = [("dispatch_copies", 0, 1), ("wait_peers_dispatch", 1, 2), ("receive_copy", 2, 3), ("swiglu", 3, 4),
+              ("return_copies", 4, 5), ("wait_peers_return", 5, 6), ("combine", 6, 7), ("step", 0, 7)]
+CPX_PHASES = [("token_copies", 0, 1), ("wait_peers_tokens", 1, 2), ("route_prep_gate_up", 2, 3),
+              ("wait_peers_gate_up", 3, 4), ("down_combine", 4, 5), ("out_copies_wait_peers", 5, 6),
+              ("copy_out", 6, 7), ("step", 0, 7)]
+TP_PHASES = [("gemvs", 0, 1), ("wait_peers", 1, 2), ("gather_copy", 2, 3), ("step", 0, 3)]
+
+
+def phase_table(dist, world: int, steps: list, phases: list) -> dict:
+    """Per phase, the median over the traced steps (us) on each rank, then the max and the mean over the ranks; the
+    phase whose max is largest bounds the step, a wait shows how long a rank idled for its slowest peer."""
+    mine = {}
+    for name, a, b in phases:
+        d = [(st[b] - st[a]) / 1e3 for st in steps if st[a] and st[b] and st[b] >= st[a]]
+        mine[name] = statistics.median(d) if d else None
+    every = [None] * world
+    dist.all_gather_object(every, mine)
+    out = {}
+    for name, _, _ in phases:
+        vals = [r[name] for r in every if r[name] is not None]
+        if vals:
+            out[name] = {"max": round(max(vals), 2), "mean": round(sum(vals) / len(vals), 2),
+                         "rank_of_max": max(range(len(every)), key=lambda i: every[i][name] or -1)}
+    return out
 
 
 def measure_c5(Q, E, torch, peaks: dict, reps: int = 5) -> dict:
@@ -422,6 +470,48 @@ def measure_c5(Q, E, torch, peaks: dict, reps: int = 5) -> dict:
                              "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "bytes": nbytes}
         del w, tr
     return {"workload": "config 5: 16384 x 53248 decode GEMV, batch 1", **res}
+
+
+def measure_c5_tp(Q, E, torch, dist, rank: int, world: int, device, peaks: dict, reps: int = 5) -> dict:
+    """Config 5 column-parallel (N > 1): rank r keeps its 128-aligned range of the 53248 output columns
+    (sharding.column_range) of the same seeded layer, and its decode GEMV stores those columns into every rank's
+    exchange over NVLink (exl3_matmul_tp); a call is begin, the GEMV and the gather of the whole y [1, 53248] on every
+    rank, replayed as a CUDA graph and timed as the max over ranks.  Bytes are the whole layer's (every rank streams
+    its share once)."""
+    from plugins_b200 import sharding as S
+    in_f, out_f = 16384, 53248
+    c0, c1 = S.column_range(out_f, rank, world)
+    res = {}
+    for bits in (2, 3, 4, 5):
+        tr, suh, svh = E.random_linear(in_f, out_f, 16 * bits, seed=5, device=device)
+        w = Q.weight_from_tensors(tr[:, c0 // 16:c1 // 16].contiguous(), suh, svh[c0:c1].contiguous())
+        del tr, svh
+        g = torch.Generator(device=device).manual_seed(6)
+        x = torch.randn((1, in_f), device=device, generator=g).half()
+        y = torch.empty(out_f, dtype=torch.float16, device=device)
+        ex = S.TpExchange(rank, world, slots=1, slot_bytes=out_f * 2, max_cb=out_f // 128)
+
+        def call():
+            ex.begin()
+            ex.matmul(w, x, 0, [c0], [out_f])
+            ex.gather(0, 1, y)
+
+        dist.barrier()
+        ms = _graph_ms(torch, call, reps)
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+        torch.cuda.synchronize()
+        dist.barrier()
+        ex.close()
+        nbytes = linear_bytes(in_f, out_f, bits, 1)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[f"{bits}bpw"] = {"ms": round(ms, 4), "value": round(gbs, 1), "unit": "GB/s (whole box)",
+                             "per_gpu": round(gbs / world, 1), "frac_of_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4),
+                             "bytes": nbytes}
+        del w
+    return {"workload": f"config 5 column-parallel over {world} GPUs: 16384 x 53248 decode GEMV, batch 1, each rank "
+                        "1/N of the 128-column blocks, y gathered inside the GEMV over NVLink", **res}
 
 
 # ------------------------------------------------------------------ clocks during the timed region
@@ -653,9 +743,9 @@ def main() -> None:
     def run_config(rows: int, steps: int, warmup: int):
         ins, outs = make_io(rows)
         ex = None
+        from plugins_b200 import sharding as S
         if fused:
             # every launch writes its columns into a slot of every rank's exchange; one gather per step
-            from plugins_b200 import sharding as S
             ex = S.TpExchange(rank, world, slots=LAYERS * len(GROUPS), slot_bytes=rows * 2 * INTER * 2,
                               max_cb=2 * INTER // 128)
             tp_out = torch.empty(LAYERS * len(GROUPS) * ex.slot_bytes, dtype=torch.uint8, device=device)
@@ -796,6 +886,31 @@ def main() -> None:
         dom_ms = time_group("gate_up")
         qkv_ms = time_group("qkv")
         graph.reset()
+        phases = None
+        if ex is not None:
+            # the step's phases: the same step on a second exchange built with EXL3_TRACE=1 (its kernels stamp
+            # %globaltimer per step), replayed apart from the timed runs
+            torch.cuda.synchronize()
+            timed_ex = ex
+            os.environ["EXL3_TRACE"] = "1"
+            ex = S.TpExchange(rank, world, slots=LAYERS * len(GROUPS), slot_bytes=timed_ex.slot_bytes,
+                              max_cb=2 * INTER // 128)
+            os.environ.pop("EXL3_TRACE", None)
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    step()
+            torch.cuda.synchronize()
+            tg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(tg, stream=s):
+                step()
+            for _ in range(20):
+                tg.replay()
+            torch.cuda.synchronize()
+            phases = phase_table(dist, world, ex.trace(), TP_PHASES)
+            tg.reset()
+            dist.barrier()  # no rank unmaps its exchange while another still writes into it
+            ex.close()
+            ex = timed_ex
         if ex is not None:
             torch.cuda.synchronize()
             if world > 1:
@@ -804,11 +919,12 @@ def main() -> None:
         return {"ms": ms, "ms_med": ms_med, "ms_fast": ms_fast, "ms_e2e": ms_e2e, "clk": clk.summary(),
                 "launches": launches_per_step * steps,
                 "h2d": in_buf.numel() * in_buf.element_size(), "d2h": out_buf.numel() * out_buf.element_size(),
-                "dom_ms": dom_ms, "qkv_ms": qkv_ms}
+                "dom_ms": dom_ms, "qkv_ms": qkv_ms, "phases": phases}
 
     peaks = load_peaks()
     r1 = run_config(args.batch, args.steps, args.warmup)
     moe_ep = None if args.no_extras else measure_moe_ep(Q, E, torch, dist, rank, world, device, peaks)
+    c5_tp = None if (args.no_extras or world == 1) else measure_c5_tp(Q, E, torch, dist, rank, world, device, peaks)
     r8 = None if (args.no_batch8 or args.batch == 8) else run_config(8, args.steps, args.warmup)
     total = step_bytes(args.batch)
     value = total / (r1["ms"] * 1e-3) / 1e9
@@ -876,6 +992,10 @@ def main() -> None:
         }
         if moe_ep is not None:
             line["moe_ep"] = moe_ep
+        if c5_tp is not None:
+            line["large_layer_tp"] = c5_tp
+        if r1.get("phases"):
+            line["tp_phases_us"] = r1["phases"]
         if world == 1 and not args.no_extras:
             line["north_star"] = measure_layer(Q, E, torch, peaks, 4096, 12288, 4, 0,
                                                "north-star layer: 4096 x 12288 @ 4 bpw decode GEMV, batch 1 "

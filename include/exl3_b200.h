@@ -346,6 +346,22 @@ exl3_verdict exl3_matmul_tp(const exl3_weight *w, const exl3_tensor *x, exl3_tp 
  * at out + i * slot_bytes.  A step's gathered outputs are readable from its gather on. */
 exl3_verdict exl3_tp_gather(exl3_tp *tp, int32_t slot0, int32_t nslots, void *stream, void *out);
 
+/* ------------------------------------------------------------------ exchange timelines
+ *
+ * An exchange created while EXL3_TRACE=1 is set in the environment records a phase timeline: its kernels write
+ * %globaltimer stamps (ns, this GPU's clock) into a device ring of 8 per step for the last 16 steps.  These calls wait
+ * for the device and copy the ring into out (128 u64, step-major, oldest step first; steps not yet run read 0); an
+ * exchange created without EXL3_TRACE=1 is refused (EXL3_UNSUPPORTED).  Stamps per step --
+ *   tp:  0 begin, 1 publish (this rank's GEMVs of the step done), 2 every rank's columns seen, 3 gathered;
+ *   epx: 0 dispatch begins, 1 its copies done, 2 every rank's dispatch seen, 3 received, 4 return begins (the
+ *        caller's swiglu done), 5 its copies done, 6 every rank's return seen, 7 combined;
+ *   cpx: 0 tokens' copies begin, 1 done, 2 every rank's tokens seen, 3 gate|up done, 4 every rank's gate|up seen,
+ *        5 down and combine done, 6 every rank's columns seen, 7 copied out.
+ * A wait's share (2 - 1, 6 - 5, ...) is the time this rank waited for the slowest peer. */
+exl3_verdict exl3_tp_trace(exl3_tp *tp, uint64_t *out);
+exl3_verdict exl3_epx_trace(exl3_epx *ep, uint64_t *out);
+exl3_verdict exl3_cpx_trace(exl3_cpx *cp, uint64_t *out);
+
 /* ------------------------------------------------------------------ the model seam's parse (linears only)
  *
  * plugins/turboexl3_qwen38/plugin.zig:38-53 ModelTable.claims / parse (config.zig:19-119, src/direct/config.zig:301-420),

@@ -36,6 +36,7 @@ EXPORTS = (
     "exl3_epx_destroy", "exl3_epx_dispatch", "exl3_epx_receive", "exl3_epx_return", "exl3_epx_combine",
     "exl3_cpx_create", "exl3_cpx_connect", "exl3_cpx_destroy", "exl3_swiglu_cp",
     "exl3_tp_create", "exl3_tp_connect", "exl3_tp_destroy", "exl3_tp_begin", "exl3_matmul_tp", "exl3_tp_gather",
+    "exl3_tp_trace", "exl3_epx_trace", "exl3_cpx_trace",
     "exl3_weight_view", "exl3_weight_stack",
     "exl3_decode_dense", "exl3_reconstruct_public", "exl3_encode_trellis", "exl3_matmul_noalloc", "exl3_device_error", "exl3_version",
     "exl3_model_claims", "exl3_model_parse", "exl3_model_bill", "exl3_model_load", "exl3_model_unload",
@@ -176,6 +177,9 @@ def lib() -> ctypes.CDLL:
                                          ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p]
             L.exl3_tp_gather.restype = Verdict
             L.exl3_tp_gather.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+            for name in ("exl3_tp_trace", "exl3_epx_trace", "exl3_cpx_trace"):
+                getattr(L, name).restype = Verdict
+                getattr(L, name).argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]
             L.exl3_ep_dispatch.restype = Verdict
             L.exl3_ep_dispatch.argtypes = [P(Tensor), P(Tensor), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                            ctypes.c_int32, ctypes.c_void_p, P(Tensor), P(Tensor)]

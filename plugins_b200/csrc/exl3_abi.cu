@@ -77,6 +77,35 @@ uint32_t* device_error_ptr() {
   if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
   return static_cast<uint32_t*>(p);
 }
+
+uint64_t* trace_alloc() {
+  const char* e = getenv("EXL3_TRACE");
+  if (!e || strcmp(e, "1") != 0) return nullptr;
+  const size_t bytes = sizeof(uint64_t) * kTraceSteps * kTraceStamps;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+    cudaFree(p);
+    return nullptr;
+  }
+  return static_cast<uint64_t*>(p);
+}
+
+bool trace_copy(const uint64_t* ring, const uint32_t* step_word, uint64_t* out) {
+  if (!ring || !step_word || !out) return false;
+  uint64_t host[kTraceSteps * kTraceStamps];
+  uint32_t step = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&step, step_word, 4, cudaMemcpyDeviceToHost) != cudaSuccess ||
+      cudaMemcpy(host, ring, sizeof host, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return false;
+  for (int i = 0; i < kTraceSteps; ++i) {  // oldest first: steps step - 15 .. step
+    const uint32_t s = step - static_cast<uint32_t>(kTraceSteps - 1 - i);
+    const bool ran = static_cast<int32_t>(step) - (kTraceSteps - 1 - i) >= 1;
+    for (int j = 0; j < kTraceStamps; ++j)
+      out[i * kTraceStamps + j] = ran ? host[(s % kTraceSteps) * kTraceStamps + j] : 0;
+  }
+  return true;
+}
 }
 
 namespace {

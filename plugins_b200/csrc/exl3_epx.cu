@@ -7,7 +7,8 @@
 //   done   [2 phases][world] u32                      per rank q: the last step whose dispatch (phase 0) or return
 //                                                     (phase 1) q has published here;
 //   step   u32                                        this rank's step counter;
-//   arrive [2 phases] u32                             CTAs of this rank's dispatch that have finished (phase 0).
+//   arrive [2 phases] u32                             CTAs of this rank's dispatch that have finished (phase 0);
+//   used   [world] i32                                this step's rows from each source (receive -> return).
 // A step: exl3_epx_dispatch (the dispatch -- the layout of exl3_ep_dispatch -- writes block `rank` of every peer's
 // recv directly; each CTA arrives; the last CTA to arrive advances the step word), exl3_epx_receive (its first CTA
 // releases done[0][rank] = step on every rank -- one system-scope fence after the dispatch launch completed -- then
@@ -39,7 +40,11 @@ struct EpxDev {
   uint32_t* done[kMaxRanks];  // [2][world]
   uint32_t* step;
   uint32_t* arrive;  // [2]
+  int32_t* used;     // [world] this step's rows from each source (the receive writes, the return reads)
   int32_t world, rank, cap, hidden, esize;
+  uint64_t* trace;   // the phase timeline ring, or null: 0 dispatch begins, 1 its copies done, 2 every rank's dispatch
+                     // seen, 3 received, 4 return begins (the caller's swiglu done), 5 its copies done, 6 every
+                     // rank's return seen, 7 combined
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
@@ -95,6 +100,7 @@ __device__ void arrive_and_advance(const EpxDev& d, uint32_t step) {
   if (s_last && threadIdx.x == 0) {
     d.arrive[0] = 0u;
     *d.step = step;
+    exl3::trace_at(d.trace, step, 1);
   }
 }
 
@@ -109,11 +115,14 @@ __global__ void __launch_bounds__(256) epx_dispatch_kernel(const EpxDev* dp, con
                                                            uint32_t* err) {
   __shared__ int s_tok[kMaxCap];
   __shared__ int s_count;
+  exl3::pdl_wait();  // every launch before this one in the stream is complete (programmatic dependent launch)
+  exl3::pdl_launch_dependents();
   const EpxDev& d = *dp;
   const int dst = blockIdx.x, cap = d.cap;
   const bool head = blockIdx.y == 0;
   const int per = experts / d.world;
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step) + 1u;  // this launch's step
+  if (dst == 0 && head && threadIdx.x == 0) exl3::trace_at(d.trace, step, 0);
   const size_t row_bytes = static_cast<size_t>(d.hidden) * d.esize;
   const size_t block_bytes = static_cast<size_t>(cap + 1) * row_bytes;
   uint8_t* block = d.recv[dst] + (static_cast<size_t>(step & 1u) * d.world + d.rank) * block_bytes;
@@ -181,10 +190,13 @@ __global__ void __launch_bounds__(256) epx_dispatch_kernel(const EpxDev* dp, con
 __global__ void __launch_bounds__(256) epx_receive_kernel(const EpxDev* dp, uint8_t* __restrict__ xbuf,
                                                           int32_t* __restrict__ inds, float* __restrict__ scores,
                                                           uint32_t* err) {
+  exl3::pdl_wait();  // the dispatch launch is complete: its stores are performed
+  exl3::pdl_launch_dependents();
   const EpxDev& d = *dp;
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
   if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) publish(d, 0, step);  // this rank's dispatch is done
   wait_all(d, 0, step, err);
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) exl3::trace_at(d.trace, step, 2);
   const int q = blockIdx.x, cap = d.cap;
   const size_t row_bytes = static_cast<size_t>(d.hidden) * d.esize;
   const size_t block_bytes = static_cast<size_t>(cap + 1) * row_bytes;
@@ -198,21 +210,34 @@ __global__ void __launch_bounds__(256) epx_receive_kernel(const EpxDev* dp, uint
       scores[at] = 1.0f;
     }
   }
-  const size_t words = static_cast<size_t>(cap) * row_bytes / 16;  // the token rows (the metadata row stays)
+  // the rows rank q sent are the block's first n (the dispatch compacts them; the rest carry metadata -1): only those
+  // are copied here and returned after swiglu
+  int n = 0;
+  for (int j0 = 0; j0 < cap; j0 += static_cast<int>(blockDim.x)) {
+    const int j = j0 + static_cast<int>(threadIdx.x);
+    n += __syncthreads_count(j < cap && meta[j] >= 0);
+  }
+  if (blockIdx.y == 0 && threadIdx.x == 0) d.used[q] = n;
+  const size_t words = static_cast<size_t>(n) * row_bytes / 16;  // the token rows (the metadata row stays)
   for (size_t w = static_cast<size_t>(blockIdx.y) * blockDim.x + threadIdx.x; w < words;
        w += static_cast<size_t>(gridDim.y) * blockDim.x)
     reinterpret_cast<uint4*>(dst)[w] = reinterpret_cast<const uint4*>(src)[w];
+  __syncthreads();
+  if (threadIdx.x == 0) exl3::trace_last(d.trace, step, 3);
 }
 
 // The swiglu output's block q (rows rank q sent) -> block `rank` of rank q's back (this parity).
 __global__ void __launch_bounds__(256) epx_return_kernel(const EpxDev* dp, const float* __restrict__ ys) {
+  exl3::pdl_wait();
+  exl3::pdl_launch_dependents();
   const EpxDev& d = *dp;
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) exl3::trace_at(d.trace, step, 4);
   const int q = blockIdx.x, cap = d.cap;
   const size_t block_floats = static_cast<size_t>(cap + 1) * d.hidden;
   const float* src = ys + static_cast<size_t>(q) * block_floats;
   float* dst = d.back[q] + (static_cast<size_t>(step & 1u) * d.world + d.rank) * block_floats;
-  const size_t words = static_cast<size_t>(cap) * d.hidden / 4;
+  const size_t words = static_cast<size_t>(d.used[q]) * d.hidden / 4;  // the rows rank q sent this step
   for (size_t w = static_cast<size_t>(blockIdx.y) * blockDim.x + threadIdx.x; w < words;
        w += static_cast<size_t>(gridDim.y) * blockDim.x)
     reinterpret_cast<float4*>(dst)[w] = reinterpret_cast<const float4*>(src)[w];
@@ -220,17 +245,26 @@ __global__ void __launch_bounds__(256) epx_return_kernel(const EpxDev* dp, const
 
 // After the return's copies (the previous launch, complete): release them to every rank, once.
 __global__ void epx_publish_return_kernel(const EpxDev* dp) {
+  exl3::pdl_wait();  // the return launch is complete: its stores are performed
+  exl3::pdl_launch_dependents();
   const EpxDev& d = *dp;
-  if (threadIdx.x == 0) publish(d, 1, *reinterpret_cast<const volatile uint32_t*>(d.step));
+  if (threadIdx.x == 0) {
+    const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
+    exl3::trace_at(d.trace, step, 5);
+    publish(d, 1, step);
+  }
 }
 
 // After every rank's return: out[t] = sum_k score * back[slot(t, k)] in k order (f32), this parity.
 __global__ void __launch_bounds__(128) epx_combine_kernel(const EpxDev* dp, const int32_t* __restrict__ back_slot,
                                                           const float* __restrict__ scores, int topk,
                                                           void* __restrict__ out, int32_t out_dtype, uint32_t* err) {
+  exl3::pdl_wait();
+  exl3::pdl_launch_dependents();
   const EpxDev& d = *dp;
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
   wait_all(d, 1, step, err);
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) exl3::trace_at(d.trace, step, 6);
   const float* back = d.back[d.rank] + static_cast<size_t>(step & 1u) * d.world * (d.cap + 1) * d.hidden;
   const int t = blockIdx.y;
   const size_t c = static_cast<size_t>(blockIdx.x) * 128 + threadIdx.x;
@@ -240,6 +274,8 @@ __global__ void __launch_bounds__(128) epx_combine_kernel(const EpxDev* dp, cons
     if (pos >= 0) acc += scores[static_cast<size_t>(t) * topk + k] * back[static_cast<size_t>(pos) * d.hidden + c];
   }
   exl3::store_act(out, static_cast<size_t>(t) * d.hidden + c, acc, out_dtype);
+  __syncthreads();
+  if (threadIdx.x == 0) exl3::trace_last(d.trace, step, 7);
 }
 
 exl3_verdict refuse(int32_t code, const char* why) { return {code, why}; }
@@ -253,6 +289,7 @@ struct exl3_epx {
   size_t recv_bytes = 0, back_bytes = 0;
   uint8_t* peer[kMaxRanks] = {};
   EpxDev* dev = nullptr;
+  uint64_t* trace = nullptr;  // the phase timeline ring (EXL3_TRACE=1 at create), or null
   bool connected = false;
 };
 
@@ -300,6 +337,7 @@ exl3_verdict exl3_epx_create(int32_t device, int32_t world, int32_t rank, int32_
   }
   memcpy(ipc_handle, &h, 64);
   e->peer[rank] = e->base;
+  e->trace = exl3::trace_alloc();
   *out = e;
   return {EXL3_OK, nullptr};
 }
@@ -324,7 +362,9 @@ exl3_verdict exl3_epx_connect(exl3_epx* e, const uint8_t* ipc_handles) {
   }
   host.step = reinterpret_cast<uint32_t*>(e->base + e->recv_bytes + e->back_bytes + 256);
   host.arrive = host.step + 4;
+  host.used = reinterpret_cast<int32_t*>(host.step + 8);
   host.world = e->world, host.rank = e->rank, host.cap = e->cap, host.hidden = e->hidden, host.esize = e->esize;
+  host.trace = e->trace;
   ok = ok && cudaMalloc(&e->dev, sizeof host) == cudaSuccess &&
        cudaMemcpy(e->dev, &host, sizeof host, cudaMemcpyHostToDevice) == cudaSuccess;
   if (!ok) return refuse(EXL3_FAILED, "exl3_epx_connect: opening a peer's exchange buffer failed");
@@ -340,6 +380,7 @@ void exl3_epx_destroy(exl3_epx* e) {
     if (q != e->rank && e->peer[q]) cudaIpcCloseMemHandle(e->peer[q]);
   if (e->dev) cudaFree(e->dev);
   if (e->base) cudaFree(e->base);
+  if (e->trace) cudaFree(e->trace);
   delete e;
 }
 
@@ -359,11 +400,13 @@ exl3_verdict exl3_epx_dispatch(exl3_epx* e, const exl3_tensor* x, const exl3_ten
   uint32_t* err = exl3::device_error_ptr();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int copy = e->world >= 148 ? 1 : (148 + e->world - 1) / e->world;
-  epx_dispatch_kernel<<<dim3(e->world, copy), 256, 0, st>>>(e->dev, x->data, static_cast<int>(x->shape[0]),
-                                                            static_cast<int>(inds->shape[1]), inds->data,
-                                                            inds->dtype == EXL3_U32, experts, shared ? 1 : 0,
-                                                            static_cast<int32_t*>(back_slot->data), err);
-  return (err && cudaGetLastError() == cudaSuccess) ? exl3_verdict{EXL3_OK, nullptr}
+  const cudaError_t le = exl3::launch_pdl_k(epx_dispatch_kernel, dim3(e->world, copy), dim3(256), st,
+                                            static_cast<const EpxDev*>(e->dev), static_cast<const void*>(x->data),
+                                            static_cast<int>(x->shape[0]), static_cast<int>(inds->shape[1]),
+                                            static_cast<const void*>(inds->data), inds->dtype == EXL3_U32 ? 1 : 0,
+                                            static_cast<int>(experts), shared ? 1 : 0,
+                                            static_cast<int32_t*>(back_slot->data), err);
+  return (err && le == cudaSuccess) ? exl3_verdict{EXL3_OK, nullptr}
                                                     : refuse(EXL3_FAILED, "exl3_epx_dispatch: launch failed");
 }
 
@@ -380,10 +423,11 @@ exl3_verdict exl3_epx_receive(exl3_epx* e, void* stream, exl3_tensor* xbuf, exl3
   if (reinterpret_cast<uintptr_t>(xbuf->data) % 16 != 0) return refuse(EXL3_UNSUPPORTED, "exl3_epx_receive: xbuf on a 16-byte boundary");
   DevScope scope(e->device);
   uint32_t* err = exl3::device_error_ptr();
-  epx_receive_kernel<<<dim3(e->world, 16), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      e->dev, static_cast<uint8_t*>(xbuf->data), static_cast<int32_t*>(inds->data), static_cast<float*>(scores->data),
-      err);
-  return (err && cudaGetLastError() == cudaSuccess) ? exl3_verdict{EXL3_OK, nullptr}
+  const cudaError_t le = exl3::launch_pdl_k(epx_receive_kernel, dim3(e->world, 16), dim3(256),
+                                            static_cast<cudaStream_t>(stream), static_cast<const EpxDev*>(e->dev),
+                                            static_cast<uint8_t*>(xbuf->data), static_cast<int32_t*>(inds->data),
+                                            static_cast<float*>(scores->data), err);
+  return (err && le == cudaSuccess) ? exl3_verdict{EXL3_OK, nullptr}
                                                     : refuse(EXL3_FAILED, "exl3_epx_receive: launch failed");
 }
 
@@ -395,9 +439,11 @@ exl3_verdict exl3_epx_return(exl3_epx* e, const exl3_tensor* ys, void* stream) {
   if (reinterpret_cast<uintptr_t>(ys->data) % 16 != 0) return refuse(EXL3_UNSUPPORTED, "exl3_epx_return: ys on a 16-byte boundary");
   DevScope scope(e->device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  epx_return_kernel<<<dim3(e->world, 16), 256, 0, st>>>(e->dev, static_cast<const float*>(ys->data));
-  epx_publish_return_kernel<<<1, 32, 0, st>>>(e->dev);
-  return cudaGetLastError() == cudaSuccess ? exl3_verdict{EXL3_OK, nullptr}
+  cudaError_t le = exl3::launch_pdl_k(epx_return_kernel, dim3(e->world, 16), dim3(256), st,
+                                      static_cast<const EpxDev*>(e->dev), static_cast<const float*>(ys->data));
+  if (le == cudaSuccess)
+    le = exl3::launch_pdl_k(epx_publish_return_kernel, dim3(1), dim3(32), st, static_cast<const EpxDev*>(e->dev));
+  return le == cudaSuccess ? exl3_verdict{EXL3_OK, nullptr}
                                            : refuse(EXL3_FAILED, "exl3_epx_return: launch failed");
 }
 
@@ -411,13 +457,24 @@ exl3_verdict exl3_epx_combine(exl3_epx* e, const exl3_tensor* back_slot, const e
   if (out->shape[0] == 0) return {EXL3_OK, nullptr};
   DevScope scope(e->device);
   uint32_t* err = exl3::device_error_ptr();
-  epx_combine_kernel<<<dim3(e->hidden / 128, static_cast<unsigned>(out->shape[0])), 128, 0,
-                       static_cast<cudaStream_t>(stream)>>>(e->dev, static_cast<const int32_t*>(back_slot->data),
-                                                           static_cast<const float*>(scores->data),
-                                                           static_cast<int>(back_slot->shape[1]), out->data,
-                                                           out->dtype, err);
-  return (err && cudaGetLastError() == cudaSuccess) ? exl3_verdict{EXL3_OK, nullptr}
+  const cudaError_t le = exl3::launch_pdl_k(epx_combine_kernel, dim3(e->hidden / 128, static_cast<unsigned>(out->shape[0])),
+                                            dim3(128), static_cast<cudaStream_t>(stream),
+                                            static_cast<const EpxDev*>(e->dev),
+                                            static_cast<const int32_t*>(back_slot->data),
+                                            static_cast<const float*>(scores->data),
+                                            static_cast<int>(back_slot->shape[1]), out->data,
+                                            static_cast<int32_t>(out->dtype), err);
+  return (err && le == cudaSuccess) ? exl3_verdict{EXL3_OK, nullptr}
                                                     : refuse(EXL3_FAILED, "exl3_epx_combine: launch failed");
+}
+
+exl3_verdict exl3_epx_trace(exl3_epx* e, uint64_t* out) {
+  if (!e || !e->connected || !out) return refuse(EXL3_FAILED, "exl3_epx_trace: bad arguments");
+  if (!e->trace) return refuse(EXL3_UNSUPPORTED, "exl3_epx_trace: the exchange was created without EXL3_TRACE=1");
+  DevScope scope(e->device);
+  const uint32_t* step = reinterpret_cast<const uint32_t*>(e->base + e->recv_bytes + e->back_bytes + 256);
+  return exl3::trace_copy(e->trace, step, out) ? exl3_verdict{EXL3_OK, nullptr}
+                                               : refuse(EXL3_FAILED, "exl3_epx_trace: copy failed");
 }
 
 }  // extern "C"

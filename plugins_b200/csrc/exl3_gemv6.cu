@@ -25,6 +25,7 @@
 //              run order and applies the output rotation -- the order of every sum is fixed by the shape and the
 //              grid, never by timing.
 #include <cuda_fp16.h>
+#include <cstdlib>
 #include <cuda_runtime.h>
 
 #include "exl3_common.cuh"
@@ -41,10 +42,22 @@ constexpr int kMinRun6 = 32;      // slabs: the shortest run a CTA takes (eight 
 constexpr int kPart6 = 16 * 128;  // floats of one run's partial of a unit (up to 16 rows)
 constexpr int kVirt6 = 3;         // virtual CTAs per SM: the work split
 constexpr int kXiSlabs = 136;     // in-CTA rotation: the most slabs one piece of a run covers (17 input blocks)
-constexpr int kXiRows = 4;        // in-CTA rotation: the most rows
+constexpr int kXiRows = 4;        // in-CTA rotation: the rows its shared-memory layout holds
+constexpr int kXiTake = 1;        // in-CTA rotation: the most rows that take it (measured: from two rows on, the
+                                  // prepare launch is faster: config 2's gate|up 35.9 against 37.9 us at two rows)
+constexpr int kXiBatch = 4;       // in-CTA rotation: a warp's jobs whose loads are in flight together
 
 template <int N>  // n halfwords per tile (16 x bits per weight)
 constexpr int stages6() { return N <= 32 ? 16 : (N <= 64 ? 12 : (N <= 80 ? 10 : 8)); }
+// With the prepared input, each ring slot also carries its unit's x fragments (RG x 256 bytes): the deepest ring that
+// still keeps 3 CTAs per SM (one row group) or 2 (two) beside the reduction buffer.
+template <int N, int RG, bool XI>
+constexpr int stages6x() {
+  if (XI) return stages6<N>();
+  constexpr int budget = RG == 1 ? 76672 : 115584;  // dynamic shared memory per CTA at 3 (2) CTAs per SM
+  constexpr int fit = (budget / kW6 - 8 * RG * kRed6 * 4) / (16 * N + 256 * RG);
+  return stages6<N>() < fit ? stages6<N>() : fit;
+}
 
 __device__ __forceinline__ void cp_async16_6(void* smem_dst, const void* gmem_src) {
   asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
@@ -104,6 +117,9 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
   float* red = reinterpret_cast<float*>(smem + kW6 * ST * kUnitBytes);  // [kW6][kRedRows][kRed6]
   // XI: the run piece's rotated x, [slab][rows 0..3][16 halfs] (the first half of a slab's fragments)
   __half* xbuf = reinterpret_cast<__half*>(smem + kW6 * ST * kUnitBytes + kW6 * kRedRows * kRed6 * 4);
+  // !XI: this warp's ring of the units' x fragments (slot i beside weight slot i: RG x 32 uint2 each)
+  uint2* xring = reinterpret_cast<uint2*>(smem + kW6 * ST * kUnitBytes + kW6 * kRedRows * kRed6 * 4) +
+                 static_cast<size_t>(warp) * ST * RG * 32;
   const int KT = p.in_features / 16, CB = p.out_features / 128, rows = p.rows;
   const size_t OT = static_cast<size_t>(p.out_features / 16);
   const size_t slab_stride = OT * kTileBytes;  // bytes from one slab's unit to the next
@@ -169,12 +185,22 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
     const uint8_t* src_next = src0;
     const size_t src_step = static_cast<size_t>(kW6) * slab_stride;
     uint32_t slot_next = 0, issued = 0, slot_use = 0;
+    // !XI: the prepared fragments of this warp's units (RG x 256 bytes each, kW6 slabs apart), copied into the x
+    // ring with their weights once the prepare launch is complete
+    const uint8_t* xsrc0 = reinterpret_cast<const uint8_t*>(xf + (static_cast<size_t>(s) * KT + k0 + warp) * RG * 128);
+    const uint8_t* xsrc_next = xsrc0;
+    constexpr size_t kXStep = static_cast<size_t>(kW6) * RG * 256;
     auto issue = [&]() {
       if (issued < mine) {
         uint8_t* dst = ring + slot_next * kUnitBytes;
 #pragma unroll
         for (uint32_t ch = lane; ch < kUnitBytes / 16u; ch += 32u) cp_async16_6(dst + ch * 16u, src_next + ch * 16u);
         src_next += src_step;
+        if constexpr (!XI) {
+          if (waited && lane < 16u * RG)
+            cp_async16_6(reinterpret_cast<uint8_t*>(xring + slot_next * RG * 32) + lane * 16u, xsrc_next + lane * 16u);
+          xsrc_next += kXStep;
+        }
       }
       ++issued;
       slot_next = slot_next + 1u == static_cast<uint32_t>(ST) ? 0u : slot_next + 1u;
@@ -187,6 +213,27 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
     if (!waited) {  // the prepared x (and, for the stream, nothing else) comes from the prepare launch
       pdl_wait();
       waited = true;
+      if constexpr (!XI) {
+        // the x fragments of the units issued before the wait, into their slots (loads batched, then stores)
+        const int pre = static_cast<int>(mine < static_cast<uint32_t>(ST - 1) ? mine : static_cast<uint32_t>(ST - 1));
+        const int total = pre * RG * 16;  // uint4s: slot u holds RG x 16 of them, slots contiguous
+        for (int base = static_cast<int>(lane); base < total; base += 32 * 8) {
+          uint4 v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int idx = base + 32 * u;
+            if (idx < total)
+              v[u] = __ldcg(reinterpret_cast<const uint4*>(xsrc0 + static_cast<size_t>(idx / (RG * 16)) * kXStep) +
+                            idx % (RG * 16));
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int idx = base + 32 * u;
+            if (idx < total) reinterpret_cast<uint4*>(xring)[idx] = v[u];
+          }
+        }
+        __syncwarp();
+      }
     }
     // x fragments of slab t, row group rg: 32 uint2 at xf + ((s KT + t) RG + rg) 128 halfs; XI: 16 uint2 per slab of
     // xbuf, lanes of rows past the launch's reading zero
@@ -194,11 +241,11 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
     bool live = true;
     if constexpr (XI) {
       const int b0 = k0 >> 3, nb = ((k1 - 1) >> 3) - b0 + 1;
-      // four of the warp's jobs at a time: their loads are issued before the first rotation (same bits)
-      for (int base = static_cast<int>(warp); base < nb * rows; base += 4 * kW6) {
-        float v[4][4];
+      // eight of the warp's jobs at a time: their loads are issued before the first rotation (same bits)
+      for (int base = static_cast<int>(warp); base < nb * rows; base += kXiBatch * kW6) {
+        float v[kXiBatch][4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kXiBatch; ++u) {
           const int j = base + u * kW6;
           if (j >= nb * rows) continue;  // (warp-uniform)
           const int blk = b0 + j / rows, r = j % rows, kb = blk * 128;
@@ -210,7 +257,7 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
           }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kXiBatch; ++u) {
           const int j = base + u * kW6;
           if (j >= nb * rows) continue;
           const int blk = b0 + j / rows, r = j % rows;
@@ -231,15 +278,12 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
       xs = reinterpret_cast<const uint2*>(xbuf) + (k0 + static_cast<int>(warp) - 8 * b0) * 16 + lane;
       live = static_cast<int>(g) < rows;
     } else {
-      xs = reinterpret_cast<const uint2*>(xf + (static_cast<size_t>(s) * KT + k0 + warp) * RG * 128) + lane;
+      xs = nullptr;  // (the x ring)
     }
-    auto xload = [&](uint32_t i, int r) -> uint2 {
-      if constexpr (XI) return live ? xs[static_cast<size_t>(kW6) * i * 16] : make_uint2(0u, 0u);
-      else return __ldcg(xs + (static_cast<size_t>(kW6) * i * RG + r) * 32);
-    };
+    auto xload = [&](uint32_t i) -> uint2 { return live ? xs[static_cast<size_t>(kW6) * i * 16] : make_uint2(0u, 0u); };
     uint2 xn[RG];
 #pragma unroll
-    for (int r = 0; r < RG; ++r) xn[r] = mine > 0 ? xload(0, r) : make_uint2(0u, 0u);
+    for (int r = 0; r < RG; ++r) xn[r] = (XI && mine > 0) ? xload(0) : make_uint2(0u, 0u);
 
     float acc[8][RG][4];
 #pragma unroll
@@ -255,8 +299,12 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
       uint2 xv[RG];
 #pragma unroll
       for (int r = 0; r < RG; ++r) {
-        xv[r] = xn[r];
-        if (i + 1 < mine) xn[r] = xload(i + 1, r);
+        if constexpr (XI) {
+          xv[r] = xn[r];
+          if (i + 1 < mine) xn[r] = xload(i + 1);
+        } else {
+          xv[r] = xring[(slot_use * RG + r) * 32 + lane];
+        }
       }
       const uint32_t* tw = reinterpret_cast<const uint32_t*>(ring + slot_use * kUnitBytes);
       slot_use = slot_use + 1u == static_cast<uint32_t>(ST) ? 0u : slot_use + 1u;
@@ -313,13 +361,41 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
       __syncthreads();
       if (!s_last) continue;
       __threadfence();
-      for (int idx = static_cast<int>(tid); idx < rows * 128; idx += kT6) {
-        float v = 0.0f;
-        for (int c = first; c <= last; ++c) {
-          const int end = static_cast<int64_t>(c) * run >= u0 ? 0 : 1;
-          v += __ldcg(part + (static_cast<size_t>(c) * 2 + end) * kPart6 + idx);
+      if (XI || rows <= 2) {
+        // one or two rows: each thread's element is the sum of the runs' partials in run order (few loads each)
+        for (int idx = static_cast<int>(tid); idx < rows * 128; idx += kT6) {
+          float v = 0.0f;
+          for (int c = first; c <= last; ++c) {
+            const int end = static_cast<int64_t>(c) * run >= u0 ? 0 : 1;
+            v += __ldcg(part + (static_cast<size_t>(c) * 2 + end) * kPart6 + idx);
+          }
+          red[(idx >> 7) * kRed6 + (idx & 127)] = v;
         }
-        red[(idx >> 7) * kRed6 + (idx & 127)] = v;
+      } else {
+        // the runs' partials, in run order: as many as the (now idle) rings hold at a time are copied into shared memory
+        // together (cp.async, so none of their latency is paid per run), then added into red element by element
+        float* stage = reinterpret_cast<float*>(smem);  // the CTA's rings
+        const int per = rows * 128;                                                // floats of one run's partial
+        const int chunk = static_cast<int>(kW6 * ST * kUnitBytes / 4u) / per;      // runs per pass
+        for (int ca = first; ca <= last; ca += chunk) {
+          const int cn = last - ca + 1 < chunk ? last - ca + 1 : chunk;
+          for (int q4 = static_cast<int>(tid); q4 < cn * per / 4; q4 += kT6) {
+            const int c = ca + q4 / (per / 4), e4 = q4 % (per / 4);
+            const int end = static_cast<int64_t>(c) * run >= u0 ? 0 : 1;
+            cp_async16_6(stage + static_cast<size_t>(q4) * 4,
+                         part + (static_cast<size_t>(c) * 2 + end) * kPart6 + static_cast<size_t>(e4) * 4);
+          }
+          cp_async_commit6();
+          cp_async_wait6<0>();
+          __syncthreads();
+          for (int idx = static_cast<int>(tid); idx < per; idx += kT6) {
+            const int at = (idx >> 7) * kRed6 + (idx & 127);
+            float v = ca == first ? 0.0f : red[at];
+            for (int c = 0; c < cn; ++c) v += stage[c * per + idx];
+            red[at] = v;
+          }
+          __syncthreads();
+        }
       }
     }
     __syncthreads();
@@ -346,10 +422,11 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
 
 template <int N, int RG, bool XI>
 cudaError_t launch6_t(const GemvParams& p, int sms, __half* xf, float* part, uint32_t* done, cudaStream_t st) {
-  constexpr int ST = stages6<N>();
+  constexpr int ST = stages6x<N, RG, XI>();
   auto kern = gemv6_kernel<N, RG, ST, XI>;
   const size_t smem = static_cast<size_t>(kW6) * ST * 8u * 2u * N +
-                      static_cast<size_t>(kW6) * (XI ? kXiRows : 8 * RG) * kRed6 * 4 + (XI ? kXiSlabs * 128 : 0);
+                      static_cast<size_t>(kW6) * (XI ? kXiRows : 8 * RG) * kRed6 * 4 +
+                      (XI ? kXiSlabs * 128 : static_cast<size_t>(kW6) * ST * RG * 256);
   static KernelSetup setup;
   int per_sm = 0;  // resident CTAs per SM (at most kVirt6): the persistent grid is exactly one wave
   if (cudaError_t e = kernel_setup(setup, kern, kT6, smem, false, &per_sm, kVirt6); e != cudaSuccess) return e;
@@ -413,8 +490,10 @@ cudaError_t launch_gemv_prep(const GemvParams& p, int row_groups, void* xf, cuda
 }
 
 bool gemv6_prefers(const GemvParams& p) {
-  const int64_t slabs = static_cast<int64_t>(p.out_features / 128) * (p.in_features / 16);
-  return slabs >= kGemv6MinSlabs || (p.in_features >= 8192 && slabs >= kGemv6MinSlabsDeep);
+  const int cb = p.out_features / 128;
+  const int64_t slabs = static_cast<int64_t>(cb) * (p.in_features / 16);
+  return slabs >= kGemv6MinSlabs || (p.in_features >= 8192 && slabs >= kGemv6MinSlabsDeep) ||
+         (cb <= kGemv6NarrowCb && slabs >= kGemv6NarrowSlabs);
 }
 
 cudaError_t launch_gemv6(const GemvParams& p, int n, int sms, void* scratch, uint32_t* counters, cudaStream_t st) {
@@ -427,7 +506,10 @@ cudaError_t launch_gemv6(const GemvParams& p, int n, int sms, void* scratch, uin
   int64_t run = 0;
   bool all_runs = false;
   split6(p, sms, &run, &all_runs);
-  if (p.rows <= kXiRows && all_runs && run <= kXiSlabs - 8)  // each CTA rotates its runs' inputs itself
+  // measurement override: EXL3_GEMV_XI = the most rows that rotate in-CTA (0 .. kXiRows)
+  int xi_rows = kXiTake;
+  if (const char* e = getenv("EXL3_GEMV_XI")) xi_rows = atoi(e) < kXiRows ? atoi(e) : kXiRows;
+  if (p.rows <= xi_rows && all_runs && run <= kXiSlabs - 8)  // each CTA rotates its runs' inputs itself
     return launch6_k<1, true>(p, n, sms, xf, part, counters, st);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.in_features / 128), static_cast<unsigned>(p.nseg));

@@ -113,6 +113,8 @@ struct TpDev {
   uint32_t* meta;               // this rank's slot metadata: [slots][4] (gathered column blocks, bytes)
   int32_t world, rank, slots, max_cb;
   int64_t slot_bytes;
+  uint64_t* trace;              // the phase timeline ring, or null: 0 begin, 1 publish (the step's GEMVs done), 2 every
+                                // rank's columns seen, 3 gather copied
 };
 
 struct GemvParams {
@@ -170,11 +172,15 @@ cudaError_t launch_gemv(const GemvParams& p, int n, int row_groups, bool imma, c
 // The persistent work-balanced decode GEMV (exl3_gemv6.cu), 1..16 rows, no column-parallel exchange: a prepare
 // launch (x rotated into fragment order in `scratch`) and the GEMV (runs' partials in `scratch` after the prepared x;
 // `counters` [out/128] zero between launches, each reset by the run that uses it).  Preferred (measured faster than
-// the cluster split) from kGemv6MinSlabs 16-row slabs of 128 columns per launch, and for inputs of 8192 and more from
-// kGemv6MinSlabsDeep (where the cluster split needs 12-16 CTAs per cluster); below that the cluster split's shorter
-// critical path wins.
+// the cluster split at 1, 2, 8 and 16 rows) from kGemv6MinSlabs 16-row slabs of 128 columns per launch, for inputs of
+// 8192 and more from kGemv6MinSlabsDeep (where the cluster split needs 12-16 CTAs per cluster), and for narrow
+// outputs -- at most kGemv6NarrowCb column blocks -- from kGemv6NarrowSlabs (config 2's o and q|k|v: 11.6 / 11.8 us
+// against 11.9 / 12.8 at one row, 15.1 / 15.3 against 17.8 / 17.9 at eight); in between (config 2's 4096 x 12288:
+// 17.5 against 19.2 us) the cluster split wins.
 constexpr int64_t kGemv6MinSlabs = 49152;
 constexpr int64_t kGemv6MinSlabsDeep = 16384;
+constexpr int kGemv6NarrowCb = 64;
+constexpr int64_t kGemv6NarrowSlabs = 8192;
 bool gemv6_prefers(const GemvParams& p);
 // x of the launch's rows rotated once into the GEMVs' fragment order (IMMA k order) at xf: [nseg][in/16][row_groups]
 // [128 halfs], rows past the launch's zero; chained to the next launch with programmatic dependent launch.
@@ -271,6 +277,49 @@ cudaError_t launch_gemm_image(const GemmParams& p, int shape, int sms, cudaStrea
 
 // the device error word of the current device (exl3_device_error reads it), or null
 uint32_t* device_error_ptr();
+
+// A launch that may begin while the previous kernel in the stream finishes (programmatic dependent launch): the
+// kernel calls pdl_wait() before it touches anything an earlier launch in the stream wrote or reads.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// An exchange's phase timeline: with EXL3_TRACE=1 in the environment when the exchange is created, its kernels write
+// %globaltimer stamps (ns) into a device ring of kTraceStamps per step for the last kTraceSteps steps (a null ring
+// records nothing).  trace_alloc: that ring (zeroed) on the current device, or null without EXL3_TRACE=1; trace_copy
+// waits for the device and writes the ring to out oldest step first, given the exchange's step word (the step of the
+// newest stamps).
+constexpr int kTraceSteps = 16, kTraceStamps = 8;
+uint64_t* trace_alloc();
+bool trace_copy(const uint64_t* ring, const uint32_t* step_word, uint64_t* out);
+
+#if defined(__CUDACC__)
+__device__ __forceinline__ uint64_t trace_now() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// one thread's stamp
+__device__ __forceinline__ void trace_at(uint64_t* ring, uint32_t step, int i) {
+  if (ring) ring[(step % kTraceSteps) * kTraceStamps + i] = trace_now();
+}
+// every CTA of a launch as it leaves: the latest is kept
+__device__ __forceinline__ void trace_last(uint64_t* ring, uint32_t step, int i) {
+  if (ring)
+    atomicMax(reinterpret_cast<unsigned long long*>(ring) + (step % kTraceSteps) * kTraceStamps + i,
+              static_cast<unsigned long long>(trace_now()));
+}
+#endif
 
 
 }  // namespace exl3

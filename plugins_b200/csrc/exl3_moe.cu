@@ -928,15 +928,16 @@ exl3_verdict moe_swiglu_impl(const exl3_weight* gate, const exl3_weight* up, con
 // Every rank holds a column slice of every expert: gate/up output columns [r inter/W, (r+1) inter/W) and down output
 // columns [r hidden/W, (r+1) hidden/W) (down's input is the whole intermediate), so each rank streams exactly 1/W of the
 // distinct experts' bytes whatever the routing.  A call (every rank brings T tokens with K slots each):
-//   in     -- each rank's x, inds, scores rows into every rank's gathered block (rows [rank T, rank T + T)); the last
-//             CTA advances the step word and releases done[0][rank] on every rank;
-//   wait 0 -- every rank's rows are in (bounded);
+//   in     -- each rank's x, inds, scores rows into every rank's gathered block (rows [rank T, rank T + T));
+//   wait 0 -- a one-CTA launch (the copies' launch has completed) advances the step word, releases done[0][rank] on
+//             every rank once and waits (bounded) until every rank's rows are in;
 //   route, prepare, gate|up GEMV on all W T rows -- the same slot order and chunk table on every rank (deterministic);
 //             the gate|up epilogue stores its blocks of the down input into every rank's down-input buffer;
 //   sync 1 -- this rank's gate|up is complete: release done[1][rank] on every rank, wait for every rank's (bounded);
 //   down GEMV over this rank's output columns (the whole down input is local now), combine -> ycol [W T][hidden/W];
-//   out    -- each owner's T rows of ycol into its output block (columns [rank hidden/W, ...)); release done[2][rank];
-//   final  -- every rank's columns are in (bounded); the T rows to the caller's out.
+//   out    -- each owner's T rows of ycol into its output block (columns [rank hidden/W, ...));
+//   final  -- its first CTA releases done[2][rank] once (the out launch has completed); every rank's columns are in
+//             (bounded); the T rows to the caller's out.
 // One copy of each buffer suffices: a rank writes a peer's buffers of call s + 1 only after passing a wait of call
 // s + 1 that the peer releases after it finished reading them in call s.  Every wait gives up after one second with
 // EXL3_ERR_EP_TIMEOUT; the done words only grow, so graph replays need nothing reset.
@@ -947,6 +948,9 @@ struct CpxDev {
   uint32_t* arrive;     // [3] (unused: each phase publishes once, from the launch that waits for it)
   int32_t world, rank, tokens, topk, hidden, hidden_out, esize;
   int64_t off_x, off_inds, off_scores, off_hp, off_y, off_done;
+  uint64_t* trace;      // the phase timeline ring, or null: 0 in begins, 1 its copies done, 2 every rank's rows seen,
+                        // 3 gate|up done, 4 every rank's gate|up seen, 5 down and combine done, 6 every rank's
+                        // columns seen, 7 copied out
 };
 
 namespace {
@@ -998,8 +1002,12 @@ __device__ void copy16(uint8_t* dst, const uint8_t* src, size_t bytes, size_t t0
 // grid (world, c): this rank's rows into block `rank` of every rank's gathered x / inds / scores
 __global__ void __launch_bounds__(256) cpx_in_kernel(const CpxDev* dp, const uint8_t* __restrict__ x,
                                                      const int32_t* __restrict__ inds, const float* __restrict__ scores) {
+  pdl_wait();  // every launch before this one in the stream is complete (programmatic dependent launch)
+  pdl_launch_dependents();
   const CpxDev& d = *dp;
   const int q = blockIdx.x;
+  if (q == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    trace_at(d.trace, *reinterpret_cast<const volatile uint32_t*>(d.step) + 1u, 0);
   const size_t xrow = static_cast<size_t>(d.hidden) * d.esize;
   const size_t t0 = static_cast<size_t>(blockIdx.y) * blockDim.x + threadIdx.x, stride = static_cast<size_t>(gridDim.y) * blockDim.x;
   copy16(d.buf[q] + d.off_x + static_cast<size_t>(d.rank) * d.tokens * xrow, x, d.tokens * xrow, t0, stride);
@@ -1015,30 +1023,44 @@ __global__ void __launch_bounds__(256) cpx_in_kernel(const CpxDev* dp, const uin
 // After this rank's copies into every rank (the previous launch, complete): advance the step word, publish phase 0
 // -- one system-scope fence for all of the launch's stores -- and wait (bounded) for every rank's.
 __global__ void cpx_in_publish_kernel(const CpxDev* dp, uint32_t* err) {
+  pdl_wait();  // the copies' launch is complete: its stores are performed
+  pdl_launch_dependents();
   const CpxDev& d = *dp;
   __shared__ uint32_t s_step;
   if (threadIdx.x == 0) {
     const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step) + 1u;
+    trace_at(d.trace, step, 1);
     *d.step = step;
     cpx_release(d, 0, step);
     s_step = step;
   }
   __syncthreads();
   cpx_wait_all(d, 0, s_step, err);
+  if (threadIdx.x == 0) trace_at(d.trace, s_step, 2);
 }
 
 // After this rank's gate|up (the previous launch, complete): publish it, wait for every rank's.
 __global__ void cpx_sync_kernel(const CpxDev* dp, uint32_t* err) {
+  pdl_wait();  // the gate|up launch is complete: its stores into every rank are performed
+  pdl_launch_dependents();
   const CpxDev& d = *dp;
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
-  if (threadIdx.x == 0) cpx_release(d, 1, step);
+  if (threadIdx.x == 0) {
+    trace_at(d.trace, step, 3);
+    cpx_release(d, 1, step);
+  }
   cpx_wait_all(d, 1, step, err);
+  if (threadIdx.x == 0) trace_at(d.trace, step, 4);
 }
 
 // grid (world, c): owner q's T rows of ycol [W T][hidden_out] -> its output block, columns [rank hidden_out, ...)
 __global__ void __launch_bounds__(256) cpx_out_kernel(const CpxDev* dp, const uint8_t* __restrict__ ycol) {
+  pdl_wait();
+  pdl_launch_dependents();
   const CpxDev& d = *dp;
   const int q = blockIdx.x;
+  if (q == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    trace_at(d.trace, *reinterpret_cast<const volatile uint32_t*>(d.step), 5);
   const size_t seg = static_cast<size_t>(d.hidden_out) * d.esize;  // bytes of one row's column slice
   const size_t words = seg / 16;
   for (size_t w = static_cast<size_t>(blockIdx.y) * blockDim.x + threadIdx.x; w < d.tokens * words;
@@ -1053,13 +1075,18 @@ __global__ void __launch_bounds__(256) cpx_out_kernel(const CpxDev* dp, const ui
 // After the out copies (the previous launch, complete): CTA 0 publishes phase 2 (one system-scope fence for all of
 // them); every rank's columns of this rank's rows are in (bounded), then they go to the caller's out
 __global__ void __launch_bounds__(256) cpx_final_kernel(const CpxDev* dp, uint8_t* __restrict__ out, uint32_t* err) {
+  pdl_wait();  // the out copies' launch is complete: its stores are performed
+  pdl_launch_dependents();
   const CpxDev& d = *dp;
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(d.step);
   if (blockIdx.x == 0 && threadIdx.x == 0) cpx_release(d, 2, step);
   cpx_wait_all(d, 2, step, err);
+  if (blockIdx.x == 0 && threadIdx.x == 0) trace_at(d.trace, step, 6);
   const size_t bytes = static_cast<size_t>(d.tokens) * d.hidden * d.esize;
   copy16(out, d.buf[d.rank] + d.off_y, bytes, static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x,
          static_cast<size_t>(gridDim.x) * blockDim.x);
+  __syncthreads();
+  if (threadIdx.x == 0) trace_last(d.trace, step, 7);
 }
 
 }  // namespace
@@ -1142,6 +1169,7 @@ exl3_verdict exl3_cpx_create(int32_t device, int32_t world, int32_t rank, int32_
   h.arrive = h.step + 4;
   h.world = world, h.rank = rank, h.tokens = tokens, h.topk = topk, h.hidden = hidden;
   h.hidden_out = hidden / world, h.esize = e->esize;
+  h.trace = trace_alloc();
   *out = e;
   return {EXL3_OK, nullptr};
 }
@@ -1175,7 +1203,17 @@ void exl3_cpx_destroy(exl3_cpx* e) {
     if (q != e->rank && e->peer[q]) cudaIpcCloseMemHandle(e->peer[q]);
   if (e->dev) cudaFree(e->dev);
   if (e->base) cudaFree(e->base);
+  if (e->host.trace) cudaFree(e->host.trace);
   delete e;
+}
+
+exl3_verdict exl3_cpx_trace(exl3_cpx* e, uint64_t* out) {
+  using namespace exl3;
+  if (!e || !e->connected || !out) return refuse_m(EXL3_FAILED, "exl3_cpx_trace: bad arguments");
+  if (!e->host.trace) return refuse_m(EXL3_UNSUPPORTED, "exl3_cpx_trace: the exchange was created without EXL3_TRACE=1");
+  CpxScope scope(e->device);
+  return trace_copy(e->host.trace, e->host.step, out) ? exl3_verdict{EXL3_OK, nullptr}
+                                                      : refuse_m(EXL3_FAILED, "exl3_cpx_trace: copy failed");
 }
 
 exl3_verdict exl3_swiglu_cp(exl3_cpx* e, const exl3_weight* gate, const exl3_weight* up, const exl3_weight* down,
@@ -1255,27 +1293,24 @@ exl3_verdict exl3_swiglu_cp(exl3_cpx* e, const exl3_weight* gate, const exl3_wei
   p.hp_world = W;
   const int S = W * T * K;
   const int copy = W >= 148 ? 1 : (148 + W - 1) / W;
-  cpx_in_kernel<<<dim3(W, copy), 256, 0, st>>>(e->dev, static_cast<const uint8_t*>(x->data),
-                                               static_cast<const int32_t*>(inds->data),
-                                               static_cast<const float*>(scores->data));
-  cpx_in_publish_kernel<<<1, 32, 0, st>>>(e->dev, err);
-  cudaError_t er = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
+  const CpxDev* dv = e->dev;
+  cudaError_t er = launch_pdl_k(cpx_in_kernel, dim3(W, copy), dim3(256), st, dv, static_cast<const uint8_t*>(x->data),
+                                static_cast<const int32_t*>(inds->data), static_cast<const float*>(scores->data));
+  if (er == cudaSuccess) er = launch_pdl_k(cpx_in_publish_kernel, dim3(1), dim3(32), st, dv, err);
+  if (er == cudaSuccess) er = launch_pdl(moe_route_kernel, dim3(1), dim3(1024), p, st);
   if (er == cudaSuccess)
     er = launch_pdl(moe_prep_kernel, dim3(hidden / 128, S < kPrepChunks ? S : kPrepChunks), dim3(128), p, st);
   if (er == cudaSuccess) er = launch_moe_gemv_k<true>(p, gate->n, sc->sms, st);
-  if (er == cudaSuccess) {
-    cpx_sync_kernel<<<1, 32, 0, st>>>(e->dev, err);
-    er = cudaGetLastError();
-  }
+  if (er == cudaSuccess) er = launch_pdl_k(cpx_sync_kernel, dim3(1), dim3(32), st, dv, err);
   if (er == cudaSuccess) er = launch_moe_gemv_k<false>(p, down->n, sc->sms, st);
   if (er == cudaSuccess)
     er = launch_pdl(moe_combine_kernel, dim3((hslice + 511) / 512, p.rows < kCombineRows ? p.rows : kCombineRows),
                     dim3(128), p, st);
-  if (er == cudaSuccess) {
-    cpx_out_kernel<<<dim3(W, copy), 256, 0, st>>>(e->dev, e->base + e->off_ycol);
-    cpx_final_kernel<<<16, 256, 0, st>>>(e->dev, static_cast<uint8_t*>(out->data), err);
-    er = cudaGetLastError();
-  }
+  if (er == cudaSuccess)
+    er = launch_pdl_k(cpx_out_kernel, dim3(W, copy), dim3(256), st, dv,
+                      static_cast<const uint8_t*>(e->base + e->off_ycol));
+  if (er == cudaSuccess)
+    er = launch_pdl_k(cpx_final_kernel, dim3(16), dim3(256), st, dv, static_cast<uint8_t*>(out->data), err);
   return er == cudaSuccess ? exl3_verdict{EXL3_OK, nullptr} : refuse_m(EXL3_FAILED, "exl3_swiglu_cp: launch failed");
 }
 

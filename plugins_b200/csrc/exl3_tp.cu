@@ -30,6 +30,7 @@ struct exl3_tp {
   size_t y_bytes = 0, flag_bytes = 0;
   uint8_t* peer[exl3::kMaxTpRanks] = {};  // every rank's buffer as mapped here (peer[rank] = base)
   exl3::TpDev* dev = nullptr;             // device copy of the table
+  uint64_t* trace = nullptr;              // the phase timeline ring (EXL3_TRACE=1 at create), or null
   bool connected = false;
 };
 
@@ -43,15 +44,24 @@ uint32_t* meta_of(uint8_t* base, size_t y_bytes, size_t flag_bytes) {
   return reinterpret_cast<uint32_t*>(base + y_bytes + flag_bytes);
 }
 
-__global__ void tp_begin_kernel(uint32_t* step) {
-  if (threadIdx.x == 0) *step += 1u;
+__global__ void tp_begin_kernel(uint32_t* step, uint64_t* trace) {
+  exl3::pdl_wait();  // the previous step's gather has read the step word
+  exl3::pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    const uint32_t s = *step + 1u;
+    *step = s;
+    exl3::trace_at(trace, s, 0);
+  }
 }
 
 // This rank's columns of the step, published to every rank: a system-scope fence (the GEMVs before this kernel in
 // stream order wrote them), then done[rank] = step on every rank.
 __global__ void tp_publish_kernel(const exl3::TpDev* tp) {
+  exl3::pdl_wait();  // the step's GEMVs are complete: their stores are performed
+  exl3::pdl_launch_dependents();
   if (threadIdx.x != 0) return;
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(tp->step);
+  exl3::trace_at(tp->trace, step, 1);
   asm volatile("fence.sc.sys;" ::: "memory");
   for (int q = 0; q < tp->world; ++q) {
     uint32_t* f = tp->flag[q] + tp->rank;
@@ -63,8 +73,10 @@ __global__ void tp_publish_kernel(const exl3::TpDev* tp) {
 __global__ void __launch_bounds__(256) tp_gather_kernel(const uint8_t* __restrict__ y, const uint32_t* done,
                                                         const uint32_t* meta, const uint32_t* step_p, int world,
                                                         int slots, int64_t slot_bytes, int slot0,
-                                                        uint8_t* __restrict__ out, uint32_t* err) {
+                                                        uint8_t* __restrict__ out, uint32_t* err, uint64_t* trace) {
   __shared__ int s_fail;
+  exl3::pdl_wait();
+  exl3::pdl_launch_dependents();
   const int slot = slot0 + static_cast<int>(blockIdx.x);
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(step_p);
   if (threadIdx.x == 0) s_fail = 0;
@@ -87,6 +99,7 @@ __global__ void __launch_bounds__(256) tp_gather_kernel(const uint8_t* __restric
   }
   __syncthreads();
   if (s_fail && threadIdx.x == 0) atomicOr(err, exl3::kErrTpTimeout);
+  if (blockIdx.x == 0 && threadIdx.x == 0) exl3::trace_at(trace, step, 2);
   const uint32_t nbytes = meta[slot * 4 + 1];
   const uint8_t* src = y + (static_cast<size_t>(step & 1u) * slots + slot) * slot_bytes;
   uint8_t* dst = out + static_cast<size_t>(blockIdx.x) * slot_bytes;
@@ -94,6 +107,8 @@ __global__ void __launch_bounds__(256) tp_gather_kernel(const uint8_t* __restric
   for (uint32_t i = threadIdx.x; i < n16; i += blockDim.x)
     reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
   for (uint32_t i = n16 * 16u + threadIdx.x; i < nbytes; i += blockDim.x) dst[i] = src[i];
+  __syncthreads();
+  if (threadIdx.x == 0) exl3::trace_last(trace, step, 3);
 }
 
 }  // namespace
@@ -127,6 +142,7 @@ exl3_verdict exl3_tp_create(int32_t device, int32_t world, int32_t rank, int32_t
   tp->slots = slots;
   tp->max_cb = max_cb;
   tp->slot_bytes = slot_bytes;
+  tp->trace = exl3::trace_alloc();
   tp->y_bytes = 2u * static_cast<size_t>(slots) * slot_bytes;
   tp->flag_bytes = 256;  // done[world]
   const size_t total = tp->y_bytes + tp->flag_bytes + static_cast<size_t>(slots) * kMetaBytes + 256;
@@ -137,6 +153,7 @@ exl3_verdict exl3_tp_create(int32_t device, int32_t world, int32_t rank, int32_t
   if (prev >= 0) cudaSetDevice(prev);
   if (!ok) {
     if (tp->base) cudaFree(tp->base);
+    if (tp->trace) cudaFree(tp->trace);
     delete tp;
     return refuse(EXL3_TOO_LARGE, "exl3_tp_create: exchange buffer allocation failed");
   }
@@ -174,6 +191,7 @@ exl3_verdict exl3_tp_connect(exl3_tp* tp, const uint8_t* ipc_handles) {
   host.slots = tp->slots;
   host.max_cb = tp->max_cb;
   host.slot_bytes = tp->slot_bytes;
+  host.trace = tp->trace;
   ok = ok && cudaMalloc(&tp->dev, sizeof host) == cudaSuccess &&
        cudaMemcpy(tp->dev, &host, sizeof host, cudaMemcpyHostToDevice) == cudaSuccess;
   if (prev >= 0) cudaSetDevice(prev);
@@ -192,6 +210,7 @@ void exl3_tp_destroy(exl3_tp* tp) {
     if (q != tp->rank && tp->peer[q]) cudaIpcCloseMemHandle(tp->peer[q]);
   if (tp->dev) cudaFree(tp->dev);
   if (tp->base) cudaFree(tp->base);
+  if (tp->trace) cudaFree(tp->trace);
   if (prev >= 0) cudaSetDevice(prev);
   delete tp;
 }
@@ -203,8 +222,8 @@ exl3_verdict exl3_tp_begin(exl3_tp* tp, void* stream) {
   if (prev != tp->device) cudaSetDevice(tp->device);
   uint32_t* step = reinterpret_cast<uint32_t*>(tp->base + tp->y_bytes + tp->flag_bytes +
                                                static_cast<size_t>(tp->slots) * kMetaBytes);
-  tp_begin_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(step);
-  const bool ok = cudaGetLastError() == cudaSuccess;
+  const bool ok = exl3::launch_pdl_k(tp_begin_kernel, dim3(1), dim3(32), static_cast<cudaStream_t>(stream), step,
+                                     tp->trace) == cudaSuccess;
   if (prev >= 0 && prev != tp->device) cudaSetDevice(prev);
   return ok ? exl3_verdict{EXL3_OK, nullptr} : refuse(EXL3_FAILED, "exl3_tp_begin: launch failed");
 }
@@ -222,13 +241,27 @@ exl3_verdict exl3_tp_gather(exl3_tp* tp, int32_t slot0, int32_t nslots, void* st
   const uint32_t* step = reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(meta) +
                                                            static_cast<size_t>(tp->slots) * kMetaBytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  tp_publish_kernel<<<1, 32, 0, st>>>(tp->dev);
-  bool ok = cudaGetLastError() == cudaSuccess;
-  tp_gather_kernel<<<nslots, 256, 0, st>>>(tp->base, done, meta, step, tp->world, tp->slots, tp->slot_bytes, slot0,
-                                           static_cast<uint8_t*>(out), err);
-  ok = ok && err && cudaGetLastError() == cudaSuccess;
+  bool ok = exl3::launch_pdl_k(tp_publish_kernel, dim3(1), dim3(32), st,
+                               static_cast<const exl3::TpDev*>(tp->dev)) == cudaSuccess;
+  ok = ok && err &&
+       exl3::launch_pdl_k(tp_gather_kernel, dim3(nslots), dim3(256), st, static_cast<const uint8_t*>(tp->base), done,
+                          meta, step, tp->world, tp->slots, tp->slot_bytes, slot0, static_cast<uint8_t*>(out), err,
+                          tp->trace) == cudaSuccess;
   if (prev >= 0 && prev != tp->device) cudaSetDevice(prev);
   return ok ? exl3_verdict{EXL3_OK, nullptr} : refuse(EXL3_FAILED, "exl3_tp_gather: launch failed");
+}
+
+exl3_verdict exl3_tp_trace(exl3_tp* tp, uint64_t* out) {
+  if (!tp || !tp->connected || !out) return refuse(EXL3_FAILED, "exl3_tp_trace: bad arguments");
+  if (!tp->trace) return refuse(EXL3_UNSUPPORTED, "exl3_tp_trace: the exchange was created without EXL3_TRACE=1");
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != tp->device) cudaSetDevice(tp->device);
+  const uint32_t* step = reinterpret_cast<const uint32_t*>(tp->base + tp->y_bytes + tp->flag_bytes +
+                                                           static_cast<size_t>(tp->slots) * kMetaBytes);
+  const bool ok = exl3::trace_copy(tp->trace, step, out);
+  if (prev >= 0 && prev != tp->device) cudaSetDevice(prev);
+  return ok ? exl3_verdict{EXL3_OK, nullptr} : refuse(EXL3_FAILED, "exl3_tp_trace: copy failed");
 }
 
 }  // extern "C"

@@ -26,6 +26,21 @@ from . import quant as Q
 COL_BLOCK = 128  # output columns per Hadamard block: the unit a column shard is made of
 
 
+TRACE_STEPS, TRACE_STAMPS = 16, 8
+
+
+def read_trace(fn, ptr) -> list[list[int]]:
+    """An exchange's phase timeline (created with EXL3_TRACE=1 in the environment): the last 16 steps' %globaltimer
+    stamps in ns, 8 per step, oldest step first; steps not yet run are left out.  Which stamp is which: the
+    exchange-timeline comment of include/exl3_b200.h."""
+    import ctypes
+    from . import _lib as L
+    buf = (ctypes.c_uint64 * (TRACE_STEPS * TRACE_STAMPS))()
+    L.check(fn(ptr, buf))
+    steps = [list(buf[i * TRACE_STAMPS:(i + 1) * TRACE_STAMPS]) for i in range(TRACE_STEPS)]
+    return [st for st in steps if any(st)]
+
+
 def column_range(out_features: int, rank: int, world: int) -> tuple[int, int]:
     """Rank r's output columns [c0, c1): whole 128-column blocks, the first (blocks % world) ranks one block more."""
     if out_features % COL_BLOCK:
@@ -141,6 +156,10 @@ class TpExchange:
         self._L.check(self._L.lib().exl3_tp_gather(self._ptr, int(slot0), int(nslots), Q._stream(stream),
                                                    out.data_ptr()))
 
+    def trace(self) -> list[list[int]]:
+        """Per step: begin, publish (this rank's GEMVs done), every rank's columns seen, gathered (ns)."""
+        return read_trace(self._L.lib().exl3_tp_trace, self._ptr)
+
     def close(self):
         if self._ptr:
             self._L.lib().exl3_tp_destroy(self._ptr)
@@ -232,6 +251,11 @@ class PeerExpertExchange:
                                                      ct.byref(Q._tensor(scores)), Q._stream(stream),
                                                      ct.byref(Q._tensor(out))))
 
+    def trace(self) -> list[list[int]]:
+        """Per step: dispatch begins / copied, every rank's dispatch seen, received, return begins (swiglu done) /
+        copied, every rank's return seen, combined (ns)."""
+        return read_trace(self._L.lib().exl3_epx_trace, self._ptr)
+
     def close(self):
         if self._ptr:
             self._L.lib().exl3_epx_destroy(self._ptr)
@@ -309,6 +333,11 @@ class ColumnParallelExperts:
             ct.byref(Q._tensor(x)), ct.byref(Q._tensor(inds)), ct.byref(Q._tensor(scores)), ct.byref(self._opts),
             Q._stream(stream), ct.byref(Q._tensor(out))))
         return out
+
+    def trace(self) -> list[list[int]]:
+        """Per step: tokens' copies begin / done, every rank's tokens seen, gate|up done, every rank's gate|up seen,
+        down and combine done, every rank's columns seen, copied out (ns)."""
+        return read_trace(self._L.lib().exl3_cpx_trace, self._ptr)
 
     def close(self):
         if self._ptr:

@@ -113,17 +113,30 @@ def test_bench_counts_launches_with_the_librarys_gemv_selection():
     spec.loader.exec_module(b)
     assert b.GEMV6_MIN_SLABS == val(hdr, "kGemv6MinSlabs")
     assert b.GEMV6_MIN_SLABS_DEEP == val(hdr, "kGemv6MinSlabsDeep")
+    assert b.GEMV6_NARROW_CB == val(hdr, "kGemv6NarrowCb") and b.GEMV6_NARROW_SLABS == val(hdr, "kGemv6NarrowSlabs")
     assert val(g6, "kVirt6") == 3 and val(g6, "kMinRun6") == 32 and val(g6, "kXiRows") == 4
+    assert b.XI_TAKE == val(g6, "kXiTake")
     assert val(g6, "kXiSlabs") - 8 == 128  # the longest run rotated in-CTA
-    # config 2's launches at batch 1 and 8, one GPU: gate|up and down on the persistent GEMV
+    # config 2's launches at batch 1 and 8, one GPU: q|k|v, o, gate|up and down on the persistent GEMV (in-CTA
+    # rotation at one row), the north-star 4096 x 12288 on the cluster split
     assert [b.gemv6_mode(i, o, False, 1) for i, o in ((4096, 6144), (4096, 4096), (4096, 24576), (12288, 4096))] == \
-        [0, 0, 1, 1]
+        [1, 1, 1, 1]
+    assert b.gemv6_mode(4096, 12288, False, 1) == 0
     assert [b.gemv_kernels(i, o, False, 8) for i, o in ((4096, 24576), (12288, 4096))] == [2, 2]
+    assert [b.gemv_kernels(4096, 4096, False, r) for r in (1, 2)] == [1, 2]
     assert b.gemv_kernels(4096, 24576, True, 1) == 1  # the column-parallel exchange stays on the cluster split
     # the cluster split rotates in-CTA at one row, else takes the prepare launch
     abi = open(os.path.join(root, "plugins_b200", "csrc", "exl3_abi.cu")).read()
     assert b.CTA_ROTATE_ROWS == val(abi, "kCtaRotateRows")
-    assert [b.gemv_kernels(4096, 6144, False, r) for r in (1, 2, 8)] == [1, 2, 2]
+    assert [b.gemv_kernels(4096, 12288, False, r) for r in (1, 2, 8)] == [1, 2, 2]
+
+
+def test_timeline_reads_refuse_a_missing_exchange_without_a_gpu_call():
+    lib = L.lib()
+    buf = (ctypes.c_uint64 * 128)()
+    for fn in (lib.exl3_tp_trace, lib.exl3_epx_trace, lib.exl3_cpx_trace):
+        v = fn(None, buf)
+        assert v.code == L.EXL3_FAILED and b"bad arguments" in v.why
 
 
 def test_exchanges_refuse_bad_shapes_before_touching_the_gpu():

@@ -241,6 +241,37 @@ def test_column_parallel_experts_on_one_rank_match_swiglu_and_replay(Q):
     cp.close()
 
 
+def test_peer_and_column_exchange_timelines_on_one_rank(monkeypatch):
+    """EXL3_TRACE=1 at create: the expert-parallel and column-parallel exchanges stamp their eight phases of every
+    step in order (dispatch / copies / waits / the caller's swiglu / return / combine; tokens / gate|up / down /
+    out), oldest step first."""
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    from plugins_b200 import sharding as S
+    experts, hidden, inter, n, tokens, topk = 8, 256, 256, 48, 6, 2
+    banks = [Q.weight_from_tensors(*b) for b in _banks(E, experts + 1, hidden, inter, n, 90)]
+    monkeypatch.setenv("EXL3_TRACE", "1")
+    peer = S.ExpertParallelSwiglu(*banks, experts=experts, tokens=tokens, topk=topk, hidden=hidden, rank=0, world=1,
+                                  shared=True, exchange="peer")
+    cp = S.ColumnParallelExperts(*banks, experts=experts, tokens=tokens, topk=topk, hidden=hidden, inter=inter, rank=0,
+                                 world=1, shared=True)
+    monkeypatch.delenv("EXL3_TRACE")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn((tokens, hidden), device="cuda", generator=g).half()
+    inds, sc = [t.cuda() for t in _routing(tokens, topk, experts, 5)]
+    for _ in range(4):
+        peer.forward(x, inds, sc)
+        cp.forward(x, inds, sc)
+    for got in (peer.peer.trace(), cp.trace()):
+        assert len(got) == 4
+        for st in got:
+            assert all(st) and all(a <= b for a, b in zip(st, st[1:])), st
+        assert all(a[7] <= b[0] for a, b in zip(got, got[1:]))
+    assert Q.device_error(0) == 0
+    peer.peer.close()
+    cp.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

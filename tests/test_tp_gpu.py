@@ -75,6 +75,36 @@ def test_one_rank_exchange_matches_matmul_and_replays():
     ex.close()
 
 
+def test_one_rank_timeline_stamps_each_phase_in_order(monkeypatch):
+    """EXL3_TRACE=1 at create: each step's four stamps (begin, publish, every rank seen, gathered) come back oldest
+    step first and in order; an exchange made without it refuses the read by name."""
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    from plugins_b200 import sharding as S
+    w = Q.weight_from_tensors(*E.random_linear(512, 1024, 64, seed=311))
+    x = torch.randn((1, 512), device="cuda", dtype=torch.float16)
+    out = torch.empty(1024 * 2, dtype=torch.uint8, device="cuda")
+    plain = S.TpExchange(0, 1, slots=1, slot_bytes=1024 * 2, max_cb=8)
+    with pytest.raises(Q.Exl3Error, match="without EXL3_TRACE=1"):
+        plain.trace()
+    plain.close()
+    monkeypatch.setenv("EXL3_TRACE", "1")
+    ex = S.TpExchange(0, 1, slots=1, slot_bytes=1024 * 2, max_cb=8)
+    monkeypatch.delenv("EXL3_TRACE")
+    for steps in (3, 20):  # 20 steps wrap the 16-step ring
+        for _ in range(steps - (3 if steps == 20 else 0)):
+            ex.begin()
+            ex.matmul(w, x, 0, [0], [1024])
+            ex.gather(0, 1, out)
+        got = ex.trace()
+        assert len(got) == min(steps, 16)
+        for st in got:
+            assert all(st[:4]) and st[0] <= st[1] <= st[2] <= st[3] and not any(st[4:]), st
+        assert all(a[0] <= b[0] for a, b in zip(got, got[1:]))
+    assert Q.device_error(0) == 0
+    ex.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
