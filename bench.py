@@ -44,12 +44,9 @@ def gemv_kernels(in_f: int, out_f: int, exchange: bool, rows: int = 1, sms: int 
     """Kernels one decode-GEMV call launches (the selection in plugins_b200/csrc/exl3_abi.cu and exl3_gemv6.cu): the
     persistent GEMV for large and for narrow launches -- one kernel when its CTAs rotate the input themselves (XI_TAKE
     rows, runs of at most 128 slabs), else a prepare launch and the GEMV -- and the cluster-split GEMV otherwise: one
-    launch at one row (its CTAs rotate their slabs' input) and with the column-parallel exchange, a prepare launch and
-    the GEMV from CTA_ROTATE_ROWS + 1 rows."""
+    launch at one row (its CTAs rotate their slabs' input), a prepare launch and the GEMV from CTA_ROTATE_ROWS + 1
+    rows; the column-parallel exchange (`exchange`) takes the same kernels as its shard's shape."""
     cb, kt = out_f // 128, in_f // 16
-    slabs = cb * kt
-    if exchange:
-        return 1
     if not gemv6_serves(in_f, out_f):
         return 1 if rows <= CTA_ROTATE_ROWS else 2
     v = sms * 3
@@ -68,8 +65,9 @@ def gemv6_serves(in_f: int, out_f: int) -> bool:
 
 
 def gemv6_mode(in_f: int, out_f: int, exchange: bool, rows: int = 1) -> int:
-    """0: the cluster-split GEMV; 1: the persistent one rotating its input in-CTA; 2: prepare launch + persistent."""
-    if exchange or not gemv6_serves(in_f, out_f):
+    """0: the cluster-split GEMV; 1: the persistent one rotating its input in-CTA; 2: prepare launch + persistent.
+    The column-parallel exchange takes the same kernel as its shard's shape."""
+    if not gemv6_serves(in_f, out_f):
         return 0
     return gemv_kernels(in_f, out_f, exchange, rows)
 

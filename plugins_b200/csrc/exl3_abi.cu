@@ -882,9 +882,22 @@ exl3_verdict exl3_matmul_tp(const exl3_weight* w, const exl3_tensor* x, exl3_tp*
   gp.tp_meta_cb = static_cast<uint32_t>(cbb);
   gp.tp_meta_bytes = static_cast<uint32_t>(rows * total * esize);
   const int rg = rows <= 8 ? 1 : 2;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the shard takes the kernel exl3_matmul gives its shape: the persistent GEMV where preferred, else the cluster
+  // split (with the prepare launch from two rows)
+  if (!gp.cw_mask && !gp.mcg && exl3::gemv6_prefers(gp) && exl3::gemv6_scratch_bytes(gp, d->sms) <= d->partial_floats * 4) {
+    if (exl3::launch_gemv6(gp, w->n, d->sms, d->partials, d->counters, st) != cudaSuccess)
+      return refuse(EXL3_FAILED, "exl3_matmul_tp: GEMV launch failed");
+    return kOk;
+  }
   const char* why = nullptr;
   if (!exl3::gemv5_geometry(gp, w->n, d->sms, rg, 0, &why)) return refuse(EXL3_UNSUPPORTED, why);
-  if (exl3::launch_gemv5(gp, w->n, rg, true, static_cast<cudaStream_t>(stream), true) != cudaSuccess)
+  if (rows > kCtaRotateRows && exl3::gemv_prep_bytes(gp, rg) <= d->partial_floats * 4) {
+    if (exl3::launch_gemv_prep(gp, rg, d->partials, st) != cudaSuccess)
+      return refuse(EXL3_FAILED, "exl3_matmul_tp: GEMV launch failed");
+    gp.xf = d->partials;
+  }
+  if (exl3::launch_gemv5(gp, w->n, rg, true, st, true) != cudaSuccess)
     return refuse(EXL3_FAILED, "exl3_matmul_tp: GEMV launch failed");
   return kOk;
 }

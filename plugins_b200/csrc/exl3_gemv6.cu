@@ -213,6 +213,10 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
     if (!waited) {  // the prepared x (and, for the stream, nothing else) comes from the prepare launch
       pdl_wait();
       waited = true;
+      if (p.tp && blockIdx.x == 0 && tid == 0) {  // the slot's size, for this rank's gather (same on every rank)
+        p.tp->meta[p.tp_slot * 4 + 0] = p.tp_meta_cb;
+        p.tp->meta[p.tp_slot * 4 + 1] = p.tp_meta_bytes;
+      }
       if constexpr (!XI) {
         // the x fragments of the units issued before the wait, into their slots (loads batched, then stores)
         const int pre = static_cast<int>(mine < static_cast<uint32_t>(ST - 1) ? mine : static_cast<uint32_t>(ST - 1));
@@ -413,8 +417,37 @@ __global__ void __launch_bounds__(kT6, RG == 1 ? 3 : 2) gemv6_kernel(GemvParams 
 #pragma unroll
         for (int k = 0; k < 4; ++k) v[k] = v[k] * kHadScale * f16_bits_to_float(p.svh[cb * 128 + lane + 32 * k]);
       }
+      if (p.tp) {
+        // column-parallel exchange: the row's 128 outputs through a staging row in the (idle) ring, then 16-byte
+        // stores into this step's slot of every rank (the step's gather publishes them)
+        const TpDev& tp = *p.tp;
+        const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(tp.step);
+        const size_t esize = p.y_dtype == kF32 ? 4 : 2;
+        const size_t slot_off = (static_cast<size_t>(step & 1u) * tp.slots + p.tp_slot) * tp.slot_bytes;
+        int64_t tot = p.tp_total[0], c0 = p.tp_col0[0], sb = p.tp_seg_base[0];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) store_act(p.y, ybase + static_cast<size_t>(cb) * 128 + lane + 32 * k, v[k], p.y_dtype);
+        for (int i = 1; i < kMaxSegments; ++i)
+          if (i == s) {
+            tot = p.tp_total[i];
+            c0 = p.tp_col0[i];
+            sb = p.tp_seg_base[i];
+          }
+        uint8_t* stage = smem + warp * 512u;
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) store_act(stage, lane + 32 * k, v[k], p.y_dtype);
+        __syncwarp();
+        const int64_t col = c0 + (static_cast<int64_t>(cb) * 128 - seg_c0);  // first gathered column of this block
+        const size_t at = static_cast<size_t>(sb + static_cast<int64_t>(p.row0 + row) * tot + col) * esize;
+        if (lane * 16u < 128u * esize) {
+          const uint4 chunk = reinterpret_cast<const uint4*>(stage)[lane];
+          for (int q2 = 0; q2 < tp.world; ++q2) reinterpret_cast<uint4*>(tp.y[q2] + slot_off + at)[lane] = chunk;
+        }
+        __syncwarp();
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) store_act(p.y, ybase + static_cast<size_t>(cb) * 128 + lane + 32 * k, v[k], p.y_dtype);
+      }
     }
     __syncthreads();
   }
@@ -498,7 +531,7 @@ bool gemv6_prefers(const GemvParams& p) {
 
 cudaError_t launch_gemv6(const GemvParams& p, int n, int sms, void* scratch, uint32_t* counters, cudaStream_t st) {
   if (p.cw_mask || p.mcg) return cudaErrorInvalidValue;  // narrowed windows and mcg take the cluster-split GEMV
-  if (p.rows < 1 || p.rows > 16 || p.tp) return cudaErrorInvalidValue;
+  if (p.rows < 1 || p.rows > 16) return cudaErrorInvalidValue;
   const int rg = p.rows <= 8 ? 1 : 2;
   __half* xf = static_cast<__half*>(scratch);
   const size_t xf_bytes = static_cast<size_t>(p.nseg) * p.in_features * 32;

@@ -124,7 +124,10 @@ def test_bench_counts_launches_with_the_librarys_gemv_selection():
     assert b.gemv6_mode(4096, 12288, False, 1) == 0
     assert [b.gemv_kernels(i, o, False, 8) for i, o in ((4096, 24576), (12288, 4096))] == [2, 2]
     assert [b.gemv_kernels(4096, 4096, False, r) for r in (1, 2)] == [1, 2]
-    assert b.gemv_kernels(4096, 24576, True, 1) == 1  # the column-parallel exchange stays on the cluster split
+    # the column-parallel exchange takes its shard's kernel: config 2's gate|up shard at two GPUs on the cluster split
+    # (a prepare launch from two rows), config 5's shard on the persistent GEMV
+    assert [b.gemv_kernels(4096, 12288, True, r) for r in (1, 8)] == [1, 2]
+    assert b.gemv6_mode(16384, 26624, True, 1) == 2 and b.gemv6_mode(4096, 12288, True, 1) == 0
     # the cluster split rotates in-CTA at one row, else takes the prepare launch
     abi = open(os.path.join(root, "plugins_b200", "csrc", "exl3_abi.cu")).read()
     assert b.CTA_ROTATE_ROWS == val(abi, "kCtaRotateRows")

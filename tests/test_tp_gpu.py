@@ -75,6 +75,29 @@ def test_one_rank_exchange_matches_matmul_and_replays():
     ex.close()
 
 
+def test_one_rank_exchange_on_the_persistent_gemv():
+    """Shards whose shape the persistent GEMV serves (a deep narrow one and a wide one) gather through its epilogue:
+    the same bytes as exl3_matmul of the shard at 1, 3 and 8 rows (in-CTA rotation, then the prepare launch)."""
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    from plugins_b200 import sharding as S
+    for in_f, out_f, n in ((12288, 2048, 48), (4096, 24576, 48)):
+        w = Q.weight_from_tensors(*E.random_linear(in_f, out_f, n, seed=320 + out_f))
+        ex = S.TpExchange(0, 1, slots=1, slot_bytes=8 * out_f * 2, max_cb=out_f // 128)
+        out = torch.empty(ex.slot_bytes, dtype=torch.uint8, device="cuda")
+        for rows in (1, 3, 8):
+            x = torch.randn((rows, in_f), device="cuda", dtype=torch.float16)
+            for _ in range(2):  # both parities
+                ex.begin()
+                ex.matmul(w, x, 0, [0], [out_f])
+                ex.gather(0, 1, out)
+                torch.cuda.synchronize()
+                got = out[:rows * out_f * 2].view(torch.float16).view(rows, out_f)
+                assert torch.equal(got, Q.matmul(w, x)), (in_f, out_f, rows)
+        assert Q.device_error(0) == 0
+        ex.close()
+
+
 def test_one_rank_timeline_stamps_each_phase_in_order(monkeypatch):
     """EXL3_TRACE=1 at create: each step's four stamps (begin, publish, every rank seen, gathered) come back oldest
     step first and in order; an exchange made without it refuses the read by name."""
