@@ -375,8 +375,14 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
         break;
       }
   }
-  if (kept) {
-    nc_cap = (static_cast<int64_t>(out_f) + bn - 1) / bn * bn;  // no column chunks: the B image is the kept one
+  // W_hat^T decoded inside the GEMM (no B image; the same bytes): taken on request (EXL3_GEMM_FUSED=1) for the full
+  // mul1 window without a kept image.  Measured on config 3's layer at 64 / 128 / 256 rows it is not the default: its
+  // 128-column tiles keep 96 of the 148 SMs decoding (68.8 / 71.2 / 85.7 us against the image path's 63.6 / 66.5 /
+  // 74.8); the routed experts' prefill, whose tiles fill every SM, takes it by default (exl3_moe_prefill.cu)
+  const char* fz = getenv("EXL3_GEMM_FUSED");
+  const bool fused = !kept && !cw_mask && !mcg && fz && atoi(fz) == 1;
+  if (kept || fused) {
+    nc_cap = (static_cast<int64_t>(out_f) + bn - 1) / bn * bn;  // no column chunks: no B image (or the kept one)
     for (int g = 0; fill && g < gcount; ++g)
       if (exl3::launch_images(nullptr, x_dtype, 0, 0, 0, nullptr, 0, nullptr, w->trellis + static_cast<size_t>(g) * tile_halfs,
                               in_f, out_f, 0, out_f, w->n, kept + static_cast<size_t>(g) * kept_group, st,
@@ -409,10 +415,13 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
           // the A image with the first column chunk's B image, in one launch
           if (exl3::launch_images(xg + static_cast<size_t>(r0) * x_stride * xsz, x_dtype, x_stride, m, mp, suh,
                                   (flags & EXL3_MATMUL_PREPARED) ? 1 : 0, j0 == 0 ? a_img : nullptr, trg, in_f, out_f,
-                                  c0 + j0, nc, w->n, kept ? nullptr : b_img, st, cw_mask, mcg) != cudaSuccess)
+                                  c0 + j0, nc, w->n, (kept || fused) ? nullptr : b_img, st, cw_mask, mcg) != cudaSuccess)
             return refuse(EXL3_FAILED, "exl3_b200: prefill operand images launch failed");
           mark(1);
-          const int shape = gemm_shape_for(m, nc, d->sms);
+          // fused: 128 or 256-row tiles (above 256 rows each row tile decodes its B blocks again), 128-column tiles to
+          // spread the decode over more SMs unless the columns fill them twice over
+          const int shape = fused ? (m > 128 ? 2 : 0) + (nc % 256 == 0 && nc / 128 >= 2 * d->sms ? 1 : 0)
+                                  : gemm_shape_for(m, nc, d->sms);
           const int tbm = exl3::gemm_block_m(shape), tbn = exl3::gemm_block_n(shape);
           exl3::GemmParams gp{};
           gp.a_img = a_img;
@@ -431,7 +440,15 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
           gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
           gp.vec_store = (reinterpret_cast<uintptr_t>(yp) % 16 == 0 && (ystride * ysz) % 16 == 0) ? 1 : 0;
           gp.err = d->err;
-          if (exl3::launch_gemm_image(gp, shape, d->sms, st) != cudaSuccess)
+          if (fused) {
+            gp.b_img = nullptr;
+            gp.trellis = trg;
+            gp.out_tiles = out_f / 16;
+            gp.tn0 = (c0 + j0) / 16;
+            gp.n = w->n;
+          }
+          if ((fused ? exl3::launch_gemm_fused(gp, shape, d->sms, st) : exl3::launch_gemm_image(gp, shape, d->sms, st)) !=
+              cudaSuccess)
             return refuse(EXL3_FAILED, "exl3_b200: prefill GEMM launch failed");
           mark(2);
           first = false;

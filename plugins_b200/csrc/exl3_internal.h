@@ -236,6 +236,12 @@ struct GemmParams {
   int64_t svh_group;
   const uint16_t* svh2;
   int32_t svh_split;
+  // the decode-in-the-GEMM form (launch_gemm_fused; b_img unused): W_hat^T blocks decoded from the trellis into shared
+  // memory at every k-step; the launch's columns start at tile column tn0 of a weight of out_tiles tile columns and n
+  // halfwords per tile; grouped, block b's expert e = m_group[b] has its trellis at trellis + (e - group0) * tr_group
+  const uint16_t* trellis;
+  int64_t tr_group;
+  int32_t out_tiles, tn0, n;
 };
 
 // One launch writes the A image of xp rows [0, mp) (rows >= m are zeros; prepared = x already holds xp; skipped when
@@ -274,6 +280,10 @@ cudaError_t launch_moe_b_images(const uint16_t* trellis, int in_features, int ou
 int gemm_block_m(int shape);
 int gemm_block_n(int shape);
 cudaError_t launch_gemm_image(const GemmParams& p, int shape, int sms, cudaStream_t st);
+// The same GEMM with W_hat^T decoded inside it (exl3_gemm_fused.cu): eight decode warps fill each k-step's B block in
+// shared memory from the trellis, so no B image is written or read.  Shapes 0..3 as above (256-row blocks for the
+// dense launch only), the full 16-bit mul1 window only.
+cudaError_t launch_gemm_fused(const GemmParams& p, int shape, int sms, cudaStream_t st);
 
 // the device error word of the current device (exl3_device_error reads it), or null
 uint32_t* device_error_ptr();

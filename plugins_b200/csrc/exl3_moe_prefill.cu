@@ -16,6 +16,8 @@
 // The images and GEMMs are the prefill linear's (exl3_gemm.cu), with a per-block expert for the B image and svh.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include <cstdint>
 #include <mutex>
 
@@ -38,6 +40,7 @@ struct Prefill {
   int32_t *counts, *cursor, *base_row, *m_group, *row_slot, *pos, *rows_total;
   int32_t* ranges;  // [groups][2]: each group of experts' rows
   int32_t* blocks;  // [groups][2]: the same as 128-row blocks (the GEMMs' device range)
+  int32_t* all;     // [4]: every block {0, blocks} and every row {0, rows} of the call (the one-pass form)
   uint8_t *a_g, *a_u, *a_d, *b_g, *b_u, *b_d;
   float* gu;   // [rows_max][2 inter] f32; the down GEMM's output reuses it ([rows_max][hidden])
   int64_t gu_stride;
@@ -71,6 +74,7 @@ size_t layout(Prefill& f, uint8_t* b) {
   f.rows_total = reinterpret_cast<int32_t*>(take(4));
   f.ranges = reinterpret_cast<int32_t*>(take(8 * static_cast<size_t>(groups)));
   f.blocks = reinterpret_cast<int32_t*>(take(8 * static_cast<size_t>(groups)));
+  f.all = reinterpret_cast<int32_t*>(take(16));
   f.a_g = take(R * f.hidden * 2);
   f.a_u = take(R * f.hidden * 2);
   f.a_d = take(R * f.inter * 2);
@@ -151,6 +155,14 @@ __global__ void pf_place_kernel(Prefill f, const void* inds, int inds_u32, int64
 __global__ void pf_blocks_kernel(const int32_t* ranges, int32_t* mt) {
   mt[0] = ranges[0] / 128;
   mt[1] = ranges[1] / 128;
+}
+
+// The call's whole range: blocks {0, rows / 128}, rows {0, rows} (rows: the padded total the layout wrote).
+__global__ void pf_all_kernel(const int32_t* rows_total, int32_t* all) {
+  all[0] = 0;
+  all[1] = *rows_total / 128;
+  all[2] = 0;
+  all[3] = *rows_total;
 }
 
 // y[t] = sum_k score[t, k] * out[pos(t, k)], k in order; grid (hidden / 512, up to 64 row columns), 128 threads of
@@ -269,8 +281,67 @@ exl3_verdict moe_prefill_run(const exl3_weight* gate, const exl3_weight* up, con
   mi.a_g = f.a_g, mi.a_u = f.a_u, mi.a_d = f.a_d;
   mi.gu = f.gu, mi.gu_stride = f.gu_stride, mi.limit = limit;
   if (err == cudaSuccess) ok(launch_moe_a_images(mi, f.sms, st));
+  // the full mul1 window: W_hat^T decoded inside the GEMMs, all experts in one pass (gate, up, the SwiGLU into down's
+  // A image, down); EXL3_GEMM_FUSED=0 keeps the image form for measurement
+  const char* fz = getenv("EXL3_GEMM_FUSED");
+  const bool fused = !cw_gu && !cw_d && !mcg_gu && !mcg_d && !(fz && atoi(fz) == 0);
+  if (fused && err == cudaSuccess) {
+    pf_all_kernel<<<1, 1, 0, st>>>(f.rows_total, f.all);
+    ok(cudaGetLastError());
+    for (int w = 0; w < 2 && err == cudaSuccess; ++w) {
+      const exl3_weight* wt = w == 0 ? gate : up;
+      GemmParams gp{};
+      gp.a_img = w == 0 ? f.a_g : f.a_u;
+      gp.svh = wt->svh;
+      gp.y = f.gu + (w == 0 ? 0 : inter);
+      gp.y_dtype = kF32;
+      gp.y_row_stride = f.gu_stride;
+      gp.m = f.rows_max;
+      gp.ncols = inter;
+      gp.tiles_m = f.rows_max / 128;
+      gp.tiles_n = inter % 256 == 0 ? inter / 256 : inter / 128;
+      gp.kb = hidden / 64;
+      gp.vec_store = 1;
+      gp.err = device_error_ptr();
+      gp.mt_range = f.all;
+      gp.m_group = f.m_group;
+      gp.group0 = 0;
+      gp.svh_group = inter;
+      gp.trellis = wt->trellis;
+      gp.tr_group = static_cast<int64_t>(hidden / 16) * (inter / 16) * wt->n;
+      gp.out_tiles = inter / 16;
+      gp.tn0 = 0;
+      gp.n = wt->n;
+      ok(launch_gemm_fused(gp, inter % 256 == 0 ? 1 : 0, f.sms, st));
+    }
+    mi.row_range = f.all + 2;
+    if (err == cudaSuccess) ok(launch_moe_mid_images(mi, f.sms, st));
+    GemmParams gd{};
+    gd.a_img = f.a_d;
+    gd.svh = down->svh;
+    gd.y = f.gu;  // the gate|up outputs are consumed: down's rows overwrite them
+    gd.y_dtype = kF32;
+    gd.y_row_stride = f.gu_stride;
+    gd.m = f.rows_max;
+    gd.ncols = hidden;
+    gd.tiles_m = f.rows_max / 128;
+    gd.tiles_n = hidden % 256 == 0 ? hidden / 256 : hidden / 128;
+    gd.kb = inter / 64;
+    gd.vec_store = 1;
+    gd.err = device_error_ptr();
+    gd.mt_range = f.all;
+    gd.m_group = f.m_group;
+    gd.group0 = 0;
+    gd.svh_group = hidden;
+    gd.trellis = down->trellis;
+    gd.tr_group = static_cast<int64_t>(inter / 16) * (hidden / 16) * down->n;
+    gd.out_tiles = hidden / 16;
+    gd.tn0 = 0;
+    gd.n = down->n;
+    if (err == cudaSuccess) ok(launch_gemm_fused(gd, hidden % 256 == 0 ? 1 : 0, f.sms, st));
+  }
   // per group of experts: B images, the gate and up GEMMs, the SwiGLU into down's A image, down's B images and GEMM
-  const int groups = (E + kGroupExperts - 1) / kGroupExperts;
+  const int groups = fused ? 0 : (E + kGroupExperts - 1) / kGroupExperts;
   const int64_t bimg = static_cast<int64_t>(hidden) * inter * 2;
   for (int g = 0; g < groups && err == cudaSuccess; ++g) {
     const int e0 = g * kGroupExperts, cnt = E - e0 < kGroupExperts ? E - e0 : kGroupExperts;

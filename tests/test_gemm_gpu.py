@@ -103,6 +103,46 @@ def test_gemm_against_f32_truth(Q, E, oracle, shape, in_f, out_f, n, rows, dtype
     assert Q.device_error(0, clear=True) == 0
 
 
+@pytest.mark.parametrize("in_f,out_f,n,rows", [
+    (4096, 12288, 64, 64),    # config 3's layer at the crossover's smallest width: 128-column tiles, one 128-row block
+    (1024, 640, 48, 200),     # two 128-row blocks in one tile, a ragged last row block
+    (512, 768, 88, 256),
+    (768, 512, 24, 100),      # a half-bit rate
+])
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
+def test_decode_in_the_gemm_gives_the_image_paths_bytes(Q, E, monkeypatch, in_f, out_f, n, rows, dtype):
+    # the GEMM that decodes W_hat^T into shared memory itself (no B image; EXL3_GEMM_FUSED=1): the same tiles, the
+    # same MMA k order and the same output Hadamard make it byte-for-byte the decode-into-an-image path
+    dt = getattr(torch, dtype)
+    tr, suh, svh = E.random_linear(in_f, out_f, n, seed=in_f + rows + n)
+    w = Q.weight_from_tensors(tr, suh, svh)
+    x = (torch.randn((rows, in_f), generator=torch.Generator().manual_seed(rows)) * 3).to(dt).cuda()
+    monkeypatch.setenv("EXL3_GEMM_FUSED", "1")
+    fused = Q.matmul(w, x)
+    monkeypatch.delenv("EXL3_GEMM_FUSED")
+    image = Q.matmul(w, x)
+    torch.cuda.synchronize()
+    assert Q.device_error(0, clear=True) == 0
+    assert torch.equal(fused.view(-1).view(torch.uint8), image.view(-1).view(torch.uint8))
+
+
+def test_decode_in_the_gemm_stacked_and_forced_past_256_rows(Q, E, oracle, monkeypatch):
+    # a stacked q|k|v-like weight (three segments, each its own svh slice) through the fused form, and 300 rows forced
+    # through it (two 256-row tiles, each decoding its B blocks again), against the truth
+    segs = [E.random_linear(512, o, 64, seed=90 + o) for o in (512, 256, 256)]
+    w = Q.stack([Q.weight_from_tensors(*s_) for s_ in segs])
+    x = (torch.randn((300, 512), generator=torch.Generator().manual_seed(5)) * 2).half().cuda()
+    monkeypatch.setenv("EXL3_GEMM_FUSED", "1")
+    y = Q.matmul(w, x)
+    monkeypatch.delenv("EXL3_GEMM_FUSED")
+    y0 = Q.matmul(w, x)
+    assert torch.equal(y.view(torch.int16), y0.view(torch.int16))
+    for s_, want_y in zip(segs, Q.segment_outputs(w, y, 300)):
+        want = _truth(oracle, x, s_[0], s_[1], s_[2], 512, s_[0].shape[1] * 16, 64)
+        assert _rel(want_y.float().cpu().numpy(), want) < REL_L2_BAR
+    assert Q.device_error(0, clear=True) == 0
+
+
 def test_gemm_and_gemv_agree(Q, E, oracle):
     # the same rows forced through either path land within the bar of each other and of the truth
     in_f, out_f, n, rows = 1024, 1536, 48, 96

@@ -301,6 +301,32 @@ def test_moe_prefill_against_truth_and_the_decode_chain(oracle, experts, hidden,
         Q.moe_prefill_reserve(experts, hidden, inter, 0)
 
 
+def test_moe_prefill_decode_in_the_gemm_gives_the_image_paths_bytes(monkeypatch):
+    # the routed experts' prefill decodes every expert's W_hat^T inside its grouped GEMMs (one pass over all experts);
+    # the per-group image form (EXL3_GEMM_FUSED=0) gives the same bytes
+    from plugins_b200 import encoder as E
+    from plugins_b200 import quant as Q
+    experts, hidden, inter, topk, rows = 12, 512, 768, 4, 400
+    banks = [_bank(E, experts, hidden, inter, 48, 500), _bank(E, experts, hidden, inter, 48, 501),
+             _bank(E, experts, inter, hidden, 40, 502)]
+    wg, wu, wd = (Q.weight_from_tensors(*b) for b in banks)
+    Q.moe_prefill_reserve(experts, hidden, inter, rows * topk)
+    try:
+        ind, sc = _route(rows, experts, topk, 11)
+        x = torch.randn((1, rows, hidden), generator=torch.Generator().manual_seed(11)).half().cuda()
+        i3, s3 = ind.view(1, rows, topk).cuda(), sc.view(1, rows, topk).cuda()
+        monkeypatch.delenv("EXL3_GEMM_FUSED", raising=False)
+        y = Q.swiglu(wg, wu, wd, x, i3, s3, limit=5)
+        monkeypatch.setenv("EXL3_GEMM_FUSED", "0")
+        y0 = Q.swiglu(wg, wu, wd, x, i3, s3, limit=5)
+        monkeypatch.delenv("EXL3_GEMM_FUSED")
+        torch.cuda.synchronize()
+        assert Q.device_error(0, clear=True) == 0
+        assert torch.equal(y.view(torch.int16), y0.view(torch.int16))
+    finally:
+        Q.moe_prefill_reserve(experts, hidden, inter, 0)
+
+
 def test_moe_prefill_config4_widths_2048_tokens_top8(oracle):
     # config 4's expert widths (4096 <-> 2048 at 3 bpw) at a 2048-token prompt, top-8 of 64 experts; 24 tokens checked
     # against the truth on their own rows
