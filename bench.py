@@ -307,8 +307,9 @@ def measure_moe_prefill(Q, E, torch, peaks: dict, tokens: int = 2048, reps: int 
                         "@ 3 bpw, top-8 + the shared slot, bf16",
             "value": round(tf, 1), "unit": "TFLOP/s", "ms": round(ms, 4), "flops_per_call": flops,
             "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4), "workspace_bytes": ws,
-            "path": "slots sorted into per-expert 128-row blocks; experts' W_hat^T decoded once per call (32 at a "
-                    "time); grouped tcgen05 GEMMs for gate, up and down; SwiGLU between (exl3_moe_prefill.cu)"}
+            "path": "slots sorted into per-expert 128-row blocks; grouped tcgen05 GEMMs for gate, up and down with "
+                    "each block's expert W_hat^T decoded inside the GEMM (no operand image); SwiGLU between "
+                    "(exl3_moe_prefill.cu, exl3_gemm_fused.cu)"}
 
 
 def measure_moe_ep(Q, E, torch, dist, rank: int, world: int, device, peaks: dict, steps: int = 20) -> dict:
