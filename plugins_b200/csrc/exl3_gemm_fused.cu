@@ -130,6 +130,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) gemm_fused_kernel(const Gemm
     tiles_m = p.mt_range[1] - mt0;
   }
   const int tiles = tiles_m * p.tiles_n;
+  // output tile t's M and N blocks.  Grouped launches walk an M block's N blocks together: the CTAs of one wave then
+  // share its A rows through L2 (read from HBM once, not once per N block) and an expert's trellis columns are read
+  // by its M blocks in the same wave.  Plain launches walk the M blocks first (A is small and stays in L2).
+  const bool n_inner = p.m_group != nullptr;
+  auto tile_mb = [&](int t) { return mt0 + (n_inner ? t / p.tiles_n : t % tiles_m); };
+  auto tile_nb = [&](int t) { return n_inner ? t % p.tiles_n : t / tiles_m; };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -138,7 +144,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) gemm_fused_kernel(const Gemm
       uint32_t stage = 0, phase = 0, fills = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-        const int mb = mt0 + t % tiles_m;
+        const int mb = tile_mb(t);
         for (int kb = 0; kb < p.kb; ++kb) {
           if (!role_wait(&empty[stage], phase ^ 1u, abort_flag, p.err)) {
             ok = false;
@@ -215,7 +221,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) gemm_fused_kernel(const Gemm
       const uint32_t aph = S::kAccBufs == 2 ? ((local >> 1) & 1) : (local & 1);
       if (!role_wait(&accf[ab], aph, abort_flag, p.err)) break;
       tc_fence_after();
-      const int mb = mt0 + t % tiles_m, nb = t / tiles_m;
+      const int mb = tile_mb(t), nb = tile_nb(t);
       const int64_t sv_e = p.m_group ? static_cast<int64_t>(p.m_group[mb]) * p.svh_group : 0;
 #pragma unroll 1
       for (int s = 0; s < MS; ++s) {
@@ -334,7 +340,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) gemm_fused_kernel(const Gemm
     uint32_t it_slot = 0;
     const uint16_t* it_base = nullptr;
     auto tile_base = [&](int t) {
-      const int mb = mt0 + t % tiles_m, nb = t / tiles_m;
+      const int mb = tile_mb(t), nb = tile_nb(t);
       const uint16_t* tr = p.trellis + (p.m_group ? static_cast<int64_t>(p.m_group[mb] - p.group0) * p.tr_group : 0);
       const int tn = p.tn0 + nb * NS * 8 + static_cast<int>(hf) * S::kTilesPerWarp;
       return tr + (static_cast<size_t>(kk) * p.out_tiles + tn) * N;  // k-step 0's tiles; + kb 4 out_tiles N per step

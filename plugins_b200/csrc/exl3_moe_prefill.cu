@@ -79,9 +79,10 @@ size_t layout(Prefill& f, uint8_t* b) {
   f.a_u = take(R * f.hidden * 2);
   f.a_d = take(R * f.inter * 2);
   const size_t bimg = static_cast<size_t>(f.hidden) * f.inter * 2;  // one expert's W_hat^T, f16
-  f.b_g = take(kGroupExperts * bimg);
-  f.b_u = take(kGroupExperts * bimg);
-  f.b_d = take(kGroupExperts * bimg);
+  const size_t ge = E < kGroupExperts ? E : kGroupExperts;            // a group's experts at most
+  f.b_g = take(ge * bimg);
+  f.b_u = take(ge * bimg);
+  f.b_d = take(ge * bimg);
   f.gu = reinterpret_cast<float*>(take(R * static_cast<size_t>(f.gu_stride) * 4));
   return at;
 }
