@@ -155,11 +155,12 @@ __global__ void __launch_bounds__(256) images_kernel(const ImageJobs j) {
 // (row_slot[row] = token * topk + k, or -1 for padding; m_group[row / 128] = the block's expert).  The A images hold
 // the gate- and up-prepared rows (x read once per job, rotated twice), the down input's A image the SwiGLU of the
 // gate|up GEMMs' outputs prepared for down; B images are each expert's decoded W_hat^T, as for a single linear.
+// Padding rows are never written: a GEMM output row depends only on its own A row, and a padding row's outputs are
+// neither read by the SwiGLU nor combined, so whatever its A row holds reaches no real row's bytes.
 
-// xp = f16-ready H128(v * suh) / sqrt(128) of one warp's 128 inputs (lane t: elements 4t .. 4t + 3), the two low
-// stages in registers, the other five across lanes (prep_job's arithmetic).
-__device__ __forceinline__ void rotate128(float (&v)[4], const uint16_t* suh, uint32_t lane) {
-  const uint2 su = *reinterpret_cast<const uint2*>(suh);
+// xp = f16-ready H128(v * suh) / sqrt(128) of one warp's 128 inputs (lane t: elements 4t .. 4t + 3, su its four suh
+// halves), the two low stages in registers, the other five across lanes (prep_job's arithmetic).
+__device__ __forceinline__ void rotate128(float (&v)[4], uint2 su, uint32_t lane) {
   const float2 s01 = __half22float2(*reinterpret_cast<const __half2*>(&su.x));
   const float2 s23 = __half22float2(*reinterpret_cast<const __half2*>(&su.y));
   v[0] *= s01.x, v[1] *= s01.y, v[2] *= s23.x, v[3] *= s23.y;
@@ -185,49 +186,91 @@ __device__ __forceinline__ void store_image4(uint8_t* img, int kblocks64, int ro
       make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
 }
 
-// One warp per (padded row, 128-input block), grid-stride over the call's rows (a device count).
+// x[i .. i + 3] as f32 (exact conversions, as load_act): one 8-byte (f16, bf16) or 16-byte (f32) load when the
+// caller's rows are aligned for it (vec), else four element loads.
+__device__ __forceinline__ void load_act4(const void* p, size_t i, int32_t dt, bool vec, float (&v)[4]) {
+  if (vec && dt == kF32) {
+    const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+  } else if (vec) {
+    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + i);
+    float2 lo, hi;
+    if (dt == kF16) {
+      lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    } else {
+      lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    }
+    v[0] = lo.x, v[1] = lo.y, v[2] = hi.x, v[3] = hi.y;
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = load_act(p, i + q, dt);
+  }
+}
+
+// One warp per (row, KB consecutive 128-input blocks), grid-stride over the call's rows (a device count).  The KB
+// blocks' loads are issued before the first rotation: one block per warp left the kernel waiting on each load in turn.
+template <int KB>
 __global__ void __launch_bounds__(256) moe_a_images_kernel(const MoeImages j) {
   const uint32_t lane = threadIdx.x & 31u;
-  const int kblk = j.hidden / 128;
-  const int64_t jobs = static_cast<int64_t>(*j.rows_total) * kblk;
+  const int groups = j.hidden / (128 * KB);
+  const int64_t jobs = static_cast<int64_t>(*j.rows_total) * groups;
   for (int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); job < jobs;
        job += static_cast<int64_t>(gridDim.x) * 8) {
-    const int row = static_cast<int>(job / kblk), b = static_cast<int>(job % kblk);
-    const int k0 = b * 128 + 4 * static_cast<int>(lane);
+    const int row = static_cast<int>(job / groups);
     const int slot = j.row_slot[row];
-    float vg[4] = {0.f, 0.f, 0.f, 0.f}, vu[4] = {0.f, 0.f, 0.f, 0.f};
-    if (slot >= 0) {  // (warp-uniform)
-      const size_t at = static_cast<size_t>(slot / j.topk) * j.x_row_stride + k0;
+    if (slot < 0) continue;  // (warp-uniform) padding
+    const int k0 = static_cast<int>(job % groups) * KB * 128 + 4 * static_cast<int>(lane);
+    const size_t e = static_cast<size_t>(j.m_group[row >> 7]);
+    const size_t at = static_cast<size_t>(slot / j.topk) * j.x_row_stride + k0;
+    float v[KB][4];
+    uint2 sg[KB], su[KB];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) vg[i] = load_act(j.x, at + i, j.x_dtype);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) vu[i] = vg[i];
-      const size_t e = static_cast<size_t>(j.m_group[row >> 7]);
-      rotate128(vg, j.suh_g + e * j.hidden + k0, lane);
-      rotate128(vu, j.suh_u + e * j.hidden + k0, lane);
+    for (int b = 0; b < KB; ++b) {
+      load_act4(j.x, at + b * 128, j.x_dtype, j.x_vec != 0, v[b]);
+      sg[b] = *reinterpret_cast<const uint2*>(j.suh_g + e * j.hidden + k0 + b * 128);
+      su[b] = *reinterpret_cast<const uint2*>(j.suh_u + e * j.hidden + k0 + b * 128);
     }
-    store_image4(j.a_g, j.hidden / kImgK, row, k0, vg);
-    store_image4(j.a_u, j.hidden / kImgK, row, k0, vu);
+#pragma unroll
+    for (int b = 0; b < KB; ++b) {
+      float vg[4] = {v[b][0], v[b][1], v[b][2], v[b][3]};
+      rotate128(vg, sg[b], lane);
+      store_image4(j.a_g, j.hidden / kImgK, row, k0 + b * 128, vg);
+      rotate128(v[b], su[b], lane);
+      store_image4(j.a_u, j.hidden / kImgK, row, k0 + b * 128, v[b]);
+    }
   }
 }
 
 // The down input: h = silu(g) * u of the gate|up GEMMs' f32 outputs (g, u: columns [0, inter) and [inter, 2 inter)
 // of gu), clamped as the routed experts' epilogue clamps, times the down bank's suh, rotated, f16 -- one warp per
-// (row, 128-block) of the rows [row_range[0], row_range[1]).
+// (row, KB 128-blocks) of the rows [row_range[0], row_range[1]), loads first as above.
+template <int KB>
 __global__ void __launch_bounds__(256) moe_mid_images_kernel(const MoeImages j) {
   const uint32_t lane = threadIdx.x & 31u;
-  const int kblk = j.inter / 128;
+  const int groups = j.inter / (128 * KB);
   const int r0 = j.row_range[0];
-  const int64_t jobs = static_cast<int64_t>(j.row_range[1] - r0) * kblk;
+  const int64_t jobs = static_cast<int64_t>(j.row_range[1] - r0) * groups;
   for (int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); job < jobs;
        job += static_cast<int64_t>(gridDim.x) * 8) {
-    const int row = r0 + static_cast<int>(job / kblk), b = static_cast<int>(job % kblk);
-    const int k0 = b * 128 + 4 * static_cast<int>(lane);
-    float h[4] = {0.f, 0.f, 0.f, 0.f};
-    if (j.row_slot[row] >= 0) {
-      const float4 g = *reinterpret_cast<const float4*>(j.gu + static_cast<size_t>(row) * j.gu_stride + k0);
-      const float4 u = *reinterpret_cast<const float4*>(j.gu + static_cast<size_t>(row) * j.gu_stride + j.inter + k0);
-      const float gv[4] = {g.x, g.y, g.z, g.w}, uv0[4] = {u.x, u.y, u.z, u.w};
+    const int row = r0 + static_cast<int>(job / groups);
+    if (j.row_slot[row] < 0) continue;  // (warp-uniform) padding
+    const int k0 = static_cast<int>(job % groups) * KB * 128 + 4 * static_cast<int>(lane);
+    const size_t e = static_cast<size_t>(j.m_group[row >> 7]);
+    const float* gr = j.gu + static_cast<size_t>(row) * j.gu_stride + k0;
+    float4 g[KB], u[KB];
+    uint2 sd[KB];
+#pragma unroll
+    for (int b = 0; b < KB; ++b) {
+      g[b] = *reinterpret_cast<const float4*>(gr + b * 128);
+      u[b] = *reinterpret_cast<const float4*>(gr + j.inter + b * 128);
+      sd[b] = *reinterpret_cast<const uint2*>(j.suh_d + e * j.inter + k0 + b * 128);
+    }
+#pragma unroll
+    for (int b = 0; b < KB; ++b) {
+      const float gv[4] = {g[b].x, g[b].y, g[b].z, g[b].w}, uv0[4] = {u[b].x, u[b].y, u[b].z, u[b].w};
+      float h[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         float gi = gv[i], ui = uv0[i];
@@ -238,10 +281,9 @@ __global__ void __launch_bounds__(256) moe_mid_images_kernel(const MoeImages j) 
         const float sig = 1.0f / (1.0f + __expf(-gi));
         h[i] = gi * sig * ui;
       }
-      const size_t e = static_cast<size_t>(j.m_group[row >> 7]);
-      rotate128(h, j.suh_d + e * j.inter + k0, lane);
+      rotate128(h, sd[b], lane);
+      store_image4(j.a_d, j.inter / kImgK, row, k0 + b * 128, h);
     }
-    store_image4(j.a_d, j.inter / kImgK, row, k0, h);
   }
 }
 
@@ -523,13 +565,15 @@ cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, 
 
 cudaError_t launch_moe_a_images(const MoeImages& j, int sms, cudaStream_t st) {
   if (j.hidden % 128 != 0) return cudaErrorInvalidValue;
-  moe_a_images_kernel<<<sms * 8, 256, 0, st>>>(j);
+  if (j.hidden % 512 == 0) moe_a_images_kernel<4><<<sms * 8, 256, 0, st>>>(j);
+  else moe_a_images_kernel<1><<<sms * 8, 256, 0, st>>>(j);
   return cudaGetLastError();
 }
 
 cudaError_t launch_moe_mid_images(const MoeImages& j, int sms, cudaStream_t st) {
   if (j.inter % 128 != 0) return cudaErrorInvalidValue;
-  moe_mid_images_kernel<<<sms * 8, 256, 0, st>>>(j);
+  if (j.inter % 512 == 0) moe_mid_images_kernel<4><<<sms * 8, 256, 0, st>>>(j);
+  else moe_mid_images_kernel<1><<<sms * 8, 256, 0, st>>>(j);
   return cudaGetLastError();
 }
 

@@ -366,6 +366,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) gemm_fused_kernel(const Gemm
       issue();
       cp_commit_f();
     }
+    // this lane's image offset in the stage for its first tile.  A warp's tiles never straddle a 128-column block
+    // (kTilesPerWarp divides 8) and every tile row of the lane has row & 7 == g, so tile t's two rows sit t * 2048
+    // and t * 2048 + 1024 bytes further: the swizzle is computed once, not twice per tile.
+    static_assert(8 % S::kTilesPerWarp == 0, "a warp's tiles stay inside one 128-column block");
+    const uint32_t t0 = hf * S::kTilesPerWarp;
+    const uint32_t lane_off = (t0 >> 3) * kImgBytes + (t0 & 7u) * 2048u + image_offset(g, kk * 16u + 4u * q);
     uint32_t stage = 0, phase = 0, slot_use = 0;
 #pragma unroll 1
     for (int i = 0; i < items; ++i) {
@@ -374,18 +380,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) gemm_fused_kernel(const Gemm
       if (!warp_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, lane)) break;
       const uint32_t* tw = reinterpret_cast<const uint32_t*>(ring + slot_use * S::kSlotBytes);
       slot_use = slot_use + 1u == static_cast<uint32_t>(kTrStages) ? 0u : slot_use + 1u;
-      uint8_t* bst = stages + stage * S::kStageBytes + MS * kImgBytes;
-      const uint32_t kin = kk * 16u + 4u * q;
+      uint8_t* bst = stages + stage * S::kStageBytes + MS * kImgBytes + lane_off;
 #pragma unroll
       for (int t = 0; t < S::kTilesPerWarp; ++t) {
         uint32_t w[8], a[4];
         tile_codewords<N>(tw + t * (N / 2), lw, w);
-        decode_afrag_imma(w, ind, a);  // a[0], a[2]: column g at k 4q .. 4q + 3; a[1], a[3]: column g + 8
-        const uint32_t tnl = hf * S::kTilesPerWarp + static_cast<uint32_t>(t);  // tile column within the stage's BN
-        const uint32_t n = (tnl & 7u) * 16u + g;
-        uint8_t* blk = bst + (tnl >> 3) * kImgBytes;
-        *reinterpret_cast<uint2*>(blk + image_offset(n, kin)) = make_uint2(a[0], a[2]);
-        *reinterpret_cast<uint2*>(blk + image_offset(n + 8u, kin)) = make_uint2(a[1], a[3]);
+        // a[0], a[2]: column g at k 4q .. 4q + 3; a[1], a[3]: column g + 8.  The f16 pairs are packed on the FMA
+        // pipe: the window extraction loads the ALU pipe (measured on B200: 2 % on the routed experts' prefill).
+        decode_afrag_imma<true>(w, ind, a);
+        *reinterpret_cast<uint2*>(bst + t * 2048u) = make_uint2(a[0], a[2]);
+        *reinterpret_cast<uint2*>(bst + t * 2048u + 1024u) = make_uint2(a[1], a[3]);
       }
       fence_proxy_async_smem();
       __syncwarp();

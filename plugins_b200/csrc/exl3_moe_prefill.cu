@@ -166,24 +166,35 @@ __global__ void pf_all_kernel(const int32_t* rows_total, int32_t* all) {
   all[3] = *rows_total;
 }
 
-// y[t] = sum_k score[t, k] * out[pos(t, k)], k in order; grid (hidden / 512, up to 64 row columns), 128 threads of
-// four columns.
+// y[t] = sum_k score[t, k] * out[pos(t, k)], k in order; grid (hidden / 512, up to 65535 token columns), 128 threads
+// of four columns.  Up to eight slots a token: their rows are loaded together, then summed in k order (one load in
+// flight per thread had left the kernel waiting on each in turn).
 __global__ void __launch_bounds__(128) pf_combine_kernel(const float* out, int64_t stride, const int32_t* pos,
                                                          const float* scores, int64_t rows, int topk, int hidden,
                                                          void* y, int32_t y_dtype) {
+  constexpr int kBatch = 8;
   const int c = (static_cast<int>(blockIdx.x) * 128 + static_cast<int>(threadIdx.x)) * 4;
   if (c >= hidden) return;
   for (int64_t t = blockIdx.y; t < rows; t += gridDim.y) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k = 0; k < topk; ++k) {
-      const int r = pos[t * topk + k];
-      if (r < 0) continue;
-      const float sc = scores[t * topk + k];
-      const float4 d = *reinterpret_cast<const float4*>(out + static_cast<size_t>(r) * stride + c);
-      acc[0] += sc * d.x;
-      acc[1] += sc * d.y;
-      acc[2] += sc * d.z;
-      acc[3] += sc * d.w;
+    for (int k0 = 0; k0 < topk; k0 += kBatch) {
+      float4 d[kBatch];
+      float sc[kBatch];
+      int r[kBatch];
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        r[i] = k0 + i < topk ? pos[t * topk + k0 + i] : -1;
+        sc[i] = r[i] >= 0 ? scores[t * topk + k0 + i] : 0.f;
+        if (r[i] >= 0) d[i] = *reinterpret_cast<const float4*>(out + static_cast<size_t>(r[i]) * stride + c);
+      }
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (r[i] < 0) continue;
+        acc[0] += sc[i] * d[i].x;
+        acc[1] += sc[i] * d[i].y;
+        acc[2] += sc[i] * d[i].z;
+        acc[3] += sc[i] * d[i].w;
+      }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) store_act(y, static_cast<size_t>(t) * hidden + c + i, acc[i], y_dtype);
@@ -278,6 +289,10 @@ exl3_verdict moe_prefill_run(const exl3_weight* gate, const exl3_weight* up, con
   MoeImages mi{};
   mi.row_slot = f.row_slot, mi.m_group = f.m_group, mi.rows_total = f.rows_total, mi.topk = topk;
   mi.x = x->data, mi.x_dtype = x->dtype, mi.x_row_stride = hidden, mi.hidden = hidden, mi.inter = inter;
+  {
+    const size_t esz = x->dtype == EXL3_F32 ? 4 : 2;
+    mi.x_vec = reinterpret_cast<uintptr_t>(x->data) % (4 * esz) == 0 ? 1 : 0;  // (hidden is a multiple of 128)
+  }
   mi.suh_g = gate->suh, mi.suh_u = up->suh, mi.suh_d = down->suh;
   mi.a_g = f.a_g, mi.a_u = f.a_u, mi.a_d = f.a_d;
   mi.gu = f.gu, mi.gu_stride = f.gu_stride, mi.limit = limit;
@@ -398,7 +413,7 @@ exl3_verdict moe_prefill_run(const exl3_weight* gate, const exl3_weight* up, con
     if (err == cudaSuccess) ok(launch_gemm_image(gd, hidden % 256 == 0 ? 1 : 0, f.sms, st));
   }
   if (err == cudaSuccess) {
-    const dim3 cg(static_cast<unsigned>((hidden + 511) / 512), static_cast<unsigned>(rows < 64 ? rows : 64));
+    const dim3 cg(static_cast<unsigned>((hidden + 511) / 512), static_cast<unsigned>(rows < 65535 ? rows : 65535));
     pf_combine_kernel<<<cg, 128, 0, st>>>(f.gu, f.gu_stride, f.pos, static_cast<const float*>(scores->data), rows,
                                           topk, hidden, out->data, out->dtype);
     ok(cudaGetLastError());
