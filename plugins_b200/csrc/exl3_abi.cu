@@ -438,7 +438,7 @@ exl3_verdict run_gemm(DeviceState* d, const exl3_weight* w, const void* x, int32
           gp.tiles_n = (nc + tbn - 1) / tbn;
           gp.kb = in_f / 64;
           gp.inner_only = (flags & EXL3_MATMUL_INNER) ? 1 : 0;
-          gp.vec_store = (reinterpret_cast<uintptr_t>(yp) % 16 == 0 && (ystride * ysz) % 16 == 0) ? 1 : 0;
+          gp.vec_store = exl3::store_width(yp, ystride * ysz);
           gp.err = d->err;
           if (fused) {
             gp.b_img = nullptr;

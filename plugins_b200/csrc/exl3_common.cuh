@@ -386,6 +386,13 @@ __device__ __forceinline__ void store_act(void* p, size_t i, float v, int32_t dt
   else static_cast<float*>(p)[i] = v;
 }
 
+// 32 bytes to a 32-byte aligned global address (sm_100's 256-bit store): a lane writes a whole L2 sector.
+__device__ __forceinline__ void st_global_v8(void* dst, const uint32_t (&r)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(r[0]), "r"(r[1]), "r"(r[2]),
+               "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 __device__ __forceinline__ float f16_bits_to_float(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 
 }  // namespace exl3

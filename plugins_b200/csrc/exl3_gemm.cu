@@ -489,7 +489,36 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
           }
           if (row < p.m) {
             const size_t at = static_cast<size_t>(row) * p.y_row_stride + col0;
-            if (p.vec_store && p.y_dtype != kF32) {
+            // 32-byte stores where y allows them: with one row per thread, a 16-byte store wrote half an L2 sector
+            // of 32 rows at once (measured on config 3's layer: the GEMM 172 -> 162 us)
+            if (p.vec_store == 2 && p.y_dtype != kF32) {
+              uint16_t* dst = static_cast<uint16_t*>(p.y) + at;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                uint32_t pk[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  const float lo = v[j * 16 + 2 * e], hi = v[j * 16 + 2 * e + 1];
+                  if (p.y_dtype == kF16) {
+                    const __half2 h2 = __floats2half2_rn(lo, hi);
+                    pk[e] = *reinterpret_cast<const uint32_t*>(&h2);
+                  } else {
+                    const __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+                    pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
+                  }
+                }
+                st_global_v8(dst + j * 16, pk);
+              }
+            } else if (p.vec_store == 2) {
+              float* dst = static_cast<float*>(p.y) + at;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                uint32_t pk[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) pk[e] = __float_as_uint(v[8 * j + e]);
+                st_global_v8(dst + j * 8, pk);
+              }
+            } else if (p.vec_store && p.y_dtype != kF32) {
               uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + at);
 #pragma unroll
               for (int j = 0; j < 16; ++j) {

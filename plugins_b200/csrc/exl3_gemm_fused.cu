@@ -302,6 +302,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) gemm_fused_kernel(const Gemm
                     }
                   }
                   *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) + aj) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                } else if (p.vec_store == 2) {
+                  uint32_t pk[8];  // eight f32 columns: one 32-byte store, a whole L2 sector
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) pk[e] = __float_as_uint(o[j][e]);
+                  st_global_v8(static_cast<float*>(p.y) + aj, pk);
                 } else if (p.vec_store) {
                   float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.y) + aj);
                   dst[0] = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);

@@ -223,7 +223,7 @@ struct GemmParams {
   int32_t ncols;         // valid columns (tiles past them are computed but not stored)
   int32_t tiles_m, tiles_n, kb;  // kb = in_features / 64
   int32_t inner_only;    // y = the f32 inner product (no output Hadamard, no svh)
-  int32_t vec_store;     // y and y_row_stride allow 16-byte stores
+  int32_t vec_store;     // y and y_row_stride allow 16-byte (1) or 32-byte (2) stores
   uint32_t* err;
   // grouped (the routed experts' prefill, 128-row blocks only): the blocks [mt_range[0], mt_range[1]) of the padded
   // rows (device words; null: blocks 0 .. tiles_m), block b's expert m_group[b]; expert e's B image at
@@ -278,6 +278,12 @@ cudaError_t launch_moe_b_images(const uint16_t* trellis, int in_features, int ou
                                 uint32_t cw_mask = 0, int mcg = 0);
 
 // shape: 0 = 128x128 tiles, 1 = 128x256, 2 = 256x128, 3 = 256x256 (rows x columns)
+// GemmParams::vec_store for output rows at y, row_bytes apart: 2 = 32-byte stores, 1 = 16-byte, 0 = element stores
+inline int32_t store_width(const void* y, int64_t row_bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(y);
+  if (a % 32 == 0 && row_bytes % 32 == 0) return 2;
+  return (a % 16 == 0 && row_bytes % 16 == 0) ? 1 : 0;
+}
 int gemm_block_m(int shape);
 int gemm_block_n(int shape);
 cudaError_t launch_gemm_image(const GemmParams& p, int shape, int sms, cudaStream_t st);

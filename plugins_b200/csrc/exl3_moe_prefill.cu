@@ -317,7 +317,7 @@ exl3_verdict moe_prefill_run(const exl3_weight* gate, const exl3_weight* up, con
       gp.tiles_m = f.rows_max / 128;
       gp.tiles_n = inter % 256 == 0 ? inter / 256 : inter / 128;
       gp.kb = hidden / 64;
-      gp.vec_store = 1;
+      gp.vec_store = store_width(f.gu, f.gu_stride * 4);
       gp.err = device_error_ptr();
       gp.mt_range = f.all;
       gp.m_group = f.m_group;
@@ -343,7 +343,7 @@ exl3_verdict moe_prefill_run(const exl3_weight* gate, const exl3_weight* up, con
     gd.tiles_m = f.rows_max / 128;
     gd.tiles_n = hidden % 256 == 0 ? hidden / 256 : hidden / 128;
     gd.kb = inter / 64;
-    gd.vec_store = 1;
+    gd.vec_store = store_width(f.gu, f.gu_stride * 4);
     gd.err = device_error_ptr();
     gd.mt_range = f.all;
     gd.m_group = f.m_group;
@@ -379,7 +379,7 @@ exl3_verdict moe_prefill_run(const exl3_weight* gate, const exl3_weight* up, con
       gp.tiles_m = f.rows_max / 128;
       gp.tiles_n = inter % 256 == 0 ? inter / 256 : inter / 128;
       gp.kb = hidden / 64;
-      gp.vec_store = 1;
+      gp.vec_store = store_width(f.gu, f.gu_stride * 4);
       gp.err = device_error_ptr();
       gp.mt_range = mtg;
       gp.m_group = f.m_group;
@@ -403,7 +403,7 @@ exl3_verdict moe_prefill_run(const exl3_weight* gate, const exl3_weight* up, con
     gd.tiles_m = f.rows_max / 128;
     gd.tiles_n = hidden % 256 == 0 ? hidden / 256 : hidden / 128;
     gd.kb = inter / 64;
-    gd.vec_store = 1;
+    gd.vec_store = store_width(f.gu, f.gu_stride * 4);
     gd.err = device_error_ptr();
     gd.mt_range = mtg;
     gd.m_group = f.m_group;
