@@ -377,15 +377,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) gemm_fused_kernel(const Gemm
     static_assert(8 % S::kTilesPerWarp == 0, "a warp's tiles stay inside one 128-column block");
     const uint32_t t0 = hf * S::kTilesPerWarp;
     const uint32_t lane_off = (t0 >> 3) * kImgBytes + (t0 & 7u) * 2048u + image_offset(g, kk * 16u + 4u * q);
+    // Two k-steps per iteration where three stages or more let the MMA drain one while the decoders fill two: the
+    // waits, fences, arrivals and ring cursors are paid once per eight tiles instead of four, and the two k-steps'
+    // decodes interleave (measured on B200: the routed experts' prefill at config 4's banks 3.46 -> 3.19 ms a call).
+    constexpr bool kPair = S::kStages >= 3;
     uint32_t stage = 0, phase = 0, slot_use = 0;
-#pragma unroll 1
-    for (int i = 0; i < items; ++i) {
-      cp_wait_f<kTrStages - 2>();
-      __syncwarp();
-      if (!warp_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, lane)) break;
-      const uint32_t* tw = reinterpret_cast<const uint32_t*>(ring + slot_use * S::kSlotBytes);
-      slot_use = slot_use + 1u == static_cast<uint32_t>(kTrStages) ? 0u : slot_use + 1u;
-      uint8_t* bst = stages + stage * S::kStageBytes + MS * kImgBytes + lane_off;
+    auto decode_item = [&](const uint32_t* tw, uint32_t st) {
+      uint8_t* bst = stages + st * S::kStageBytes + MS * kImgBytes + lane_off;
 #pragma unroll
       for (int t = 0; t < S::kTilesPerWarp; ++t) {
         uint32_t w[8], a[4];
@@ -396,15 +394,45 @@ __global__ void __launch_bounds__(kFusedThreads, 1) gemm_fused_kernel(const Gemm
         *reinterpret_cast<uint2*>(bst + t * 2048u) = make_uint2(a[0], a[2]);
         *reinterpret_cast<uint2*>(bst + t * 2048u + 1024u) = make_uint2(a[1], a[3]);
       }
+    };
+    auto next_stage = [](uint32_t& st, uint32_t& ph) {
+      if (++st == static_cast<uint32_t>(S::kStages)) {
+        st = 0;
+        ph ^= 1u;
+      }
+    };
+    auto next_slot = [](uint32_t sl) { return sl + 1u == static_cast<uint32_t>(kTrStages) ? 0u : sl + 1u; };
+#pragma unroll 1
+    for (int i = 0; i < items; i += kPair ? 2 : 1) {
+      const bool two = kPair && i + 1 < items;  // (warp-uniform)
+      // item i's trellis words (and item i + 1's) have landed: one commit group per item, kTrStages - 1 ahead
+      cp_wait_f<kPair ? kTrStages - 3 : kTrStages - 2>();
+      __syncwarp();
+      uint32_t stage2 = stage, phase2 = phase;
+      next_stage(stage2, phase2);
+      if (!warp_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, lane)) break;
+      if (two && !warp_wait(&empty[stage2], phase2 ^ 1u, abort_flag, p.err, lane)) break;
+      const uint32_t slot2 = next_slot(slot_use);
+      decode_item(reinterpret_cast<const uint32_t*>(ring + slot_use * S::kSlotBytes), stage);
+      if (two) decode_item(reinterpret_cast<const uint32_t*>(ring + slot2 * S::kSlotBytes), stage2);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&full[stage]);
+      if (lane == 0) {
+        mbar_arrive(&full[stage]);
+        if (two) mbar_arrive(&full[stage2]);
+      }
       issue();
       cp_commit_f();
-      if (++stage == S::kStages) {
-        stage = 0;
-        phase ^= 1u;
+      if (kPair) {
+        issue();
+        cp_commit_f();
+        slot_use = next_slot(slot2);
+        stage = stage2;
+        phase = phase2;
+      } else {
+        slot_use = slot2;
       }
+      next_stage(stage, phase);
     }
     cp_wait_f<0>();  // no copy outlives the CTA
     __syncwarp();
