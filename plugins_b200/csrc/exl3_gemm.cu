@@ -243,6 +243,103 @@ __global__ void __launch_bounds__(256) moe_a_images_kernel(const MoeImages j) {
   }
 }
 
+// H128(v * suh) / sqrt(128) with sixteen elements per lane (lanes 8b .. 8b + 7 hold block b, lane 8b + p its
+// elements 16p .. 16p + 15): stages h = 1 .. 8 in registers, h = 16, 32, 64 across the block's eight lanes -- the
+// butterflies of rotate128 in the same stage order, so the same bytes, with 48 shuffles a block-quad instead of 80.
+__device__ __forceinline__ void rotate128x16(float (&v)[16], const uint4 (&su)[2], uint32_t lane) {
+  const uint32_t sw[8] = {su[0].x, su[0].y, su[0].z, su[0].w, su[1].x, su[1].y, su[1].z, su[1].w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&sw[e]));
+    v[2 * e] *= f.x, v[2 * e + 1] *= f.y;
+  }
+#pragma unroll
+  for (int h = 1; h < 16; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if ((i & h) == 0) {
+        const float a = v[i], c = v[i + h];
+        v[i] = a + c;
+        v[i + h] = a - c;
+      }
+    }
+  }
+#pragma unroll
+  for (uint32_t bit = 1; bit <= 4; bit <<= 1) {
+    const bool lower = (lane & bit) == 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], bit);
+      v[i] = lower ? v[i] + p : p - v[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] *= kHadScale;
+}
+
+// Sixteen f16 elements k0 .. k0 + 15 (k0 a multiple of 16) of one image row: two 16-byte swizzled chunks.
+__device__ __forceinline__ void store_image16(uint8_t* img, int kblocks64, int row, int k0, const float (&v)[16]) {
+  uint32_t h[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const __half2 t = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    h[e] = *reinterpret_cast<const uint32_t*>(&t);
+  }
+  uint8_t* blk = img + ((static_cast<size_t>(row) >> 7) * kblocks64 + (k0 >> 6)) * kImgBytes;
+  const uint32_t r = static_cast<uint32_t>(row) & 127u, kk = static_cast<uint32_t>(k0 & 63);
+  *reinterpret_cast<uint4*>(blk + image_offset(r, kk)) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(blk + image_offset(r, kk + 8u)) = make_uint4(h[4], h[5], h[6], h[7]);
+}
+
+// The gate and up A images with sixteen elements per lane: one warp per (row, 512 inputs), grid-stride over the
+// call's rows.  Taken when x's rows are 16-byte aligned (x_vec) and hidden is a multiple of 512: fewer shuffles than
+// the four-per-lane form, whose rotations were bound by the shuffle rate.
+__global__ void __launch_bounds__(256) moe_a_images16_kernel(const MoeImages j) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const int groups = j.hidden / 512;
+  const int64_t jobs = static_cast<int64_t>(*j.rows_total) * groups;
+  for (int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); job < jobs;
+       job += static_cast<int64_t>(gridDim.x) * 8) {
+    const int row = static_cast<int>(job / groups);
+    const int slot = j.row_slot[row];
+    if (slot < 0) continue;  // (warp-uniform) padding
+    const int k0 = static_cast<int>(job % groups) * 512 + 16 * static_cast<int>(lane);
+    const size_t e = static_cast<size_t>(j.m_group[row >> 7]);
+    const size_t at = static_cast<size_t>(slot / j.topk) * j.x_row_stride + k0;
+    float vg[16], vu[16];
+    if (j.x_dtype == kF32) {
+      const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(j.x) + at);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 f = xp[q];
+        vg[4 * q] = f.x, vg[4 * q + 1] = f.y, vg[4 * q + 2] = f.z, vg[4 * q + 3] = f.w;
+      }
+    } else {
+      const uint4* xp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(j.x) + at);
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const uint4 u = xp[q];
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float2 f = j.x_dtype == kF16 ? __half22float2(*reinterpret_cast<const __half2*>(&w4[c]))
+                                             : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[c]));
+          vg[8 * q + 2 * c] = f.x, vg[8 * q + 2 * c + 1] = f.y;
+        }
+      }
+    }
+    const uint4* sgp = reinterpret_cast<const uint4*>(j.suh_g + e * j.hidden + k0);
+    const uint4* sup = reinterpret_cast<const uint4*>(j.suh_u + e * j.hidden + k0);
+    const uint4 sg[2] = {sgp[0], sgp[1]}, su[2] = {sup[0], sup[1]};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) vu[i] = vg[i];
+    rotate128x16(vg, sg, lane);
+    store_image16(j.a_g, j.hidden / kImgK, row, k0, vg);
+    rotate128x16(vu, su, lane);
+    store_image16(j.a_u, j.hidden / kImgK, row, k0, vu);
+  }
+}
+
 // The down input: h = silu(g) * u of the gate|up GEMMs' f32 outputs (g, u: columns [0, inter) and [inter, 2 inter)
 // of gu), clamped as the routed experts' epilogue clamps, times the down bank's suh, rotated, f16 -- one warp per
 // (row, KB 128-blocks) of the rows [row_range[0], row_range[1]), loads first as above.
@@ -594,7 +691,8 @@ cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, 
 
 cudaError_t launch_moe_a_images(const MoeImages& j, int sms, cudaStream_t st) {
   if (j.hidden % 128 != 0) return cudaErrorInvalidValue;
-  if (j.hidden % 512 == 0) moe_a_images_kernel<4><<<sms * 8, 256, 0, st>>>(j);
+  if (j.hidden % 512 == 0 && j.x_vec) moe_a_images16_kernel<<<sms * 8, 256, 0, st>>>(j);
+  else if (j.hidden % 512 == 0) moe_a_images_kernel<4><<<sms * 8, 256, 0, st>>>(j);
   else moe_a_images_kernel<1><<<sms * 8, 256, 0, st>>>(j);
   return cudaGetLastError();
 }

@@ -260,7 +260,7 @@ struct MoeImages {
   int32_t topk;
   const void* x;
   int32_t x_dtype;
-  int32_t x_vec;  // x's rows take 4-element vector loads (base and row stride aligned to 4 elements)
+  int32_t x_vec;  // x's rows take vector loads: 4 elements and 16 bytes aligned (row strides are multiples of 128)
   int64_t x_row_stride;
   int32_t hidden, inter;
   const uint16_t *suh_g, *suh_u, *suh_d;  // [E][hidden], [E][hidden], [E][inter]

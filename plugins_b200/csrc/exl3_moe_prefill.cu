@@ -291,7 +291,9 @@ exl3_verdict moe_prefill_run(const exl3_weight* gate, const exl3_weight* up, con
   mi.x = x->data, mi.x_dtype = x->dtype, mi.x_row_stride = hidden, mi.hidden = hidden, mi.inter = inter;
   {
     const size_t esz = x->dtype == EXL3_F32 ? 4 : 2;
-    mi.x_vec = reinterpret_cast<uintptr_t>(x->data) % (4 * esz) == 0 ? 1 : 0;  // (hidden is a multiple of 128)
+    // (hidden is a multiple of 128, so every row starts as aligned as x)
+    mi.x_vec = reinterpret_cast<uintptr_t>(x->data) % (4 * esz) == 0 ? 1 : 0;
+    if (reinterpret_cast<uintptr_t>(x->data) % 16 != 0) mi.x_vec = 0;  // the sixteen-per-lane form's 16-byte loads
   }
   mi.suh_g = gate->suh, mi.suh_u = up->suh, mi.suh_d = down->suh;
   mi.a_g = f.a_g, mi.a_u = f.a_u, mi.a_d = f.a_d;
