@@ -43,7 +43,8 @@ struct ImageJobs {
   int32_t m, mp, prepared;
   const uint16_t* suh;
   uint8_t* a_img;
-  int64_t prep_jobs;     // mp * in/128 warps, 0 = no A image
+  int64_t prep_jobs;     // mp * in/128 warps (prep16: mp * in/512), 0 = no A image
+  int32_t prep16;        // the sixteen-per-lane prepare jobs
   // B image: trellis columns [16 tn0, 16 (tn0 + ncol_tiles))
   const uint16_t* trellis;
   int32_t out_tiles, tn0, ncol_tiles;
@@ -52,6 +53,54 @@ struct ImageJobs {
   int32_t in_features;
   uint32_t cw_mask;      // a narrowed codeword window's mask (0: the full 16-bit window)
 };
+
+// H128(v * suh) / sqrt(128) with sixteen elements per lane (lanes 8b .. 8b + 7 hold block b, lane 8b + p its
+// elements 16p .. 16p + 15): stages h = 1 .. 8 in registers, h = 16, 32, 64 across the block's eight lanes -- the
+// butterflies of rotate128 in the same stage order, so the same bytes, with 48 shuffles a block-quad instead of 80.
+__device__ __forceinline__ void rotate128x16(float (&v)[16], const uint4 (&su)[2], uint32_t lane) {
+  const uint32_t sw[8] = {su[0].x, su[0].y, su[0].z, su[0].w, su[1].x, su[1].y, su[1].z, su[1].w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&sw[e]));
+    v[2 * e] *= f.x, v[2 * e + 1] *= f.y;
+  }
+#pragma unroll
+  for (int h = 1; h < 16; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if ((i & h) == 0) {
+        const float a = v[i], c = v[i + h];
+        v[i] = a + c;
+        v[i + h] = a - c;
+      }
+    }
+  }
+#pragma unroll
+  for (uint32_t bit = 1; bit <= 4; bit <<= 1) {
+    const bool lower = (lane & bit) == 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], bit);
+      v[i] = lower ? v[i] + p : p - v[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] *= kHadScale;
+}
+
+// Sixteen f16 elements k0 .. k0 + 15 (k0 a multiple of 16) of one image row: two 16-byte swizzled chunks.
+__device__ __forceinline__ void store_image16(uint8_t* img, int kblocks64, int row, int k0, const float (&v)[16]) {
+  uint32_t h[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const __half2 t = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    h[e] = *reinterpret_cast<const uint32_t*>(&t);
+  }
+  uint8_t* blk = img + ((static_cast<size_t>(row) >> 7) * kblocks64 + (k0 >> 6)) * kImgBytes;
+  const uint32_t r = static_cast<uint32_t>(row) & 127u, kk = static_cast<uint32_t>(k0 & 63);
+  *reinterpret_cast<uint4*>(blk + image_offset(r, kk)) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(blk + image_offset(r, kk + 8u)) = make_uint4(h[4], h[5], h[6], h[7]);
+}
 
 // Prepare job: one warp per (row, 128-wide input block), lane t holding elements 4t..4t+3 (vector loads and one
 // 8-byte store); the Hadamard's two low stages run in registers, the other five across lanes.
@@ -103,6 +152,49 @@ __device__ __forceinline__ void prep_job(const ImageJobs& j, int64_t job, uint32
       make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
 }
 
+// Prepare job with sixteen elements per lane: one warp per (row, 512 inputs), lanes 8b .. 8b + 7 holding 128-block b
+// (two 16-byte loads and two 16-byte stores a lane; three shuffle stages instead of five) -- the same bytes as four
+// prep_job calls.  Taken when in_features is a multiple of 512 and x's rows are 16-byte aligned: the one-block jobs
+// were short warps whose many waves of load latency set the prepare's time.
+__device__ __forceinline__ void prep16_job(const ImageJobs& j, int64_t job, uint32_t lane) {
+  const int kq = j.in_features / 512;
+  const int row = static_cast<int>(job / kq);
+  const int k0 = static_cast<int>(job % kq) * 512 + 16 * static_cast<int>(lane);
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = 0.f;
+  if (row < j.m) {
+    const size_t at = static_cast<size_t>(row) * j.x_row_stride + k0;
+    if (j.x_dtype == kF32) {
+      const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(j.x) + at);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float4 f = xp[c];
+        v[4 * c] = f.x, v[4 * c + 1] = f.y, v[4 * c + 2] = f.z, v[4 * c + 3] = f.w;
+      }
+    } else {
+      const uint4* xp = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(j.x) + at);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint4 u = xp[c];
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = j.x_dtype == kF16 ? __half22float2(*reinterpret_cast<const __half2*>(&w4[e]))
+                                             : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[e]));
+          v[8 * c + 2 * e] = f.x, v[8 * c + 2 * e + 1] = f.y;
+        }
+      }
+    }
+    if (!j.prepared) {
+      const uint4* sp = reinterpret_cast<const uint4*>(j.suh + k0);
+      const uint4 su[2] = {sp[0], sp[1]};
+      rotate128x16(v, su, lane);
+    }
+  }
+  store_image16(j.a_img, j.in_features / kImgK, row, k0, v);
+}
+
 // Decode job: kDecodeTilesPerWarp consecutive 16x16 tiles of one k-row (contiguous in the trellis).  Each lane holds
 // one column's four consecutive k per tile (the IMMA byte-sum order) and writes them as one 8-byte store; a warp's
 // stores fill whole 32-byte sectors.
@@ -146,7 +238,10 @@ __global__ void __launch_bounds__(256) images_kernel(const ImageJobs j) {
   const uint32_t lane = threadIdx.x & 31u;
   const int64_t job = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);  // warp-uniform
   if (job < j.decode_jobs) decode_job<N, DS>(j, job, lane);
-  else if (job < j.decode_jobs + j.prep_jobs) prep_job(j, job - j.decode_jobs, lane);
+  else if (job < j.decode_jobs + j.prep_jobs) {
+    if (j.prep16) prep16_job(j, job - j.decode_jobs, lane);
+    else prep_job(j, job - j.decode_jobs, lane);
+  }
 }
 
 // ------------------------------------------------------------------ the routed experts' prefill images
@@ -241,54 +336,6 @@ __global__ void __launch_bounds__(256) moe_a_images_kernel(const MoeImages j) {
       store_image4(j.a_u, j.hidden / kImgK, row, k0 + b * 128, v[b]);
     }
   }
-}
-
-// H128(v * suh) / sqrt(128) with sixteen elements per lane (lanes 8b .. 8b + 7 hold block b, lane 8b + p its
-// elements 16p .. 16p + 15): stages h = 1 .. 8 in registers, h = 16, 32, 64 across the block's eight lanes -- the
-// butterflies of rotate128 in the same stage order, so the same bytes, with 48 shuffles a block-quad instead of 80.
-__device__ __forceinline__ void rotate128x16(float (&v)[16], const uint4 (&su)[2], uint32_t lane) {
-  const uint32_t sw[8] = {su[0].x, su[0].y, su[0].z, su[0].w, su[1].x, su[1].y, su[1].z, su[1].w};
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&sw[e]));
-    v[2 * e] *= f.x, v[2 * e + 1] *= f.y;
-  }
-#pragma unroll
-  for (int h = 1; h < 16; h <<= 1) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      if ((i & h) == 0) {
-        const float a = v[i], c = v[i + h];
-        v[i] = a + c;
-        v[i + h] = a - c;
-      }
-    }
-  }
-#pragma unroll
-  for (uint32_t bit = 1; bit <= 4; bit <<= 1) {
-    const bool lower = (lane & bit) == 0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], bit);
-      v[i] = lower ? v[i] + p : p - v[i];
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] *= kHadScale;
-}
-
-// Sixteen f16 elements k0 .. k0 + 15 (k0 a multiple of 16) of one image row: two 16-byte swizzled chunks.
-__device__ __forceinline__ void store_image16(uint8_t* img, int kblocks64, int row, int k0, const float (&v)[16]) {
-  uint32_t h[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const __half2 t = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
-    h[e] = *reinterpret_cast<const uint32_t*>(&t);
-  }
-  uint8_t* blk = img + ((static_cast<size_t>(row) >> 7) * kblocks64 + (k0 >> 6)) * kImgBytes;
-  const uint32_t r = static_cast<uint32_t>(row) & 127u, kk = static_cast<uint32_t>(k0 & 63);
-  *reinterpret_cast<uint4*>(blk + image_offset(r, kk)) = make_uint4(h[0], h[1], h[2], h[3]);
-  *reinterpret_cast<uint4*>(blk + image_offset(r, kk + 8u)) = make_uint4(h[4], h[5], h[6], h[7]);
 }
 
 // The gate and up A images with sixteen elements per lane: one warp per (row, 512 inputs), grid-stride over the
@@ -672,7 +719,10 @@ cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, 
       return cudaErrorInvalidValue;
     j.x = x, j.x_dtype = x_dtype, j.x_row_stride = x_row_stride;
     j.m = m, j.mp = mp, j.prepared = prepared, j.suh = suh, j.a_img = a_img;
-    j.prep_jobs = static_cast<int64_t>(mp) * (in_features / 128);
+    const size_t xsz = x_dtype == kF32 ? 4 : 2;
+    j.prep16 = in_features % 512 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 && (x_row_stride * xsz) % 16 == 0 &&
+               (prepared || reinterpret_cast<uintptr_t>(suh) % 16 == 0);
+    j.prep_jobs = static_cast<int64_t>(mp) * (in_features / (j.prep16 ? 512 : 128));
   }
   if (b_img) {
     if (col0 % 128 != 0 || ncols % 128 != 0) return cudaErrorInvalidValue;
@@ -691,7 +741,8 @@ cudaError_t launch_images(const void* x, int32_t x_dtype, int64_t x_row_stride, 
 
 cudaError_t launch_moe_a_images(const MoeImages& j, int sms, cudaStream_t st) {
   if (j.hidden % 128 != 0) return cudaErrorInvalidValue;
-  if (j.hidden % 512 == 0 && j.x_vec) moe_a_images16_kernel<<<sms * 8, 256, 0, st>>>(j);
+  const bool suh16 = reinterpret_cast<uintptr_t>(j.suh_g) % 16 == 0 && reinterpret_cast<uintptr_t>(j.suh_u) % 16 == 0;
+  if (j.hidden % 512 == 0 && j.x_vec && suh16) moe_a_images16_kernel<<<sms * 8, 256, 0, st>>>(j);
   else if (j.hidden % 512 == 0) moe_a_images_kernel<4><<<sms * 8, 256, 0, st>>>(j);
   else moe_a_images_kernel<1><<<sms * 8, 256, 0, st>>>(j);
   return cudaGetLastError();
