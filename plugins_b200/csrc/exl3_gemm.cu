@@ -458,7 +458,8 @@ struct GemmShape {
   static constexpr int kAccCols = MS * BN;
   static constexpr int kAccBufs = kAccCols * 2 <= 512 ? 2 : 1;
   static constexpr int kTmemCols = kAccCols * kAccBufs <= 256 ? 256 : 512;
-  static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
+  // stages, 1024-byte alignment slack, barriers, and the four epilogue warps' two svh slots of NS x 128 halves
+  static constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256 + 4 * 2 * NS * 256;
   static_assert(BN <= 256, "one MMA covers at most 256 columns");
   static_assert(kAccCols * kAccBufs <= 512, "TMEM holds 512 columns");
 };
@@ -590,14 +591,30 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
   } else if (warp >= 4) {
     // ---------------- epilogue: warp 4 + j reads TMEM lanes 32 j .. 32 j + 31
     const uint32_t wq = warp - 4;
+    uint8_t* svs = stages + S::kStages * S::kStageBytes + 256 + wq * 2 * (NS * 256);  // this warp's [2][NS*128] svh
     int local = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
       const int ab = S::kAccBufs == 2 ? (local & 1) : 0;
       const uint32_t aph = S::kAccBufs == 2 ? ((local >> 1) & 1) : (local & 1);
-      if (!role_wait(&accf[ab], aph, abort_flag, p.err)) break;
-      tc_fence_after();
       const int mb = mt0 + t % tiles_m, nb = t / tiles_m;
       const int64_t sv_e = p.m_group ? static_cast<int64_t>(p.m_group[mb]) * p.svh_group : 0;
+      // the tile's svh columns into this warp's shared-memory slot before the accumulator wait, so their load latency
+      // hides under it instead of following the Hadamard (measured on config 3's layer: the GEMM 165 -> 161 us)
+      uint8_t* svt = svs + (local & 1) * (NS * 256);
+      if (!p.inner_only && lane < static_cast<uint32_t>(NS * 16)) {
+        const int c = static_cast<int>(lane) / 16, q16 = static_cast<int>(lane) % 16;
+        const int col0 = (nb * NS + c) * 128;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (col0 < p.ncols) {
+          const uint16_t* svc = p.svh2 && col0 >= p.svh_split ? p.svh2 + sv_e + (col0 - p.svh_split)
+                                                              : p.svh + sv_e + col0;
+          v = __ldg(reinterpret_cast<const uint4*>(svc) + q16);
+        }
+        reinterpret_cast<uint4*>(svt)[lane] = v;
+      }
+      if (!role_wait(&accf[ab], aph, abort_flag, p.err)) break;
+      tc_fence_after();
+      __syncwarp();
 #pragma unroll 1
       for (int s = 0; s < MS; ++s) {
         const int row = (mb * MS + s) * 128 + static_cast<int>(wq * 32 + lane);
@@ -618,12 +635,10 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
           }
           if (!p.inner_only) {
             fwht128_regs(v);
-            const uint16_t* svc = p.svh2 && col0 >= p.svh_split ? p.svh2 + sv_e + (col0 - p.svh_split)
-                                                                : p.svh + sv_e + col0;
-            const uint4* sv4 = reinterpret_cast<const uint4*>(svc);
+            const uint4* sv4 = reinterpret_cast<const uint4*>(svt + c * 256);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const uint4 u = __ldg(sv4 + j);
+              const uint4 u = sv4[j];
               const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
