@@ -450,6 +450,17 @@ __global__ void __launch_bounds__(256) moe_b_images_kernel(ImageJobs j, int e0, 
 
 // ------------------------------------------------------------------ the GEMM
 
+// Orders uses of r after an earlier tcgen05.wait::ld (both asm statements are volatile, so they keep their order).
+__device__ __forceinline__ void tmem_after_wait(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                 "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
 template <int MS, int NS>
 struct GemmShape {
   static constexpr int BM = 128 * MS, BN = 128 * NS;
@@ -623,16 +634,18 @@ __global__ void __launch_bounds__(256, 1) gemm_image_kernel(const GemmParams p) 
           const int col0 = (nb * NS + c) * 128;
           if (col0 >= p.ncols) continue;  // warp-uniform: a ragged tile's padding columns are neither read nor stored
           float v[128];
+          uint32_t rr[4][32];
           const uint32_t taddr =
               tmem + ((wq * 32u) << 16) + static_cast<uint32_t>(ab * S::kAccCols + s * S::BN + c * 128);
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            uint32_t r[32];
-            tmem_ld32(taddr + h * 32, r);
-            tmem_wait_ld(r);
+          for (int h = 0; h < 4; ++h) tmem_ld32(taddr + h * 32, rr[h]);  // four loads, one wait (1 % on config 3)
+          tmem_wait_ld(rr[0]);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[h * 32 + i] = __uint_as_float(r[i]);
-          }
+          for (int h = 1; h < 4; ++h) tmem_after_wait(rr[h]);
+#pragma unroll
+          for (int h = 0; h < 4; ++h)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[h * 32 + i] = __uint_as_float(rr[h][i]);
           if (!p.inner_only) {
             fwht128_regs(v);
             const uint4* sv4 = reinterpret_cast<const uint4*>(svt + c * 256);
